@@ -1,0 +1,141 @@
+/*
+ * duplex_b200.h -- C ABI of the B200 (sm_100a) int4 dequant-GEMV / fused-MoE path.
+ *
+ * This is the drop-in boundary for the reference's hot path
+ * (thecodacus/qwen3-omni-duplex).  Every entry point takes plain device pointers,
+ * sizes and a cudaStream_t (passed as void*), returns an int status
+ * (DUPLEX_OK == 0), never allocates, never synchronises, and launches only on the
+ * given stream, so every call can be captured in a CUDA graph.
+ *
+ * Weight format (unchanged from the reference's stacked buffers,
+ * src/duplex/streaming/fused_packed_moe.py:68-80, 117-123):
+ *   packed [E][Rs][K/8] int32   -- column i + 8m is nibble i (bits 4i..4i+3) of word m
+ *   scale  [E][Rs][G]   fp16|bf16, G = ceil(K / group)
+ *   zeros  [E][Rs][ceil(G/8)] int32 or NULL -- 4-bit zero point per (row, group), same
+ *          nibble order along the group axis; NULL means zero point 8 everywhere,
+ *          which is the reference's symmetric format (value = nibble - 8).
+ * Rs (rows allocated per expert) must be a multiple of 16 and >= R (rows used);
+ * K % 32 == 0; group % 32 == 0; every base pointer 16-byte aligned.
+ *
+ * Activations are fp16 or bf16 (DUPLEX_DTYPE_*), accumulation is fp32.
+ */
+#ifndef DUPLEX_B200_H
+#define DUPLEX_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes */
+#define DUPLEX_OK 0
+#define DUPLEX_ERR_ARG 1          /* bad size / null pointer / unsupported combination */
+#define DUPLEX_ERR_ALIGN 2        /* pointer or stride not 16-byte aligned */
+#define DUPLEX_ERR_DTYPE 3        /* unsupported dtype code */
+#define DUPLEX_ERR_WORKSPACE 4    /* workspace too small */
+#define DUPLEX_ERR_CUDA 5         /* a CUDA runtime call failed (see duplex_last_cuda_error) */
+#define DUPLEX_ERR_UNSUPPORTED 6  /* shape outside what the kernels implement */
+
+/* ---- device-side error word bits (written with atomicOr into `err`, never trap) */
+#define DUPLEX_DEVERR_EXPERT 1    /* an expert id outside [0, E) was clamped to 0 */
+#define DUPLEX_DEVERR_TIMEOUT 2   /* a bounded pipeline wait gave up */
+
+/* ---- dtype codes */
+#define DUPLEX_DTYPE_F16 0
+#define DUPLEX_DTYPE_BF16 1
+#define DUPLEX_DTYPE_F32 2
+
+int duplex_version(void);
+const char* duplex_error_string(int status);
+int duplex_last_cuda_error(void);
+
+/*
+ * unpack4 -- reference `unpack4` (src/duplex/streaming/fused_packed_moe.py:54-65).
+ * packed [rows][C] int32 -> out [rows][out_cols] int32 in [-8, 7]; out_cols <= 8*C.
+ */
+int duplex_unpack4(const int32_t* packed, int64_t rows, int32_t C, int32_t out_cols,
+                   int32_t* out, void* stream);
+
+/*
+ * dequant -- reference `FusedPackedMoE._dequant` (fused_packed_moe.py:183-189) and
+ * `dequantize_weight` (src/duplex/quant/dequant.py:40-77), zero-point generalised:
+ * out[r][c] = round_out((nibble - zero) * scale[r][c / group]) with ONE rounding of
+ * the exact product into out_dtype (F16 / BF16 / F32).  rows = E * R (any layout of
+ * the leading dims), K columns.  scale_dtype F16 / BF16 / F32.
+ */
+int duplex_dequant(const int32_t* packed, const void* scale, int scale_dtype,
+                   const int32_t* zeros, int64_t rows, int32_t K, int32_t group,
+                   void* out, int out_dtype, void* stream);
+
+/*
+ * dq_gemv -- reference `dequant_gemv` (src/duplex/streaming/triton_dequant_gemv.py:85-113).
+ * out[j][r] = sum_c W[sel[j]][r][c] * x_j[c] in fp32 for r < R.
+ * x: [K] shared by all slots (x_slot_stride = 0) or [nsel][x_slot_stride] rows.
+ * sel: [nsel] int32 expert ids (device).  out: [nsel][R] fp32.
+ * err: optional device int (bit DUPLEX_DEVERR_EXPERT when a sel id is out of range).
+ */
+int duplex_dq_gemv(const void* x, int act_dtype, int64_t x_slot_stride,
+                   const int32_t* packed, const void* scale, const int32_t* zeros,
+                   int scale_dtype, int32_t E, int32_t R, int32_t Rs, int32_t K,
+                   int32_t group, const int32_t* sel, int32_t nsel, float* out,
+                   int32_t* err, void* stream);
+
+/*
+ * packed_linear -- reference `TritonPackedLinear.forward` (triton_dequant_gemv.py:151-159)
+ * for B <= 8 rows in one launch (the reference launches once per row):
+ * y[b][r] = round_act(round_act(sum_c W[r][c] x[b][c]) + bias[r]) (+ residual[b][r], fp32 add,
+ * one more rounding; not in the reference, used by the clock-path stack).
+ * x [B][K] rows x_row_stride apart; out [B][R] rows out_row_stride apart (act dtype).
+ * pdl != 0 launches with programmatic dependent launch and prefetches the weights
+ * before waiting on the previous kernel.
+ */
+int duplex_packed_linear(const void* x, int act_dtype, int32_t B, int64_t x_row_stride,
+                         const int32_t* packed, const void* scale, const int32_t* zeros,
+                         int scale_dtype, int32_t R, int32_t Rs, int32_t K, int32_t group,
+                         const void* bias, const void* residual, int64_t res_row_stride,
+                         void* out, int64_t out_row_stride, int pdl, void* stream);
+
+/*
+ * moe_workspace_bytes -- bytes of scratch the MoE entry points need for T tokens.
+ */
+int duplex_moe_workspace_bytes(int32_t T, int32_t E, int32_t I, int32_t top_k, size_t* bytes);
+
+/*
+ * moe_route -- router of `FusedPackedMoE.forward` (fused_packed_moe.py:195-199):
+ * logits = x @ gate_w^T (+ gate_b), rounded to the act dtype (nn.Linear in the module
+ * dtype), softmax in fp32, top-k (ties -> lower expert id), renormalised when
+ * norm_topk != 0.  x [T][H], gate_w [E][H] (act dtype), gate_b [E] or NULL.
+ * w_out [T][top_k] fp32, sel_out [T][top_k] int32.  T <= 8, E <= 256, top_k <= 8.
+ * workspace: duplex_moe_workspace_bytes bytes, zero-filled once before first use.
+ */
+int duplex_moe_route(const void* x, int act_dtype, int32_t T, const void* gate_w,
+                     const void* gate_b, int32_t E, int32_t H, int32_t top_k,
+                     int32_t norm_topk, float* w_out, int32_t* sel_out, void* workspace,
+                     size_t workspace_bytes, int pdl, void* stream);
+
+/*
+ * moe_forward -- the whole of `FusedPackedMoE.forward` (fused_packed_moe.py:191-275) for
+ * T <= 8 tokens: route -> gate|up dequant-GEMV with SiLU(gate)*up epilogue -> down
+ * dequant-GEMV with the routing-weighted combine epilogue, three launches chained by
+ * programmatic dependent launch when pdl != 0.  Tokens that pick the same expert
+ * share one pass over its weights.
+ * gu_* : [E][2I][H/8] (gate rows 0..I-1, up rows I..2I-1), dn_* : [E][H][I/8].
+ * out [T][H] act dtype (+ residual [T][H] when not NULL, fp32 add).  w_out/sel_out as in
+ * moe_route (may be NULL).  err: optional device int.
+ */
+int duplex_moe_forward(const void* x, int act_dtype, int32_t T, const void* gate_w,
+                       const void* gate_b, int32_t E, int32_t H, int32_t I, int32_t top_k,
+                       int32_t norm_topk, const int32_t* gu_packed, const void* gu_scale,
+                       const int32_t* gu_zeros, const int32_t* dn_packed,
+                       const void* dn_scale, const int32_t* dn_zeros, int scale_dtype,
+                       int32_t group, const void* residual, void* out, float* w_out,
+                       int32_t* sel_out, void* workspace, size_t workspace_bytes,
+                       int32_t* err, int pdl, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DUPLEX_B200_H */

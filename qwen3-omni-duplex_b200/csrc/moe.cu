@@ -1,0 +1,317 @@
+// Decode MoE (T <= 8 tokens): router kernel + orchestration of the three launches.
+//
+// Router: one warp per expert row of the gate (E/4 CTAs of 4 warps).  The gate
+// rows are loaded into registers before griddepcontrol.wait (they are weights),
+// the dot products with the T token rows are done in fp32, each logit is rounded
+// once into the activation dtype (nn.Linear in the module dtype,
+// fused_packed_moe.py:112,195), and the CTA that arrives last on a global
+// counter does, per token, softmax in fp32, top-k (ties -> lower expert id) and
+// renormalisation (fused_packed_moe.py:195-199), then builds the unit plan: the
+// distinct experts selected by the T tokens, each with its token mask and
+// routing weights, so tokens that share an expert share one weight pass.
+#include "common.cuh"
+#include "moe.cuh"
+
+namespace duplex {
+
+int record_cuda(cudaError_t e);
+int num_sms();
+int launch_moe_experts(int act_dtype, int scale_dtype, int T, int E, int H, int I, int group,
+                       const int32_t* gu_packed, const void* gu_scale, const int32_t* gu_zeros,
+                       const int32_t* dn_packed, const void* dn_scale, const int32_t* dn_zeros,
+                       const MoePlan* plan, const void* x, void* act, const void* residual,
+                       void* out, int* err, int max_units, bool pdl, cudaStream_t st);
+
+constexpr int kRouteWarps = 4;
+constexpr int kRouteMaxChunks = 16;  // 16-byte chunks per lane: H <= 16 * 32 * 8 = 4096
+
+struct RouteParams {
+  const void* x;
+  const void* gate_w;
+  const void* gate_b;
+  int T, E, H, top_k, norm;
+  float* w_out;
+  int32_t* sel_out;
+  float* logits;
+  int* counter;
+  MoePlan* plan;
+};
+
+template <typename T>
+DEVI void dot8(const uint4& a, const uint4& b, float& acc) {
+  const T* pa = reinterpret_cast<const T*>(&a);
+  const T* pb = reinterpret_cast<const T*>(&b);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) acc = fmaf(to_f32<T>(pa[q]), to_f32<T>(pb[q]), acc);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(const __grid_constant__ RouteParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ int s_last;
+  __shared__ int s_sel[kMaxTokens * kMaxTopK];
+  __shared__ float s_w[kMaxTokens * kMaxTopK];
+
+  pdl_launch_dependents();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int e = blockIdx.x * kRouteWarps + warp;
+  const int nchunk = p.H >> 3;
+
+  // gate row -> registers (independent of the previous kernel)
+  uint4 wr[kRouteMaxChunks];
+#pragma unroll
+  for (int j = 0; j < kRouteMaxChunks; ++j) {
+    const int c = lane + 32 * j;
+    if (e < p.E && c < nchunk)
+      wr[j] = reinterpret_cast<const uint4*>(p.gate_w)[(size_t)e * nchunk + c];
+    else
+      wr[j] = make_uint4(0, 0, 0, 0);
+  }
+  pdl_wait();
+
+  // token rows -> shared memory
+  uint4* xs = reinterpret_cast<uint4*>(smem);
+  for (int idx = tid; idx < p.T * nchunk; idx += blockDim.x)
+    xs[idx] = reinterpret_cast<const uint4*>(p.x)[idx];
+  __syncthreads();
+
+  if (e < p.E) {
+    float acc[kMaxTokens];
+#pragma unroll
+    for (int t = 0; t < kMaxTokens; ++t) acc[t] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kRouteMaxChunks; ++j) {
+      const int c = lane + 32 * j;
+      if (c < nchunk) {
+#pragma unroll
+        for (int t = 0; t < kMaxTokens; ++t)
+          if (t < p.T) dot8<T>(wr[j], xs[t * nchunk + c], acc[t]);
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < kMaxTokens; ++t) {
+      float v = acc[t];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0 && t < p.T) {
+        if (p.gate_b) v += to_f32<T>(reinterpret_cast<const T*>(p.gate_b)[e]);
+        p.logits[t * p.E + e] = to_f32<T>(from_f32<T>(v));
+      }
+    }
+  }
+
+  // ---- last CTA to arrive selects
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const int prev = atomicAdd(p.counter, 1);
+    s_last = (prev == (int)gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+
+  const int per_lane = (p.E + 31) >> 5;  // <= 8
+  for (int t = warp; t < p.T; t += kRouteWarps) {
+    float v[8];
+    unsigned taken = 0;
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int ei = lane + 32 * i;
+      v[i] = (i < per_lane && ei < p.E) ? __ldcg(p.logits + t * p.E + ei) : -INFINITY;
+      m = fmaxf(m, v[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float S = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (v[i] != -INFINITY) S += expf(v[i] - m);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+
+    float pj[kMaxTopK];
+    int sj[kMaxTopK];
+    float psum = 0.f;
+    for (int j = 0; j < p.top_k; ++j) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int ei = lane + 32 * i;
+        if (!((taken >> i) & 1u) && ei < p.E && (v[i] > bv || (v[i] == bv && ei < bi))) {
+          bv = v[i];
+          bi = ei;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+      sj[j] = bi;
+      pj[j] = expf(bv - m) / S;
+      psum += pj[j];
+    }
+    if (lane == 0) {
+      for (int j = 0; j < p.top_k; ++j) {
+        const float w = p.norm ? pj[j] / psum : pj[j];
+        p.w_out[t * p.top_k + j] = w;
+        p.sel_out[t * p.top_k + j] = sj[j];
+        s_w[t * kMaxTopK + j] = w;
+        s_sel[t * kMaxTopK + j] = sj[j];
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- unit plan: distinct experts in ascending id order
+  if (warp == 0) {
+    int base = 0;
+    for (int i = 0; i < per_lane; ++i) {
+      const int ei = lane + 32 * i;
+      uint32_t mask = 0;
+      float wv[kMaxTokens];
+#pragma unroll
+      for (int t = 0; t < kMaxTokens; ++t) wv[t] = 0.f;
+      if (ei < p.E) {
+        for (int t = 0; t < p.T; ++t)
+          for (int j = 0; j < p.top_k; ++j)
+            if (s_sel[t * kMaxTopK + j] == ei) {
+              mask |= 1u << t;
+              wv[t] = s_w[t * kMaxTopK + j];
+            }
+      }
+      const unsigned bal = __ballot_sync(0xffffffffu, mask != 0u);
+      if (mask) {
+        const int pos = base + __popc(bal & ((1u << lane) - 1u));
+        if (pos < kMaxUnits) {
+          p.plan->unit_expert[pos] = ei;
+          p.plan->unit_mask[pos] = mask;
+#pragma unroll
+          for (int t = 0; t < kMaxTokens; ++t) p.plan->unit_w[pos * kMaxTokens + t] = wv[t];
+        }
+      }
+      base += __popc(bal);
+    }
+    if (lane == 0) {
+      p.plan->n_units = base < kMaxUnits ? base : kMaxUnits;
+      *p.counter = 0;  // ready for the next launch / graph replay
+    }
+  }
+}
+
+static inline bool al16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+static int launch_route(int act_dtype, const RouteParams& rp, bool pdl, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((rp.E + kRouteWarps - 1) / kRouteWarps);
+  cfg.blockDim = dim3(kRouteWarps * 32);
+  cfg.dynamicSmemBytes = (size_t)rp.T * rp.H * 2;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  if (act_dtype == DUPLEX_DTYPE_F16) {
+    auto k = route_kernel<__half>;
+    if (cfg.dynamicSmemBytes > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+      if (e != cudaSuccess) return record_cuda(e);
+    }
+    return record_cuda(cudaLaunchKernelEx(&cfg, k, rp));
+  }
+  if (act_dtype == DUPLEX_DTYPE_BF16) {
+    auto k = route_kernel<__nv_bfloat16>;
+    if (cfg.dynamicSmemBytes > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+      if (e != cudaSuccess) return record_cuda(e);
+    }
+    return record_cuda(cudaLaunchKernelEx(&cfg, k, rp));
+  }
+  return DUPLEX_ERR_DTYPE;
+}
+
+static int check_route(const void* x, int act_dtype, int T, const void* gate_w, int E, int H,
+                       int top_k, void* ws, size_t ws_bytes, int I) {
+  if (!x || !gate_w || !ws) return DUPLEX_ERR_ARG;
+  if (act_dtype != DUPLEX_DTYPE_F16 && act_dtype != DUPLEX_DTYPE_BF16) return DUPLEX_ERR_DTYPE;
+  if (T < 1 || T > kMaxTokens || E < 1 || E > kMaxExperts || top_k < 1 || top_k > kMaxTopK ||
+      top_k > E || H < 8)
+    return DUPLEX_ERR_ARG;
+  if ((H & 7) || H > kRouteMaxChunks * 32 * 8) return DUPLEX_ERR_UNSUPPORTED;
+  if (!al16(x) || !al16(gate_w) || !al16(ws)) return DUPLEX_ERR_ALIGN;
+  if (ws_bytes < moe_scratch_layout(T, E, I, top_k).total) return DUPLEX_ERR_WORKSPACE;
+  return DUPLEX_OK;
+}
+
+static RouteParams make_route(const void* x, int T, const void* gate_w, const void* gate_b, int E,
+                              int H, int top_k, int norm, float* w_out, int32_t* sel_out,
+                              uint8_t* ws, const MoeScratch& L) {
+  RouteParams rp = {};
+  rp.x = x; rp.gate_w = gate_w; rp.gate_b = gate_b;
+  rp.T = T; rp.E = E; rp.H = H; rp.top_k = top_k; rp.norm = norm;
+  rp.w_out = w_out ? w_out : reinterpret_cast<float*>(ws + L.w);
+  rp.sel_out = sel_out ? sel_out : reinterpret_cast<int32_t*>(ws + L.sel);
+  rp.logits = reinterpret_cast<float*>(ws + L.logits);
+  rp.counter = reinterpret_cast<int*>(ws + L.counter);
+  rp.plan = reinterpret_cast<MoePlan*>(ws + L.plan);
+  return rp;
+}
+
+}  // namespace duplex
+
+using namespace duplex;
+
+extern "C" int duplex_moe_workspace_bytes(int32_t T, int32_t E, int32_t I, int32_t top_k,
+                                          size_t* bytes) {
+  if (!bytes || T < 1 || E < 1 || I < 1 || top_k < 1) return DUPLEX_ERR_ARG;
+  *bytes = moe_scratch_layout(T, E, I, top_k).total;
+  return DUPLEX_OK;
+}
+
+extern "C" int duplex_moe_route(const void* x, int act_dtype, int32_t T, const void* gate_w,
+                                const void* gate_b, int32_t E, int32_t H, int32_t top_k,
+                                int32_t norm_topk, float* w_out, int32_t* sel_out, void* workspace,
+                                size_t workspace_bytes, int pdl, void* stream) {
+  int rc = check_route(x, act_dtype, T, gate_w, E, H, top_k, workspace, workspace_bytes, 16);
+  if (rc) return rc;
+  const MoeScratch L = moe_scratch_layout(T, E, 16, top_k);
+  RouteParams rp = make_route(x, T, gate_w, gate_b, E, H, top_k, norm_topk, w_out, sel_out,
+                              reinterpret_cast<uint8_t*>(workspace), L);
+  return launch_route(act_dtype, rp, pdl != 0, (cudaStream_t)stream);
+}
+
+extern "C" int duplex_moe_forward(const void* x, int act_dtype, int32_t T, const void* gate_w,
+                                  const void* gate_b, int32_t E, int32_t H, int32_t I,
+                                  int32_t top_k, int32_t norm_topk, const int32_t* gu_packed,
+                                  const void* gu_scale, const int32_t* gu_zeros,
+                                  const int32_t* dn_packed, const void* dn_scale,
+                                  const int32_t* dn_zeros, int scale_dtype, int32_t group,
+                                  const void* residual, void* out, float* w_out, int32_t* sel_out,
+                                  void* workspace, size_t workspace_bytes, int32_t* err, int pdl,
+                                  void* stream) {
+  int rc = check_route(x, act_dtype, T, gate_w, E, H, top_k, workspace, workspace_bytes, I);
+  if (rc) return rc;
+  if (!out || I < 16) return DUPLEX_ERR_ARG;
+  if (!al16(out) || (residual && !al16(residual))) return DUPLEX_ERR_ALIGN;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  const MoeScratch L = moe_scratch_layout(T, E, I, top_k);
+  RouteParams rp = make_route(x, T, gate_w, gate_b, E, H, top_k, norm_topk, w_out, sel_out, ws, L);
+  cudaStream_t st = (cudaStream_t)stream;
+  rc = launch_route(act_dtype, rp, pdl != 0, st);
+  if (rc) return rc;
+  int max_units = T * top_k < E ? T * top_k : E;
+  if (max_units > kMaxUnits) max_units = kMaxUnits;
+  return launch_moe_experts(act_dtype, scale_dtype, T, E, H, I, group, gu_packed, gu_scale,
+                            gu_zeros, dn_packed, dn_scale, dn_zeros,
+                            reinterpret_cast<const MoePlan*>(ws + L.plan), x, ws + L.act, residual,
+                            out, err, max_units, pdl != 0, st);
+}

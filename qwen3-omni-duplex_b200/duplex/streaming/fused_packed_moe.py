@@ -1,0 +1,251 @@
+"""Fused int4 MoE on B200: router, gate|up, SiLU*up, down and combine in three kernels.
+
+Drop-in for the reference module of the same name
+(src/duplex/streaming/fused_packed_moe.py).  Same public names and contracts:
+
+  unpack4(packed, out_cols)                                 (reference :54-65)
+  _stack_packed(linears, dtype, device)                     (reference :68-80)
+  FusedPackedMoE(block, dtype, device, host_resident, cpu_compute)   (:83-275)
+      .forward(hidden_states) -> same shape and dtype
+      ._dequant(packed, scale, cols)                        (:183-189)
+  fuse_packed_moe_blocks(model, dtype, device, n_pinned, cpu_compute, verbose) -> int
+                                                            (:278-319)
+
+Differences, all deliberate:
+  * every layer is GPU resident (180 GB of HBM holds all 48 layers' experts), so
+    `host_resident`, `n_pinned` and `cpu_compute` are accepted and recorded, but
+    weights are never staged from host memory and nothing is computed on the CPU;
+  * batches of up to 8 tokens run as ONE pass (tokens that select the same expert
+    share its weight stream) instead of a per-token Python loop; larger batches
+    are processed 8 tokens at a time;
+  * optional 4-bit zero points (`weight_zeros` on the expert linears,
+    [R, ceil(G/8)] int32, nibble order along the group axis); absent means the
+    reference's symmetric format (value = nibble - 8);
+  * activations must be fp16 or bf16 CUDA tensors; there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import gc
+
+import torch
+import torch.nn as nn
+
+from duplex import _lib
+from duplex.streaming.triton_dequant_gemv import HAVE_TRITON, dequant_gemv  # noqa: F401
+
+NUM_BITS = 4
+PACK = 32 // NUM_BITS
+GROUP = 32
+
+
+def unpack4(packed: torch.Tensor, out_cols: int) -> torch.Tensor:
+    """Unpack int32-packed signed int4 along the last dim -> int32 in [-8, 7]."""
+    _lib.require_cuda(packed)
+    p = _lib.aligned(packed.to(torch.int32))
+    C = p.shape[-1]
+    rows = p.numel() // C if C else 0
+    out = torch.empty(*p.shape[:-1], out_cols, dtype=torch.int32, device=p.device)
+    _lib.call("duplex_unpack4", _lib.ptr(p), rows, C, out_cols, _lib.ptr(out), _lib.stream_of(p))
+    return out
+
+
+def _stack_packed(linears, dtype, device):
+    """Stack packed Linears into (packed, scale, out_features, in_features) (ref :68-80)."""
+    l0 = linears[0]
+    out_f, in_f = (int(v) for v in l0.weight_shape.tolist())
+    E = len(linears)
+    packed = torch.empty(E, out_f, l0.weight_packed.shape[1], dtype=torch.int32, device=device)
+    scale = torch.empty(E, out_f, l0.weight_scale.shape[1], dtype=dtype, device=device)
+    for i, lin in enumerate(linears):
+        packed[i] = lin.weight_packed.to(device)
+        scale[i] = lin.weight_scale.to(device, dtype)
+    return packed, scale, out_f, in_f
+
+
+def _stack_zeros(linears, device):
+    if getattr(linears[0], "weight_zeros", None) is None:
+        return None
+    return torch.stack([lin.weight_zeros.to(device, torch.int32) for lin in linears])
+
+
+class FusedPackedMoE(nn.Module):
+    """SparseMoeBlock replacement for int4-packed experts, on the B200 kernels."""
+
+    def __init__(self, block: nn.Module = None, dtype=torch.bfloat16, device="cuda",
+                 host_resident: bool = False, cpu_compute: bool = False):
+        super().__init__()
+        if dtype not in (torch.float16, torch.bfloat16):
+            raise _lib.DuplexError("FusedPackedMoE on B200 runs fp16 or bf16 modules")
+        self.host_resident = host_resident      # recorded; all weights stay in HBM
+        self.cpu_compute = cpu_compute and host_resident
+        self.pdl = True
+        if block is None:                       # filled by from_stacked()
+            return
+        experts = block.experts
+        self.num_experts = len(experts)
+        self.top_k = block.top_k
+        self.norm_topk_prob = getattr(block, "norm_topk_prob", True)
+        self.gate = block.gate.to(device=device, dtype=dtype)
+        gp, gs, inter, hidden = _stack_packed([e.gate_proj for e in experts], dtype, device)
+        up, us, _, _ = _stack_packed([e.up_proj for e in experts], dtype, device)
+        dp, ds, hid_out, inter_in = _stack_packed([e.down_proj for e in experts], dtype, device)
+        gz = _stack_zeros([e.gate_proj for e in experts], device)
+        uz = _stack_zeros([e.up_proj for e in experts], device)
+        dz = _stack_zeros([e.down_proj for e in experts], device)
+        gu_p, gu_s = torch.cat([gp, up], dim=1), torch.cat([gs, us], dim=1)
+        gu_z = None if gz is None else torch.cat([gz, uz], dim=1)
+        del gp, up, gs, us
+        self._install(gu_p, gu_s, gu_z, dp, ds, dz, inter, hidden, hid_out, inter_in)
+
+    @classmethod
+    def from_stacked(cls, gate_weight, gu_packed, gu_scale, dn_packed, dn_scale, top_k,
+                     gu_zeros=None, dn_zeros=None, norm_topk_prob=True, gate_bias=None,
+                     dtype=torch.float16, device="cuda"):
+        """Build from raw stacked tensors ([E,2I,H/8], [E,2I,G], [E,H,I/8], [E,H,G'])."""
+        m = cls(None, dtype=dtype, device=device)
+        E, H = gate_weight.shape
+        m.num_experts, m.top_k, m.norm_topk_prob = E, top_k, norm_topk_prob
+        m.gate = nn.Linear(H, E, bias=gate_bias is not None).to(device=device, dtype=dtype)
+        with torch.no_grad():
+            m.gate.weight.copy_(gate_weight)
+            if gate_bias is not None:
+                m.gate.bias.copy_(gate_bias)
+        I = gu_packed.shape[1] // 2
+        m._install(gu_packed.to(device), gu_scale.to(device, dtype),
+                   None if gu_zeros is None else gu_zeros.to(device),
+                   dn_packed.to(device), dn_scale.to(device, dtype),
+                   None if dn_zeros is None else dn_zeros.to(device),
+                   I, H, dn_packed.shape[1], dn_packed.shape[2] * PACK)
+        return m
+
+    def _install(self, gu_p, gu_s, gu_z, dp, ds, dz, inter, hidden, hid_out, inter_in):
+        if inter % 16 or hidden % 32 or inter_in % 32 or hid_out % 16:
+            raise _lib.DuplexError("expert dims must satisfy inter % 16 == 0 and hidden, "
+                                   "inter % 32 == 0 for the B200 kernels")
+        G = gu_s.shape[-1]
+        self.group = -(-hidden // G)
+        if -(-inter_in // ds.shape[-1]) != self.group:
+            raise _lib.DuplexError("gate|up and down must use the same group size")
+        a = _lib.aligned
+        self.register_buffer("gu_packed", a(gu_p.to(torch.int32)), persistent=False)
+        self.register_buffer("gu_scale", a(gu_s), persistent=False)
+        self.register_buffer("gu_zeros", None if gu_z is None else a(gu_z.to(torch.int32)),
+                             persistent=False)
+        self.register_buffer("down_packed", a(dp.to(torch.int32)), persistent=False)
+        self.register_buffer("down_scale", a(ds), persistent=False)
+        self.register_buffer("down_zeros", None if dz is None else a(dz.to(torch.int32)),
+                             persistent=False)
+        self.register_buffer("err", torch.zeros(1, dtype=torch.int32, device=gu_p.device),
+                             persistent=False)
+        self.inter, self.hidden, self.hid_out, self.inter_in = inter, hidden, hid_out, inter_in
+        self._ws = {}
+
+    @staticmethod
+    def _dequant(packed, scale, cols, zeros=None):
+        """[..., R, C] int32 + [..., R, G] scale -> [..., R, cols] in scale dtype (ref :183-189),
+        one rounding of the exact (nibble - zero) * scale product."""
+        _lib.require_cuda(packed, scale, zeros)
+        G = scale.shape[-1]
+        if cols % G:
+            raise _lib.DuplexError(f"cols {cols} not divisible by {G} scale groups")
+        p = _lib.aligned(packed.to(torch.int32)[..., : cols // PACK])
+        s = _lib.aligned(scale)
+        z = None if zeros is None else _lib.aligned(zeros.to(torch.int32))
+        out = torch.empty(*p.shape[:-1], cols, dtype=scale.dtype, device=p.device)
+        rows = p.numel() // p.shape[-1]
+        code = _lib.dtype_code(scale.dtype)
+        _lib.call("duplex_dequant", _lib.ptr(p), _lib.ptr(s), code, _lib.ptr(z), rows, cols,
+                  cols // G, _lib.ptr(out), code, _lib.stream_of(p))
+        return out
+
+    def workspace(self, T: int, device) -> torch.Tensor:
+        ws = self._ws.get((T, device))
+        if ws is None:
+            n = _lib.ctypes.c_size_t()
+            _lib.call("duplex_moe_workspace_bytes", T, self.num_experts, self.inter, self.top_k,
+                      _lib.ctypes.byref(n))
+            ws = torch.zeros(n.value, dtype=torch.uint8, device=device)
+            self._ws[(T, device)] = ws
+        return ws
+
+    def forward_into(self, x, out, residual=None, w_out=None, sel_out=None):
+        """x [T<=8, H] -> out [T, H] (+ residual), no host synchronisation."""
+        T = x.shape[0]
+        ws = self.workspace(T, x.device)
+        g = self.gate
+        _lib.call(
+            "duplex_moe_forward", _lib.ptr(x), _lib.dtype_code(x.dtype), T, _lib.ptr(g.weight),
+            _lib.ptr(g.bias), self.num_experts, self.hidden, self.inter, self.top_k,
+            1 if self.norm_topk_prob else 0, _lib.ptr(self.gu_packed), _lib.ptr(self.gu_scale),
+            _lib.ptr(self.gu_zeros), _lib.ptr(self.down_packed), _lib.ptr(self.down_scale),
+            _lib.ptr(self.down_zeros), _lib.dtype_code(self.gu_scale.dtype), self.group,
+            _lib.ptr(residual), _lib.ptr(out), _lib.ptr(w_out), _lib.ptr(sel_out), _lib.ptr(ws),
+            ws.numel(), _lib.ptr(self.err), 1 if self.pdl else 0, _lib.stream_of(x))
+        return out
+
+    def route(self, hidden_states):
+        """(w [T, k] fp32, sel [T, k] int32) exactly as the forward routes them."""
+        x = _lib.aligned(hidden_states.reshape(-1, self.hidden))
+        T = x.shape[0]
+        w = torch.empty(T, self.top_k, dtype=torch.float32, device=x.device)
+        sel = torch.empty(T, self.top_k, dtype=torch.int32, device=x.device)
+        for t0 in range(0, T, 8):
+            xs = x[t0:t0 + 8]
+            ws = self.workspace(xs.shape[0], x.device)
+            g = self.gate
+            _lib.call("duplex_moe_route", _lib.ptr(xs), _lib.dtype_code(x.dtype), xs.shape[0],
+                      _lib.ptr(g.weight), _lib.ptr(g.bias), self.num_experts, self.hidden,
+                      self.top_k, 1 if self.norm_topk_prob else 0, _lib.ptr(w[t0:t0 + 8]),
+                      _lib.ptr(sel[t0:t0 + 8]), _lib.ptr(ws), ws.numel(), 0, _lib.stream_of(x))
+        return w, sel
+
+    def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
+        _lib.require_cuda(hidden_states)
+        shape = hidden_states.shape
+        x = _lib.aligned(hidden_states.reshape(-1, shape[-1]))
+        if x.dtype != self.gate.weight.dtype:
+            x = x.to(self.gate.weight.dtype)
+        T = x.shape[0]
+        out = torch.empty(T, self.hid_out, dtype=x.dtype, device=x.device)
+        for t0 in range(0, T, 8):
+            self.forward_into(x[t0:t0 + 8], out[t0:t0 + 8])
+        return out.to(hidden_states.dtype).view(shape)
+
+    def device_errors(self) -> int:
+        """Read (and clear) the device error word: bit 1 = expert id out of range,
+        bit 2 = a bounded wait timed out.  Synchronises."""
+        v = int(self.err.item())
+        self.err.zero_()
+        return v
+
+
+def fuse_packed_moe_blocks(model, dtype=torch.bfloat16, device="cuda",
+                           n_pinned: int | None = None, cpu_compute: bool = False,
+                           verbose: bool = True) -> int:
+    """Replace every packed SparseMoeBlock with a FusedPackedMoE (reference :278-319)."""
+    sites = []
+    for parent in model.modules():
+        for name, child in list(parent.named_children()):
+            if type(child).__name__.endswith("SparseMoeBlock") and hasattr(child, "experts"):
+                gp = getattr(child.experts[0], "gate_proj", None)
+                if gp is not None and hasattr(gp, "weight_packed"):
+                    sites.append((parent, name))
+    n = 0
+    for parent, name in sites:
+        child = getattr(parent, name)
+        host = n_pinned is not None and n >= n_pinned
+        setattr(parent, name, FusedPackedMoE(child, dtype, device, host_resident=host,
+                                             cpu_compute=cpu_compute))
+        child.experts = None
+        del child
+        gc.collect()
+        if torch.cuda.is_available():
+            torch.cuda.empty_cache()
+        n += 1
+        if verbose and n % 6 == 0:
+            used = torch.cuda.memory_allocated() / 1024**3 if torch.cuda.is_available() else 0
+            print(f"    fused {n}/{len(sites)} packed blocks, {used:.2f} GB", flush=True)
+    if verbose:
+        print(f"fused {n} packed MoE blocks, all GPU-resident (B200 kernels)")
+    return n

@@ -1,0 +1,343 @@
+"""GPU parity: the sm_100a kernels (through libduplex_b200.so) against the numpy
+oracle and the reference's golden vectors.
+
+Bars (from the task): unpacking, dequantised values and top-k ids bit-exact;
+layer outputs max|d| <= 2e-3 * max|y_ref| against the fp32 dequant-then-matmul.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from duplex import synth
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3          # max|d| / max|y_ref| for fp32-accumulated layer outputs
+GEMV_TOL = 2e-5     # single dequant-GEMV: exact products, fp32 sums
+
+
+def T(a, dev, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    return t if dtype is None else t.to(dtype)
+
+
+def np_round(a, dt):
+    return O.round_to(np.asarray(a, np.float32), {torch.float16: "float16",
+                                                  torch.bfloat16: "bfloat16"}[dt])
+
+
+def rel_err(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return np.abs(a - b).max() / max(np.abs(b).max(), 1e-30)
+
+
+# ------------------------------------------------------------------ unpack / dequant
+def test_unpack4_bit_exact(cuda, golden_dir):
+    from duplex.streaming.fused_packed_moe import unpack4
+    g = np.load(golden_dir / "golden_unpack.npz")
+    out = unpack4(T(g["words"], cuda), 190).cpu().numpy()
+    assert out.dtype == np.int32
+    assert np.array_equal(out, g["unpack4_190"])
+    rng = np.random.default_rng(0)
+    w = rng.integers(0, 2**32, size=(3, 7, 33), dtype=np.uint64).astype(np.uint32).view(np.int32)
+    assert np.array_equal(unpack4(T(w, cuda), 264).cpu().numpy(), O.unpack4(w, 264))
+
+
+@pytest.mark.parametrize("gname,G", [("g32", 8), ("g128", 2)])
+@pytest.mark.parametrize("dname,dt", [("f32", torch.float32), ("f16", torch.float16),
+                                      ("bf16", torch.bfloat16)])
+def test_dequant_bit_exact_vs_reference(cuda, golden_dir, gname, G, dname, dt):
+    from duplex.streaming.fused_packed_moe import FusedPackedMoE
+    d = np.load(golden_dir / "golden_dequant.npz")
+    s = T(d[f"{gname}_scale_f16"], cuda).to(dt)
+    w = FusedPackedMoE._dequant(T(d[f"{gname}_packed"], cuda), s, 256).float().cpu().numpy()
+    assert np.array_equal(w, d[f"{gname}_{dname}"])
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_dequant_zero_points_bit_exact(cuda, dt):
+    from duplex.streaming.fused_packed_moe import FusedPackedMoE
+    rng = np.random.default_rng(1)
+    lin = synth.linear_np(rng, 40, 512, 128, True)
+    s = np_round(lin["scale"].astype(np.float32), dt)
+    ref = O.dequant(lin["packed"], s, 512, lin["zeros"], {torch.float16: "float16",
+                                                          torch.bfloat16: "bfloat16"}[dt])
+    got = FusedPackedMoE._dequant(T(lin["packed"], cuda), T(s, cuda, dt), 512,
+                                  zeros=T(lin["zeros"], cuda)).float().cpu().numpy()
+    assert np.array_equal(got, np.asarray(ref, np.float32))
+
+
+@pytest.mark.parametrize("dname,dt", [("f32", torch.float32), ("f16", torch.float16),
+                                      ("bf16", torch.bfloat16)])
+def test_dequantize_weight_bit_exact(cuda, golden_dir, dname, dt):
+    from types import SimpleNamespace as NS
+    from duplex.quant.dequant import dequantize_weight
+    g = np.load(golden_dir / "golden_dequantize_weight.npz")
+    m = NS(weight_packed=T(g["packed"], cuda), weight_scale=T(g["scale"], cuda),
+           weight_shape=torch.tensor([48, 256]))
+    assert np.array_equal(dequantize_weight(m, dtype=dt).float().cpu().numpy(), g[dname])
+
+
+# ------------------------------------------------------------------ dequant-GEMV
+def test_dq_gemv_matches_reference_gemv_golden(cuda, golden_dir):
+    from duplex.streaming.triton_dequant_gemv import dequant_gemv
+    g = np.load(golden_dir / "golden_gemv.npz")
+    y = dequant_gemv(T(g["x"], cuda), T(g["packed"], cuda), T(g["scale"], cuda),
+                     T(g["sel"], cuda), group=32).cpu().numpy()
+    assert y.shape == g["y"].shape
+    assert rel_err(y, g["y"]) <= GEMV_TOL
+
+
+@pytest.mark.parametrize("K,R,group", [(256, 96, 32), (2048, 100, 128), (96, 48, 32),
+                                       (768, 2048, 128), (4096, 64, 64)])
+@pytest.mark.parametrize("zp", [False, True])
+@pytest.mark.parametrize("act", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("per_slot_x", [False, True])
+def test_dq_gemv_vs_oracle(cuda, K, R, group, zp, act, per_slot_x):
+    from duplex.streaming.triton_dequant_gemv import dequant_gemv
+    rng = np.random.default_rng(K + R + group + zp)
+    E = 5
+    lin = synth.linear_np(rng, E * R, K, group, zp)
+    packed = lin["packed"].reshape(E, R, -1)
+    scale = np_round(lin["scale"].astype(np.float32), act).reshape(E, R, -1)
+    zeros = None if lin["zeros"] is None else lin["zeros"].reshape(E, R, -1)
+    sel = np.array([3, 0, 4, 4], np.int32)
+    x = np_round(rng.standard_normal((4, K) if per_slot_x else (K,)), act)
+    ref = O.dequant_gemv(x, packed, scale, sel, zeros)
+    got = dequant_gemv(T(x, cuda, act), T(packed, cuda), T(scale, cuda, act), T(sel, cuda),
+                       group=group, zeros=None if zeros is None else T(zeros, cuda)).cpu().numpy()
+    assert got.shape == (4, R)
+    assert rel_err(got, ref) <= GEMV_TOL
+
+
+def test_dq_gemv_out_of_range_expert_sets_error_word(cuda):
+    from duplex import _lib
+    from duplex.streaming.triton_dequant_gemv import prepare_int4
+    rng = np.random.default_rng(2)
+    E, R, K = 4, 32, 256
+    lin = synth.linear_np(rng, E * R, K, 32, False)
+    packed, scale, zeros, R_, Rs = prepare_int4(T(lin["packed"].reshape(E, R, -1), cuda),
+                                                T(lin["scale"].reshape(E, R, -1), cuda))
+    x = T(rng.standard_normal(K).astype(np.float16), cuda)
+    sel = torch.tensor([1, 99, 2], dtype=torch.int32, device=cuda)
+    out = torch.empty(3, R, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    _lib.call("duplex_dq_gemv", _lib.ptr(x), 0, 0, _lib.ptr(packed), _lib.ptr(scale), None, 0,
+              E, R, Rs, K, 32, _lib.ptr(sel), 3, _lib.ptr(out), _lib.ptr(err), _lib.stream_of(x))
+    torch.cuda.synchronize()
+    assert int(err.item()) & _lib.DEVERR_EXPERT
+    ref = O.dequant_gemv(x.cpu().numpy(), lin["packed"].reshape(E, R, -1),
+                         lin["scale"].reshape(E, R, -1), [1, 2])
+    got = out.cpu().numpy()[[0, 2]]
+    assert rel_err(got, ref) <= GEMV_TOL
+
+
+# ------------------------------------------------------------------ dense linear
+@pytest.mark.parametrize("B", [1, 2, 3, 8, 11])
+@pytest.mark.parametrize("R,K", [(512, 2048), (272, 4096), (100, 256)])
+def test_packed_linear_vs_oracle(cuda, B, R, K):
+    from types import SimpleNamespace as NS
+    from duplex.streaming.triton_dequant_gemv import TritonPackedLinear
+    rng = np.random.default_rng(B * 7 + R)
+    lin = synth.linear_np(rng, R, K, 128, True)
+    bias = (rng.standard_normal(R) * 0.1).astype(np.float16)
+    mod = NS(weight_packed=T(lin["packed"], cuda), weight_scale=T(lin["scale"], cuda),
+             weight_zeros=T(lin["zeros"], cuda), weight_shape=torch.tensor([R, K]),
+             bias=T(bias, cuda))
+    m = TritonPackedLinear(mod, cuda)
+    x = rng.standard_normal((B, K)).astype(np.float16)
+    got = m(T(x, cuda)).float().cpu().numpy()
+    ref = O.packed_linear(x, lin["packed"], lin["scale"], lin["zeros"], bias, "float16")
+    ref = np.asarray(ref, np.float32)
+    assert got.shape == (B, R)
+    assert rel_err(got, ref) <= TOL
+    # only fp16 rounding-boundary cases may differ, by one ulp
+    assert (got == ref).mean() >= 0.98
+
+
+# ------------------------------------------------------------------ router
+def test_route_selection_bit_exact_on_exact_logits(cuda):
+    """x = e_0 makes every logit exactly gate_w[e, 0]: selection must match the oracle
+    bit for bit, including ties (lower expert id first)."""
+    from duplex.streaming.fused_packed_moe import FusedPackedMoE
+    E, H, I, k = 128, 256, 64, 8
+    rng = np.random.default_rng(4)
+    L = synth.moe_layer_np(seed=4, E=E, H=H, I=I, top_k=k, group=32, zero_points=False, T=8)
+    W = L["gate_w"].copy()
+    col = (rng.integers(-40, 40, size=E) / 16.0).astype(np.float16)  # many exact ties
+    W[:, 0] = col
+    W[:, 1:] = 0
+    x = np.zeros((8, H), np.float16)
+    for t in range(8):
+        x[t, 0] = 1.0 if t % 2 == 0 else -1.0
+        x[t, 1 + t] = 1.0
+    m = FusedPackedMoE.from_stacked(T(W, cuda), T(L["gu_packed"], cuda), T(L["gu_scale"], cuda),
+                                    T(L["dn_packed"], cuda), T(L["dn_scale"], cuda), k,
+                                    dtype=torch.float16)
+    w, sel = m.route(T(x, cuda))
+    w_ref, sel_ref, _ = O.router(x, W, k, True, None, "float16")
+    assert np.array_equal(sel.cpu().numpy(), sel_ref)
+    np.testing.assert_allclose(w.cpu().numpy(), w_ref, rtol=2e-6, atol=1e-7)
+
+
+def test_route_random_tokens_flip_rate(cuda):
+    from duplex.streaming.fused_packed_moe import FusedPackedMoE
+    L = synth.moe_layer_np(seed=11, E=128, H=2048, I=64, top_k=8, group=128, zero_points=True,
+                           T=8)
+    m = FusedPackedMoE.from_stacked(T(L["gate_w"], cuda), T(L["gu_packed"], cuda),
+                                    T(L["gu_scale"], cuda), T(L["dn_packed"], cuda),
+                                    T(L["dn_scale"], cuda), 8, gu_zeros=T(L["gu_zeros"], cuda),
+                                    dn_zeros=T(L["dn_zeros"], cuda), dtype=torch.float16)
+    rng = np.random.default_rng(12)
+    flips = 0
+    n = 0
+    for _ in range(16):
+        x = rng.standard_normal((8, 2048)).astype(np.float16)
+        _, sel = m.route(T(x, cuda))
+        _, sel_ref, _ = O.router(x, L["gate_w"], 8, True, None, "float16")
+        flips += int((np.sort(sel.cpu().numpy(), 1) != np.sort(sel_ref, 1)).any(1).sum())
+        n += 8
+    assert flips <= max(1, n // 50), f"{flips} of {n} tokens selected a different expert set"
+
+
+# ------------------------------------------------------------------ fused MoE
+def _moe_case(cuda, seed, E, H, I, k, group, zp, Tn, act):
+    from duplex.streaming.fused_packed_moe import FusedPackedMoE
+    L = synth.moe_layer_np(seed=seed, E=E, H=H, I=I, top_k=k, group=group, zero_points=zp, T=Tn)
+    name = {torch.float16: "float16", torch.bfloat16: "bfloat16"}[act]
+    x = np_round(L["x"], act)
+    gw = np_round(L["gate_w"], act)
+    gs = np_round(L["gu_scale"].astype(np.float32), act)
+    ds = np_round(L["dn_scale"].astype(np.float32), act)
+    m = FusedPackedMoE.from_stacked(
+        T(gw, cuda, act), T(L["gu_packed"], cuda), T(gs, cuda, act), T(L["dn_packed"], cuda),
+        T(ds, cuda, act), k, gu_zeros=None if not zp else T(L["gu_zeros"], cuda),
+        dn_zeros=None if not zp else T(L["dn_zeros"], cuda), dtype=act)
+    return L, m, x, gw, gs, ds, name
+
+
+@pytest.mark.parametrize("Tn", [1, 2, 5, 8, 13])
+@pytest.mark.parametrize("group,zp", [(32, False), (128, True)])
+@pytest.mark.parametrize("act", [torch.float16, torch.bfloat16])
+def test_moe_forward_small_vs_oracle(cuda, Tn, group, zp, act):
+    L, m, x, gw, gs, ds, name = _moe_case(cuda, 100 + Tn, 16, 256, 128, 4, group, zp, Tn, act)
+    y = m(T(x, cuda, act)).float().cpu().numpy()
+    w, sel = m.route(T(x, cuda, act))
+    sel = sel.cpu().numpy()
+    w_ref, sel_ref, _ = O.router(x, gw, 4, True, None, name)
+    assert np.array_equal(np.sort(sel, 1), np.sort(sel_ref, 1))
+    ref = O.moe_experts(x, sel_ref, w_ref, L["gu_packed"], gs, L["dn_packed"], ds,
+                        L["gu_zeros"] if zp else None, L["dn_zeros"] if zp else None)
+    assert y.shape == (Tn, 256)
+    assert rel_err(y, ref) <= TOL
+    assert m.device_errors() == 0
+
+
+@pytest.mark.parametrize("Tn,zp", [(1, True), (4, True), (1, False)])
+def test_moe_forward_thinker_geometry_vs_oracle(cuda, Tn, zp):
+    """Config 0: 128 experts, hidden 2048, inter 768, top-8, group 128, fp16."""
+    L, m, x, gw, gs, ds, name = _moe_case(cuda, 0, 128, 2048, 768, 8, 128, zp, Tn, torch.float16)
+    y = m(T(x, cuda, torch.float16)).float().cpu().numpy()
+    w_ref, sel_ref, _ = O.router(x, gw, 8, True, None, name)
+    _, sel = m.route(T(x, cuda, torch.float16))
+    assert np.array_equal(np.sort(sel.cpu().numpy(), 1), np.sort(sel_ref, 1))
+    ref = O.moe_experts(x, sel_ref, w_ref, L["gu_packed"], gs, L["dn_packed"], ds,
+                        L["gu_zeros"] if zp else None, L["dn_zeros"] if zp else None)
+    assert rel_err(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("group", [128, 32])
+def test_moe_forward_vs_reference_golden(cuda, golden_dir, group):
+    """The reference's own FusedPackedMoE(dtype=float32) output at Thinker geometry."""
+    g = np.load(golden_dir / f"golden_moe_thinker_g{group}.npz")
+    L, m, x, gw, gs, ds, name = _moe_case(cuda, int(g["seed"]), 128, 2048, 768, 8, group, False, 1,
+                                          torch.float16)
+    y = m(T(x, cuda, torch.float16)).float().cpu().numpy()
+    _, sel = m.route(T(x, cuda, torch.float16))
+    assert np.array_equal(np.sort(sel.cpu().numpy(), 1), np.sort(g["sel_f32"], 1))
+    assert rel_err(y, g["y_f32"]) <= TOL
+
+
+@pytest.mark.parametrize("group", [32, 128])
+def test_moe_forward_vs_reference_small_golden(cuda, golden_dir, group):
+    from duplex.streaming.fused_packed_moe import FusedPackedMoE
+    g = np.load(golden_dir / f"golden_moe_small_g{group}.npz")
+    k = int(g["top_k"])
+    m = FusedPackedMoE.from_stacked(T(g["gate_w"], cuda), T(g["gu_packed"], cuda),
+                                    T(g["gu_scale"], cuda), T(g["dn_packed"], cuda),
+                                    T(g["dn_scale"], cuda), k, dtype=torch.float16)
+    y = m(T(g["x"], cuda)).float().cpu().numpy()
+    assert rel_err(y, g["y_f32"]) <= TOL
+
+
+def test_moe_block_duck_type_and_installer(cuda):
+    """fuse_packed_moe_blocks finds a per-expert packed SparseMoeBlock and replaces it."""
+    import torch.nn as nn
+    from duplex.streaming.fused_packed_moe import FusedPackedMoE, fuse_packed_moe_blocks
+    E, H, I, k = 8, 256, 64, 2
+    L = synth.moe_layer_np(seed=9, E=E, H=H, I=I, top_k=k, group=32, zero_points=False, T=3)
+
+    class Lin(nn.Module):
+        def __init__(self, p, s, o, i):
+            super().__init__()
+            self.register_buffer("weight_packed", torch.from_numpy(p))
+            self.register_buffer("weight_scale", torch.from_numpy(s))
+            self.register_buffer("weight_shape", torch.tensor([o, i]))
+
+    class Exp(nn.Module):
+        def __init__(self, e):
+            super().__init__()
+            self.gate_proj = Lin(L["gu_packed"][e, :I].copy(), L["gu_scale"][e, :I].copy(), I, H)
+            self.up_proj = Lin(L["gu_packed"][e, I:].copy(), L["gu_scale"][e, I:].copy(), I, H)
+            self.down_proj = Lin(L["dn_packed"][e].copy(), L["dn_scale"][e].copy(), H, I)
+
+    class Qwen3StubSparseMoeBlock(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.experts = nn.ModuleList([Exp(e) for e in range(E)])
+            self.top_k, self.norm_topk_prob = k, True
+            self.gate = nn.Linear(H, E, bias=False)
+            with torch.no_grad():
+                self.gate.weight.copy_(torch.from_numpy(L["gate_w"].astype(np.float32)))
+
+    model = nn.Sequential(nn.Identity(), Qwen3StubSparseMoeBlock())
+    n = fuse_packed_moe_blocks(model, dtype=torch.float16, device=cuda, verbose=False)
+    assert n == 1 and isinstance(model[1], FusedPackedMoE)
+    x = L["x"]
+    y = model[1](T(x, cuda)).float().cpu().numpy()
+    w_ref, sel_ref, _ = O.router(x, L["gate_w"], k, True, None, "float16")
+    ref = O.moe_experts(x, sel_ref, w_ref, L["gu_packed"], L["gu_scale"], L["dn_packed"],
+                        L["dn_scale"])
+    assert rel_err(y, ref) <= TOL
+
+
+def test_moe_graph_capture_and_pdl_bit_identical(cuda):
+    L, m, x, gw, gs, ds, name = _moe_case(cuda, 21, 128, 2048, 768, 8, 128, True, 1, torch.float16)
+    xt = T(x, cuda, torch.float16)
+    m.pdl = False
+    y0 = m(xt).clone()
+    m.pdl = True
+    y1 = m(xt).clone()
+    assert torch.equal(y0, y1)
+    # graph capture / replay with fresh inputs
+    xin = xt.clone()
+    out = torch.empty_like(xt)
+    m.forward_into(xin, out)  # warm (workspace)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            m.forward_into(xin, out)
+    torch.cuda.current_stream().wait_stream(s)
+    for seed in range(3):
+        xn = torch.randn(1, 2048, generator=torch.Generator(device=cuda).manual_seed(seed),
+                         device=cuda).half()
+        xin.copy_(xn)
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, m(xn))
+    assert m.device_errors() == 0
