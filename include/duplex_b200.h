@@ -88,6 +88,8 @@ int duplex_dq_gemv(const void* x, int act_dtype, int64_t x_slot_stride,
  * y[b][r] = round_act(round_act(sum_c W[r][c] x[b][c]) + bias[r]) (+ residual[b][r], fp32 add,
  * one more rounding; not in the reference, used by the clock-path stack).
  * x [B][K] rows x_row_stride apart; out [B][R] rows out_row_stride apart (act dtype).
+ * rms_eps > 0 first RMS-normalises each x row (x * rsqrt(mean(x^2) + rms_eps), rounded to the
+ * act dtype; a weightless RMSNorm, used by the clock-path stack), rms_eps <= 0 leaves x as is.
  * pdl != 0 launches with programmatic dependent launch and prefetches the weights
  * before waiting on the previous kernel.
  */
@@ -95,12 +97,14 @@ int duplex_packed_linear(const void* x, int act_dtype, int32_t B, int64_t x_row_
                          const int32_t* packed, const void* scale, const int32_t* zeros,
                          int scale_dtype, int32_t R, int32_t Rs, int32_t K, int32_t group,
                          const void* bias, const void* residual, int64_t res_row_stride,
-                         void* out, int64_t out_row_stride, int pdl, void* stream);
+                         void* out, int64_t out_row_stride, float rms_eps, int pdl,
+                         void* stream);
 
 /*
  * moe_workspace_bytes -- bytes of scratch the MoE entry points need for T tokens.
  */
-int duplex_moe_workspace_bytes(int32_t T, int32_t E, int32_t I, int32_t top_k, size_t* bytes);
+int duplex_moe_workspace_bytes(int32_t T, int32_t E, int32_t H, int32_t I, int32_t top_k,
+                               size_t* bytes);
 
 /*
  * moe_route -- router of `FusedPackedMoE.forward` (fused_packed_moe.py:195-199):
@@ -109,11 +113,13 @@ int duplex_moe_workspace_bytes(int32_t T, int32_t E, int32_t I, int32_t top_k, s
  * norm_topk != 0.  x [T][H], gate_w [E][H] (act dtype), gate_b [E] or NULL.
  * w_out [T][top_k] fp32, sel_out [T][top_k] int32.  T <= 8, E <= 256, top_k <= 8.
  * workspace: duplex_moe_workspace_bytes bytes, zero-filled once before first use.
+ * rms_eps > 0 routes the RMS-normalised tokens (as packed_linear) and leaves them in the
+ * workspace for the expert kernels.
  */
 int duplex_moe_route(const void* x, int act_dtype, int32_t T, const void* gate_w,
                      const void* gate_b, int32_t E, int32_t H, int32_t top_k,
                      int32_t norm_topk, float* w_out, int32_t* sel_out, void* workspace,
-                     size_t workspace_bytes, int pdl, void* stream);
+                     size_t workspace_bytes, float rms_eps, int pdl, void* stream);
 
 /*
  * moe_forward -- the whole of `FusedPackedMoE.forward` (fused_packed_moe.py:191-275) for
@@ -123,7 +129,8 @@ int duplex_moe_route(const void* x, int act_dtype, int32_t T, const void* gate_w
  * share one pass over its weights.
  * gu_* : [E][2I][H/8] (gate rows 0..I-1, up rows I..2I-1), dn_* : [E][H][I/8].
  * out [T][H] act dtype (+ residual [T][H] when not NULL, fp32 add).  w_out/sel_out as in
- * moe_route (may be NULL).  err: optional device int.
+ * moe_route (may be NULL).  err: optional device int.  rms_eps > 0: the experts see the
+ * RMS-normalised tokens, the residual is added to the un-normalised output.
  */
 int duplex_moe_forward(const void* x, int act_dtype, int32_t T, const void* gate_w,
                        const void* gate_b, int32_t E, int32_t H, int32_t I, int32_t top_k,
@@ -132,7 +139,7 @@ int duplex_moe_forward(const void* x, int act_dtype, int32_t T, const void* gate
                        const void* dn_scale, const int32_t* dn_zeros, int scale_dtype,
                        int32_t group, const void* residual, void* out, float* w_out,
                        int32_t* sel_out, void* workspace, size_t workspace_bytes,
-                       int32_t* err, int pdl, void* stream);
+                       int32_t* err, float rms_eps, int pdl, void* stream);
 
 #ifdef __cplusplus
 }

@@ -74,6 +74,7 @@ struct GemvParams {
   uint32_t smem_stage0;
   int prefetch;
   int x_per_stage;
+  float rms_eps;            // > 0: RMS-normalise the shared activation rows on load
 };
 
 template <int MODE>
@@ -275,6 +276,38 @@ __global__ void __launch_bounds__(kThreads, 2) dq_gemv_kernel(const __grid_const
     for (int idx = tid; idx < n_units * kMaxTokens; idx += kConsumers) unit_w[idx] = p.plan->unit_w[idx];
   }
   named_bar_sync(1, kConsumers);
+  if (!p.x_per_stage && p.rms_eps > 0.f) {
+    // y = round(x * rsqrt(mean(x^2) + eps)) per activation row (weightless RMSNorm)
+    float ss[kMaxTokens];
+#pragma unroll
+    for (int n = 0; n < kMaxTokens; ++n) {
+      float a = 0.f;
+      if (n < p.ncols) {
+        const T* row = reinterpret_cast<const T*>(xsh + (uint32_t)n * p.x_pitch);
+        for (int c = tid; c < p.K; c += kConsumers) {
+          const float v = to_f32<T>(row[c]);
+          a = fmaf(v, v, a);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      ss[n] = a;
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int n = 0; n < kMaxTokens; ++n) red[warp * kMaxTokens + n] = ss[n];
+    }
+    named_bar_sync(1, kConsumers);
+    for (int n = 0; n < p.ncols; ++n) {
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kCW; ++w) tot += red[w * kMaxTokens + n];
+      const float inv = 1.0f / sqrtf(tot / (float)p.K + p.rms_eps);
+      T* row = reinterpret_cast<T*>(xsh + (uint32_t)n * p.x_pitch);
+      for (int c = tid; c < p.K; c += kConsumers) row[c] = from_f32<T>(to_f32<T>(row[c]) * inv);
+    }
+    named_bar_sync(1, kConsumers);
+  }
 
   const int ntiles = tiles_of<MODE>(p, n_units, Rb);
   const int nst = stages_of<MODE>(n_units);
@@ -559,7 +592,8 @@ extern "C" int duplex_packed_linear(const void* x, int act_dtype, int32_t B, int
                                     const int32_t* packed, const void* scale, const int32_t* zeros,
                                     int scale_dtype, int32_t R, int32_t Rs, int32_t K, int32_t group,
                                     const void* bias, const void* residual, int64_t res_row_stride,
-                                    void* out, int64_t out_row_stride, int pdl, void* stream) {
+                                    void* out, int64_t out_row_stride, float rms_eps, int pdl,
+                                    void* stream) {
   int rc = check_weights(packed, scale, zeros, scale_dtype, 1, R, Rs, K, group);
   if (rc) return rc;
   if (!x || !out || B < 1 || B > kMaxTokens) return DUPLEX_ERR_ARG;
@@ -572,6 +606,7 @@ extern "C" int duplex_packed_linear(const void* x, int act_dtype, int32_t B, int
   p.bias = bias; p.residual = residual; p.res_col_stride = res_row_stride;
   p.prefetch = pdl ? 1 : 0;
   p.x_per_stage = 0;
+  p.rms_eps = rms_eps;
   const size_t smem = plan_geometry(p, zeros != nullptr, kDefaultSmemBudget);
   if (!smem) return DUPLEX_ERR_UNSUPPORTED;
   const int tiles = (R + 15) / 16;

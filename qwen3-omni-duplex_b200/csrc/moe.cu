@@ -30,6 +30,8 @@ struct RouteParams {
   const void* gate_w;
   const void* gate_b;
   int T, E, H, top_k, norm;
+  float rms_eps;   // > 0: route on RMS-normalised tokens and publish them in xn
+  void* xn;
   float* w_out;
   int32_t* sel_out;
   float* logits;
@@ -74,6 +76,36 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(const __grid_co
   for (int idx = tid; idx < p.T * nchunk; idx += blockDim.x)
     xs[idx] = reinterpret_cast<const uint4*>(p.x)[idx];
   __syncthreads();
+  if (p.rms_eps > 0.f) {
+    // weightless RMSNorm of every token row, identical in every CTA; CTA 0 publishes
+    // the normalised rows for the gate|up kernel
+    __shared__ float s_ss[kRouteWarps][kMaxTokens];
+    T* xe = reinterpret_cast<T*>(smem);
+    for (int t = 0; t < p.T; ++t) {
+      float a = 0.f;
+      for (int c = tid; c < p.H; c += blockDim.x) {
+        const float v = to_f32<T>(xe[t * p.H + c]);
+        a = fmaf(v, v, a);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      if (lane == 0) s_ss[warp][t] = a;
+    }
+    __syncthreads();
+    for (int t = 0; t < p.T; ++t) {
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kRouteWarps; ++w) tot += s_ss[w][t];
+      const float inv = 1.0f / sqrtf(tot / (float)p.H + p.rms_eps);
+      for (int c = tid; c < p.H; c += blockDim.x)
+        xe[t * p.H + c] = from_f32<T>(to_f32<T>(xe[t * p.H + c]) * inv);
+    }
+    __syncthreads();
+    if (blockIdx.x == 0 && p.xn) {
+      for (int idx = tid; idx < p.T * nchunk; idx += blockDim.x)
+        reinterpret_cast<uint4*>(p.xn)[idx] = xs[idx];
+    }
+  }
 
   if (e < p.E) {
     float acc[kMaxTokens];
@@ -241,6 +273,7 @@ static int launch_route(int act_dtype, const RouteParams& rp, bool pdl, cudaStre
 
 static int check_route(const void* x, int act_dtype, int T, const void* gate_w, int E, int H,
                        int top_k, void* ws, size_t ws_bytes, int I) {
+  if (I < 1) return DUPLEX_ERR_ARG;
   if (!x || !gate_w || !ws) return DUPLEX_ERR_ARG;
   if (act_dtype != DUPLEX_DTYPE_F16 && act_dtype != DUPLEX_DTYPE_BF16) return DUPLEX_ERR_DTYPE;
   if (T < 1 || T > kMaxTokens || E < 1 || E > kMaxExperts || top_k < 1 || top_k > kMaxTopK ||
@@ -248,16 +281,18 @@ static int check_route(const void* x, int act_dtype, int T, const void* gate_w, 
     return DUPLEX_ERR_ARG;
   if ((H & 7) || H > kRouteMaxChunks * 32 * 8) return DUPLEX_ERR_UNSUPPORTED;
   if (!al16(x) || !al16(gate_w) || !al16(ws)) return DUPLEX_ERR_ALIGN;
-  if (ws_bytes < moe_scratch_layout(T, E, I, top_k).total) return DUPLEX_ERR_WORKSPACE;
+  if (ws_bytes < moe_scratch_layout(T, E, H, I, top_k).total) return DUPLEX_ERR_WORKSPACE;
   return DUPLEX_OK;
 }
 
 static RouteParams make_route(const void* x, int T, const void* gate_w, const void* gate_b, int E,
-                              int H, int top_k, int norm, float* w_out, int32_t* sel_out,
-                              uint8_t* ws, const MoeScratch& L) {
+                              int H, int top_k, int norm, float rms_eps, float* w_out,
+                              int32_t* sel_out, uint8_t* ws, const MoeScratch& L) {
   RouteParams rp = {};
   rp.x = x; rp.gate_w = gate_w; rp.gate_b = gate_b;
   rp.T = T; rp.E = E; rp.H = H; rp.top_k = top_k; rp.norm = norm;
+  rp.rms_eps = rms_eps;
+  rp.xn = ws + L.xn;
   rp.w_out = w_out ? w_out : reinterpret_cast<float*>(ws + L.w);
   rp.sel_out = sel_out ? sel_out : reinterpret_cast<int32_t*>(ws + L.sel);
   rp.logits = reinterpret_cast<float*>(ws + L.logits);
@@ -270,22 +305,22 @@ static RouteParams make_route(const void* x, int T, const void* gate_w, const vo
 
 using namespace duplex;
 
-extern "C" int duplex_moe_workspace_bytes(int32_t T, int32_t E, int32_t I, int32_t top_k,
-                                          size_t* bytes) {
-  if (!bytes || T < 1 || E < 1 || I < 1 || top_k < 1) return DUPLEX_ERR_ARG;
-  *bytes = moe_scratch_layout(T, E, I, top_k).total;
+extern "C" int duplex_moe_workspace_bytes(int32_t T, int32_t E, int32_t H, int32_t I,
+                                          int32_t top_k, size_t* bytes) {
+  if (!bytes || T < 1 || E < 1 || H < 1 || I < 1 || top_k < 1) return DUPLEX_ERR_ARG;
+  *bytes = moe_scratch_layout(T, E, H, I, top_k).total;
   return DUPLEX_OK;
 }
 
 extern "C" int duplex_moe_route(const void* x, int act_dtype, int32_t T, const void* gate_w,
                                 const void* gate_b, int32_t E, int32_t H, int32_t top_k,
                                 int32_t norm_topk, float* w_out, int32_t* sel_out, void* workspace,
-                                size_t workspace_bytes, int pdl, void* stream) {
-  int rc = check_route(x, act_dtype, T, gate_w, E, H, top_k, workspace, workspace_bytes, 16);
+                                size_t workspace_bytes, float rms_eps, int pdl, void* stream) {
+  int rc = check_route(x, act_dtype, T, gate_w, E, H, top_k, workspace, workspace_bytes, 1);
   if (rc) return rc;
-  const MoeScratch L = moe_scratch_layout(T, E, 16, top_k);
-  RouteParams rp = make_route(x, T, gate_w, gate_b, E, H, top_k, norm_topk, w_out, sel_out,
-                              reinterpret_cast<uint8_t*>(workspace), L);
+  const MoeScratch L = moe_scratch_layout(T, E, H, 1, top_k);
+  RouteParams rp = make_route(x, T, gate_w, gate_b, E, H, top_k, norm_topk, rms_eps, w_out,
+                              sel_out, reinterpret_cast<uint8_t*>(workspace), L);
   return launch_route(act_dtype, rp, pdl != 0, (cudaStream_t)stream);
 }
 
@@ -296,15 +331,16 @@ extern "C" int duplex_moe_forward(const void* x, int act_dtype, int32_t T, const
                                   const int32_t* dn_packed, const void* dn_scale,
                                   const int32_t* dn_zeros, int scale_dtype, int32_t group,
                                   const void* residual, void* out, float* w_out, int32_t* sel_out,
-                                  void* workspace, size_t workspace_bytes, int32_t* err, int pdl,
-                                  void* stream) {
+                                  void* workspace, size_t workspace_bytes, int32_t* err,
+                                  float rms_eps, int pdl, void* stream) {
   int rc = check_route(x, act_dtype, T, gate_w, E, H, top_k, workspace, workspace_bytes, I);
   if (rc) return rc;
   if (!out || I < 16) return DUPLEX_ERR_ARG;
   if (!al16(out) || (residual && !al16(residual))) return DUPLEX_ERR_ALIGN;
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
-  const MoeScratch L = moe_scratch_layout(T, E, I, top_k);
-  RouteParams rp = make_route(x, T, gate_w, gate_b, E, H, top_k, norm_topk, w_out, sel_out, ws, L);
+  const MoeScratch L = moe_scratch_layout(T, E, H, I, top_k);
+  RouteParams rp = make_route(x, T, gate_w, gate_b, E, H, top_k, norm_topk, rms_eps, w_out,
+                              sel_out, ws, L);
   cudaStream_t st = (cudaStream_t)stream;
   rc = launch_route(act_dtype, rp, pdl != 0, st);
   if (rc) return rc;
@@ -312,6 +348,7 @@ extern "C" int duplex_moe_forward(const void* x, int act_dtype, int32_t T, const
   if (max_units > kMaxUnits) max_units = kMaxUnits;
   return launch_moe_experts(act_dtype, scale_dtype, T, E, H, I, group, gu_packed, gu_scale,
                             gu_zeros, dn_packed, dn_scale, dn_zeros,
-                            reinterpret_cast<const MoePlan*>(ws + L.plan), x, ws + L.act, residual,
+                            reinterpret_cast<const MoePlan*>(ws + L.plan),
+                            rms_eps > 0.f ? (const void*)(ws + L.xn) : x, ws + L.act, residual,
                             out, err, max_units, pdl != 0, st);
 }

@@ -24,12 +24,12 @@ struct MoePlan {
 
 // Scratch layout inside the caller's workspace (all offsets 256-byte aligned).
 struct MoeScratch {
-  size_t counter, logits, plan, w, sel, act, total;
+  size_t counter, logits, plan, w, sel, xn, act, total;
 };
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-inline MoeScratch moe_scratch_layout(int T, int E, int I, int top_k) {
+inline MoeScratch moe_scratch_layout(int T, int E, int H, int I, int top_k) {
   MoeScratch s;
   size_t off = 0;
   s.counter = off; off += 256;
@@ -37,6 +37,7 @@ inline MoeScratch moe_scratch_layout(int T, int E, int I, int top_k) {
   s.plan = off; off += align_up(sizeof(MoePlan), 256);
   s.w = off; off += align_up((size_t)T * top_k * 4, 256);
   s.sel = off; off += align_up((size_t)T * top_k * 4, 256);
+  s.xn = off; off += align_up((size_t)T * H * 2, 256);     // RMS-normalised tokens
   int units = T * top_k < E ? T * top_k : E;
   if (units > kMaxUnits) units = kMaxUnits;
   s.act = off; off += align_up((size_t)units * kMaxTokens * I * 2, 256);

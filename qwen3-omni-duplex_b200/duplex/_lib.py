@@ -20,8 +20,9 @@ LIB_PATH = Path(os.environ.get("DUPLEX_B200_LIB", _PKG / "libduplex_b200.so"))
 DTYPE_F16, DTYPE_BF16, DTYPE_F32 = 0, 1, 2
 DEVERR_EXPERT, DEVERR_TIMEOUT = 1, 2
 
-_c_int, _c_i32, _c_i64, _c_ptr, _c_size = (ctypes.c_int, ctypes.c_int32, ctypes.c_int64,
-                                           ctypes.c_void_p, ctypes.c_size_t)
+_c_int, _c_i32, _c_i64, _c_ptr, _c_size, _c_f32 = (ctypes.c_int, ctypes.c_int32, ctypes.c_int64,
+                                                   ctypes.c_void_p, ctypes.c_size_t,
+                                                   ctypes.c_float)
 
 _SIGNATURES = {
     "duplex_version": ([], _c_int),
@@ -34,15 +35,15 @@ _SIGNATURES = {
                         _c_i32, _c_i32, _c_i32, _c_ptr, _c_i32, _c_ptr, _c_ptr, _c_ptr], _c_int),
     "duplex_packed_linear": ([_c_ptr, _c_int, _c_i32, _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_int,
                               _c_i32, _c_i32, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_i64, _c_ptr,
-                              _c_i64, _c_int, _c_ptr], _c_int),
-    "duplex_moe_workspace_bytes": ([_c_i32, _c_i32, _c_i32, _c_i32,
+                              _c_i64, _c_f32, _c_int, _c_ptr], _c_int),
+    "duplex_moe_workspace_bytes": ([_c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
                                     ctypes.POINTER(ctypes.c_size_t)], _c_int),
     "duplex_moe_route": ([_c_ptr, _c_int, _c_i32, _c_ptr, _c_ptr, _c_i32, _c_i32, _c_i32, _c_i32,
-                          _c_ptr, _c_ptr, _c_ptr, _c_size, _c_int, _c_ptr], _c_int),
+                          _c_ptr, _c_ptr, _c_ptr, _c_size, _c_f32, _c_int, _c_ptr], _c_int),
     "duplex_moe_forward": ([_c_ptr, _c_int, _c_i32, _c_ptr, _c_ptr, _c_i32, _c_i32, _c_i32,
                             _c_i32, _c_i32, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
                             _c_int, _c_i32, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size,
-                            _c_ptr, _c_int, _c_ptr], _c_int),
+                            _c_ptr, _c_f32, _c_int, _c_ptr], _c_int),
 }
 
 _lib = None

@@ -1,0 +1,111 @@
+"""Helpers of the benchmark harness: rank plumbing, max-over-ranks timing, clock sampling."""
+
+from __future__ import annotations
+
+import os
+import statistics
+import subprocess
+import threading
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def init_dist(backend: str, timeout_s: int = 120):
+    ws, rank, _ = dist_env()
+    if ws > 1 and not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group(backend, timeout=timedelta(seconds=timeout_s))
+    return ws, rank
+
+
+def barrier():
+    if dist.is_available() and dist.is_initialized():
+        dist.barrier()
+
+
+def max_over_ranks(value: float, device=None) -> float:
+    """Max of a per-rank float over all ranks (identity without a process group)."""
+    if not (dist.is_available() and dist.is_initialized()):
+        return float(value)
+    t = torch.tensor([float(value)], dtype=torch.float64,
+                     device=device if device is not None else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+
+class ClockSampler:
+    """nvidia-smi sampling (every `ms`) of SM clock and throttle reasons while a
+    workload runs; `summary()` gives median SM MHz, max MHz and active reasons."""
+
+    def __init__(self, indices=None, ms: int = 100):
+        self.indices, self.ms = indices, ms
+        self.rows, self.proc, self.thread = [], None, None
+
+    def start(self):
+        cmd = ["nvidia-smi", f"--query-gpu={QUERY}", "--format=csv,noheader,nounits",
+               "-lms", str(self.ms)]
+        if self.indices:
+            cmd += ["-i", ",".join(str(i) for i in self.indices)]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                         text=True)
+        except OSError:
+            self.proc = None
+            return self
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+        return self
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        pw = [float(r[3]) for r in self.rows if r[3].replace(".", "").isdigit()]
+        active = sorted({name for r in self.rows for name, v in zip(REASONS, r[5:9])
+                         if v.strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(pw) if pw else None,
+                "reasons": active, "samples": len(self.rows)}
+
+
+def visible_gpu_indices(n: int):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if all(i.isdigit() for i in ids):
+            return [int(i) for i in ids[:n]]
+    return list(range(n))

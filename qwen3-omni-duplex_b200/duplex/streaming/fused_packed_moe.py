@@ -163,14 +163,15 @@ class FusedPackedMoE(nn.Module):
         ws = self._ws.get((T, device))
         if ws is None:
             n = _lib.ctypes.c_size_t()
-            _lib.call("duplex_moe_workspace_bytes", T, self.num_experts, self.inter, self.top_k,
-                      _lib.ctypes.byref(n))
+            _lib.call("duplex_moe_workspace_bytes", T, self.num_experts, self.hidden, self.inter,
+                      self.top_k, _lib.ctypes.byref(n))
             ws = torch.zeros(n.value, dtype=torch.uint8, device=device)
             self._ws[(T, device)] = ws
         return ws
 
-    def forward_into(self, x, out, residual=None, w_out=None, sel_out=None):
-        """x [T<=8, H] -> out [T, H] (+ residual), no host synchronisation."""
+    def forward_into(self, x, out, residual=None, w_out=None, sel_out=None, rms_eps=0.0):
+        """x [T<=8, H] -> out [T, H] (+ residual), no host synchronisation.  rms_eps > 0 routes
+        and computes on the RMS-normalised x (clock-path stack)."""
         T = x.shape[0]
         ws = self.workspace(T, x.device)
         g = self.gate
@@ -181,7 +182,8 @@ class FusedPackedMoE(nn.Module):
             _lib.ptr(self.gu_zeros), _lib.ptr(self.down_packed), _lib.ptr(self.down_scale),
             _lib.ptr(self.down_zeros), _lib.dtype_code(self.gu_scale.dtype), self.group,
             _lib.ptr(residual), _lib.ptr(out), _lib.ptr(w_out), _lib.ptr(sel_out), _lib.ptr(ws),
-            ws.numel(), _lib.ptr(self.err), 1 if self.pdl else 0, _lib.stream_of(x))
+            ws.numel(), _lib.ptr(self.err), float(rms_eps), 1 if self.pdl else 0,
+            _lib.stream_of(x))
         return out
 
     def route(self, hidden_states):
@@ -197,7 +199,8 @@ class FusedPackedMoE(nn.Module):
             _lib.call("duplex_moe_route", _lib.ptr(xs), _lib.dtype_code(x.dtype), xs.shape[0],
                       _lib.ptr(g.weight), _lib.ptr(g.bias), self.num_experts, self.hidden,
                       self.top_k, 1 if self.norm_topk_prob else 0, _lib.ptr(w[t0:t0 + 8]),
-                      _lib.ptr(sel[t0:t0 + 8]), _lib.ptr(ws), ws.numel(), 0, _lib.stream_of(x))
+                      _lib.ptr(sel[t0:t0 + 8]), _lib.ptr(ws), ws.numel(), 0.0, 0,
+                      _lib.stream_of(x))
         return w, sel
 
     def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:

@@ -139,10 +139,16 @@ class TritonPackedLinear(torch.nn.Module):
                              persistent=False)
         self.pdl = False
 
-    def forward(self, x, residual=None, out=None):
+    def forward(self, x, residual=None, out=None, rms_eps: float = 0.0, x_row_stride=None):
+        """y = x W^T (+ bias).  Extensions used by the clock-path stack: `residual` is added
+        in fp32, `rms_eps > 0` RMS-normalises each input row first, `out` receives y."""
         _lib.require_cuda(x)
         lead, K = x.shape[:-1], x.shape[-1]
-        flat = _lib.aligned(x.reshape(-1, K))
+        if x_row_stride is not None and x.dim() == 2 and x.stride(1) == 1:
+            flat, xs = x, x_row_stride      # strided row view (e.g. q out of a fused qkv)
+        else:
+            flat = _lib.aligned(x.reshape(-1, K))
+            xs = K
         N = flat.shape[0]
         y = out if out is not None else torch.empty(N, self.out_features, device=x.device,
                                                     dtype=x.dtype)
@@ -153,12 +159,12 @@ class TritonPackedLinear(torch.nn.Module):
             b = min(8, N - r0)
             xr = flat[r0:r0 + b]
             yr = y[r0:r0 + b]
-            _lib.call("duplex_packed_linear", _lib.ptr(xr), _lib.dtype_code(x.dtype), b, K,
+            _lib.call("duplex_packed_linear", _lib.ptr(xr), _lib.dtype_code(x.dtype), b, xs,
                       _lib.ptr(self.packed), _lib.ptr(self.scale), _lib.ptr(self.zeros),
                       _lib.dtype_code(self.scale.dtype), self.out_features, self.rows_alloc,
                       K, self.group, _lib.ptr(bias),
                       None if res is None else _lib.ptr(res[r0:r0 + b]), self.out_features,
-                      _lib.ptr(yr), self.out_features, 1 if self.pdl else 0, st)
+                      _lib.ptr(yr), self.out_features, float(rms_eps), 1 if self.pdl else 0, st)
         return y.view(*lead, self.out_features)
 
 

@@ -48,8 +48,8 @@ def test_bad_arguments_are_rejected_without_cuda(lib):
     assert lib.duplex_unpack4(null, 1, 1, 8, null, null) == 1
     assert lib.duplex_dequant(null, null, 0, null, 1, 64, 32, null, 0, null) == 1
     n = ctypes.c_size_t()
-    assert lib.duplex_moe_workspace_bytes(0, 128, 768, 8, ctypes.byref(n)) == 1
-    assert lib.duplex_moe_workspace_bytes(1, 128, 768, 8, ctypes.byref(n)) == 0
+    assert lib.duplex_moe_workspace_bytes(0, 128, 2048, 768, 8, ctypes.byref(n)) == 1
+    assert lib.duplex_moe_workspace_bytes(1, 128, 2048, 768, 8, ctypes.byref(n)) == 0
     assert n.value > 0
 
 
@@ -58,27 +58,27 @@ def test_unsupported_shapes_are_rejected(lib):
     p = ctypes.c_void_p(1 << 20)
     # K not a multiple of 32
     assert lib.duplex_packed_linear(p, 0, 1, 48, p, p, None, 0, 16, 16, 48, 32, None, None, 0, p,
-                                    16, 0, None) == 6
+                                    16, 0.0, 0, None) == 6
     # rows per expert not a multiple of 16
     assert lib.duplex_packed_linear(p, 0, 1, 64, p, p, None, 0, 10, 10, 64, 32, None, None, 0, p,
-                                    10, 0, None) == 6
+                                    10, 0.0, 0, None) == 6
     # batch > 8
     assert lib.duplex_packed_linear(p, 0, 9, 64, p, p, None, 0, 16, 16, 64, 32, None, None, 0, p,
-                                    16, 0, None) == 1
+                                    16, 0.0, 0, None) == 1
     # misaligned activation pointer
     q = ctypes.c_void_p((1 << 20) + 8)
     assert lib.duplex_packed_linear(q, 0, 1, 64, p, p, None, 0, 16, 16, 64, 32, None, None, 0, p,
-                                    16, 0, None) == 2
+                                    16, 0.0, 0, None) == 2
     # bad dtype
     assert lib.duplex_packed_linear(p, 0, 1, 64, p, p, None, 7, 16, 16, 64, 32, None, None, 0, p,
-                                    16, 0, None) == 3
+                                    16, 0.0, 0, None) == 3
     # router: T > 8, top_k > E
-    assert lib.duplex_moe_route(p, 0, 9, p, None, 128, 2048, 8, 1, None, None, p, 1 << 30, 0,
+    assert lib.duplex_moe_route(p, 0, 9, p, None, 128, 2048, 8, 1, None, None, p, 1 << 30, 0.0, 0,
                                 None) == 1
-    assert lib.duplex_moe_route(p, 0, 1, p, None, 4, 2048, 8, 1, None, None, p, 1 << 30, 0,
+    assert lib.duplex_moe_route(p, 0, 1, p, None, 4, 2048, 8, 1, None, None, p, 1 << 30, 0.0, 0,
                                 None) == 1
     # workspace too small
-    assert lib.duplex_moe_route(p, 0, 1, p, None, 128, 2048, 8, 1, None, None, p, 16, 0,
+    assert lib.duplex_moe_route(p, 0, 1, p, None, 128, 2048, 8, 1, None, None, p, 16, 0.0, 0,
                                 None) == 4
 
 

@@ -1,0 +1,60 @@
+"""GPU parity of the clock-path stack (fused qkv, o, MoE per layer, RMSNorm inputs)
+against the numpy restatement, plus graph replay and the host-buffer decode call."""
+
+import numpy as np
+import pytest
+import torch
+
+from duplex import synth
+from oracle.clock_oracle import clock_layer
+
+pytestmark = pytest.mark.gpu
+
+
+def small_layers(n, seed=3, H=256, q=256, kv=64, E=16, I=128, top_k=4, group=128):
+    rng = np.random.Generator(np.random.PCG64(seed))
+    out = []
+    for l in range(n):
+        a = synth.linear_np(rng, q + 2 * kv, H, group, True)
+        b = synth.linear_np(rng, H, q, group, True)
+        m = synth.moe_layer_np(seed=seed * 100 + l, E=E, H=H, I=I, top_k=top_k, group=group)
+        d = dict(qkv_packed=a["packed"], qkv_scale=a["scale"], qkv_zeros=a["zeros"],
+                 o_packed=b["packed"], o_scale=b["scale"], o_zeros=b["zeros"])
+        for k in ("gate_w", "gu_packed", "gu_scale", "gu_zeros", "dn_packed", "dn_scale",
+                  "dn_zeros"):
+            d[k] = m[k]
+        out.append(d)
+    return out
+
+
+@pytest.mark.parametrize("T", [1, 3])
+def test_clock_stack_vs_oracle(cuda, T):
+    from duplex.clock import ClockStack
+    layers = small_layers(3)
+    st = ClockStack.from_arrays(layers, top_k=4, device=cuda, T=T)
+    x = np.random.default_rng(1).standard_normal((T, 256)).astype(np.float16)
+    out = torch.zeros(T, 256, device=cuda, dtype=torch.float16)
+    st.step_into(torch.from_numpy(x).to(cuda), out)
+    h = x.astype(np.float32)
+    for d in layers:
+        h, _ = clock_layer(h, d, 4)
+    y = out.float().cpu().numpy()
+    assert np.isfinite(y).all()
+    assert np.abs(y - h).max() <= 2e-3 * np.abs(h).max()
+    assert st.device_errors() == 0
+
+
+def test_clock_stack_graph_and_decode(cuda):
+    from duplex.clock import ClockStack
+    st = ClockStack.synthetic(n_layers=2, seed=0, device=cuda)
+    st.capture()
+    x = torch.randn(1, 2048, device=cuda, dtype=torch.float16)
+    eager = torch.zeros_like(x)
+    st.step_into(x, eager)
+    xh = x.cpu().pin_memory()
+    oh = torch.empty(1, 2048, dtype=torch.float16).pin_memory()
+    st.decode(xh, oh)
+    torch.cuda.synchronize()
+    assert torch.equal(oh, eager.cpu())
+    assert torch.isfinite(eager).all()
+    assert st.device_errors() == 0

@@ -14,7 +14,10 @@ from duplex import synth
 
 pytestmark = pytest.mark.gpu
 
-TOL = 2e-3          # max|d| / max|y_ref| for fp32-accumulated layer outputs
+TOL = 2e-3          # max|d| / max|y_ref| for fp32-accumulated layer outputs, fp16 I/O
+# bf16 I/O: rounding the output alone costs up to 2^-9 = 1.95e-3 of max|y|, so the bar is
+# 8e-3 (the reference's own bf16 path deviates 1.07e-2 / 9.1e-3 for g32 / g128)
+TOL_BF16 = 8e-3
 GEMV_TOL = 2e-5     # single dequant-GEMV: exact products, fp32 sums
 
 
@@ -185,7 +188,7 @@ def test_route_selection_bit_exact_on_exact_logits(cuda):
 
 def test_route_random_tokens_flip_rate(cuda):
     from duplex.streaming.fused_packed_moe import FusedPackedMoE
-    L = synth.moe_layer_np(seed=11, E=128, H=2048, I=64, top_k=8, group=128, zero_points=True,
+    L = synth.moe_layer_np(seed=11, E=128, H=2048, I=128, top_k=8, group=128, zero_points=True,
                            T=8)
     m = FusedPackedMoE.from_stacked(T(L["gate_w"], cuda), T(L["gu_packed"], cuda),
                                     T(L["gu_scale"], cuda), T(L["dn_packed"], cuda),
@@ -232,7 +235,7 @@ def test_moe_forward_small_vs_oracle(cuda, Tn, group, zp, act):
     ref = O.moe_experts(x, sel_ref, w_ref, L["gu_packed"], gs, L["dn_packed"], ds,
                         L["gu_zeros"] if zp else None, L["dn_zeros"] if zp else None)
     assert y.shape == (Tn, 256)
-    assert rel_err(y, ref) <= TOL
+    assert rel_err(y, ref) <= (TOL if act == torch.float16 else TOL_BF16)
     assert m.device_errors() == 0
 
 
