@@ -14,8 +14,8 @@
  *   zeros  [E][Rs][ceil(G/8)] int32 or NULL -- 4-bit zero point per (row, group), same
  *          nibble order along the group axis; NULL means zero point 8 everywhere,
  *          which is the reference's symmetric format (value = nibble - 8).
- * Rs (rows allocated per expert) must be a multiple of 16 and >= R (rows used);
- * K % 32 == 0; group % 32 == 0; every base pointer 16-byte aligned.
+ * The GEMV entry points read it after a one-time repack into tile records
+ * (duplex_repack_tiles).  K % 32 == 0; group 32 or 64 * 2^k; base pointers 16-byte aligned.
  *
  * Activations are fp16 or bf16 (DUPLEX_DTYPE_*), accumulation is fp32.
  */
@@ -70,23 +70,39 @@ int duplex_dequant(const int32_t* packed, const void* scale, int scale_dtype,
                    void* out, int out_dtype, void* stream);
 
 /*
+ * tile_record_bytes / repack_tiles -- the one-time weight preparation (the reference
+ * restacks its experts once at module construction, fused_packed_moe.py:68-80,117-123).
+ * A stacked int4 matrix in the reference layout (packed [E][R][K/8] int32, scale
+ * [E][R][G] fp16|bf16, zeros [E][R][ceil(G/8)] int32 or NULL) is rewritten into one
+ * record per (expert, 16-row block): fragment-ordered nibbles, pair-interleaved scales
+ * and zero points, padded to 128 bytes (layout: csrc/tiles.cuh).  tiles must hold
+ * E * ceil(R/16) * record_bytes bytes.  pair_halves != 0 (gate|up stacks, R % 32 == 0)
+ * places row block j of the first half next to row block j of the second half.
+ * K % 32 == 0; group 32 or 64 * 2^k.
+ */
+int duplex_tile_record_bytes(int32_t K, int32_t group, int has_zeros, size_t* bytes);
+int duplex_repack_tiles(const int32_t* packed, const void* scale, const int32_t* zeros,
+                        int scale_dtype, int32_t E, int32_t R, int32_t K, int32_t group,
+                        int32_t pair_halves, void* tiles, size_t tiles_bytes, void* stream);
+
+/*
  * dq_gemv -- reference `dequant_gemv` (src/duplex/streaming/triton_dequant_gemv.py:85-113).
- * out[j][r] = sum_c W[sel[j]][r][c] * x_j[c] in fp32 for r < R.
+ * out[j][r] = sum_c W[sel[j]][r][c] * x_j[c] in fp32 for r < R, W given as tiles
+ * (repack_tiles with pair_halves = 0).
  * x: [K] shared by all slots (x_slot_stride = 0) or [nsel][x_slot_stride] rows.
  * sel: [nsel] int32 expert ids (device).  out: [nsel][R] fp32.
  * err: optional device int (bit DUPLEX_DEVERR_EXPERT when a sel id is out of range).
  */
-int duplex_dq_gemv(const void* x, int act_dtype, int64_t x_slot_stride,
-                   const int32_t* packed, const void* scale, const int32_t* zeros,
-                   int scale_dtype, int32_t E, int32_t R, int32_t Rs, int32_t K,
-                   int32_t group, const int32_t* sel, int32_t nsel, float* out,
-                   int32_t* err, void* stream);
+int duplex_dq_gemv(const void* x, int act_dtype, int64_t x_slot_stride, const void* tiles,
+                   int scale_dtype, int has_zeros, int32_t E, int32_t R, int32_t K,
+                   int32_t group, const int32_t* sel, int32_t nsel, float* out, int32_t* err,
+                   void* stream);
 
 /*
  * packed_linear -- reference `TritonPackedLinear.forward` (triton_dequant_gemv.py:151-159)
  * for B <= 8 rows in one launch (the reference launches once per row):
- * y[b][r] = round_act(round_act(sum_c W[r][c] x[b][c]) + bias[r]) (+ residual[b][r], fp32 add,
- * one more rounding; not in the reference, used by the clock-path stack).
+ * y[b][r] = round_act(round_act(sum_c W[r][c] x[b][c]) + bias[r]) (+ residual[b][r], one
+ * more rounding; not in the reference, used by the clock-path stack).  W as tiles (E = 1).
  * x [B][K] rows x_row_stride apart; out [B][R] rows out_row_stride apart (act dtype).
  * rms_eps > 0 first RMS-normalises each x row (x * rsqrt(mean(x^2) + rms_eps), rounded to the
  * act dtype; a weightless RMSNorm, used by the clock-path stack), rms_eps <= 0 leaves x as is.
@@ -94,11 +110,10 @@ int duplex_dq_gemv(const void* x, int act_dtype, int64_t x_slot_stride,
  * before waiting on the previous kernel.
  */
 int duplex_packed_linear(const void* x, int act_dtype, int32_t B, int64_t x_row_stride,
-                         const int32_t* packed, const void* scale, const int32_t* zeros,
-                         int scale_dtype, int32_t R, int32_t Rs, int32_t K, int32_t group,
-                         const void* bias, const void* residual, int64_t res_row_stride,
-                         void* out, int64_t out_row_stride, float rms_eps, int pdl,
-                         void* stream);
+                         const void* tiles, int scale_dtype, int has_zeros, int32_t R,
+                         int32_t K, int32_t group, const void* bias, const void* residual,
+                         int64_t res_row_stride, void* out, int64_t out_row_stride,
+                         float rms_eps, int pdl, void* stream);
 
 /*
  * moe_workspace_bytes -- bytes of scratch the MoE entry points need for T tokens.
@@ -127,17 +142,17 @@ int duplex_moe_route(const void* x, int act_dtype, int32_t T, const void* gate_w
  * dequant-GEMV with the routing-weighted combine epilogue, three launches chained by
  * programmatic dependent launch when pdl != 0.  Tokens that pick the same expert
  * share one pass over its weights.
- * gu_* : [E][2I][H/8] (gate rows 0..I-1, up rows I..2I-1), dn_* : [E][H][I/8].
+ * gu_tiles: repack_tiles of [E][2I][H/8] (gate rows 0..I-1, up rows I..2I-1) with
+ * pair_halves = 1; dn_tiles: repack_tiles of [E][H][I/8].  Same group and zero-point use.
  * out [T][H] act dtype (+ residual [T][H] when not NULL, fp32 add).  w_out/sel_out as in
  * moe_route (may be NULL).  err: optional device int.  rms_eps > 0: the experts see the
  * RMS-normalised tokens, the residual is added to the un-normalised output.
  */
 int duplex_moe_forward(const void* x, int act_dtype, int32_t T, const void* gate_w,
                        const void* gate_b, int32_t E, int32_t H, int32_t I, int32_t top_k,
-                       int32_t norm_topk, const int32_t* gu_packed, const void* gu_scale,
-                       const int32_t* gu_zeros, const int32_t* dn_packed,
-                       const void* dn_scale, const int32_t* dn_zeros, int scale_dtype,
-                       int32_t group, const void* residual, void* out, float* w_out,
+                       int32_t norm_topk, const void* gu_tiles, const void* dn_tiles,
+                       int scale_dtype, int has_zeros, int32_t group, const void* residual,
+                       void* out, float* w_out,
                        int32_t* sel_out, void* workspace, size_t workspace_bytes,
                        int32_t* err, float rms_eps, int pdl, void* stream);
 

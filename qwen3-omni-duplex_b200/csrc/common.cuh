@@ -124,7 +124,7 @@ DEVI void ldsm_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, uint32
 
 DEVI uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {  // (a & b) | c
   uint32_t d;
-  asm volatile("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
   return d;
 }
 
@@ -133,7 +133,7 @@ template <typename T> struct MmaOp;
 template <> struct MmaOp<__half> {
   static DEVI void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                        uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
         "{%8,%9}, {%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -144,7 +144,7 @@ template <> struct MmaOp<__half> {
 template <> struct MmaOp<__nv_bfloat16> {
   static DEVI void run(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                        uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
         "{%8,%9}, {%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -239,6 +239,79 @@ template <> struct Dq<__nv_bfloat16> {
     DQ_BF16(B[2], wa >> 12, ca)
     DQ_BF16(B[3], wb >> 12, cb)
 #undef DQ_BF16
+  }
+};
+
+// Offset dequant (no subtraction in the inner loop): the A operands hold M + n,
+// exact in the 16-bit type.  fp16: M = 1024 for the low nibble of each byte and
+// 1024 + 16n for the high nibble, whose activations are stored pre-divided by 16,
+// so sum_k A.x = 1024 X_even + 64 X_odd + sum n.x over a group (X_even / X_odd: the
+// group's activation sums over even / odd columns).  bf16 (7-bit mantissa):
+// every nibble is shifted down first and M = 128, giving 128 X + sum n.x.  One
+// extra MMA per column pair with `corr_a` coefficients and exact multi-part sums
+// as B subtracts (M + z) X, which also applies the zero point.  The column sums
+// are kept per 64-column pair, so the correction is exact however a group's pairs
+// are split between warps.
+template <typename T> struct DqOff;
+
+template <> struct DqOff<__half> {
+  static constexpr bool kOddDiv16 = true;
+  static DEVI void expand(uint32_t wa, uint32_t wb, uint32_t (&A)[4], uint32_t (&B)[4]) {
+    const uint32_t MAG = 0x64006400u, M_LO = 0x000F000Fu, M_HI = 0x00F000F0u;
+    A[0] = lop3_and_or(wa, M_LO, MAG);
+    A[1] = lop3_and_or(wb, M_LO, MAG);
+    A[2] = lop3_and_or(wa, M_HI, MAG);
+    A[3] = lop3_and_or(wb, M_HI, MAG);
+    const uint32_t sa = wa >> 8, sb = wb >> 8;
+    B[0] = lop3_and_or(sa, M_LO, MAG);
+    B[1] = lop3_and_or(sb, M_LO, MAG);
+    B[2] = lop3_and_or(sa, M_HI, MAG);
+    B[3] = lop3_and_or(sb, M_HI, MAG);
+  }
+  // correction coefficients of one column pair, lane (g, t): k = 2t, 2t+1 carry
+  // window t/2; even t -> -(1024 + z), odd t -> -(64 + z), rows g (a0) and g+8 (a1).
+  // `wmask` bit h keeps window h (both set unless each window is its own group).
+  static DEVI void corr_a(uint32_t za, uint32_t zb, int t, uint32_t wmask, uint32_t& a0,
+                          uint32_t& a1) {
+    uint32_t ca = 0, cb = 0;
+    if ((wmask >> (t >> 1)) & 1u) {
+      if ((t & 1) == 0) {
+        ca = 0xE400u | za;
+        cb = 0xE400u | zb;
+      } else {
+        ca = 0xD400u | (za << 4);
+        cb = 0xD400u | (zb << 4);
+      }
+    }
+    a0 = ca | (ca << 16);
+    a1 = cb | (cb << 16);
+  }
+};
+
+template <> struct DqOff<__nv_bfloat16> {
+  static constexpr bool kOddDiv16 = false;
+  static DEVI void expand(uint32_t wa, uint32_t wb, uint32_t (&A)[4], uint32_t (&B)[4]) {
+    const uint32_t MAG = 0x43004300u, M_LO = 0x000F000Fu;
+    A[0] = lop3_and_or(wa, M_LO, MAG);
+    A[1] = lop3_and_or(wb, M_LO, MAG);
+    A[2] = lop3_and_or(wa >> 4, M_LO, MAG);
+    A[3] = lop3_and_or(wb >> 4, M_LO, MAG);
+    B[0] = lop3_and_or(wa >> 8, M_LO, MAG);
+    B[1] = lop3_and_or(wb >> 8, M_LO, MAG);
+    B[2] = lop3_and_or(wa >> 12, M_LO, MAG);
+    B[3] = lop3_and_or(wb >> 12, M_LO, MAG);
+  }
+  // -(128 + z) on every lane of a kept window (three-part column sum per window:
+  // k = 4h .. 4h+2 for window h)
+  static DEVI void corr_a(uint32_t za, uint32_t zb, int t, uint32_t wmask, uint32_t& a0,
+                          uint32_t& a1) {
+    uint32_t ca = 0, cb = 0;
+    if ((wmask >> (t >> 1)) & 1u) {
+      ca = 0xC300u | za;
+      cb = 0xC300u | zb;
+    }
+    a0 = ca | (ca << 16);
+    a1 = cb | (cb << 16);
   }
 };
 

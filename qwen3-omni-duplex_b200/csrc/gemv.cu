@@ -1,63 +1,71 @@
-// int4 dequant-GEMV family for batch <= 8 on sm_100a.
+// int4 dequant-GEMV family for batch <= 8 on sm_100a, over tile records (tiles.cuh).
 //
 // One persistent CTA per SM = 8 consumer warps + 1 producer warp.
 //
-// Producer: streams "stages" = 16 weight rows x full K of one expert, straight
-// from the reference's packed layout [E][Rs][K/8] int32 (rows are contiguous
-// K/2 bytes), plus the 16 rows' group scales and zero points, with 1-D bulk
-// copies (cp.async.bulk, no multicast) into a ring of shared-memory stages.
-// Weight rows land at a pitch of an odd number of 16-byte units so ldmatrix
-// reads of 8 rows hit 8 distinct bank groups.  Weights never exist in a
-// dequantised form outside registers.
+// Producer (one lane): a stage is one tile record (16 weight rows x all K, with
+// their scales and zero points) or two adjacent records (gate block + up block),
+// fetched with ONE 1-D bulk copy (cp.async.bulk, no multicast) into a ring of
+// shared-memory stages; per-stage activations (down projection: one row per
+// token) follow with one bulk copy per row.  Completion is mbarrier transaction
+// bytes; stages are recycled through a second mbarrier per slot.
 //
-// Consumers: every consumer warp owns a fixed slice of the K windows (32
-// columns each) of every stage (split-K).  Per window: one ldmatrix.x2 gives the
-// lane the packed word of row g and row g+8, the nibbles become exact 16-bit
-// (n - z) integers in registers (Dq<T>), and two m16n8k16 MMAs multiply them by
-// the activations, whose 8 batch rows are the MMA's N dimension.  Group scales
-// are applied in fp32 when the group changes.  Partial sums of the 8 warps are
-// reduced through shared memory once per output tile.
+// Consumers: the work of a stage is split into items = (record, 64-column pair);
+// warp w takes items w, w+8, ...  Per item a lane does one 16-byte shared load of
+// its weight words (rows g and g+8, two 32-column windows), two 16-byte loads of
+// activation fragments, turns the nibbles into exact 16-bit (n - z) values in
+// registers (Dq<T>) and issues four m16n8k16 MMAs (the 8 batch rows are the N
+// dimension), alternating two accumulator chains.  Group scales (and, in the MoE
+// down projection, the per-token routing weights) are applied in fp32 per item.
+// Warps' partial sums meet in shared memory once per output tile.
 //
-// Modes (template):
-//   kPlain  : out[j][r] fp32 = W[sel[j]] . x_j           (dequant_gemv)
-//   kLinear : dense rows, bias / residual epilogue       (TritonPackedLinear)
-//   kGateUp : unit u rows [rb] and [I+rb] -> act = silu(gate) * up   (MoE)
-//   kDown   : all units of one row block, routing-weighted combine   (MoE)
+// Modes:
+//   kPlain  : out[j][r] fp32 = W[sel[j]] . x_j                    (dequant_gemv)
+//   kLinear : y[b][r] = round(round(W . x_b) + bias) (+ residual)    (TritonPackedLinear)
+//   kGateUp : unit u, row block j: act = silu(gate) * up, written in fragment order
+//   kDown   : row block j over all units, routing-weighted combine (+ residual)
 //
-// PDL: kLinear/kDown issue their weight copies before griddepcontrol.wait (the
-// weights do not depend on the previous kernel); kDown reads the routing plan
-// before the wait because the gate|up kernel only triggers its dependents after
-// its own wait on the router has returned.
+// PDL: kLinear / kDown issue their weight copies before griddepcontrol.wait;
+// kDown also reads the routing plan there, because the gate|up kernel triggers
+// its dependents only after its own wait on the router has returned.
 #include "common.cuh"
 #include "moe.cuh"
+#include "tiles.cuh"
+
+#include <mutex>
+#include <set>
+#include <utility>
 
 namespace duplex {
 
-constexpr int kCW = 8;  // consumer warps
+constexpr int kCW = 16;  // consumer warps
 constexpr int kConsumers = kCW * 32;
 constexpr int kThreads = kConsumers + 32;
 constexpr int kStagesMax = 16;
 
 enum : int { kPlain = 0, kLinear = 1, kGateUp = 2, kDown = 3 };
+enum : int { kXShared = 0, kXStageFrag = 1, kXStageRaw = 2 };
 
 // fixed shared-memory map (bytes)
 constexpr uint32_t kOffFull = 0;       // kStagesMax mbarriers
 constexpr uint32_t kOffEmpty = 128;    // kStagesMax mbarriers
 constexpr uint32_t kOffAbort = 256;    // int
+constexpr uint32_t kOffNUnits = 260;   // int
 constexpr uint32_t kOffXslot = 320;    // kStagesMax ints (producer bookkeeping)
-constexpr uint32_t kOffUnitW = 512;    // kMaxUnits * kMaxTokens floats (2048 B)
-constexpr uint32_t kOffRed = 2560;     // kCW * 8 * 32 floats (8192 B)
-constexpr uint32_t kOffXsh = 10752;    // shared activations, then the stage ring
+constexpr uint32_t kOffUnitE = 384;    // kMaxUnits ints
+constexpr uint32_t kOffUnitM = 640;    // kMaxUnits uints
+constexpr uint32_t kOffUnitW = 1024;   // kMaxUnits * kMaxTokens floats
+constexpr uint32_t kOffRed = 3072;     // kCW * 8 * 32 floats
+constexpr uint32_t kOffCorr = kOffRed + kCW * 8 * 32 * 4;  // npairs x 32 correction words
 
 struct GemvParams {
-  const int32_t* packed;
-  const void* scale;
-  const int32_t* zeros;
-  int E, R, Rs, K, G, GZ, group;
+  const uint8_t* tiles;
+  int E, R, Rb;          // rows used, records per expert
+  TileGeom tg;
   const void* x;
   long long x_col_stride;   // elements between batch columns
   long long x_slot_stride;  // elements between slots / units (per-stage activations)
   int ncols;
+  int x_mode;
   const int32_t* sel;
   int nslots;
   const MoePlan* plan;
@@ -68,50 +76,47 @@ struct GemvParams {
   const void* residual;
   long long res_col_stride;
   int* err;
-  int nstages;
-  uint32_t row_pitch, off_scale, off_zero, off_x, stage_bytes, x_pitch;
-  uint32_t wbytes, sbytes, zbytes, xbytes_row;
-  uint32_t smem_stage0;
+  int nstages, nrec;
+  uint32_t stage_bytes, off_x, x_pitch, xbytes_row, smem_stage0, off_xsh;
   int prefetch;
-  int x_per_stage;
-  float rms_eps;            // > 0: RMS-normalise the shared activation rows on load
+  float rms_eps;
 };
 
 template <int MODE>
-DEVI int tiles_of(const GemvParams& p, int n_units, int Rb) {
-  if (MODE == kPlain) return p.nslots * Rb;
-  if (MODE == kLinear) return Rb;
-  if (MODE == kGateUp) return n_units * (p.I >> 4);
-  return Rb;  // kDown
+DEVI int tiles_of(const GemvParams& p, int n_units) {
+  if (MODE == kPlain) return p.nslots * p.Rb;
+  if (MODE == kLinear) return p.Rb;
+  if (MODE == kGateUp) return n_units * (p.Rb >> 1);
+  return p.Rb;  // kDown
 }
 
 template <int MODE>
 DEVI int stages_of(int n_units) {
-  return MODE == kGateUp ? 2 : (MODE == kDown ? n_units : 1);
+  return MODE == kDown ? n_units : 1;
 }
 
-// stage -> (expert, row block, activation slot)
+// stage -> (expert, first record of the copy, activation slot)
 template <int MODE>
-DEVI void stage_decode(const GemvParams& p, int tile, int s, int Rb, int& expert, int& rb,
-                       int& xs) {
+DEVI void stage_decode(const GemvParams& p, const int* unit_e, int tile, int s, int& expert,
+                       int& rec, int& xs) {
   if (MODE == kPlain) {
-    const int slot = tile / Rb;
-    rb = tile - slot * Rb;
+    const int slot = tile / p.Rb;
+    rec = tile - slot * p.Rb;
     expert = p.sel[slot];
     xs = slot;
   } else if (MODE == kLinear) {
     expert = 0;
-    rb = tile;
+    rec = tile;
     xs = 0;
   } else if (MODE == kGateUp) {
-    const int per = p.I >> 4;
+    const int per = p.Rb >> 1;
     const int u = tile / per;
-    rb = (tile - u * per) + s * per;
-    expert = p.plan->unit_expert[u];
+    rec = 2 * (tile - u * per);
+    expert = unit_e[u];
     xs = u;
   } else {
-    rb = tile;
-    expert = p.plan->unit_expert[s];
+    rec = tile;
+    expert = unit_e[s];
     xs = s;
   }
 }
@@ -124,13 +129,117 @@ DEVI bool wait_limited(uint64_t* bar, uint32_t parity, long long limit) {
   return true;
 }
 
-template <typename T, typename S, int MODE>
-__global__ void __launch_bounds__(kThreads, 2) dq_gemv_kernel(const __grid_constant__ GemvParams p) {
+// position of logical column c inside its 8-column group in fragment order
+// (stored sequence x0 x4 x1 x5 x2 x6 x3 x7)
+DEVI int frag_pos(int c) {
+  const int r = c & 7;
+  return (c & ~7) | ((r & 3) << 1) | (r >> 2);
+}
+
+DEVI uint4 to_frag_order(uint4 v) {
+  uint4 o;
+  o.x = __byte_perm(v.x, v.z, 0x5410);  // (x0, x4)
+  o.y = __byte_perm(v.x, v.z, 0x7632);  // (x1, x5)
+  o.z = __byte_perm(v.y, v.w, 0x5410);  // (x2, x6)
+  o.w = __byte_perm(v.y, v.w, 0x7632);  // (x3, x7)
+  return o;
+}
+
+DEVI float2 scale_pair(uint32_t s2, __half*) { return __half22float2(*reinterpret_cast<__half2*>(&s2)); }
+DEVI float2 scale_pair(uint32_t s2, __nv_bfloat16*) {
+  return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&s2));
+}
+
+// ---- exact path (per-stage activations): item = (record, column pair p)
+// acc += (scale * colw) * sum over the pair of (n - z) * x
+template <typename T, typename S, bool G32>
+DEVI void item_exact(const uint8_t* rec, const TileGeom& tg, int p, int lane, const uint8_t* xrow,
+                     bool xon, bool xraw, float w0, float w1, float (&acc)[4]) {
+  const int g = lane >> 2;
+  const uint4 w = *reinterpret_cast<const uint4*>(rec + (((uint32_t)p << 5) + lane) * 16u);
+  uint4 xa = make_uint4(0, 0, 0, 0), xb = make_uint4(0, 0, 0, 0);
+  if (xon) {
+    xa = *reinterpret_cast<const uint4*>(xrow + (uint32_t)p * 128u);
+    xb = *reinterpret_cast<const uint4*>(xrow + (uint32_t)p * 128u + 64u);
+    if (xraw) {
+      xa = to_frag_order(xa);
+      xb = to_frag_order(xb);
+    }
+  }
+  const uint32_t* sc = reinterpret_cast<const uint32_t*>(rec + tg.off_scale);
+  const uint8_t* zr = rec + tg.off_zero;
+  uint32_t A[4], B[4], lo_a, hi_a, lo_b, hi_b;
+#pragma unroll
+  for (int h = 0; h < (G32 ? 2 : 1); ++h) {
+    const int grp = G32 ? 2 * p + h : (p >> tg.gshift);
+    const uint32_t zz = tg.has_zeros ? (uint32_t)zr[grp * 8 + g] : 0x88u;
+    Dq<T>::consts(zz & 15u, lo_a, hi_a);
+    Dq<T>::consts(zz >> 4, lo_b, hi_b);
+    float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+    if (!G32 || h == 0) {
+      Dq<T>::expand(w.x, w.y, lo_a, hi_a, lo_b, hi_b, A, B);
+      MmaOp<T>::run(c0, A[0], A[1], A[2], A[3], xa.x, xa.y);
+      MmaOp<T>::run(c1, B[0], B[1], B[2], B[3], xa.z, xa.w);
+    }
+    if (!G32 || h == 1) {
+      Dq<T>::expand(w.z, w.w, lo_a, hi_a, lo_b, hi_b, A, B);
+      MmaOp<T>::run(c0, A[0], A[1], A[2], A[3], xb.x, xb.y);
+      MmaOp<T>::run(c1, B[0], B[1], B[2], B[3], xb.z, xb.w);
+    }
+    const float2 s = scale_pair(sc[grp * 8 + g], (S*)nullptr);
+    acc[0] = fmaf(s.x * w0, c0[0] + c1[0], acc[0]);
+    acc[1] = fmaf(s.x * w1, c0[1] + c1[1], acc[1]);
+    acc[2] = fmaf(s.y * w0, c0[2] + c1[2], acc[2]);
+    acc[3] = fmaf(s.y * w1, c0[3] + c1[3], acc[3]);
+  }
+}
+
+// ---- offset path (shared activations): per column pair, four MMAs of (M + n) x
+// plus one correction MMA (corr_a coefficients x the pair's exact column sums);
+// the group scale is applied when the warp's run of a group ends.
+template <typename T, typename S>
+struct OffAcc {
+  float d0[4], d1[4];
+  int rec, grp;
+  uint32_t ca0, ca1;
+  DEVI void reset() {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) d0[r] = d1[r] = 0.f;
+  }
+  DEVI void window(uint32_t wa, uint32_t wb, uint4 xv) {
+    uint32_t A[4], B[4];
+    DqOff<T>::expand(wa, wb, A, B);
+    MmaOp<T>::run(d0, A[0], A[1], A[2], A[3], xv.x, xv.y);
+    MmaOp<T>::run(d1, B[0], B[1], B[2], B[3], xv.z, xv.w);
+  }
+  DEVI void set_group(const uint8_t* r, const TileGeom& tg, int lane, uint32_t wmask) {
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t zz = tg.has_zeros ? (uint32_t)r[tg.off_zero + grp * 8 + g] : 0x88u;
+    DqOff<T>::corr_a(zz & 15u, zz >> 4, t, wmask, ca0, ca1);
+  }
+  DEVI void correct(uint32_t bcorr) { MmaOp<T>::run(d0, ca0, ca1, 0u, 0u, bcorr, 0u); }
+  DEVI void flush(const uint8_t* r, const TileGeom& tg, int lane, float (&acc)[4]) {
+    const int g = lane >> 2;
+    const float2 s = scale_pair(reinterpret_cast<const uint32_t*>(r + tg.off_scale)[grp * 8 + g],
+                                (S*)nullptr);
+    acc[0] = fmaf(s.x, d0[0] + d1[0], acc[0]);
+    acc[1] = fmaf(s.x, d0[1] + d1[1], acc[1]);
+    acc[2] = fmaf(s.y, d0[2] + d1[2], acc[2]);
+    acc[3] = fmaf(s.y, d0[3] + d1[3], acc[3]);
+  }
+};
+
+template <typename T, typename S, int MODE, bool G32, bool CORR>
+__global__ void __launch_bounds__(kThreads, 1) dq_gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffFull);
   uint64_t* empty = reinterpret_cast<uint64_t*>(smem + kOffEmpty);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffAbort);
+  int* n_units_s = reinterpret_cast<int*>(smem + kOffNUnits);
   int* xslot_of = reinterpret_cast<int*>(smem + kOffXslot);
+  int* unit_e = reinterpret_cast<int*>(smem + kOffUnitE);
+  uint32_t* unit_m = reinterpret_cast<uint32_t*>(smem + kOffUnitM);
+  float* unit_w = reinterpret_cast<float*>(smem + kOffUnitW);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int NS = p.nstages;
@@ -146,14 +255,8 @@ __global__ void __launch_bounds__(kThreads, 2) dq_gemv_kernel(const __grid_const
   __syncthreads();
   if (MODE != kGateUp) pdl_launch_dependents();
 
-  const int Rb = (p.R + 15) >> 4;
-
   if (warp == kCW) {
     // ------------------------------------------------------------ producer warp
-    const uint8_t* wsrc = reinterpret_cast<const uint8_t*>(p.packed);
-    const uint8_t* ssrc = reinterpret_cast<const uint8_t*>(p.scale);
-    const uint8_t* zsrc = reinterpret_cast<const uint8_t*>(p.zeros);
-    const uint8_t* xsrc = reinterpret_cast<const uint8_t*>(p.x);
     const uint64_t pol = policy_evict_first();
     bool waited = false;
     if (!p.prefetch) {
@@ -165,13 +268,18 @@ __global__ void __launch_bounds__(kThreads, 2) dq_gemv_kernel(const __grid_const
     if (MODE == kGateUp || MODE == kDown) {
       n_units = p.plan->n_units;
       n_units = n_units < 0 ? 0 : (n_units > kMaxUnits ? kMaxUnits : n_units);
+      for (int u = lane; u < n_units; u += 32) unit_e[u] = p.plan->unit_expert[u];
+      if (lane == 0) *n_units_s = n_units;
+      __syncwarp();
     }
-    const int ntiles = tiles_of<MODE>(p, n_units, Rb);
+    const int ntiles = tiles_of<MODE>(p, n_units);
     const int nst = stages_of<MODE>(n_units);
+    const uint32_t wbytes = (uint32_t)p.nrec * p.tg.rec_bytes;
+    const uint8_t* xsrc = reinterpret_cast<const uint8_t*>(p.x);
 
     auto issue_x = [&](int j) {
       const int slot = j % NS;
-      if (p.x_per_stage) {
+      if (p.x_mode != kXShared) {
         const int xs = xslot_of[slot];
         if (lane == 0) mbar_arrive_expect_tx(&full[slot], (uint32_t)p.ncols * p.xbytes_row);
         __syncwarp();
@@ -203,26 +311,19 @@ __global__ void __launch_bounds__(kThreads, 2) dq_gemv_kernel(const __grid_const
             if (lane == 0) set_error(p.err, DUPLEX_DEVERR_TIMEOUT);
           }
         }
-        int expert, rb, xs;
-        stage_decode<MODE>(p, tile, s, Rb, expert, rb, xs);
+        int expert, rec, xs;
+        stage_decode<MODE>(p, unit_e, tile, s, expert, rec, xs);
         if ((unsigned)expert >= (unsigned)p.E) {
           if (lane == 0) set_error(p.err, DUPLEX_DEVERR_EXPERT);
           expert = 0;
         }
-        if (lane == 0) xslot_of[slot] = xs;
-        uint8_t* st = smem + p.smem_stage0 + (uint32_t)slot * p.stage_bytes;
-        const size_t row0 = (size_t)expert * (size_t)p.Rs + (size_t)rb * 16u;
-        if (lane == 0) mbar_arrive_expect_tx(&full[slot], 16u * p.wbytes + p.sbytes + p.zbytes);
-        __syncwarp();
-        if (lane < 16) {
-          bulk_g2s_stream(st + (uint32_t)lane * p.row_pitch, wsrc + (row0 + lane) * p.wbytes,
-                          p.wbytes, &full[slot], pol);
-        } else if (lane == 16) {
-          bulk_g2s_stream(st + p.off_scale, ssrc + row0 * (size_t)p.G * 2u, p.sbytes, &full[slot],
-                          pol);
-        } else if (lane == 17 && p.zbytes) {
-          bulk_g2s_stream(st + p.off_zero, zsrc + row0 * (size_t)p.GZ * 4u, p.zbytes, &full[slot],
-                          pol);
+        if (lane == 0) {
+          xslot_of[slot] = xs;
+          mbar_arrive_expect_tx(&full[slot], wbytes);
+          const uint8_t* src =
+              p.tiles + ((size_t)expert * (size_t)p.Rb + (size_t)rec) * (size_t)p.tg.rec_bytes;
+          bulk_g2s_stream(smem + p.smem_stage0 + (uint32_t)slot * p.stage_bytes, src, wbytes,
+                          &full[slot], pol);
         }
         __syncwarp();
         if (waited) {
@@ -253,73 +354,143 @@ __global__ void __launch_bounds__(kThreads, 2) dq_gemv_kernel(const __grid_const
   pdl_wait();
   if (MODE == kGateUp) pdl_launch_dependents();
   const int g = lane >> 2, t = lane & 3;
-  uint8_t* xsh = smem + kOffXsh;
+  uint8_t* xsh = smem + p.off_xsh;
   float* red = reinterpret_cast<float*>(smem + kOffRed);
-  float* unit_w = reinterpret_cast<float*>(smem + kOffUnitW);
+  uint32_t* corr = reinterpret_cast<uint32_t*>(smem + kOffCorr);
+  const TileGeom& tg = p.tg;
 
   int n_units = 0;
   if (MODE == kGateUp || MODE == kDown) {
     n_units = p.plan->n_units;
     n_units = n_units < 0 ? 0 : (n_units > kMaxUnits ? kMaxUnits : n_units);
+    for (int u = tid; u < n_units; u += kConsumers) unit_m[u] = p.plan->unit_mask[u];
+    if (MODE == kDown)
+      for (int idx = tid; idx < n_units * kMaxTokens; idx += kConsumers)
+        unit_w[idx] = p.plan->unit_w[idx];
   }
-  if (!p.x_per_stage) {
-    const int per_row = p.K >> 3;  // 16-byte chunks per activation row
+  if (p.x_mode == kXShared) {
+    // activations -> shared memory in fragment order, zero beyond K; with the
+    // offset path (fp16) odd columns are stored divided by 16 (exact)
+    const int nq = tg.Kp >> 3;
     const uint8_t* xb = reinterpret_cast<const uint8_t*>(p.x);
-    for (int idx = tid; idx < p.ncols * per_row; idx += kConsumers) {
-      const int n = idx / per_row, c = idx - n * per_row;
-      const uint4 v =
-          *reinterpret_cast<const uint4*>(xb + ((size_t)n * p.x_col_stride + (size_t)c * 8) * 2);
-      *reinterpret_cast<uint4*>(xsh + (uint32_t)n * p.x_pitch + (uint32_t)c * 16) = v;
-    }
-  }
-  if (MODE == kDown) {
-    for (int idx = tid; idx < n_units * kMaxTokens; idx += kConsumers) unit_w[idx] = p.plan->unit_w[idx];
-  }
-  named_bar_sync(1, kConsumers);
-  if (!p.x_per_stage && p.rms_eps > 0.f) {
-    // y = round(x * rsqrt(mean(x^2) + eps)) per activation row (weightless RMSNorm)
-    float ss[kMaxTokens];
+    float* invs = red + kCW * kMaxTokens;  // per-row RMS scale
+    if (tid < kMaxTokens) invs[tid] = 1.f;
+    if (p.rms_eps > 0.f) {
+      // weightless RMSNorm per row: x * rsqrt(mean(x^2) + eps), rounded to T
+      for (int n = 0; n < p.ncols; ++n) {
+        float a = 0.f;
+        for (int q = tid; q < (tg.K >> 3); q += kConsumers) {
+          const uint4 v = *reinterpret_cast<const uint4*>(xb + ((size_t)n * p.x_col_stride + q * 8) * 2);
+          const T* e = reinterpret_cast<const T*>(&v);
 #pragma unroll
-    for (int n = 0; n < kMaxTokens; ++n) {
-      float a = 0.f;
-      if (n < p.ncols) {
-        const T* row = reinterpret_cast<const T*>(xsh + (uint32_t)n * p.x_pitch);
-        for (int c = tid; c < p.K; c += kConsumers) {
-          const float v = to_f32<T>(row[c]);
-          a = fmaf(v, v, a);
+          for (int k = 0; k < 8; ++k) a = fmaf(to_f32<T>(e[k]), to_f32<T>(e[k]), a);
         }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (lane == 0) red[warp * kMaxTokens + n] = a;
       }
+      named_bar_sync(1, kConsumers);
+      if (tid < p.ncols) {
+        float tot = 0.f;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-      ss[n] = a;
-    }
-    if (lane == 0) {
-#pragma unroll
-      for (int n = 0; n < kMaxTokens; ++n) red[warp * kMaxTokens + n] = ss[n];
+        for (int w = 0; w < kCW; ++w) tot += red[w * kMaxTokens + tid];
+        invs[tid] = 1.0f / sqrtf(tot / (float)tg.K + p.rms_eps);
+      }
     }
     named_bar_sync(1, kConsumers);
-    for (int n = 0; n < p.ncols; ++n) {
-      float tot = 0.f;
+    for (int idx = tid; idx < p.ncols * nq; idx += kConsumers) {
+      const int n = idx / nq, q = idx - n * nq;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (q * 8 < tg.K) {
+        v = *reinterpret_cast<const uint4*>(xb + ((size_t)n * p.x_col_stride + q * 8) * 2);
+        if (p.rms_eps > 0.f) {
+          const float inv = invs[n];
+          T* e = reinterpret_cast<T*>(&v);
 #pragma unroll
-      for (int w = 0; w < kCW; ++w) tot += red[w * kMaxTokens + n];
-      const float inv = 1.0f / sqrtf(tot / (float)p.K + p.rms_eps);
-      T* row = reinterpret_cast<T*>(xsh + (uint32_t)n * p.x_pitch);
-      for (int c = tid; c < p.K; c += kConsumers) row[c] = from_f32<T>(to_f32<T>(row[c]) * inv);
+          for (int k = 0; k < 8; ++k) e[k] = from_f32<T>(to_f32<T>(e[k]) * inv);
+        }
+      }
+      uint4 o = to_frag_order(v);
+      if (CORR && DqOff<T>::kOddDiv16) {
+        const __half2 q16 = __float2half2_rn(0.0625f);
+        __half2 hy = __hmul2(*reinterpret_cast<__half2*>(&o.y), q16);
+        __half2 hw = __hmul2(*reinterpret_cast<__half2*>(&o.w), q16);
+        o.y = *reinterpret_cast<uint32_t*>(&hy);
+        o.w = *reinterpret_cast<uint32_t*>(&hw);
+      }
+      *reinterpret_cast<uint4*>(xsh + (uint32_t)n * p.x_pitch + (uint32_t)q * 16u) = o;
     }
+    named_bar_sync(1, kConsumers);
+    if (CORR) {
+      // exact activation sums per 32-column window in 16-bit parts; word (pair p,
+      // lane g*4 + t) is the correction MMA's B fragment for column g: t = 0 / 1 ->
+      // window 2p (fp16: even / odd columns), t = 2 / 3 -> window 2p + 1
+      for (int idx = tid; idx < tg.npairs * kMaxTokens; idx += kConsumers) {
+        const int pp = idx / kMaxTokens, n = idx - pp * kMaxTokens;
+        uint32_t b[4] = {0u, 0u, 0u, 0u};
+        if (n < p.ncols) {
+          const uint8_t* row = xsh + (uint32_t)n * p.x_pitch + (uint32_t)pp * 128u;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float se = 0.f, so = 0.f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 o = *reinterpret_cast<const uint4*>(row + h * 64 + q * 16);
+              const T* e = reinterpret_cast<const T*>(&o);
+              // fragment order: e0 = x0, e1 = x4, e2 = x1, e3 = x5, e4 = x2, e5 = x6, e6 = x3, e7 = x7
+              se += (to_f32<T>(e[0]) + to_f32<T>(e[1])) + (to_f32<T>(e[4]) + to_f32<T>(e[5]));
+              so += (to_f32<T>(e[2]) + to_f32<T>(e[3])) + (to_f32<T>(e[6]) + to_f32<T>(e[7]));
+            }
+            if (DqOff<T>::kOddDiv16) {
+              so *= 16.f;
+              const T eh = from_f32<T>(se), oh = from_f32<T>(so);
+              const T el = from_f32<T>(se - to_f32<T>(eh)), ol = from_f32<T>(so - to_f32<T>(oh));
+              b[2 * h] = (uint32_t)*reinterpret_cast<const uint16_t*>(&eh) |
+                         ((uint32_t)*reinterpret_cast<const uint16_t*>(&el) << 16);
+              b[2 * h + 1] = (uint32_t)*reinterpret_cast<const uint16_t*>(&oh) |
+                             ((uint32_t)*reinterpret_cast<const uint16_t*>(&ol) << 16);
+            } else {
+              const float x = se + so;
+              const T x1 = from_f32<T>(x);
+              const T x2 = from_f32<T>(x - to_f32<T>(x1));
+              const T x3 = from_f32<T>(x - to_f32<T>(x1) - to_f32<T>(x2));
+              b[2 * h] = (uint32_t)*reinterpret_cast<const uint16_t*>(&x1) |
+                         ((uint32_t)*reinterpret_cast<const uint16_t*>(&x2) << 16);
+              b[2 * h + 1] = (uint32_t)*reinterpret_cast<const uint16_t*>(&x3);
+            }
+          }
+        }
+        uint4* dst = reinterpret_cast<uint4*>(corr + pp * 32 + n * 4);
+        *dst = make_uint4(b[0], b[1], b[2], b[3]);
+      }
+    }
+  }
+  named_bar_sync(1, kConsumers);
+  // zero the padded activation tail of every per-stage activation row (never copied)
+  if (p.x_mode != kXShared && tg.Kp > tg.K) {
+    const int tail = (tg.Kp - tg.K) * 2;
+    for (int s = 0; s < NS; ++s)
+      for (int idx = tid; idx < p.ncols * tail; idx += kConsumers) {
+        const int n = idx / tail, b = idx - n * tail;
+        smem[p.smem_stage0 + (uint32_t)s * p.stage_bytes + p.off_x + (uint32_t)n * p.x_pitch +
+             (uint32_t)tg.K * 2u + b] = 0;
+      }
     named_bar_sync(1, kConsumers);
   }
 
-  const int ntiles = tiles_of<MODE>(p, n_units, Rb);
+  const int ntiles = tiles_of<MODE>(p, n_units);
   const int nst = stages_of<MODE>(n_units);
-  const int nW = p.K >> 5;
-  const int wbeg = (warp * nW) / kCW, wend = ((warp + 1) * nW) / kCW;
   const bool xon = g < p.ncols;
+  const bool xraw = p.x_mode == kXStageRaw;
+  const int npairs = tg.npairs;
+  const int ips = p.nrec * npairs;  // items per stage
 
   int i = 0;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    float acc[8];
-#pragma unroll
-    for (int r = 0; r < 8; ++r) acc[r] = 0.f;
+    float acc0[4] = {0.f, 0.f, 0.f, 0.f};
+    float acc1[4] = {0.f, 0.f, 0.f, 0.f};
+    const int npt = nst * ips;
+    const int ib = (warp * npt) / kCW, ie = ((warp + 1) * npt) / kCW;
 
     for (int s = 0; s < nst; ++s, ++i) {
       const int slot = i % NS;
@@ -327,81 +498,75 @@ __global__ void __launch_bounds__(kThreads, 2) dq_gemv_kernel(const __grid_const
         if (lane == 0) set_error(p.err, DUPLEX_DEVERR_TIMEOUT);
       }
       const uint8_t* st = smem + p.smem_stage0 + (uint32_t)slot * p.stage_bytes;
-      const uint8_t* xs = p.x_per_stage ? st + p.off_x : xsh;
-      const S* sc = reinterpret_cast<const S*>(st + p.off_scale);
-      const uint32_t* zw = reinterpret_cast<const uint32_t*>(st + p.off_zero);
-      const uint32_t wrow = smem_u32(st) + (uint32_t)(lane & 15) * p.row_pitch;
-      const uint8_t* xrow = xs + (uint32_t)g * p.x_pitch + (uint32_t)t * 16;
-
-      float part[4] = {0.f, 0.f, 0.f, 0.f};
-      float sacc[4] = {0.f, 0.f, 0.f, 0.f};
-      int cur = -1;
-      float sa = 0.f, sb = 0.f;
-      uint32_t loa = 0, hia = 0, lob = 0, hib = 0;
-      for (int win = wbeg; win < wend; ++win) {
-        const int grp = (win << 5) / p.group;
-        if (grp != cur) {
-          if (cur >= 0) {
-            sacc[0] += sa * part[0];
-            sacc[1] += sa * part[1];
-            sacc[2] += sb * part[2];
-            sacc[3] += sb * part[3];
-            part[0] = part[1] = part[2] = part[3] = 0.f;
+      const int lo = ib > s * ips ? ib - s * ips : 0;
+      const int hi = ie < (s + 1) * ips ? ie - s * ips : ips;
+      if (CORR) {
+        const uint8_t* xrow = xsh + (uint32_t)g * p.x_pitch + (uint32_t)t * 16u;
+        OffAcc<T, S> oa;
+        oa.reset();
+        oa.rec = -1;
+        oa.grp = -1;
+        for (int it = lo; it < hi; ++it) {
+          const int r = it >= npairs ? 1 : 0;
+          const int pp = it - r * npairs;
+          const uint8_t* rec = st + (uint32_t)r * tg.rec_bytes;
+          const uint4 w = *reinterpret_cast<const uint4*>(rec + (((uint32_t)pp << 5) + lane) * 16u);
+          const uint32_t bc = corr[pp * 32 + lane];
+          uint4 xa = make_uint4(0, 0, 0, 0), xb = make_uint4(0, 0, 0, 0);
+          if (xon) {
+            xa = *reinterpret_cast<const uint4*>(xrow + (uint32_t)pp * 128u);
+            xb = *reinterpret_cast<const uint4*>(xrow + (uint32_t)pp * 128u + 64u);
           }
-          cur = grp;
-          sa = to_f32<S>(sc[g * p.G + grp]);
-          sb = to_f32<S>(sc[(g + 8) * p.G + grp]);
-          uint32_t za = 8u, zb = 8u;
-          if (p.zbytes) {
-            const int sh = (grp & 7) * 4;
-            za = (zw[g * p.GZ + (grp >> 3)] >> sh) & 0xFu;
-            zb = (zw[(g + 8) * p.GZ + (grp >> 3)] >> sh) & 0xFu;
+          if (G32) {
+            // each 32-column window is its own group
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              oa.reset();
+              oa.grp = 2 * pp + h;
+              oa.set_group(rec, tg, lane, 1u << h);
+              oa.window(h ? w.z : w.x, h ? w.w : w.y, h ? xb : xa);
+              oa.correct(bc);
+              oa.flush(rec, tg, lane, r ? acc1 : acc0);
+            }
+          } else {
+            const int grp = pp >> tg.gshift;
+            if (grp != oa.grp || r != oa.rec) {
+              if (oa.grp >= 0)
+                oa.flush(st + (uint32_t)oa.rec * tg.rec_bytes, tg, lane, oa.rec ? acc1 : acc0);
+              oa.reset();
+              oa.grp = grp;
+              oa.rec = r;
+              oa.set_group(rec, tg, lane, 3u);
+            }
+            oa.window(w.x, w.y, xa);
+            oa.window(w.z, w.w, xb);
+            oa.correct(bc);
           }
-          Dq<T>::consts(za, loa, hia);
-          Dq<T>::consts(zb, lob, hib);
         }
-        uint32_t wa, wb;
-        ldsm_x2(wa, wb, wrow + (uint32_t)win * 16u);
-        uint32_t xa0 = 0, xa1 = 0, xb0 = 0, xb1 = 0;
-        if (xon) {
-          const uint4 v = *reinterpret_cast<const uint4*>(xrow + (uint32_t)win * 64u);
-          x_frags(v, xa0, xa1, xb0, xb1);
+        if (!G32 && oa.grp >= 0)
+          oa.flush(st + (uint32_t)oa.rec * tg.rec_bytes, tg, lane, oa.rec ? acc1 : acc0);
+      } else {
+        const uint8_t* xrow = st + p.off_x + (uint32_t)g * p.x_pitch + (uint32_t)t * 16u;
+        float w0 = 1.f, w1 = 1.f;
+        if (MODE == kDown) {
+          w0 = unit_w[s * kMaxTokens + 2 * t];
+          w1 = unit_w[s * kMaxTokens + 2 * t + 1];
         }
-        uint32_t A[4], B[4];
-        Dq<T>::expand(wa, wb, loa, hia, lob, hib, A, B);
-        MmaOp<T>::run(part, A[0], A[1], A[2], A[3], xa0, xa1);
-        MmaOp<T>::run(part, B[0], B[1], B[2], B[3], xb0, xb1);
-      }
-      if (cur >= 0) {
-        sacc[0] += sa * part[0];
-        sacc[1] += sa * part[1];
-        sacc[2] += sb * part[2];
-        sacc[3] += sb * part[3];
+#pragma unroll 2
+        for (int it = lo; it < hi; ++it)
+          item_exact<T, S, G32>(st, tg, it, lane, xrow, xon, xraw, w0, w1, acc0);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
-
-      if (MODE == kGateUp) {
-        const int o = s * 4;
-#pragma unroll
-        for (int r = 0; r < 4; ++r) acc[o + r] = sacc[r];
-      } else if (MODE == kDown) {
-        const float w0 = unit_w[s * kMaxTokens + 2 * t];
-        const float w1 = unit_w[s * kMaxTokens + 2 * t + 1];
-        acc[0] += w0 * sacc[0];
-        acc[1] += w1 * sacc[1];
-        acc[2] += w0 * sacc[2];
-        acc[3] += w1 * sacc[3];
-      } else {
-#pragma unroll
-        for (int r = 0; r < 4; ++r) acc[r] += sacc[r];
-      }
     }
 
-    // ---- split-K reduction across the 8 consumer warps, then the epilogue
-    constexpr int NREG = (MODE == kGateUp) ? 8 : 4;
+    // ---- split-K reduction across the consumer warps, then the epilogue
 #pragma unroll
-    for (int r = 0; r < NREG; ++r) red[(warp * 8 + r) * 32 + lane] = acc[r];
+    for (int r = 0; r < 4; ++r) red[(warp * 8 + r) * 32 + lane] = acc0[r];
+    if (MODE == kGateUp) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) red[(warp * 8 + 4 + r) * 32 + lane] = acc1[r];
+    }
     named_bar_sync(1, kConsumers);
     if (tid < 128) {
       const int n = tid >> 4, r = tid & 15;
@@ -414,8 +579,8 @@ __global__ void __launch_bounds__(kThreads, 2) dq_gemv_kernel(const __grid_const
         if (MODE == kGateUp) v2 += red[(w * 8 + 4 + ri) * 32 + gl];
       }
       if (MODE == kPlain) {
-        const int slot = tile / Rb;
-        const int row = (tile - slot * Rb) * 16 + r;
+        const int slot = tile / p.Rb;
+        const int row = (tile - slot * p.Rb) * 16 + r;
         if (n < p.ncols && row < p.R)
           reinterpret_cast<float*>(p.out)[slot * p.out_slot_stride + n * p.out_col_stride + row] = v;
       } else if (MODE == kLinear) {
@@ -429,13 +594,13 @@ __global__ void __launch_bounds__(kThreads, 2) dq_gemv_kernel(const __grid_const
           reinterpret_cast<T*>(p.out)[n * p.out_col_stride + row] = y;
         }
       } else if (MODE == kGateUp) {
-        const int per = p.I >> 4;
+        const int per = p.Rb >> 1;
         const int u = tile / per;
         const int row = (tile - u * per) * 16 + r;
         if (n < p.ncols) {
-          const uint32_t mask = p.plan->unit_mask[u];
-          const float a = ((mask >> n) & 1u) ? silu_f32(v) * v2 : 0.f;
-          reinterpret_cast<T*>(p.out)[((size_t)u * kMaxTokens + n) * p.I + row] = from_f32<T>(a);
+          const float a = ((unit_m[u] >> n) & 1u) ? silu_f32(v) * v2 : 0.f;
+          reinterpret_cast<T*>(p.out)[((size_t)u * kMaxTokens + n) * p.I + frag_pos(row)] =
+              from_f32<T>(a);
         }
       } else {
         const int row = tile * 16 + r;
@@ -448,6 +613,60 @@ __global__ void __launch_bounds__(kThreads, 2) dq_gemv_kernel(const __grid_const
       }
     }
     named_bar_sync(1, kConsumers);
+  }
+}
+
+// ---------------------------------------------------------------------- repack
+template <typename S>
+__global__ void repack_kernel(const int32_t* __restrict__ packed, const S* __restrict__ scale,
+                              const int32_t* __restrict__ zeros, int E, int R, int Rb, int C, int G,
+                              int GZ, TileGeom tg, int pair_halves, uint32_t* __restrict__ tiles) {
+  const uint32_t wpr = tg.rec_bytes / 4u;
+  const long long total = (long long)E * Rb * wpr;
+  const int half = Rb >> 1;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const long long recg = idx / wpr;
+    const uint32_t o = (uint32_t)(idx - recg * wpr) * 4u;
+    const int e = (int)(recg / Rb);
+    const int rout = (int)(recg - (long long)e * Rb);
+    const int rb = pair_halves ? ((rout & 1) ? half + (rout >> 1) : (rout >> 1)) : rout;
+    uint32_t val = 0;
+    if (o < tg.off_scale) {
+      const int pr = (int)(o >> 9);
+      const int ln = (int)((o & 511u) >> 4);
+      const int j = (int)((o & 15u) >> 2);
+      const int g = ln >> 2, t = ln & 3;
+      const int row = rb * 16 + g + ((j & 1) ? 8 : 0);
+      const int word = 8 * pr + t + ((j & 2) ? 4 : 0);
+      if (row < R && word < C) val = (uint32_t)packed[((long long)e * R + row) * C + word];
+    } else if (o < tg.off_zero) {
+      const int q = (int)((o - tg.off_scale) >> 2);
+      const int grp = q >> 3, g = q & 7;
+      const int ra = rb * 16 + g, rbw = ra + 8;
+      uint16_t sa = 0, sb = 0;
+      if (grp < G) {
+        if (ra < R) sa = *reinterpret_cast<const uint16_t*>(&scale[((long long)e * R + ra) * G + grp]);
+        if (rbw < R) sb = *reinterpret_cast<const uint16_t*>(&scale[((long long)e * R + rbw) * G + grp]);
+      }
+      val = (uint32_t)sa | ((uint32_t)sb << 16);
+    } else if (tg.has_zeros && o < tg.off_zero + (uint32_t)tg.Gr * 8u) {
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int q = (int)(o - tg.off_zero) + b;
+        const int grp = q >> 3, g = q & 7;
+        const int ra = rb * 16 + g, rbw = ra + 8;
+        uint32_t za = 0, zb = 0;
+        if (grp < G) {
+          if (ra < R)
+            za = ((uint32_t)zeros[((long long)e * R + ra) * GZ + (grp >> 3)] >> ((grp & 7) * 4)) & 15u;
+          if (rbw < R)
+            zb = ((uint32_t)zeros[((long long)e * R + rbw) * GZ + (grp >> 3)] >> ((grp & 7) * 4)) & 15u;
+        }
+        val |= (za | (zb << 4)) << (8 * b);
+      }
+    }
+    tiles[idx] = val;
   }
 }
 
@@ -476,28 +695,21 @@ int last_cuda_error() { return g_last_cuda; }
 
 static inline uint32_t up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
-constexpr size_t kDefaultSmemBudget = 112 * 1024;
 constexpr size_t kMaxSmem = 227 * 1024;
+size_t g_smem_linear = 112 * 1024, g_smem_gateup = 148 * 1024, g_smem_down = 76 * 1024,
+       g_smem_plain = 112 * 1024;
 
 // Fill the shared-memory geometry of `p`; returns the dynamic smem bytes or 0.
-static size_t plan_geometry(GemvParams& p, bool has_zeros, size_t budget) {
-  p.G = (p.K + p.group - 1) / p.group;
-  p.GZ = (p.G + 7) / 8;
-  p.wbytes = (uint32_t)p.K / 2u;
-  uint32_t P = up(p.wbytes, 16);
-  if (((P >> 4) & 1u) == 0) P += 16;
-  p.row_pitch = P;
-  p.sbytes = 16u * (uint32_t)p.G * 2u;
-  p.zbytes = has_zeros ? 16u * (uint32_t)p.GZ * 4u : 0u;
-  p.off_scale = 16u * P;
-  p.off_zero = p.off_scale + up(p.sbytes, 16);
-  p.x_pitch = up((uint32_t)p.K * 2u, 128) + 64u;
-  p.off_x = up(p.off_zero + p.zbytes, 128);
-  p.xbytes_row = (uint32_t)p.K * 2u;
-  const uint32_t sb = p.off_x + (p.x_per_stage ? (uint32_t)p.ncols * p.x_pitch : 0u);
+static size_t plan_geometry(GemvParams& p, size_t budget) {
+  p.x_pitch = up((uint32_t)p.tg.Kp * 2u, 128) + 64u;
+  p.xbytes_row = (uint32_t)p.tg.K * 2u;
+  p.off_x = (uint32_t)p.nrec * p.tg.rec_bytes;
+  const uint32_t sb = p.off_x + (p.x_mode != kXShared ? (uint32_t)p.ncols * p.x_pitch : 0u);
   p.stage_bytes = up(sb, 128);
-  p.smem_stage0 = up(kOffXsh + (p.x_per_stage ? 0u : (uint32_t)p.ncols * p.x_pitch), 128);
-  size_t b = budget;
+  const uint32_t corr_bytes = p.x_mode == kXShared ? (uint32_t)p.tg.npairs * 128u : 0u;
+  p.off_xsh = up(kOffCorr + corr_bytes, 128);
+  p.smem_stage0 = up(p.off_xsh + (p.x_mode == kXShared ? (uint32_t)p.ncols * p.x_pitch : 0u), 128);
+  size_t b = budget < kMaxSmem ? budget : kMaxSmem;
   int ns = (int)((b > p.smem_stage0 ? b - p.smem_stage0 : 0) / p.stage_bytes);
   if (ns < 2) {
     b = kMaxSmem;
@@ -509,15 +721,28 @@ static size_t plan_geometry(GemvParams& p, bool has_zeros, size_t budget) {
   return (size_t)p.smem_stage0 + (size_t)ns * p.stage_bytes;
 }
 
-template <typename T, typename S, int MODE>
+// cudaFuncAttributeMaxDynamicSharedMemorySize, once per (kernel, device)
+int ensure_smem_attr(const void* fn, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({fn, dev})) return DUPLEX_OK;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return record_cuda(e);
+  done.insert({fn, dev});
+  return DUPLEX_OK;
+}
+
+template <typename T, typename S, int MODE, bool G32>
 static int launch(GemvParams& p, int grid, size_t smem, bool pdl, cudaStream_t stream) {
-  auto kern = dq_gemv_kernel<T, S, MODE>;
-  static size_t configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
-    if (e != cudaSuccess) return record_cuda(e);
-    configured = kMaxSmem;
-  }
+  // offset dequant + correction MMA wherever the activations are shared by all stages
+  const bool corr = p.x_mode == kXShared;
+  void (*kern)(GemvParams) = corr ? dq_gemv_kernel<T, S, MODE, G32, true>
+                                  : dq_gemv_kernel<T, S, MODE, G32, false>;
+  int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), (int)kMaxSmem);
+  if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
@@ -531,133 +756,176 @@ static int launch(GemvParams& p, int grid, size_t smem, bool pdl, cudaStream_t s
   return record_cuda(cudaLaunchKernelEx(&cfg, kern, p));
 }
 
+template <int MODE, bool G32>
+static int dispatch_g(int act_dtype, int scale_dtype, GemvParams& p, int grid, size_t smem, bool pdl,
+                      cudaStream_t st) {
+  if (act_dtype == DUPLEX_DTYPE_F16 && scale_dtype == DUPLEX_DTYPE_F16)
+    return launch<__half, __half, MODE, G32>(p, grid, smem, pdl, st);
+  if (act_dtype == DUPLEX_DTYPE_F16 && scale_dtype == DUPLEX_DTYPE_BF16)
+    return launch<__half, __nv_bfloat16, MODE, G32>(p, grid, smem, pdl, st);
+  if (act_dtype == DUPLEX_DTYPE_BF16 && scale_dtype == DUPLEX_DTYPE_BF16)
+    return launch<__nv_bfloat16, __nv_bfloat16, MODE, G32>(p, grid, smem, pdl, st);
+  if (act_dtype == DUPLEX_DTYPE_BF16 && scale_dtype == DUPLEX_DTYPE_F16)
+    return launch<__nv_bfloat16, __half, MODE, G32>(p, grid, smem, pdl, st);
+  return DUPLEX_ERR_DTYPE;
+}
+
 template <int MODE>
 static int dispatch(int act_dtype, int scale_dtype, GemvParams& p, int grid, size_t smem, bool pdl,
                     cudaStream_t st) {
-  if (act_dtype == DUPLEX_DTYPE_F16 && scale_dtype == DUPLEX_DTYPE_F16)
-    return launch<__half, __half, MODE>(p, grid, smem, pdl, st);
-  if (act_dtype == DUPLEX_DTYPE_F16 && scale_dtype == DUPLEX_DTYPE_BF16)
-    return launch<__half, __nv_bfloat16, MODE>(p, grid, smem, pdl, st);
-  if (act_dtype == DUPLEX_DTYPE_BF16 && scale_dtype == DUPLEX_DTYPE_BF16)
-    return launch<__nv_bfloat16, __nv_bfloat16, MODE>(p, grid, smem, pdl, st);
-  if (act_dtype == DUPLEX_DTYPE_BF16 && scale_dtype == DUPLEX_DTYPE_F16)
-    return launch<__nv_bfloat16, __half, MODE>(p, grid, smem, pdl, st);
-  return DUPLEX_ERR_DTYPE;
+  if (p.tg.gshift < 0) return dispatch_g<MODE, true>(act_dtype, scale_dtype, p, grid, smem, pdl, st);
+  return dispatch_g<MODE, false>(act_dtype, scale_dtype, p, grid, smem, pdl, st);
 }
 
 static inline bool al16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
-static int check_weights(const int32_t* packed, const void* scale, const int32_t* zeros,
-                         int scale_dtype, int E, int R, int Rs, int K, int group) {
-  if (!packed || !scale) return DUPLEX_ERR_ARG;
-  if (E < 1 || R < 1 || Rs < R || K < 32 || group < 32) return DUPLEX_ERR_ARG;
+static int check_tiles(const void* tiles, int scale_dtype, int E, int R, int K, int group,
+                       int has_zeros, TileGeom* tg) {
+  if (!tiles) return DUPLEX_ERR_ARG;
+  if (E < 1 || R < 1 || K < 1 || group < 1) return DUPLEX_ERR_ARG;
   if (scale_dtype != DUPLEX_DTYPE_F16 && scale_dtype != DUPLEX_DTYPE_BF16) return DUPLEX_ERR_DTYPE;
-  if ((Rs & 15) || (K & 31) || (group & 31)) return DUPLEX_ERR_UNSUPPORTED;
-  if (!al16(packed) || !al16(scale) || (zeros && !al16(zeros))) return DUPLEX_ERR_ALIGN;
+  if (tile_geom(K, group, has_zeros, tg)) return DUPLEX_ERR_UNSUPPORTED;
+  if (!al16(tiles)) return DUPLEX_ERR_ALIGN;
   return DUPLEX_OK;
 }
-
-struct MoeLaunch;  // fwd
 
 }  // namespace duplex
 
 using namespace duplex;
 
-extern "C" int duplex_dq_gemv(const void* x, int act_dtype, int64_t x_slot_stride,
-                              const int32_t* packed, const void* scale, const int32_t* zeros,
-                              int scale_dtype, int32_t E, int32_t R, int32_t Rs, int32_t K,
+extern "C" int duplex_tile_record_bytes(int32_t K, int32_t group, int has_zeros, size_t* bytes) {
+  TileGeom tg;
+  if (!bytes) return DUPLEX_ERR_ARG;
+  if (tile_geom(K, group, has_zeros, &tg)) return DUPLEX_ERR_UNSUPPORTED;
+  *bytes = tg.rec_bytes;
+  return DUPLEX_OK;
+}
+
+extern "C" int duplex_repack_tiles(const int32_t* packed, const void* scale, const int32_t* zeros,
+                                   int scale_dtype, int32_t E, int32_t R, int32_t K, int32_t group,
+                                   int32_t pair_halves, void* tiles, size_t tiles_bytes,
+                                   void* stream) {
+  if (!packed || !scale || !tiles || E < 1 || R < 1) return DUPLEX_ERR_ARG;
+  TileGeom tg;
+  if (tile_geom(K, group, zeros != nullptr, &tg)) return DUPLEX_ERR_UNSUPPORTED;
+  int Rb = (R + 15) / 16;
+  if (pair_halves) {
+    if ((R & 31) != 0) return DUPLEX_ERR_UNSUPPORTED;  // both halves whole 16-row blocks
+  }
+  if ((size_t)E * Rb * tg.rec_bytes > tiles_bytes) return DUPLEX_ERR_WORKSPACE;
+  if (!al16(tiles)) return DUPLEX_ERR_ALIGN;
+  const int C = K / 8, G = (K + group - 1) / group, GZ = (G + 7) / 8;
+  const long long words = (long long)E * Rb * (tg.rec_bytes / 4);
+  int blocks = (int)((words + 255) / 256);
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (scale_dtype == DUPLEX_DTYPE_F16)
+    repack_kernel<__half><<<blocks, 256, 0, st>>>(packed, reinterpret_cast<const __half*>(scale),
+                                                   zeros, E, R, Rb, C, G, GZ, tg, pair_halves,
+                                                   reinterpret_cast<uint32_t*>(tiles));
+  else if (scale_dtype == DUPLEX_DTYPE_BF16)
+    repack_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+        packed, reinterpret_cast<const __nv_bfloat16*>(scale), zeros, E, R, Rb, C, G, GZ, tg,
+        pair_halves, reinterpret_cast<uint32_t*>(tiles));
+  else
+    return DUPLEX_ERR_DTYPE;
+  return record_cuda(cudaGetLastError());
+}
+
+extern "C" int duplex_dq_gemv(const void* x, int act_dtype, int64_t x_slot_stride, const void* tiles,
+                              int scale_dtype, int has_zeros, int32_t E, int32_t R, int32_t K,
                               int32_t group, const int32_t* sel, int32_t nsel, float* out,
                               int32_t* err, void* stream) {
-  int rc = check_weights(packed, scale, zeros, scale_dtype, E, R, Rs, K, group);
+  GemvParams p = {};
+  int rc = check_tiles(tiles, scale_dtype, E, R, K, group, has_zeros, &p.tg);
   if (rc) return rc;
   if (!x || !sel || !out || nsel < 1) return DUPLEX_ERR_ARG;
   if (!al16(x) || (x_slot_stride & 7)) return DUPLEX_ERR_ALIGN;
-  GemvParams p = {};
-  p.packed = packed; p.scale = scale; p.zeros = zeros;
-  p.E = E; p.R = R; p.Rs = Rs; p.K = K; p.group = group;
+  p.tiles = reinterpret_cast<const uint8_t*>(tiles);
+  p.E = E; p.R = R; p.Rb = (R + 15) / 16;
   p.x = x; p.x_col_stride = 0; p.x_slot_stride = x_slot_stride; p.ncols = 1;
+  p.x_mode = x_slot_stride != 0 ? kXStageRaw : kXShared;
   p.sel = sel; p.nslots = nsel;
   p.out = out; p.out_slot_stride = R; p.out_col_stride = 0;
   p.err = err;
-  p.prefetch = 0;
-  p.x_per_stage = x_slot_stride != 0;
-  const size_t smem = plan_geometry(p, zeros != nullptr, kDefaultSmemBudget);
+  p.nrec = 1;
+  const size_t smem = plan_geometry(p, g_smem_plain);
   if (!smem) return DUPLEX_ERR_UNSUPPORTED;
-  const int tiles = nsel * ((R + 15) / 16);
-  const int grid = tiles < num_sms() ? tiles : num_sms();
+  const int tiles_n = nsel * p.Rb;
+  const int grid = tiles_n < num_sms() ? tiles_n : num_sms();
   return dispatch<kPlain>(act_dtype, scale_dtype, p, grid, smem, false, (cudaStream_t)stream);
 }
 
 extern "C" int duplex_packed_linear(const void* x, int act_dtype, int32_t B, int64_t x_row_stride,
-                                    const int32_t* packed, const void* scale, const int32_t* zeros,
-                                    int scale_dtype, int32_t R, int32_t Rs, int32_t K, int32_t group,
-                                    const void* bias, const void* residual, int64_t res_row_stride,
-                                    void* out, int64_t out_row_stride, float rms_eps, int pdl,
-                                    void* stream) {
-  int rc = check_weights(packed, scale, zeros, scale_dtype, 1, R, Rs, K, group);
+                                    const void* tiles, int scale_dtype, int has_zeros, int32_t R,
+                                    int32_t K, int32_t group, const void* bias,
+                                    const void* residual, int64_t res_row_stride, void* out,
+                                    int64_t out_row_stride, float rms_eps, int pdl, void* stream) {
+  GemvParams p = {};
+  int rc = check_tiles(tiles, scale_dtype, 1, R, K, group, has_zeros, &p.tg);
   if (rc) return rc;
   if (!x || !out || B < 1 || B > kMaxTokens) return DUPLEX_ERR_ARG;
   if (!al16(x) || (x_row_stride & 7)) return DUPLEX_ERR_ALIGN;
-  GemvParams p = {};
-  p.packed = packed; p.scale = scale; p.zeros = zeros;
-  p.E = 1; p.R = R; p.Rs = Rs; p.K = K; p.group = group;
+  p.tiles = reinterpret_cast<const uint8_t*>(tiles);
+  p.E = 1; p.R = R; p.Rb = (R + 15) / 16;
   p.x = x; p.x_col_stride = x_row_stride; p.x_slot_stride = 0; p.ncols = B;
+  p.x_mode = kXShared;
   p.out = out; p.out_slot_stride = 0; p.out_col_stride = out_row_stride;
   p.bias = bias; p.residual = residual; p.res_col_stride = res_row_stride;
   p.prefetch = pdl ? 1 : 0;
-  p.x_per_stage = 0;
   p.rms_eps = rms_eps;
-  const size_t smem = plan_geometry(p, zeros != nullptr, kDefaultSmemBudget);
+  p.nrec = 1;
+  const size_t smem = plan_geometry(p, g_smem_linear);
   if (!smem) return DUPLEX_ERR_UNSUPPORTED;
-  const int tiles = (R + 15) / 16;
-  const int grid = tiles < num_sms() ? tiles : num_sms();
+  const int grid = p.Rb < num_sms() ? p.Rb : num_sms();
   return dispatch<kLinear>(act_dtype, scale_dtype, p, grid, smem, pdl != 0, (cudaStream_t)stream);
 }
 
 namespace duplex {
 
 // Gate|up and down launches of the decode MoE (T <= 8); called by moe.cu.
-int launch_moe_experts(int act_dtype, int scale_dtype, int T, int E, int H, int I, int group,
-                       const int32_t* gu_packed, const void* gu_scale, const int32_t* gu_zeros,
-                       const int32_t* dn_packed, const void* dn_scale, const int32_t* dn_zeros,
-                       const MoePlan* plan, const void* x, void* act, const void* residual,
-                       void* out, int* err, int max_units, bool pdl, cudaStream_t st) {
-  int rc = check_weights(gu_packed, gu_scale, gu_zeros, scale_dtype, E, 2 * I, 2 * I, H, group);
-  if (rc) return rc;
-  rc = check_weights(dn_packed, dn_scale, dn_zeros, scale_dtype, E, H, H, I, group);
-  if (rc) return rc;
-  if ((I & 15) || (H & 15)) return DUPLEX_ERR_UNSUPPORTED;
-
+int launch_moe_experts(int act_dtype, int scale_dtype, int has_zeros, int T, int E, int H, int I,
+                       int group, const void* gu_tiles, const void* dn_tiles, const MoePlan* plan,
+                       const void* x, void* act, const void* residual, void* out, int* err,
+                       int max_units, bool pdl, cudaStream_t st) {
   GemvParams a = {};
-  a.packed = gu_packed; a.scale = gu_scale; a.zeros = gu_zeros;
-  a.E = E; a.R = 2 * I; a.Rs = 2 * I; a.K = H; a.group = group;
+  int rc = check_tiles(gu_tiles, scale_dtype, E, 2 * I, H, group, has_zeros, &a.tg);
+  if (rc) return rc;
+  GemvParams d = {};
+  rc = check_tiles(dn_tiles, scale_dtype, E, H, I, group, has_zeros, &d.tg);
+  if (rc) return rc;
+  if ((I & 15) || (H & 7)) return DUPLEX_ERR_UNSUPPORTED;
+
+  a.tiles = reinterpret_cast<const uint8_t*>(gu_tiles);
+  a.E = E; a.R = 2 * I; a.Rb = 2 * I / 16;
   a.x = x; a.x_col_stride = H; a.x_slot_stride = 0; a.ncols = T;
+  a.x_mode = kXShared;
   a.plan = plan; a.I = I;
   a.out = act;
   a.err = err;
   a.prefetch = 0;
-  a.x_per_stage = 0;
-  size_t smem = plan_geometry(a, gu_zeros != nullptr, kDefaultSmemBudget);
+  a.nrec = 2;
+  size_t smem = plan_geometry(a, g_smem_gateup);
   if (!smem) return DUPLEX_ERR_UNSUPPORTED;
-  int tiles = max_units * (I / 16);
-  int grid = tiles < num_sms() ? tiles : num_sms();
+  int tiles_n = max_units * (I / 16);
+  int grid = tiles_n < num_sms() ? tiles_n : num_sms();
   rc = dispatch<kGateUp>(act_dtype, scale_dtype, a, grid, smem, pdl, st);
   if (rc) return rc;
 
-  GemvParams d = {};
-  d.packed = dn_packed; d.scale = dn_scale; d.zeros = dn_zeros;
-  d.E = E; d.R = H; d.Rs = H; d.K = I; d.group = group;
+  d.tiles = reinterpret_cast<const uint8_t*>(dn_tiles);
+  d.E = E; d.R = H; d.Rb = (H + 15) / 16;
   d.x = act; d.x_col_stride = I; d.x_slot_stride = (long long)kMaxTokens * I; d.ncols = T;
+  d.x_mode = kXStageFrag;
   d.plan = plan; d.I = I;
   d.out = out; d.out_col_stride = H;
   d.residual = residual; d.res_col_stride = H;
   d.err = err;
   d.prefetch = pdl ? 1 : 0;
-  d.x_per_stage = 1;
-  smem = plan_geometry(d, dn_zeros != nullptr, kDefaultSmemBudget);
+  d.nrec = 1;
+  smem = plan_geometry(d, g_smem_down);
   if (!smem) return DUPLEX_ERR_UNSUPPORTED;
-  tiles = (H + 15) / 16;
-  grid = tiles < num_sms() ? tiles : num_sms();
+  tiles_n = d.Rb;
+  grid = tiles_n < num_sms() ? tiles_n : num_sms();
   return dispatch<kDown>(act_dtype, scale_dtype, d, grid, smem, pdl, st);
 }
 

@@ -16,11 +16,11 @@ namespace duplex {
 
 int record_cuda(cudaError_t e);
 int num_sms();
-int launch_moe_experts(int act_dtype, int scale_dtype, int T, int E, int H, int I, int group,
-                       const int32_t* gu_packed, const void* gu_scale, const int32_t* gu_zeros,
-                       const int32_t* dn_packed, const void* dn_scale, const int32_t* dn_zeros,
-                       const MoePlan* plan, const void* x, void* act, const void* residual,
-                       void* out, int* err, int max_units, bool pdl, cudaStream_t st);
+int ensure_smem_attr(const void* fn, int bytes);
+int launch_moe_experts(int act_dtype, int scale_dtype, int has_zeros, int T, int E, int H, int I,
+                       int group, const void* gu_tiles, const void* dn_tiles, const MoePlan* plan,
+                       const void* x, void* act, const void* residual, void* out, int* err,
+                       int max_units, bool pdl, cudaStream_t st);
 
 constexpr int kRouteWarps = 4;
 constexpr int kRouteMaxChunks = 16;  // 16-byte chunks per lane: H <= 16 * 32 * 8 = 4096
@@ -37,6 +37,7 @@ struct RouteParams {
   float* logits;
   int* counter;
   MoePlan* plan;
+  int* err;
 };
 
 template <typename T>
@@ -49,52 +50,58 @@ DEVI void dot8(const uint4& a, const uint4& b, float& acc) {
 
 template <typename T>
 __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(const __grid_constant__ RouteParams p) {
-  extern __shared__ __align__(16) uint8_t smem[];
+  // dynamic smem: [gate rows of this CTA: kRouteWarps x H][tokens: T x H]
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t bar;
   __shared__ int s_last;
+  __shared__ int s_abort;
+  __shared__ float s_ss[kRouteWarps][kMaxTokens];
   __shared__ int s_sel[kMaxTokens * kMaxTopK];
   __shared__ float s_w[kMaxTokens * kMaxTopK];
 
-  pdl_launch_dependents();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int e = blockIdx.x * kRouteWarps + warp;
+  const int e0 = blockIdx.x * kRouteWarps;
+  const int nrows = (p.E - e0) < kRouteWarps ? (p.E - e0) : kRouteWarps;
   const int nchunk = p.H >> 3;
+  const uint32_t row_bytes = (uint32_t)p.H * 2u;
+  uint4* wsm = reinterpret_cast<uint4*>(smem);
+  uint4* xs = reinterpret_cast<uint4*>(smem + (size_t)kRouteWarps * row_bytes);
 
-  // gate row -> registers (independent of the previous kernel)
-  uint4 wr[kRouteMaxChunks];
-#pragma unroll
-  for (int j = 0; j < kRouteMaxChunks; ++j) {
-    const int c = lane + 32 * j;
-    if (e < p.E && c < nchunk)
-      wr[j] = reinterpret_cast<const uint4*>(p.gate_w)[(size_t)e * nchunk + c];
-    else
-      wr[j] = make_uint4(0, 0, 0, 0);
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    s_abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+  // the CTA's gate rows (weights: independent of the previous kernel) in one bulk copy
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bar, (uint32_t)nrows * row_bytes);
+    bulk_g2s(wsm, reinterpret_cast<const uint8_t*>(p.gate_w) + (size_t)e0 * row_bytes,
+             (uint32_t)nrows * row_bytes, &bar);
   }
   pdl_wait();
 
   // token rows -> shared memory
-  uint4* xs = reinterpret_cast<uint4*>(smem);
   for (int idx = tid; idx < p.T * nchunk; idx += blockDim.x)
     xs[idx] = reinterpret_cast<const uint4*>(p.x)[idx];
   __syncthreads();
   if (p.rms_eps > 0.f) {
     // weightless RMSNorm of every token row, identical in every CTA; CTA 0 publishes
     // the normalised rows for the gate|up kernel
-    __shared__ float s_ss[kRouteWarps][kMaxTokens];
-    T* xe = reinterpret_cast<T*>(smem);
+    T* xe = reinterpret_cast<T*>(xs);
     for (int t = 0; t < p.T; ++t) {
       float a = 0.f;
       for (int c = tid; c < p.H; c += blockDim.x) {
         const float v = to_f32<T>(xe[t * p.H + c]);
         a = fmaf(v, v, a);
       }
-#pragma unroll
       for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
       if (lane == 0) s_ss[warp][t] = a;
     }
     __syncthreads();
     for (int t = 0; t < p.T; ++t) {
       float tot = 0.f;
-#pragma unroll
       for (int w = 0; w < kRouteWarps; ++w) tot += s_ss[w][t];
       const float inv = 1.0f / sqrtf(tot / (float)p.H + p.rms_eps);
       for (int c = tid; c < p.H; c += blockDim.x)
@@ -106,26 +113,27 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(const __grid_co
         reinterpret_cast<uint4*>(p.xn)[idx] = xs[idx];
     }
   }
+  if (!mbar_wait_bounded(&bar, 0u, &s_abort)) {
+    if (tid == 0 && p.err) atomicOr(p.err, DUPLEX_DEVERR_TIMEOUT);
+  }
 
-  if (e < p.E) {
+  if (warp < nrows) {
+    const int e = e0 + warp;
     float acc[kMaxTokens];
 #pragma unroll
     for (int t = 0; t < kMaxTokens; ++t) acc[t] = 0.f;
+    const uint4* wr = wsm + (size_t)warp * nchunk;
+#pragma unroll 2
+    for (int c = lane; c < nchunk; c += 32) {
+      const uint4 wv = wr[c];
 #pragma unroll
-    for (int j = 0; j < kRouteMaxChunks; ++j) {
-      const int c = lane + 32 * j;
-      if (c < nchunk) {
-#pragma unroll
-        for (int t = 0; t < kMaxTokens; ++t)
-          if (t < p.T) dot8<T>(wr[j], xs[t * nchunk + c], acc[t]);
-      }
+      for (int t = 0; t < kMaxTokens; ++t)
+        if (t < p.T) dot8<T>(wv, xs[t * nchunk + c], acc[t]);
     }
-#pragma unroll
-    for (int t = 0; t < kMaxTokens; ++t) {
+    for (int t = 0; t < p.T; ++t) {
       float v = acc[t];
-#pragma unroll
       for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0 && t < p.T) {
+      if (lane == 0) {
         if (p.gate_b) v += to_f32<T>(reinterpret_cast<const T*>(p.gate_b)[e]);
         p.logits[t * p.E + e] = to_f32<T>(from_f32<T>(v));
       }
@@ -245,7 +253,7 @@ static int launch_route(int act_dtype, const RouteParams& rp, bool pdl, cudaStre
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((rp.E + kRouteWarps - 1) / kRouteWarps);
   cfg.blockDim = dim3(kRouteWarps * 32);
-  cfg.dynamicSmemBytes = (size_t)rp.T * rp.H * 2;
+  cfg.dynamicSmemBytes = (size_t)(kRouteWarps + rp.T) * rp.H * 2;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -253,19 +261,15 @@ static int launch_route(int act_dtype, const RouteParams& rp, bool pdl, cudaStre
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   if (act_dtype == DUPLEX_DTYPE_F16) {
-    auto k = route_kernel<__half>;
-    if (cfg.dynamicSmemBytes > 48 * 1024) {
-      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-      if (e != cudaSuccess) return record_cuda(e);
-    }
+    void (*k)(RouteParams) = route_kernel<__half>;
+    int rc = ensure_smem_attr(reinterpret_cast<const void*>(k), 200 * 1024);
+    if (rc) return rc;
     return record_cuda(cudaLaunchKernelEx(&cfg, k, rp));
   }
   if (act_dtype == DUPLEX_DTYPE_BF16) {
-    auto k = route_kernel<__nv_bfloat16>;
-    if (cfg.dynamicSmemBytes > 48 * 1024) {
-      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-      if (e != cudaSuccess) return record_cuda(e);
-    }
+    void (*k)(RouteParams) = route_kernel<__nv_bfloat16>;
+    int rc = ensure_smem_attr(reinterpret_cast<const void*>(k), 200 * 1024);
+    if (rc) return rc;
     return record_cuda(cudaLaunchKernelEx(&cfg, k, rp));
   }
   return DUPLEX_ERR_DTYPE;
@@ -326,10 +330,9 @@ extern "C" int duplex_moe_route(const void* x, int act_dtype, int32_t T, const v
 
 extern "C" int duplex_moe_forward(const void* x, int act_dtype, int32_t T, const void* gate_w,
                                   const void* gate_b, int32_t E, int32_t H, int32_t I,
-                                  int32_t top_k, int32_t norm_topk, const int32_t* gu_packed,
-                                  const void* gu_scale, const int32_t* gu_zeros,
-                                  const int32_t* dn_packed, const void* dn_scale,
-                                  const int32_t* dn_zeros, int scale_dtype, int32_t group,
+                                  int32_t top_k, int32_t norm_topk, const void* gu_tiles,
+                                  const void* dn_tiles, int scale_dtype, int has_zeros,
+                                  int32_t group,
                                   const void* residual, void* out, float* w_out, int32_t* sel_out,
                                   void* workspace, size_t workspace_bytes, int32_t* err,
                                   float rms_eps, int pdl, void* stream) {
@@ -341,14 +344,14 @@ extern "C" int duplex_moe_forward(const void* x, int act_dtype, int32_t T, const
   const MoeScratch L = moe_scratch_layout(T, E, H, I, top_k);
   RouteParams rp = make_route(x, T, gate_w, gate_b, E, H, top_k, norm_topk, rms_eps, w_out,
                               sel_out, ws, L);
+  rp.err = err;
   cudaStream_t st = (cudaStream_t)stream;
   rc = launch_route(act_dtype, rp, pdl != 0, st);
   if (rc) return rc;
   int max_units = T * top_k < E ? T * top_k : E;
   if (max_units > kMaxUnits) max_units = kMaxUnits;
-  return launch_moe_experts(act_dtype, scale_dtype, T, E, H, I, group, gu_packed, gu_scale,
-                            gu_zeros, dn_packed, dn_scale, dn_zeros,
-                            reinterpret_cast<const MoePlan*>(ws + L.plan),
+  return launch_moe_experts(act_dtype, scale_dtype, has_zeros, T, E, H, I, group, gu_tiles,
+                            dn_tiles, reinterpret_cast<const MoePlan*>(ws + L.plan),
                             rms_eps > 0.f ? (const void*)(ws + L.xn) : x, ws + L.act, residual,
                             out, err, max_units, pdl != 0, st);
 }

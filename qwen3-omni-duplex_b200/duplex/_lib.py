@@ -31,19 +31,22 @@ _SIGNATURES = {
     "duplex_unpack4": ([_c_ptr, _c_i64, _c_i32, _c_i32, _c_ptr, _c_ptr], _c_int),
     "duplex_dequant": ([_c_ptr, _c_ptr, _c_int, _c_ptr, _c_i64, _c_i32, _c_i32, _c_ptr, _c_int,
                         _c_ptr], _c_int),
-    "duplex_dq_gemv": ([_c_ptr, _c_int, _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_int, _c_i32, _c_i32,
-                        _c_i32, _c_i32, _c_i32, _c_ptr, _c_i32, _c_ptr, _c_ptr, _c_ptr], _c_int),
-    "duplex_packed_linear": ([_c_ptr, _c_int, _c_i32, _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_int,
-                              _c_i32, _c_i32, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_i64, _c_ptr,
-                              _c_i64, _c_f32, _c_int, _c_ptr], _c_int),
+    "duplex_tile_record_bytes": ([_c_i32, _c_i32, _c_int, ctypes.POINTER(ctypes.c_size_t)], _c_int),
+    "duplex_repack_tiles": ([_c_ptr, _c_ptr, _c_ptr, _c_int, _c_i32, _c_i32, _c_i32, _c_i32,
+                             _c_i32, _c_ptr, _c_size, _c_ptr], _c_int),
+    "duplex_dq_gemv": ([_c_ptr, _c_int, _c_i64, _c_ptr, _c_int, _c_int, _c_i32, _c_i32, _c_i32,
+                        _c_i32, _c_ptr, _c_i32, _c_ptr, _c_ptr, _c_ptr], _c_int),
+    "duplex_packed_linear": ([_c_ptr, _c_int, _c_i32, _c_i64, _c_ptr, _c_int, _c_int, _c_i32,
+                              _c_i32, _c_i32, _c_ptr, _c_ptr, _c_i64, _c_ptr, _c_i64, _c_f32,
+                              _c_int, _c_ptr], _c_int),
     "duplex_moe_workspace_bytes": ([_c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
                                     ctypes.POINTER(ctypes.c_size_t)], _c_int),
     "duplex_moe_route": ([_c_ptr, _c_int, _c_i32, _c_ptr, _c_ptr, _c_i32, _c_i32, _c_i32, _c_i32,
                           _c_ptr, _c_ptr, _c_ptr, _c_size, _c_f32, _c_int, _c_ptr], _c_int),
     "duplex_moe_forward": ([_c_ptr, _c_int, _c_i32, _c_ptr, _c_ptr, _c_i32, _c_i32, _c_i32,
-                            _c_i32, _c_i32, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
-                            _c_int, _c_i32, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size,
-                            _c_ptr, _c_f32, _c_int, _c_ptr], _c_int),
+                            _c_i32, _c_i32, _c_ptr, _c_ptr, _c_int, _c_int, _c_i32, _c_ptr,
+                            _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr, _c_f32, _c_int,
+                            _c_ptr], _c_int),
 }
 
 _lib = None

@@ -39,11 +39,17 @@ def _linear(packed, scale, zeros, out_f, in_f, device):
     return lin
 
 
+def _groups(K, group):
+    return -(-K // group)
+
+
 def linear_bytes(lin: TritonPackedLinear) -> int:
-    n = lin.out_features * lin.in_features // 2
-    n += lin.out_features * lin.scale.shape[-1] * lin.scale.element_size()
-    if lin.zeros is not None:
-        n += lin.out_features * lin.zeros.shape[-1] * 4
+    """Algorithmic bytes of an int4 linear: nibbles, one 16-bit scale and (if present)
+    one 4-bit zero point per (row, group)."""
+    R, K, G = lin.out_features, lin.in_features, _groups(lin.in_features, lin.group)
+    n = R * K // 2 + R * G * 2
+    if lin.tiles.has_zeros:
+        n += R * G // 2
     return n
 
 
@@ -51,11 +57,10 @@ def moe_bytes(moe: FusedPackedMoE, T: int = 1) -> int:
     """Algorithmic HBM bytes of one decode MoE layer at batch T=1: router weights,
     the 8 selected experts' nibbles + scales + zero points, token in and out."""
     E, H, I, k = moe.num_experts, moe.hidden, moe.inter, moe.top_k
-    per = 2 * I * H // 2 + H * I // 2
-    per += 2 * I * moe.gu_scale.shape[-1] * moe.gu_scale.element_size()
-    per += H * moe.down_scale.shape[-1] * moe.down_scale.element_size()
-    if moe.gu_zeros is not None:
-        per += 2 * I * moe.gu_zeros.shape[-1] * 4 + H * moe.down_zeros.shape[-1] * 4
+    g_gu, g_dn = _groups(H, moe.group), _groups(I, moe.group)
+    per = 2 * I * H // 2 + H * I // 2 + (2 * I * g_gu + H * g_dn) * 2
+    if moe.has_zeros:
+        per += (2 * I * g_gu + H * g_dn) // 2
     return E * H * moe.gate.weight.element_size() + k * per + 2 * T * H * 2
 
 

@@ -32,7 +32,7 @@ import torch
 import torch.nn as nn
 
 from duplex import _lib
-from duplex.streaming.triton_dequant_gemv import HAVE_TRITON, dequant_gemv  # noqa: F401
+from duplex.streaming.triton_dequant_gemv import HAVE_TRITON, Int4Tiles, dequant_gemv  # noqa: F401
 
 NUM_BITS = 4
 PACK = 32 // NUM_BITS
@@ -120,6 +120,7 @@ class FusedPackedMoE(nn.Module):
         return m
 
     def _install(self, gu_p, gu_s, gu_z, dp, ds, dz, inter, hidden, hid_out, inter_in):
+        """Repack the stacked experts once into tile records (gate and up blocks paired)."""
         if inter % 16 or hidden % 32 or inter_in % 32 or hid_out % 16:
             raise _lib.DuplexError("expert dims must satisfy inter % 16 == 0 and hidden, "
                                    "inter % 32 == 0 for the B200 kernels")
@@ -127,18 +128,14 @@ class FusedPackedMoE(nn.Module):
         self.group = -(-hidden // G)
         if -(-inter_in // ds.shape[-1]) != self.group:
             raise _lib.DuplexError("gate|up and down must use the same group size")
-        a = _lib.aligned
-        self.register_buffer("gu_packed", a(gu_p.to(torch.int32)), persistent=False)
-        self.register_buffer("gu_scale", a(gu_s), persistent=False)
-        self.register_buffer("gu_zeros", None if gu_z is None else a(gu_z.to(torch.int32)),
-                             persistent=False)
-        self.register_buffer("down_packed", a(dp.to(torch.int32)), persistent=False)
-        self.register_buffer("down_scale", a(ds), persistent=False)
-        self.register_buffer("down_zeros", None if dz is None else a(dz.to(torch.int32)),
-                             persistent=False)
+        if (gu_z is None) != (dz is None):
+            raise _lib.DuplexError("gate|up and down must both have or both lack zero points")
+        self.gu_tiles = Int4Tiles(gu_p, gu_s, gu_z, group=self.group, K=hidden, pair_halves=True)
+        self.dn_tiles = Int4Tiles(dp, ds, dz, group=self.group, K=inter_in)
         self.register_buffer("err", torch.zeros(1, dtype=torch.int32, device=gu_p.device),
                              persistent=False)
         self.inter, self.hidden, self.hid_out, self.inter_in = inter, hidden, hid_out, inter_in
+        self.has_zeros = gu_z is not None
         self._ws = {}
 
     @staticmethod
@@ -178,9 +175,9 @@ class FusedPackedMoE(nn.Module):
         _lib.call(
             "duplex_moe_forward", _lib.ptr(x), _lib.dtype_code(x.dtype), T, _lib.ptr(g.weight),
             _lib.ptr(g.bias), self.num_experts, self.hidden, self.inter, self.top_k,
-            1 if self.norm_topk_prob else 0, _lib.ptr(self.gu_packed), _lib.ptr(self.gu_scale),
-            _lib.ptr(self.gu_zeros), _lib.ptr(self.down_packed), _lib.ptr(self.down_scale),
-            _lib.ptr(self.down_zeros), _lib.dtype_code(self.gu_scale.dtype), self.group,
+            1 if self.norm_topk_prob else 0, _lib.ptr(self.gu_tiles.buf),
+            _lib.ptr(self.dn_tiles.buf), self.gu_tiles.scale_code, 1 if self.has_zeros else 0,
+            self.group,
             _lib.ptr(residual), _lib.ptr(out), _lib.ptr(w_out), _lib.ptr(sel_out), _lib.ptr(ws),
             ws.numel(), _lib.ptr(self.err), float(rms_eps), 1 if self.pdl else 0,
             _lib.stream_of(x))

@@ -12,11 +12,16 @@ the reference:
   TritonPackedLinear(mod, device)                           (reference :125-159)
   patch_attention_to_triton(model, device, verbose) -> int  (reference :162-172)
 
-Packing (unchanged): unpacked column j = i + 8*m is nibble i of int32 word m;
-scales per group of `group` columns; optional zero points (see `duplex._lib`).
+Packing (unchanged at this interface): unpacked column j = i + 8*m is nibble i of
+int32 word m; scales per group of `group` columns; optional zero points.  The
+kernels read a one-time repack of that layout (`Int4Tiles`, tile records of 16
+rows); modules repack at construction, `dequant_gemv` keeps a small cache keyed by
+the source tensors and their version counters.
 """
 
 from __future__ import annotations
+
+import collections
 
 import torch
 
@@ -45,26 +50,71 @@ def _kernel_scale(scale: torch.Tensor) -> torch.Tensor:
     raise _lib.DuplexError(f"scale dtype {scale.dtype} is not exactly representable in fp16/bf16")
 
 
-def pad_rows(t: torch.Tensor | None, rows_to: int) -> torch.Tensor | None:
-    """Pad dim -2 of a stacked [..., R, C] tensor with zeros up to `rows_to`."""
-    if t is None or t.shape[-2] == rows_to:
-        return t
-    pad = list(t.shape)
-    pad[-2] = rows_to - t.shape[-2]
-    return torch.cat([t, t.new_zeros(pad)], dim=-2)
+class Int4Tiles:
+    """Tile records of a stacked int4 matrix [E, R, K/8] (+ scales, zero points).
+
+    One record per (expert, 16-row block) holds the block's nibbles in MMA fragment
+    order with its group scales and zero points, so one bulk copy feeds a kernel
+    stage (layout documented in csrc/tiles.cuh).  `pair_halves` interleaves the row
+    blocks of the two halves (gate | up), so a gate block and its up block are one
+    contiguous pair of records.
+    """
+
+    def __init__(self, packed, scale, zeros=None, group=None, K=None, pair_halves=False):
+        _lib.require_cuda(packed, scale, zeros)
+        if packed.dim() == 2:
+            packed, scale = packed.unsqueeze(0), scale.unsqueeze(0)
+            zeros = None if zeros is None else zeros.unsqueeze(0)
+        E, R, NW = packed.shape
+        K = int(K if K is not None else NW * 8)
+        G = scale.shape[-1]
+        group = int(group if group is not None else -(-K // G))
+        if NW * 8 != K:
+            packed = packed[..., : K // 8]
+        self.E, self.R, self.K, self.group = E, R, K, group
+        self.has_zeros = zeros is not None
+        scale = _lib.aligned(_kernel_scale(scale))
+        self.scale_dtype = scale.dtype
+        n = _lib.ctypes.c_size_t()
+        _lib.call("duplex_tile_record_bytes", K, group, 1 if self.has_zeros else 0,
+                  _lib.ctypes.byref(n))
+        self.record_bytes = n.value
+        rb = -(-R // 16)
+        self.buf = torch.empty(E * rb * n.value, dtype=torch.uint8, device=packed.device)
+        p = _lib.aligned(packed.to(torch.int32))
+        z = None if zeros is None else _lib.aligned(zeros.to(torch.int32))
+        _lib.call("duplex_repack_tiles", _lib.ptr(p), _lib.ptr(scale), _lib.ptr(z),
+                  _lib.dtype_code(scale.dtype), E, R, K, group, 1 if pair_halves else 0,
+                  _lib.ptr(self.buf), self.buf.numel(), _lib.stream_of(p))
+
+    @property
+    def scale_code(self) -> int:
+        return _lib.dtype_code(self.scale_dtype)
+
+    def nbytes(self) -> int:
+        return self.buf.numel()
 
 
-def prepare_int4(packed, scale, zeros=None):
-    """-> (packed, scale, zeros, R, Rs) laid out as the kernels need: rows padded to a
-    multiple of 16, contiguous, 16-byte aligned.  One-time cost for modules."""
-    R = packed.shape[-2]
-    Rs = (R + 15) // 16 * 16
-    scale = _kernel_scale(scale)
-    packed, scale, zeros = (pad_rows(packed, Rs), pad_rows(scale, Rs), pad_rows(zeros, Rs))
-    packed = _lib.aligned(packed.to(torch.int32))
-    scale = _lib.aligned(scale)
-    zeros = None if zeros is None else _lib.aligned(zeros.to(torch.int32))
-    return packed, scale, zeros, R, Rs
+_TILE_CACHE: collections.OrderedDict = collections.OrderedDict()
+_TILE_CACHE_MAX = 16
+
+
+def _key(t):
+    return None if t is None else (t.data_ptr(), t._version, tuple(t.shape), t.dtype)
+
+
+def tiles_for(packed, scale, zeros, K, group) -> Int4Tiles:
+    """Cached Int4Tiles of (packed, scale, zeros); invalidated by in-place writes."""
+    key = (_key(packed), _key(scale), _key(zeros), K, group)
+    hit = _TILE_CACHE.get(key)
+    if hit is not None:
+        _TILE_CACHE.move_to_end(key)
+        return hit[0]
+    tl = Int4Tiles(packed, scale, zeros, group=group, K=K)
+    _TILE_CACHE[key] = (tl, packed, scale, zeros)   # keep sources alive while cached
+    if len(_TILE_CACHE) > _TILE_CACHE_MAX:
+        _TILE_CACHE.popitem(last=False)
+    return tl
 
 
 def dequant_gemv(x, packed, scale, sel, group=32, block_r=64, nw_blk=8, zeros=None):
@@ -84,7 +134,7 @@ def dequant_gemv(x, packed, scale, sel, group=32, block_r=64, nw_blk=8, zeros=No
     K = x.shape[-1]
     if NW * 8 < K:
         raise _lib.DuplexError(f"packed has {NW} words per row, fewer than K/8 = {K // 8}")
-    packed, scale, zeros, R, Rs = prepare_int4(packed[..., : K // 8], scale, zeros)
+    tl = tiles_for(packed, scale, zeros, K, group)
     sel32 = _lib.aligned(sel.reshape(-1).to(torch.int32))
     k = sel32.numel()
     x = _lib.aligned(x)
@@ -92,9 +142,9 @@ def dequant_gemv(x, packed, scale, sel, group=32, block_r=64, nw_blk=8, zeros=No
     if x.dim() == 2 and x.shape[0] != k:
         raise _lib.DuplexError("per-expert x must have one row per selected expert")
     out = torch.empty(k, R, device=x.device, dtype=torch.float32)
-    _lib.call("duplex_dq_gemv", _lib.ptr(x), _lib.dtype_code(x.dtype), x_slot, _lib.ptr(packed),
-              _lib.ptr(scale), _lib.ptr(zeros), _lib.dtype_code(scale.dtype), E, R, Rs, K, group,
-              _lib.ptr(sel32), k, _lib.ptr(out), None, _lib.stream_of(x))
+    _lib.call("duplex_dq_gemv", _lib.ptr(x), _lib.dtype_code(x.dtype), x_slot, _lib.ptr(tl.buf),
+              tl.scale_code, 1 if tl.has_zeros else 0, E, R, K, group, _lib.ptr(sel32), k,
+              _lib.ptr(out), None, _lib.stream_of(x))
     return out
 
 
@@ -124,15 +174,11 @@ class TritonPackedLinear(torch.nn.Module):
         shape = tuple(int(v) for v in mod.weight_shape.tolist())
         self.out_features, self.in_features = shape
         zeros = getattr(mod, "weight_zeros", None)
-        packed, scale, zeros, R, Rs = prepare_int4(
-            mod.weight_packed.to(device), mod.weight_scale.to(device),
-            None if zeros is None else zeros.to(device))
+        scale = mod.weight_scale.to(device)
         self.group = -(-self.in_features // scale.shape[-1])
-        self.rows_alloc = Rs
-        self.register_buffer("packed", packed.unsqueeze(0), persistent=False)
-        self.register_buffer("scale", scale.unsqueeze(0), persistent=False)
-        self.register_buffer("zeros", None if zeros is None else zeros.unsqueeze(0),
-                             persistent=False)
+        self.tiles = Int4Tiles(mod.weight_packed.to(device), scale,
+                               None if zeros is None else zeros.to(device), group=self.group,
+                               K=self.in_features)
         b = getattr(mod, "bias", None)
         self.register_buffer("bias", b.to(device) if b is not None else None, persistent=False)
         self.register_buffer("_sel", torch.zeros(1, dtype=torch.int32, device=device),
@@ -155,16 +201,15 @@ class TritonPackedLinear(torch.nn.Module):
         bias = None if self.bias is None else _lib.aligned(self.bias.to(x.dtype))
         res = None if residual is None else _lib.aligned(residual.reshape(-1, self.out_features))
         st = _lib.stream_of(x)
+        tl = self.tiles
         for r0 in range(0, N, 8):
             b = min(8, N - r0)
-            xr = flat[r0:r0 + b]
-            yr = y[r0:r0 + b]
-            _lib.call("duplex_packed_linear", _lib.ptr(xr), _lib.dtype_code(x.dtype), b, xs,
-                      _lib.ptr(self.packed), _lib.ptr(self.scale), _lib.ptr(self.zeros),
-                      _lib.dtype_code(self.scale.dtype), self.out_features, self.rows_alloc,
-                      K, self.group, _lib.ptr(bias),
+            _lib.call("duplex_packed_linear", _lib.ptr(flat[r0:r0 + b]), _lib.dtype_code(x.dtype),
+                      b, xs, _lib.ptr(tl.buf), tl.scale_code, 1 if tl.has_zeros else 0,
+                      self.out_features, K, self.group, _lib.ptr(bias),
                       None if res is None else _lib.ptr(res[r0:r0 + b]), self.out_features,
-                      _lib.ptr(yr), self.out_features, float(rms_eps), 1 if self.pdl else 0, st)
+                      _lib.ptr(y[r0:r0 + b]), self.out_features, float(rms_eps),
+                      1 if self.pdl else 0, st)
         return y.view(*lead, self.out_features)
 
 

@@ -43,8 +43,14 @@ def test_version_and_errors(lib):
 def test_bad_arguments_are_rejected_without_cuda(lib):
     null = None
     # null pointers
-    assert lib.duplex_dq_gemv(null, 0, 0, null, null, null, 0, 1, 16, 16, 64, 32, null, 1, null,
-                              null, null) == 1
+    assert lib.duplex_dq_gemv(null, 0, 0, null, 0, 0, 1, 16, 64, 32, null, 1, null, null,
+                              null) == 1
+    assert lib.duplex_repack_tiles(null, null, null, 0, 1, 16, 64, 32, 0, null, 0, null) == 1
+    assert lib.duplex_tile_record_bytes(2048, 128, 1, ctypes.byref(n := ctypes.c_size_t())) == 0
+    assert n.value == 16384 + 16 * 32 + 16 * 8
+    assert lib.duplex_tile_record_bytes(768, 128, 0, ctypes.byref(n)) == 0
+    assert n.value == 6144 + 6 * 32 + 64   # padded to 128 bytes
+    assert lib.duplex_tile_record_bytes(2048, 96, 0, ctypes.byref(n)) == 6
     assert lib.duplex_unpack4(null, 1, 1, 8, null, null) == 1
     assert lib.duplex_dequant(null, null, 0, null, 1, 64, 32, null, 0, null) == 1
     n = ctypes.c_size_t()
@@ -56,22 +62,16 @@ def test_bad_arguments_are_rejected_without_cuda(lib):
 def test_unsupported_shapes_are_rejected(lib):
     # fake but aligned addresses: validation must reject before any launch
     p = ctypes.c_void_p(1 << 20)
-    # K not a multiple of 32
-    assert lib.duplex_packed_linear(p, 0, 1, 48, p, p, None, 0, 16, 16, 48, 32, None, None, 0, p,
-                                    16, 0.0, 0, None) == 6
-    # rows per expert not a multiple of 16
-    assert lib.duplex_packed_linear(p, 0, 1, 64, p, p, None, 0, 10, 10, 64, 32, None, None, 0, p,
-                                    10, 0.0, 0, None) == 6
-    # batch > 8
-    assert lib.duplex_packed_linear(p, 0, 9, 64, p, p, None, 0, 16, 16, 64, 32, None, None, 0, p,
-                                    16, 0.0, 0, None) == 1
-    # misaligned activation pointer
-    q = ctypes.c_void_p((1 << 20) + 8)
-    assert lib.duplex_packed_linear(q, 0, 1, 64, p, p, None, 0, 16, 16, 64, 32, None, None, 0, p,
-                                    16, 0.0, 0, None) == 2
-    # bad dtype
-    assert lib.duplex_packed_linear(p, 0, 1, 64, p, p, None, 7, 16, 16, 64, 32, None, None, 0, p,
-                                    16, 0.0, 0, None) == 3
+
+    def lin(x=p, act=0, B=1, xs=64, sdt=0, R=16, K=64, group=32):
+        return lib.duplex_packed_linear(x, act, B, xs, p, sdt, 0, R, K, group, None, None, 0, p,
+                                        R, 0.0, 0, None)
+
+    assert lin(K=48, xs=48) == 6                   # K not a multiple of 32
+    assert lin(group=48) == 6                      # group neither 32 nor 64 * 2^k
+    assert lin(B=9) == 1                           # batch > 8
+    assert lin(x=ctypes.c_void_p((1 << 20) + 8)) == 2   # misaligned activations
+    assert lin(sdt=7) == 3                         # bad scale dtype
     # router: T > 8, top_k > E
     assert lib.duplex_moe_route(p, 0, 9, p, None, 128, 2048, 8, 1, None, None, p, 1 << 30, 0.0, 0,
                                 None) == 1

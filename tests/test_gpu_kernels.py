@@ -118,18 +118,18 @@ def test_dq_gemv_vs_oracle(cuda, K, R, group, zp, act, per_slot_x):
 
 def test_dq_gemv_out_of_range_expert_sets_error_word(cuda):
     from duplex import _lib
-    from duplex.streaming.triton_dequant_gemv import prepare_int4
+    from duplex.streaming.triton_dequant_gemv import Int4Tiles
     rng = np.random.default_rng(2)
     E, R, K = 4, 32, 256
     lin = synth.linear_np(rng, E * R, K, 32, False)
-    packed, scale, zeros, R_, Rs = prepare_int4(T(lin["packed"].reshape(E, R, -1), cuda),
-                                                T(lin["scale"].reshape(E, R, -1), cuda))
+    tl = Int4Tiles(T(lin["packed"].reshape(E, R, -1), cuda), T(lin["scale"].reshape(E, R, -1), cuda),
+                   group=32)
     x = T(rng.standard_normal(K).astype(np.float16), cuda)
     sel = torch.tensor([1, 99, 2], dtype=torch.int32, device=cuda)
     out = torch.empty(3, R, device=cuda)
     err = torch.zeros(1, dtype=torch.int32, device=cuda)
-    _lib.call("duplex_dq_gemv", _lib.ptr(x), 0, 0, _lib.ptr(packed), _lib.ptr(scale), None, 0,
-              E, R, Rs, K, 32, _lib.ptr(sel), 3, _lib.ptr(out), _lib.ptr(err), _lib.stream_of(x))
+    _lib.call("duplex_dq_gemv", _lib.ptr(x), 0, 0, _lib.ptr(tl.buf), tl.scale_code, 0, E, R, K, 32,
+              _lib.ptr(sel), 3, _lib.ptr(out), _lib.ptr(err), _lib.stream_of(x))
     torch.cuda.synchronize()
     assert int(err.item()) & _lib.DEVERR_EXPERT
     ref = O.dequant_gemv(x.cpu().numpy(), lin["packed"].reshape(E, R, -1),
@@ -157,8 +157,10 @@ def test_packed_linear_vs_oracle(cuda, B, R, K):
     ref = np.asarray(ref, np.float32)
     assert got.shape == (B, R)
     assert rel_err(got, ref) <= TOL
-    # only fp16 rounding-boundary cases may differ, by one ulp
-    assert (got == ref).mean() >= 0.98
+    # fp32 summation order (the offset-dequant path sums M + n products) moves the
+    # result by ~1e-5 of max|y|; after the two fp16 roundings that is at most 2 ulp
+    ulp = np.spacing(np.abs(ref).astype(np.float16)).astype(np.float32)
+    assert np.all(np.abs(got - ref) <= 2 * ulp + 2e-5 * np.abs(ref).max())
 
 
 # ------------------------------------------------------------------ router
