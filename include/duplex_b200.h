@@ -37,6 +37,7 @@ extern "C" {
 #define DUPLEX_ERR_WORKSPACE 4    /* workspace too small */
 #define DUPLEX_ERR_CUDA 5         /* a CUDA runtime call failed (see duplex_last_cuda_error) */
 #define DUPLEX_ERR_UNSUPPORTED 6  /* shape outside what the kernels implement */
+#define DUPLEX_ERR_SCRATCH_LIMIT 7 /* problem needs more than the static scratch of a _noalloc call */
 
 /* ---- device-side error word bits (written with atomicOr into `err`, never trap) */
 #define DUPLEX_DEVERR_EXPERT 1    /* an expert id outside [0, E) was clamped to 0 */
@@ -155,6 +156,27 @@ int duplex_moe_forward(const void* x, int act_dtype, int32_t T, const void* gate
                        void* out, float* w_out,
                        int32_t* sel_out, void* workspace, size_t workspace_bytes,
                        int32_t* err, float rms_eps, int pdl, void* stream);
+
+/*
+ * moe_forward_noalloc -- no counterpart in the reference.  Same computation and
+ * arguments as duplex_moe_forward, minus the workspace: for callers that cannot
+ * call cudaMalloc (a real-time frame loop, where an allocation can synchronise the
+ * device and miss the frame deadline, or a C host without a caching allocator).
+ * The scratch is a file-scope device array of duplex_moe_noalloc_scratch_bytes()
+ * (1.25 MiB) per GPU, kept until the process exits; problems that need more
+ * (duplex_moe_workspace_bytes larger than that) return DUPLEX_ERR_SCRATCH_LIMIT.
+ * The first call on a device looks the array's address up (make it before any
+ * stream capture).  All calls share the array: calls that overlap on the GPU race
+ * and must be serialised by the caller.  Nothing is allocated.
+ */
+size_t duplex_moe_noalloc_scratch_bytes(void);
+int duplex_moe_forward_noalloc(const void* x, int act_dtype, int32_t T, const void* gate_w,
+                               const void* gate_b, int32_t E, int32_t H, int32_t I,
+                               int32_t top_k, int32_t norm_topk, const void* gu_tiles,
+                               const void* dn_tiles, int scale_dtype, int has_zeros,
+                               int32_t group, const void* residual, void* out, float* w_out,
+                               int32_t* sel_out, int32_t* err, float rms_eps, int pdl,
+                               void* stream);
 
 #ifdef __cplusplus
 }

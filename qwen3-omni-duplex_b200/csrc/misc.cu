@@ -80,6 +80,8 @@ extern "C" const char* duplex_error_string(int status) {
     case DUPLEX_ERR_WORKSPACE: return "workspace too small";
     case DUPLEX_ERR_CUDA: return "CUDA runtime error";
     case DUPLEX_ERR_UNSUPPORTED: return "shape not supported by the kernels";
+    case DUPLEX_ERR_SCRATCH_LIMIT:
+      return "problem needs more scratch than the no-allocation entry point's static array";
     default: return "unknown status";
   }
 }

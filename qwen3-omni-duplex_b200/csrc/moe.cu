@@ -12,6 +12,9 @@
 #include "common.cuh"
 #include "moe.cuh"
 
+#include <map>
+#include <mutex>
+
 namespace duplex {
 
 int record_cuda(cudaError_t e);
@@ -354,4 +357,68 @@ extern "C" int duplex_moe_forward(const void* x, int act_dtype, int32_t T, const
                             dn_tiles, reinterpret_cast<const MoePlan*>(ws + L.plan),
                             rms_eps > 0.f ? (const void*)(ws + L.xn) : x, ws + L.act, residual,
                             out, err, max_units, pdl != 0, st);
+}
+
+// ---------------------------------------------------------------------------
+// No-allocation variant of duplex_moe_forward.
+//
+// Some callers cannot call cudaMalloc (or any allocating routine) for the MoE
+// scratch: a real-time frame loop such as the duplex clock path, where an
+// allocation can synchronise the device and blow the 80 ms frame deadline, and
+// plain C hosts that have no caching allocator to hand them a workspace.  For
+// them the scratch lives in this file-scope device array instead.  It is a fixed
+// kNoAllocScratchBytes per GPU, held by every GPU that loads the library until
+// the process exits.  Its device address is looked up once per device with
+// cudaGetSymbolAddress (on the first call made on that device, which should
+// therefore happen before any stream capture).  Every call shares the array and
+// finds the previous call's contents in it; the router's arrival counter is the
+// only part that must start at zero and is cleared on every call.  Calls whose
+// executions overlap on the GPU (different streams, or different host threads)
+// race on the array and must be serialised by the caller.
+namespace duplex {
+
+constexpr size_t kNoAllocScratchBytes = (size_t)1280 * 1024;
+static __device__ __align__(256) uint8_t g_moe_scratch[kNoAllocScratchBytes];
+
+static int noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static std::map<int, void*> by_device;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return record_cuda(e);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = by_device.find(dev);
+  if (it == by_device.end()) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_moe_scratch);
+    if (e != cudaSuccess) return record_cuda(e);
+    it = by_device.emplace(dev, ptr).first;
+  }
+  *out = it->second;
+  return DUPLEX_OK;
+}
+
+}  // namespace duplex
+
+extern "C" size_t duplex_moe_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+extern "C" int duplex_moe_forward_noalloc(
+    const void* x, int act_dtype, int32_t T, const void* gate_w, const void* gate_b, int32_t E,
+    int32_t H, int32_t I, int32_t top_k, int32_t norm_topk, const void* gu_tiles,
+    const void* dn_tiles, int scale_dtype, int has_zeros, int32_t group, const void* residual,
+    void* out, float* w_out, int32_t* sel_out, int32_t* err, float rms_eps, int pdl,
+    void* stream) {
+  if (T < 1 || E < 1 || H < 1 || I < 1 || top_k < 1) return DUPLEX_ERR_ARG;
+  const MoeScratch L = moe_scratch_layout(T, E, H, I, top_k);
+  if (L.total > kNoAllocScratchBytes) return DUPLEX_ERR_SCRATCH_LIMIT;
+  void* ws = nullptr;
+  int rc = noalloc_scratch(&ws);
+  if (rc) return rc;
+  // the router's arrival counter must start at zero
+  rc = record_cuda(cudaMemsetAsync(reinterpret_cast<uint8_t*>(ws) + L.counter, 0, sizeof(int),
+                                   (cudaStream_t)stream));
+  if (rc) return rc;
+  return duplex_moe_forward(x, act_dtype, T, gate_w, gate_b, E, H, I, top_k, norm_topk, gu_tiles,
+                            dn_tiles, scale_dtype, has_zeros, group, residual, out, w_out,
+                            sel_out, ws, kNoAllocScratchBytes, err, rms_eps, pdl, stream);
 }

@@ -47,6 +47,11 @@ _SIGNATURES = {
                             _c_i32, _c_i32, _c_ptr, _c_ptr, _c_int, _c_int, _c_i32, _c_ptr,
                             _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr, _c_f32, _c_int,
                             _c_ptr], _c_int),
+    "duplex_moe_noalloc_scratch_bytes": ([], _c_size),
+    "duplex_moe_forward_noalloc": ([_c_ptr, _c_int, _c_i32, _c_ptr, _c_ptr, _c_i32, _c_i32,
+                                    _c_i32, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_int, _c_int,
+                                    _c_i32, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_f32,
+                                    _c_int, _c_ptr], _c_int),
 }
 
 _lib = None

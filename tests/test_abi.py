@@ -35,7 +35,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 def test_version_and_errors(lib):
     assert lib.duplex_version() >= 100
-    for code in range(0, 7):
+    for code in range(0, 8):
         assert lib.duplex_error_string(code)
     assert b"unknown" in lib.duplex_error_string(99)
 
