@@ -196,18 +196,17 @@ def run_ours(args):
     ms_e2e = bu.max_over_ranks(e0.elapsed_time(e1), dev)
     e2e_value = ws * K / (ms_e2e / 1e3)
 
-    # roofline unit: the decode MoE layer (router + gate|up + down, PDL-chained),
-    # config 0 geometry, timed over the 24 distinct layers of the stack
+    # roofline unit: the decode MoE layer (router, top-k, gate|up, down, combine) of
+    # config 0, timed over the 24 distinct MoE layers of the stack in one persistent
+    # launch: x -> MoE(rms(x)) layer after layer
+    from duplex.clock import MoEChain
     moes = [L.moe for L in stack.layers]
-    hbuf = [torch.zeros(1, HIDDEN, device=dev, dtype=torch.float16) for _ in range(2)]
+    chain = MoEChain(moes, rms_eps=1e-6, residual=False)
     hx = torch.zeros(1, HIDDEN, device=dev, dtype=torch.float16)
+    hout = torch.zeros(1, HIDDEN, device=dev, dtype=torch.float16)
 
     def moe_chain():
-        h = hx
-        for j, m in enumerate(moes):
-            o = hbuf[j % 2]
-            m.forward_into(h, o, rms_eps=1e-6)
-            h = o
+        chain.forward_into(hx, hout)
 
     moe_chain()
     torch.cuda.synchronize(dev)
@@ -264,8 +263,9 @@ def run_ours(args):
                      "frac": bytes_step / (ms_step * 1e-3) / 1e9 / peak},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": None,
-                     "kernel": "decode MoE layer (router + gate|up + down, PDL chain), "
-                               "config 0 geometry, batch 1",
+                     "kernel": "decode MoE layer (router, top-k, gate|up, down, combine) in the "
+                               "persistent stack kernel, config 0 geometry, batch 1, 24 distinct "
+                               "layers per launch",
                      "us_per_launch": us_moe, "algorithmic_bytes": mb,
                      "peak_kind": f"{peak_kind} (copy bandwidth, MEASURED_PEAKS.json)"},
         "cpu_baseline": cpu,

@@ -158,6 +158,37 @@ int duplex_moe_forward(const void* x, int act_dtype, int32_t T, const void* gate
                        int32_t* err, float rms_eps, int pdl, void* stream);
 
 /*
+ * Persistent clock-path stack -- the reference's clock path (src/duplex/streaming/clock.py:
+ * 162-197) runs Thinker layers 0..23 per frame with TritonPackedLinear q/k/v/o and
+ * FusedPackedMoE; this is every int4 linear of n_layers such layers for T <= 8 tokens in ONE
+ * launch: per layer q|k|v of rms(h), o of q (+ h) -> h1, router / top-k / plan on rms(h1),
+ * gate|up + SiLU, down + combine (+ h1 when moe_residual) -> next h.  With has_attn == 0 a
+ * layer is only the MoE (x -> MoE(rms(x)) (+ x)).  `layers` is a DEVICE array of n_layers
+ * descriptors (tiles from duplex_repack_tiles: qkv [qkv_R][H], o [H][q_dim], gate|up with
+ * pair_halves, down).  The attention core is not part of it: o reads the first q_dim
+ * outputs of q|k|v.  H, I, q_dim and group multiples of 64; scale dtype == act dtype.
+ * workspace: duplex_stack_workspace_bytes; the kernel's grid barrier counter in it is
+ * cleared by a memset issued on the same stream before the launch.
+ */
+typedef struct duplex_stack_layer {
+  const void* qkv_tiles;
+  const void* o_tiles;
+  const void* gate_w;
+  const void* gate_b;
+  const void* gu_tiles;
+  const void* dn_tiles;
+} duplex_stack_layer;
+
+int duplex_stack_workspace_bytes(int32_t T, int32_t H, int32_t E, int32_t I, int32_t top_k,
+                                 int32_t qkv_R, size_t* bytes);
+int duplex_stack_forward(const duplex_stack_layer* layers, int32_t n_layers, int32_t has_attn,
+                         int32_t moe_residual, const void* x_in, void* out, int act_dtype,
+                         int scale_dtype, int has_zeros, int32_t T, int32_t H, int32_t E,
+                         int32_t I, int32_t top_k, int32_t norm_topk, int32_t qkv_R,
+                         int32_t q_dim, int32_t group, float rms_eps, void* workspace,
+                         size_t workspace_bytes, int32_t* err, void* stream);
+
+/*
  * moe_forward_noalloc -- no counterpart in the reference.  Same computation and
  * arguments as duplex_moe_forward, minus the workspace: for callers that cannot
  * call cudaMalloc (a real-time frame loop, where an allocation can synchronise the

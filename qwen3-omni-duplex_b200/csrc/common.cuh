@@ -101,6 +101,10 @@ DEVI uint64_t policy_evict_first() {
   return pol;
 }
 
+// order this thread's view of generic-proxy global writes (made visible to it by an
+// acquire) before its subsequent async-proxy (bulk copy) reads of global memory
+DEVI void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
 DEVI void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

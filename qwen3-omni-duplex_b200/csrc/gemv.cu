@@ -30,6 +30,7 @@
 #include "common.cuh"
 #include "moe.cuh"
 #include "tiles.cuh"
+#include "gemv_core.cuh"
 
 #include <mutex>
 #include <set>
@@ -37,9 +38,6 @@
 
 namespace duplex {
 
-constexpr int kCW = 16;  // consumer warps
-constexpr int kConsumers = kCW * 32;
-constexpr int kThreads = kConsumers + 32;
 constexpr int kStagesMax = 16;
 
 enum : int { kPlain = 0, kLinear = 1, kGateUp = 2, kDown = 3 };
@@ -120,114 +118,6 @@ DEVI void stage_decode(const GemvParams& p, const int* unit_e, int tile, int s, 
     xs = s;
   }
 }
-
-DEVI bool wait_limited(uint64_t* bar, uint32_t parity, long long limit) {
-  const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > limit) return false;
-  }
-  return true;
-}
-
-// position of logical column c inside its 8-column group in fragment order
-// (stored sequence x0 x4 x1 x5 x2 x6 x3 x7)
-DEVI int frag_pos(int c) {
-  const int r = c & 7;
-  return (c & ~7) | ((r & 3) << 1) | (r >> 2);
-}
-
-DEVI uint4 to_frag_order(uint4 v) {
-  uint4 o;
-  o.x = __byte_perm(v.x, v.z, 0x5410);  // (x0, x4)
-  o.y = __byte_perm(v.x, v.z, 0x7632);  // (x1, x5)
-  o.z = __byte_perm(v.y, v.w, 0x5410);  // (x2, x6)
-  o.w = __byte_perm(v.y, v.w, 0x7632);  // (x3, x7)
-  return o;
-}
-
-DEVI float2 scale_pair(uint32_t s2, __half*) { return __half22float2(*reinterpret_cast<__half2*>(&s2)); }
-DEVI float2 scale_pair(uint32_t s2, __nv_bfloat16*) {
-  return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&s2));
-}
-
-// ---- exact path (per-stage activations): item = (record, column pair p)
-// acc += (scale * colw) * sum over the pair of (n - z) * x
-template <typename T, typename S, bool G32>
-DEVI void item_exact(const uint8_t* rec, const TileGeom& tg, int p, int lane, const uint8_t* xrow,
-                     bool xon, bool xraw, float w0, float w1, float (&acc)[4]) {
-  const int g = lane >> 2;
-  const uint4 w = *reinterpret_cast<const uint4*>(rec + (((uint32_t)p << 5) + lane) * 16u);
-  uint4 xa = make_uint4(0, 0, 0, 0), xb = make_uint4(0, 0, 0, 0);
-  if (xon) {
-    xa = *reinterpret_cast<const uint4*>(xrow + (uint32_t)p * 128u);
-    xb = *reinterpret_cast<const uint4*>(xrow + (uint32_t)p * 128u + 64u);
-    if (xraw) {
-      xa = to_frag_order(xa);
-      xb = to_frag_order(xb);
-    }
-  }
-  const uint32_t* sc = reinterpret_cast<const uint32_t*>(rec + tg.off_scale);
-  const uint8_t* zr = rec + tg.off_zero;
-  uint32_t A[4], B[4], lo_a, hi_a, lo_b, hi_b;
-#pragma unroll
-  for (int h = 0; h < (G32 ? 2 : 1); ++h) {
-    const int grp = G32 ? 2 * p + h : (p >> tg.gshift);
-    const uint32_t zz = tg.has_zeros ? (uint32_t)zr[grp * 8 + g] : 0x88u;
-    Dq<T>::consts(zz & 15u, lo_a, hi_a);
-    Dq<T>::consts(zz >> 4, lo_b, hi_b);
-    float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
-    if (!G32 || h == 0) {
-      Dq<T>::expand(w.x, w.y, lo_a, hi_a, lo_b, hi_b, A, B);
-      MmaOp<T>::run(c0, A[0], A[1], A[2], A[3], xa.x, xa.y);
-      MmaOp<T>::run(c1, B[0], B[1], B[2], B[3], xa.z, xa.w);
-    }
-    if (!G32 || h == 1) {
-      Dq<T>::expand(w.z, w.w, lo_a, hi_a, lo_b, hi_b, A, B);
-      MmaOp<T>::run(c0, A[0], A[1], A[2], A[3], xb.x, xb.y);
-      MmaOp<T>::run(c1, B[0], B[1], B[2], B[3], xb.z, xb.w);
-    }
-    const float2 s = scale_pair(sc[grp * 8 + g], (S*)nullptr);
-    acc[0] = fmaf(s.x * w0, c0[0] + c1[0], acc[0]);
-    acc[1] = fmaf(s.x * w1, c0[1] + c1[1], acc[1]);
-    acc[2] = fmaf(s.y * w0, c0[2] + c1[2], acc[2]);
-    acc[3] = fmaf(s.y * w1, c0[3] + c1[3], acc[3]);
-  }
-}
-
-// ---- offset path (shared activations): per column pair, four MMAs of (M + n) x
-// plus one correction MMA (corr_a coefficients x the pair's exact column sums);
-// the group scale is applied when the warp's run of a group ends.
-template <typename T, typename S>
-struct OffAcc {
-  float d0[4], d1[4];
-  int rec, grp;
-  uint32_t ca0, ca1;
-  DEVI void reset() {
-#pragma unroll
-    for (int r = 0; r < 4; ++r) d0[r] = d1[r] = 0.f;
-  }
-  DEVI void window(uint32_t wa, uint32_t wb, uint4 xv) {
-    uint32_t A[4], B[4];
-    DqOff<T>::expand(wa, wb, A, B);
-    MmaOp<T>::run(d0, A[0], A[1], A[2], A[3], xv.x, xv.y);
-    MmaOp<T>::run(d1, B[0], B[1], B[2], B[3], xv.z, xv.w);
-  }
-  DEVI void set_group(const uint8_t* r, const TileGeom& tg, int lane, uint32_t wmask) {
-    const int g = lane >> 2, t = lane & 3;
-    const uint32_t zz = tg.has_zeros ? (uint32_t)r[tg.off_zero + grp * 8 + g] : 0x88u;
-    DqOff<T>::corr_a(zz & 15u, zz >> 4, t, wmask, ca0, ca1);
-  }
-  DEVI void correct(uint32_t bcorr) { MmaOp<T>::run(d0, ca0, ca1, 0u, 0u, bcorr, 0u); }
-  DEVI void flush(const uint8_t* r, const TileGeom& tg, int lane, float (&acc)[4]) {
-    const int g = lane >> 2;
-    const float2 s = scale_pair(reinterpret_cast<const uint32_t*>(r + tg.off_scale)[grp * 8 + g],
-                                (S*)nullptr);
-    acc[0] = fmaf(s.x, d0[0] + d1[0], acc[0]);
-    acc[1] = fmaf(s.x, d0[1] + d1[1], acc[1]);
-    acc[2] = fmaf(s.y, d0[2] + d1[2], acc[2]);
-    acc[3] = fmaf(s.y, d0[3] + d1[3], acc[3]);
-  }
-};
 
 template <typename T, typename S, int MODE, bool G32, bool CORR>
 __global__ void __launch_bounds__(kThreads, 1) dq_gemv_kernel(const __grid_constant__ GemvParams p) {
@@ -369,101 +259,9 @@ __global__ void __launch_bounds__(kThreads, 1) dq_gemv_kernel(const __grid_const
         unit_w[idx] = p.plan->unit_w[idx];
   }
   if (p.x_mode == kXShared) {
-    // activations -> shared memory in fragment order, zero beyond K; with the
-    // offset path (fp16) odd columns are stored divided by 16 (exact)
-    const int nq = tg.Kp >> 3;
-    const uint8_t* xb = reinterpret_cast<const uint8_t*>(p.x);
-    float* invs = red + kCW * kMaxTokens;  // per-row RMS scale
-    if (tid < kMaxTokens) invs[tid] = 1.f;
-    if (p.rms_eps > 0.f) {
-      // weightless RMSNorm per row: x * rsqrt(mean(x^2) + eps), rounded to T
-      for (int n = 0; n < p.ncols; ++n) {
-        float a = 0.f;
-        for (int q = tid; q < (tg.K >> 3); q += kConsumers) {
-          const uint4 v = *reinterpret_cast<const uint4*>(xb + ((size_t)n * p.x_col_stride + q * 8) * 2);
-          const T* e = reinterpret_cast<const T*>(&v);
-#pragma unroll
-          for (int k = 0; k < 8; ++k) a = fmaf(to_f32<T>(e[k]), to_f32<T>(e[k]), a);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-        if (lane == 0) red[warp * kMaxTokens + n] = a;
-      }
-      named_bar_sync(1, kConsumers);
-      if (tid < p.ncols) {
-        float tot = 0.f;
-#pragma unroll
-        for (int w = 0; w < kCW; ++w) tot += red[w * kMaxTokens + tid];
-        invs[tid] = 1.0f / sqrtf(tot / (float)tg.K + p.rms_eps);
-      }
-    }
-    named_bar_sync(1, kConsumers);
-    for (int idx = tid; idx < p.ncols * nq; idx += kConsumers) {
-      const int n = idx / nq, q = idx - n * nq;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (q * 8 < tg.K) {
-        v = *reinterpret_cast<const uint4*>(xb + ((size_t)n * p.x_col_stride + q * 8) * 2);
-        if (p.rms_eps > 0.f) {
-          const float inv = invs[n];
-          T* e = reinterpret_cast<T*>(&v);
-#pragma unroll
-          for (int k = 0; k < 8; ++k) e[k] = from_f32<T>(to_f32<T>(e[k]) * inv);
-        }
-      }
-      uint4 o = to_frag_order(v);
-      if (CORR && DqOff<T>::kOddDiv16) {
-        const __half2 q16 = __float2half2_rn(0.0625f);
-        __half2 hy = __hmul2(*reinterpret_cast<__half2*>(&o.y), q16);
-        __half2 hw = __hmul2(*reinterpret_cast<__half2*>(&o.w), q16);
-        o.y = *reinterpret_cast<uint32_t*>(&hy);
-        o.w = *reinterpret_cast<uint32_t*>(&hw);
-      }
-      *reinterpret_cast<uint4*>(xsh + (uint32_t)n * p.x_pitch + (uint32_t)q * 16u) = o;
-    }
-    named_bar_sync(1, kConsumers);
-    if (CORR) {
-      // exact activation sums per 32-column window in 16-bit parts; word (pair p,
-      // lane g*4 + t) is the correction MMA's B fragment for column g: t = 0 / 1 ->
-      // window 2p (fp16: even / odd columns), t = 2 / 3 -> window 2p + 1
-      for (int idx = tid; idx < tg.npairs * kMaxTokens; idx += kConsumers) {
-        const int pp = idx / kMaxTokens, n = idx - pp * kMaxTokens;
-        uint32_t b[4] = {0u, 0u, 0u, 0u};
-        if (n < p.ncols) {
-          const uint8_t* row = xsh + (uint32_t)n * p.x_pitch + (uint32_t)pp * 128u;
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            float se = 0.f, so = 0.f;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const uint4 o = *reinterpret_cast<const uint4*>(row + h * 64 + q * 16);
-              const T* e = reinterpret_cast<const T*>(&o);
-              // fragment order: e0 = x0, e1 = x4, e2 = x1, e3 = x5, e4 = x2, e5 = x6, e6 = x3, e7 = x7
-              se += (to_f32<T>(e[0]) + to_f32<T>(e[1])) + (to_f32<T>(e[4]) + to_f32<T>(e[5]));
-              so += (to_f32<T>(e[2]) + to_f32<T>(e[3])) + (to_f32<T>(e[6]) + to_f32<T>(e[7]));
-            }
-            if (DqOff<T>::kOddDiv16) {
-              so *= 16.f;
-              const T eh = from_f32<T>(se), oh = from_f32<T>(so);
-              const T el = from_f32<T>(se - to_f32<T>(eh)), ol = from_f32<T>(so - to_f32<T>(oh));
-              b[2 * h] = (uint32_t)*reinterpret_cast<const uint16_t*>(&eh) |
-                         ((uint32_t)*reinterpret_cast<const uint16_t*>(&el) << 16);
-              b[2 * h + 1] = (uint32_t)*reinterpret_cast<const uint16_t*>(&oh) |
-                             ((uint32_t)*reinterpret_cast<const uint16_t*>(&ol) << 16);
-            } else {
-              const float x = se + so;
-              const T x1 = from_f32<T>(x);
-              const T x2 = from_f32<T>(x - to_f32<T>(x1));
-              const T x3 = from_f32<T>(x - to_f32<T>(x1) - to_f32<T>(x2));
-              b[2 * h] = (uint32_t)*reinterpret_cast<const uint16_t*>(&x1) |
-                         ((uint32_t)*reinterpret_cast<const uint16_t*>(&x2) << 16);
-              b[2 * h + 1] = (uint32_t)*reinterpret_cast<const uint16_t*>(&x3);
-            }
-          }
-        }
-        uint4* dst = reinterpret_cast<uint4*>(corr + pp * 32 + n * 4);
-        *dst = make_uint4(b[0], b[1], b[2], b[3]);
-      }
-    }
+    stage_x_shared<T, CORR>(xsh, p.x_pitch, reinterpret_cast<const uint8_t*>(p.x), p.x_col_stride,
+                            p.ncols, tg, p.rms_eps, red, tid, warp, lane);
+    if (CORR) build_corr<T>(corr, xsh, p.x_pitch, tg.npairs, p.ncols, tid);
   }
   named_bar_sync(1, kConsumers);
   // zero the padded activation tail of every per-stage activation row (never copied)
@@ -501,50 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1) dq_gemv_kernel(const __grid_const
       const int lo = ib > s * ips ? ib - s * ips : 0;
       const int hi = ie < (s + 1) * ips ? ie - s * ips : ips;
       if (CORR) {
-        const uint8_t* xrow = xsh + (uint32_t)g * p.x_pitch + (uint32_t)t * 16u;
-        OffAcc<T, S> oa;
-        oa.reset();
-        oa.rec = -1;
-        oa.grp = -1;
-        for (int it = lo; it < hi; ++it) {
-          const int r = it >= npairs ? 1 : 0;
-          const int pp = it - r * npairs;
-          const uint8_t* rec = st + (uint32_t)r * tg.rec_bytes;
-          const uint4 w = *reinterpret_cast<const uint4*>(rec + (((uint32_t)pp << 5) + lane) * 16u);
-          const uint32_t bc = corr[pp * 32 + lane];
-          uint4 xa = make_uint4(0, 0, 0, 0), xb = make_uint4(0, 0, 0, 0);
-          if (xon) {
-            xa = *reinterpret_cast<const uint4*>(xrow + (uint32_t)pp * 128u);
-            xb = *reinterpret_cast<const uint4*>(xrow + (uint32_t)pp * 128u + 64u);
-          }
-          if (G32) {
-            // each 32-column window is its own group
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              oa.reset();
-              oa.grp = 2 * pp + h;
-              oa.set_group(rec, tg, lane, 1u << h);
-              oa.window(h ? w.z : w.x, h ? w.w : w.y, h ? xb : xa);
-              oa.correct(bc);
-              oa.flush(rec, tg, lane, r ? acc1 : acc0);
-            }
-          } else {
-            const int grp = pp >> tg.gshift;
-            if (grp != oa.grp || r != oa.rec) {
-              if (oa.grp >= 0)
-                oa.flush(st + (uint32_t)oa.rec * tg.rec_bytes, tg, lane, oa.rec ? acc1 : acc0);
-              oa.reset();
-              oa.grp = grp;
-              oa.rec = r;
-              oa.set_group(rec, tg, lane, 3u);
-            }
-            oa.window(w.x, w.y, xa);
-            oa.window(w.z, w.w, xb);
-            oa.correct(bc);
-          }
-        }
-        if (!G32 && oa.grp >= 0)
-          oa.flush(st + (uint32_t)oa.rec * tg.rec_bytes, tg, lane, oa.rec ? acc1 : acc0);
+        consume_corr<T, S, G32>(st, tg, lo, hi, lane, xsh, p.x_pitch, corr, xon, acc0, acc1);
       } else {
         const uint8_t* xrow = st + p.off_x + (uint32_t)g * p.x_pitch + (uint32_t)t * 16u;
         float w0 = 1.f, w1 = 1.f;
@@ -561,23 +316,10 @@ __global__ void __launch_bounds__(kThreads, 1) dq_gemv_kernel(const __grid_const
     }
 
     // ---- split-K reduction across the consumer warps, then the epilogue
-#pragma unroll
-    for (int r = 0; r < 4; ++r) red[(warp * 8 + r) * 32 + lane] = acc0[r];
-    if (MODE == kGateUp) {
-#pragma unroll
-      for (int r = 0; r < 4; ++r) red[(warp * 8 + 4 + r) * 32 + lane] = acc1[r];
-    }
-    named_bar_sync(1, kConsumers);
+    float v, v2;
+    reduce_tile(red, acc0, acc1, MODE == kGateUp, tid, warp, lane, v, v2);
     if (tid < 128) {
       const int n = tid >> 4, r = tid & 15;
-      const int gl = (r & 7) * 4 + (n >> 1);
-      const int ri = (r >> 3) * 2 + (n & 1);
-      float v = 0.f, v2 = 0.f;
-#pragma unroll
-      for (int w = 0; w < kCW; ++w) {
-        v += red[(w * 8 + ri) * 32 + gl];
-        if (MODE == kGateUp) v2 += red[(w * 8 + 4 + ri) * 32 + gl];
-      }
       if (MODE == kPlain) {
         const int slot = tile / p.Rb;
         const int row = (tile - slot * p.Rb) * 16 + r;

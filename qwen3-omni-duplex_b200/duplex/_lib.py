@@ -52,7 +52,20 @@ _SIGNATURES = {
                                     _c_i32, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_int, _c_int,
                                     _c_i32, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_f32,
                                     _c_int, _c_ptr], _c_int),
+    "duplex_stack_workspace_bytes": ([_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
+                                      ctypes.POINTER(ctypes.c_size_t)], _c_int),
+    "duplex_stack_forward": ([_c_ptr, _c_i32, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_int, _c_int,
+                              _c_int, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
+                              _c_i32, _c_i32, _c_f32, _c_ptr, _c_size, _c_ptr, _c_ptr], _c_int),
 }
+
+
+class StackLayer(ctypes.Structure):
+    """duplex_stack_layer of include/duplex_b200.h (device pointers of one layer)."""
+    _fields_ = [("qkv_tiles", ctypes.c_void_p), ("o_tiles", ctypes.c_void_p),
+                ("gate_w", ctypes.c_void_p), ("gate_b", ctypes.c_void_p),
+                ("gu_tiles", ctypes.c_void_p), ("dn_tiles", ctypes.c_void_p)]
+
 
 _lib = None
 

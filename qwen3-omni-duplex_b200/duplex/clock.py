@@ -12,10 +12,13 @@ the hidden state stays finite through the stack:
        -> h1  = h + W_o . qkv[:, :4096]        (K 4096)
        -> h'  = h1 + MoE(rms(h1))              (router + 128-expert top-8 int4 MoE)
 
-Each layer is 5 kernels (fused qkv, o, router, gate|up, down) chained with
-programmatic dependent launch; `capture()` records the whole stack in one CUDA
-graph and `decode()` is the user-facing call: host -> device copy of the
-step's tokens, graph replay, device -> host copy of the result.
+By default the whole stack is ONE launch of the persistent clock-path kernel
+(`duplex_stack_forward`: one CTA per SM, grid barriers between the phases of a
+layer, weights streamed ahead across phases).  `fused=False` runs the same math
+as 5 kernels per layer (fused qkv, o, router, gate|up, down) chained with
+programmatic dependent launch.  `capture()` records a step in a CUDA graph and
+`decode()` is the user-facing call: host -> device copy of the step's tokens,
+graph replay, device -> host copy of the result.
 """
 
 from __future__ import annotations
@@ -64,6 +67,63 @@ def moe_bytes(moe: FusedPackedMoE, T: int = 1) -> int:
     return E * H * moe.gate.weight.element_size() + k * per + 2 * T * H * 2
 
 
+class Persistent:
+    """Device-side layer descriptors and workspace of one `duplex_stack_forward` program."""
+
+    def __init__(self, descs, has_attn, moe_residual, T, H, E, I, top_k, norm, qkv_R, q_dim,
+                 group, has_zeros, dtype, rms_eps, device):
+        arr = (_lib.StackLayer * len(descs))(*descs)
+        raw = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8)
+        self.desc = raw.to(device)
+        self.n = len(descs)
+        n = _lib.ctypes.c_size_t()
+        _lib.call("duplex_stack_workspace_bytes", T, H, E, I, top_k, qkv_R, _lib.ctypes.byref(n))
+        self.ws = torch.zeros(n.value, dtype=torch.uint8, device=device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.args = (has_attn, moe_residual, T, H, E, I, top_k, norm, qkv_R, q_dim, group,
+                     has_zeros, _lib.dtype_code(dtype), float(rms_eps))
+
+    def run(self, x, out):
+        (has_attn, moe_res, T, H, E, I, top_k, norm, qkv_R, q_dim, group, hz, code,
+         eps) = self.args
+        _lib.call("duplex_stack_forward", _lib.ptr(self.desc), self.n, has_attn, moe_res,
+                  _lib.ptr(x), _lib.ptr(out), code, code, hz, T, H, E, I, top_k, norm, qkv_R,
+                  q_dim, group, eps, _lib.ptr(self.ws), self.ws.numel(), _lib.ptr(self.err),
+                  _lib.stream_of(x))
+        return out
+
+    def device_errors(self) -> int:
+        v = int(self.err.item())
+        self.err.zero_()
+        return v
+
+
+def _moe_desc(moe: FusedPackedMoE, qkv=None, o=None):
+    g = moe.gate
+    return _lib.StackLayer(
+        qkv_tiles=None if qkv is None else qkv.tiles.buf.data_ptr(),
+        o_tiles=None if o is None else o.tiles.buf.data_ptr(),
+        gate_w=g.weight.data_ptr(), gate_b=None if g.bias is None else g.bias.data_ptr(),
+        gu_tiles=moe.gu_tiles.buf.data_ptr(), dn_tiles=moe.dn_tiles.buf.data_ptr())
+
+
+class MoEChain:
+    """n MoE layers chained through the persistent kernel: x -> MoE(rms(x)) (+ x).
+    The decode-MoE layer of config 0, repeated over distinct weights."""
+
+    def __init__(self, moes, rms_eps=RMS_EPS, residual=False, T=1):
+        m0 = moes[0]
+        dev = m0.gu_tiles.buf.device
+        self.moes = moes
+        self.p = Persistent([_moe_desc(m) for m in moes], 0, 1 if residual else 0, T, m0.hidden,
+                            m0.num_experts, m0.inter, m0.top_k, 1 if m0.norm_topk_prob else 0, 0,
+                            0, m0.group, 1 if m0.has_zeros else 0, m0.gate.weight.dtype, rms_eps,
+                            dev)
+
+    def forward_into(self, x, out):
+        return self.p.run(x, out)
+
+
 class ClockLayer:
     def __init__(self, qkv: TritonPackedLinear, o: TritonPackedLinear, moe: FusedPackedMoE):
         self.qkv, self.o, self.moe = qkv, o, moe
@@ -73,8 +133,10 @@ class ClockStack:
     """Thinker layers [0, n) of the clock path on the B200 kernels (batch T <= 8)."""
 
     def __init__(self, layers, hidden=synth.THINKER_HIDDEN, q_dim=None, T=1, rms_eps=RMS_EPS,
-                 device="cuda", dtype=torch.float16):
+                 device="cuda", dtype=torch.float16, fused=True):
         self.layers = layers
+        self.fused = fused
+        self._persist = None
         self.hidden, self.T, self.rms_eps = hidden, T, rms_eps
         self.qkv_dim = layers[0].qkv.out_features
         self.q_dim = q_dim or layers[0].o.in_features
@@ -92,7 +154,7 @@ class ClockStack:
                   dtype=torch.float16, E=synth.THINKER_EXPERTS, H=synth.THINKER_HIDDEN,
                   I=synth.THINKER_MOE_INTER, top_k=synth.THINKER_ACTIVE,
                   n_q=synth.THINKER_Q_HEADS, n_kv=synth.THINKER_KV_HEADS, head_dim=synth.HEAD_DIM,
-                  T=1):
+                  T=1, fused=True):
         """Seeded synthetic weights with the benchmark distributions, drawn on `device`."""
         gen = torch.Generator(device=device).manual_seed(seed)
         q, kv = n_q * head_dim, n_kv * head_dim
@@ -108,10 +170,11 @@ class ClockStack:
                                               gu_zeros=m["gu_zeros"], dn_zeros=m["dn_zeros"],
                                               dtype=dtype, device=device)
             layers.append(ClockLayer(qkv, o, moe))
-        return cls(layers, H, q, T, device=device, dtype=dtype)
+        return cls(layers, H, q, T, device=device, dtype=dtype, fused=fused)
 
     @classmethod
-    def from_arrays(cls, arrays, top_k, device="cuda", dtype=torch.float16, T=1, group=None):
+    def from_arrays(cls, arrays, top_k, device="cuda", dtype=torch.float16, T=1, group=None,
+                    fused=True):
         """From per-layer dicts of numpy/torch arrays (used to check the stack against
         the oracle): keys qkv_packed/qkv_scale/qkv_zeros, o_*, gate_w, gu_*, dn_*."""
         t = lambda a: None if a is None else torch.as_tensor(a).to(device)  # noqa: E731
@@ -129,7 +192,7 @@ class ClockStack:
                                               device=device)
             layers.append(ClockLayer(qkv, o, moe))
         H = arrays[0]["gate_w"].shape[1]
-        return cls(layers, H, None, T, device=device, dtype=dtype)
+        return cls(layers, H, None, T, device=device, dtype=dtype, fused=fused)
 
     # ------------------------------------------------------------------ execution
     def bytes_per_step(self) -> int:
@@ -139,10 +202,22 @@ class ClockStack:
         return n
 
     def kernels_per_step(self) -> int:
-        return 5 * len(self.layers)
+        return 1 if self.fused else 5 * len(self.layers)
+
+    def persistent(self) -> Persistent:
+        if self._persist is None:
+            m0 = self.layers[0].moe
+            self._persist = Persistent(
+                [_moe_desc(L.moe, L.qkv, L.o) for L in self.layers], 1, 1, self.T, self.hidden,
+                m0.num_experts, m0.inter, m0.top_k, 1 if m0.norm_topk_prob else 0, self.qkv_dim,
+                self.q_dim, m0.group, 1 if m0.has_zeros else 0, self.dtype, self.rms_eps,
+                self.device)
+        return self._persist
 
     def step_into(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         """Enqueue one decode step for x [T, H] on the current stream; result in out."""
+        if self.fused:
+            return self.persistent().run(x, out)
         h_in = x
         n = len(self.layers)
         for i, L in enumerate(self.layers):
@@ -183,4 +258,7 @@ class ClockStack:
         return out_host
 
     def device_errors(self) -> int:
-        return sum(L.moe.device_errors() for L in self.layers)
+        n = sum(L.moe.device_errors() for L in self.layers)
+        if self._persist is not None:
+            n += self._persist.device_errors()
+        return n

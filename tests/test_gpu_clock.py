@@ -27,11 +27,12 @@ def small_layers(n, seed=3, H=256, q=256, kv=64, E=16, I=128, top_k=4, group=128
     return out
 
 
-@pytest.mark.parametrize("T", [1, 3])
-def test_clock_stack_vs_oracle(cuda, T):
+@pytest.mark.parametrize("T", [1, 3, 8])
+@pytest.mark.parametrize("fused", [True, False])
+def test_clock_stack_vs_oracle(cuda, T, fused):
     from duplex.clock import ClockStack
     layers = small_layers(3)
-    st = ClockStack.from_arrays(layers, top_k=4, device=cuda, T=T)
+    st = ClockStack.from_arrays(layers, top_k=4, device=cuda, T=T, fused=fused)
     x = np.random.default_rng(1).standard_normal((T, 256)).astype(np.float16)
     out = torch.zeros(T, 256, device=cuda, dtype=torch.float16)
     st.step_into(torch.from_numpy(x).to(cuda), out)
@@ -58,3 +59,49 @@ def test_clock_stack_graph_and_decode(cuda):
     assert torch.equal(oh, eager.cpu())
     assert torch.isfinite(eager).all()
     assert st.device_errors() == 0
+
+
+def test_persistent_matches_kernel_chain_thinker_geometry(cuda):
+    """The one-launch stack and the 5-kernels-per-layer chain agree at Thinker geometry."""
+    from duplex.clock import ClockStack
+    a = ClockStack.synthetic(n_layers=3, seed=5, device=cuda, fused=True)
+    b = ClockStack(a.layers, fused=False, device=cuda)
+    x = torch.randn(1, 2048, device=cuda, dtype=torch.float16,
+                    generator=torch.Generator(device=cuda).manual_seed(3))
+    ya, yb = torch.zeros_like(x), torch.zeros_like(x)
+    a.step_into(x, ya)
+    b.step_into(x, yb)
+    torch.cuda.synchronize()
+    ya, yb = ya.float().cpu().numpy(), yb.float().cpu().numpy()
+    assert np.isfinite(ya).all()
+    assert np.abs(ya - yb).max() <= 2e-3 * np.abs(yb).max()
+    assert a.device_errors() == 0
+
+
+@pytest.mark.parametrize("T", [1, 4])
+def test_moe_chain_vs_modules(cuda, T):
+    """x -> MoE(rms(x)) over several layers in one launch == the per-layer module calls."""
+    from duplex.clock import MoEChain
+    from duplex.streaming.fused_packed_moe import FusedPackedMoE
+    moes = []
+    for l in range(3):
+        L = synth.moe_layer_np(seed=40 + l, E=32, H=512, I=128, top_k=4, group=128, T=1)
+        t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+        moes.append(FusedPackedMoE.from_stacked(t(L["gate_w"]), t(L["gu_packed"]), t(L["gu_scale"]),
+                                                t(L["dn_packed"]), t(L["dn_scale"]), 4,
+                                                gu_zeros=t(L["gu_zeros"]), dn_zeros=t(L["dn_zeros"]),
+                                                dtype=torch.float16, device=cuda))
+    chain = MoEChain(moes, rms_eps=1e-6, residual=False, T=T)
+    x = torch.randn(T, 512, device=cuda, dtype=torch.float16,
+                    generator=torch.Generator(device=cuda).manual_seed(7))
+    got = torch.zeros_like(x)
+    chain.forward_into(x, got)
+    h = x
+    for m in moes:
+        o = torch.zeros_like(x)
+        m.forward_into(h, o, rms_eps=1e-6)
+        h = o
+    torch.cuda.synchronize()
+    g, r = got.float().cpu().numpy(), h.float().cpu().numpy()
+    assert np.abs(g - r).max() <= 2e-3 * np.abs(r).max()
+    assert chain.p.device_errors() == 0
