@@ -42,6 +42,9 @@ extern "C" {
 /* ---- device-side error word bits (written with atomicOr into `err`, never trap) */
 #define DUPLEX_DEVERR_EXPERT 1    /* an expert id outside [0, E) was clamped to 0 */
 #define DUPLEX_DEVERR_TIMEOUT 2   /* a bounded pipeline wait gave up */
+/* duplex_stack_forward also ORs, from this bit up, which of its waits gave up:
+ * 1 ring slot free, 2 routing plan, 3 ring slot filled, 4 exchange word, 5 drain. */
+#define DUPLEX_DEVERR_SITE_SHIFT 8
 
 /* ---- dtype codes */
 #define DUPLEX_DTYPE_F16 0
@@ -167,8 +170,13 @@ int duplex_moe_forward(const void* x, int act_dtype, int32_t T, const void* gate
  * descriptors (tiles from duplex_repack_tiles: qkv [qkv_R][H], o [H][q_dim], gate|up with
  * pair_halves, down).  The attention core is not part of it: o reads the first q_dim
  * outputs of q|k|v.  H, I, q_dim and group multiples of 64; scale dtype == act dtype.
- * workspace: duplex_stack_workspace_bytes; the kernel's grid barrier counter in it is
- * cleared by a memset issued on the same stream before the launch.
+ * workspace: duplex_stack_workspace_bytes, ZERO-FILLED before the first call and kept
+ * unchanged between calls (phases hand data over through flagged words in it, and a
+ * generation counter in it, advanced by every launch, keeps the flags of earlier
+ * launches from matching).  One call at a time per workspace.  err is required: a
+ * wait that times out sets DUPLEX_DEVERR_TIMEOUT in it, and while that bit stays set
+ * later launches give up at once instead of waiting.  The launch is cooperative (one
+ * CTA per SM, all co-resident).
  */
 typedef struct duplex_stack_layer {
   const void* qkv_tiles;

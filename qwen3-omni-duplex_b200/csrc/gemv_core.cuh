@@ -284,165 +284,252 @@ DEVI void consume_corr(const uint8_t* st, const TileGeom& tg, int lo, int hi, in
     oa.flush(st + (uint32_t)oa.rec * tg.rec_bytes, tg, lane, oa.rec ? acc1 : acc0);
 }
 
-// Per-lane constant parts of the correction coefficients (see DqOff::corr_a):
-// coefficient = base | (z << shift), duplicated into both halves.
-template <typename T> struct CorrLane;
-template <> struct CorrLane<__half> {
-  static DEVI void init(int t, uint32_t& base, int& shift) {
-    base = (t & 1) ? 0xD400u : 0xE400u;
-    shift = (t & 1) ? 4 : 0;
-  }
-};
-template <> struct CorrLane<__nv_bfloat16> {
-  static DEVI void init(int, uint32_t& base, int& shift) {
-    base = 0xC300u;
-    shift = 0;
-  }
-};
+// ---- offset path with the correction applied in fp32, once per group --------
+// The MMAs of one group accumulate D = sum (M + n) x' over the group's columns,
+// x' being the staged activations (fp16: odd columns stored / 16).  With the
+// per-token sums of the columns covered
+//   fp16: P = 1024 (SE + SO'),  Q = SE + 16 SO'   (SE: even columns, SO': odd, staged)
+//   bf16: P = 128 SX,            Q = SX
+// the exact dot product is D - P - z Q; it is scaled by the group scale (and a
+// per-column weight) in fp32.  `gsum` holds (P, Q) as float2 [unit][8 tokens] per
+// 64-column pair (per 32-column window when the group is 32), so a warp that
+// covers only part of a group subtracts exactly the part it covered; lane (g, t)
+// reads tokens 2t, 2t + 1 as one float4.
+template <typename S>
+DEVI void flush_group(float (&acc)[4], const float (&d0)[4], const float (&d1)[4],
+                      const uint8_t* rec, const TileGeom& tg, int grp, int g, float4 gs,
+                      float w0, float w1) {
+  const uint32_t zz = tg.has_zeros ? (uint32_t)rec[tg.off_zero + grp * 8 + g] : 0x88u;
+  const float za = (float)(zz & 15u), zb = (float)(zz >> 4);
+  const float2 s =
+      scale_pair(reinterpret_cast<const uint32_t*>(rec + tg.off_scale)[grp * 8 + g], (S*)nullptr);
+  acc[0] = fmaf(s.x * w0, (d0[0] + d1[0]) - fmaf(za, gs.y, gs.x), acc[0]);
+  acc[1] = fmaf(s.x * w1, (d0[1] + d1[1]) - fmaf(za, gs.w, gs.z), acc[1]);
+  acc[2] = fmaf(s.y * w0, (d0[2] + d1[2]) - fmaf(zb, gs.y, gs.x), acc[2]);
+  acc[3] = fmaf(s.y * w1, (d0[3] + d1[3]) - fmaf(zb, gs.w, gs.z), acc[3]);
+}
 
-DEVI uint32_t dup16(uint32_t v) { return v | (v << 16); }
+template <typename T>
+DEVI void mma_window(float (&d0)[4], float (&d1)[4], uint32_t wa, uint32_t wb, uint4 x) {
+  uint32_t A[4], B[4];
+  DqOff<T>::expand(wa, wb, A, B);
+  MmaOp<T>::run(d0, A[0], A[1], A[2], A[3], x.x, x.y);
+  MmaOp<T>::run(d1, B[0], B[1], B[2], B[3], x.z, x.w);
+}
 
-// Offset path, pair-major: the warp walks columns pairs [pb, pe) and, for every pair,
-// all NREC records of the stage, so the activation fragments and the correction
-// word of a pair are loaded once for all records.  Group constants (scales, zero
-// points -> correction coefficients) are refreshed only when the group changes.
-template <typename T, typename S, int NREC>
-DEVI void consume_corr_pm(const uint8_t* st, const TileGeom& tg, int pb, int pe, int lane,
-                          const uint8_t* xsh, uint32_t pitch, const uint32_t* corr, bool xon,
-                          float (&acc)[NREC][4]) {
+DEVI void zero4(float (&d)[4]) { d[0] = d[1] = d[2] = d[3] = 0.f; }
+
+// Pair-major walk over column pairs [pb, pe) of the NREC records of a stage that
+// share one set of staged activation rows (xsh, fragment order): each pair's
+// activation fragments are loaded once for all records; acc[r] collects record r
+// (rows g, g + 8 x tokens 2t, 2t + 1 of lane (g, t)).
+template <typename T, typename S, int NREC, bool G32>
+DEVI void pm_offset(const uint8_t* st, const TileGeom& tg, int pb, int pe, int lane,
+                    const uint8_t* xsh, uint32_t pitch, const float2* gsum, bool xon,
+                    float (&acc)[NREC][4]) {
   const int g = lane >> 2, t = lane & 3;
-  const uint8_t* xrow = xsh + (uint32_t)g * pitch + (uint32_t)t * 16u;
-  uint32_t cbase;
-  int csh;
-  CorrLane<T>::init(t, cbase, csh);
-  float d0[NREC][4], d1[NREC][4];
-  uint32_t ca0[NREC], ca1[NREC];
-  float sa[NREC], sb[NREC];
-  int cur = -1;
-  const uint8_t* xp = xrow + (uint32_t)pb * 128u;
+  const uint8_t* xp = xsh + (uint32_t)g * pitch + (uint32_t)t * 16u + (uint32_t)pb * 128u;
   const uint8_t* wp = st + (((uint32_t)pb << 5) + lane) * 16u;
-  for (int p = pb; p < pe; ++p, xp += 128, wp += 512) {
-    const int grp = p >> tg.gshift;
-    if (grp != cur) {
-      if (cur >= 0) {
-#pragma unroll
-        for (int r = 0; r < NREC; ++r) {
-          acc[r][0] = fmaf(sa[r], d0[r][0] + d1[r][0], acc[r][0]);
-          acc[r][1] = fmaf(sa[r], d0[r][1] + d1[r][1], acc[r][1]);
-          acc[r][2] = fmaf(sb[r], d0[r][2] + d1[r][2], acc[r][2]);
-          acc[r][3] = fmaf(sb[r], d0[r][3] + d1[r][3], acc[r][3]);
-        }
+  int p = pb;
+  while (p < pe) {
+    if (G32) {
+      uint4 xa = make_uint4(0, 0, 0, 0), xb = make_uint4(0, 0, 0, 0);
+      if (xon) {
+        xa = *reinterpret_cast<const uint4*>(xp);
+        xb = *reinterpret_cast<const uint4*>(xp + 64);
       }
-      cur = grp;
+      const float4 g0 = *reinterpret_cast<const float4*>(gsum + (2 * p) * 8 + 2 * t);
+      const float4 g1 = *reinterpret_cast<const float4*>(gsum + (2 * p + 1) * 8 + 2 * t);
 #pragma unroll
       for (int r = 0; r < NREC; ++r) {
         const uint8_t* rec = st + (uint32_t)r * tg.rec_bytes;
-        const uint32_t zz = tg.has_zeros ? (uint32_t)rec[tg.off_zero + grp * 8 + g] : 0x88u;
-        ca0[r] = dup16(cbase | ((zz & 15u) << csh));
-        ca1[r] = dup16(cbase | ((zz >> 4) << csh));
-        const float2 s2 =
-            scale_pair(reinterpret_cast<const uint32_t*>(rec + tg.off_scale)[grp * 8 + g], (S*)nullptr);
-        sa[r] = s2.x;
-        sb[r] = s2.y;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) d0[r][q] = d1[r][q] = 0.f;
+        const uint4 w = *reinterpret_cast<const uint4*>(wp + (uint32_t)r * tg.rec_bytes);
+        float d0[4], d1[4];
+        zero4(d0);
+        zero4(d1);
+        mma_window<T>(d0, d1, w.x, w.y, xa);
+        flush_group<S>(acc[r], d0, d1, rec, tg, 2 * p, g, g0, 1.f, 1.f);
+        zero4(d0);
+        zero4(d1);
+        mma_window<T>(d0, d1, w.z, w.w, xb);
+        flush_group<S>(acc[r], d0, d1, rec, tg, 2 * p + 1, g, g1, 1.f, 1.f);
       }
-    }
-    uint4 xa = make_uint4(0, 0, 0, 0), xb = make_uint4(0, 0, 0, 0);
-    if (xon) {
-      xa = *reinterpret_cast<const uint4*>(xp);
-      xb = *reinterpret_cast<const uint4*>(xp + 64);
-    }
-    const uint32_t bc = corr[p * 32 + lane];
+      ++p;
+      xp += 128;
+      wp += 512;
+    } else {
+      const int grp = p >> tg.gshift;
+      int pend = (grp + 1) << tg.gshift;
+      if (pend > pe) pend = pe;
+      float d0[NREC][4], d1[NREC][4];
 #pragma unroll
-    for (int r = 0; r < NREC; ++r) {
-      const uint4 w = *reinterpret_cast<const uint4*>(wp + (uint32_t)r * tg.rec_bytes);
-      uint32_t A[4], B[4];
-      DqOff<T>::expand(w.x, w.y, A, B);
-      MmaOp<T>::run(d0[r], A[0], A[1], A[2], A[3], xa.x, xa.y);
-      MmaOp<T>::run(d1[r], B[0], B[1], B[2], B[3], xa.z, xa.w);
-      DqOff<T>::expand(w.z, w.w, A, B);
-      MmaOp<T>::run(d0[r], A[0], A[1], A[2], A[3], xb.x, xb.y);
-      MmaOp<T>::run(d1[r], B[0], B[1], B[2], B[3], xb.z, xb.w);
-      MmaOp<T>::run(d0[r], ca0[r], ca1[r], 0u, 0u, bc, 0u);
-    }
-  }
-  if (cur >= 0) {
+      for (int r = 0; r < NREC; ++r) {
+        zero4(d0[r]);
+        zero4(d1[r]);
+      }
+      float4 gs = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (; p < pend; ++p, xp += 128, wp += 512) {
+        const float4 gp = *reinterpret_cast<const float4*>(gsum + p * 8 + 2 * t);
+        gs.x += gp.x;
+        gs.y += gp.y;
+        gs.z += gp.z;
+        gs.w += gp.w;
+        uint4 xa = make_uint4(0, 0, 0, 0), xb = make_uint4(0, 0, 0, 0);
+        if (xon) {
+          xa = *reinterpret_cast<const uint4*>(xp);
+          xb = *reinterpret_cast<const uint4*>(xp + 64);
+        }
 #pragma unroll
-    for (int r = 0; r < NREC; ++r) {
-      acc[r][0] = fmaf(sa[r], d0[r][0] + d1[r][0], acc[r][0]);
-      acc[r][1] = fmaf(sa[r], d0[r][1] + d1[r][1], acc[r][1]);
-      acc[r][2] = fmaf(sb[r], d0[r][2] + d1[r][2], acc[r][2]);
-      acc[r][3] = fmaf(sb[r], d0[r][3] + d1[r][3], acc[r][3]);
+        for (int r = 0; r < NREC; ++r) {
+          const uint4 w = *reinterpret_cast<const uint4*>(wp + (uint32_t)r * tg.rec_bytes);
+          mma_window<T>(d0[r], d1[r], w.x, w.y, xa);
+          mma_window<T>(d0[r], d1[r], w.z, w.w, xb);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < NREC; ++r)
+        flush_group<S>(acc[r], d0[r], d1[r], st + (uint32_t)r * tg.rec_bytes, tg, grp, g, gs, 1.f,
+                       1.f);
     }
   }
 }
 
-// Exact path over items [ib, ie) of `cnt` records that each have their own
-// activation rows (the down projection's units): item = (record us, pair pp),
-// record-major.  w0s / w1s: per-record column weights (routing weights of the
-// lane's two output columns).
-template <typename T, typename S>
-DEVI void consume_exact_rm(const uint8_t* st, const TileGeom& tg, int ib, int ie, int lane,
-                           const uint8_t* xb0, uint32_t xpitch, int rows_per_rec,
-                           const float* colw, bool xon, float (&acc)[4]) {
+// First MMA of a fresh accumulator: D = A B (no accumulator input).
+template <typename T>
+DEVI void mma_first(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                    uint32_t b1) {
+  d[0] = d[1] = d[2] = d[3] = 0.f;
+  MmaOp<T>::run(d, a0, a1, a2, a3, b0, b1);
+}
+
+// pm_offset for the common fixed geometry: the 16 warps each take PPW pairs
+// (npairs == 16 PPW), a whole number of groups of PPG pairs, fully unrolled, one
+// accumulator chain per record.
+template <typename T, typename S, int NREC, int PPW, int PPG>
+DEVI void pm_fixed(const uint8_t* st, const TileGeom& tg, int warp, int lane, const uint8_t* xsh,
+                   uint32_t pitch, const float2* gsum, bool xon, float (&acc)[NREC][4]) {
+  static_assert(PPW % PPG == 0, "warp ranges must hold whole groups");
+  const int g = lane >> 2, t = lane & 3;
+  const int pb = warp * PPW;
+  const uint8_t* xp = xsh + (uint32_t)g * pitch + (uint32_t)t * 16u + (uint32_t)pb * 128u;
+  const uint8_t* wp = st + (((uint32_t)pb << 5) + lane) * 16u;
+  const float2* gp = gsum + pb * 8 + 2 * t;
+#pragma unroll
+  for (int gi = 0; gi < PPW / PPG; ++gi) {
+    float d[NREC][4];
+    float4 gs = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < PPG; ++k) {
+      const int pi = gi * PPG + k;
+      const float4 gq = *reinterpret_cast<const float4*>(gp + pi * 8);
+      gs.x += gq.x;
+      gs.y += gq.y;
+      gs.z += gq.z;
+      gs.w += gq.w;
+      uint4 xa = make_uint4(0, 0, 0, 0), xb = make_uint4(0, 0, 0, 0);
+      if (xon) {
+        xa = *reinterpret_cast<const uint4*>(xp + pi * 128);
+        xb = *reinterpret_cast<const uint4*>(xp + pi * 128 + 64);
+      }
+#pragma unroll
+      for (int r = 0; r < NREC; ++r) {
+        const uint4 w = *reinterpret_cast<const uint4*>(wp + (uint32_t)r * tg.rec_bytes + pi * 512);
+        uint32_t A[4], B[4];
+        DqOff<T>::expand(w.x, w.y, A, B);
+        if (k == 0)
+          mma_first<T>(d[r], A[0], A[1], A[2], A[3], xa.x, xa.y);
+        else
+          MmaOp<T>::run(d[r], A[0], A[1], A[2], A[3], xa.x, xa.y);
+        MmaOp<T>::run(d[r], B[0], B[1], B[2], B[3], xa.z, xa.w);
+        DqOff<T>::expand(w.z, w.w, A, B);
+        MmaOp<T>::run(d[r], A[0], A[1], A[2], A[3], xb.x, xb.y);
+        MmaOp<T>::run(d[r], B[0], B[1], B[2], B[3], xb.z, xb.w);
+      }
+    }
+    const int grp = (pb + gi * PPG) / PPG;
+    const float zero4v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < NREC; ++r)
+      flush_group<S>(acc[r], d[r], zero4v, st + (uint32_t)r * tg.rec_bytes, tg, grp, g, gs, 1.f, 1.f);
+  }
+}
+
+// Record-major walk over items [lo, hi) of a stage whose records each have their
+// own activation rows (the MoE down projection: record us = unit us, rows
+// us * rows_per_unit + token): item = (record, column pair), record-major.  gsum is
+// [record][gr_stride pairs (windows when G32)][8 tokens]; colw [record][8] weights
+// token columns.
+template <typename T, typename S, bool G32>
+DEVI void rm_offset(const uint8_t* st, const TileGeom& tg, int lo, int hi, int lane,
+                    const uint8_t* xd, uint32_t xpitch, int rows_per_unit, const float2* gsum,
+                    int gr_stride, const float* colw, bool xon, float (&acc)[4]) {
   const int g = lane >> 2, t = lane & 3;
   const int np = tg.npairs;
-  int us = ib / np, pp = ib - us * np;
-  int cur_grp = -1, cur_us = -1;
-  uint32_t lo_a = 0, hi_a = 0, lo_b = 0, hi_b = 0;
-  float fa0 = 0.f, fa1 = 0.f, fb0 = 0.f, fb1 = 0.f;
-  float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int it = ib; it < ie; ++it) {
+  int us = lo / np, pp = lo - us * np;
+  int it = lo;
+  while (it < hi) {
     const uint8_t* rec = st + (uint32_t)us * tg.rec_bytes;
-    const int grp = pp >> tg.gshift;
-    if (grp != cur_grp || us != cur_us) {
-      if (cur_grp >= 0) {
-        acc[0] = fmaf(fa0, c0[0] + c1[0], acc[0]);
-        acc[1] = fmaf(fa1, c0[1] + c1[1], acc[1]);
-        acc[2] = fmaf(fb0, c0[2] + c1[2], acc[2]);
-        acc[3] = fmaf(fb1, c0[3] + c1[3], acc[3]);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) c0[q] = c1[q] = 0.f;
+    const uint8_t* xrow =
+        xd + (uint32_t)(us * rows_per_unit + g) * xpitch + (uint32_t)t * 16u + (uint32_t)pp * 128u;
+    const uint8_t* wp = rec + (((uint32_t)pp << 5) + lane) * 16u;
+    const float w0 = colw[us * 8 + 2 * t], w1 = colw[us * 8 + 2 * t + 1];
+    const float2* gsu = gsum + (size_t)us * gr_stride * 8;
+    if (G32) {
+      uint4 xa = make_uint4(0, 0, 0, 0), xb = make_uint4(0, 0, 0, 0);
+      if (xon) {
+        xa = *reinterpret_cast<const uint4*>(xrow);
+        xb = *reinterpret_cast<const uint4*>(xrow + 64);
       }
-      cur_grp = grp;
-      cur_us = us;
-      const uint32_t zz = tg.has_zeros ? (uint32_t)rec[tg.off_zero + grp * 8 + g] : 0x88u;
-      Dq<T>::consts(zz & 15u, lo_a, hi_a);
-      Dq<T>::consts(zz >> 4, lo_b, hi_b);
-      const float2 s2 =
-          scale_pair(reinterpret_cast<const uint32_t*>(rec + tg.off_scale)[grp * 8 + g], (S*)nullptr);
-      const float w0 = colw[us * 8 + 2 * t], w1 = colw[us * 8 + 2 * t + 1];
-      fa0 = s2.x * w0;
-      fa1 = s2.x * w1;
-      fb0 = s2.y * w0;
-      fb1 = s2.y * w1;
+      const uint4 w = *reinterpret_cast<const uint4*>(wp);
+      float d0[4], d1[4];
+      zero4(d0);
+      zero4(d1);
+      mma_window<T>(d0, d1, w.x, w.y, xa);
+      flush_group<S>(acc, d0, d1, rec, tg, 2 * pp, g,
+                     *reinterpret_cast<const float4*>(gsu + (2 * pp) * 8 + 2 * t), w0, w1);
+      zero4(d0);
+      zero4(d1);
+      mma_window<T>(d0, d1, w.z, w.w, xb);
+      flush_group<S>(acc, d0, d1, rec, tg, 2 * pp + 1, g,
+                     *reinterpret_cast<const float4*>(gsu + (2 * pp + 1) * 8 + 2 * t), w0, w1);
+      ++it;
+      if (++pp == np) {
+        pp = 0;
+        ++us;
+      }
+    } else {
+      const int grp = pp >> tg.gshift;
+      int pend = (grp + 1) << tg.gshift;
+      if (pend > np) pend = np;
+      int n_it = pend - pp;
+      if (n_it > hi - it) n_it = hi - it;
+      float d0[4], d1[4];
+      zero4(d0);
+      zero4(d1);
+      float4 gs = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k = 0; k < n_it; ++k, xrow += 128, wp += 512) {
+        const float4 gp = *reinterpret_cast<const float4*>(gsu + (pp + k) * 8 + 2 * t);
+        gs.x += gp.x;
+        gs.y += gp.y;
+        gs.z += gp.z;
+        gs.w += gp.w;
+        uint4 xa = make_uint4(0, 0, 0, 0), xb = make_uint4(0, 0, 0, 0);
+        if (xon) {
+          xa = *reinterpret_cast<const uint4*>(xrow);
+          xb = *reinterpret_cast<const uint4*>(xrow + 64);
+        }
+        const uint4 w = *reinterpret_cast<const uint4*>(wp);
+        mma_window<T>(d0, d1, w.x, w.y, xa);
+        mma_window<T>(d0, d1, w.z, w.w, xb);
+      }
+      flush_group<S>(acc, d0, d1, rec, tg, grp, g, gs, w0, w1);
+      it += n_it;
+      pp += n_it;
+      if (pp == np) {
+        pp = 0;
+        ++us;
+      }
     }
-    const uint4 w = *reinterpret_cast<const uint4*>(rec + (((uint32_t)pp << 5) + lane) * 16u);
-    uint4 xa = make_uint4(0, 0, 0, 0), xb = make_uint4(0, 0, 0, 0);
-    if (xon) {
-      const uint8_t* xr = xb0 + (uint32_t)(us * rows_per_rec + g) * xpitch + (uint32_t)t * 16u +
-                          (uint32_t)pp * 128u;
-      xa = *reinterpret_cast<const uint4*>(xr);
-      xb = *reinterpret_cast<const uint4*>(xr + 64);
-    }
-    uint32_t A[4], B[4];
-    Dq<T>::expand(w.x, w.y, lo_a, hi_a, lo_b, hi_b, A, B);
-    MmaOp<T>::run(c0, A[0], A[1], A[2], A[3], xa.x, xa.y);
-    MmaOp<T>::run(c1, B[0], B[1], B[2], B[3], xa.z, xa.w);
-    Dq<T>::expand(w.z, w.w, lo_a, hi_a, lo_b, hi_b, A, B);
-    MmaOp<T>::run(c0, A[0], A[1], A[2], A[3], xb.x, xb.y);
-    MmaOp<T>::run(c1, B[0], B[1], B[2], B[3], xb.z, xb.w);
-    if (++pp == np) {
-      pp = 0;
-      ++us;
-    }
-  }
-  if (cur_grp >= 0) {
-    acc[0] = fmaf(fa0, c0[0] + c1[0], acc[0]);
-    acc[1] = fmaf(fa1, c0[1] + c1[1], acc[1]);
-    acc[2] = fmaf(fb0, c0[2] + c1[2], acc[2]);
-    acc[3] = fmaf(fb1, c0[3] + c1[3], acc[3]);
   }
 }
 

@@ -8,25 +8,29 @@
 //   D  top-k / softmax / renormalise / unit plan, redundantly in every CTA
 //   G  gate|up of the selected experts, SiLU(gate)*up           -> act
 //   N  down projection over all units, routing-weighted combine (+ h1) -> h'
-// separated by grid-wide barriers (a global arrival counter, bounded spin).  The
-// producer warp walks the same schedule and streams the weight records of the
-// CTA's tiles into a shared-memory ring with one bulk copy each, independent of
-// the phase barriers: the static weights (q|k|v, o, gate rows) of the next
-// phases are in flight while the current phase computes, and while the router
-// decides it prefetches the next layer's static weights into L2.  Expert records
-// follow as soon as this CTA has built the routing plan; the down projection's
-// activation rows are copied once the gate|up phase has finished everywhere.
 //
-// Numerics are those of dq_gemv_kernel (gemv.cu) and route_kernel (moe.cu): offset
-// dequantisation with a correction MMA for Q/O/G, exact (n - z) for N, fp32
-// accumulation, logits rounded to the activation dtype, fp32 softmax, ties of the
-// top-k to the lower expert id.
+// Phases hand their outputs to the next phase through small buffers in global
+// memory, separated by grid-wide barriers: one red.release per CTA on a counter
+// and one acquiring poller per CTA, the fastest all-to-all hand-off measured on
+// this part (~1.3 us for 148 CTAs; polling the data words themselves from many
+// threads turns the few lines involved into L2 hot spots and is several times
+// slower).  Outputs are read back through L2 (ld.global.cg).  Per MoE layer
+// there are three barriers (h, logits, act), per clock layer five (+ qkv, h1).
+//
+// The producer warp walks the same schedule and streams the weight records of the
+// CTA's tiles into a shared-memory ring with one bulk copy each: the static
+// weights (q|k|v, o, gate rows) are in flight ahead of their phase, the next
+// layer's static weights are prefetched into L2 while the router decides, and
+// the experts' gate|up and down records are all issued as soon as this CTA has
+// built the routing plan.
+//
+// Numerics follow dq_gemv_kernel (gemv.cu) and route_kernel (moe.cu): offset
+// dequantisation ((M + n) in fp16/bf16 straight into mma.sync, fp32 accumulation,
+// the exact group correction D - P - z Q applied in fp32 with the group scale),
+// logits rounded to the activation dtype, fp32 softmax, ties of the top-k to the
+// lower expert id.
 #include "gemv_core.cuh"
 #include "moe.cuh"
-
-#include <mutex>
-#include <set>
-#include <utility>
 
 namespace duplex {
 
@@ -38,54 +42,71 @@ struct StackParams {
   const duplex_stack_layer* layers;
   int n_layers, T, H, E, I, top_k, norm, q_dim, qkv_R, has_attn, moe_residual;
   TileGeom tq, to, tgu, tdn;
-  int RbQ, RbO, RbGU, RbD;
+  int RbQ, RbO, RbD;
   float rms_eps;
   const void* x_in;
   void* out;
-  void* hbuf0;
-  void* hbuf1;
-  void* qkv;
-  void* h1;
-  void* act;
-  float* logits;
-  unsigned* barrier;
+  void* hbuf[2];  // layer input / output h   [T][H] (layer parity)
+  void* qkv;      // q|k|v                     [T][qkv_R]
+  void* h1;       // h + o(q)                  [T][H]
+  float* logits;  // [T][E]
+  void* act;      // SiLU(gate)*up            [units][T][I]
+  unsigned* barrier;  // grid barrier counter, zeroed before the launch
   int* err;
-  int nslots, ups;
-  uint32_t slot_bytes, off_ring, off_xsh, off_plain, off_xd, x_pitch, xd_pitch;
+  int nslots, ups, act_units;
+  uint32_t slot_bytes, off_ring, off_x, off_plain, off_gsum, x_pitch, xd_pitch;
 };
 
 // fixed shared-memory map (bytes)
 constexpr uint32_t kSFull = 0;        // 16 mbarriers
 constexpr uint32_t kSEmpty = 128;     // 16 mbarriers
 constexpr uint32_t kSPlan = 256;      // mbarrier: plan of the current layer ready
-constexpr uint32_t kSActR = 264;      // mbarrier: gate|up finished grid-wide
 constexpr uint32_t kSAbort = 272;     // int
 constexpr uint32_t kSNUnits = 276;    // int
-constexpr uint32_t kSCnt = 320;       // 8 ints (plan compaction)
 constexpr uint32_t kSSel = 512;       // [8 tokens][8] ints
-constexpr uint32_t kSW = 768;         // [8 tokens][8] floats
+constexpr uint32_t kSSelBits = 768;   // [8 tokens][8] words: selected experts
 constexpr uint32_t kSUnitE = 1024;    // kMaxUnits ints
 constexpr uint32_t kSUnitM = 1280;    // kMaxUnits uints
 constexpr uint32_t kSUnitW = 1536;    // kMaxUnits * 8 floats
 constexpr uint32_t kSLogit = 3584;    // [8][kMaxExperts] floats
-constexpr uint32_t kSRed = kSLogit + 8 * kMaxExperts * 4;   // kCW * 8 * 32 floats
-constexpr uint32_t kSCorr = kSRed + kCW * 8 * 32 * 4;       // correction table (dynamic size)
+// cross-warp reductions (kCW warps x 2 records x kRedStride floats) and scratch
+constexpr int kRedStride = 152;  // swizzled [8 tokens][16 rows] block, see red_at
+constexpr uint32_t kSRed = kSLogit + 8 * kMaxExperts * 4;
+constexpr uint32_t kSRedBytes = kCW * 2 * kRedStride * 4;
+constexpr uint32_t kSFixedEnd = kSRed + kSRedBytes;
 constexpr int kSlotsMax = 16;
+constexpr int kMaxChunks = 8;  // 8-value chunks of staged rows per consumer thread
 
-DEVI bool mbar_test(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
+// Which wait of this kernel gave up first: err bits from DUPLEX_DEVERR_SITE_SHIFT.
+enum : int { kSiteEmpty = 1, kSitePlan = 2, kSiteFull = 3, kSiteGrid = 4, kSiteDrain = 5 };
+
+// Code size matters here: every layer walks all phases, so the per-phase work
+// lives in one non-inlined copy each (staging, tile compute, router, plan, the
+// barrier, the slow path of the waits) to keep the loop inside the instruction
+// cache.
+#define DEVN __device__ __noinline__
+
+DEVI void give_up(volatile int* abort, int* err, int site) {
+  *abort = 1;
+  set_error(err, DUPLEX_DEVERR_TIMEOUT | (site << DUPLEX_DEVERR_SITE_SHIFT));
 }
 
-DEVI void prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+DEVN void wait_phase_slow(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
+                          int site) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort) return;
+    if (clock64() - t0 > kWaitLimitCycles) {
+      give_up(abort, err, site);
+      return;
+    }
+  }
+}
+
+// Bounded wait on an mbarrier phase; returns at once when this CTA has given up.
+DEVI void wait_phase(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int site) {
+  if (*abort || mbar_try_wait(bar, parity)) return;
+  wait_phase_slow(bar, parity, abort, err, site);
 }
 
 DEVI unsigned ld_acquire_gpu(const unsigned* p) {
@@ -94,37 +115,439 @@ DEVI unsigned ld_acquire_gpu(const unsigned* p) {
   return v;
 }
 
-// Grid-wide barrier of the consumer warps of every CTA.  Bounded: after ~2 s it
-// records DUPLEX_DEVERR_TIMEOUT, sets the CTA's abort flag and stops waiting.
-DEVI void grid_sync(const StackParams& p, unsigned& nb, int tid, volatile int* abort) {
+// Grid-wide barrier of the consumer warps of all CTAs, split into arrival and
+// wait so that local work can run in between: the n-th barrier of a launch (n
+// from 1) completes when the counter reaches n * gridDim.x.  grid_arrive follows
+// a consumer barrier, so the CTA's writes before it are released with the
+// arrival (cumulativity), and they are visible to every CTA after grid_wait.
+// Bounded: gives up after ~kWaitLimitCycles, or as soon as any CTA has given up.
+DEVI void grid_arrive(unsigned* counter) {
   named_bar_sync(1, kConsumers);
-  ++nb;
-  if (tid == 0) {
-    __threadfence();
-    atomicAdd(p.barrier, 1u);
-    const unsigned target = nb * gridDim.x;
-    if (!*abort) {
-      const long long t0 = clock64();
-      while (ld_acquire_gpu(p.barrier) < target) {
-        if (clock64() - t0 > kWaitLimitCycles) {
-          *abort = 1;
-          set_error(p.err, DUPLEX_DEVERR_TIMEOUT);
-          break;
-        }
+  if (threadIdx.x == 0)
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
+}
+
+DEVN void grid_wait(unsigned* counter, unsigned n, volatile int* abort, int* err) {
+  if (threadIdx.x == 0 && !*abort) {
+    const unsigned target = n * gridDim.x;
+    const long long t0 = clock64();
+    int k = 0;
+    while ((int)(ld_acquire_gpu(counter) - target) < 0) {
+      if ((++k & 63) == 0 && (*reinterpret_cast<volatile int*>(err) & DUPLEX_DEVERR_TIMEOUT)) {
+        *abort = 1;
+        break;
+      }
+      if (clock64() - t0 > kWaitLimitCycles) {
+        give_up(abort, err, kSiteGrid);
+        break;
       }
     }
-    __threadfence();
   }
   named_bar_sync(1, kConsumers);
 }
 
-template <typename T, typename S>
+// floor(i / d) for 0 <= i < 2^32 / d, d > 0: one multiply-high with m = fast_div_m(d)
+DEVI uint32_t fast_div_m(uint32_t d) { return 0xFFFFFFFFu / d + 1u; }
+DEVI uint32_t fast_div(uint32_t i, uint32_t m, uint32_t d) { return d == 1u ? i : __umulhi(i, m); }
+
+// Stage `nrows` rows of K 16-bit values (row r at src + r * row_stride elements,
+// read through L2; K % 64 == 0, nrows * K <= 32768) into shared memory in
+// fragment order for the offset path (fp16: odd columns / 16), optionally
+// RMS-normalised per row (rounded to T) and copied in natural order to
+// `plain_out`, and build the correction sums of every `cw` 32-column windows (a
+// pair, or a window for group 32): gsum [unit][K / (32 cw)][8 tokens] float2,
+// row r = unit * rows_per_unit + token.  `part` is 16 KB of scratch.  Runs on the
+// 512 consumer threads; starts and ends with a consumer-wide barrier.
+// mode kStageAll does everything; kStageNorm stops after the (normalised)
+// natural-order rows are in xsh (and plain_out); kStageFrag takes them from there
+// and does the rest (fragment order, correction sums).
+enum : int { kStageAll = 0, kStageNorm = 1, kStageFrag = 2 };
+
+template <typename T>
+DEVN void stage_rows(const uint8_t* src, int row_stride, int nrows, int K, int rows_per_unit,
+                     uint8_t* xsh, uint32_t pitch, bool rms, float eps, uint8_t* plain_out,
+                     float2* gsum, int cw, float* part, int mode) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int nq = K >> 3;  // 8-value chunks per row, a multiple of 8
+  const int total = nrows * nq;
+  const uint32_t mq = fast_div_m((uint32_t)nq), mu = fast_div_m((uint32_t)rows_per_unit);
+  // sums of squares: one partial per 32 chunks when rows are whole warps, else
+  // per 8 chunks; each row's partials are added in a fixed order (identical run
+  // to run)
+  const int seg = (nq & 31) == 0 ? 32 : 8;
+  named_bar_sync(1, kConsumers);
+  // pass 1: fetch into xsh in natural order; sums of squares
+  for (int base = 0; mode != kStageFrag && base < total; base += kConsumers) {
+    const int idx = base + tid;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (idx < total) {
+      const int r = (int)fast_div((uint32_t)idx, mq, (uint32_t)nq), q = idx - r * nq;
+      v = __ldcg(reinterpret_cast<const uint4*>(src + ((size_t)r * row_stride + q * 8) * 2));
+      *reinterpret_cast<uint4*>(xsh + (uint32_t)r * pitch + (uint32_t)q * 16u) = v;
+    }
+    if (rms) {
+      float a = 0.f;
+      const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) a = fmaf(to_f32<T>(e[k]), to_f32<T>(e[k]), a);
+      a += __shfl_xor_sync(0xffffffffu, a, 1);
+      a += __shfl_xor_sync(0xffffffffu, a, 2);
+      a += __shfl_xor_sync(0xffffffffu, a, 4);
+      if (seg == 32) {
+        a += __shfl_xor_sync(0xffffffffu, a, 8);
+        a += __shfl_xor_sync(0xffffffffu, a, 16);
+      }
+      if ((lane & (seg - 1)) == 0 && idx < total) part[idx / seg] = a;
+    }
+  }
+  if (mode != kStageFrag) named_bar_sync(1, kConsumers);
+  // pass 2: normalise, natural-order copy, fragment order (+ /16), correction sums
+  const int cq = 4 * cw;  // chunks per correction unit
+  const int Nc = nq / cq;
+  for (int base = 0; base < total; base += kConsumers) {
+    const int idx = base + tid;
+    float se = 0.f, so = 0.f;
+    int r = 0, q = 0;
+    if (idx < total) {
+      r = (int)fast_div((uint32_t)idx, mq, (uint32_t)nq);
+      q = idx - r * nq;
+      uint8_t* cp = xsh + (uint32_t)r * pitch + (uint32_t)q * 16u;
+      uint4 o = *reinterpret_cast<const uint4*>(cp);
+      if (rms && mode != kStageFrag) {
+        const int per = nq / seg;
+        const float* pr = part + r * per;
+        float a = 0.f;
+        for (int c = 0; c < per; ++c) a += pr[c];
+        const float sc = 1.0f / sqrtf(a / (float)K + eps);
+        T* e = reinterpret_cast<T*>(&o);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) e[k] = from_f32<T>(to_f32<T>(e[k]) * sc);
+      }
+      if (plain_out && mode != kStageFrag)
+        *reinterpret_cast<uint4*>(plain_out + ((size_t)r * K + q * 8) * 2) = o;
+      if (mode != kStageNorm) {
+        o = to_frag_order(o);
+        if (DqOff<T>::kOddDiv16) {
+          const __half2 q16 = __float2half2_rn(0.0625f);
+          __half2 hy = __hmul2(*reinterpret_cast<__half2*>(&o.y), q16);
+          __half2 hw = __hmul2(*reinterpret_cast<__half2*>(&o.w), q16);
+          o.y = *reinterpret_cast<uint32_t*>(&hy);
+          o.w = *reinterpret_cast<uint32_t*>(&hw);
+        }
+        // fragment order: e0 = x0, e1 = x4, e2 = x1, e3 = x5, e4 = x2, e5 = x6, e6 = x3, e7 = x7
+        const T* e = reinterpret_cast<const T*>(&o);
+        se = (to_f32<T>(e[0]) + to_f32<T>(e[1])) + (to_f32<T>(e[4]) + to_f32<T>(e[5]));
+        so = (to_f32<T>(e[2]) + to_f32<T>(e[3])) + (to_f32<T>(e[6]) + to_f32<T>(e[7]));
+      }
+      *reinterpret_cast<uint4*>(cp) = o;
+    }
+    if (mode == kStageNorm) continue;  // uniform: the same for every thread
+    // a correction unit is cq consecutive chunks of one row (aligned lanes)
+    se += __shfl_xor_sync(0xffffffffu, se, 1);
+    so += __shfl_xor_sync(0xffffffffu, so, 1);
+    se += __shfl_xor_sync(0xffffffffu, se, 2);
+    so += __shfl_xor_sync(0xffffffffu, so, 2);
+    if (cq == 8) {
+      se += __shfl_xor_sync(0xffffffffu, se, 4);
+      so += __shfl_xor_sync(0xffffffffu, so, 4);
+    }
+    if (idx < total && (q & (cq - 1)) == 0) {
+      const int u = (int)fast_div((uint32_t)r, mu, (uint32_t)rows_per_unit);
+      const int n = r - u * rows_per_unit;
+      float P, Q;
+      if (DqOff<T>::kOddDiv16) {
+        P = 1024.f * (se + so);
+        Q = fmaf(16.f, so, se);
+      } else {
+        Q = se + so;
+        P = 128.f * Q;
+      }
+      gsum[((size_t)u * Nc + q / cq) * 8 + n] = make_float2(P, Q);
+    }
+  }
+  named_bar_sync(1, kConsumers);
+}
+
+// Cross-warp reduction of one 16-row output tile for NREC records.  Each warp's
+// partial (lane (g, t): rows g, g + 8 x tokens 2t, 2t + 1) goes to a swizzled
+// [token][row] block, (n, r) at n * 16 + r + (n >> 1) * 8, so that both the
+// writes and the readers' column reads are bank-conflict free; only tokens < nT
+// are written.  Threads tid < nT * 16 return the sums of row tid & 15, token
+// tid >> 4 (record 0 in .x, record 1 in .y).  The caller synchronises before
+// `red` is used again.
+DEVI int red_at(int n, int r) { return n * 16 + r + (n >> 1) * 8; }
+static_assert(7 * 16 + 15 + 3 * 8 < kRedStride, "reduction block");
+static_assert(kSRedBytes >= 16384, "scratch users of red: RMS partials, plan keys");
+
+template <int NREC>
+DEVI float2 reduce_rows(float* red, const float (&acc)[NREC][4], int nT, int tid, int warp,
+                        int lane) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int r = 0; r < NREC; ++r) {
+    float* b = red + (warp * NREC + r) * kRedStride;
+    if (2 * t < nT) {
+      b[red_at(2 * t, g)] = acc[r][0];
+      b[red_at(2 * t, g + 8)] = acc[r][2];
+    }
+    if (2 * t + 1 < nT) {
+      b[red_at(2 * t + 1, g)] = acc[r][1];
+      b[red_at(2 * t + 1, g + 8)] = acc[r][3];
+    }
+  }
+  named_bar_sync(1, kConsumers);
+  float v = 0.f, v2 = 0.f;
+  if (tid < nT * 16) {
+    const int a = red_at(tid >> 4, tid & 15);
+#pragma unroll
+    for (int w = 0; w < kCW; ++w) {
+      v += red[(w * NREC) * kRedStride + a];
+      if (NREC == 2) v2 += red[(w * NREC + 1) * kRedStride + a];
+    }
+  }
+  return make_float2(v, v2);
+}
+
+// One ring stage of NREC records sharing the staged rows: the warp's pair range,
+// the slot released, then the cross-warp reduction.  Threads tid < 128 get the
+// sums of row tid & 15, token tid >> 4 (record 0 in .x, record 1 in .y).
+template <typename T, typename S, int NREC, bool G32>
+DEVN float2 tile_pm(const uint8_t* st, const TileGeom tg, const uint8_t* xsh, uint32_t pitch,
+                    const float2* gsum, int nT, float* red, uint64_t* empty_bar) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int np = tg.npairs;
+  float acc[NREC][4];
+#pragma unroll
+  for (int r = 0; r < NREC; ++r) zero4(acc[r]);
+  const bool xon = (lane >> 2) < nT;
+  if (!G32 && tg.gshift == 1 && np == 2 * kCW)
+    pm_fixed<T, S, NREC, 2, 2>(st, tg, warp, lane, xsh, pitch, gsum, xon, acc);
+  else if (!G32 && tg.gshift == 1 && np == 4 * kCW)
+    pm_fixed<T, S, NREC, 4, 2>(st, tg, warp, lane, xsh, pitch, gsum, xon, acc);
+  else
+    pm_offset<T, S, NREC, G32>(st, tg, (warp * np) / kCW, ((warp + 1) * np) / kCW, lane, xsh,
+                               pitch, gsum, xon, acc);
+  __syncwarp();
+  if (lane == 0) mbar_arrive(empty_bar);
+  return reduce_rows<NREC>(red, acc, nT, tid, warp, lane);
+}
+
+// One down-projection stage: `cnt` unit records, each with its own staged rows;
+// returns this lane's partial sums (rows g, g + 8 x tokens 2t, 2t + 1).
+template <typename T, typename S, bool G32>
+DEVN float4 stage_rm(const uint8_t* st, const TileGeom tg, int cnt, const uint8_t* xd,
+                     uint32_t xpitch, int nT, const float2* gsum, int ncu, const float* colw,
+                     uint64_t* empty_bar) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int items = cnt * tg.npairs;
+  float acc[4];
+  zero4(acc);
+  rm_offset<T, S, G32>(st, tg, (warp * items) / kCW, ((warp + 1) * items) / kCW, lane, xd, xpitch,
+                       nT, gsum, ncu, colw, (lane >> 2) < nT, acc);
+  __syncwarp();
+  if (lane == 0) mbar_arrive(empty_bar);
+  return make_float4(acc[0], acc[1], acc[2], acc[3]);
+}
+
+DEVN float reduce4(float* red, const float4 a, int nT) {
+  const int tid = threadIdx.x;
+  const float acc[1][4] = {{a.x, a.y, a.z, a.w}};
+  return reduce_rows<1>(red, acc, nT, tid, tid >> 5, tid & 31).x;
+}
+
+// Router logits of expert e for nT tokens: the gate row (H values, natural order)
+// in `wrow`, the normalised tokens in `xplain`.  Thread n < nT returns logit n.
+template <typename T>
+DEVN float router_row(const uint8_t* wrow, const uint8_t* xplain, int H, int nT, const void* gate_b,
+                      int e, float* red, uint64_t* empty_bar) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint4* wr = reinterpret_cast<const uint4*>(wrow);
+  const int nq = H >> 3;
+  float part[kMaxTokens];
+#pragma unroll
+  for (int n = 0; n < kMaxTokens; ++n) part[n] = 0.f;
+  for (int q = tid; q < nq; q += kConsumers) {
+    const uint4 wv = wr[q];
+    const T* we = reinterpret_cast<const T*>(&wv);
+#pragma unroll
+    for (int n = 0; n < kMaxTokens; ++n) {
+      if (n < nT) {
+        const uint4 xv = *reinterpret_cast<const uint4*>(xplain + ((size_t)n * H + q * 8) * 2);
+        const T* xe = reinterpret_cast<const T*>(&xv);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) part[n] = fmaf(to_f32<T>(we[k]), to_f32<T>(xe[k]), part[n]);
+      }
+    }
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(empty_bar);
+#pragma unroll
+  for (int n = 0; n < kMaxTokens; ++n) {
+    if (n < nT) {
+      float a = part[n];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      if (lane == 0) red[warp * 8 + n] = a;
+    }
+  }
+  named_bar_sync(1, kConsumers);
+  float a = 0.f;
+  if (tid < nT) {
+#pragma unroll
+    for (int w = 0; w < kCW; ++w) a += red[w * 8 + tid];
+    if (gate_b) a += to_f32<T>(reinterpret_cast<const T*>(gate_b)[e]);
+    a = to_f32<T>(from_f32<T>(a));
+  }
+  named_bar_sync(1, kConsumers);
+  return a;
+}
+
+// Order key of a logit for the top-k.  Logits are rounded to the 16-bit
+// activation type, so (ordered 16-bit value << 15) | (0x7FFF - expert) is a unique
+// 31-bit key per expert and "k > v" is the sign of v - k: larger logit first, ties
+// to the lower expert id, NaN above everything (as torch.topk), -0 equal to +0.
+// Every CTA derives the same plan from the same logits, whatever their values.
+template <typename T>
+DEVI uint32_t order_key(float f, int e) {
+  const T h = from_f32<T>(f);
+  uint32_t b = (uint32_t)*reinterpret_cast<const uint16_t*>(&h);
+  const bool nan = DqOff<T>::kOddDiv16 ? ((b & 0x7C00u) == 0x7C00u && (b & 0x3FFu))
+                                       : ((b & 0x7F80u) == 0x7F80u && (b & 0x7Fu));
+  if (b == 0x8000u) b = 0u;
+  b = nan ? 0xFFFFu : ((b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u));
+  return (b << 15) | (0x7FFFu - (uint32_t)e);
+}
+
+// Top-k of every token and the unit plan (distinct selected experts in ascending
+// id order, their token masks), identical in every CTA.  The routing weights
+// follow in plan_weights, off the critical path.  Returns the unit count.
+// scratch: keys [T][E], then unit_of [E].
+template <typename T>
+DEVN int plan_units(const float* logits, int nT, int E, int top_k, uint8_t* smem, float* scratch) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float* ls = reinterpret_cast<float*>(smem + kSLogit);
+  int* sel_s = reinterpret_cast<int*>(smem + kSSel);
+  int* unit_e = reinterpret_cast<int*>(smem + kSUnitE);
+  uint32_t* unit_m = reinterpret_cast<uint32_t*>(smem + kSUnitM);
+  float* unit_w = reinterpret_cast<float*>(smem + kSUnitW);
+  int* n_units_s = reinterpret_cast<int*>(smem + kSNUnits);
+  uint32_t* selbits = reinterpret_cast<uint32_t*>(smem + kSSelBits);
+  uint32_t* keys = reinterpret_cast<uint32_t*>(scratch);
+  int* unit_of = reinterpret_cast<int*>(scratch) + kMaxTokens * kMaxExperts;
+  const int TE = nT * E;
+  for (int idx = tid; idx < TE; idx += kConsumers) {
+    const float v = __ldcg(logits + idx);
+    const int tk = idx / E;
+    ls[idx] = v;
+    keys[idx] = order_key<T>(v, idx - tk * E);
+  }
+  if (tid < kMaxTokens * 8) selbits[tid] = 0u;
+  named_bar_sync(1, kConsumers);
+  // rank of each logit within its token: four lanes per logit, each counting the
+  // larger keys in a quarter of the experts (vector loads, rotated per lane so
+  // the four quarters hit different banks)
+  const bool vec = (E & 15) == 0;
+  const int items = ((TE * 4 + 31) / 32) * 32;
+  for (int idx = tid; idx < items; idx += kConsumers) {
+    const int te = idx >> 2, qq = idx & 3;
+    uint32_t rank = 0;
+    int tk = 0;
+    if (te < TE) {
+      tk = te / E;
+      const uint32_t v = keys[te];
+      const uint32_t* row = keys + tk * E;
+      if (vec) {
+        const int nc = E >> 4;  // 4-key chunks per quarter
+        const uint4* q4 = reinterpret_cast<const uint4*>(row) + qq * nc;
+        const int rot = (2 * qq) % nc;
+        for (int j = 0; j < nc; ++j) {
+          const int jj = j + rot < nc ? j + rot : j + rot - nc;
+          const uint4 k4 = q4[jj];
+          rank += ((v - k4.x) >> 31) + ((v - k4.y) >> 31) + ((v - k4.z) >> 31) + ((v - k4.w) >> 31);
+        }
+      } else {
+        for (int e2 = qq; e2 < E; e2 += 4) rank += (v - row[e2]) >> 31;
+      }
+    }
+    rank += __shfl_xor_sync(0xffffffffu, rank, 1);
+    rank += __shfl_xor_sync(0xffffffffu, rank, 2);
+    if (te < TE && qq == 0 && rank < (uint32_t)top_k) {
+      const int e = te - tk * E;
+      sel_s[tk * 8 + rank] = e;
+      atomicOr(&selbits[tk * 8 + (e >> 5)], 1u << (e & 31));
+    }
+  }
+  named_bar_sync(1, kConsumers);
+  // unit plan: position of a selected expert = selected experts below it
+  const int nw = (E + 31) >> 5;
+  if (warp < nw) {
+    const int e = warp * 32 + lane;
+    uint32_t mask = 0, below = 0, all = 0;
+    for (int w = 0; w < nw; ++w) {
+      uint32_t any = 0;
+      for (int tk = 0; tk < nT; ++tk) any |= selbits[tk * 8 + w];
+      if (w < warp) below += __popc(any);
+      all += __popc(any);
+      if (w == warp) {
+        below += __popc(any & ((1u << lane) - 1u));
+        for (int tk = 0; tk < nT; ++tk) mask |= ((selbits[tk * 8 + w] >> lane) & 1u) << tk;
+      }
+    }
+    if (mask && below < (uint32_t)kMaxUnits) {
+      unit_e[below] = e;
+      unit_m[below] = mask;
+      unit_of[e] = (int)below;
+#pragma unroll
+      for (int n = 0; n < kMaxTokens; ++n) unit_w[below * kMaxTokens + n] = 0.f;
+    }
+    if (tid == 0) *n_units_s = all < (uint32_t)kMaxUnits ? (int)all : kMaxUnits;
+  }
+  named_bar_sync(1, kConsumers);
+  return *n_units_s;
+}
+
+// Routing weights of the plan: softmax over all experts, the top-k probabilities
+// renormalised (their sum taken in selection order), into unit_w.
+DEVN void plan_weights(int nT, int E, int top_k, int norm, uint8_t* smem, const float* scratch) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const float* ls = reinterpret_cast<const float*>(smem + kSLogit);
+  const int* sel_s = reinterpret_cast<const int*>(smem + kSSel);
+  float* unit_w = reinterpret_cast<float*>(smem + kSUnitW);
+  const int* unit_of = reinterpret_cast<const int*>(scratch) + kMaxTokens * kMaxExperts;
+  if (warp < nT) {
+    const int tk = warp;
+    const float* row = ls + tk * E;
+    const float m = row[sel_s[tk * 8]];
+    float den = 0.f;
+    for (int e = lane; e < E; e += 32) den += expf(row[e] - m);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    const int ej = lane < top_k ? sel_s[tk * 8 + lane] : 0;
+    const float pj = lane < top_k ? expf(row[ej] - m) / den : 0.f;
+    float psum = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j) {
+      const float x = __shfl_sync(0xffffffffu, pj, j);
+      if (j < top_k) psum += x;
+    }
+    if (lane < top_k) {
+      const int u = unit_of[ej];
+      if (u < kMaxUnits) unit_w[u * kMaxTokens + tk] = norm ? pj / psum : pj;
+    }
+  }
+  named_bar_sync(1, kConsumers);
+}
+
+DEVI void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+template <typename T, typename S, bool G32>
 __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constant__ StackParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSFull);
   uint64_t* empty = reinterpret_cast<uint64_t*>(smem + kSEmpty);
   uint64_t* plan_ready = reinterpret_cast<uint64_t*>(smem + kSPlan);
-  uint64_t* act_ready = reinterpret_cast<uint64_t*>(smem + kSActR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSAbort);
   int* n_units_s = reinterpret_cast<int*>(smem + kSNUnits);
   int* unit_e = reinterpret_cast<int*>(smem + kSUnitE);
@@ -141,7 +564,6 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
       mbar_init(&empty[s], kCW);
     }
     mbar_init(plan_ready, 1);
-    mbar_init(act_ready, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -154,13 +576,11 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
     const uint64_t pol = policy_evict_first();
     int i = 0;  // stage sequence number
     auto acquire = [&](int j) {
-      if (j >= NS) {
-        if (!mbar_wait_bounded(&empty[j % NS], (uint32_t)((j / NS) - 1) & 1u, abort_flag))
-          if (lane == 0) set_error(p.err, DUPLEX_DEVERR_TIMEOUT);
-      }
+      if (j >= NS)
+        wait_phase(&empty[j % NS], (uint32_t)((j / NS) - 1) & 1u, abort_flag, p.err, kSiteEmpty);
     };
     auto slot_ptr = [&](int j) { return smem + p.off_ring + (uint32_t)(j % NS) * p.slot_bytes; };
-    // one-copy stage (weights), the second arrival follows immediately
+    // one-copy stage (weights); the second arrival of the full barrier follows at once
     auto issue1 = [&](const uint8_t* src, uint32_t bytes) {
       acquire(i);
       if (lane == 0) {
@@ -201,8 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
       }
       __syncwarp();
       // routing plan of this layer (built by this CTA's consumers)
-      if (!mbar_wait_bounded(plan_ready, (uint32_t)(l & 1), abort_flag))
-        if (lane == 0) set_error(p.err, DUPLEX_DEVERR_TIMEOUT);
+      wait_phase(plan_ready, (uint32_t)(l & 1), abort_flag, p.err, kSitePlan);
       int nu = *n_units_s;
       nu = nu < 0 ? 0 : (nu > kMaxUnits ? kMaxUnits : nu);
       // never turn an out-of-range id into a copy address
@@ -216,44 +635,18 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
       for (int t = cta; t < nu * perG; t += G) {
         const int u = t / perG, rbi = t - u * perG;
         issue1(reinterpret_cast<const uint8_t*>(L.gu_tiles) +
-                   ((size_t)unit_e[u] * p.RbGU + 2 * rbi) * p.tgu.rec_bytes,
+                   ((size_t)unit_e[u] * (2 * perG) + 2 * rbi) * p.tgu.rec_bytes,
                2u * p.tgu.rec_bytes);
       }
-      // down: weights now, activation rows once gate|up has finished everywhere
-      bool act_seen = false;
-      int npend = 0;
-      struct Pend { int seq, u0, cnt; } pq[kSlotsMax];
-      auto flush = [&]() {
-        fence_proxy_async_global();
-        for (int q = 0; q < npend; ++q) {
-          const Pend& pp = pq[q];
-          uint8_t* dst = smem + p.off_ring + (uint32_t)(pp.seq % NS) * p.slot_bytes + p.off_xd;
-          if (lane == 0)
-            mbar_arrive_expect_tx(&full[pp.seq % NS], (uint32_t)(pp.cnt * p.T) * (uint32_t)p.I * 2u);
-          __syncwarp();
-          for (int r = lane; r < pp.cnt * p.T; r += 32) {
-            const int us = r / p.T, n = r - us * p.T;
-            const uint8_t* src = reinterpret_cast<const uint8_t*>(p.act) +
-                                 ((size_t)(pp.u0 + us) * kMaxTokens + n) * p.I * 2;
-            bulk_g2s(dst + (uint32_t)r * p.xd_pitch, src, (uint32_t)p.I * 2u, &full[pp.seq % NS]);
-          }
-          __syncwarp();
-        }
-        npend = 0;
-      };
+      // down: the records of up to `ups` units per stage, one copy per lane.  Down
+      // tiles are dealt from the last CTA backwards, so the CTAs with the fewest
+      // gate|up tiles take them first.
       const int nstg = (nu + p.ups - 1) / p.ups;
-      for (int t = cta; t < p.RbD; t += G) {
+      for (int t = G - 1 - cta; t < p.RbD; t += G) {
         for (int s = 0; s < nstg; ++s) {
-          if (!act_seen && npend > 0 && i >= NS &&
-              !mbar_test(&empty[i % NS], (uint32_t)((i / NS) - 1) & 1u)) {
-            if (!mbar_wait_bounded(act_ready, (uint32_t)(l & 1), abort_flag))
-              if (lane == 0) set_error(p.err, DUPLEX_DEVERR_TIMEOUT);
-            act_seen = true;
-            flush();
-          }
-          acquire(i);
           const int u0 = s * p.ups;
           const int cnt = (nu - u0) < p.ups ? (nu - u0) : p.ups;
+          acquire(i);
           if (lane == 0) mbar_arrive_expect_tx(&full[i % NS], (uint32_t)cnt * p.tdn.rec_bytes);
           __syncwarp();
           if (lane < cnt)
@@ -262,15 +655,10 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
                                 ((size_t)unit_e[u0 + lane] * p.RbD + t) * p.tdn.rec_bytes,
                             p.tdn.rec_bytes, &full[i % NS], pol);
           __syncwarp();
-          pq[npend++] = Pend{i, u0, cnt};
-          if (act_seen) flush();
+          if (lane == 0) mbar_arrive(&full[i % NS]);
+          __syncwarp();
           ++i;
         }
-      }
-      if (!act_seen) {
-        if (!mbar_wait_bounded(act_ready, (uint32_t)(l & 1), abort_flag))
-          if (lane == 0) set_error(p.err, DUPLEX_DEVERR_TIMEOUT);
-        flush();
       }
     }
     // drain: never leave the CTA while a bulk copy may still target its smem
@@ -285,7 +673,7 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
             break;
           }
         if (!ok) {
-          set_error(p.err, DUPLEX_DEVERR_TIMEOUT);
+          give_up(abort_flag, p.err, kSiteDrain);
           break;
         }
       }
@@ -294,265 +682,133 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
   }
 
   // ================================================================== consumers
-  const int g = lane >> 2, t = lane & 3;
   float* red = reinterpret_cast<float*>(smem + kSRed);
-  uint32_t* corr = reinterpret_cast<uint32_t*>(smem + kSCorr);
-  uint8_t* xsh = smem + p.off_xsh;
+  uint8_t* xsh = smem + p.off_x;
   uint8_t* xplain = smem + p.off_plain;
-  const bool xon = g < p.T;
+  float2* gsum = reinterpret_cast<float2*>(smem + p.off_gsum);
+  const int nT = p.T;
+  const int cw = G32 ? 1 : 2;
+  int* err = p.err;
+  int i = 0;       // stage sequence number
   unsigned nb = 0;  // grid barriers passed
-  int i = 0;        // stage sequence number
 
   auto wait_full = [&](int j) {
-    if (!mbar_wait_bounded(&full[j % NS], (uint32_t)(j / NS) & 1u, abort_flag))
-      if (lane == 0) set_error(p.err, DUPLEX_DEVERR_TIMEOUT);
-  };
-  auto release = [&](int j) {
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[j % NS]);
+    wait_phase(&full[j % NS], (uint32_t)(j / NS) & 1u, abort_flag, err, kSiteFull);
   };
   auto slot_ptr = [&](int j) { return smem + p.off_ring + (uint32_t)(j % NS) * p.slot_bytes; };
+  auto sync_grid = [&]() {
+    grid_arrive(p.barrier);
+    grid_wait(p.barrier, ++nb, abort_flag, err);
+  };
 
-  const uint8_t* h_prev = reinterpret_cast<const uint8_t*>(p.x_in);
   for (int l = 0; l < p.n_layers; ++l) {
     const duplex_stack_layer L = p.layers[l];
-    uint8_t* h_out = reinterpret_cast<uint8_t*>(l == p.n_layers - 1 ? p.out
-                                                : (l & 1) ? p.hbuf1 : p.hbuf0);
-    const uint8_t* hm = h_prev;  // MoE input
+    const bool last = l == p.n_layers - 1;
+    const T* hin = reinterpret_cast<const T*>(l == 0 ? p.x_in : p.hbuf[l & 1]);
+    T* hout = reinterpret_cast<T*>(last ? p.out : p.hbuf[(l + 1) & 1]);
+    const T* hm = hin;  // MoE input
     if (p.has_attn) {
       // ---------------------------------------------------------------- Q
-      stage_x_shared<T, true>(xsh, p.x_pitch, h_prev, p.H, p.T, p.tq, p.rms_eps, red, tid, warp,
-                              lane);
-      build_corr<T>(corr, xsh, p.x_pitch, p.tq.npairs, p.T, tid);
-      named_bar_sync(1, kConsumers);
+      stage_rows<T>(reinterpret_cast<const uint8_t*>(hin), p.H, nT, p.H, nT, xsh, p.x_pitch,
+                    p.rms_eps > 0.f, p.rms_eps, nullptr, gsum, cw, red, kStageAll);
       for (int tile = cta; tile < p.RbQ; tile += G, ++i) {
         wait_full(i);
-        const int np = p.tq.npairs;
-        const int lo = (warp * np) / kCW, hi = ((warp + 1) * np) / kCW;
-        float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
-        consume_corr<T, S, false>(slot_ptr(i), p.tq, lo, hi, lane, xsh, p.x_pitch, corr, xon, a0, a1);
-        release(i);
-        float v, v2;
-        reduce_tile(red, a0, a1, false, tid, warp, lane, v, v2);
-        if (tid < 128) {
-          const int n = tid >> 4, r = tid & 15, row = tile * 16 + r;
-          if (n < p.T && row < p.qkv_R)
-            reinterpret_cast<T*>(p.qkv)[(size_t)n * p.qkv_R + row] = from_f32<T>(v);
+        const float2 v = tile_pm<T, S, 1, G32>(slot_ptr(i), p.tq, xsh, p.x_pitch, gsum, nT, red,
+                                               &empty[i % NS]);
+        if (tid < nT * 16) {
+          const int n = tid >> 4, row = tile * 16 + (tid & 15);
+          reinterpret_cast<T*>(p.qkv)[(size_t)n * p.qkv_R + row] = from_f32<T>(v.x);
         }
         named_bar_sync(1, kConsumers);
       }
-      grid_sync(p, nb, tid, abort_flag);
+      sync_grid();
       // ---------------------------------------------------------------- O
-      stage_x_shared<T, true>(xsh, p.x_pitch, reinterpret_cast<const uint8_t*>(p.qkv), p.qkv_R, p.T,
-                              p.to, 0.f, red, tid, warp, lane);
-      build_corr<T>(corr, xsh, p.x_pitch, p.to.npairs, p.T, tid);
-      named_bar_sync(1, kConsumers);
+      if (cta < p.RbO)
+        stage_rows<T>(reinterpret_cast<const uint8_t*>(p.qkv), p.qkv_R, nT, p.q_dim, nT, xsh,
+                      p.x_pitch, false, 0.f, nullptr, gsum, cw, red, kStageAll);
       for (int tile = cta; tile < p.RbO; tile += G, ++i) {
         wait_full(i);
-        const int np = p.to.npairs;
-        const int lo = (warp * np) / kCW, hi = ((warp + 1) * np) / kCW;
-        float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
-        consume_corr<T, S, false>(slot_ptr(i), p.to, lo, hi, lane, xsh, p.x_pitch, corr, xon, a0, a1);
-        release(i);
-        float v, v2;
-        reduce_tile(red, a0, a1, false, tid, warp, lane, v, v2);
-        if (tid < 128) {
-          const int n = tid >> 4, r = tid & 15, row = tile * 16 + r;
-          if (n < p.T && row < p.H) {
-            const T res = __ldcg(reinterpret_cast<const T*>(h_prev) + (size_t)n * p.H + row);
-            reinterpret_cast<T*>(p.h1)[(size_t)n * p.H + row] =
-                from_f32<T>(to_f32<T>(from_f32<T>(v)) + to_f32<T>(res));
-          }
+        const float2 v = tile_pm<T, S, 1, G32>(slot_ptr(i), p.to, xsh, p.x_pitch, gsum, nT, red,
+                                               &empty[i % NS]);
+        if (tid < nT * 16) {
+          const int n = tid >> 4, row = tile * 16 + (tid & 15);
+          const float res = to_f32<T>(__ldcg(hin + (size_t)n * p.H + row));
+          reinterpret_cast<T*>(p.h1)[(size_t)n * p.H + row] =
+              from_f32<T>(to_f32<T>(from_f32<T>(v.x)) + res);
         }
         named_bar_sync(1, kConsumers);
       }
-      grid_sync(p, nb, tid, abort_flag);
-      hm = reinterpret_cast<const uint8_t*>(p.h1);
+      sync_grid();
+      hm = reinterpret_cast<const T*>(p.h1);
     }
     // ------------------------------------------------------------------ R
-    stage_x_shared<T, true>(xsh, p.x_pitch, hm, p.H, p.T, p.tgu, p.rms_eps, red, tid, warp, lane,
-                            xplain);
-    build_corr<T>(corr, xsh, p.x_pitch, p.tgu.npairs, p.T, tid);
-    named_bar_sync(1, kConsumers);
+    // normalised rows for the router first; their fragment-order staging for the
+    // gate|up tiles runs while the logits barrier is in flight
+    stage_rows<T>(reinterpret_cast<const uint8_t*>(hm), p.H, nT, p.H, nT, xsh, p.x_pitch,
+                  p.rms_eps > 0.f, p.rms_eps, xplain, gsum, cw, red, kStageNorm);
     for (int e = cta; e < p.E; e += G, ++i) {
       wait_full(i);
-      const uint4* wr = reinterpret_cast<const uint4*>(slot_ptr(i));
-      const int nq = p.H >> 3;
-      float part[kMaxTokens];
-#pragma unroll
-      for (int n = 0; n < kMaxTokens; ++n) part[n] = 0.f;
-      for (int q = tid; q < nq; q += kConsumers) {
-        const uint4 wv = wr[q];
-        const T* we = reinterpret_cast<const T*>(&wv);
-#pragma unroll
-        for (int n = 0; n < kMaxTokens; ++n) {
-          if (n < p.T) {
-            const uint4 xv = *reinterpret_cast<const uint4*>(xplain + ((size_t)n * p.H + q * 8) * 2);
-            const T* xe = reinterpret_cast<const T*>(&xv);
-#pragma unroll
-            for (int k = 0; k < 8; ++k) part[n] = fmaf(to_f32<T>(we[k]), to_f32<T>(xe[k]), part[n]);
-          }
-        }
-      }
-      release(i);
-#pragma unroll
-      for (int n = 0; n < kMaxTokens; ++n) {
-        float a = part[n];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-        if (lane == 0) red[warp * 8 + n] = a;
-      }
-      named_bar_sync(1, kConsumers);
-      if (tid < p.T) {
-        float a = 0.f;
-#pragma unroll
-        for (int w = 0; w < kCW; ++w) a += red[w * 8 + tid];
-        if (L.gate_b) a += to_f32<T>(reinterpret_cast<const T*>(L.gate_b)[e]);
-        p.logits[(size_t)tid * p.E + e] = to_f32<T>(from_f32<T>(a));
-      }
-      named_bar_sync(1, kConsumers);
+      const float a = router_row<T>(slot_ptr(i), xplain, p.H, nT, L.gate_b, e, red, &empty[i % NS]);
+      if (tid < nT) p.logits[(size_t)tid * p.E + e] = a;
     }
-    grid_sync(p, nb, tid, abort_flag);
+    grid_arrive(p.barrier);
+    stage_rows<T>(nullptr, 0, nT, p.H, nT, xsh, p.x_pitch, false, 0.f, nullptr, gsum, cw, red,
+                  kStageFrag);
+    grid_wait(p.barrier, ++nb, abort_flag, err);
     // ------------------------------------------------------------------ D
-    {
-      float* ls = reinterpret_cast<float*>(smem + kSLogit);
-      int* sel_s = reinterpret_cast<int*>(smem + kSSel);
-      float* w_s = reinterpret_cast<float*>(smem + kSW);
-      int* cnt = reinterpret_cast<int*>(smem + kSCnt);
-      const int TE = p.T * p.E;
-      for (int idx = tid; idx < TE; idx += kConsumers) ls[idx] = __ldcg(p.logits + idx);
-      if (tid < kMaxTokens * 8) sel_s[tid] = 0;
-      named_bar_sync(1, kConsumers);
-      // rank of each logit within its token (ties -> lower expert id first)
-      for (int idx = tid; idx < TE; idx += kConsumers) {
-        const int tk = idx / p.E, e = idx - tk * p.E;
-        const float v = ls[idx];
-        const float* row = ls + tk * p.E;
-        int rank = 0;
-        for (int e2 = 0; e2 < p.E; ++e2) {
-          const float v2 = row[e2];
-          rank += (v2 > v) || (v2 == v && e2 < e);
-        }
-        if (rank < p.top_k) sel_s[tk * 8 + rank] = e;
-      }
-      named_bar_sync(1, kConsumers);
-      if (warp < p.T) {
-        const int tk = warp;
-        const float* row = ls + tk * p.E;
-        const float m = row[sel_s[tk * 8]];
-        float den = 0.f;
-        for (int e = lane; e < p.E; e += 32) den += expf(row[e] - m);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-        if (lane == 0) {
-          float pj[kMaxTopK], psum = 0.f;
-          for (int j = 0; j < p.top_k; ++j) {
-            pj[j] = expf(row[sel_s[tk * 8 + j]] - m) / den;
-            psum += pj[j];
-          }
-          for (int j = 0; j < p.top_k; ++j) w_s[tk * 8 + j] = p.norm ? pj[j] / psum : pj[j];
-        }
-      }
-      named_bar_sync(1, kConsumers);
-      // unit plan: distinct selected experts in ascending id order
-      const int nw = (p.E + 31) >> 5;
-      uint32_t mask = 0;
-      float wv[kMaxTokens];
-#pragma unroll
-      for (int n = 0; n < kMaxTokens; ++n) wv[n] = 0.f;
-      unsigned bal = 0;
-      const int e = warp * 32 + lane;
-      if (warp < nw) {
-        if (e < p.E)
-          for (int tk = 0; tk < p.T; ++tk)
-            for (int j = 0; j < p.top_k; ++j)
-              if (sel_s[tk * 8 + j] == e) {
-                mask |= 1u << tk;
-                wv[tk] = w_s[tk * 8 + j];
-              }
-        bal = __ballot_sync(0xffffffffu, mask != 0u);
-        if (lane == 0) cnt[warp] = __popc(bal);
-      }
-      named_bar_sync(1, kConsumers);
-      if (warp < nw && mask) {
-        int base = 0;
-        for (int w = 0; w < warp; ++w) base += cnt[w];
-        const int pos = base + __popc(bal & ((1u << lane) - 1u));
-        if (pos < kMaxUnits) {
-          unit_e[pos] = e;
-          unit_m[pos] = mask;
-#pragma unroll
-          for (int n = 0; n < kMaxTokens; ++n) unit_w[pos * kMaxTokens + n] = wv[n];
-        }
-      }
-      if (tid == 0) {
-        int tot = 0;
-        for (int w = 0; w < nw; ++w) tot += cnt[w];
-        *n_units_s = tot < kMaxUnits ? tot : kMaxUnits;
-      }
-      named_bar_sync(1, kConsumers);
-      if (tid == 0) mbar_arrive(plan_ready);
-    }
-    const int nu = *n_units_s;
+    const int nu = plan_units<T>(p.logits, nT, p.E, p.top_k, smem, red);
+    if (tid == 0) mbar_arrive(plan_ready);
+    plan_weights(nT, p.E, p.top_k, p.norm, smem, red);
     // ------------------------------------------------------------------ G
     for (int tile = cta; tile < nu * perG; tile += G, ++i) {
       wait_full(i);
-      const int np = p.tgu.npairs;
-      const int lo = (warp * 2 * np) / kCW, hi = ((warp + 1) * 2 * np) / kCW;
-      float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
-      consume_corr<T, S, false>(slot_ptr(i), p.tgu, lo, hi, lane, xsh, p.x_pitch, corr, xon, a0, a1);
-      release(i);
-      float v, v2;
-      reduce_tile(red, a0, a1, true, tid, warp, lane, v, v2);
-      if (tid < 128) {
+      const float2 v = tile_pm<T, S, 2, G32>(slot_ptr(i), p.tgu, xsh, p.x_pitch, gsum, nT, red,
+                                             &empty[i % NS]);
+      if (tid < nT * 16) {
         const int n = tid >> 4, r = tid & 15;
         const int u = tile / perG, row = (tile - u * perG) * 16 + r;
-        if (n < p.T) {
-          const float a = ((unit_m[u] >> n) & 1u) ? silu_f32(v) * v2 : 0.f;
-          reinterpret_cast<T*>(p.act)[((size_t)u * kMaxTokens + n) * p.I + frag_pos(row)] =
-              from_f32<T>(a);
-        }
+        const float a = ((unit_m[u] >> n) & 1u) ? silu_f32(v.x) * v.y : 0.f;
+        reinterpret_cast<T*>(p.act)[((size_t)u * nT + n) * p.I + row] = from_f32<T>(a);
       }
       named_bar_sync(1, kConsumers);
     }
-    grid_sync(p, nb, tid, abort_flag);
-    if (tid == 0) mbar_arrive(act_ready);
+    sync_grid();
     // ------------------------------------------------------------------ N
     const int nstg = (nu + p.ups - 1) / p.ups;
-    for (int tile = cta; tile < p.RbD; tile += G) {
-      float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
+    const int ncu = p.tdn.npairs * (G32 ? 2 : 1);  // correction units per record
+    int a0 = -1, acnt = 0;                         // staged activation units [a0, a0 + acnt)
+    for (int tile = G - 1 - cta; tile < p.RbD; tile += G) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int s = 0; s < nstg; ++s, ++i) {
-        wait_full(i);
         const int u0 = s * p.ups;
         const int cnt = (nu - u0) < p.ups ? (nu - u0) : p.ups;
-        const int np = p.tdn.npairs;
-        const int items = cnt * np;
-        const int lo = (warp * items) / kCW, hi = ((warp + 1) * items) / kCW;
-        const uint8_t* st = slot_ptr(i);
-        for (int it = lo; it < hi; ++it) {
-          const int us = it / np, pp = it - us * np;
-          const int u = u0 + us;
-          const uint8_t* xrow = st + p.off_xd + (uint32_t)(us * p.T + g) * p.xd_pitch + (uint32_t)t * 16u;
-          item_exact<T, S, false>(st + (uint32_t)us * p.tdn.rec_bytes, p.tdn, pp, lane, xrow, xon,
-                                  false, unit_w[u * kMaxTokens + 2 * t],
-                                  unit_w[u * kMaxTokens + 2 * t + 1], a0);
+        if (a0 < 0 || u0 < a0 || u0 + cnt > a0 + acnt) {
+          a0 = u0;
+          acnt = (nu - u0) < p.act_units ? (nu - u0) : p.act_units;
+          stage_rows<T>(reinterpret_cast<const uint8_t*>(p.act) + (size_t)a0 * nT * p.I * 2, p.I,
+                        acnt * nT, p.I, nT, xsh, p.xd_pitch, false, 0.f, nullptr, gsum, cw, red,
+                        kStageAll);
         }
-        release(i);
+        wait_full(i);
+        const float4 d = stage_rm<T, S, G32>(slot_ptr(i), p.tdn, cnt,
+                                             xsh + (uint32_t)((u0 - a0) * nT) * p.xd_pitch,
+                                             p.xd_pitch, nT, gsum + (size_t)(u0 - a0) * ncu * 8, ncu,
+                                             unit_w + u0 * kMaxTokens, &empty[i % NS]);
+        acc.x += d.x;
+        acc.y += d.y;
+        acc.z += d.z;
+        acc.w += d.w;
       }
-      float v, v2;
-      reduce_tile(red, a0, a1, false, tid, warp, lane, v, v2);
-      if (tid < 128) {
-        const int n = tid >> 4, r = tid & 15, row = tile * 16 + r;
-        if (n < p.T && row < p.H) {
-          float y = v;
-          if (p.moe_residual) y += to_f32<T>(__ldcg(reinterpret_cast<const T*>(hm) + (size_t)n * p.H + row));
-          reinterpret_cast<T*>(h_out)[(size_t)n * p.H + row] = from_f32<T>(y);
-        }
+      const float v = reduce4(red, acc, nT);
+      if (tid < nT * 16) {
+        const int n = tid >> 4, row = tile * 16 + (tid & 15);
+        float y = v;
+        if (p.moe_residual) y += to_f32<T>(__ldcg(hm + (size_t)n * p.H + row));
+        hout[(size_t)n * p.H + row] = from_f32<T>(y);
       }
       named_bar_sync(1, kConsumers);
     }
-    grid_sync(p, nb, tid, abort_flag);
-    h_prev = h_out;
+    if (!last) sync_grid();
   }
 }
 
@@ -560,21 +816,31 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
 static inline uint32_t up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
 struct StackScratch {
-  size_t barrier, h0, h1buf, hm, qkv, act, logits, total;
+  size_t barrier, hbuf[2], qkv, h1, logits, act, total;
 };
+
+static int units_cap(int T, int E, int top_k) {
+  int units = T * top_k < E ? T * top_k : E;
+  return units > kMaxUnits ? kMaxUnits : units;
+}
 
 static StackScratch stack_scratch(int T, int H, int E, int I, int top_k, int qkv_R) {
   StackScratch s;
   size_t off = 0;
-  s.barrier = off; off += 256;
-  s.h0 = off; off += align_up((size_t)T * H * 2, 256);
-  s.h1buf = off; off += align_up((size_t)T * H * 2, 256);
-  s.hm = off; off += align_up((size_t)T * H * 2, 256);
-  s.qkv = off; off += align_up((size_t)T * (qkv_R > 0 ? qkv_R : 1) * 2, 256);
-  int units = T * top_k < E ? T * top_k : E;
-  if (units > kMaxUnits) units = kMaxUnits;
-  s.act = off; off += align_up((size_t)units * kMaxTokens * I * 2, 256);
-  s.logits = off; off += align_up((size_t)T * E * 4, 256);
+  s.barrier = off;
+  off += 256;
+  for (int k = 0; k < 2; ++k) {
+    s.hbuf[k] = off;
+    off += align_up((size_t)T * H * 2, 256);
+  }
+  s.qkv = off;
+  off += align_up((size_t)T * (qkv_R > 0 ? qkv_R : 1) * 2, 256);
+  s.h1 = off;
+  off += align_up((size_t)T * H * 2, 256);
+  s.logits = off;
+  off += align_up((size_t)T * E * 4, 256);
+  s.act = off;
+  off += align_up((size_t)units_cap(T, E, top_k) * T * I * 2, 256);
   s.total = off;
   return s;
 }
@@ -597,13 +863,14 @@ extern "C" int duplex_stack_forward(const duplex_stack_layer* layers, int32_t n_
                                     int32_t norm_topk, int32_t qkv_R, int32_t q_dim,
                                     int32_t group, float rms_eps, void* workspace,
                                     size_t workspace_bytes, int32_t* err, void* stream) {
-  if (!layers || n_layers < 1 || !x_in || !out || !workspace) return DUPLEX_ERR_ARG;
+  if (!layers || n_layers < 1 || n_layers > 255 || !x_in || !out || !workspace || !err)
+    return DUPLEX_ERR_ARG;
   if (T < 1 || T > kMaxTokens || E < 1 || E > kMaxExperts || top_k < 1 || top_k > kMaxTopK ||
       top_k > E)
     return DUPLEX_ERR_ARG;
   if (act_dtype != DUPLEX_DTYPE_F16 && act_dtype != DUPLEX_DTYPE_BF16) return DUPLEX_ERR_DTYPE;
   if (scale_dtype != act_dtype) return DUPLEX_ERR_DTYPE;
-  if ((H & 63) || (I & 63) || (group & 63)) return DUPLEX_ERR_UNSUPPORTED;
+  if ((H & 63) || (I & 63) || group < 32 || (group & (group - 1))) return DUPLEX_ERR_UNSUPPORTED;
   StackParams p = {};
   if (tile_geom(H, group, has_zeros, &p.tgu) || tile_geom(I, group, has_zeros, &p.tdn))
     return DUPLEX_ERR_UNSUPPORTED;
@@ -614,66 +881,78 @@ extern "C" int duplex_stack_forward(const duplex_stack_layer* layers, int32_t n_
     if (tile_geom(H, group, has_zeros, &p.tq) || tile_geom(q_dim, group, has_zeros, &p.to))
       return DUPLEX_ERR_UNSUPPORTED;
   }
+  const int G = num_sms();
   const StackScratch L = stack_scratch(T, H, E, I, top_k, p.has_attn ? qkv_R : 0);
   if (workspace_bytes < L.total) return DUPLEX_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) | reinterpret_cast<uintptr_t>(x_in) |
        reinterpret_cast<uintptr_t>(out)) & 15u)
     return DUPLEX_ERR_ALIGN;
+  // staged rows must fit the per-thread chunk registers
+  const int maxK = p.has_attn && q_dim > H ? q_dim : H;
+  if (T * maxK > kMaxChunks * 8 * kConsumers) return DUPLEX_ERR_UNSUPPORTED;
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
   p.layers = layers;
   p.n_layers = n_layers;
   p.T = T; p.H = H; p.E = E; p.I = I; p.top_k = top_k; p.norm = norm_topk;
   p.q_dim = q_dim; p.qkv_R = qkv_R; p.moe_residual = moe_residual ? 1 : 0;
-  p.RbQ = (qkv_R + 15) / 16; p.RbO = (H + 15) / 16; p.RbGU = 2 * I / 16; p.RbD = (H + 15) / 16;
+  p.RbQ = (qkv_R + 15) / 16; p.RbO = (H + 15) / 16; p.RbD = (H + 15) / 16;
   p.rms_eps = rms_eps;
   p.x_in = x_in; p.out = out;
-  p.hbuf0 = ws + L.h0; p.hbuf1 = ws + L.h1buf; p.h1 = ws + L.hm; p.qkv = ws + L.qkv;
-  p.act = ws + L.act; p.logits = reinterpret_cast<float*>(ws + L.logits);
+  for (int k = 0; k < 2; ++k) p.hbuf[k] = ws + L.hbuf[k];
+  p.qkv = ws + L.qkv;
+  p.h1 = ws + L.h1;
+  p.logits = reinterpret_cast<float*>(ws + L.logits);
+  p.act = ws + L.act;
   p.barrier = reinterpret_cast<unsigned*>(ws + L.barrier);
   p.err = err;
-  // shared memory: fixed map | correction table | staged x | plain x | ring
-  int maxK = H, maxPairs = p.tgu.npairs;
-  if (p.has_attn) {
-    if (p.to.K > maxK) maxK = p.to.K;
-    if (p.to.npairs > maxPairs) maxPairs = p.to.npairs;
-  }
-  p.x_pitch = up((uint32_t)((maxK + 63) / 64 * 64) * 2u, 128) + 64u;
-  const uint32_t off_corr_end = kSCorr + (uint32_t)maxPairs * 128u;
-  p.off_xsh = up(off_corr_end, 128);
-  p.off_plain = up(p.off_xsh + (uint32_t)T * p.x_pitch, 128);
-  p.off_ring = up(p.off_plain + (uint32_t)T * H * 2u, 128);
-  // slot: the largest stage -- a q|k|v record, an o record, a gate row, a gate|up
-  // record pair, or `ups` down records with their activation rows
+  // ring slot: the largest stage -- a q|k|v record, an o record, a gate row, or a
+  // gate|up record pair; down stages take as many unit records as fit
   uint32_t slot = 2u * p.tgu.rec_bytes;
   if (p.has_attn) {
     slot = slot > p.tq.rec_bytes ? slot : p.tq.rec_bytes;
     slot = slot > p.to.rec_bytes ? slot : p.to.rec_bytes;
   }
   slot = slot > (uint32_t)H * 2u ? slot : (uint32_t)H * 2u;
-  p.xd_pitch = up((uint32_t)I * 2u, 128) + 64u;
-  const uint32_t per_unit = p.tdn.rec_bytes + (uint32_t)T * p.xd_pitch;
-  int ups = (int)(slot / per_unit);
-  if (ups < 1) {
-    ups = 1;
-    slot = per_unit;
-  }
+  if (slot < p.tdn.rec_bytes) slot = p.tdn.rec_bytes;
+  slot = up(slot, 128);
+  int ups = (int)(slot / p.tdn.rec_bytes);
   if (ups > 32) ups = 32;
+  // activation units staged at once for the down projection (a multiple of ups)
+  const int by_regs = (kMaxChunks * 8 * kConsumers) / (T * I);
+  if (by_regs < 1) return DUPLEX_ERR_UNSUPPORTED;
+  if (ups > by_regs) ups = by_regs;
+  const int ucap = units_cap(T, E, top_k);
+  int act_units = ucap < by_regs ? ucap : by_regs;
+  act_units = act_units < ups ? ups : act_units / ups * ups;
   p.ups = ups;
-  p.off_xd = up((uint32_t)ups * p.tdn.rec_bytes, 128);
-  slot = up(slot > p.off_xd + (uint32_t)ups * T * p.xd_pitch ? slot
-                                                           : p.off_xd + (uint32_t)ups * T * p.xd_pitch,
-            128);
+  p.act_units = act_units;
   p.slot_bytes = slot;
+  p.x_pitch = up((uint32_t)((maxK + 63) / 64 * 64) * 2u, 128) + 64u;
+  p.xd_pitch = up((uint32_t)I * 2u, 128) + 64u;
+  const uint32_t x_bytes_q = (uint32_t)T * p.x_pitch;
+  const uint32_t x_bytes_d = (uint32_t)(act_units * T) * p.xd_pitch;
+  const uint32_t x_bytes = x_bytes_q > x_bytes_d ? x_bytes_q : x_bytes_d;
+  const int gs_q = (maxK / 32) * 8, gs_d = act_units * (I / 32) * 8;
+  const uint32_t gsum_bytes = (uint32_t)((gs_q > gs_d ? gs_q : gs_d) * 8);
+  p.off_gsum = up(kSFixedEnd, 128);
+  p.off_x = up(p.off_gsum + gsum_bytes, 128);
+  p.off_plain = up(p.off_x + x_bytes, 128);
+  p.off_ring = up(p.off_plain + (uint32_t)T * H * 2u, 128);
   const size_t kMax = 227 * 1024;
-  int ns = (int)((kMax - p.off_ring) / slot);
+  int ns = p.off_ring < kMax ? (int)((kMax - p.off_ring) / slot) : 0;
   if (ns > kSlotsMax) ns = kSlotsMax;
   if (ns < 2) return DUPLEX_ERR_UNSUPPORTED;
   p.nslots = ns;
   const size_t smem = p.off_ring + (size_t)ns * slot;
 
   cudaStream_t st = (cudaStream_t)stream;
-  void (*kern)(StackParams) = act_dtype == DUPLEX_DTYPE_F16 ? stack_kernel<__half, __half>
-                                                            : stack_kernel<__nv_bfloat16, __nv_bfloat16>;
+  const bool g32 = group == 32;
+  void (*kern)(StackParams);
+  if (act_dtype == DUPLEX_DTYPE_F16)
+    kern = g32 ? stack_kernel<__half, __half, true> : stack_kernel<__half, __half, false>;
+  else
+    kern = g32 ? stack_kernel<__nv_bfloat16, __nv_bfloat16, true>
+               : stack_kernel<__nv_bfloat16, __nv_bfloat16, false>;
   int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), (int)kMax);
   if (rc) return rc;
   int occ = 0;
@@ -682,10 +961,15 @@ extern "C" int duplex_stack_forward(const duplex_stack_layer* layers, int32_t n_
   if (occ < 1) return DUPLEX_ERR_UNSUPPORTED;
   rc = record_cuda(cudaMemsetAsync(ws + L.barrier, 0, 256, st));
   if (rc) return rc;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(num_sms());
+  cfg.gridDim = dim3(G);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   return record_cuda(cudaLaunchKernelEx(&cfg, kern, p));
 }

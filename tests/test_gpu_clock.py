@@ -79,29 +79,40 @@ def test_persistent_matches_kernel_chain_thinker_geometry(cuda):
 
 
 @pytest.mark.parametrize("T", [1, 4])
-def test_moe_chain_vs_modules(cuda, T):
-    """x -> MoE(rms(x)) over several layers in one launch == the per-layer module calls."""
+def test_moe_chain_vs_oracle(cuda, T):
+    """x -> MoE(rms(x)) over three layers in one launch against the numpy oracle
+    chained layer by layer (each layer's output rounded to fp16, as on the GPU), and
+    one layer of it against the per-layer module call."""
     from duplex.clock import MoEChain
     from duplex.streaming.fused_packed_moe import FusedPackedMoE
-    moes = []
+    from oracle.clock_oracle import moe_layer, rms_norm
+    from oracle.moe_oracle import round_to
+    moes, arrays = [], []
     for l in range(3):
         L = synth.moe_layer_np(seed=40 + l, E=32, H=512, I=128, top_k=4, group=128, T=1)
+        arrays.append(L)
         t = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
         moes.append(FusedPackedMoE.from_stacked(t(L["gate_w"]), t(L["gu_packed"]), t(L["gu_scale"]),
                                                 t(L["dn_packed"]), t(L["dn_scale"]), 4,
                                                 gu_zeros=t(L["gu_zeros"]), dn_zeros=t(L["dn_zeros"]),
                                                 dtype=torch.float16, device=cuda))
-    chain = MoEChain(moes, rms_eps=1e-6, residual=False, T=T)
     x = torch.randn(T, 512, device=cuda, dtype=torch.float16,
                     generator=torch.Generator(device=cuda).manual_seed(7))
+    chain = MoEChain(moes, rms_eps=1e-6, residual=False, T=T)
     got = torch.zeros_like(x)
     chain.forward_into(x, got)
-    h = x
-    for m in moes:
-        o = torch.zeros_like(x)
-        m.forward_into(h, o, rms_eps=1e-6)
-        h = o
+    one = MoEChain(moes[:1], rms_eps=1e-6, residual=False, T=T)
+    got1 = torch.zeros_like(x)
+    one.forward_into(x, got1)
+    mod1 = torch.zeros_like(x)
+    moes[0].forward_into(x, mod1, rms_eps=1e-6)
     torch.cuda.synchronize()
-    g, r = got.float().cpu().numpy(), h.float().cpu().numpy()
-    assert np.abs(g - r).max() <= 2e-3 * np.abs(r).max()
-    assert chain.p.device_errors() == 0
+    h = x.float().cpu().numpy()
+    for L in arrays:
+        y, _ = moe_layer(rms_norm(h, 1e-6), L, 4)
+        h = np.asarray(round_to(y, "float16"), np.float32)
+    g = got.float().cpu().numpy()
+    assert np.abs(g - h).max() <= 2e-3 * np.abs(h).max()
+    g1, m1 = got1.float().cpu().numpy(), mod1.float().cpu().numpy()
+    assert np.abs(g1 - m1).max() <= 2e-3 * np.abs(m1).max()
+    assert chain.p.device_errors() == 0 and one.p.device_errors() == 0
