@@ -454,6 +454,54 @@ DEVI void pm_fixed(const uint8_t* st, const TileGeom& tg, int warp, int lane, co
   }
 }
 
+// rm_offset for records whose pairs form whole groups of PPG pairs (npairs % PPG
+// == 0): the items are (record, group), dealt round-robin to the 16 warps, each
+// group's pairs fully unrolled with one accumulator chain.
+template <typename T, typename S, int PPG>
+DEVI void rm_grouped(const uint8_t* st, const TileGeom& tg, int nrec, int warp, int lane,
+                     const uint8_t* xd, uint32_t xpitch, int rows_per_unit, const float2* gsum,
+                     int gr_stride, const float* colw, bool xon, float (&acc)[4]) {
+  const int g = lane >> 2, t = lane & 3;
+  const int gpr = tg.npairs / PPG;  // groups per record
+  for (int it = warp; it < nrec * gpr; it += kCW) {
+    const int us = it / gpr, grp = it - us * gpr;
+    const uint8_t* rec = st + (uint32_t)us * tg.rec_bytes;
+    const int p0 = grp * PPG;
+    const uint8_t* xrow =
+        xd + (uint32_t)(us * rows_per_unit + g) * xpitch + (uint32_t)t * 16u + (uint32_t)p0 * 128u;
+    const uint8_t* wp = rec + (((uint32_t)p0 << 5) + lane) * 16u;
+    const float2* gp = gsum + (size_t)us * gr_stride * 8 + p0 * 8 + 2 * t;
+    float d[4];
+    float4 gs = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < PPG; ++k) {
+      const float4 gq = *reinterpret_cast<const float4*>(gp + k * 8);
+      gs.x += gq.x;
+      gs.y += gq.y;
+      gs.z += gq.z;
+      gs.w += gq.w;
+      uint4 xa = make_uint4(0, 0, 0, 0), xb = make_uint4(0, 0, 0, 0);
+      if (xon) {
+        xa = *reinterpret_cast<const uint4*>(xrow + k * 128);
+        xb = *reinterpret_cast<const uint4*>(xrow + k * 128 + 64);
+      }
+      const uint4 w = *reinterpret_cast<const uint4*>(wp + k * 512);
+      uint32_t A[4], B[4];
+      DqOff<T>::expand(w.x, w.y, A, B);
+      if (k == 0)
+        mma_first<T>(d, A[0], A[1], A[2], A[3], xa.x, xa.y);
+      else
+        MmaOp<T>::run(d, A[0], A[1], A[2], A[3], xa.x, xa.y);
+      MmaOp<T>::run(d, B[0], B[1], B[2], B[3], xa.z, xa.w);
+      DqOff<T>::expand(w.z, w.w, A, B);
+      MmaOp<T>::run(d, A[0], A[1], A[2], A[3], xb.x, xb.y);
+      MmaOp<T>::run(d, B[0], B[1], B[2], B[3], xb.z, xb.w);
+    }
+    const float zero4v[4] = {0.f, 0.f, 0.f, 0.f};
+    flush_group<S>(acc, d, zero4v, rec, tg, grp, g, gs, colw[us * 8 + 2 * t], colw[us * 8 + 2 * t + 1]);
+  }
+}
+
 // Record-major walk over items [lo, hi) of a stage whose records each have their
 // own activation rows (the MoE down projection: record us = unit us, rows
 // us * rows_per_unit + token): item = (record, column pair), record-major.  gsum is

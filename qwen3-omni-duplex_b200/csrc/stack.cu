@@ -308,12 +308,16 @@ DEVI float2 reduce_rows(float* red, const float (&acc)[NREC][4], int nT, int tid
   return make_float2(v, v2);
 }
 
+// Accumulators of one lane for up to two records (rows g, g + 8 x tokens 2t, 2t + 1).
+struct Acc2 {
+  float v[2][4];
+};
+
 // One ring stage of NREC records sharing the staged rows: the warp's pair range,
-// the slot released, then the cross-warp reduction.  Threads tid < 128 get the
-// sums of row tid & 15, token tid >> 4 (record 0 in .x, record 1 in .y).
+// then the slot is released.  Returns this lane's accumulators.
 template <typename T, typename S, int NREC, bool G32>
-DEVN float2 tile_pm(const uint8_t* st, const TileGeom tg, const uint8_t* xsh, uint32_t pitch,
-                    const float2* gsum, int nT, float* red, uint64_t* empty_bar) {
+DEVN Acc2 tile_acc(const uint8_t* st, const TileGeom tg, const uint8_t* xsh, uint32_t pitch,
+                   const float2* gsum, int nT, uint64_t* empty_bar) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int np = tg.npairs;
   float acc[NREC][4];
@@ -329,7 +333,53 @@ DEVN float2 tile_pm(const uint8_t* st, const TileGeom tg, const uint8_t* xsh, ui
                                pitch, gsum, xon, acc);
   __syncwarp();
   if (lane == 0) mbar_arrive(empty_bar);
-  return reduce_rows<NREC>(red, acc, nT, tid, warp, lane);
+  Acc2 out;
+#pragma unroll
+  for (int r = 0; r < 2; ++r)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) out.v[r][k] = r < NREC ? acc[r][k] : 0.f;
+  return out;
+}
+
+// Deferred cross-warp reduction: the warps' partial sums of up to `rmax` tiles
+// wait in `red` ([tile][record][warp][token][row]); one barrier and one pass then
+// reduce them all.  Only tokens < nT are kept.
+template <int NREC>
+DEVI void put_partials(float* red, int jj, const Acc2& a, int nT, int warp, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int r = 0; r < NREC; ++r) {
+    float* b = red + ((jj * NREC + r) * kCW + warp) * (nT * 16);
+    if (2 * t < nT) {
+      b[(2 * t) * 16 + g] = a.v[r][0];
+      b[(2 * t) * 16 + g + 8] = a.v[r][2];
+    }
+    if (2 * t + 1 < nT) {
+      b[(2 * t + 1) * 16 + g] = a.v[r][1];
+      b[(2 * t + 1) * 16 + g + 8] = a.v[r][3];
+    }
+  }
+}
+
+// Sums of output o = jj * nT * 16 + token * 16 + row (records 0 and 1).
+template <int NREC>
+DEVI float2 sum_partials(const float* red, int o, int nT) {
+  const int per = nT * 16;
+  const int jj = o / per, rem = o - jj * per;
+  float v = 0.f, v2 = 0.f;
+#pragma unroll
+  for (int w = 0; w < kCW; ++w) {
+    v += red[((jj * NREC) * kCW + w) * per + rem];
+    if (NREC == 2) v2 += red[((jj * NREC + 1) * kCW + w) * per + rem];
+  }
+  return make_float2(v, v2);
+}
+
+// Tiles whose partials fit in `red` at once.
+DEVI int defer_tiles(int nrec, int nT) {
+  int r = (int)(kSRedBytes / 4) / (nrec * kCW * nT * 16);
+  const int by_threads = kConsumers / (nT * 16);
+  return r < by_threads ? r : by_threads;
 }
 
 // One down-projection stage: `cnt` unit records, each with its own staged rows;
@@ -342,8 +392,12 @@ DEVN float4 stage_rm(const uint8_t* st, const TileGeom tg, int cnt, const uint8_
   const int items = cnt * tg.npairs;
   float acc[4];
   zero4(acc);
-  rm_offset<T, S, G32>(st, tg, (warp * items) / kCW, ((warp + 1) * items) / kCW, lane, xd, xpitch,
-                       nT, gsum, ncu, colw, (lane >> 2) < nT, acc);
+  const bool xon = (lane >> 2) < nT;
+  if (!G32 && tg.gshift == 1 && (tg.npairs & 1) == 0)
+    rm_grouped<T, S, 2>(st, tg, cnt, warp, lane, xd, xpitch, nT, gsum, ncu, colw, xon, acc);
+  else
+    rm_offset<T, S, G32>(st, tg, (warp * items) / kCW, ((warp + 1) * items) / kCW, lane, xd, xpitch,
+                         nT, gsum, ncu, colw, xon, acc);
   __syncwarp();
   if (lane == 0) mbar_arrive(empty_bar);
   return make_float4(acc[0], acc[1], acc[2], acc[3]);
@@ -711,32 +765,56 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
       // ---------------------------------------------------------------- Q
       stage_rows<T>(reinterpret_cast<const uint8_t*>(hin), p.H, nT, p.H, nT, xsh, p.x_pitch,
                     p.rms_eps > 0.f, p.rms_eps, nullptr, gsum, cw, red, kStageAll);
-      for (int tile = cta; tile < p.RbQ; tile += G, ++i) {
-        wait_full(i);
-        const float2 v = tile_pm<T, S, 1, G32>(slot_ptr(i), p.tq, xsh, p.x_pitch, gsum, nT, red,
-                                               &empty[i % NS]);
-        if (tid < nT * 16) {
-          const int n = tid >> 4, row = tile * 16 + (tid & 15);
-          reinterpret_cast<T*>(p.qkv)[(size_t)n * p.qkv_R + row] = from_f32<T>(v.x);
+      {
+        const int rmax = defer_tiles(1, nT);
+        int j = 0, t0 = cta;
+        for (int tile = cta; tile < p.RbQ; tile += G, ++i) {
+          wait_full(i);
+          const Acc2 a = tile_acc<T, S, 1, G32>(slot_ptr(i), p.tq, xsh, p.x_pitch, gsum, nT,
+                                                &empty[i % NS]);
+          put_partials<1>(red, j++, a, nT, warp, lane);
+          if (j == rmax || tile + G >= p.RbQ) {
+            named_bar_sync(1, kConsumers);
+            if (tid < j * nT * 16) {
+              const float v = sum_partials<1>(red, tid, nT).x;
+              const int jj = tid / (nT * 16), n = (tid >> 4) - jj * nT;
+              const int row = (t0 + jj * G) * 16 + (tid & 15);
+              reinterpret_cast<T*>(p.qkv)[(size_t)n * p.qkv_R + row] = from_f32<T>(v);
+            }
+            named_bar_sync(1, kConsumers);
+            j = 0;
+            t0 = tile + G;
+          }
         }
-        named_bar_sync(1, kConsumers);
       }
       sync_grid();
       // ---------------------------------------------------------------- O
       if (cta < p.RbO)
         stage_rows<T>(reinterpret_cast<const uint8_t*>(p.qkv), p.qkv_R, nT, p.q_dim, nT, xsh,
                       p.x_pitch, false, 0.f, nullptr, gsum, cw, red, kStageAll);
-      for (int tile = cta; tile < p.RbO; tile += G, ++i) {
-        wait_full(i);
-        const float2 v = tile_pm<T, S, 1, G32>(slot_ptr(i), p.to, xsh, p.x_pitch, gsum, nT, red,
-                                               &empty[i % NS]);
-        if (tid < nT * 16) {
-          const int n = tid >> 4, row = tile * 16 + (tid & 15);
-          const float res = to_f32<T>(__ldcg(hin + (size_t)n * p.H + row));
-          reinterpret_cast<T*>(p.h1)[(size_t)n * p.H + row] =
-              from_f32<T>(to_f32<T>(from_f32<T>(v.x)) + res);
+      {
+        const int rmax = defer_tiles(1, nT);
+        int j = 0, t0 = cta;
+        for (int tile = cta; tile < p.RbO; tile += G, ++i) {
+          wait_full(i);
+          const Acc2 a = tile_acc<T, S, 1, G32>(slot_ptr(i), p.to, xsh, p.x_pitch, gsum, nT,
+                                                &empty[i % NS]);
+          put_partials<1>(red, j++, a, nT, warp, lane);
+          if (j == rmax || tile + G >= p.RbO) {
+            named_bar_sync(1, kConsumers);
+            if (tid < j * nT * 16) {
+              const float v = sum_partials<1>(red, tid, nT).x;
+              const int jj = tid / (nT * 16), n = (tid >> 4) - jj * nT;
+              const int row = (t0 + jj * G) * 16 + (tid & 15);
+              const float res = to_f32<T>(__ldcg(hin + (size_t)n * p.H + row));
+              reinterpret_cast<T*>(p.h1)[(size_t)n * p.H + row] =
+                  from_f32<T>(to_f32<T>(from_f32<T>(v)) + res);
+            }
+            named_bar_sync(1, kConsumers);
+            j = 0;
+            t0 = tile + G;
+          }
         }
-        named_bar_sync(1, kConsumers);
       }
       sync_grid();
       hm = reinterpret_cast<const T*>(p.h1);
@@ -760,17 +838,29 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
     if (tid == 0) mbar_arrive(plan_ready);
     plan_weights(nT, p.E, p.top_k, p.norm, smem, red);
     // ------------------------------------------------------------------ G
-    for (int tile = cta; tile < nu * perG; tile += G, ++i) {
-      wait_full(i);
-      const float2 v = tile_pm<T, S, 2, G32>(slot_ptr(i), p.tgu, xsh, p.x_pitch, gsum, nT, red,
-                                             &empty[i % NS]);
-      if (tid < nT * 16) {
-        const int n = tid >> 4, r = tid & 15;
-        const int u = tile / perG, row = (tile - u * perG) * 16 + r;
-        const float a = ((unit_m[u] >> n) & 1u) ? silu_f32(v.x) * v.y : 0.f;
-        reinterpret_cast<T*>(p.act)[((size_t)u * nT + n) * p.I + row] = from_f32<T>(a);
+    {
+      const int rmax = defer_tiles(2, nT);
+      int j = 0, t0 = cta;
+      for (int tile = cta; tile < nu * perG; tile += G, ++i) {
+        wait_full(i);
+        const Acc2 a = tile_acc<T, S, 2, G32>(slot_ptr(i), p.tgu, xsh, p.x_pitch, gsum, nT,
+                                              &empty[i % NS]);
+        put_partials<2>(red, j++, a, nT, warp, lane);
+        if (j == rmax || tile + G >= nu * perG) {
+          named_bar_sync(1, kConsumers);
+          if (tid < j * nT * 16) {
+            const float2 v = sum_partials<2>(red, tid, nT);
+            const int jj = tid / (nT * 16), n = (tid >> 4) - jj * nT;
+            const int tl = t0 + jj * G;
+            const int u = tl / perG, row = (tl - u * perG) * 16 + (tid & 15);
+            const float a = ((unit_m[u] >> n) & 1u) ? silu_f32(v.x) * v.y : 0.f;
+            reinterpret_cast<T*>(p.act)[((size_t)u * nT + n) * p.I + row] = from_f32<T>(a);
+          }
+          named_bar_sync(1, kConsumers);
+          j = 0;
+          t0 = tile + G;
+        }
       }
-      named_bar_sync(1, kConsumers);
     }
     sync_grid();
     // ------------------------------------------------------------------ N
@@ -917,13 +1007,13 @@ extern "C" int duplex_stack_forward(const duplex_stack_layer* layers, int32_t n_
   slot = up(slot, 128);
   int ups = (int)(slot / p.tdn.rec_bytes);
   if (ups > 32) ups = 32;
-  // activation units staged at once for the down projection (a multiple of ups)
+  // activation units staged at once for the down projection (at least one stage)
   const int by_regs = (kMaxChunks * 8 * kConsumers) / (T * I);
   if (by_regs < 1) return DUPLEX_ERR_UNSUPPORTED;
   if (ups > by_regs) ups = by_regs;
   const int ucap = units_cap(T, E, top_k);
   int act_units = ucap < by_regs ? ucap : by_regs;
-  act_units = act_units < ups ? ups : act_units / ups * ups;
+  if (act_units < ups) act_units = ups;
   p.ups = ups;
   p.act_units = act_units;
   p.slot_bytes = slot;
