@@ -54,7 +54,7 @@ struct StackParams {
   unsigned* barrier;  // grid barrier counter, zeroed before the launch
   int* err;
   int nslots, ups, act_units;
-  uint32_t slot_bytes, off_ring, off_x, off_plain, off_gsum, x_pitch, xd_pitch;
+  uint32_t slot_bytes, off_ring, off_x, off_gsum, x_pitch, xd_pitch;
 };
 
 // fixed shared-memory map (bytes)
@@ -177,12 +177,24 @@ DEVN void stage_rows(const uint8_t* src, int row_stride, int nrows, int K, int r
   const int seg = (nq & 31) == 0 ? 32 : 8;
   named_bar_sync(1, kConsumers);
   // pass 1: fetch into xsh in natural order; sums of squares
-  for (int base = 0; mode != kStageFrag && base < total; base += kConsumers) {
-    const int idx = base + tid;
-    uint4 v = make_uint4(0, 0, 0, 0);
+  for (int base = 0; mode != kStageFrag && base < total; base += 2 * kConsumers) {
+    // both loads of the pair are issued before either is used
+    uint4 vv[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int idx = base + h * kConsumers + tid;
+      vv[h] = make_uint4(0, 0, 0, 0);
+      if (idx < total) {
+        const int r = (int)fast_div((uint32_t)idx, mq, (uint32_t)nq), q = idx - r * nq;
+        vv[h] = __ldcg(reinterpret_cast<const uint4*>(src + ((size_t)r * row_stride + q * 8) * 2));
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+    const int idx = base + h * kConsumers + tid;
+    const uint4 v = vv[h];
     if (idx < total) {
       const int r = (int)fast_div((uint32_t)idx, mq, (uint32_t)nq), q = idx - r * nq;
-      v = __ldcg(reinterpret_cast<const uint4*>(src + ((size_t)r * row_stride + q * 8) * 2));
       *reinterpret_cast<uint4*>(xsh + (uint32_t)r * pitch + (uint32_t)q * 16u) = v;
     }
     if (rms) {
@@ -198,6 +210,7 @@ DEVN void stage_rows(const uint8_t* src, int row_stride, int nrows, int K, int r
         a += __shfl_xor_sync(0xffffffffu, a, 16);
       }
       if ((lane & (seg - 1)) == 0 && idx < total) part[idx / seg] = a;
+    }
     }
   }
   if (mode != kStageFrag) named_bar_sync(1, kConsumers);
@@ -277,7 +290,9 @@ DEVN void stage_rows(const uint8_t* src, int row_stride, int nrows, int K, int r
 // `red` is used again.
 DEVI int red_at(int n, int r) { return n * 16 + r + (n >> 1) * 8; }
 static_assert(7 * 16 + 15 + 3 * 8 < kRedStride, "reduction block");
-static_assert(kSRedBytes >= 16384, "scratch users of red: RMS partials, plan keys");
+static_assert(kSRedBytes >= 4 * (kMaxTokens * kMaxExperts + kMaxTokens * kMaxExperts / 4 +
+                                   kMaxExperts),
+              "scratch users of red: RMS partials, plan keys, candidates, unit_of");
 
 template <int NREC>
 DEVI float2 reduce_rows(float* red, const float (&acc)[NREC][4], int nT, int tid, int warp,
@@ -410,10 +425,11 @@ DEVN float reduce4(float* red, const float4 a, int nT) {
 }
 
 // Router logits of expert e for nT tokens: the gate row (H values, natural order)
-// in `wrow`, the normalised tokens in `xplain`.  Thread n < nT returns logit n.
+// in `wrow`, the normalised tokens in natural order at xrows + n * xpitch.  Thread
+// n < nT returns logit n.
 template <typename T>
-DEVN float router_row(const uint8_t* wrow, const uint8_t* xplain, int H, int nT, const void* gate_b,
-                      int e, float* red, uint64_t* empty_bar) {
+DEVN float router_row(const uint8_t* wrow, const uint8_t* xrows, uint32_t xpitch, int H, int nT,
+                      const void* gate_b, int e, float* red, uint64_t* empty_bar) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint4* wr = reinterpret_cast<const uint4*>(wrow);
   const int nq = H >> 3;
@@ -426,7 +442,7 @@ DEVN float router_row(const uint8_t* wrow, const uint8_t* xplain, int H, int nT,
 #pragma unroll
     for (int n = 0; n < kMaxTokens; ++n) {
       if (n < nT) {
-        const uint4 xv = *reinterpret_cast<const uint4*>(xplain + ((size_t)n * H + q * 8) * 2);
+        const uint4 xv = *reinterpret_cast<const uint4*>(xrows + (size_t)n * xpitch + (size_t)q * 16);
         const T* xe = reinterpret_cast<const T*>(&xv);
 #pragma unroll
         for (int k = 0; k < 8; ++k) part[n] = fmaf(to_f32<T>(we[k]), to_f32<T>(xe[k]), part[n]);
@@ -456,6 +472,104 @@ DEVN float router_row(const uint8_t* wrow, const uint8_t* xplain, int H, int nT,
   return a;
 }
 
+// Router logits with the RMS staging fused in: fetch the nT rows of h (H values,
+// through L2), RMS-normalise them in registers (rounded to T), leave them in
+// natural order in xsh for the fragment staging that follows, and dot them with
+// this CTA's gate row `wrow` (natural order in the ring slot; null when the CTA has
+// no router row).  Threads tid < nT return the rounded logit of row tid.  Every
+// sum runs in a fixed order.  nT * H <= kMaxChunks * 8 * 512.
+template <typename T>
+DEVN float router_fused(const uint8_t* src, int H, int nT, bool rms, float eps, uint8_t* xsh,
+                        uint32_t pitch, const uint8_t* wrow, const void* gate_b, int e, float* red,
+                        uint64_t* empty_bar) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int nq = H >> 3, total = nT * nq;
+  const uint32_t mq = fast_div_m((uint32_t)nq);
+  const int seg = (nq & 31) == 0 ? 32 : 8;
+  const int per = nq / seg;  // segments per row
+  float* part = red;         // sums of squares, one per segment
+  float* dotp = red + 1024;  // dot products, one per segment
+  named_bar_sync(1, kConsumers);
+  uint4 v[kMaxChunks];
+#pragma unroll
+  for (int j = 0; j < kMaxChunks; ++j) {
+    const int idx = tid + j * kConsumers;
+    v[j] = make_uint4(0, 0, 0, 0);
+    if (idx < total) {
+      const int r = (int)fast_div((uint32_t)idx, mq, (uint32_t)nq), q = idx - r * nq;
+      v[j] = __ldcg(reinterpret_cast<const uint4*>(src + ((size_t)r * H + q * 8) * 2));
+    }
+  }
+  if (rms) {
+#pragma unroll
+    for (int j = 0; j < kMaxChunks; ++j) {
+      if (j * kConsumers >= total) break;  // uniform
+      const int idx = tid + j * kConsumers;
+      float a = 0.f;
+      const T* x = reinterpret_cast<const T*>(&v[j]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) a = fmaf(to_f32<T>(x[k]), to_f32<T>(x[k]), a);
+      a += __shfl_xor_sync(0xffffffffu, a, 1);
+      a += __shfl_xor_sync(0xffffffffu, a, 2);
+      a += __shfl_xor_sync(0xffffffffu, a, 4);
+      if (seg == 32) {
+        a += __shfl_xor_sync(0xffffffffu, a, 8);
+        a += __shfl_xor_sync(0xffffffffu, a, 16);
+      }
+      if ((lane & (seg - 1)) == 0 && idx < total) part[idx / seg] = a;
+    }
+    named_bar_sync(1, kConsumers);
+  }
+#pragma unroll
+  for (int j = 0; j < kMaxChunks; ++j) {
+    if (j * kConsumers >= total) break;  // uniform
+    const int idx = tid + j * kConsumers;
+    float d = 0.f;
+    if (idx < total) {
+      const int r = (int)fast_div((uint32_t)idx, mq, (uint32_t)nq), q = idx - r * nq;
+      uint4 o = v[j];
+      if (rms) {
+        float a = 0.f;
+        for (int c = 0; c < per; ++c) a += part[r * per + c];
+        const float sc = 1.0f / sqrtf(a / (float)H + eps);
+        T* x = reinterpret_cast<T*>(&o);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) x[k] = from_f32<T>(to_f32<T>(x[k]) * sc);
+      }
+      *reinterpret_cast<uint4*>(xsh + (uint32_t)r * pitch + (uint32_t)q * 16u) = o;
+      if (wrow) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(wrow + (size_t)q * 16);
+        const T* w = reinterpret_cast<const T*>(&wv);
+        const T* x = reinterpret_cast<const T*>(&o);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) d = fmaf(to_f32<T>(w[k]), to_f32<T>(x[k]), d);
+      }
+    }
+    if (wrow) {
+      d += __shfl_xor_sync(0xffffffffu, d, 1);
+      d += __shfl_xor_sync(0xffffffffu, d, 2);
+      d += __shfl_xor_sync(0xffffffffu, d, 4);
+      if (seg == 32) {
+        d += __shfl_xor_sync(0xffffffffu, d, 8);
+        d += __shfl_xor_sync(0xffffffffu, d, 16);
+      }
+      if ((lane & (seg - 1)) == 0 && idx < total) dotp[idx / seg] = d;
+    }
+  }
+  if (wrow) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty_bar);
+  }
+  named_bar_sync(1, kConsumers);
+  float a = 0.f;
+  if (wrow && tid < nT) {
+    for (int c = 0; c < per; ++c) a += dotp[tid * per + c];
+    if (gate_b) a += to_f32<T>(reinterpret_cast<const T*>(gate_b)[e]);
+    a = to_f32<T>(from_f32<T>(a));
+  }
+  return a;
+}
+
 // Order key of a logit for the top-k.  Logits are rounded to the 16-bit
 // activation type, so (ordered 16-bit value << 15) | (0x7FFF - expert) is a unique
 // 31-bit key per expert and "k > v" is the sign of v - k: larger logit first, ties
@@ -475,7 +589,10 @@ DEVI uint32_t order_key(float f, int e) {
 // Top-k of every token and the unit plan (distinct selected experts in ascending
 // id order, their token masks), identical in every CTA.  The routing weights
 // follow in plan_weights, off the critical path.  Returns the unit count.
-// scratch: keys [T][E], then unit_of [E].
+// Top-k by warp max-reductions over the unique keys: per (token, 32-expert block)
+// a warp takes the block's top k (k rounds of redux.sync max, the winner's lane
+// clears its key), then one warp per token merges the blocks' candidates.
+// scratch: keys [T][E] | candidates [T][blocks * top_k] | unit_of [E].
 template <typename T>
 DEVN int plan_units(const float* logits, int nT, int E, int top_k, uint8_t* smem, float* scratch) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -487,7 +604,9 @@ DEVN int plan_units(const float* logits, int nT, int E, int top_k, uint8_t* smem
   int* n_units_s = reinterpret_cast<int*>(smem + kSNUnits);
   uint32_t* selbits = reinterpret_cast<uint32_t*>(smem + kSSelBits);
   uint32_t* keys = reinterpret_cast<uint32_t*>(scratch);
-  int* unit_of = reinterpret_cast<int*>(scratch) + kMaxTokens * kMaxExperts;
+  const int nblk = (E + 31) >> 5;
+  uint32_t* cand = keys + kMaxTokens * kMaxExperts;  // [T][nblk * top_k], every slot written
+  int* unit_of = reinterpret_cast<int*>(cand + kMaxTokens * (kMaxExperts / 4));
   const int TE = nT * E;
   for (int idx = tid; idx < TE; idx += kConsumers) {
     const float v = __ldcg(logits + idx);
@@ -497,43 +616,40 @@ DEVN int plan_units(const float* logits, int nT, int E, int top_k, uint8_t* smem
   }
   if (tid < kMaxTokens * 8) selbits[tid] = 0u;
   named_bar_sync(1, kConsumers);
-  // rank of each logit within its token: four lanes per logit, each counting the
-  // larger keys in a quarter of the experts (vector loads, rotated per lane so
-  // the four quarters hit different banks)
-  const bool vec = (E & 15) == 0;
-  const int items = ((TE * 4 + 31) / 32) * 32;
-  for (int idx = tid; idx < items; idx += kConsumers) {
-    const int te = idx >> 2, qq = idx & 3;
-    uint32_t rank = 0;
-    int tk = 0;
-    if (te < TE) {
-      tk = te / E;
-      const uint32_t v = keys[te];
-      const uint32_t* row = keys + tk * E;
-      if (vec) {
-        const int nc = E >> 4;  // 4-key chunks per quarter
-        const uint4* q4 = reinterpret_cast<const uint4*>(row) + qq * nc;
-        const int rot = (2 * qq) % nc;
-        for (int j = 0; j < nc; ++j) {
-          const int jj = j + rot < nc ? j + rot : j + rot - nc;
-          const uint4 k4 = q4[jj];
-          rank += ((v - k4.x) >> 31) + ((v - k4.y) >> 31) + ((v - k4.z) >> 31) + ((v - k4.w) >> 31);
-        }
-      } else {
-        for (int e2 = qq; e2 < E; e2 += 4) rank += (v - row[e2]) >> 31;
-      }
+  // per (token, block): the block's top k, in descending order
+  for (int wu = warp; wu < nT * nblk; wu += kCW) {
+    const int tk = wu / nblk, blk = wu - tk * nblk;
+    const int e = blk * 32 + lane;
+    uint32_t key = e < E ? keys[tk * E + e] : 0u;
+    uint32_t* cb = cand + (tk * nblk + blk) * top_k;
+    for (int j = 0; j < top_k; ++j) {
+      const uint32_t m = __reduce_max_sync(0xffffffffu, key);
+      if (key == m && m != 0u) key = 0u;
+      if (lane == 0) cb[j] = m;  // 0 once the block has no experts left
     }
-    rank += __shfl_xor_sync(0xffffffffu, rank, 1);
-    rank += __shfl_xor_sync(0xffffffffu, rank, 2);
-    if (te < TE && qq == 0 && rank < (uint32_t)top_k) {
-      const int e = te - tk * E;
-      sel_s[tk * 8 + rank] = e;
-      atomicOr(&selbits[tk * 8 + (e >> 5)], 1u << (e & 31));
+  }
+  named_bar_sync(1, kConsumers);
+  // per token: merge the blocks' candidates (at most 64, two per lane)
+  if (warp < nT) {
+    const int tk = warp, nc = nblk * top_k;  // <= 64
+    uint32_t c0 = lane < nc ? cand[tk * nc + lane] : 0u;
+    uint32_t c1 = lane + 32 < nc ? cand[tk * nc + lane + 32] : 0u;
+    for (int j = 0; j < top_k; ++j) {
+      const uint32_t m = __reduce_max_sync(0xffffffffu, c0 > c1 ? c0 : c1);
+      if (m != 0u && c0 == m) c0 = 0u;
+      else if (m != 0u && c1 == m) c1 = 0u;
+      if (lane == 0) {
+        // keys are never 0 and top_k <= E, so m names an expert; clamp regardless
+        int e = (int)(0x7FFFu - (m & 0x7FFFu));
+        e = (m == 0u || e >= E) ? 0 : e;
+        sel_s[tk * 8 + j] = e;
+        atomicOr(&selbits[tk * 8 + (e >> 5)], 1u << (e & 31));
+      }
     }
   }
   named_bar_sync(1, kConsumers);
   // unit plan: position of a selected expert = selected experts below it
-  const int nw = (E + 31) >> 5;
+  const int nw = nblk;
   if (warp < nw) {
     const int e = warp * 32 + lane;
     uint32_t mask = 0, below = 0, all = 0;
@@ -547,10 +663,10 @@ DEVN int plan_units(const float* logits, int nT, int E, int top_k, uint8_t* smem
         for (int tk = 0; tk < nT; ++tk) mask |= ((selbits[tk * 8 + w] >> lane) & 1u) << tk;
       }
     }
+    if (mask) unit_of[e] = below < (uint32_t)kMaxUnits ? (int)below : kMaxUnits;
     if (mask && below < (uint32_t)kMaxUnits) {
       unit_e[below] = e;
       unit_m[below] = mask;
-      unit_of[e] = (int)below;
 #pragma unroll
       for (int n = 0; n < kMaxTokens; ++n) unit_w[below * kMaxTokens + n] = 0.f;
     }
@@ -567,7 +683,8 @@ DEVN void plan_weights(int nT, int E, int top_k, int norm, uint8_t* smem, const 
   const float* ls = reinterpret_cast<const float*>(smem + kSLogit);
   const int* sel_s = reinterpret_cast<const int*>(smem + kSSel);
   float* unit_w = reinterpret_cast<float*>(smem + kSUnitW);
-  const int* unit_of = reinterpret_cast<const int*>(scratch) + kMaxTokens * kMaxExperts;
+  const int* unit_of = reinterpret_cast<const int*>(scratch) + kMaxTokens * kMaxExperts +
+                       kMaxTokens * (kMaxExperts / 4);
   if (warp < nT) {
     const int tk = warp;
     const float* row = ls + tk * E;
@@ -584,9 +701,9 @@ DEVN void plan_weights(int nT, int E, int top_k, int norm, uint8_t* smem, const 
       const float x = __shfl_sync(0xffffffffu, pj, j);
       if (j < top_k) psum += x;
     }
-    if (lane < top_k) {
+    if (lane < top_k && ej >= 0 && ej < E) {
       const int u = unit_of[ej];
-      if (u < kMaxUnits) unit_w[u * kMaxTokens + tk] = norm ? pj / psum : pj;
+      if (u >= 0 && u < kMaxUnits) unit_w[u * kMaxTokens + tk] = norm ? pj / psum : pj;
     }
   }
   named_bar_sync(1, kConsumers);
@@ -738,7 +855,6 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
   // ================================================================== consumers
   float* red = reinterpret_cast<float*>(smem + kSRed);
   uint8_t* xsh = smem + p.off_x;
-  uint8_t* xplain = smem + p.off_plain;
   float2* gsum = reinterpret_cast<float2*>(smem + p.off_gsum);
   const int nT = p.T;
   const int cw = G32 ? 1 : 2;
@@ -820,14 +936,24 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
       hm = reinterpret_cast<const T*>(p.h1);
     }
     // ------------------------------------------------------------------ R
-    // normalised rows for the router first; their fragment-order staging for the
-    // gate|up tiles runs while the logits barrier is in flight
-    stage_rows<T>(reinterpret_cast<const uint8_t*>(hm), p.H, nT, p.H, nT, xsh, p.x_pitch,
-                  p.rms_eps > 0.f, p.rms_eps, xplain, gsum, cw, red, kStageNorm);
-    for (int e = cta; e < p.E; e += G, ++i) {
-      wait_full(i);
-      const float a = router_row<T>(slot_ptr(i), xplain, p.H, nT, L.gate_b, e, red, &empty[i % NS]);
-      if (tid < nT) p.logits[(size_t)tid * p.E + e] = a;
+    // normalised rows and this CTA's logit first; their fragment-order staging for
+    // the gate|up tiles runs while the logits barrier is in flight
+    {
+      const bool row = cta < p.E;
+      if (row) wait_full(i);
+      const float a = router_fused<T>(reinterpret_cast<const uint8_t*>(hm), p.H, nT, p.rms_eps > 0.f,
+                                      p.rms_eps, xsh, p.x_pitch, row ? slot_ptr(i) : nullptr,
+                                      L.gate_b, cta, red, &empty[i % NS]);
+      if (row) {
+        if (tid < nT) p.logits[(size_t)tid * p.E + cta] = a;
+        ++i;
+      }
+      for (int e = cta + G; e < p.E; e += G, ++i) {  // more experts than CTAs
+        wait_full(i);
+        const float a2 = router_row<T>(slot_ptr(i), xsh, p.x_pitch, p.H, nT, L.gate_b, e, red,
+                                       &empty[i % NS]);
+        if (tid < nT) p.logits[(size_t)tid * p.E + e] = a2;
+      }
     }
     grid_arrive(p.barrier);
     stage_rows<T>(nullptr, 0, nT, p.H, nT, xsh, p.x_pitch, false, 0.f, nullptr, gsum, cw, red,
@@ -1026,8 +1152,7 @@ extern "C" int duplex_stack_forward(const duplex_stack_layer* layers, int32_t n_
   const uint32_t gsum_bytes = (uint32_t)((gs_q > gs_d ? gs_q : gs_d) * 8);
   p.off_gsum = up(kSFixedEnd, 128);
   p.off_x = up(p.off_gsum + gsum_bytes, 128);
-  p.off_plain = up(p.off_x + x_bytes, 128);
-  p.off_ring = up(p.off_plain + (uint32_t)T * H * 2u, 128);
+  p.off_ring = up(p.off_x + x_bytes, 128);
   const size_t kMax = 227 * 1024;
   int ns = p.off_ring < kMax ? (int)((kMax - p.off_ring) / slot) : 0;
   if (ns > kSlotsMax) ns = kSlotsMax;
