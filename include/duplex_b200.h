@@ -161,6 +161,40 @@ int duplex_moe_forward(const void* x, int act_dtype, int32_t T, const void* gate
                        int32_t* err, float rms_eps, int pdl, void* stream);
 
 /*
+ * moe_grouped_workspace_bytes -- scratch of duplex_moe_grouped for T tokens (logits,
+ * selection, the expert-sorted assignment list, the unit list and one fp32 output row
+ * per (token, slot)).  No zero fill needed.  Returns DUPLEX_ERR_UNSUPPORTED for a
+ * geometry the grouped path does not take (see duplex_moe_grouped), so it doubles as
+ * the support query.
+ */
+int duplex_moe_grouped_workspace_bytes(int32_t T, int32_t E, int32_t H, int32_t I,
+                                       int32_t top_k, int32_t group, int has_zeros,
+                                       size_t* bytes);
+
+/*
+ * moe_grouped -- `FusedPackedMoE.forward` (fused_packed_moe.py:191-275) for a batch of
+ * T <= 512 tokens (batched decode of many streams, prefill chunks), where the T <= 8
+ * entry points above do not apply.  Five launches on `stream`: router logits on the
+ * tensor cores (skipped when logits_in != NULL: [T][E] fp32, already rounded to the act
+ * dtype), top-k + softmax, a stable counting sort of the T*top_k (token, slot) pairs by
+ * expert into units of <= 20 tokens, one CTA per unit streaming its expert's gate|up and
+ * down tiles once (SiLU(gate)*up kept in shared memory), and the routing-weighted
+ * combine in selection order (+ residual), one rounding.  Arguments as duplex_moe_forward
+ * (rms_eps and pdl excepted); E <= 256, top_k <= 8, H and I multiples of 64, group a
+ * power of two >= 64, one unit's tokens, intermediate and two weight stages within
+ * 227 KB of shared memory (Thinker geometry, hidden 2048 / inter 768, takes 212 KB),
+ * scale dtype == act dtype.  x, out, tiles, gate_w and workspace
+ * 16-byte aligned.  err: device int, DUPLEX_DEVERR_EXPERT when a selected id is out of
+ * range, DUPLEX_DEVERR_TIMEOUT when a copy wait gives up (bounded, about 2 s).
+ */
+int duplex_moe_grouped(const void* x, int act_dtype, int32_t T, const void* gate_w,
+                       const void* gate_b, const float* logits_in, int32_t E, int32_t H,
+                       int32_t I, int32_t top_k, int32_t norm_topk, const void* gu_tiles,
+                       const void* dn_tiles, int scale_dtype, int has_zeros, int32_t group,
+                       const void* residual, void* out, float* w_out, int32_t* sel_out,
+                       void* workspace, size_t workspace_bytes, int32_t* err, void* stream);
+
+/*
  * Persistent clock-path stack -- the reference's clock path (src/duplex/streaming/clock.py:
  * 162-197) runs Thinker layers 0..23 per frame with TritonPackedLinear q/k/v/o and
  * FusedPackedMoE; this is every int4 linear of n_layers such layers for T <= 8 tokens in ONE

@@ -27,7 +27,8 @@ import numpy as np
 __all__ = [
     "PACK", "round_to", "np_dtype", "pack4", "unpack_nibbles", "unpack4",
     "pack_zeros", "unpack_zeros", "dequant", "dequantize_weight", "router",
-    "moe_experts", "moe_forward", "dequant_gemv", "packed_linear", "silu",
+    "moe_experts", "moe_experts_by_expert", "moe_forward", "dequant_gemv", "packed_linear",
+    "silu",
 ]
 
 PACK = 8          # nibbles per int32 word (fused_packed_moe.py:33-34)
@@ -226,6 +227,33 @@ def moe_experts(x, sel, w, gu_packed, gu_scale, dn_packed, dn_scale,
         dn = dequant(dn_packed[st], np.asarray(dn_scale[st], np.float32).astype(ct), Ki, dz, sdt)
         y = np.matmul(dn, act[:, :Ki, None])[..., 0]               # [k, H]
         out[t] = (y * np.asarray(w[t], dtype=ct)[:, None]).sum(axis=0)
+    return out
+
+
+def moe_experts_by_expert(x, sel, w, gu_packed, gu_scale, dn_packed, dn_scale,
+                          gu_zeros=None, dn_zeros=None):
+    """`moe_experts` in fp32 with one dequantisation per selected expert, shared by every
+    token that selects it (the reference's per-token loop of fused_packed_moe.py:265-275,
+    reordered so that batches of hundreds of tokens finish in seconds).  Same values up
+    to fp32 summation order: each token's slots are added in ascending expert order."""
+    x = np.asarray(x, dtype=np.float32)
+    sel = np.asarray(sel)
+    w = np.asarray(w, dtype=np.float32)
+    T, H = x.shape
+    I = gu_packed.shape[-2] // 2
+    Ki = dn_packed.shape[-1] * PACK
+    out = np.zeros((T, dn_packed.shape[-2]), dtype=np.float32)
+    for e in np.unique(sel):
+        t_idx, j_idx = np.nonzero(sel == e)
+        gz = None if gu_zeros is None else gu_zeros[e]
+        dz = None if dn_zeros is None else dn_zeros[e]
+        gu = dequant(gu_packed[e], np.asarray(gu_scale[e], np.float32), H, gz, "float32")
+        h = x[t_idx] @ gu.T                                          # [n, 2I]
+        g, u = h[:, :I], h[:, I:]
+        act = (g / (np.float32(1.0) + np.exp(-g))) * u
+        dn = dequant(dn_packed[e], np.asarray(dn_scale[e], np.float32), Ki, dz, "float32")
+        y = act[:, :Ki] @ dn.T                                       # [n, H]
+        out[t_idx] += y * w[t_idx, j_idx][:, None]
     return out
 
 

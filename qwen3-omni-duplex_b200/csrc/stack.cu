@@ -31,6 +31,7 @@
 // lower expert id.
 #include "gemv_core.cuh"
 #include "moe.cuh"
+#include "topk.cuh"
 
 namespace duplex {
 
@@ -568,22 +569,6 @@ DEVN float router_fused(const uint8_t* src, int H, int nT, bool rms, float eps, 
     a = to_f32<T>(from_f32<T>(a));
   }
   return a;
-}
-
-// Order key of a logit for the top-k.  Logits are rounded to the 16-bit
-// activation type, so (ordered 16-bit value << 15) | (0x7FFF - expert) is a unique
-// 31-bit key per expert and "k > v" is the sign of v - k: larger logit first, ties
-// to the lower expert id, NaN above everything (as torch.topk), -0 equal to +0.
-// Every CTA derives the same plan from the same logits, whatever their values.
-template <typename T>
-DEVI uint32_t order_key(float f, int e) {
-  const T h = from_f32<T>(f);
-  uint32_t b = (uint32_t)*reinterpret_cast<const uint16_t*>(&h);
-  const bool nan = DqOff<T>::kOddDiv16 ? ((b & 0x7C00u) == 0x7C00u && (b & 0x3FFu))
-                                       : ((b & 0x7F80u) == 0x7F80u && (b & 0x7Fu));
-  if (b == 0x8000u) b = 0u;
-  b = nan ? 0xFFFFu : ((b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u));
-  return (b << 15) | (0x7FFFu - (uint32_t)e);
 }
 
 // Top-k of every token and the unit plan (distinct selected experts in ascending

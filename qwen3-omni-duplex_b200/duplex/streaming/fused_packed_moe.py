@@ -17,7 +17,9 @@ Differences, all deliberate:
     weights are never staged from host memory and nothing is computed on the CPU;
   * batches of up to 8 tokens run as ONE pass (tokens that select the same expert
     share its weight stream) instead of a per-token Python loop; larger batches
-    are processed 8 tokens at a time;
+    (batched decode of many streams, prefill chunks) run the grouped path, up to
+    512 tokens per call: tokens sorted by expert, every selected expert's weights
+    streamed once per 20 of its tokens;
   * optional 4-bit zero points (`weight_zeros` on the expert linears,
     [R, ceil(G/8)] int32, nibble order along the group axis); absent means the
     reference's symmetric format (value = nibble - 8);
@@ -37,6 +39,7 @@ from duplex.streaming.triton_dequant_gemv import HAVE_TRITON, Int4Tiles, dequant
 NUM_BITS = 4
 PACK = 32 // NUM_BITS
 GROUP = 32
+GROUPED_MAX_TOKENS = 512    # tokens per duplex_moe_grouped call
 
 
 def unpack4(packed: torch.Tensor, out_cols: int) -> torch.Tensor:
@@ -166,6 +169,49 @@ class FusedPackedMoE(nn.Module):
             self._ws[(T, device)] = ws
         return ws
 
+    def grouped_supported(self) -> bool:
+        """Whether the grouped path takes this layer's geometry (asked of the library:
+        group a power of two >= 64, hidden and inter multiples of 64, one unit's working
+        set within shared memory; down projection [hidden, inter])."""
+        if self.hid_out != self.hidden or self.inter_in != self.inter:
+            return False
+        n = _lib.ctypes.c_size_t()
+        rc = _lib.load().duplex_moe_grouped_workspace_bytes(
+            1, self.num_experts, self.hidden, self.inter, self.top_k, self.group,
+            1 if self.has_zeros else 0, _lib.ctypes.byref(n))
+        return rc == 0
+
+    def grouped_workspace(self, T: int, device) -> torch.Tensor:
+        ws = self._ws.get(("grouped", T, device))
+        if ws is None:
+            n = _lib.ctypes.c_size_t()
+            _lib.call("duplex_moe_grouped_workspace_bytes", T, self.num_experts, self.hidden,
+                      self.inter, self.top_k, self.group, 1 if self.has_zeros else 0,
+                      _lib.ctypes.byref(n))
+            ws = torch.empty(n.value, dtype=torch.uint8, device=device)
+            self._ws[("grouped", T, device)] = ws
+        return ws
+
+    def forward_grouped_into(self, x, out, residual=None, w_out=None, sel_out=None,
+                             logits=None):
+        """x [T<=512, H] -> out [T, H] (+ residual) through the grouped path, no host
+        synchronisation.  logits: optional [T, E] fp32 router logits (already rounded to
+        the module dtype) used in place of the gate."""
+        T = x.shape[0]
+        if T > GROUPED_MAX_TOKENS:
+            raise _lib.DuplexError(f"grouped MoE takes at most {GROUPED_MAX_TOKENS} tokens")
+        ws = self.grouped_workspace(T, x.device)
+        g = self.gate
+        lg = None if logits is None else _lib.aligned(logits.float())
+        _lib.call(
+            "duplex_moe_grouped", _lib.ptr(x), _lib.dtype_code(x.dtype), T, _lib.ptr(g.weight),
+            _lib.ptr(g.bias), _lib.ptr(lg), self.num_experts, self.hidden, self.inter,
+            self.top_k, 1 if self.norm_topk_prob else 0, _lib.ptr(self.gu_tiles.buf),
+            _lib.ptr(self.dn_tiles.buf), self.gu_tiles.scale_code, 1 if self.has_zeros else 0,
+            self.group, _lib.ptr(residual), _lib.ptr(out), _lib.ptr(w_out), _lib.ptr(sel_out),
+            _lib.ptr(ws), ws.numel(), _lib.ptr(self.err), _lib.stream_of(x))
+        return out
+
     def forward_into(self, x, out, residual=None, w_out=None, sel_out=None, rms_eps=0.0):
         """x [T<=8, H] -> out [T, H] (+ residual), no host synchronisation.  rms_eps > 0 routes
         and computes on the RMS-normalised x (clock-path stack)."""
@@ -208,8 +254,13 @@ class FusedPackedMoE(nn.Module):
             x = x.to(self.gate.weight.dtype)
         T = x.shape[0]
         out = torch.empty(T, self.hid_out, dtype=x.dtype, device=x.device)
-        for t0 in range(0, T, 8):
-            self.forward_into(x[t0:t0 + 8], out[t0:t0 + 8])
+        if T > 8 and self.grouped_supported():
+            for t0 in range(0, T, GROUPED_MAX_TOKENS):
+                self.forward_grouped_into(x[t0:t0 + GROUPED_MAX_TOKENS],
+                                          out[t0:t0 + GROUPED_MAX_TOKENS])
+        else:
+            for t0 in range(0, T, 8):
+                self.forward_into(x[t0:t0 + 8], out[t0:t0 + 8])
         return out.to(hidden_states.dtype).view(shape)
 
     def device_errors(self) -> int:

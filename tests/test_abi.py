@@ -82,6 +82,36 @@ def test_unsupported_shapes_are_rejected(lib):
                                 None) == 4
 
 
+def test_grouped_moe_rejects_before_any_launch(lib):
+    n = ctypes.c_size_t()
+
+    def wsb(T=256, E=128, H=2048, I=768, k=8, group=128, zp=1):
+        return lib.duplex_moe_grouped_workspace_bytes(T, E, H, I, k, group, zp, ctypes.byref(n))
+
+    assert wsb() == 0 and n.value > 256 * 8 * 2048 * 4   # one fp32 row per (token, slot)
+    assert wsb(T=512) == 0
+    assert wsb(T=513) == 1                         # more tokens than one call takes
+    assert wsb(E=257) == 1 and wsb(k=9) == 1
+    assert wsb(group=32) == 6                      # groups below 64 columns
+    assert wsb(group=96) == 6
+    assert wsb(H=4096) == 6                        # one unit's working set > 227 KB of smem
+    assert wsb(I=1536) == 6
+    p = ctypes.c_void_p(1 << 20)
+    big = 1 << 30
+
+    def grouped(x=p, T=64, group=128, ws=big, logits=None, gate=p, act=0, sdt=0):
+        return lib.duplex_moe_grouped(x, act, T, gate, None, logits, 128, 2048, 768, 8, 1, p, p,
+                                      sdt, 1, group, None, p, None, None, p, ws, p, None)
+
+    assert grouped(T=0) == 1 and grouped(T=513) == 1
+    assert grouped(gate=None) == 1                 # neither a gate nor logits
+    assert grouped(x=ctypes.c_void_p((1 << 20) + 4)) == 2
+    assert grouped(logits=ctypes.c_void_p((1 << 20) + 4)) == 2
+    assert grouped(sdt=1) == 3 and grouped(act=2, sdt=2) == 3
+    assert grouped(group=32) == 6
+    assert grouped(ws=16) == 4
+
+
 def test_python_wrappers_refuse_cpu_tensors():
     import torch
     from duplex.streaming.fused_packed_moe import unpack4
