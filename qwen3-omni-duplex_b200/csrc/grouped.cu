@@ -28,7 +28,7 @@ int num_sms();
 int ensure_smem_attr(const void* fn, int bytes);
 
 constexpr int kGTok = 20;    // tokens of one expert unit
-constexpr int kGNB = 3;      // 8-token MMA column blocks (kGNB * 8 >= kGTok)
+constexpr int kGNB = 3;      // 8-token MMA column blocks at most (kGNB * 8 >= kGTok)
 constexpr int kGPad = 24;    // token slots per pair in the correction sums
 constexpr int kGMaxT = 512;  // tokens per call
 constexpr int kGSmemMax = 227 * 1024;
@@ -236,8 +236,22 @@ __global__ void __launch_bounds__(512) g_bucket_kernel(const int* sel, int nT, i
 }
 
 // ------------------------------------------------------------------ 4. experts
+// Two persistent kernels, one CTA per SM, over flattened work lists so that every
+// SM streams whatever the routing: gate|up items (unit, record pair) and down items
+// (unit, stage of 8 down records).  A CTA takes a contiguous range of the list, so
+// it re-stages a unit's token rows only when its range crosses into the next unit.
+// One producer thread keeps a ring of bulk copies in flight; 16 consumer warps
+// apply each dequantised weight fragment to the unit's NB = ceil(n / 8) 8-token MMA
+// column blocks (NB dispatched per unit, warp-uniform).
+//
+// MMA columns of absent tokens (rows n .. 8 NB - 1 of the staged block) are never
+// read back: each output column depends on its own token only, so those rows are
+// neither zeroed nor masked (they lie inside this CTA's shared memory).
+constexpr int kGMaxSlots = 8;
+constexpr int kGDnRec = 8;  // down records per stage (one per warp of an 8-warp group)
+
 struct GExpParams {
-  int H, I, E, top_k;
+  int H, I, E, top_k, max_units;
   TileGeom tgu, tdn;
   const uint8_t* x;
   const uint8_t* gu_tiles;
@@ -245,196 +259,380 @@ struct GExpParams {
   const int* assign;
   const int* units;
   const int* n_units;
-  float* ypart;  // [T][k][H]
+  uint8_t* act;   // [T*k][I] SiLU(gate)*up per sorted assignment, fragment order
+  float* ypart;   // [T][k][H]
   int* err;
-  uint32_t x_pitch, a_pitch, slot_bytes;
-  uint32_t off_x, off_gx, off_a, off_ga, off_red, off_ring;
+  uint32_t x_pitch, a_pitch;
+  // gate|up kernel map: token rows, per-pair and per-group correction sums, partials, ring
+  uint32_t off_x, off_gx, off_gxg, off_red_a, off_ring_a, slot_a, smem_a;
+  int ns_a;
+  // down kernel map
+  uint32_t off_a, off_ga, off_gag, off_ring_d, slot_d, smem_d;
+  int ns_d;
 };
 
-constexpr uint32_t kGFull = 0, kGEmpty = 16, kGAbort = 32, kGTokS = 64,
-                   kGSlotS = 64 + 4 * kGTok, kGFixedEnd = 256;
+constexpr uint32_t kGFull = 0, kGEmpty = 8 * kGMaxSlots, kGAbort = 16 * kGMaxSlots,
+                   kGTokS = kGAbort + 16, kGSlotS = kGTokS + 4 * kGTok, kGFixedEnd = 384;
 static_assert(kGSlotS + 4 * kGTok <= kGFixedEnd, "fixed map");
+constexpr uint32_t kGRedBytes = kCW * kGNB * 4 * 32 * 4;  // gate|up partials: 2 groups x 8 warps x 3 blocks
 
-// One warp's pairs [pb, pe) of one record against ntok staged token rows (up to
-// kGNB blocks of 8): each pair's weights are dequantised once and applied to every
-// block.  gsum: [pair][kGPad] float2 correction sums.
-template <typename T, typename S>
-DEVI void gmm_pairs(const uint8_t* rec, const TileGeom& tg, int pb, int pe, int lane,
-                    const uint8_t* xsh, uint32_t pitch, const float2* gsum, int ntok,
-                    float (&acc)[kGNB][4]) {
+// Correction term of one group for NB blocks: acc += s * (D - (P + z Q)), the scale
+// and zero point read once for all blocks; gs[nb] = (P, Q) of tokens 2t and 2t + 1.
+template <typename S, int NB>
+DEVI void flush_nb(float (&acc)[NB][4], const float (&d)[NB][4], const uint8_t* rec, const TileGeom& tg,
+                   int grp, int g, const float4 (&gs)[NB]) {
+  const uint32_t zz = tg.has_zeros ? (uint32_t)rec[tg.off_zero + grp * 8 + g] : 0x88u;
+  const float za = (float)(zz & 15u), zb = (float)(zz >> 4);
+  const float2 s = scale_pair(reinterpret_cast<const uint32_t*>(rec + tg.off_scale)[grp * 8 + g], (S*)nullptr);
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb) {
+    acc[nb][0] = fmaf(s.x, d[nb][0] - fmaf(za, gs[nb].y, gs[nb].x), acc[nb][0]);
+    acc[nb][1] = fmaf(s.x, d[nb][1] - fmaf(za, gs[nb].w, gs[nb].z), acc[nb][1]);
+    acc[nb][2] = fmaf(s.y, d[nb][2] - fmaf(zb, gs[nb].y, gs[nb].x), acc[nb][2]);
+    acc[nb][3] = fmaf(s.y, d[nb][3] - fmaf(zb, gs[nb].w, gs[nb].z), acc[nb][3]);
+  }
+}
+
+// One pair's weights against NB blocks of staged rows (xp: this lane's row g of block
+// 0 at the pair; blocks 8 rows apart).  FIRST: the group's first pair (C = 0).
+template <typename T, int NB, bool FIRST>
+DEVI void pair_mma(float (&d)[NB][4], uint4 w, const uint8_t* xp, uint32_t pitch8) {
+  uint32_t A0[4], B0[4], A1[4], B1[4];
+  DqOff<T>::expand(w.x, w.y, A0, B0);
+  DqOff<T>::expand(w.z, w.w, A1, B1);
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb) {
+    const uint4 xa = *reinterpret_cast<const uint4*>(xp + nb * pitch8);
+    const uint4 xb = *reinterpret_cast<const uint4*>(xp + nb * pitch8 + 64);
+    if (FIRST)
+      mma_first<T>(d[nb], A0[0], A0[1], A0[2], A0[3], xa.x, xa.y);
+    else
+      MmaOp<T>::run(d[nb], A0[0], A0[1], A0[2], A0[3], xa.x, xa.y);
+    MmaOp<T>::run(d[nb], B0[0], B0[1], B0[2], B0[3], xa.z, xa.w);
+    MmaOp<T>::run(d[nb], A1[0], A1[1], A1[2], A1[3], xb.x, xb.y);
+    MmaOp<T>::run(d[nb], B1[0], B1[1], B1[2], B1[3], xb.z, xb.w);
+  }
+}
+
+// Fixed geometry: NPW pairs from pair pb, whole groups of PPG pairs, fully unrolled.
+// gsg: per-group correction sums [group][kGPad].
+template <typename T, typename S, int NB, int NPW, int PPG>
+DEVI void gmm_fixed(const uint8_t* rec, const TileGeom& tg, int pb, int lane, const uint8_t* xsh,
+                    uint32_t pitch, const float2* gsg, float (&acc)[NB][4]) {
+  static_assert(NPW % PPG == 0, "warp ranges must hold whole groups");
   const int g = lane >> 2, t = lane & 3;
-  const int nbv = (ntok + 7) >> 3;
   const uint8_t* wp = rec + (((uint32_t)pb << 5) + lane) * 16u;
+  const uint8_t* xp = xsh + (uint32_t)g * pitch + (uint32_t)t * 16u + (uint32_t)pb * 128u;
+  const uint32_t pitch8 = pitch * 8u;
+#pragma unroll
+  for (int gi = 0; gi < NPW / PPG; ++gi) {
+    float d[NB][4];
+#pragma unroll
+    for (int k = 0; k < PPG; ++k) {
+      const int pi = gi * PPG + k;
+      const uint4 w = *reinterpret_cast<const uint4*>(wp + pi * 512);
+      if (k == 0)
+        pair_mma<T, NB, true>(d, w, xp + pi * 128, pitch8);
+      else
+        pair_mma<T, NB, false>(d, w, xp + pi * 128, pitch8);
+    }
+    const int grp = pb / PPG + gi;
+    float4 gs[NB];
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) gs[nb] = *reinterpret_cast<const float4*>(gsg + grp * kGPad + nb * 8 + 2 * t);
+    flush_nb<S, NB>(acc, d, rec, tg, grp, g, gs);
+  }
+}
+
+// Any geometry: pairs [pb, pe), groups cut where they begin and end, per-pair sums
+// gx [pair][kGPad] accumulated over the pairs of a group this warp covers.
+template <typename T, typename S, int NB>
+DEVI void gmm_pairs(const uint8_t* rec, const TileGeom& tg, int pb, int pe, int lane, const uint8_t* xsh,
+                    uint32_t pitch, const float2* gx, float (&acc)[NB][4]) {
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t pitch8 = pitch * 8u;
+  const uint8_t* xrow = xsh + (uint32_t)g * pitch + (uint32_t)t * 16u;
   int p = pb;
   while (p < pe) {
     const int grp = p >> tg.gshift;
     int pend = (grp + 1) << tg.gshift;
     if (pend > pe) pend = pe;
-    float d[kGNB][4];
-    float4 gs[kGNB];
+    float d[NB][4];
+    float4 gs[NB];
 #pragma unroll
-    for (int nb = 0; nb < kGNB; ++nb) {
-      zero4(d[nb]);
-      gs[nb] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    for (; p < pend; ++p, wp += 512) {
-      const uint4 w = *reinterpret_cast<const uint4*>(wp);
-      uint32_t A0[4], B0[4], A1[4], B1[4];
-      DqOff<T>::expand(w.x, w.y, A0, B0);
-      DqOff<T>::expand(w.z, w.w, A1, B1);
+    for (int nb = 0; nb < NB; ++nb) gs[nb] = make_float4(0.f, 0.f, 0.f, 0.f);
+    bool first = true;
+    for (; p < pend; ++p) {
+      const uint4 w = *reinterpret_cast<const uint4*>(rec + (((uint32_t)p << 5) + lane) * 16u);
+      if (first)
+        pair_mma<T, NB, true>(d, w, xrow + (uint32_t)p * 128u, pitch8);
+      else
+        pair_mma<T, NB, false>(d, w, xrow + (uint32_t)p * 128u, pitch8);
+      first = false;
 #pragma unroll
-      for (int nb = 0; nb < kGNB; ++nb) {
-        if (nb < nbv) {  // warp-uniform
-          const float4 gq = *reinterpret_cast<const float4*>(gsum + p * kGPad + nb * 8 + 2 * t);
-          gs[nb].x += gq.x;
-          gs[nb].y += gq.y;
-          gs[nb].z += gq.z;
-          gs[nb].w += gq.w;
-          uint4 xa = make_uint4(0, 0, 0, 0), xb = make_uint4(0, 0, 0, 0);
-          if (nb * 8 + g < ntok) {
-            const uint8_t* xr = xsh + (uint32_t)(nb * 8 + g) * pitch + (uint32_t)t * 16u + (uint32_t)p * 128u;
-            xa = *reinterpret_cast<const uint4*>(xr);
-            xb = *reinterpret_cast<const uint4*>(xr + 64);
-          }
-          MmaOp<T>::run(d[nb], A0[0], A0[1], A0[2], A0[3], xa.x, xa.y);
-          MmaOp<T>::run(d[nb], B0[0], B0[1], B0[2], B0[3], xa.z, xa.w);
-          MmaOp<T>::run(d[nb], A1[0], A1[1], A1[2], A1[3], xb.x, xb.y);
-          MmaOp<T>::run(d[nb], B1[0], B1[1], B1[2], B1[3], xb.z, xb.w);
-        }
+      for (int nb = 0; nb < NB; ++nb) {
+        const float4 gq = *reinterpret_cast<const float4*>(gx + p * kGPad + nb * 8 + 2 * t);
+        gs[nb].x += gq.x;
+        gs[nb].y += gq.y;
+        gs[nb].z += gq.z;
+        gs[nb].w += gq.w;
       }
     }
-    const float zero4v[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int nb = 0; nb < kGNB; ++nb)
-      if (nb < nbv) flush_group<S>(acc[nb], d[nb], zero4v, rec, tg, grp, g, gs[nb], 1.f, 1.f);
+    flush_nb<S, NB>(acc, d, rec, tg, grp, g, gs);
   }
 }
 
 // Partial sums of lane (g, t) -> red[warp][nb][q][lane]; read back per (row, token).
-DEVI void put_acc(float* red, int warp, int lane, const float (&acc)[kGNB][4]) {
+template <int NB>
+DEVI void put_acc(float* red, int warp, int lane, const float (&acc)[NB][4]) {
 #pragma unroll
-  for (int nb = 0; nb < kGNB; ++nb)
+  for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
-    for (int q = 0; q < 4; ++q) red[((warp * kGNB + nb) * 4 + q) * 32 + lane] = acc[nb][q];
+    for (int q = 0; q < 4; ++q) red[((warp * NB + nb) * 4 + q) * 32 + lane] = acc[nb][q];
 }
 
-DEVI int acc_at(int warp, int row, int tok) {
+// index of (row, token) in warp 0's partials; warp w's is this + w * NB * 128
+template <int NB>
+DEVI int acc_at0(int row, int tok) {
   const int g = row & 7, q = (row >> 3) * 2 + (tok & 1), t = (tok & 7) >> 1, nb = tok >> 3;
-  return ((warp * kGNB + nb) * 4 + q) * 32 + g * 4 + t;
+  return (nb * 4 + q) * 32 + g * 4 + t;
 }
 
-template <typename T, typename S>
-__global__ void __launch_bounds__(kThreads, 1) g_expert_kernel(const __grid_constant__ GExpParams p) {
+// Correction sums (P, Q) of 8 fragment-ordered 16-bit values (odd columns of fp16 rows
+// already scaled by 1/16): se over the even columns, so over the odd ones.
+template <typename T>
+DEVI void frag_sums(const uint4& o, float& se, float& so) {
+  const T* v = reinterpret_cast<const T*>(&o);
+  se += (to_f32<T>(v[0]) + to_f32<T>(v[1])) + (to_f32<T>(v[4]) + to_f32<T>(v[5]));
+  so += (to_f32<T>(v[2]) + to_f32<T>(v[3])) + (to_f32<T>(v[6]) + to_f32<T>(v[7]));
+}
+
+template <typename T>
+DEVI float2 corr_pq(float se, float so) {
+  const float P = DqOff<T>::kOddDiv16 ? 1024.f * (se + so) : 128.f * (se + so);
+  const float Q = DqOff<T>::kOddDiv16 ? fmaf(16.f, so, se) : se + so;
+  return make_float2(P, Q);
+}
+
+// per-group sums from the per-pair table, in pair order
+DEVI void group_sums(const float2* gx, float2* gxg, int ngroups, int ppg, int tid) {
+  for (int idx = tid; idx < ngroups * kGPad; idx += kConsumers) {
+    const int grp = idx / kGPad, tk = idx - grp * kGPad;
+    float2 s = gx[(grp * ppg) * kGPad + tk];
+    for (int k = 1; k < ppg; ++k) {
+      const float2 v = gx[(grp * ppg + k) * kGPad + tk];
+      s.x += v.x;
+      s.y += v.y;
+    }
+    gxg[idx] = s;
+  }
+}
+
+// The ring of one CTA: slot s, phase bit ph, both advanced once per stage by the
+// producer and by the consumers alike.
+struct GRing {
+  int slot = 0;
+  uint32_t ph = 0;
+  int n = 0;  // stages so far
+  DEVI void next(int ns) {
+    ++n;
+    if (++slot == ns) {
+      slot = 0;
+      ph ^= 1u;
+    }
+  }
+};
+
+// Producer: arm slot r.slot for `bytes` and issue the copy, after the consumers
+// released the slot's previous use.  Returns false (nothing issued) after an abort.
+DEVI bool g_issue(uint64_t* full, uint64_t* empty, volatile int* abort_flag, int* err, const GRing& r, int ns,
+                  uint8_t* dst, const uint8_t* src, uint32_t bytes, uint64_t pol) {
+  if (*abort_flag) return false;
+  if (r.n >= ns) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(&empty[r.slot], r.ph ^ 1u)) {
+      if (*abort_flag) return false;
+      if (clock64() - t0 > kWaitLimitCycles) {
+        *abort_flag = 1;
+        set_error(err, DUPLEX_DEVERR_TIMEOUT);
+        return false;
+      }
+    }
+  }
+  mbar_arrive_expect_tx(&full[r.slot], bytes);
+  bulk_g2s_stream(dst, src, bytes, &full[r.slot], pol);
+  return true;
+}
+
+// Producer exit: wait (bounded) for the last min(n, ns) issued copies.
+DEVI void g_drain(uint64_t* full, int n, int ns, int* err) {
+  for (int j = n > ns ? n - ns : 0; j < n; ++j) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(&full[j % ns], (uint32_t)(j / ns) & 1u))
+      if (clock64() - t0 > 200000000LL) {
+        set_error(err, DUPLEX_DEVERR_TIMEOUT);
+        break;
+      }
+  }
+}
+
+DEVI void g_range(int W, int& i0, int& i1) {
+  i0 = (int)((long long)W * blockIdx.x / gridDim.x);
+  i1 = (int)((long long)W * (blockIdx.x + 1) / gridDim.x);
+}
+
+DEVI void g_init(uint64_t* full, uint64_t* empty, volatile int* abort_flag, int ns, int consumers_per_stage) {
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ns; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], consumers_per_stage);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+}
+
+DEVI void g_unit(const GExpParams& p, int u, int& e, int& first, int& n) {
+  e = p.units[u * 3 + 0];
+  e = (e < 0 || e >= p.E) ? 0 : e;
+  first = p.units[u * 3 + 1];
+  n = p.units[u * 3 + 2];
+  n = n < 1 ? 1 : (n > kGTok ? kGTok : n);
+}
+
+// Ring position of the j-th stage of a CTA's range.
+DEVI void g_slot(int j, int ns, int& slot, uint32_t& ph) {
+  const int k = j / ns;
+  slot = j - k * ns;
+  ph = (uint32_t)k & 1u;
+}
+
+DEVI void g_wait_stage(uint64_t* full, volatile int* abort_flag, int* err, int slot, uint32_t ph) {
+  if (*abort_flag) return;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(&full[slot], ph)) {
+    if (*abort_flag) return;
+    if (clock64() - t0 > kWaitLimitCycles) {
+      *abort_flag = 1;
+      set_error(err, DUPLEX_DEVERR_TIMEOUT);
+      return;
+    }
+  }
+}
+
+// Producer of both expert kernels: stages i0 .. i1-1 of the flattened list, stage
+// `it` = (unit it / per_unit, part it % per_unit) at src(e, part), bytes(part).
+template <typename Src>
+DEVI void g_produce(const GExpParams& p, uint64_t* full, uint64_t* empty, volatile int* abort_flag,
+                    uint8_t* ring, uint32_t slot_bytes, int ns, int i0, int i1, int per_unit, Src src) {
+  const uint64_t pol = policy_evict_first();
+  GRing r;
+  for (int it = i0; it < i1; ++it) {
+    const int u = it / per_unit, part = it - u * per_unit;
+    int e, first, n;
+    g_unit(p, u, e, first, n);
+    uint32_t bytes;
+    const uint8_t* from = src(e, part, bytes);
+    if (!g_issue(full, empty, abort_flag, p.err, r, ns, ring + (uint32_t)r.slot * slot_bytes, from, bytes, pol))
+      break;
+    r.next(ns);
+  }
+  g_drain(full, r.n, ns, p.err);
+}
+
+// ---- gate|up item of one 8-warp group: warps 0-3 the gate record, 4-7 the up record,
+// 4-way K split; act[first + tk][rb*16 .. +16] = SiLU(gate) * up.  red: this group's
+// partials [8 warps][NB][4][32]; bar: the group's named barrier (256 threads).
+template <typename T, typename S, int NB, int NPW, int PPG>
+DEVI void gu_item(const GExpParams& p, const uint8_t* st, uint64_t* empty_slot, int rb, int first, int n,
+                  const uint8_t* xsh, const float2* gx, const float2* gxg, float* red, int bar) {
+  const int lane = threadIdx.x & 31, wi = (threadIdx.x >> 5) & 7, gt = threadIdx.x & 255;
+  const int rec = wi >> 2, kq = wi & 3;
+  float acc[NB][4];
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb) zero4(acc[nb]);
+  const uint8_t* rp = st + (uint32_t)rec * p.tgu.rec_bytes;
+  if constexpr (NPW > 0) {
+    gmm_fixed<T, S, NB, NPW, PPG>(rp, p.tgu, kq * NPW, lane, xsh, p.x_pitch, gxg, acc);
+  } else {
+    const int np = p.tgu.npairs;
+    gmm_pairs<T, S, NB>(rp, p.tgu, (kq * np) >> 2, ((kq + 1) * np) >> 2, lane, xsh, p.x_pitch, gx, acc);
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(empty_slot);
+  put_acc<NB>(red, wi, lane, acc);
+  named_bar_sync(bar, 256);
+  constexpr int WS = NB * 128;  // one warp's partials
+  for (int o = gt; o < 16 * n; o += 256) {
+    const int row = o & 15, tk = o >> 4;
+    const float* rr = red + acc_at0<NB>(row, tk);
+    const float gsum_ = (rr[0] + rr[WS]) + (rr[2 * WS] + rr[3 * WS]);
+    const float usum = (rr[4 * WS] + rr[5 * WS]) + (rr[6 * WS] + rr[7 * WS]);
+    const int col = rb * 16 + row;
+    T a = from_f32<T>(silu_f32(gsum_) * usum);
+    if (DqOff<T>::kOddDiv16 && (col & 1)) a = from_f32<T>(to_f32<T>(a) * 0.0625f);
+    reinterpret_cast<T*>(p.act + (size_t)(first + tk) * p.I * 2)[frag_pos(col)] = a;
+  }
+  named_bar_sync(bar, 256);
+}
+
+// Unit segments of a CTA's range: [it, seg_end) all belong to unit it / per_unit.
+DEVI int g_seg_end(int it, int i1, int per_unit) {
+  const int e = (it / per_unit + 1) * per_unit;
+  return e < i1 ? e : i1;
+}
+
+template <typename T, typename S, int NPW, int PPG>
+__global__ void __launch_bounds__(kThreads, 1) g_gateup_kernel(const __grid_constant__ GExpParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kGFull);
   uint64_t* empty = reinterpret_cast<uint64_t*>(smem + kGEmpty);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kGAbort);
   int* tok = reinterpret_cast<int*>(smem + kGTokS);
-  int* slot = reinterpret_cast<int*>(smem + kGSlotS);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int u = blockIdx.x;
-  if (u >= *p.n_units) return;  // the whole CTA: units are fewer than the grid bound
-  const int e = p.units[u * 3 + 0], first = p.units[u * 3 + 1];
-  int n = p.units[u * 3 + 2];
-  n = n < 0 ? 0 : (n > kGTok ? kGTok : n);
-  const int perG = p.I >> 4;                // gate|up record pairs
-  const int RbD = p.H >> 4;                 // down records
-  const int nDN = (RbD + 3) >> 2;           // down stages of up to 4 records
-  if (tid == 0) {
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kCW);
-    }
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (tid < n) {
-    const int a = p.assign[first + tid];
-    tok[tid] = a >> 3;
-    slot[tid] = a & 7;
-  }
-  __syncthreads();
+  const int perG = p.I >> 4, ns = p.ns_a;
+  int nu = *p.n_units;
+  nu = nu < 0 ? 0 : (nu > p.max_units ? p.max_units : nu);
+  int i0, i1;
+  g_range(nu * perG, i0, i1);
+  g_init(full, empty, abort_flag, ns, kCW / 2);
+  uint8_t* ring = smem + p.off_ring_a;
 
   if (warp == kCW) {
-    // ============================================================ producer
-    // One thread.  After an abort nothing more is issued (a slot whose empty phase
-    // did not complete is never re-armed); the copies already issued are drained.
     if (lane != 0) return;
-    const uint64_t pol = policy_evict_first();
-    int i = 0;
-    auto issue = [&](const uint8_t* src, uint32_t bytes) {
-      if (*abort_flag) return;
-      if (i >= 2) {
-        const long long t0 = clock64();
-        while (!mbar_try_wait(&empty[i & 1], (uint32_t)((i >> 1) - 1) & 1u)) {
-          if (*abort_flag) return;
-          if (clock64() - t0 > kWaitLimitCycles) {
-            *abort_flag = 1;
-            set_error(p.err, DUPLEX_DEVERR_TIMEOUT);
-            return;
-          }
-        }
-      }
-      mbar_arrive_expect_tx(&full[i & 1], bytes);
-      bulk_g2s_stream(smem + p.off_ring + (uint32_t)(i & 1) * p.slot_bytes, src, bytes, &full[i & 1], pol);
-      ++i;
-    };
-    for (int rb = 0; rb < perG; ++rb)
-      issue(p.gu_tiles + ((size_t)e * 2 * perG + 2 * rb) * p.tgu.rec_bytes, 2u * p.tgu.rec_bytes);
-    for (int s = 0; s < nDN; ++s) {
-      const int cnt = RbD - 4 * s < 4 ? RbD - 4 * s : 4;
-      issue(p.dn_tiles + ((size_t)e * RbD + 4 * s) * p.tdn.rec_bytes, (uint32_t)cnt * p.tdn.rec_bytes);
-    }
-    // drain: never leave while a copy may still target shared memory
-    for (int j = i > 2 ? i - 2 : 0; j < i; ++j) {
-      const long long t0 = clock64();
-      while (!mbar_try_wait(&full[j & 1], (uint32_t)(j >> 1) & 1u))
-        if (clock64() - t0 > 200000000LL) {
-          set_error(p.err, DUPLEX_DEVERR_TIMEOUT);
-          break;
-        }
-    }
+    g_produce(p, full, empty, abort_flag, ring, p.slot_a, ns, i0, i1, perG,
+              [&](int e, int rb, uint32_t& bytes) {
+                bytes = 2u * p.tgu.rec_bytes;
+                return p.gu_tiles + ((size_t)e * 2 * perG + 2 * rb) * p.tgu.rec_bytes;
+              });
     return;
   }
 
-  // ============================================================== consumers
   uint8_t* xsh = smem + p.off_x;
   float2* gx = reinterpret_cast<float2*>(smem + p.off_gx);
-  uint8_t* act = smem + p.off_a;
-  float2* ga = reinterpret_cast<float2*>(smem + p.off_ga);
-  float* red = reinterpret_cast<float*>(smem + p.off_red);
-  uint8_t* ring = smem + p.off_ring;
-  const int H = p.H, I = p.I;
-  int i = 0;
-  auto wait_full = [&](int j) {
-    if (*abort_flag) return;
-    const long long t0 = clock64();
-    while (!mbar_try_wait(&full[j & 1], (uint32_t)(j >> 1) & 1u)) {
-      if (*abort_flag) return;
-      if (clock64() - t0 > kWaitLimitCycles) {
-        *abort_flag = 1;
-        set_error(p.err, DUPLEX_DEVERR_TIMEOUT);
-        return;
-      }
-    }
-  };
-  auto release = [&](int j) {
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[j & 1]);
-  };
-
-  // ---- the unit's token rows: fragment order (fp16: odd columns / 16), and the
-  // per-pair correction sums (zero for absent tokens)
-  {
+  float2* gxg = reinterpret_cast<float2*>(smem + p.off_gxg);
+  const int grp = warp >> 3;
+  float* red = reinterpret_cast<float*>(smem + p.off_red_a) + grp * (kGRedBytes / 8);
+  const int H = p.H, np = p.tgu.npairs;
+  for (int s0 = i0; s0 < i1;) {
+    const int s1 = g_seg_end(s0, i1, perG);
+    // ---- the unit's token rows in fragment order (fp16: odd columns / 16) and their
+    // correction sums per pair and per group (zero for absent tokens)
+    int e, first, n;
+    g_unit(p, s0 / perG, e, first, n);
+    named_bar_sync(1, kConsumers);  // both groups are done with the previous unit
+    if (tid < n) tok[tid] = p.assign[first + tid] >> 3;
+    named_bar_sync(1, kConsumers);
     const int nq = H >> 3, total = n * nq;
-    for (int base = 0; base < total + (kConsumers - 1) && base < total; base += kConsumers) {
+    for (int base = 0; base < total; base += kConsumers) {
       const int idx = base + tid;
       float se = 0.f, so = 0.f;
-      int r = 0, q = 0;
+      int rr = 0, q = 0;
       if (idx < total) {
-        r = idx / nq;
-        q = idx - r * nq;
-        uint4 o = __ldg(reinterpret_cast<const uint4*>(p.x + (size_t)tok[r] * H * 2) + q);
+        rr = idx / nq;
+        q = idx - rr * nq;
+        uint4 o = __ldg(reinterpret_cast<const uint4*>(p.x + (size_t)tok[rr] * H * 2) + q);
         o = to_frag_order(o);
         if (DqOff<T>::kOddDiv16) {
           const __half2 q16 = __float2half2_rn(0.0625f);
@@ -443,109 +641,153 @@ __global__ void __launch_bounds__(kThreads, 1) g_expert_kernel(const __grid_cons
           o.y = *reinterpret_cast<uint32_t*>(&hy);
           o.w = *reinterpret_cast<uint32_t*>(&hw);
         }
-        *reinterpret_cast<uint4*>(xsh + (uint32_t)r * p.x_pitch + (uint32_t)q * 16u) = o;
-        const T* v = reinterpret_cast<const T*>(&o);
-        se = (to_f32<T>(v[0]) + to_f32<T>(v[1])) + (to_f32<T>(v[4]) + to_f32<T>(v[5]));
-        so = (to_f32<T>(v[2]) + to_f32<T>(v[3])) + (to_f32<T>(v[6]) + to_f32<T>(v[7]));
+        *reinterpret_cast<uint4*>(xsh + (uint32_t)rr * p.x_pitch + (uint32_t)q * 16u) = o;
+        frag_sums<T>(o, se, so);
       }
 #pragma unroll
       for (int o = 1; o < 8; o <<= 1) {
         se += __shfl_xor_sync(0xffffffffu, se, o);
         so += __shfl_xor_sync(0xffffffffu, so, o);
       }
-      if (idx < total && (q & 7) == 0) {
-        const float P = DqOff<T>::kOddDiv16 ? 1024.f * (se + so) : 128.f * (se + so);
-        const float Q = DqOff<T>::kOddDiv16 ? fmaf(16.f, so, se) : se + so;
-        gx[(q >> 3) * kGPad + r] = make_float2(P, Q);
-      }
+      if (idx < total && (q & 7) == 0) gx[(q >> 3) * kGPad + rr] = corr_pq<T>(se, so);
     }
-    const int np = p.tgu.npairs;
     for (int idx = tid; idx < np * kGPad; idx += kConsumers)
       if (idx % kGPad >= n) gx[idx] = make_float2(0.f, 0.f);
-  }
-  named_bar_sync(1, kConsumers);
-
-  // ---- gate|up: warps 0-7 the gate record, 8-15 the up record, 8-way K split
-  {
-    const int rec = warp >> 3, kw = warp & 7, np = p.tgu.npairs;
-    for (int rb = 0; rb < perG; ++rb, ++i) {
-      wait_full(i);
-      const uint8_t* st = ring + (uint32_t)(i & 1) * p.slot_bytes + (uint32_t)rec * p.tgu.rec_bytes;
-      float acc[kGNB][4];
-#pragma unroll
-      for (int nb = 0; nb < kGNB; ++nb) zero4(acc[nb]);
-      gmm_pairs<T, S>(st, p.tgu, (kw * np) >> 3, ((kw + 1) * np) >> 3, lane, xsh, p.x_pitch, gx, n,
-                      acc);
-      release(i);
-      put_acc(red, warp, lane, acc);
-      named_bar_sync(1, kConsumers);
-      for (int o = tid; o < 16 * n; o += kConsumers) {
-        const int row = o & 15, tk = o >> 4;
-        float gsum_ = 0.f, usum = 0.f;
-#pragma unroll
-        for (int w = 0; w < 8; ++w) {
-          gsum_ += red[acc_at(w, row, tk)];
-          usum += red[acc_at(8 + w, row, tk)];
-        }
-        const int col = rb * 16 + row;
-        T a = from_f32<T>(silu_f32(gsum_) * usum);
-        if (DqOff<T>::kOddDiv16 && (col & 1)) a = from_f32<T>(to_f32<T>(a) * 0.0625f);
-        reinterpret_cast<T*>(act + (uint32_t)tk * p.a_pitch)[frag_pos(col)] = a;
-      }
-      named_bar_sync(1, kConsumers);
+    named_bar_sync(1, kConsumers);
+    group_sums(gx, gxg, np >> p.tgu.gshift, 1 << p.tgu.gshift, tid);
+    named_bar_sync(1, kConsumers);
+    // ---- the segment's items, alternately to the two groups
+    const int nbv = (n + 7) >> 3;
+    for (int it = s0 + grp; it < s1; it += 2) {
+      int slot;
+      uint32_t ph;
+      g_slot(it - i0, ns, slot, ph);
+      g_wait_stage(full, abort_flag, p.err, slot, ph);
+      const uint8_t* st = ring + (uint32_t)slot * p.slot_a;
+      const int rb = it - (it / perG) * perG;
+      if (nbv == 1)
+        gu_item<T, S, 1, NPW, PPG>(p, st, &empty[slot], rb, first, n, xsh, gx, gxg, red, 2 + grp);
+      else if (nbv == 2)
+        gu_item<T, S, 2, NPW, PPG>(p, st, &empty[slot], rb, first, n, xsh, gx, gxg, red, 2 + grp);
+      else
+        gu_item<T, S, 3, NPW, PPG>(p, st, &empty[slot], rb, first, n, xsh, gx, gxg, red, 2 + grp);
     }
+    s0 = s1;
+  }
+}
+
+// ---- down item: one warp, one record (16 rows of H) over the whole K; the outputs
+// go from the accumulators straight to ypart[tok][slot][row] for the live tokens.
+template <typename T, typename S, int NB, int NPW, int PPG>
+DEVI void dn_item(const GExpParams& p, const uint8_t* rp, uint64_t* empty_slot, int row0, int n,
+                  const int* tok, const int* slt, const uint8_t* act, const float2* ga, const float2* gag) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  float acc[NB][4];
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb) zero4(acc[nb]);
+  if (rp) {
+    if constexpr (NPW > 0)
+      gmm_fixed<T, S, NB, NPW, PPG>(rp, p.tdn, 0, lane, act, p.a_pitch, gag, acc);
+    else
+      gmm_pairs<T, S, NB>(rp, p.tdn, 0, p.tdn.npairs, lane, act, p.a_pitch, ga, acc);
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(empty_slot);
+  if (!rp) return;
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int tk = nb * 8 + 2 * t + (q & 1), row = row0 + g + (q >> 1) * 8;
+      if (tk < n) p.ypart[((size_t)tok[tk] * p.top_k + slt[tk]) * p.H + row] = acc[nb][q];
+    }
+}
+
+template <typename T, typename S, int NPW, int PPG>
+__global__ void __launch_bounds__(kThreads, 1) g_down_kernel(const __grid_constant__ GExpParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kGFull);
+  uint64_t* empty = reinterpret_cast<uint64_t*>(smem + kGEmpty);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kGAbort);
+  int* tok = reinterpret_cast<int*>(smem + kGTokS);
+  int* slt = reinterpret_cast<int*>(smem + kGSlotS);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int RbD = p.H >> 4, nDN = (RbD + kGDnRec - 1) / kGDnRec, ns = p.ns_d;
+  int nu = *p.n_units;
+  nu = nu < 0 ? 0 : (nu > p.max_units ? p.max_units : nu);
+  int i0, i1;
+  g_range(nu * nDN, i0, i1);
+  g_init(full, empty, abort_flag, ns, kCW / 2);
+  uint8_t* ring = smem + p.off_ring_d;
+
+  if (warp == kCW) {
+    if (lane != 0) return;
+    g_produce(p, full, empty, abort_flag, ring, p.slot_d, ns, i0, i1, nDN,
+              [&](int e, int s, uint32_t& bytes) {
+                const int cnt = RbD - kGDnRec * s < kGDnRec ? RbD - kGDnRec * s : kGDnRec;
+                bytes = (uint32_t)cnt * p.tdn.rec_bytes;
+                return p.dn_tiles + ((size_t)e * RbD + kGDnRec * s) * p.tdn.rec_bytes;
+              });
+    return;
   }
 
-  // ---- correction sums of the intermediate
-  {
-    const int np = p.tdn.npairs;
+  uint8_t* act = smem + p.off_a;
+  float2* ga = reinterpret_cast<float2*>(smem + p.off_ga);
+  float2* gag = reinterpret_cast<float2*>(smem + p.off_gag);
+  const int I = p.I, np = p.tdn.npairs;
+  const int grp = warp >> 3, rc = warp & 7;
+  for (int s0 = i0; s0 < i1;) {
+    const int s1 = g_seg_end(s0, i1, nDN);
+    // ---- the unit's intermediate rows (already in fragment order) and their
+    // correction sums per pair and per group
+    int e, first, n;
+    g_unit(p, s0 / nDN, e, first, n);
+    named_bar_sync(1, kConsumers);
+    if (tid < n) {
+      const int a = p.assign[first + tid];
+      tok[tid] = a >> 3;
+      slt[tid] = a & 7;
+    }
+    const int nq = I >> 3;
+    for (int idx = tid; idx < n * nq; idx += kConsumers) {
+      const int rr = idx / nq, q = idx - rr * nq;
+      *reinterpret_cast<uint4*>(act + (uint32_t)rr * p.a_pitch + (uint32_t)q * 16u) =
+          __ldcg(reinterpret_cast<const uint4*>(p.act + (size_t)(first + rr) * I * 2) + q);
+    }
+    named_bar_sync(1, kConsumers);
     for (int idx = tid; idx < np * kGPad; idx += kConsumers) {
       const int pp = idx / kGPad, tk = idx - pp * kGPad;
       float se = 0.f, so = 0.f;
       if (tk < n) {
         const uint8_t* rowp = act + (uint32_t)tk * p.a_pitch + (uint32_t)pp * 128u;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint4 o = *reinterpret_cast<const uint4*>(rowp + c * 16);
-          const T* v = reinterpret_cast<const T*>(&o);
-          se += (to_f32<T>(v[0]) + to_f32<T>(v[1])) + (to_f32<T>(v[4]) + to_f32<T>(v[5]));
-          so += (to_f32<T>(v[2]) + to_f32<T>(v[3])) + (to_f32<T>(v[6]) + to_f32<T>(v[7]));
-        }
+        for (int c = 0; c < 8; ++c) frag_sums<T>(*reinterpret_cast<const uint4*>(rowp + c * 16), se, so);
       }
-      const float P = DqOff<T>::kOddDiv16 ? 1024.f * (se + so) : 128.f * (se + so);
-      const float Q = DqOff<T>::kOddDiv16 ? fmaf(16.f, so, se) : se + so;
-      ga[idx] = make_float2(P, Q);
+      ga[idx] = corr_pq<T>(se, so);
     }
-  }
-  named_bar_sync(1, kConsumers);
-
-  // ---- down: 4 records per stage, 4 warps per record (K split)
-  {
-    const int q4 = warp >> 2, kp = warp & 3, np = p.tdn.npairs;
-    for (int s = 0; s < nDN; ++s, ++i) {
-      wait_full(i);
-      const int cnt = RbD - 4 * s < 4 ? RbD - 4 * s : 4;
-      float acc[kGNB][4];
-#pragma unroll
-      for (int nb = 0; nb < kGNB; ++nb) zero4(acc[nb]);
-      if (q4 < cnt)
-        gmm_pairs<T, S>(ring + (uint32_t)(i & 1) * p.slot_bytes + (uint32_t)q4 * p.tdn.rec_bytes, p.tdn,
-                        (kp * np) >> 2, ((kp + 1) * np) >> 2, lane, act, p.a_pitch, ga, n, acc);
-      release(i);
-      put_acc(red, warp, lane, acc);
-      named_bar_sync(1, kConsumers);
-      for (int o = tid; o < cnt * 16 * n; o += kConsumers) {
-        const int rq = o / n, tk = o - rq * n;  // rq = record * 16 + row
-        const int rc = rq >> 4, row = rq & 15;
-        float y = 0.f;
-#pragma unroll
-        for (int w = 0; w < 4; ++w) y += red[acc_at(rc * 4 + w, row, tk)];
-        p.ypart[((size_t)tok[tk] * p.top_k + slot[tk]) * H + (4 * s + rc) * 16 + row] = y;
-      }
-      named_bar_sync(1, kConsumers);
+    named_bar_sync(1, kConsumers);
+    group_sums(ga, gag, np >> p.tdn.gshift, 1 << p.tdn.gshift, tid);
+    named_bar_sync(1, kConsumers);
+    // ---- the segment's stages, alternately to the two groups, one record per warp
+    const int nbv = (n + 7) >> 3;
+    for (int it = s0 + grp; it < s1; it += 2) {
+      int slot;
+      uint32_t ph;
+      g_slot(it - i0, ns, slot, ph);
+      g_wait_stage(full, abort_flag, p.err, slot, ph);
+      const int s = it - (it / nDN) * nDN;
+      const int cnt = RbD - kGDnRec * s < kGDnRec ? RbD - kGDnRec * s : kGDnRec;
+      const uint8_t* rp = rc < cnt ? ring + (uint32_t)slot * p.slot_d + (uint32_t)rc * p.tdn.rec_bytes : nullptr;
+      const int row0 = (kGDnRec * s + rc) * 16;
+      if (nbv == 1)
+        dn_item<T, S, 1, NPW, PPG>(p, rp, &empty[slot], row0, n, tok, slt, act, ga, gag);
+      else if (nbv == 2)
+        dn_item<T, S, 2, NPW, PPG>(p, rp, &empty[slot], row0, n, tok, slt, act, ga, gag);
+      else
+        dn_item<T, S, 3, NPW, PPG>(p, rp, &empty[slot], row0, n, tok, slt, act, ga, gag);
     }
+    s0 = s1;
   }
-  (void)I;
 }
 
 // ------------------------------------------------------------------ 5. combine
@@ -563,11 +805,11 @@ __global__ void __launch_bounds__(256) g_combine_kernel(const float* ypart, cons
 
 // ====================================================================== host side
 struct GScratch {
-  size_t logits, sel, w, assign, units, n_units, ypart, total;
+  size_t logits, sel, w, assign, units, n_units, act, ypart, total;
   int max_units;
 };
 
-static GScratch g_scratch(int T, int E, int H, int top_k) {
+static GScratch g_scratch(int T, int E, int H, int I, int top_k) {
   GScratch s;
   size_t off = 0;
   s.max_units = E + (T * top_k + kGTok - 1) / kGTok + 1;
@@ -577,30 +819,72 @@ static GScratch g_scratch(int T, int E, int H, int top_k) {
   s.assign = off; off += align_up((size_t)T * top_k * 4, 256);
   s.units = off; off += align_up((size_t)s.max_units * 12, 256);
   s.n_units = off; off += 256;
+  s.act = off; off += align_up((size_t)T * top_k * I * 2, 256);
   s.ypart = off; off += align_up((size_t)T * top_k * H * 4, 256);
   s.total = off;
   return s;
 }
 
-// Shared-memory map of the expert kernel for one geometry; false when it does not fit.
-static bool g_layout(int H, int I, int group, int has_zeros, GExpParams* p, size_t* smem) {
+// Shared-memory maps of the two expert kernels for one geometry (the ring takes what
+// is left, up to kGMaxSlots slots, at least 2); false when a map does not fit.  The
+// staged rows are sized for kGTok tokens; MMA blocks read up to kGPad rows, which
+// stay inside the map because the tables, partials and ring follow them.
+static bool g_layout(int H, int I, int group, int has_zeros, GExpParams* p) {
   if ((H & 63) || (I & 63) || group < 64 || (group & (group - 1))) return false;
   if (32 * (H * 2 + 16) + 8 * 256 * 4 > kGSmemMax) return false;  // router tile
   if (tile_geom(H, group, has_zeros, &p->tgu) || tile_geom(I, group, has_zeros, &p->tdn)) return false;
   auto up = [](uint32_t v, uint32_t a) { return (v + a - 1) / a * a; };
   p->x_pitch = up((uint32_t)H * 2u, 128) + 64u;
   p->a_pitch = up((uint32_t)I * 2u, 128) + 64u;
-  uint32_t slot = 2u * p->tgu.rec_bytes;
-  if (slot < 4u * p->tdn.rec_bytes) slot = 4u * p->tdn.rec_bytes;
-  p->slot_bytes = up(slot, 128);
+  const uint32_t ppg = 1u << p->tgu.gshift;
+  // gate|up
+  p->slot_a = up(2u * p->tgu.rec_bytes, 128);
   p->off_x = kGFixedEnd;
   p->off_gx = up(p->off_x + kGTok * p->x_pitch, 128);
-  p->off_a = up(p->off_gx + (uint32_t)p->tgu.npairs * kGPad * 8u, 128);
+  p->off_gxg = up(p->off_gx + (uint32_t)p->tgu.npairs * kGPad * 8u, 128);
+  p->off_red_a = up(p->off_gxg + (uint32_t)p->tgu.npairs / ppg * kGPad * 8u, 128);
+  p->off_ring_a = up(p->off_red_a + kGRedBytes, 128);
+  if (p->off_ring_a + 2 * p->slot_a > (uint32_t)kGSmemMax) return false;
+  p->ns_a = (int)((kGSmemMax - p->off_ring_a) / p->slot_a);
+  if (p->ns_a > kGMaxSlots) p->ns_a = kGMaxSlots;
+  p->smem_a = p->off_ring_a + (uint32_t)p->ns_a * p->slot_a;
+  if (p->off_x + kGPad * p->x_pitch > p->smem_a) return false;
+  // down
+  p->slot_d = up((uint32_t)kGDnRec * p->tdn.rec_bytes, 128);
+  p->off_a = kGFixedEnd;
   p->off_ga = up(p->off_a + kGTok * p->a_pitch, 128);
-  p->off_red = up(p->off_ga + (uint32_t)p->tdn.npairs * kGPad * 8u, 128);
-  p->off_ring = up(p->off_red + kCW * kGNB * 4 * 32 * 4, 128);
-  *smem = p->off_ring + 2 * (size_t)p->slot_bytes;
-  return *smem <= (size_t)kGSmemMax;
+  p->off_gag = up(p->off_ga + (uint32_t)p->tdn.npairs * kGPad * 8u, 128);
+  p->off_ring_d = up(p->off_gag + (uint32_t)p->tdn.npairs / ppg * kGPad * 8u, 128);
+  if (p->off_ring_d + 2 * p->slot_d > (uint32_t)kGSmemMax) return false;
+  p->ns_d = (int)((kGSmemMax - p->off_ring_d) / p->slot_d);
+  if (p->ns_d > kGMaxSlots) p->ns_d = kGMaxSlots;
+  p->smem_d = p->off_ring_d + (uint32_t)p->ns_d * p->slot_d;
+  if (p->off_a + kGPad * p->a_pitch > p->smem_d) return false;
+  return true;
+}
+
+// Kernel instances: the fixed-geometry loop where a warp's pair range holds whole
+// groups (gate|up: a quarter of a record's K, down: a whole record), else the general one.
+template <typename T, typename S>
+static void (*g_gateup_fn(const TileGeom& tg))(GExpParams) {
+  const int ppg = 1 << tg.gshift;
+  if (tg.npairs == 32) {  // K = 2048
+    if (ppg == 1) return g_gateup_kernel<T, S, 8, 1>;
+    if (ppg == 2) return g_gateup_kernel<T, S, 8, 2>;
+    if (ppg == 4) return g_gateup_kernel<T, S, 8, 4>;
+  }
+  return g_gateup_kernel<T, S, 0, 1>;
+}
+
+template <typename T, typename S>
+static void (*g_down_fn(const TileGeom& tg))(GExpParams) {
+  const int ppg = 1 << tg.gshift;
+  if (tg.npairs == 12) {  // K = 768
+    if (ppg == 1) return g_down_kernel<T, S, 12, 1>;
+    if (ppg == 2) return g_down_kernel<T, S, 12, 2>;
+    if (ppg == 4) return g_down_kernel<T, S, 12, 4>;
+  }
+  return g_down_kernel<T, S, 0, 1>;
 }
 
 }  // namespace duplex
@@ -614,9 +898,8 @@ extern "C" int duplex_moe_grouped_workspace_bytes(int32_t T, int32_t E, int32_t 
       top_k > kMaxTopK || top_k > E || H < 1 || I < 1)
     return DUPLEX_ERR_ARG;
   GExpParams p = {};
-  size_t smem = 0;
-  if (!g_layout(H, I, group, has_zeros, &p, &smem)) return DUPLEX_ERR_UNSUPPORTED;
-  *bytes = g_scratch(T, E, H, top_k).total;
+  if (!g_layout(H, I, group, has_zeros, &p)) return DUPLEX_ERR_UNSUPPORTED;
+  *bytes = g_scratch(T, E, H, I, top_k).total;
   return DUPLEX_OK;
 }
 
@@ -633,9 +916,8 @@ extern "C" int duplex_moe_grouped(const void* x, int act_dtype, int32_t T, const
   if (act_dtype != DUPLEX_DTYPE_F16 && act_dtype != DUPLEX_DTYPE_BF16) return DUPLEX_ERR_DTYPE;
   if (scale_dtype != act_dtype) return DUPLEX_ERR_DTYPE;
   GExpParams p = {};
-  size_t smem = 0;
-  if (!g_layout(H, I, group, has_zeros, &p, &smem)) return DUPLEX_ERR_UNSUPPORTED;
-  const GScratch L = g_scratch(T, E, H, top_k);
+  if (!g_layout(H, I, group, has_zeros, &p)) return DUPLEX_ERR_UNSUPPORTED;
+  const GScratch L = g_scratch(T, E, H, I, top_k);
   if (workspace_bytes < L.total) return DUPLEX_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) |
        reinterpret_cast<uintptr_t>(workspace) | reinterpret_cast<uintptr_t>(gu_tiles) |
@@ -687,20 +969,30 @@ extern "C" int duplex_moe_grouped(const void* x, int act_dtype, int32_t T, const
                                           reinterpret_cast<int*>(ws + L.n_units), L.max_units, err);
     if ((rc = record_cuda(cudaGetLastError()))) return rc;
   }
-  // 4. experts
-  p.H = H; p.I = I; p.E = E; p.top_k = top_k;
+  // 4. experts: gate|up, then down, each one CTA per SM
+  p.H = H; p.I = I; p.E = E; p.top_k = top_k; p.max_units = L.max_units;
   p.x = reinterpret_cast<const uint8_t*>(x);
   p.gu_tiles = reinterpret_cast<const uint8_t*>(gu_tiles);
   p.dn_tiles = reinterpret_cast<const uint8_t*>(dn_tiles);
   p.assign = reinterpret_cast<const int*>(ws + L.assign);
   p.units = reinterpret_cast<const int*>(ws + L.units);
   p.n_units = reinterpret_cast<const int*>(ws + L.n_units);
+  p.act = ws + L.act;
   p.ypart = reinterpret_cast<float*>(ws + L.ypart);
   p.err = err;
-  void (*ek)(GExpParams) = f16 ? g_expert_kernel<__half, __half> : g_expert_kernel<__nv_bfloat16, __nv_bfloat16>;
-  if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(ek), kGSmemMax))) return rc;
-  ek<<<L.max_units, kThreads, smem, st>>>(p);
-  if ((rc = record_cuda(cudaGetLastError()))) return rc;
+  {
+    void (*ka)(GExpParams) = f16 ? g_gateup_fn<__half, __half>(p.tgu)
+                                 : g_gateup_fn<__nv_bfloat16, __nv_bfloat16>(p.tgu);
+    void (*kd)(GExpParams) = f16 ? g_down_fn<__half, __half>(p.tdn)
+                                 : g_down_fn<__nv_bfloat16, __nv_bfloat16>(p.tdn);
+    if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(ka), kGSmemMax))) return rc;
+    if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(kd), kGSmemMax))) return rc;
+    const int G = num_sms();
+    ka<<<G, kThreads, p.smem_a, st>>>(p);
+    if ((rc = record_cuda(cudaGetLastError()))) return rc;
+    kd<<<G, kThreads, p.smem_d, st>>>(p);
+    if ((rc = record_cuda(cudaGetLastError()))) return rc;
+  }
   // 5. combine
   const size_t n_out = (size_t)T * H;
   const unsigned blocks = (unsigned)((n_out + 255) / 256);

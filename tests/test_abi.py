@@ -94,8 +94,9 @@ def test_grouped_moe_rejects_before_any_launch(lib):
     assert wsb(E=257) == 1 and wsb(k=9) == 1
     assert wsb(group=32) == 6                      # groups below 64 columns
     assert wsb(group=96) == 6
-    assert wsb(H=4096) == 6                        # one unit's working set > 227 KB of smem
+    assert wsb(H=4096) == 6                        # one unit's token rows + 2 slots > 227 KB
     assert wsb(I=1536) == 6
+    assert wsb(I=1024) == 0
     p = ctypes.c_void_p(1 << 20)
     big = 1 << 30
 
