@@ -4,7 +4,8 @@
 //   2. top-k per token (one warp per token, warp max-reductions over order keys),
 //      fp32 softmax, renormalised weights;
 //   3. a stable counting sort of the T*k (token, slot) assignments by expert and
-//      the unit list: each expert's tokens split into units of <= kGTok;
+//      the unit list: each expert's tokens split into units of <= tcap (8, 16 or 20,
+//      from the expected tokens per expert);
 //   4. the expert kernel: one CTA per unit streams its expert's gate|up and down
 //      tile records exactly once (one bulk copy per stage, a 2-slot ring), keeps
 //      the unit's tokens and the SiLU(gate)*up intermediate in shared memory, and
@@ -27,35 +28,56 @@ int record_cuda(cudaError_t e);
 int num_sms();
 int ensure_smem_attr(const void* fn, int bytes);
 
-constexpr int kGTok = 20;    // tokens of one expert unit
+constexpr int kGTok = 20;    // tokens of one expert unit at most (the per-call cap tcap <= kGTok)
 constexpr int kGNB = 3;      // 8-token MMA column blocks at most (kGNB * 8 >= kGTok)
 constexpr int kGPad = 24;    // token slots per pair in the correction sums
 constexpr int kGMaxT = 512;  // tokens per call
-constexpr int kGSmemMax = 227 * 1024;
+constexpr int kGSmemMax = 227 * 1024;  // dynamic shared memory of every kernel here (no static)
+// router CTA: 32 operand rows, the partials of 8 warps, its barrier
+constexpr int g_router_smem(int H) { return 32 * (H * 2 + 16) + 8 * 256 * 4 + 16; }
 
 // ------------------------------------------------------------------ 1. router
 // logits[t][e] = round_T(x[t] . gate_w[e] (+ b[e])): a CTA takes 16 experts x 16
-// tokens, its 8 warps split K into k16 steps (ldmatrix + mma.sync, fp32).
+// tokens; its 32 operand rows arrive by bulk copies (one thread issues them, rows past
+// E or T are zero-filled), then 8 warps split K into k16 steps (ldmatrix + mma.sync,
+// fp32) and the partials are added in warp order.
 template <typename T>
 __global__ void __launch_bounds__(256) g_router_kernel(const T* x, const T* gw, const T* gb, int nT,
-                                                       int E, int H, float* logits) {
+                                                       int E, int H, float* logits, int* err) {
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t pitch = (uint32_t)H * 2u + 16u;  // 16-byte skew: conflict-free ldmatrix
   uint8_t* ws = smem;
   uint8_t* xs = smem + 16 * pitch;
   float* red = reinterpret_cast<float*>(smem + 32 * pitch);  // [8 warps][16][16]
+  uint64_t& bar = *reinterpret_cast<uint64_t*>(smem + 32 * pitch + 8 * 256 * 4);
   const int e0 = blockIdx.x * 16, t0 = blockIdx.y * 16;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ne = E - e0 < 16 ? E - e0 : 16, nt = nT - t0 < 16 ? nT - t0 : 16;
+  const uint32_t row_bytes = (uint32_t)H * 2u;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bar, (uint32_t)(ne + nt) * row_bytes);
+    for (int r = 0; r < ne; ++r) bulk_g2s(ws + r * pitch, gw + (size_t)(e0 + r) * H, row_bytes, &bar);
+    for (int r = 0; r < nt; ++r) bulk_g2s(xs + r * pitch, x + (size_t)(t0 + r) * H, row_bytes, &bar);
+  }
   const int nq = H >> 3;
   for (int idx = tid; idx < 32 * nq; idx += 256) {
     const int r = idx / nq, q = idx - r * nq;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < 16) {
-      if (e0 + r < E) v = __ldg(reinterpret_cast<const uint4*>(gw + (size_t)(e0 + r) * H) + q);
-    } else if (t0 + r - 16 < nT) {
-      v = __ldg(reinterpret_cast<const uint4*>(x + (size_t)(t0 + r - 16) * H) + q);
+    if ((r < 16 && r >= ne) || (r >= 16 && r - 16 >= nt))
+      *reinterpret_cast<uint4*>(smem + r * pitch + q * 16) = make_uint4(0, 0, 0, 0);
+  }
+  {
+    const long long start = clock64();
+    while (!mbar_try_wait(&bar, 0)) {
+      if (clock64() - start > kWaitLimitCycles) {
+        set_error(err, DUPLEX_DEVERR_TIMEOUT);
+        break;
+      }
     }
-    *reinterpret_cast<uint4*>(smem + r * pitch + q * 16) = v;
   }
   __syncthreads();
   float acc[2][4];
@@ -79,12 +101,12 @@ __global__ void __launch_bounds__(256) g_router_kernel(const T* x, const T* gw, 
       red[warp * 256 + (g + (q >> 1) * 8) * 16 + nb * 8 + 2 * t + (q & 1)] = acc[nb][q];
   __syncthreads();
   const int el = tid >> 4, tl = tid & 15;
-  float s = 0.f;
+  float sum = 0.f;
 #pragma unroll
-  for (int w = 0; w < 8; ++w) s += red[w * 256 + tid];
-  if (e0 + el < E && t0 + tl < nT) {
-    if (gb) s += to_f32<T>(gb[e0 + el]);
-    logits[(size_t)(t0 + tl) * E + e0 + el] = to_f32<T>(from_f32<T>(s));
+  for (int w = 0; w < 8; ++w) sum += red[w * 256 + tid];
+  if (el < ne && tl < nt) {
+    if (gb) sum += to_f32<T>(gb[e0 + el]);
+    logits[(size_t)(t0 + tl) * E + e0 + el] = to_f32<T>(from_f32<T>(sum));
   }
 }
 
@@ -155,11 +177,11 @@ __global__ void __launch_bounds__(512) g_topk_kernel(const float* logits, int nT
 // ------------------------------------------------------------------ 3. bucketing
 // Stable counting sort of the T*k assignments by expert (within an expert: token,
 // then slot) into assign[] = token << 3 | slot, and the unit list: an expert's n
-// assignments split into ceil(n / kGTok) units of near-equal size, units[u] =
+// assignments split into ceil(n / tcap) units of near-equal size, units[u] =
 // (expert, first assignment, count).  One CTA of 512 threads; chunks of 32
 // assignments per warp (__match_any_sync gives ranks within a chunk).  Out-of-range
 // expert ids are clamped to 0 and flagged.
-__global__ void __launch_bounds__(512) g_bucket_kernel(const int* sel, int nT, int E, int top_k,
+__global__ void __launch_bounds__(512) g_bucket_kernel(const int* sel, int nT, int E, int top_k, int tcap,
                                                        int* assign, int* units, int* n_units,
                                                        int max_units, int* err) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -198,15 +220,41 @@ __global__ void __launch_bounds__(512) g_bucket_kernel(const int* sel, int nT, i
     total[e] = s;
   }
   __syncthreads();
-  if (tid == 0) {
-    int b = 0, ub = 0;
-    for (int e = 0; e < E; ++e) {
-      base[e] = b;
-      b += total[e];
-      ubase[e] = ub;
-      ub += (total[e] + kGTok - 1) / kGTok;
+  {
+    // exclusive scans of the assignment and unit counts over the experts (E <= 256:
+    // warps 0-7, warp-level inclusive scans, then the warp totals in order)
+    int* wsum = ubase + kMaxExperts;  // [2][8]
+    int tot = 0, nun = 0, inc = 0, incu = 0;
+    if (tid < 256) {
+      tot = tid < E ? total[tid] : 0;
+      nun = (tot + tcap - 1) / tcap;
+      inc = tot;
+      incu = nun;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int a = __shfl_up_sync(0xffffffffu, inc, o), b = __shfl_up_sync(0xffffffffu, incu, o);
+        if (lane >= o) {
+          inc += a;
+          incu += b;
+        }
+      }
+      if (lane == 31) {
+        wsum[warp] = inc;
+        wsum[8 + warp] = incu;
+      }
     }
-    *n_units = ub < max_units ? ub : max_units;
+    __syncthreads();
+    if (tid < 256) {
+      for (int w = 0; w < warp; ++w) {
+        inc += wsum[w];
+        incu += wsum[8 + w];
+      }
+      if (tid < E) {
+        base[tid] = inc - tot;
+        ubase[tid] = incu - nun;
+      }
+      if (tid == 255) *n_units = incu < max_units ? incu : max_units;
+    }
   }
   __syncthreads();
   for (int c = warp; c < nch; c += 16) {
@@ -220,7 +268,7 @@ __global__ void __launch_bounds__(512) g_bucket_kernel(const int* sel, int nT, i
   }
   for (int e = tid; e < E; e += 512) {
     const int n = total[e];
-    const int nu = (n + kGTok - 1) / kGTok;
+    const int nu = (n + tcap - 1) / tcap;
     int off = 0;
     for (int k = 0; k < nu; ++k) {
       const int sz = n / nu + (k < n % nu ? 1 : 0);
@@ -252,6 +300,8 @@ constexpr int kGDnRec = 8;  // down records per stage (one per warp of an 8-warp
 
 struct GExpParams {
   int H, I, E, top_k, max_units;
+  int tcap;        // tokens of one unit at most (<= kGTok)
+  int red_floats;  // one warp group's partials: 8 warps x ceil(tcap / 8) blocks x 128
   TileGeom tgu, tdn;
   const uint8_t* x;
   const uint8_t* gu_tiles;
@@ -274,29 +324,32 @@ struct GExpParams {
 constexpr uint32_t kGFull = 0, kGEmpty = 8 * kGMaxSlots, kGAbort = 16 * kGMaxSlots,
                    kGTokS = kGAbort + 16, kGSlotS = kGTokS + 4 * kGTok, kGFixedEnd = 384;
 static_assert(kGSlotS + 4 * kGTok <= kGFixedEnd, "fixed map");
-constexpr uint32_t kGRedBytes = kCW * kGNB * 4 * 32 * 4;  // gate|up partials: 2 groups x 8 warps x 3 blocks
 
 // Correction term of one group for NB blocks: acc += s * (D - (P + z Q)), the scale
 // and zero point read once for all blocks; gs[nb] = (P, Q) of tokens 2t and 2t + 1.
 template <typename S, int NB>
-DEVI void flush_nb(float (&acc)[NB][4], const float (&d)[NB][4], const uint8_t* rec, const TileGeom& tg,
-                   int grp, int g, const float4 (&gs)[NB]) {
+DEVI void flush_nb(float (&acc)[NB][4], const float (&d0)[NB][4], const float (&d1)[NB][4], const uint8_t* rec,
+                   const TileGeom& tg, int grp, int g, const float4 (&gs)[NB]) {
   const uint32_t zz = tg.has_zeros ? (uint32_t)rec[tg.off_zero + grp * 8 + g] : 0x88u;
   const float za = (float)(zz & 15u), zb = (float)(zz >> 4);
   const float2 s = scale_pair(reinterpret_cast<const uint32_t*>(rec + tg.off_scale)[grp * 8 + g], (S*)nullptr);
 #pragma unroll
   for (int nb = 0; nb < NB; ++nb) {
-    acc[nb][0] = fmaf(s.x, d[nb][0] - fmaf(za, gs[nb].y, gs[nb].x), acc[nb][0]);
-    acc[nb][1] = fmaf(s.x, d[nb][1] - fmaf(za, gs[nb].w, gs[nb].z), acc[nb][1]);
-    acc[nb][2] = fmaf(s.y, d[nb][2] - fmaf(zb, gs[nb].y, gs[nb].x), acc[nb][2]);
-    acc[nb][3] = fmaf(s.y, d[nb][3] - fmaf(zb, gs[nb].w, gs[nb].z), acc[nb][3]);
+    acc[nb][0] = fmaf(s.x, (d0[nb][0] + d1[nb][0]) - fmaf(za, gs[nb].y, gs[nb].x), acc[nb][0]);
+    acc[nb][1] = fmaf(s.x, (d0[nb][1] + d1[nb][1]) - fmaf(za, gs[nb].w, gs[nb].z), acc[nb][1]);
+    acc[nb][2] = fmaf(s.y, (d0[nb][2] + d1[nb][2]) - fmaf(zb, gs[nb].y, gs[nb].x), acc[nb][2]);
+    acc[nb][3] = fmaf(s.y, (d0[nb][3] + d1[nb][3]) - fmaf(zb, gs[nb].w, gs[nb].z), acc[nb][3]);
   }
 }
 
 // One pair's weights against NB blocks of staged rows (xp: this lane's row g of block
-// 0 at the pair; blocks 8 rows apart).  FIRST: the group's first pair (C = 0).
+// 0 at the pair; blocks 8 rows apart).  With one block the MMAs alternate between two
+// accumulator chains (k-steps A and B of each 32-column window) so that consecutive
+// MMAs do not wait on each other; with two or three blocks the blocks are the
+// independent chains (d1 stays unused, flush_nb adds its zeros).
+// FIRST: the group's first pair (C = 0).
 template <typename T, int NB, bool FIRST>
-DEVI void pair_mma(float (&d)[NB][4], uint4 w, const uint8_t* xp, uint32_t pitch8) {
+DEVI void pair_mma(float (&d0)[NB][4], float (&d1)[NB][4], uint4 w, const uint8_t* xp, uint32_t pitch8) {
   uint32_t A0[4], B0[4], A1[4], B1[4];
   DqOff<T>::expand(w.x, w.y, A0, B0);
   DqOff<T>::expand(w.z, w.w, A1, B1);
@@ -304,13 +357,19 @@ DEVI void pair_mma(float (&d)[NB][4], uint4 w, const uint8_t* xp, uint32_t pitch
   for (int nb = 0; nb < NB; ++nb) {
     const uint4 xa = *reinterpret_cast<const uint4*>(xp + nb * pitch8);
     const uint4 xb = *reinterpret_cast<const uint4*>(xp + nb * pitch8 + 64);
-    if (FIRST)
-      mma_first<T>(d[nb], A0[0], A0[1], A0[2], A0[3], xa.x, xa.y);
-    else
-      MmaOp<T>::run(d[nb], A0[0], A0[1], A0[2], A0[3], xa.x, xa.y);
-    MmaOp<T>::run(d[nb], B0[0], B0[1], B0[2], B0[3], xa.z, xa.w);
-    MmaOp<T>::run(d[nb], A1[0], A1[1], A1[2], A1[3], xb.x, xb.y);
-    MmaOp<T>::run(d[nb], B1[0], B1[1], B1[2], B1[3], xb.z, xb.w);
+    float (&db)[4] = NB == 1 ? d1[nb] : d0[nb];
+    if (FIRST) {
+      mma_first<T>(d0[nb], A0[0], A0[1], A0[2], A0[3], xa.x, xa.y);
+      if (NB == 1)
+        mma_first<T>(db, B0[0], B0[1], B0[2], B0[3], xa.z, xa.w);
+      else
+        MmaOp<T>::run(db, B0[0], B0[1], B0[2], B0[3], xa.z, xa.w);
+    } else {
+      MmaOp<T>::run(d0[nb], A0[0], A0[1], A0[2], A0[3], xa.x, xa.y);
+      MmaOp<T>::run(db, B0[0], B0[1], B0[2], B0[3], xa.z, xa.w);
+    }
+    MmaOp<T>::run(d0[nb], A1[0], A1[1], A1[2], A1[3], xb.x, xb.y);
+    MmaOp<T>::run(db, B1[0], B1[1], B1[2], B1[3], xb.z, xb.w);
   }
 }
 
@@ -326,21 +385,25 @@ DEVI void gmm_fixed(const uint8_t* rec, const TileGeom& tg, int pb, int lane, co
   const uint32_t pitch8 = pitch * 8u;
 #pragma unroll
   for (int gi = 0; gi < NPW / PPG; ++gi) {
-    float d[NB][4];
+    float d0[NB][4], d1[NB][4];
+    if (NB > 1) {
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) zero4(d1[nb]);
+    }
 #pragma unroll
     for (int k = 0; k < PPG; ++k) {
       const int pi = gi * PPG + k;
       const uint4 w = *reinterpret_cast<const uint4*>(wp + pi * 512);
       if (k == 0)
-        pair_mma<T, NB, true>(d, w, xp + pi * 128, pitch8);
+        pair_mma<T, NB, true>(d0, d1, w, xp + pi * 128, pitch8);
       else
-        pair_mma<T, NB, false>(d, w, xp + pi * 128, pitch8);
+        pair_mma<T, NB, false>(d0, d1, w, xp + pi * 128, pitch8);
     }
     const int grp = pb / PPG + gi;
     float4 gs[NB];
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) gs[nb] = *reinterpret_cast<const float4*>(gsg + grp * kGPad + nb * 8 + 2 * t);
-    flush_nb<S, NB>(acc, d, rec, tg, grp, g, gs);
+    flush_nb<S, NB>(acc, d0, d1, rec, tg, grp, g, gs);
   }
 }
 
@@ -357,7 +420,11 @@ DEVI void gmm_pairs(const uint8_t* rec, const TileGeom& tg, int pb, int pe, int 
     const int grp = p >> tg.gshift;
     int pend = (grp + 1) << tg.gshift;
     if (pend > pe) pend = pe;
-    float d[NB][4];
+    float d0[NB][4], d1[NB][4];
+    if (NB > 1) {
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) zero4(d1[nb]);
+    }
     float4 gs[NB];
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) gs[nb] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -365,9 +432,9 @@ DEVI void gmm_pairs(const uint8_t* rec, const TileGeom& tg, int pb, int pe, int 
     for (; p < pend; ++p) {
       const uint4 w = *reinterpret_cast<const uint4*>(rec + (((uint32_t)p << 5) + lane) * 16u);
       if (first)
-        pair_mma<T, NB, true>(d, w, xrow + (uint32_t)p * 128u, pitch8);
+        pair_mma<T, NB, true>(d0, d1, w, xrow + (uint32_t)p * 128u, pitch8);
       else
-        pair_mma<T, NB, false>(d, w, xrow + (uint32_t)p * 128u, pitch8);
+        pair_mma<T, NB, false>(d0, d1, w, xrow + (uint32_t)p * 128u, pitch8);
       first = false;
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb) {
@@ -378,7 +445,7 @@ DEVI void gmm_pairs(const uint8_t* rec, const TileGeom& tg, int pb, int pe, int 
         gs[nb].w += gq.w;
       }
     }
-    flush_nb<S, NB>(acc, d, rec, tg, grp, g, gs);
+    flush_nb<S, NB>(acc, d0, d1, rec, tg, grp, g, gs);
   }
 }
 
@@ -498,7 +565,7 @@ DEVI void g_unit(const GExpParams& p, int u, int& e, int& first, int& n) {
   e = (e < 0 || e >= p.E) ? 0 : e;
   first = p.units[u * 3 + 1];
   n = p.units[u * 3 + 2];
-  n = n < 1 ? 1 : (n > kGTok ? kGTok : n);
+  n = n < 1 ? 1 : (n > p.tcap ? p.tcap : n);
 }
 
 // Ring position of the j-th stage of a CTA's range.
@@ -508,9 +575,27 @@ DEVI void g_slot(int j, int ns, int& slot, uint32_t& ph) {
   ph = (uint32_t)k & 1u;
 }
 
-DEVI void g_wait_stage(uint64_t* full, volatile int* abort_flag, int* err, int slot, uint32_t ph) {
+// Consumer wait for stage j (slot, phase ph) when the two warp groups take alternate
+// stages: a slot's previous stage may belong to the other group, which may not have
+// consumed it yet, and a parity wait on `full` that ran two phases ahead would return
+// at once.  So first the release of stage j - ns (empty phase k - 1, k = j / ns): its
+// phase k - 2 is complete (stage j - 2 ns is this group's own earlier stage, or came
+// before the last re-staging barrier), so that wait cannot alias; once it passes,
+// `full` is in the phase of stage j.
+DEVI void g_wait_stage(uint64_t* full, uint64_t* empty, volatile int* abort_flag, int* err, int j, int ns,
+                       int slot, uint32_t ph) {
   if (*abort_flag) return;
   const long long t0 = clock64();
+  if (j >= ns) {
+    while (!mbar_try_wait(&empty[slot], ph ^ 1u)) {
+      if (*abort_flag) return;
+      if (clock64() - t0 > kWaitLimitCycles) {
+        *abort_flag = 1;
+        set_error(err, DUPLEX_DEVERR_TIMEOUT);
+        return;
+      }
+    }
+  }
   while (!mbar_try_wait(&full[slot], ph)) {
     if (*abort_flag) return;
     if (clock64() - t0 > kWaitLimitCycles) {
@@ -544,20 +629,24 @@ DEVI void g_produce(const GExpParams& p, uint64_t* full, uint64_t* empty, volati
 // ---- gate|up item of one 8-warp group: warps 0-3 the gate record, 4-7 the up record,
 // 4-way K split; act[first + tk][rb*16 .. +16] = SiLU(gate) * up.  red: this group's
 // partials [8 warps][NB][4][32]; bar: the group's named barrier (256 threads).
+// The tile geometry and pitches come in by value (copied once per kernel into
+// registers): read through the parameter block, the compiler reloads them after every
+// shared-memory store it cannot tell apart from that block, inside the pair loop.
 template <typename T, typename S, int NB, int NPW, int PPG>
-DEVI void gu_item(const GExpParams& p, const uint8_t* st, uint64_t* empty_slot, int rb, int first, int n,
-                  const uint8_t* xsh, const float2* gx, const float2* gxg, float* red, int bar) {
+DEVI void gu_item(const TileGeom tg, uint32_t x_pitch, uint8_t* act, int I, const uint8_t* st,
+                  uint64_t* empty_slot, int rb, int first, int n, const uint8_t* xsh, const float2* gx,
+                  const float2* gxg, float* red, int bar) {
   const int lane = threadIdx.x & 31, wi = (threadIdx.x >> 5) & 7, gt = threadIdx.x & 255;
   const int rec = wi >> 2, kq = wi & 3;
   float acc[NB][4];
 #pragma unroll
   for (int nb = 0; nb < NB; ++nb) zero4(acc[nb]);
-  const uint8_t* rp = st + (uint32_t)rec * p.tgu.rec_bytes;
+  const uint8_t* rp = st + (uint32_t)rec * tg.rec_bytes;
   if constexpr (NPW > 0) {
-    gmm_fixed<T, S, NB, NPW, PPG>(rp, p.tgu, kq * NPW, lane, xsh, p.x_pitch, gxg, acc);
+    gmm_fixed<T, S, NB, NPW, PPG>(rp, tg, kq * NPW, lane, xsh, x_pitch, gxg, acc);
   } else {
-    const int np = p.tgu.npairs;
-    gmm_pairs<T, S, NB>(rp, p.tgu, (kq * np) >> 2, ((kq + 1) * np) >> 2, lane, xsh, p.x_pitch, gx, acc);
+    const int np = tg.npairs;
+    gmm_pairs<T, S, NB>(rp, tg, (kq * np) >> 2, ((kq + 1) * np) >> 2, lane, xsh, x_pitch, gx, acc);
   }
   __syncwarp();
   if (lane == 0) mbar_arrive(empty_slot);
@@ -572,7 +661,7 @@ DEVI void gu_item(const GExpParams& p, const uint8_t* st, uint64_t* empty_slot, 
     const int col = rb * 16 + row;
     T a = from_f32<T>(silu_f32(gsum_) * usum);
     if (DqOff<T>::kOddDiv16 && (col & 1)) a = from_f32<T>(to_f32<T>(a) * 0.0625f);
-    reinterpret_cast<T*>(p.act + (size_t)(first + tk) * p.I * 2)[frag_pos(col)] = a;
+    reinterpret_cast<T*>(act + (size_t)(first + tk) * I * 2)[frag_pos(col)] = a;
   }
   named_bar_sync(bar, 256);
 }
@@ -612,8 +701,12 @@ __global__ void __launch_bounds__(kThreads, 1) g_gateup_kernel(const __grid_cons
   uint8_t* xsh = smem + p.off_x;
   float2* gx = reinterpret_cast<float2*>(smem + p.off_gx);
   float2* gxg = reinterpret_cast<float2*>(smem + p.off_gxg);
+  const TileGeom tgu = p.tgu;
+  const uint32_t x_pitch = p.x_pitch;
+  uint8_t* const act = p.act;
+  const int I = p.I;
   const int grp = warp >> 3;
-  float* red = reinterpret_cast<float*>(smem + p.off_red_a) + grp * (kGRedBytes / 8);
+  float* red = reinterpret_cast<float*>(smem + p.off_red_a) + grp * p.red_floats;
   const int H = p.H, np = p.tgu.npairs;
   for (int s0 = i0; s0 < i1;) {
     const int s1 = g_seg_end(s0, i1, perG);
@@ -624,16 +717,29 @@ __global__ void __launch_bounds__(kThreads, 1) g_gateup_kernel(const __grid_cons
     named_bar_sync(1, kConsumers);  // both groups are done with the previous unit
     if (tid < n) tok[tid] = p.assign[first + tid] >> 3;
     named_bar_sync(1, kConsumers);
+    // a thread's row loads are issued kRL at a time before any is used (one memory
+    // latency per kRL passes)
     const int nq = H >> 3, total = n * nq;
-    for (int base = 0; base < total; base += kConsumers) {
-      const int idx = base + tid;
+    constexpr int kRL = 5;  // loads in flight per thread (two rounds for 20 tokens at hidden 2048)
+    for (int base0 = 0; base0 < total; base0 += kRL * kConsumers) {
+      uint4 ld[kRL];
+#pragma unroll
+      for (int k = 0; k < kRL; ++k) {
+        const int idx = base0 + k * kConsumers + tid;
+        if (idx < total) {
+          const int rr = idx / nq, q = idx - rr * nq;
+          ld[k] = __ldg(reinterpret_cast<const uint4*>(p.x + (size_t)tok[rr] * H * 2) + q);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kRL; ++k) {
+      const int idx = base0 + k * kConsumers + tid;
       float se = 0.f, so = 0.f;
       int rr = 0, q = 0;
       if (idx < total) {
         rr = idx / nq;
         q = idx - rr * nq;
-        uint4 o = __ldg(reinterpret_cast<const uint4*>(p.x + (size_t)tok[rr] * H * 2) + q);
-        o = to_frag_order(o);
+        uint4 o = to_frag_order(ld[k]);
         if (DqOff<T>::kOddDiv16) {
           const __half2 q16 = __float2half2_rn(0.0625f);
           __half2 hy = __hmul2(*reinterpret_cast<__half2*>(&o.y), q16);
@@ -650,6 +756,7 @@ __global__ void __launch_bounds__(kThreads, 1) g_gateup_kernel(const __grid_cons
         so += __shfl_xor_sync(0xffffffffu, so, o);
       }
       if (idx < total && (q & 7) == 0) gx[(q >> 3) * kGPad + rr] = corr_pq<T>(se, so);
+      }
     }
     for (int idx = tid; idx < np * kGPad; idx += kConsumers)
       if (idx % kGPad >= n) gx[idx] = make_float2(0.f, 0.f);
@@ -662,15 +769,18 @@ __global__ void __launch_bounds__(kThreads, 1) g_gateup_kernel(const __grid_cons
       int slot;
       uint32_t ph;
       g_slot(it - i0, ns, slot, ph);
-      g_wait_stage(full, abort_flag, p.err, slot, ph);
+      g_wait_stage(full, empty, abort_flag, p.err, it - i0, ns, slot, ph);
       const uint8_t* st = ring + (uint32_t)slot * p.slot_a;
       const int rb = it - (it / perG) * perG;
       if (nbv == 1)
-        gu_item<T, S, 1, NPW, PPG>(p, st, &empty[slot], rb, first, n, xsh, gx, gxg, red, 2 + grp);
+        gu_item<T, S, 1, NPW, PPG>(tgu, x_pitch, act, I, st, &empty[slot], rb, first, n, xsh, gx, gxg, red,
+                                   2 + grp);
       else if (nbv == 2)
-        gu_item<T, S, 2, NPW, PPG>(p, st, &empty[slot], rb, first, n, xsh, gx, gxg, red, 2 + grp);
+        gu_item<T, S, 2, NPW, PPG>(tgu, x_pitch, act, I, st, &empty[slot], rb, first, n, xsh, gx, gxg, red,
+                                   2 + grp);
       else
-        gu_item<T, S, 3, NPW, PPG>(p, st, &empty[slot], rb, first, n, xsh, gx, gxg, red, 2 + grp);
+        gu_item<T, S, 3, NPW, PPG>(tgu, x_pitch, act, I, st, &empty[slot], rb, first, n, xsh, gx, gxg, red,
+                                   2 + grp);
     }
     s0 = s1;
   }
@@ -679,17 +789,18 @@ __global__ void __launch_bounds__(kThreads, 1) g_gateup_kernel(const __grid_cons
 // ---- down item: one warp, one record (16 rows of H) over the whole K; the outputs
 // go from the accumulators straight to ypart[tok][slot][row] for the live tokens.
 template <typename T, typename S, int NB, int NPW, int PPG>
-DEVI void dn_item(const GExpParams& p, const uint8_t* rp, uint64_t* empty_slot, int row0, int n,
-                  const int* tok, const int* slt, const uint8_t* act, const float2* ga, const float2* gag) {
+DEVI void dn_item(const TileGeom tg, uint32_t a_pitch, float* ypart, int top_k, int H, const uint8_t* rp,
+                  uint64_t* empty_slot, int row0, int n, const int* tok, const int* slt, const uint8_t* act,
+                  const float2* ga, const float2* gag) {
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   float acc[NB][4];
 #pragma unroll
   for (int nb = 0; nb < NB; ++nb) zero4(acc[nb]);
   if (rp) {
     if constexpr (NPW > 0)
-      gmm_fixed<T, S, NB, NPW, PPG>(rp, p.tdn, 0, lane, act, p.a_pitch, gag, acc);
+      gmm_fixed<T, S, NB, NPW, PPG>(rp, tg, 0, lane, act, a_pitch, gag, acc);
     else
-      gmm_pairs<T, S, NB>(rp, p.tdn, 0, p.tdn.npairs, lane, act, p.a_pitch, ga, acc);
+      gmm_pairs<T, S, NB>(rp, tg, 0, tg.npairs, lane, act, a_pitch, ga, acc);
   }
   __syncwarp();
   if (lane == 0) mbar_arrive(empty_slot);
@@ -699,7 +810,7 @@ DEVI void dn_item(const GExpParams& p, const uint8_t* rp, uint64_t* empty_slot, 
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const int tk = nb * 8 + 2 * t + (q & 1), row = row0 + g + (q >> 1) * 8;
-      if (tk < n) p.ypart[((size_t)tok[tk] * p.top_k + slt[tk]) * p.H + row] = acc[nb][q];
+      if (tk < n) ypart[((size_t)tok[tk] * top_k + slt[tk]) * H + row] = acc[nb][q];
     }
 }
 
@@ -734,6 +845,10 @@ __global__ void __launch_bounds__(kThreads, 1) g_down_kernel(const __grid_consta
   uint8_t* act = smem + p.off_a;
   float2* ga = reinterpret_cast<float2*>(smem + p.off_ga);
   float2* gag = reinterpret_cast<float2*>(smem + p.off_gag);
+  const TileGeom tdn = p.tdn;
+  const uint32_t a_pitch = p.a_pitch;
+  float* const ypart = p.ypart;
+  const int top_k = p.top_k, H = p.H;
   const int I = p.I, np = p.tdn.npairs;
   const int grp = warp >> 3, rc = warp & 7;
   for (int s0 = i0; s0 < i1;) {
@@ -749,10 +864,24 @@ __global__ void __launch_bounds__(kThreads, 1) g_down_kernel(const __grid_consta
       slt[tid] = a & 7;
     }
     const int nq = I >> 3;
-    for (int idx = tid; idx < n * nq; idx += kConsumers) {
-      const int rr = idx / nq, q = idx - rr * nq;
-      *reinterpret_cast<uint4*>(act + (uint32_t)rr * p.a_pitch + (uint32_t)q * 16u) =
-          __ldcg(reinterpret_cast<const uint4*>(p.act + (size_t)(first + rr) * I * 2) + q);
+    for (int base0 = 0; base0 < n * nq; base0 += 4 * kConsumers) {
+      uint4 ld[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int idx = base0 + k * kConsumers + tid;
+        if (idx < n * nq) {
+          const int rr = idx / nq, q = idx - rr * nq;
+          ld[k] = __ldcg(reinterpret_cast<const uint4*>(p.act + (size_t)(first + rr) * I * 2) + q);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int idx = base0 + k * kConsumers + tid;
+        if (idx < n * nq) {
+          const int rr = idx / nq, q = idx - rr * nq;
+          *reinterpret_cast<uint4*>(act + (uint32_t)rr * a_pitch + (uint32_t)q * 16u) = ld[k];
+        }
+      }
     }
     named_bar_sync(1, kConsumers);
     for (int idx = tid; idx < np * kGPad; idx += kConsumers) {
@@ -774,33 +903,60 @@ __global__ void __launch_bounds__(kThreads, 1) g_down_kernel(const __grid_consta
       int slot;
       uint32_t ph;
       g_slot(it - i0, ns, slot, ph);
-      g_wait_stage(full, abort_flag, p.err, slot, ph);
+      g_wait_stage(full, empty, abort_flag, p.err, it - i0, ns, slot, ph);
       const int s = it - (it / nDN) * nDN;
       const int cnt = RbD - kGDnRec * s < kGDnRec ? RbD - kGDnRec * s : kGDnRec;
       const uint8_t* rp = rc < cnt ? ring + (uint32_t)slot * p.slot_d + (uint32_t)rc * p.tdn.rec_bytes : nullptr;
       const int row0 = (kGDnRec * s + rc) * 16;
       if (nbv == 1)
-        dn_item<T, S, 1, NPW, PPG>(p, rp, &empty[slot], row0, n, tok, slt, act, ga, gag);
+        dn_item<T, S, 1, NPW, PPG>(tdn, a_pitch, ypart, top_k, H, rp, &empty[slot], row0, n, tok, slt, act,
+                                   ga, gag);
       else if (nbv == 2)
-        dn_item<T, S, 2, NPW, PPG>(p, rp, &empty[slot], row0, n, tok, slt, act, ga, gag);
+        dn_item<T, S, 2, NPW, PPG>(tdn, a_pitch, ypart, top_k, H, rp, &empty[slot], row0, n, tok, slt, act,
+                                   ga, gag);
       else
-        dn_item<T, S, 3, NPW, PPG>(p, rp, &empty[slot], row0, n, tok, slt, act, ga, gag);
+        dn_item<T, S, 3, NPW, PPG>(tdn, a_pitch, ypart, top_k, H, rp, &empty[slot], row0, n, tok, slt, act,
+                                   ga, gag);
     }
     s0 = s1;
   }
 }
 
 // ------------------------------------------------------------------ 5. combine
+// out[t][r] = round_T(sum over slots j in selection order of w[t][j] * y[t][j][r]
+// (+ residual[t][r])); four consecutive outputs per thread.
 template <typename T>
 __global__ void __launch_bounds__(256) g_combine_kernel(const float* ypart, const float* w, const T* residual,
                                                         int nT, int H, int top_k, T* out) {
+  const int H4 = H >> 2;
   const size_t idx = (size_t)blockIdx.x * 256 + threadIdx.x;
-  if (idx >= (size_t)nT * H) return;
-  const int t = (int)(idx / H), r = (int)(idx - (size_t)t * H);
-  float s = 0.f;
-  for (int j = 0; j < top_k; ++j) s = fmaf(w[(size_t)t * top_k + j], ypart[((size_t)t * top_k + j) * H + r], s);
-  if (residual) s += to_f32<T>(residual[idx]);
-  out[idx] = from_f32<T>(s);
+  if (idx >= (size_t)nT * H4) return;
+  const int t = (int)(idx / H4), r4 = (int)(idx - (size_t)t * H4);
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j = 0; j < top_k; ++j) {
+    const float wj = w[(size_t)t * top_k + j];
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(ypart + ((size_t)t * top_k + j) * H) + r4);
+    s.x = fmaf(wj, v.x, s.x);
+    s.y = fmaf(wj, v.y, s.y);
+    s.z = fmaf(wj, v.z, s.z);
+    s.w = fmaf(wj, v.w, s.w);
+  }
+  const size_t o = (size_t)t * H + (size_t)r4 * 4;
+  if (residual) {
+    const uint2 rv = *reinterpret_cast<const uint2*>(residual + o);
+    const T* rr = reinterpret_cast<const T*>(&rv);
+    s.x += to_f32<T>(rr[0]);
+    s.y += to_f32<T>(rr[1]);
+    s.z += to_f32<T>(rr[2]);
+    s.w += to_f32<T>(rr[3]);
+  }
+  uint2 ov;
+  T* oo = reinterpret_cast<T*>(&ov);
+  oo[0] = from_f32<T>(s.x);
+  oo[1] = from_f32<T>(s.y);
+  oo[2] = from_f32<T>(s.z);
+  oo[3] = from_f32<T>(s.w);
+  *reinterpret_cast<uint2*>(out + o) = ov;
 }
 
 // ====================================================================== host side
@@ -809,10 +965,20 @@ struct GScratch {
   int max_units;
 };
 
+// Unit token cap of one call, from the expected tokens per expert mu = T k / E: small
+// batches stage fewer rows, which leaves room for a deeper weight ring.
+static int g_tcap(int T, int E, int top_k) {
+  const int tk = T * top_k;
+  if (tk <= 4 * E) return 8;
+  if (tk <= 9 * E) return 16;
+  return kGTok;
+}
+
 static GScratch g_scratch(int T, int E, int H, int I, int top_k) {
   GScratch s;
   size_t off = 0;
-  s.max_units = E + (T * top_k + kGTok - 1) / kGTok + 1;
+  const int tcap = g_tcap(T, E, top_k);
+  s.max_units = E + (T * top_k + tcap - 1) / tcap + 1;
   s.logits = off; off += align_up((size_t)T * E * 4, 256);
   s.sel = off; off += align_up((size_t)T * top_k * 4, 256);
   s.w = off; off += align_up((size_t)T * top_k * 4, 256);
@@ -825,41 +991,44 @@ static GScratch g_scratch(int T, int E, int H, int I, int top_k) {
   return s;
 }
 
-// Shared-memory maps of the two expert kernels for one geometry (the ring takes what
-// is left, up to kGMaxSlots slots, at least 2); false when a map does not fit.  The
-// staged rows are sized for kGTok tokens; MMA blocks read up to kGPad rows, which
-// stay inside the map because the tables, partials and ring follow them.
-static bool g_layout(int H, int I, int group, int has_zeros, GExpParams* p) {
+// Shared-memory maps of the two expert kernels for one geometry and unit cap tcap (the
+// ring takes what is left, up to kGMaxSlots slots, at least 2); false when a map does
+// not fit.  The staged rows are sized for tcap tokens; MMA blocks read up to
+// 8 ceil(tcap / 8) <= kGPad rows, which stay inside the map because the tables,
+// partials and ring follow them.
+static bool g_layout(int H, int I, int group, int has_zeros, int tcap, GExpParams* p) {
   if ((H & 63) || (I & 63) || group < 64 || (group & (group - 1))) return false;
-  if (32 * (H * 2 + 16) + 8 * 256 * 4 > kGSmemMax) return false;  // router tile
+  if (g_router_smem(H) > kGSmemMax) return false;  // router tile
   if (tile_geom(H, group, has_zeros, &p->tgu) || tile_geom(I, group, has_zeros, &p->tdn)) return false;
   auto up = [](uint32_t v, uint32_t a) { return (v + a - 1) / a * a; };
   p->x_pitch = up((uint32_t)H * 2u, 128) + 64u;
   p->a_pitch = up((uint32_t)I * 2u, 128) + 64u;
   const uint32_t ppg = 1u << p->tgu.gshift;
+  p->tcap = tcap;
+  p->red_floats = 8 * ((tcap + 7) / 8) * 128;
   // gate|up
   p->slot_a = up(2u * p->tgu.rec_bytes, 128);
   p->off_x = kGFixedEnd;
-  p->off_gx = up(p->off_x + kGTok * p->x_pitch, 128);
+  p->off_gx = up(p->off_x + (uint32_t)tcap * p->x_pitch, 128);
   p->off_gxg = up(p->off_gx + (uint32_t)p->tgu.npairs * kGPad * 8u, 128);
   p->off_red_a = up(p->off_gxg + (uint32_t)p->tgu.npairs / ppg * kGPad * 8u, 128);
-  p->off_ring_a = up(p->off_red_a + kGRedBytes, 128);
+  p->off_ring_a = up(p->off_red_a + 2u * (uint32_t)p->red_floats * 4u, 128);
   if (p->off_ring_a + 2 * p->slot_a > (uint32_t)kGSmemMax) return false;
   p->ns_a = (int)((kGSmemMax - p->off_ring_a) / p->slot_a);
   if (p->ns_a > kGMaxSlots) p->ns_a = kGMaxSlots;
   p->smem_a = p->off_ring_a + (uint32_t)p->ns_a * p->slot_a;
-  if (p->off_x + kGPad * p->x_pitch > p->smem_a) return false;
+  if (p->off_x + 8u * ((tcap + 7) / 8) * p->x_pitch > p->smem_a) return false;
   // down
   p->slot_d = up((uint32_t)kGDnRec * p->tdn.rec_bytes, 128);
   p->off_a = kGFixedEnd;
-  p->off_ga = up(p->off_a + kGTok * p->a_pitch, 128);
+  p->off_ga = up(p->off_a + (uint32_t)tcap * p->a_pitch, 128);
   p->off_gag = up(p->off_ga + (uint32_t)p->tdn.npairs * kGPad * 8u, 128);
   p->off_ring_d = up(p->off_gag + (uint32_t)p->tdn.npairs / ppg * kGPad * 8u, 128);
   if (p->off_ring_d + 2 * p->slot_d > (uint32_t)kGSmemMax) return false;
   p->ns_d = (int)((kGSmemMax - p->off_ring_d) / p->slot_d);
   if (p->ns_d > kGMaxSlots) p->ns_d = kGMaxSlots;
   p->smem_d = p->off_ring_d + (uint32_t)p->ns_d * p->slot_d;
-  if (p->off_a + kGPad * p->a_pitch > p->smem_d) return false;
+  if (p->off_a + 8u * ((tcap + 7) / 8) * p->a_pitch > p->smem_d) return false;
   return true;
 }
 
@@ -898,7 +1067,7 @@ extern "C" int duplex_moe_grouped_workspace_bytes(int32_t T, int32_t E, int32_t 
       top_k > kMaxTopK || top_k > E || H < 1 || I < 1)
     return DUPLEX_ERR_ARG;
   GExpParams p = {};
-  if (!g_layout(H, I, group, has_zeros, &p)) return DUPLEX_ERR_UNSUPPORTED;
+  if (!g_layout(H, I, group, has_zeros, kGTok, &p)) return DUPLEX_ERR_UNSUPPORTED;  // every cap fits
   *bytes = g_scratch(T, E, H, I, top_k).total;
   return DUPLEX_OK;
 }
@@ -916,7 +1085,9 @@ extern "C" int duplex_moe_grouped(const void* x, int act_dtype, int32_t T, const
   if (act_dtype != DUPLEX_DTYPE_F16 && act_dtype != DUPLEX_DTYPE_BF16) return DUPLEX_ERR_DTYPE;
   if (scale_dtype != act_dtype) return DUPLEX_ERR_DTYPE;
   GExpParams p = {};
-  if (!g_layout(H, I, group, has_zeros, &p)) return DUPLEX_ERR_UNSUPPORTED;
+  if (!g_layout(H, I, group, has_zeros, kGTok, &p)) return DUPLEX_ERR_UNSUPPORTED;
+  const int tcap = g_tcap(T, E, top_k);
+  if (!g_layout(H, I, group, has_zeros, tcap, &p)) return DUPLEX_ERR_UNSUPPORTED;
   const GScratch L = g_scratch(T, E, H, I, top_k);
   if (workspace_bytes < L.total) return DUPLEX_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) |
@@ -933,9 +1104,9 @@ extern "C" int duplex_moe_grouped(const void* x, int act_dtype, int32_t T, const
   int rc;
   // 1. router
   if (!logits_in) {
-    const int smem = 32 * (H * 2 + 16) + 8 * 256 * 4;
-    void (*rk)(const __half*, const __half*, const __half*, int, int, int, float*) = g_router_kernel<__half>;
-    void (*rkb)(const __nv_bfloat16*, const __nv_bfloat16*, const __nv_bfloat16*, int, int, int, float*) =
+    const int smem = g_router_smem(H);
+    void (*rk)(const __half*, const __half*, const __half*, int, int, int, float*, int*) = g_router_kernel<__half>;
+    void (*rkb)(const __nv_bfloat16*, const __nv_bfloat16*, const __nv_bfloat16*, int, int, int, float*, int*) =
         g_router_kernel<__nv_bfloat16>;
     const void* fn = f16 ? reinterpret_cast<const void*>(rk) : reinterpret_cast<const void*>(rkb);
     // the attribute is set once per kernel (to the ceiling), whatever this call's size
@@ -944,11 +1115,11 @@ extern "C" int duplex_moe_grouped(const void* x, int act_dtype, int32_t T, const
     const dim3 grid((E + 15) / 16, (T + 15) / 16);
     if (f16)
       rk<<<grid, 256, smem, st>>>(reinterpret_cast<const __half*>(x), reinterpret_cast<const __half*>(gate_w),
-                                  reinterpret_cast<const __half*>(gate_b), T, E, H, logits);
+                                  reinterpret_cast<const __half*>(gate_b), T, E, H, logits, err);
     else
       rkb<<<grid, 256, smem, st>>>(reinterpret_cast<const __nv_bfloat16*>(x),
                                    reinterpret_cast<const __nv_bfloat16*>(gate_w),
-                                   reinterpret_cast<const __nv_bfloat16*>(gate_b), T, E, H, logits);
+                                   reinterpret_cast<const __nv_bfloat16*>(gate_b), T, E, H, logits, err);
     if ((rc = record_cuda(cudaGetLastError()))) return rc;
   }
   // 2. top-k
@@ -962,9 +1133,9 @@ extern "C" int duplex_moe_grouped(const void* x, int act_dtype, int32_t T, const
   {
     const int N = T * top_k, nch = (N + 31) / 32;
     const int smem = (int)(align_up((size_t)nch * E, 16) + align_up((size_t)nch * E * 2, 16) +
-                           3 * kMaxExperts * 4);
+                           3 * kMaxExperts * 4 + 16 * 4);
     if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(g_bucket_kernel), kGSmemMax))) return rc;
-    g_bucket_kernel<<<1, 512, smem, st>>>(sel, T, E, top_k, reinterpret_cast<int*>(ws + L.assign),
+    g_bucket_kernel<<<1, 512, smem, st>>>(sel, T, E, top_k, tcap, reinterpret_cast<int*>(ws + L.assign),
                                           reinterpret_cast<int*>(ws + L.units),
                                           reinterpret_cast<int*>(ws + L.n_units), L.max_units, err);
     if ((rc = record_cuda(cudaGetLastError()))) return rc;
@@ -994,7 +1165,7 @@ extern "C" int duplex_moe_grouped(const void* x, int act_dtype, int32_t T, const
     if ((rc = record_cuda(cudaGetLastError()))) return rc;
   }
   // 5. combine
-  const size_t n_out = (size_t)T * H;
+  const size_t n_out = (size_t)T * H / 4;
   const unsigned blocks = (unsigned)((n_out + 255) / 256);
   if (f16)
     g_combine_kernel<__half><<<blocks, 256, 0, st>>>(reinterpret_cast<const float*>(ws + L.ypart), w,
