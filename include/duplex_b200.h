@@ -186,6 +186,8 @@ int duplex_moe_grouped_workspace_bytes(int32_t T, int32_t E, int32_t H, int32_t 
  * scale dtype == act dtype.  x, out, tiles, gate_w and workspace
  * 16-byte aligned.  err: device int, DUPLEX_DEVERR_EXPERT when a selected id is out of
  * range, DUPLEX_DEVERR_TIMEOUT when a copy wait gives up (bounded, about 2 s).
+ * Deterministic: every reduction runs in a fixed order (bit-identical across calls and
+ * graph replays).
  */
 int duplex_moe_grouped(const void* x, int act_dtype, int32_t T, const void* gate_w,
                        const void* gate_b, const float* logits_in, int32_t E, int32_t H,
@@ -193,6 +195,41 @@ int duplex_moe_grouped(const void* x, int act_dtype, int32_t T, const void* gate
                        const void* dn_tiles, int scale_dtype, int has_zeros, int32_t group,
                        const void* residual, void* out, float* w_out, int32_t* sel_out,
                        void* workspace, size_t workspace_bytes, int32_t* err, void* stream);
+
+/*
+ * moe_route_grouped -- the router of duplex_moe_grouped alone (logits on the tensor
+ * cores unless logits_in is given, fp32 softmax, top-k, renormalised) for T <= 512
+ * tokens: w_out / sel_out [T][top_k].  Same numerics as duplex_moe_route (T <= 8).
+ * workspace: at least T * E * 4 bytes (the logits), 16-byte aligned.
+ */
+int duplex_moe_route_grouped(const void* x, int act_dtype, int32_t T, const void* gate_w,
+                             const void* gate_b, const float* logits_in, int32_t E, int32_t H,
+                             int32_t top_k, int32_t norm_topk, float* w_out, int32_t* sel_out,
+                             void* workspace, size_t workspace_bytes, int32_t* err, void* stream);
+
+/*
+ * moe_experts_grouped -- the expert half of duplex_moe_grouped for a given selection,
+ * restricted to one expert-parallel rank's experts: for every token t and slot j whose
+ * expert e = sel[t][j] lies in [e_begin, e_begin + E_local), y = down(SiLU(gate(x_t)) *
+ * up(x_t)) with that expert's tiles (gu_tiles / dn_tiles hold the E_local local experts,
+ * local index e - e_begin); out[t] = sum of w[t][j] * y over those slots in selection
+ * order (+ residual[t]), rounded once to out_dtype (the act dtype, or DUPLEX_DTYPE_F32 for
+ * partial sums that other ranks' partials are added to).  Slots of other ranks'
+ * experts are skipped; ids outside [0, E_total) set DUPLEX_DEVERR_EXPERT and are
+ * skipped.  sel [T][top_k] int32, w [T][top_k] fp32 (device).  T <= 512; the unit token
+ * cap is chosen from T * top_k / E_total.  Other arguments and limits as
+ * duplex_moe_grouped; workspace: duplex_moe_experts_grouped_workspace_bytes.
+ */
+int duplex_moe_experts_grouped_workspace_bytes(int32_t T, int32_t E_local, int32_t E_total,
+                                               int32_t H, int32_t I, int32_t top_k,
+                                               int32_t group, int has_zeros, size_t* bytes);
+int duplex_moe_experts_grouped(const void* x, int act_dtype, int32_t T, const int32_t* sel,
+                               const float* w, int32_t top_k, int32_t e_begin, int32_t E_local,
+                               int32_t E_total, int32_t H, int32_t I, const void* gu_tiles,
+                               const void* dn_tiles, int scale_dtype, int has_zeros,
+                               int32_t group, const void* residual, void* out, int out_dtype,
+                               void* workspace, size_t workspace_bytes, int32_t* err,
+                               void* stream);
 
 /*
  * Persistent clock-path stack -- the reference's clock path (src/duplex/streaming/clock.py:

@@ -22,6 +22,9 @@
 #include "moe.cuh"
 #include "topk.cuh"
 
+#include <initializer_list>
+#include <type_traits>
+
 namespace duplex {
 
 int record_cuda(cudaError_t e);
@@ -29,7 +32,8 @@ int num_sms();
 int ensure_smem_attr(const void* fn, int bytes);
 
 constexpr int kGTok = 20;    // tokens of one expert unit at most (the per-call cap tcap <= kGTok)
-constexpr int kGNB = 3;      // 8-token MMA column blocks at most (kGNB * 8 >= kGTok)
+constexpr int kGNB = 3;      // 8-token MMA column blocks at most
+static_assert(kGNB * 8 >= kGTok, "a unit's tokens fit the MMA column blocks");
 constexpr int kGPad = 24;    // token slots per pair in the correction sums
 constexpr int kGMaxT = 512;  // tokens per call
 constexpr int kGSmemMax = 227 * 1024;  // dynamic shared memory of every kernel here (no static)
@@ -179,11 +183,12 @@ __global__ void __launch_bounds__(512) g_topk_kernel(const float* logits, int nT
 // then slot) into assign[] = token << 3 | slot, and the unit list: an expert's n
 // assignments split into ceil(n / tcap) units of near-equal size, units[u] =
 // (expert, first assignment, count).  One CTA of 512 threads; chunks of 32
-// assignments per warp (__match_any_sync gives ranks within a chunk).  Out-of-range
-// expert ids are clamped to 0 and flagged.
+// assignments per warp (__match_any_sync gives ranks within a chunk).  Only experts
+// [e_begin, e_begin + E) are bucketed (an expert-parallel rank's own); ids outside
+// [0, E_total) are flagged in err and skipped.
 __global__ void __launch_bounds__(512) g_bucket_kernel(const int* sel, int nT, int E, int top_k, int tcap,
-                                                       int* assign, int* units, int* n_units,
-                                                       int max_units, int* err) {
+                                                       int e_begin, int E_total, int* assign, int* units,
+                                                       int* n_units, int max_units, int* err) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int N = nT * top_k, nch = (N + 31) >> 5;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -196,13 +201,17 @@ __global__ void __launch_bounds__(512) g_bucket_kernel(const int* sel, int nT, i
   int* ubase = base + kMaxExperts;                                         // [E]
   for (int i = tid; i < nch * E; i += 512) cnt[i] = 0;
   __syncthreads();
+  // local expert of assignment a: ids outside [0, E_total) are flagged and skipped,
+  // ids of other ranks' experts (outside [e_begin, e_begin + E)) are skipped
   auto expert_of = [&](int a) {
-    int e = a < N ? sel[a] : -1;
-    if (a < N && (e < 0 || e >= E)) {
+    if (a >= N) return -1;
+    const int g = sel[a];
+    if (g < 0 || g >= E_total) {
       set_error(err, DUPLEX_DEVERR_EXPERT);
-      e = 0;
+      return -1;
     }
-    return e;
+    const int e = g - e_begin;
+    return (e < 0 || e >= E) ? -1 : e;
   };
   for (int c = warp; c < nch; c += 16) {
     const int a = c * 32 + lane;
@@ -923,17 +932,22 @@ __global__ void __launch_bounds__(kThreads, 1) g_down_kernel(const __grid_consta
 }
 
 // ------------------------------------------------------------------ 5. combine
-// out[t][r] = round_T(sum over slots j in selection order of w[t][j] * y[t][j][r]
-// (+ residual[t][r])); four consecutive outputs per thread.
-template <typename T>
-__global__ void __launch_bounds__(256) g_combine_kernel(const float* ypart, const float* w, const T* residual,
-                                                        int nT, int H, int top_k, T* out) {
+// out[t][r] = sum over the slots j in selection order whose expert is in
+// [e_begin, e_begin + E) of w[t][j] * y[t][j][r] (+ residual[t][r]), rounded once to
+// the output type O (the activation type, or fp32 partial sums for expert-parallel
+// ranks); four consecutive outputs per thread.
+template <typename T, typename O>
+__global__ void __launch_bounds__(256) g_combine_kernel(const float* ypart, const float* w, const int* sel,
+                                                        int e_begin, int E, const T* residual, int nT, int H,
+                                                        int top_k, O* out) {
   const int H4 = H >> 2;
   const size_t idx = (size_t)blockIdx.x * 256 + threadIdx.x;
   if (idx >= (size_t)nT * H4) return;
   const int t = (int)(idx / H4), r4 = (int)(idx - (size_t)t * H4);
   float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int j = 0; j < top_k; ++j) {
+    const unsigned e = (unsigned)(sel[(size_t)t * top_k + j] - e_begin);
+    if (e >= (unsigned)E) continue;
     const float wj = w[(size_t)t * top_k + j];
     const float4 v = __ldcg(reinterpret_cast<const float4*>(ypart + ((size_t)t * top_k + j) * H) + r4);
     s.x = fmaf(wj, v.x, s.x);
@@ -950,13 +964,17 @@ __global__ void __launch_bounds__(256) g_combine_kernel(const float* ypart, cons
     s.z += to_f32<T>(rr[2]);
     s.w += to_f32<T>(rr[3]);
   }
-  uint2 ov;
-  T* oo = reinterpret_cast<T*>(&ov);
-  oo[0] = from_f32<T>(s.x);
-  oo[1] = from_f32<T>(s.y);
-  oo[2] = from_f32<T>(s.z);
-  oo[3] = from_f32<T>(s.w);
-  *reinterpret_cast<uint2*>(out + o) = ov;
+  if constexpr (std::is_same<O, float>::value) {
+    *reinterpret_cast<float4*>(out + o) = s;
+  } else {
+    uint2 ov;
+    O* oo = reinterpret_cast<O*>(&ov);
+    oo[0] = from_f32<O>(s.x);
+    oo[1] = from_f32<O>(s.y);
+    oo[2] = from_f32<O>(s.z);
+    oo[3] = from_f32<O>(s.w);
+    *reinterpret_cast<uint2*>(out + o) = ov;
+  }
 }
 
 // ====================================================================== host side
@@ -974,10 +992,9 @@ static int g_tcap(int T, int E, int top_k) {
   return kGTok;
 }
 
-static GScratch g_scratch(int T, int E, int H, int I, int top_k) {
+static GScratch g_scratch(int T, int E, int H, int I, int top_k, int tcap) {
   GScratch s;
   size_t off = 0;
-  const int tcap = g_tcap(T, E, top_k);
   s.max_units = E + (T * top_k + tcap - 1) / tcap + 1;
   s.logits = off; off += align_up((size_t)T * E * 4, 256);
   s.sel = off; off += align_up((size_t)T * top_k * 4, 256);
@@ -1056,91 +1073,24 @@ static void (*g_down_fn(const TileGeom& tg))(GExpParams) {
   return g_down_kernel<T, S, 0, 1>;
 }
 
-}  // namespace duplex
-
-using namespace duplex;
-
-extern "C" int duplex_moe_grouped_workspace_bytes(int32_t T, int32_t E, int32_t H, int32_t I,
-                                                  int32_t top_k, int32_t group, int has_zeros,
-                                                  size_t* bytes) {
-  if (!bytes || T < 1 || T > kGMaxT || E < 1 || E > kMaxExperts || top_k < 1 ||
-      top_k > kMaxTopK || top_k > E || H < 1 || I < 1)
-    return DUPLEX_ERR_ARG;
-  GExpParams p = {};
-  if (!g_layout(H, I, group, has_zeros, kGTok, &p)) return DUPLEX_ERR_UNSUPPORTED;  // every cap fits
-  *bytes = g_scratch(T, E, H, I, top_k).total;
-  return DUPLEX_OK;
-}
-
-extern "C" int duplex_moe_grouped(const void* x, int act_dtype, int32_t T, const void* gate_w,
-                                  const void* gate_b, const float* logits_in, int32_t E, int32_t H,
-                                  int32_t I, int32_t top_k, int32_t norm_topk, const void* gu_tiles,
-                                  const void* dn_tiles, int scale_dtype, int has_zeros,
-                                  int32_t group, const void* residual, void* out, float* w_out,
-                                  int32_t* sel_out, void* workspace, size_t workspace_bytes,
-                                  int32_t* err, void* stream) {
-  if (!x || !out || !gu_tiles || !dn_tiles || !workspace || (!gate_w && !logits_in)) return DUPLEX_ERR_ARG;
-  if (T < 1 || T > kGMaxT || E < 1 || E > kMaxExperts || top_k < 1 || top_k > kMaxTopK || top_k > E)
-    return DUPLEX_ERR_ARG;
-  if (act_dtype != DUPLEX_DTYPE_F16 && act_dtype != DUPLEX_DTYPE_BF16) return DUPLEX_ERR_DTYPE;
-  if (scale_dtype != act_dtype) return DUPLEX_ERR_DTYPE;
-  GExpParams p = {};
-  if (!g_layout(H, I, group, has_zeros, kGTok, &p)) return DUPLEX_ERR_UNSUPPORTED;
-  const int tcap = g_tcap(T, E, top_k);
-  if (!g_layout(H, I, group, has_zeros, tcap, &p)) return DUPLEX_ERR_UNSUPPORTED;
-  const GScratch L = g_scratch(T, E, H, I, top_k);
-  if (workspace_bytes < L.total) return DUPLEX_ERR_WORKSPACE;
-  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) |
-       reinterpret_cast<uintptr_t>(workspace) | reinterpret_cast<uintptr_t>(gu_tiles) |
-       reinterpret_cast<uintptr_t>(dn_tiles) | reinterpret_cast<uintptr_t>(gate_w) |
-       reinterpret_cast<uintptr_t>(residual) | reinterpret_cast<uintptr_t>(logits_in)) & 15u)
-    return DUPLEX_ERR_ALIGN;
-  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
-  float* logits = logits_in ? const_cast<float*>(logits_in) : reinterpret_cast<float*>(ws + L.logits);
-  int* sel = reinterpret_cast<int*>(ws + L.sel);
-  float* w = reinterpret_cast<float*>(ws + L.w);
-  cudaStream_t st = (cudaStream_t)stream;
-  const bool f16 = act_dtype == DUPLEX_DTYPE_F16;
+// Bucketing, the two expert kernels and the combine, for the assignments in sel [T][k]
+// whose experts are [e_begin, e_begin + E) (tiles indexed from e_begin); out [T][H] in
+// the activation type (out_f32 == 0) or fp32.
+static int g_expert_stage(const void* x, bool f16, int T, const int* sel, const float* w, int top_k, int e_begin,
+                          int E, int E_total, int H, int I, const void* gu_tiles, const void* dn_tiles,
+                          GExpParams& p, const GScratch& L, int tcap, uint8_t* ws, const void* residual, void* out,
+                          int out_f32, int* err, cudaStream_t st) {
   int rc;
-  // 1. router
-  if (!logits_in) {
-    const int smem = g_router_smem(H);
-    void (*rk)(const __half*, const __half*, const __half*, int, int, int, float*, int*) = g_router_kernel<__half>;
-    void (*rkb)(const __nv_bfloat16*, const __nv_bfloat16*, const __nv_bfloat16*, int, int, int, float*, int*) =
-        g_router_kernel<__nv_bfloat16>;
-    const void* fn = f16 ? reinterpret_cast<const void*>(rk) : reinterpret_cast<const void*>(rkb);
-    // the attribute is set once per kernel (to the ceiling), whatever this call's size
-    if (smem > kGSmemMax) return DUPLEX_ERR_UNSUPPORTED;
-    if ((rc = ensure_smem_attr(fn, kGSmemMax))) return rc;
-    const dim3 grid((E + 15) / 16, (T + 15) / 16);
-    if (f16)
-      rk<<<grid, 256, smem, st>>>(reinterpret_cast<const __half*>(x), reinterpret_cast<const __half*>(gate_w),
-                                  reinterpret_cast<const __half*>(gate_b), T, E, H, logits, err);
-    else
-      rkb<<<grid, 256, smem, st>>>(reinterpret_cast<const __nv_bfloat16*>(x),
-                                   reinterpret_cast<const __nv_bfloat16*>(gate_w),
-                                   reinterpret_cast<const __nv_bfloat16*>(gate_b), T, E, H, logits, err);
-    if ((rc = record_cuda(cudaGetLastError()))) return rc;
-  }
-  // 2. top-k
-  if (f16)
-    g_topk_kernel<__half><<<(T + 15) / 16, 512, 0, st>>>(logits, T, E, top_k, norm_topk, sel, w, sel_out, w_out);
-  else
-    g_topk_kernel<__nv_bfloat16><<<(T + 15) / 16, 512, 0, st>>>(logits, T, E, top_k, norm_topk, sel, w, sel_out,
-                                                                w_out);
-  if ((rc = record_cuda(cudaGetLastError()))) return rc;
-  // 3. bucketing
   {
     const int N = T * top_k, nch = (N + 31) / 32;
     const int smem = (int)(align_up((size_t)nch * E, 16) + align_up((size_t)nch * E * 2, 16) +
                            3 * kMaxExperts * 4 + 16 * 4);
     if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(g_bucket_kernel), kGSmemMax))) return rc;
-    g_bucket_kernel<<<1, 512, smem, st>>>(sel, T, E, top_k, tcap, reinterpret_cast<int*>(ws + L.assign),
-                                          reinterpret_cast<int*>(ws + L.units),
+    g_bucket_kernel<<<1, 512, smem, st>>>(sel, T, E, top_k, tcap, e_begin, E_total,
+                                          reinterpret_cast<int*>(ws + L.assign), reinterpret_cast<int*>(ws + L.units),
                                           reinterpret_cast<int*>(ws + L.n_units), L.max_units, err);
     if ((rc = record_cuda(cudaGetLastError()))) return rc;
   }
-  // 4. experts: gate|up, then down, each one CTA per SM
   p.H = H; p.I = I; p.E = E; p.top_k = top_k; p.max_units = L.max_units;
   p.x = reinterpret_cast<const uint8_t*>(x);
   p.gu_tiles = reinterpret_cast<const uint8_t*>(gu_tiles);
@@ -1164,16 +1114,171 @@ extern "C" int duplex_moe_grouped(const void* x, int act_dtype, int32_t T, const
     kd<<<G, kThreads, p.smem_d, st>>>(p);
     if ((rc = record_cuda(cudaGetLastError()))) return rc;
   }
-  // 5. combine
-  const size_t n_out = (size_t)T * H / 4;
-  const unsigned blocks = (unsigned)((n_out + 255) / 256);
-  if (f16)
-    g_combine_kernel<__half><<<blocks, 256, 0, st>>>(reinterpret_cast<const float*>(ws + L.ypart), w,
-                                                      reinterpret_cast<const __half*>(residual), T, H, top_k,
-                                                      reinterpret_cast<__half*>(out));
-  else
-    g_combine_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(reinterpret_cast<const float*>(ws + L.ypart), w,
-                                                             reinterpret_cast<const __nv_bfloat16*>(residual),
-                                                             T, H, top_k, reinterpret_cast<__nv_bfloat16*>(out));
+  const float* yp = reinterpret_cast<const float*>(ws + L.ypart);
+  const unsigned blocks = (unsigned)(((size_t)T * H / 4 + 255) / 256);
+  if (f16) {
+    const __half* res = reinterpret_cast<const __half*>(residual);
+    if (out_f32)
+      g_combine_kernel<__half, float><<<blocks, 256, 0, st>>>(yp, w, sel, e_begin, E, res, T, H, top_k,
+                                                              reinterpret_cast<float*>(out));
+    else
+      g_combine_kernel<__half, __half><<<blocks, 256, 0, st>>>(yp, w, sel, e_begin, E, res, T, H, top_k,
+                                                               reinterpret_cast<__half*>(out));
+  } else {
+    const __nv_bfloat16* res = reinterpret_cast<const __nv_bfloat16*>(residual);
+    if (out_f32)
+      g_combine_kernel<__nv_bfloat16, float><<<blocks, 256, 0, st>>>(yp, w, sel, e_begin, E, res, T, H, top_k,
+                                                                     reinterpret_cast<float*>(out));
+    else
+      g_combine_kernel<__nv_bfloat16, __nv_bfloat16><<<blocks, 256, 0, st>>>(
+          yp, w, sel, e_begin, E, res, T, H, top_k, reinterpret_cast<__nv_bfloat16*>(out));
+  }
   return record_cuda(cudaGetLastError());
+}
+
+// Router logits (unless given) and top-k: sel / w [T][top_k] (and the optional copies
+// sel_out / w_out).
+static int g_route(const void* x, bool f16, int T, const void* gate_w, const void* gate_b, const float* logits_in,
+                   int E, int H, int top_k, int norm_topk, uint8_t* ws, const GScratch& L, int* sel, float* w,
+                   int32_t* sel_out, float* w_out, int* err, cudaStream_t st) {
+  int rc;
+  float* logits = logits_in ? const_cast<float*>(logits_in) : reinterpret_cast<float*>(ws + L.logits);
+  // router
+  if (!logits_in) {
+    const int smem = g_router_smem(H);
+    void (*rk)(const __half*, const __half*, const __half*, int, int, int, float*, int*) = g_router_kernel<__half>;
+    void (*rkb)(const __nv_bfloat16*, const __nv_bfloat16*, const __nv_bfloat16*, int, int, int, float*, int*) =
+        g_router_kernel<__nv_bfloat16>;
+    const void* fn = f16 ? reinterpret_cast<const void*>(rk) : reinterpret_cast<const void*>(rkb);
+    // the attribute is set once per kernel (to the ceiling), whatever this call's size
+    if (smem > kGSmemMax) return DUPLEX_ERR_UNSUPPORTED;
+    if ((rc = ensure_smem_attr(fn, kGSmemMax))) return rc;
+    const dim3 grid((E + 15) / 16, (T + 15) / 16);
+    if (f16)
+      rk<<<grid, 256, smem, st>>>(reinterpret_cast<const __half*>(x), reinterpret_cast<const __half*>(gate_w),
+                                  reinterpret_cast<const __half*>(gate_b), T, E, H, logits, err);
+    else
+      rkb<<<grid, 256, smem, st>>>(reinterpret_cast<const __nv_bfloat16*>(x),
+                                   reinterpret_cast<const __nv_bfloat16*>(gate_w),
+                                   reinterpret_cast<const __nv_bfloat16*>(gate_b), T, E, H, logits, err);
+    if ((rc = record_cuda(cudaGetLastError()))) return rc;
+  }
+  // top-k
+  if (f16)
+    g_topk_kernel<__half><<<(T + 15) / 16, 512, 0, st>>>(logits, T, E, top_k, norm_topk, sel, w, sel_out, w_out);
+  else
+    g_topk_kernel<__nv_bfloat16><<<(T + 15) / 16, 512, 0, st>>>(logits, T, E, top_k, norm_topk, sel, w, sel_out,
+                                                                w_out);
+  if ((rc = record_cuda(cudaGetLastError()))) return rc;
+  return DUPLEX_OK;
+}
+
+static bool g_misaligned(std::initializer_list<const void*> ptrs) {
+  for (const void* q : ptrs)
+    if (reinterpret_cast<uintptr_t>(q) & 15u) return true;
+  return false;
+}
+
+}  // namespace duplex
+
+using namespace duplex;
+
+extern "C" int duplex_moe_grouped_workspace_bytes(int32_t T, int32_t E, int32_t H, int32_t I,
+                                                  int32_t top_k, int32_t group, int has_zeros,
+                                                  size_t* bytes) {
+  if (!bytes || T < 1 || T > kGMaxT || E < 1 || E > kMaxExperts || top_k < 1 ||
+      top_k > kMaxTopK || top_k > E || H < 1 || I < 1)
+    return DUPLEX_ERR_ARG;
+  GExpParams p = {};
+  if (!g_layout(H, I, group, has_zeros, kGTok, &p)) return DUPLEX_ERR_UNSUPPORTED;  // every cap fits
+  *bytes = g_scratch(T, E, H, I, top_k, g_tcap(T, E, top_k)).total;
+  return DUPLEX_OK;
+}
+
+extern "C" int duplex_moe_grouped(const void* x, int act_dtype, int32_t T, const void* gate_w,
+                                  const void* gate_b, const float* logits_in, int32_t E, int32_t H,
+                                  int32_t I, int32_t top_k, int32_t norm_topk, const void* gu_tiles,
+                                  const void* dn_tiles, int scale_dtype, int has_zeros,
+                                  int32_t group, const void* residual, void* out, float* w_out,
+                                  int32_t* sel_out, void* workspace, size_t workspace_bytes,
+                                  int32_t* err, void* stream) {
+  if (!x || !out || !gu_tiles || !dn_tiles || !workspace || (!gate_w && !logits_in)) return DUPLEX_ERR_ARG;
+  if (T < 1 || T > kGMaxT || E < 1 || E > kMaxExperts || top_k < 1 || top_k > kMaxTopK || top_k > E)
+    return DUPLEX_ERR_ARG;
+  if (act_dtype != DUPLEX_DTYPE_F16 && act_dtype != DUPLEX_DTYPE_BF16) return DUPLEX_ERR_DTYPE;
+  if (scale_dtype != act_dtype) return DUPLEX_ERR_DTYPE;
+  GExpParams p = {};
+  if (!g_layout(H, I, group, has_zeros, kGTok, &p)) return DUPLEX_ERR_UNSUPPORTED;
+  const int tcap = g_tcap(T, E, top_k);
+  if (!g_layout(H, I, group, has_zeros, tcap, &p)) return DUPLEX_ERR_UNSUPPORTED;
+  const GScratch L = g_scratch(T, E, H, I, top_k, tcap);
+  if (workspace_bytes < L.total) return DUPLEX_ERR_WORKSPACE;
+  if (g_misaligned({x, out, workspace, gu_tiles, dn_tiles, gate_w, residual, logits_in})) return DUPLEX_ERR_ALIGN;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  int* sel = reinterpret_cast<int*>(ws + L.sel);
+  float* w = reinterpret_cast<float*>(ws + L.w);
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool f16 = act_dtype == DUPLEX_DTYPE_F16;
+  int rc;
+  if ((rc = g_route(x, f16, T, gate_w, gate_b, logits_in, E, H, top_k, norm_topk, ws, L, sel, w, sel_out, w_out,
+                    err, st)))
+    return rc;
+  // 3-5. bucketing, experts, combine
+  return g_expert_stage(x, f16, T, sel, w, top_k, 0, E, E, H, I, gu_tiles, dn_tiles, p, L, tcap, ws, residual, out,
+                        0, err, st);
+}
+
+extern "C" int duplex_moe_experts_grouped_workspace_bytes(int32_t T, int32_t E_local, int32_t E_total,
+                                                          int32_t H, int32_t I, int32_t top_k, int32_t group,
+                                                          int has_zeros, size_t* bytes) {
+  if (!bytes || T < 1 || T > kGMaxT || E_local < 1 || E_total < E_local || E_total > kMaxExperts ||
+      top_k < 1 || top_k > kMaxTopK || top_k > E_total || H < 1 || I < 1)
+    return DUPLEX_ERR_ARG;
+  GExpParams p = {};
+  if (!g_layout(H, I, group, has_zeros, kGTok, &p)) return DUPLEX_ERR_UNSUPPORTED;
+  *bytes = g_scratch(T, E_local, H, I, top_k, g_tcap(T, E_total, top_k)).total;
+  return DUPLEX_OK;
+}
+
+extern "C" int duplex_moe_experts_grouped(const void* x, int act_dtype, int32_t T, const int32_t* sel,
+                                          const float* w, int32_t top_k, int32_t e_begin, int32_t E_local,
+                                          int32_t E_total, int32_t H, int32_t I, const void* gu_tiles,
+                                          const void* dn_tiles, int scale_dtype, int has_zeros, int32_t group,
+                                          const void* residual, void* out, int out_dtype, void* workspace,
+                                          size_t workspace_bytes, int32_t* err, void* stream) {
+  if (!x || !sel || !w || !out || !gu_tiles || !dn_tiles || !workspace) return DUPLEX_ERR_ARG;
+  if (T < 1 || T > kGMaxT || E_local < 1 || e_begin < 0 || e_begin + E_local > E_total ||
+      E_total > kMaxExperts || top_k < 1 || top_k > kMaxTopK || top_k > E_total)
+    return DUPLEX_ERR_ARG;
+  if (act_dtype != DUPLEX_DTYPE_F16 && act_dtype != DUPLEX_DTYPE_BF16) return DUPLEX_ERR_DTYPE;
+  if (scale_dtype != act_dtype) return DUPLEX_ERR_DTYPE;
+  if (out_dtype != act_dtype && out_dtype != DUPLEX_DTYPE_F32) return DUPLEX_ERR_DTYPE;
+  GExpParams p = {};
+  if (!g_layout(H, I, group, has_zeros, kGTok, &p)) return DUPLEX_ERR_UNSUPPORTED;
+  const int tcap = g_tcap(T, E_total, top_k);
+  if (!g_layout(H, I, group, has_zeros, tcap, &p)) return DUPLEX_ERR_UNSUPPORTED;
+  const GScratch L = g_scratch(T, E_local, H, I, top_k, tcap);
+  if (workspace_bytes < L.total) return DUPLEX_ERR_WORKSPACE;
+  if (g_misaligned({x, out, workspace, gu_tiles, dn_tiles, residual})) return DUPLEX_ERR_ALIGN;
+  return g_expert_stage(x, act_dtype == DUPLEX_DTYPE_F16, T, sel, w, top_k, e_begin, E_local, E_total, H, I,
+                        gu_tiles, dn_tiles, p, L, tcap, reinterpret_cast<uint8_t*>(workspace), residual, out,
+                        out_dtype == DUPLEX_DTYPE_F32, err, (cudaStream_t)stream);
+}
+
+extern "C" int duplex_moe_route_grouped(const void* x, int act_dtype, int32_t T, const void* gate_w,
+                                        const void* gate_b, const float* logits_in, int32_t E, int32_t H,
+                                        int32_t top_k, int32_t norm_topk, float* w_out, int32_t* sel_out,
+                                        void* workspace, size_t workspace_bytes, int32_t* err, void* stream) {
+  if (!x || !w_out || !sel_out || !workspace || (!gate_w && !logits_in)) return DUPLEX_ERR_ARG;
+  if (T < 1 || T > kGMaxT || E < 1 || E > kMaxExperts || top_k < 1 || top_k > kMaxTopK || top_k > E)
+    return DUPLEX_ERR_ARG;
+  if (act_dtype != DUPLEX_DTYPE_F16 && act_dtype != DUPLEX_DTYPE_BF16) return DUPLEX_ERR_DTYPE;
+  if (H < 8 || (H & 7)) return DUPLEX_ERR_UNSUPPORTED;
+  if (g_router_smem(H) > kGSmemMax) return DUPLEX_ERR_UNSUPPORTED;
+  const GScratch L = g_scratch(T, E, H, 64, top_k, 8);
+  if (workspace_bytes < L.logits + (size_t)T * E * 4) return DUPLEX_ERR_WORKSPACE;
+  if (g_misaligned({x, gate_w, logits_in, workspace})) return DUPLEX_ERR_ALIGN;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  return g_route(x, act_dtype == DUPLEX_DTYPE_F16, T, gate_w, gate_b, logits_in, E, H, top_k, norm_topk, ws, L,
+                 sel_out, w_out, nullptr, nullptr, err, (cudaStream_t)stream);
 }

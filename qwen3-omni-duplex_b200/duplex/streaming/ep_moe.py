@@ -1,0 +1,156 @@
+"""Expert-parallel Thinker MoE: one layer's 128 experts sharded over the ranks of a
+process group (one process per GPU), tokens data-parallel.
+
+The reference runs every expert on one GPU (`src/duplex/streaming/fused_packed_moe.py`);
+this is the multi-GPU form of the same layer, `FusedPackedMoE.forward` semantics per
+token, for batched decode (many streams per rank):
+
+  1. route the rank's own tokens over all E experts (router logits, fp32 softmax,
+     top-k, renormalise: `duplex_moe_route_grouped`);
+  2. exchange: all-gather of the tokens and of their (expert, weight) selections, so
+     that every rank sees every token that may pick one of its experts;
+  3. the rank's experts [rank * E/N, (rank + 1) * E/N) on all gathered tokens, one fp32
+     partial sum per token over the slots that hit them (`duplex_moe_experts_grouped`);
+  4. exchange back: reduce-scatter (sum) of the fp32 partials, so each token's owner
+     receives the sum over ranks; then + residual, one rounding to the activation type.
+
+Both exchanges are NCCL collectives of fixed size (N * T_local rows), so no host
+synchronisation is needed and the layer can be captured in a CUDA graph.  The host
+logic lives in `ep_forward`, which takes the routing and expert steps as callables: the
+module passes the sm_100a kernels; the multi-rank CPU tests pass the numpy oracle.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from duplex import _lib
+from duplex.streaming.triton_dequant_gemv import Int4Tiles
+
+PACK = 8
+
+
+def ep_forward(x, route_fn, experts_fn, top_k: int, group=None, residual=None, out_dtype=None):
+    """Host side of one expert-parallel layer on this rank.
+
+    x [T_local, H]; route_fn(x) -> (w [T_local, k] fp32, sel [T_local, k] int32);
+    experts_fn(x_all, sel_all, w_all) -> fp32 [N * T_local, H]: this rank's experts'
+    weighted sum per gathered token (zero where none of its experts is selected).
+    Returns [T_local, H] in out_dtype (default x.dtype).
+    """
+    world = dist.get_world_size(group)
+    T_l, H = x.shape
+    w, sel = route_fn(x)
+    x_all = torch.empty(world * T_l, H, dtype=x.dtype, device=x.device)
+    dist.all_gather_into_tensor(x_all, x.contiguous(), group=group)
+    meta = torch.cat([sel.to(torch.int32), w.to(torch.float32).view(torch.int32)], dim=1).contiguous()
+    meta_all = torch.empty(world * T_l, 2 * top_k, dtype=torch.int32, device=x.device)
+    dist.all_gather_into_tensor(meta_all, meta, group=group)
+    sel_all = meta_all[:, :top_k].contiguous()
+    w_all = meta_all[:, top_k:].contiguous().view(torch.float32)
+    partial = experts_fn(x_all, sel_all, w_all)
+    red = torch.empty(T_l, H, dtype=torch.float32, device=x.device)
+    dist.reduce_scatter_tensor(red, partial.contiguous(), op=dist.ReduceOp.SUM, group=group)
+    if residual is not None:
+        red += residual.to(torch.float32)
+    return red.to(out_dtype or x.dtype)
+
+
+class ExpertParallelMoE(nn.Module):
+    """One MoE layer whose experts are split evenly over the ranks of `group`.
+
+    Built from the full stacked tensors (`FusedPackedMoE.from_stacked` layout: gate
+    [E, H], gate|up packed [E, 2I, H/8] + scales [E, 2I, G] (+ zeros), down packed
+    [E, H, I/8] + scales [E, H, G'] (+ zeros)); every rank keeps the router and its own
+    E/N experts (repacked once into tile records).  forward(x [T_local, H]) returns the
+    layer output for this rank's tokens; N * T_local <= 512.
+    """
+
+    def __init__(self, gate_weight, gu_packed, gu_scale, dn_packed, dn_scale, top_k,
+                 gu_zeros=None, dn_zeros=None, norm_topk_prob=True, gate_bias=None,
+                 dtype=torch.float16, device="cuda", group=None):
+        super().__init__()
+        if dtype not in (torch.float16, torch.bfloat16):
+            raise _lib.DuplexError("ExpertParallelMoE runs fp16 or bf16 modules")
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        E, H = gate_weight.shape
+        if E % self.world:
+            raise _lib.DuplexError(f"{E} experts do not split evenly over {self.world} ranks")
+        self.num_experts, self.hidden, self.top_k = E, H, top_k
+        self.norm_topk_prob = norm_topk_prob
+        self.E_local = E // self.world
+        self.e_begin = self.rank * self.E_local
+        sl = slice(self.e_begin, self.e_begin + self.E_local)
+        self.gate = nn.Linear(H, E, bias=gate_bias is not None).to(device=device, dtype=dtype)
+        with torch.no_grad():
+            self.gate.weight.copy_(gate_weight)
+            if gate_bias is not None:
+                self.gate.bias.copy_(gate_bias)
+        self.inter = gu_packed.shape[1] // 2
+        G = gu_scale.shape[-1]
+        self.group_size = -(-H // G)
+        self.has_zeros = gu_zeros is not None
+        self.gu_tiles = Int4Tiles(gu_packed[sl].to(device), gu_scale[sl].to(device, dtype),
+                                  None if gu_zeros is None else gu_zeros[sl].to(device),
+                                  group=self.group_size, K=H, pair_halves=True)
+        self.dn_tiles = Int4Tiles(dn_packed[sl].to(device), dn_scale[sl].to(device, dtype),
+                                  None if dn_zeros is None else dn_zeros[sl].to(device),
+                                  group=self.group_size, K=dn_packed.shape[2] * PACK)
+        self.register_buffer("err", torch.zeros(1, dtype=torch.int32, device=device), persistent=False)
+        self._ws = {}
+
+    def _workspace(self, key, nbytes_fn, device):
+        ws = self._ws.get(key)
+        if ws is None:
+            n = _lib.ctypes.c_size_t()
+            nbytes_fn(_lib.ctypes.byref(n))
+            ws = torch.empty(max(n.value, 16), dtype=torch.uint8, device=device)
+            self._ws[key] = ws
+        return ws
+
+    def route(self, x):
+        """(w [T, k] fp32, sel [T, k] int32) over all experts, for this rank's tokens."""
+        T = x.shape[0]
+        w = torch.empty(T, self.top_k, dtype=torch.float32, device=x.device)
+        sel = torch.empty(T, self.top_k, dtype=torch.int32, device=x.device)
+        ws = self._ws.get(("route", T))
+        if ws is None:
+            ws = torch.empty(T * self.num_experts * 4, dtype=torch.uint8, device=x.device)
+            self._ws[("route", T)] = ws
+        g = self.gate
+        _lib.call("duplex_moe_route_grouped", _lib.ptr(x), _lib.dtype_code(x.dtype), T,
+                  _lib.ptr(g.weight), _lib.ptr(g.bias), None, self.num_experts, self.hidden,
+                  self.top_k, 1 if self.norm_topk_prob else 0, _lib.ptr(w), _lib.ptr(sel),
+                  _lib.ptr(ws), ws.numel(), _lib.ptr(self.err), _lib.stream_of(x))
+        return w, sel
+
+    def local_experts(self, x_all, sel_all, w_all):
+        """fp32 [T_all, H]: this rank's experts' weighted sums for the gathered tokens."""
+        T = x_all.shape[0]
+        out = torch.empty(T, self.hidden, dtype=torch.float32, device=x_all.device)
+        ws = self._workspace(("experts", T), lambda p: _lib.call(
+            "duplex_moe_experts_grouped_workspace_bytes", T, self.E_local, self.num_experts,
+            self.hidden, self.inter, self.top_k, self.group_size, 1 if self.has_zeros else 0, p),
+            x_all.device)
+        _lib.call("duplex_moe_experts_grouped", _lib.ptr(x_all), _lib.dtype_code(x_all.dtype), T,
+                  _lib.ptr(sel_all), _lib.ptr(w_all), self.top_k, self.e_begin, self.E_local,
+                  self.num_experts, self.hidden, self.inter, _lib.ptr(self.gu_tiles.buf),
+                  _lib.ptr(self.dn_tiles.buf), self.gu_tiles.scale_code,
+                  1 if self.has_zeros else 0, self.group_size, None, _lib.ptr(out),
+                  _lib.DTYPE_F32, _lib.ptr(ws), ws.numel(), _lib.ptr(self.err),
+                  _lib.stream_of(x_all))
+        return out
+
+    def forward(self, x, residual=None):
+        _lib.require_cuda(x)
+        x = _lib.aligned(x.to(self.gate.weight.dtype))
+        return ep_forward(x, self.route, self.local_experts, self.top_k, self.group, residual)
+
+    def device_errors(self) -> int:
+        v = int(self.err.item())
+        self.err.zero_()
+        return v

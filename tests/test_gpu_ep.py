@@ -1,0 +1,188 @@
+"""GPU checks of the expert-parallel pieces: duplex_moe_experts_grouped on expert shards
+(partial sums over shards = the whole layer), the route-only entry point, and the
+ExpertParallelMoE module over NCCL (one rank here; two ranks when two GPUs are present).
+"""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from duplex import _lib, synth
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+
+
+def T(a, dev, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    return t if dtype is None else t.to(dtype)
+
+
+def rel_err(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return np.abs(a - b).max() / max(np.abs(b).max(), 1e-30)
+
+
+def _layer(cuda, seed, E, H, I, k, Tn, group=128):
+    from duplex.streaming.fused_packed_moe import FusedPackedMoE
+    L = synth.moe_layer_np(seed=seed, E=E, H=H, I=I, top_k=k, group=group, zero_points=True, T=Tn)
+    x = O.round_to(L["x"].astype(np.float32), "float16")
+    m = FusedPackedMoE.from_stacked(T(L["gate_w"], cuda), T(L["gu_packed"], cuda), T(L["gu_scale"], cuda),
+                                    T(L["dn_packed"], cuda), T(L["dn_scale"], cuda), k,
+                                    gu_zeros=T(L["gu_zeros"], cuda), dn_zeros=T(L["dn_zeros"], cuda),
+                                    dtype=torch.float16)
+    return L, m, x
+
+
+def _shard_partial(cuda, L, m, x_t, sel, w, e0, n_loc, out_dtype=torch.float32, residual=None):
+    from duplex.streaming.triton_dequant_gemv import Int4Tiles
+    sl = slice(e0, e0 + n_loc)
+    H = x_t.shape[1]
+    gu = Int4Tiles(T(L["gu_packed"][sl], cuda), T(L["gu_scale"][sl], cuda, torch.float16),
+                   T(L["gu_zeros"][sl], cuda), group=m.group, K=H, pair_halves=True)
+    dn = Int4Tiles(T(L["dn_packed"][sl], cuda), T(L["dn_scale"][sl], cuda, torch.float16),
+                   T(L["dn_zeros"][sl], cuda), group=m.group, K=m.inter)
+    Tn, k = sel.shape
+    n = _lib.ctypes.c_size_t()
+    _lib.call("duplex_moe_experts_grouped_workspace_bytes", Tn, n_loc, m.num_experts, H, m.inter, k,
+              m.group, 1, _lib.ctypes.byref(n))
+    ws = torch.empty(n.value, dtype=torch.uint8, device=cuda)
+    out = torch.empty(Tn, H, dtype=out_dtype, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    _lib.call("duplex_moe_experts_grouped", _lib.ptr(x_t), _lib.DTYPE_F16, Tn, _lib.ptr(sel), _lib.ptr(w), k,
+              e0, n_loc, m.num_experts, H, m.inter, _lib.ptr(gu.buf), _lib.ptr(dn.buf), gu.scale_code, 1,
+              m.group, _lib.ptr(residual), _lib.ptr(out), _lib.dtype_code(out_dtype), _lib.ptr(ws),
+              ws.numel(), _lib.ptr(err), _lib.stream_of(x_t))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    return out
+
+
+@pytest.mark.parametrize("shards", [2, 4, 8])
+def test_expert_shards_sum_to_the_layer(cuda, shards):
+    """Config 4 geometry (128 experts, top-8): the fp32 partial sums of `shards`
+    expert shards, added in rank order, give the whole layer."""
+    L, m, x = _layer(cuda, 40 + shards, 128, 2048, 768, 8, 64)
+    x_t = T(x, cuda, torch.float16)
+    Tn = x.shape[0]
+    out_full = torch.empty(Tn, 2048, dtype=torch.float16, device=cuda)
+    w = torch.empty(Tn, 8, dtype=torch.float32, device=cuda)
+    sel = torch.empty(Tn, 8, dtype=torch.int32, device=cuda)
+    m.forward_grouped_into(x_t, out_full, w_out=w, sel_out=sel)
+    total = torch.zeros(Tn, 2048, dtype=torch.float32, device=cuda)
+    n_loc = 128 // shards
+    for r in range(shards):
+        total += _shard_partial(cuda, L, m, x_t, sel, w, r * n_loc, n_loc)
+    ref = O.moe_experts_by_expert(x, sel.cpu().numpy(), w.cpu().numpy(), L["gu_packed"], L["gu_scale"],
+                                  L["dn_packed"], L["dn_scale"], L["gu_zeros"], L["dn_zeros"])
+    assert rel_err(total.cpu().numpy(), ref) <= TOL
+    assert rel_err(total.cpu().numpy(), out_full.float().cpu().numpy()) <= 1e-3
+
+
+def test_all_local_shard_is_the_grouped_layer_bit_for_bit(cuda):
+    """One shard holding every expert, fp16 out + residual: the same kernels in the same
+    order as duplex_moe_grouped, so the same bits."""
+    L, m, x = _layer(cuda, 50, 32, 512, 256, 4, 100)
+    x_t = T(x, cuda, torch.float16)
+    Tn = x.shape[0]
+    res = T(O.round_to(np.random.default_rng(3).standard_normal((Tn, 512)), "float16"), cuda, torch.float16)
+    out_full = torch.empty(Tn, 512, dtype=torch.float16, device=cuda)
+    w = torch.empty(Tn, 4, dtype=torch.float32, device=cuda)
+    sel = torch.empty(Tn, 4, dtype=torch.int32, device=cuda)
+    m.forward_grouped_into(x_t, out_full, residual=res, w_out=w, sel_out=sel)
+    torch.cuda.synchronize()
+    out = _shard_partial(cuda, L, m, x_t, sel, w, 0, 32, out_dtype=torch.float16, residual=res)
+    assert torch.equal(out, out_full)
+
+
+def test_route_grouped_matches_the_grouped_layer_routing(cuda):
+    L, m, x = _layer(cuda, 51, 128, 2048, 768, 8, 200)
+    x_t = T(x, cuda, torch.float16)
+    Tn = x.shape[0]
+    out_full = torch.empty(Tn, 2048, dtype=torch.float16, device=cuda)
+    w = torch.empty(Tn, 8, dtype=torch.float32, device=cuda)
+    sel = torch.empty(Tn, 8, dtype=torch.int32, device=cuda)
+    m.forward_grouped_into(x_t, out_full, w_out=w, sel_out=sel)
+    w2 = torch.empty_like(w)
+    sel2 = torch.empty_like(sel)
+    ws = torch.empty(Tn * 128 * 4, dtype=torch.uint8, device=cuda)
+    g = m.gate
+    _lib.call("duplex_moe_route_grouped", _lib.ptr(x_t), _lib.DTYPE_F16, Tn, _lib.ptr(g.weight), None, None,
+              128, 2048, 8, 1, _lib.ptr(w2), _lib.ptr(sel2), _lib.ptr(ws), ws.numel(), None,
+              _lib.stream_of(x_t))
+    torch.cuda.synchronize()
+    assert torch.equal(sel, sel2) and torch.equal(w, w2)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _ep_rank(rank, world, port, q, T_l):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+
+    import torch.distributed as dist
+    from duplex.streaming.ep_moe import ExpertParallelMoE
+    from duplex.streaming.fused_packed_moe import FusedPackedMoE
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    L = synth.moe_layer_np(seed=60, E=128, H=2048, I=768, top_k=8, group=128, zero_points=True,
+                           T=world * T_l)
+    x_full = O.round_to(L["x"].astype(np.float32), "float16")
+    args = [T(L[n], dev) for n in ("gate_w", "gu_packed", "gu_scale", "dn_packed", "dn_scale")]
+    ep = ExpertParallelMoE(*args, 8, gu_zeros=T(L["gu_zeros"], dev), dn_zeros=T(L["dn_zeros"], dev),
+                           dtype=torch.float16, device=dev)
+    x = T(x_full[rank * T_l:(rank + 1) * T_l], dev, torch.float16)
+    y = ep(x)
+    torch.cuda.synchronize()
+    full = FusedPackedMoE.from_stacked(*args, 8, gu_zeros=T(L["gu_zeros"], dev), dn_zeros=T(L["dn_zeros"], dev),
+                                       dtype=torch.float16, device=dev)
+    y_ref = torch.empty(world * T_l, 2048, dtype=torch.float16, device=dev)
+    full.forward_grouped_into(T(x_full, dev, torch.float16), y_ref)
+    torch.cuda.synchronize()
+    err = rel_err(y.float().cpu().numpy(), y_ref[rank * T_l:(rank + 1) * T_l].float().cpu().numpy())
+    q.put((rank, err, ep.device_errors()))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _run_ranks(world, T_l):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_ep_rank, args=(r, world, port, q, T_l)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = sorted(q.get(timeout=300) for _ in ps)
+    for p in ps:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return res
+
+
+def test_expert_parallel_module_one_rank(cuda):
+    """NCCL group of one: the module's exchange degenerates to copies; the output equals
+    the single-GPU grouped layer within the fp32 summation-order bar."""
+    for rank, err, derr in _run_ranks(1, 64):
+        assert err <= 1e-3 and derr == 0
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_expert_parallel_module_two_ranks(cuda):
+    """Two GPUs, 64 experts each, 32 streams per rank (no multicast loads anywhere)."""
+    for rank, err, derr in _run_ranks(2, 32):
+        assert err <= 1e-3 and derr == 0

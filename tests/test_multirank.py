@@ -44,3 +44,64 @@ def test_max_over_ranks_gloo():
 def test_max_over_ranks_without_group():
     from duplex import benchutil as bu
     assert bu.max_over_ranks(3.5) == 3.5
+
+
+# ------------------------------------------------------------------ expert parallelism
+def _ep_worker(rank, ws, port, q):
+    """One rank of the expert-parallel layer's host logic (ep_forward) on CPU/gloo, with
+    the numpy oracle as the routing and local-expert steps."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(ws),
+                      RANK=str(rank), LOCAL_RANK=str(rank))
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import oracle as O
+    from duplex import synth
+    from duplex.streaming.ep_moe import ep_forward
+
+    dist.init_process_group("gloo", rank=rank, world_size=ws)
+    E, H, I, k, T_l = 8, 64, 64, 3, 5
+    L = synth.moe_layer_np(seed=21, E=E, H=H, I=I, top_k=k, group=64, zero_points=True, T=ws * T_l)
+    x_full = L["x"].astype(np.float32)
+    x = torch.from_numpy(x_full[rank * T_l:(rank + 1) * T_l].copy())
+    e0, e1 = rank * (E // ws), (rank + 1) * (E // ws)
+    res = torch.from_numpy(np.random.default_rng(rank).standard_normal((T_l, H)).astype(np.float32))
+
+    def route_fn(xt):
+        w, sel, _ = O.router(xt.numpy(), L["gate_w"], k, True, None, "float32")
+        return torch.from_numpy(w), torch.from_numpy(sel.astype(np.int32))
+
+    def experts_fn(x_all, sel_all, w_all):
+        s = sel_all.numpy()
+        w = np.where((s >= e0) & (s < e1), w_all.numpy(), 0.0).astype(np.float32)
+        y = O.moe_experts_by_expert(x_all.numpy(), s, w, L["gu_packed"], L["gu_scale"],
+                                    L["dn_packed"], L["dn_scale"], L["gu_zeros"], L["dn_zeros"])
+        return torch.from_numpy(y)
+
+    out = ep_forward(x, route_fn, experts_fn, k, residual=res, out_dtype=torch.float32)
+    w_ref, sel_ref, _ = O.router(x_full, L["gate_w"], k, True, None, "float32")
+    ref = O.moe_experts_by_expert(x_full, sel_ref, w_ref, L["gu_packed"], L["gu_scale"],
+                                  L["dn_packed"], L["dn_scale"], L["gu_zeros"], L["dn_zeros"])
+    ref = ref[rank * T_l:(rank + 1) * T_l] + res.numpy()
+    err = float(np.abs(out.numpy() - ref).max() / np.abs(ref).max())
+    q.put((rank, err, tuple(out.shape)))
+    dist.destroy_process_group()
+
+
+def test_expert_parallel_host_logic_gloo():
+    """Two ranks, four experts each: gathered routing, local experts, reduce-scatter of
+    the partial sums give each rank the single-process layer output for its tokens."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_ep_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted(q.get(timeout=180) for _ in ps)
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, err, shape in res:
+        assert shape == (5, 64)
+        assert err < 1e-5, (rank, err)
