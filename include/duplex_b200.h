@@ -216,15 +216,18 @@ int duplex_moe_route_grouped(const void* x, int act_dtype, int32_t T, const void
  * order (+ residual[t]), rounded once to out_dtype (the act dtype, or DUPLEX_DTYPE_F32 for
  * partial sums that other ranks' partials are added to).  Slots of other ranks'
  * experts are skipped; ids outside [0, E_total) set DUPLEX_DEVERR_EXPERT and are
- * skipped.  sel [T][top_k] int32, w [T][top_k] fp32 (device).  T <= 512; the unit token
+ * skipped.  x: T rows x_row_stride elements apart (>= H, a multiple of 8: token rows
+ * packed with other per-token data, as an expert-parallel exchange delivers them).
+ * sel [T][top_k] int32, w [T][top_k] fp32 (device).  T <= 512; the unit token
  * cap is chosen from T * top_k / E_total.  Other arguments and limits as
  * duplex_moe_grouped; workspace: duplex_moe_experts_grouped_workspace_bytes.
  */
 int duplex_moe_experts_grouped_workspace_bytes(int32_t T, int32_t E_local, int32_t E_total,
                                                int32_t H, int32_t I, int32_t top_k,
                                                int32_t group, int has_zeros, size_t* bytes);
-int duplex_moe_experts_grouped(const void* x, int act_dtype, int32_t T, const int32_t* sel,
-                               const float* w, int32_t top_k, int32_t e_begin, int32_t E_local,
+int duplex_moe_experts_grouped(const void* x, int act_dtype, int32_t T, int64_t x_row_stride,
+                               const int32_t* sel, const float* w, int32_t top_k, int32_t e_begin,
+                               int32_t E_local,
                                int32_t E_total, int32_t H, int32_t I, const void* gu_tiles,
                                const void* dn_tiles, int scale_dtype, int has_zeros,
                                int32_t group, const void* residual, void* out, int out_dtype,

@@ -313,6 +313,7 @@ struct GExpParams {
   int red_floats;  // one warp group's partials: 8 warps x ceil(tcap / 8) blocks x 128
   TileGeom tgu, tdn;
   const uint8_t* x;
+  size_t x_row_bytes;  // token rows of x this many bytes apart (2 H when packed)
   const uint8_t* gu_tiles;
   const uint8_t* dn_tiles;
   const int* assign;
@@ -737,7 +738,7 @@ __global__ void __launch_bounds__(kThreads, 1) g_gateup_kernel(const __grid_cons
         const int idx = base0 + k * kConsumers + tid;
         if (idx < total) {
           const int rr = idx / nq, q = idx - rr * nq;
-          ld[k] = __ldg(reinterpret_cast<const uint4*>(p.x + (size_t)tok[rr] * H * 2) + q);
+          ld[k] = __ldg(reinterpret_cast<const uint4*>(p.x + (size_t)tok[rr] * p.x_row_bytes) + q);
         }
       }
 #pragma unroll
@@ -1076,7 +1077,8 @@ static void (*g_down_fn(const TileGeom& tg))(GExpParams) {
 // Bucketing, the two expert kernels and the combine, for the assignments in sel [T][k]
 // whose experts are [e_begin, e_begin + E) (tiles indexed from e_begin); out [T][H] in
 // the activation type (out_f32 == 0) or fp32.
-static int g_expert_stage(const void* x, bool f16, int T, const int* sel, const float* w, int top_k, int e_begin,
+static int g_expert_stage(const void* x, size_t x_row_bytes, bool f16, int T, const int* sel, const float* w,
+                          int top_k, int e_begin,
                           int E, int E_total, int H, int I, const void* gu_tiles, const void* dn_tiles,
                           GExpParams& p, const GScratch& L, int tcap, uint8_t* ws, const void* residual, void* out,
                           int out_f32, int* err, cudaStream_t st) {
@@ -1093,6 +1095,7 @@ static int g_expert_stage(const void* x, bool f16, int T, const int* sel, const 
   }
   p.H = H; p.I = I; p.E = E; p.top_k = top_k; p.max_units = L.max_units;
   p.x = reinterpret_cast<const uint8_t*>(x);
+  p.x_row_bytes = x_row_bytes;
   p.gu_tiles = reinterpret_cast<const uint8_t*>(gu_tiles);
   p.dn_tiles = reinterpret_cast<const uint8_t*>(dn_tiles);
   p.assign = reinterpret_cast<const int*>(ws + L.assign);
@@ -1224,8 +1227,8 @@ extern "C" int duplex_moe_grouped(const void* x, int act_dtype, int32_t T, const
                     err, st)))
     return rc;
   // 3-5. bucketing, experts, combine
-  return g_expert_stage(x, f16, T, sel, w, top_k, 0, E, E, H, I, gu_tiles, dn_tiles, p, L, tcap, ws, residual, out,
-                        0, err, st);
+  return g_expert_stage(x, (size_t)H * 2, f16, T, sel, w, top_k, 0, E, E, H, I, gu_tiles, dn_tiles, p, L, tcap, ws,
+                        residual, out, 0, err, st);
 }
 
 extern "C" int duplex_moe_experts_grouped_workspace_bytes(int32_t T, int32_t E_local, int32_t E_total,
@@ -1240,8 +1243,9 @@ extern "C" int duplex_moe_experts_grouped_workspace_bytes(int32_t T, int32_t E_l
   return DUPLEX_OK;
 }
 
-extern "C" int duplex_moe_experts_grouped(const void* x, int act_dtype, int32_t T, const int32_t* sel,
-                                          const float* w, int32_t top_k, int32_t e_begin, int32_t E_local,
+extern "C" int duplex_moe_experts_grouped(const void* x, int act_dtype, int32_t T, int64_t x_row_stride,
+                                          const int32_t* sel, const float* w, int32_t top_k, int32_t e_begin,
+                                          int32_t E_local,
                                           int32_t E_total, int32_t H, int32_t I, const void* gu_tiles,
                                           const void* dn_tiles, int scale_dtype, int has_zeros, int32_t group,
                                           const void* residual, void* out, int out_dtype, void* workspace,
@@ -1259,8 +1263,10 @@ extern "C" int duplex_moe_experts_grouped(const void* x, int act_dtype, int32_t 
   if (!g_layout(H, I, group, has_zeros, tcap, &p)) return DUPLEX_ERR_UNSUPPORTED;
   const GScratch L = g_scratch(T, E_local, H, I, top_k, tcap);
   if (workspace_bytes < L.total) return DUPLEX_ERR_WORKSPACE;
+  if (x_row_stride < H || (x_row_stride & 7)) return DUPLEX_ERR_ALIGN;
   if (g_misaligned({x, out, workspace, gu_tiles, dn_tiles, residual})) return DUPLEX_ERR_ALIGN;
-  return g_expert_stage(x, act_dtype == DUPLEX_DTYPE_F16, T, sel, w, top_k, e_begin, E_local, E_total, H, I,
+  return g_expert_stage(x, (size_t)x_row_stride * 2, act_dtype == DUPLEX_DTYPE_F16, T, sel, w, top_k, e_begin,
+                        E_local, E_total, H, I,
                         gu_tiles, dn_tiles, p, L, tcap, reinterpret_cast<uint8_t*>(workspace), residual, out,
                         out_dtype == DUPLEX_DTYPE_F32, err, (cudaStream_t)stream);
 }

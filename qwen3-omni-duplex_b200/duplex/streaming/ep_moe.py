@@ -7,8 +7,8 @@ token, for batched decode (many streams per rank):
 
   1. route the rank's own tokens over all E experts (router logits, fp32 softmax,
      top-k, renormalise: `duplex_moe_route_grouped`);
-  2. exchange: all-gather of the tokens and of their (expert, weight) selections, so
-     that every rank sees every token that may pick one of its experts;
+  2. exchange: one all-gather of the tokens packed with their (expert, weight)
+     selections, so that every rank sees every token that may pick one of its experts;
   3. the rank's experts [rank * E/N, (rank + 1) * E/N) on all gathered tokens, one fp32
      partial sum per token over the slots that hit them (`duplex_moe_experts_grouped`);
   4. exchange back: reduce-scatter (sum) of the fp32 partials, so each token's owner
@@ -37,19 +37,26 @@ def ep_forward(x, route_fn, experts_fn, top_k: int, group=None, residual=None, o
 
     x [T_local, H]; route_fn(x) -> (w [T_local, k] fp32, sel [T_local, k] int32);
     experts_fn(x_all, sel_all, w_all) -> fp32 [N * T_local, H]: this rank's experts'
-    weighted sum per gathered token (zero where none of its experts is selected).
-    Returns [T_local, H] in out_dtype (default x.dtype).
+    weighted sum per gathered token (zero where none of its experts is selected); x_all
+    may be a row-strided view.  Returns [T_local, H] in out_dtype (default x.dtype).
+
+    The tokens and their selections travel in ONE all-gather: each row packs the token
+    (2 H bytes for 16-bit activations), its k expert ids and its k weights.
     """
     world = dist.get_world_size(group)
     T_l, H = x.shape
     w, sel = route_fn(x)
-    x_all = torch.empty(world * T_l, H, dtype=x.dtype, device=x.device)
-    dist.all_gather_into_tensor(x_all, x.contiguous(), group=group)
-    meta = torch.cat([sel.to(torch.int32), w.to(torch.float32).view(torch.int32)], dim=1).contiguous()
-    meta_all = torch.empty(world * T_l, 2 * top_k, dtype=torch.int32, device=x.device)
-    dist.all_gather_into_tensor(meta_all, meta, group=group)
-    sel_all = meta_all[:, :top_k].contiguous()
-    w_all = meta_all[:, top_k:].contiguous().view(torch.float32)
+    xb = x.contiguous().view(torch.uint8)                      # [T_l, H * elt]
+    row = xb.shape[1] + 8 * top_k
+    pack = torch.empty(T_l, row, dtype=torch.uint8, device=x.device)
+    pack[:, :xb.shape[1]] = xb
+    pack[:, xb.shape[1]:xb.shape[1] + 4 * top_k] = sel.to(torch.int32).contiguous().view(torch.uint8)
+    pack[:, xb.shape[1] + 4 * top_k:] = w.to(torch.float32).contiguous().view(torch.uint8)
+    pall = torch.empty(world * T_l, row, dtype=torch.uint8, device=x.device)
+    dist.all_gather_into_tensor(pall, pack, group=group)
+    x_all = pall.view(x.dtype)[:, :H]                          # rows `row` bytes apart
+    sel_all = pall[:, xb.shape[1]:xb.shape[1] + 4 * top_k].contiguous().view(torch.int32)
+    w_all = pall[:, xb.shape[1] + 4 * top_k:].contiguous().view(torch.float32)
     partial = experts_fn(x_all, sel_all, w_all)
     red = torch.empty(T_l, H, dtype=torch.float32, device=x.device)
     dist.reduce_scatter_tensor(red, partial.contiguous(), op=dist.ReduceOp.SUM, group=group)
@@ -136,8 +143,11 @@ class ExpertParallelMoE(nn.Module):
             "duplex_moe_experts_grouped_workspace_bytes", T, self.E_local, self.num_experts,
             self.hidden, self.inter, self.top_k, self.group_size, 1 if self.has_zeros else 0, p),
             x_all.device)
+        if x_all.stride(1) != 1 or x_all.data_ptr() % 16:
+            raise _lib.DuplexError("token rows must be contiguous and 16-byte aligned")
         _lib.call("duplex_moe_experts_grouped", _lib.ptr(x_all), _lib.dtype_code(x_all.dtype), T,
-                  _lib.ptr(sel_all), _lib.ptr(w_all), self.top_k, self.e_begin, self.E_local,
+                  x_all.stride(0), _lib.ptr(sel_all), _lib.ptr(w_all), self.top_k, self.e_begin,
+                  self.E_local,
                   self.num_experts, self.hidden, self.inter, _lib.ptr(self.gu_tiles.buf),
                   _lib.ptr(self.dn_tiles.buf), self.gu_tiles.scale_code,
                   1 if self.has_zeros else 0, self.group_size, None, _lib.ptr(out),

@@ -55,8 +55,9 @@ def _shard_partial(cuda, L, m, x_t, sel, w, e0, n_loc, out_dtype=torch.float32, 
     ws = torch.empty(n.value, dtype=torch.uint8, device=cuda)
     out = torch.empty(Tn, H, dtype=out_dtype, device=cuda)
     err = torch.zeros(1, dtype=torch.int32, device=cuda)
-    _lib.call("duplex_moe_experts_grouped", _lib.ptr(x_t), _lib.DTYPE_F16, Tn, _lib.ptr(sel), _lib.ptr(w), k,
-              e0, n_loc, m.num_experts, H, m.inter, _lib.ptr(gu.buf), _lib.ptr(dn.buf), gu.scale_code, 1,
+    _lib.call("duplex_moe_experts_grouped", _lib.ptr(x_t), _lib.DTYPE_F16, Tn, H, _lib.ptr(sel),
+              _lib.ptr(w), k, e0, n_loc, m.num_experts, H, m.inter, _lib.ptr(gu.buf), _lib.ptr(dn.buf),
+              gu.scale_code, 1,
               m.group, _lib.ptr(residual), _lib.ptr(out), _lib.dtype_code(out_dtype), _lib.ptr(ws),
               ws.numel(), _lib.ptr(err), _lib.stream_of(x_t))
     torch.cuda.synchronize()
