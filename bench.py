@@ -42,6 +42,9 @@ for _p in (str(ROOT), str(ROOT / "qwen3-omni-duplex_b200")):
 METRIC = ("int4 MoE+GEMV µs/layer @batch1, % HBM peak; decode tok/s at 1/2/4/8 GPUs")
 N_LAYERS = 24
 HIDDEN = 2048
+# DRAM bytes (read + write) per MoE layer of the roofline unit, from one ncu capture of
+# the 24-layer MoE-chain launch (profiles/moe_chain_dram_24layers.md)
+MOE_LAYER_DRAM_BYTES = 20_302_560
 
 
 def peaks():
@@ -265,7 +268,10 @@ def run_ours(args):
         "step_hbm": {"bytes": bytes_step, "GBps": bytes_step / (ms_step * 1e-3) / 1e9,
                      "frac": bytes_step / (ms_step * 1e-3) / 1e9 / peak},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": None,
+                     "frac": achieved / peak, "traffic": MOE_LAYER_DRAM_BYTES,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                       "24-layer MoE-chain launch / 24 "
+                                       "(profiles/moe_chain_dram_24layers.md)",
                      "kernel": "decode MoE layer (router, top-k, gate|up, down, combine) in the "
                                "persistent stack kernel, config 0 geometry, batch 1, 24 distinct "
                                "layers per launch",
