@@ -58,11 +58,13 @@ __global__ void __launch_bounds__(256) g_router_kernel(const T* x, const T* gw, 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ne = E - e0 < 16 ? E - e0 : 16, nt = nT - t0 < 16 ? nT - t0 : 16;
   const uint32_t row_bytes = (uint32_t)H * 2u;
+  pdl_launch_dependents();
   if (tid == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_wait();
   if (tid == 0) {
     mbar_arrive_expect_tx(&bar, (uint32_t)(ne + nt) * row_bytes);
     for (int r = 0; r < ne; ++r) bulk_g2s(ws + r * pitch, gw + (size_t)(e0 + r) * H, row_bytes, &bar);
@@ -125,6 +127,8 @@ __global__ void __launch_bounds__(512) g_topk_kernel(const float* logits, int nT
                                                      float* w_out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 16 + warp;
+  pdl_launch_dependents();
+  pdl_wait();
   if (t >= nT) return;  // whole warp
   const float* row = logits + (size_t)t * E;
   uint32_t key[8];
@@ -194,6 +198,8 @@ __global__ void __launch_bounds__(512) g_bucket_kernel(const int* sel, int nT, i
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t c_bytes = ((uint32_t)(nch * E) + 15u) & ~15u;
   const uint32_t p_bytes = ((uint32_t)(nch * E * 2) + 15u) & ~15u;
+  pdl_launch_dependents();
+  pdl_wait();
   uint8_t* cnt = smem;                                                  // [nch][E]
   uint16_t* pre = reinterpret_cast<uint16_t*>(smem + c_bytes);          // [nch][E]
   int* total = reinterpret_cast<int*>(smem + c_bytes + p_bytes);        // [E]
@@ -691,11 +697,13 @@ __global__ void __launch_bounds__(kThreads, 1) g_gateup_kernel(const __grid_cons
   int* tok = reinterpret_cast<int*>(smem + kGTokS);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int perG = p.I >> 4, ns = p.ns_a;
+  pdl_launch_dependents();
+  g_init(full, empty, abort_flag, ns, kCW / 2);
+  pdl_wait();  // the unit list and tokens come from the previous launches
   int nu = *p.n_units;
   nu = nu < 0 ? 0 : (nu > p.max_units ? p.max_units : nu);
   int i0, i1;
   g_range(nu * perG, i0, i1);
-  g_init(full, empty, abort_flag, ns, kCW / 2);
   uint8_t* ring = smem + p.off_ring_a;
 
   if (warp == kCW) {
@@ -834,11 +842,13 @@ __global__ void __launch_bounds__(kThreads, 1) g_down_kernel(const __grid_consta
   int* slt = reinterpret_cast<int*>(smem + kGSlotS);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int RbD = p.H >> 4, nDN = (RbD + kGDnRec - 1) / kGDnRec, ns = p.ns_d;
+  pdl_launch_dependents();
+  g_init(full, empty, abort_flag, ns, kCW / 2);
+  pdl_wait();  // the unit list and tokens come from the previous launches
   int nu = *p.n_units;
   nu = nu < 0 ? 0 : (nu > p.max_units ? p.max_units : nu);
   int i0, i1;
   g_range(nu * nDN, i0, i1);
-  g_init(full, empty, abort_flag, ns, kCW / 2);
   uint8_t* ring = smem + p.off_ring_d;
 
   if (warp == kCW) {
@@ -943,6 +953,8 @@ __global__ void __launch_bounds__(256) g_combine_kernel(const float* ypart, cons
                                                         int top_k, O* out) {
   const int H4 = H >> 2;
   const size_t idx = (size_t)blockIdx.x * 256 + threadIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();
   if (idx >= (size_t)nT * H4) return;
   const int t = (int)(idx / H4), r4 = (int)(idx - (size_t)t * H4);
   float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -1074,6 +1086,25 @@ static void (*g_down_fn(const TileGeom& tg))(GExpParams) {
   return g_down_kernel<T, S, 0, 1>;
 }
 
+// Launch on `st`; with pdl the kernel may start while the previous one on the stream
+// finishes (programmatic dependent launch): every kernel here calls griddepcontrol.wait
+// before it reads anything the previous launch wrote.
+template <typename... KArgs, typename... Args>
+static int g_launch(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                    Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return record_cuda(cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...));
+}
+
 // Bucketing, the two expert kernels and the combine, for the assignments in sel [T][k]
 // whose experts are [e_begin, e_begin + E) (tiles indexed from e_begin); out [T][H] in
 // the activation type (out_f32 == 0) or fp32.
@@ -1081,17 +1112,17 @@ static int g_expert_stage(const void* x, size_t x_row_bytes, bool f16, int T, co
                           int top_k, int e_begin,
                           int E, int E_total, int H, int I, const void* gu_tiles, const void* dn_tiles,
                           GExpParams& p, const GScratch& L, int tcap, uint8_t* ws, const void* residual, void* out,
-                          int out_f32, int* err, cudaStream_t st) {
+                          int out_f32, int* err, cudaStream_t st, bool pdl_first) {
   int rc;
   {
     const int N = T * top_k, nch = (N + 31) / 32;
     const int smem = (int)(align_up((size_t)nch * E, 16) + align_up((size_t)nch * E * 2, 16) +
                            3 * kMaxExperts * 4 + 16 * 4);
     if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(g_bucket_kernel), kGSmemMax))) return rc;
-    g_bucket_kernel<<<1, 512, smem, st>>>(sel, T, E, top_k, tcap, e_begin, E_total,
-                                          reinterpret_cast<int*>(ws + L.assign), reinterpret_cast<int*>(ws + L.units),
-                                          reinterpret_cast<int*>(ws + L.n_units), L.max_units, err);
-    if ((rc = record_cuda(cudaGetLastError()))) return rc;
+    if ((rc = g_launch(g_bucket_kernel, dim3(1), dim3(512), smem, st, pdl_first, sel, T, E, top_k, tcap, e_begin,
+                       E_total, reinterpret_cast<int*>(ws + L.assign), reinterpret_cast<int*>(ws + L.units),
+                       reinterpret_cast<int*>(ws + L.n_units), L.max_units, err)))
+      return rc;
   }
   p.H = H; p.I = I; p.E = E; p.top_k = top_k; p.max_units = L.max_units;
   p.x = reinterpret_cast<const uint8_t*>(x);
@@ -1112,31 +1143,26 @@ static int g_expert_stage(const void* x, size_t x_row_bytes, bool f16, int T, co
     if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(ka), kGSmemMax))) return rc;
     if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(kd), kGSmemMax))) return rc;
     const int G = num_sms();
-    ka<<<G, kThreads, p.smem_a, st>>>(p);
-    if ((rc = record_cuda(cudaGetLastError()))) return rc;
-    kd<<<G, kThreads, p.smem_d, st>>>(p);
-    if ((rc = record_cuda(cudaGetLastError()))) return rc;
+    if ((rc = g_launch(ka, dim3(G), dim3(kThreads), p.smem_a, st, true, p))) return rc;
+    if ((rc = g_launch(kd, dim3(G), dim3(kThreads), p.smem_d, st, true, p))) return rc;
   }
   const float* yp = reinterpret_cast<const float*>(ws + L.ypart);
   const unsigned blocks = (unsigned)(((size_t)T * H / 4 + 255) / 256);
+  const dim3 cg(blocks), cb(256);
   if (f16) {
     const __half* res = reinterpret_cast<const __half*>(residual);
     if (out_f32)
-      g_combine_kernel<__half, float><<<blocks, 256, 0, st>>>(yp, w, sel, e_begin, E, res, T, H, top_k,
-                                                              reinterpret_cast<float*>(out));
-    else
-      g_combine_kernel<__half, __half><<<blocks, 256, 0, st>>>(yp, w, sel, e_begin, E, res, T, H, top_k,
-                                                               reinterpret_cast<__half*>(out));
-  } else {
-    const __nv_bfloat16* res = reinterpret_cast<const __nv_bfloat16*>(residual);
-    if (out_f32)
-      g_combine_kernel<__nv_bfloat16, float><<<blocks, 256, 0, st>>>(yp, w, sel, e_begin, E, res, T, H, top_k,
-                                                                     reinterpret_cast<float*>(out));
-    else
-      g_combine_kernel<__nv_bfloat16, __nv_bfloat16><<<blocks, 256, 0, st>>>(
-          yp, w, sel, e_begin, E, res, T, H, top_k, reinterpret_cast<__nv_bfloat16*>(out));
+      return g_launch(g_combine_kernel<__half, float>, cg, cb, 0, st, true, yp, w, sel, e_begin, E, res, T, H,
+                      top_k, reinterpret_cast<float*>(out));
+    return g_launch(g_combine_kernel<__half, __half>, cg, cb, 0, st, true, yp, w, sel, e_begin, E, res, T, H, top_k,
+                    reinterpret_cast<__half*>(out));
   }
-  return record_cuda(cudaGetLastError());
+  const __nv_bfloat16* res = reinterpret_cast<const __nv_bfloat16*>(residual);
+  if (out_f32)
+    return g_launch(g_combine_kernel<__nv_bfloat16, float>, cg, cb, 0, st, true, yp, w, sel, e_begin, E, res, T, H,
+                    top_k, reinterpret_cast<float*>(out));
+  return g_launch(g_combine_kernel<__nv_bfloat16, __nv_bfloat16>, cg, cb, 0, st, true, yp, w, sel, e_begin, E, res,
+                  T, H, top_k, reinterpret_cast<__nv_bfloat16*>(out));
 }
 
 // Router logits (unless given) and top-k: sel / w [T][top_k] (and the optional copies
@@ -1158,22 +1184,24 @@ static int g_route(const void* x, bool f16, int T, const void* gate_w, const voi
     if ((rc = ensure_smem_attr(fn, kGSmemMax))) return rc;
     const dim3 grid((E + 15) / 16, (T + 15) / 16);
     if (f16)
-      rk<<<grid, 256, smem, st>>>(reinterpret_cast<const __half*>(x), reinterpret_cast<const __half*>(gate_w),
-                                  reinterpret_cast<const __half*>(gate_b), T, E, H, logits, err);
+      rc = g_launch(rk, grid, dim3(256), smem, st, false, reinterpret_cast<const __half*>(x),
+                    reinterpret_cast<const __half*>(gate_w), reinterpret_cast<const __half*>(gate_b), T, E, H, logits,
+                    err);
     else
-      rkb<<<grid, 256, smem, st>>>(reinterpret_cast<const __nv_bfloat16*>(x),
-                                   reinterpret_cast<const __nv_bfloat16*>(gate_w),
-                                   reinterpret_cast<const __nv_bfloat16*>(gate_b), T, E, H, logits, err);
-    if ((rc = record_cuda(cudaGetLastError()))) return rc;
+      rc = g_launch(rkb, grid, dim3(256), smem, st, false, reinterpret_cast<const __nv_bfloat16*>(x),
+                    reinterpret_cast<const __nv_bfloat16*>(gate_w), reinterpret_cast<const __nv_bfloat16*>(gate_b),
+                    T, E, H, logits, err);
+    if (rc) return rc;
   }
   // top-k
+  const bool pdl = !logits_in;  // after the router launch
   if (f16)
-    g_topk_kernel<__half><<<(T + 15) / 16, 512, 0, st>>>(logits, T, E, top_k, norm_topk, sel, w, sel_out, w_out);
+    rc = g_launch(g_topk_kernel<__half>, dim3((T + 15) / 16), dim3(512), 0, st, pdl, (const float*)logits, T, E,
+                  top_k, norm_topk, sel, w, sel_out, w_out);
   else
-    g_topk_kernel<__nv_bfloat16><<<(T + 15) / 16, 512, 0, st>>>(logits, T, E, top_k, norm_topk, sel, w, sel_out,
-                                                                w_out);
-  if ((rc = record_cuda(cudaGetLastError()))) return rc;
-  return DUPLEX_OK;
+    rc = g_launch(g_topk_kernel<__nv_bfloat16>, dim3((T + 15) / 16), dim3(512), 0, st, pdl, (const float*)logits,
+                  T, E, top_k, norm_topk, sel, w, sel_out, w_out);
+  return rc;
 }
 
 static bool g_misaligned(std::initializer_list<const void*> ptrs) {
@@ -1228,7 +1256,7 @@ extern "C" int duplex_moe_grouped(const void* x, int act_dtype, int32_t T, const
     return rc;
   // 3-5. bucketing, experts, combine
   return g_expert_stage(x, (size_t)H * 2, f16, T, sel, w, top_k, 0, E, E, H, I, gu_tiles, dn_tiles, p, L, tcap, ws,
-                        residual, out, 0, err, st);
+                        residual, out, 0, err, st, true);
 }
 
 extern "C" int duplex_moe_experts_grouped_workspace_bytes(int32_t T, int32_t E_local, int32_t E_total,
@@ -1268,7 +1296,7 @@ extern "C" int duplex_moe_experts_grouped(const void* x, int act_dtype, int32_t 
   return g_expert_stage(x, (size_t)x_row_stride * 2, act_dtype == DUPLEX_DTYPE_F16, T, sel, w, top_k, e_begin,
                         E_local, E_total, H, I,
                         gu_tiles, dn_tiles, p, L, tcap, reinterpret_cast<uint8_t*>(workspace), residual, out,
-                        out_dtype == DUPLEX_DTYPE_F32, err, (cudaStream_t)stream);
+                        out_dtype == DUPLEX_DTYPE_F32, err, (cudaStream_t)stream, false);
 }
 
 extern "C" int duplex_moe_route_grouped(const void* x, int act_dtype, int32_t T, const void* gate_w,
