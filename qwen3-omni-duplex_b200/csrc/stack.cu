@@ -571,6 +571,69 @@ DEVN float router_fused(const uint8_t* src, int H, int nT, bool rms, float eps, 
   return a;
 }
 
+// plan_units for one token: warp 0 alone (lane holds experts lane + 32 i), the same
+// keys and max-reductions as the general path, so the same selection; the units are
+// the k selected experts in ascending id order (position = number of selected ids
+// below).  A function of its own: inside plan_units the general path's code made this
+// path ~2.5x slower (3,100 vs 1,250 cycles measured).
+template <typename T>
+DEVN int plan_one(const float* logits, int E, int top_k, uint8_t* smem, float* scratch) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float* ls = reinterpret_cast<float*>(smem + kSLogit);
+  int* sel_s = reinterpret_cast<int*>(smem + kSSel);
+  int* unit_e = reinterpret_cast<int*>(smem + kSUnitE);
+  uint32_t* unit_m = reinterpret_cast<uint32_t*>(smem + kSUnitM);
+  float* unit_w = reinterpret_cast<float*>(smem + kSUnitW);
+  int* n_units_s = reinterpret_cast<int*>(smem + kSNUnits);
+  int* unit_of =  // plan_units's layout of the scratch, read again by plan_weights
+      reinterpret_cast<int*>(scratch) + kMaxTokens * kMaxExperts + kMaxTokens * (kMaxExperts / 4);
+  (void)tid;
+  if (warp == 0) {
+    uint32_t key[kMaxExperts / 32];
+#pragma unroll
+    for (int i = 0; i < kMaxExperts / 32; ++i) {
+      const int e = lane + 32 * i;
+      const float v = e < E ? __ldcg(logits + e) : 0.f;
+      key[i] = e < E ? order_key<T>(v, e) : 0u;
+      if (e < E) ls[e] = v;
+    }
+    int sel[kMaxTopK];
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j) {
+      sel[j] = 0;
+      if (j < top_k) {
+        uint32_t lm = 0u;
+#pragma unroll
+        for (int i = 0; i < kMaxExperts / 32; ++i) lm = key[i] > lm ? key[i] : lm;
+        const uint32_t m = __reduce_max_sync(0xffffffffu, lm);
+#pragma unroll
+        for (int i = 0; i < kMaxExperts / 32; ++i)
+          if (key[i] == m) key[i] = 0u;
+        const int e = key_expert(m);
+        sel[j] = (m == 0u || e >= E) ? 0 : e;
+      }
+    }
+    int mine = 0, rank = 0;
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j)
+      if (j == lane) mine = sel[j];
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j)
+      if (j < top_k && sel[j] < mine) ++rank;
+    if (lane < top_k) {
+      sel_s[lane] = mine;
+      unit_of[mine] = rank;
+      unit_e[rank] = mine;
+      unit_m[rank] = 1u;
+#pragma unroll
+      for (int n = 0; n < kMaxTokens; ++n) unit_w[rank * kMaxTokens + n] = 0.f;
+    }
+    if (lane == 0) *n_units_s = top_k;
+  }
+  named_bar_sync(1, kConsumers);
+  return top_k;
+}
+
 // Top-k of every token and the unit plan (distinct selected experts in ascending
 // id order, their token masks), identical in every CTA.  The routing weights
 // follow in plan_weights, off the critical path.  Returns the unit count.
@@ -592,55 +655,6 @@ DEVN int plan_units(const float* logits, int nT, int E, int top_k, uint8_t* smem
   const int nblk = (E + 31) >> 5;
   uint32_t* cand = keys + kMaxTokens * kMaxExperts;  // [T][nblk * top_k], every slot written
   int* unit_of = reinterpret_cast<int*>(cand + kMaxTokens * (kMaxExperts / 4));
-  if (nT == 1) {
-    // One token: warp 0 alone (lane holds experts lane + 32 i), the same keys and
-    // max-reductions as below, so the same selection; the units are the k selected
-    // experts in ascending id order (position = number of selected ids below).
-    if (warp == 0) {
-      uint32_t key[kMaxExperts / 32];
-#pragma unroll
-      for (int i = 0; i < kMaxExperts / 32; ++i) {
-        const int e = lane + 32 * i;
-        const float v = e < E ? __ldcg(logits + e) : 0.f;
-        key[i] = e < E ? order_key<T>(v, e) : 0u;
-        if (e < E) ls[e] = v;
-      }
-      int sel[kMaxTopK];
-#pragma unroll
-      for (int j = 0; j < kMaxTopK; ++j) {
-        sel[j] = 0;
-        if (j < top_k) {
-          uint32_t lm = 0u;
-#pragma unroll
-          for (int i = 0; i < kMaxExperts / 32; ++i) lm = key[i] > lm ? key[i] : lm;
-          const uint32_t m = __reduce_max_sync(0xffffffffu, lm);
-#pragma unroll
-          for (int i = 0; i < kMaxExperts / 32; ++i)
-            if (key[i] == m) key[i] = 0u;
-          const int e = key_expert(m);
-          sel[j] = (m == 0u || e >= E) ? 0 : e;
-        }
-      }
-      int mine = 0, rank = 0;
-#pragma unroll
-      for (int j = 0; j < kMaxTopK; ++j)
-        if (j == lane) mine = sel[j];
-#pragma unroll
-      for (int j = 0; j < kMaxTopK; ++j)
-        if (j < top_k && sel[j] < mine) ++rank;
-      if (lane < top_k) {
-        sel_s[lane] = mine;
-        unit_of[mine] = rank;
-        unit_e[rank] = mine;
-        unit_m[rank] = 1u;
-#pragma unroll
-        for (int n = 0; n < kMaxTokens; ++n) unit_w[rank * kMaxTokens + n] = 0.f;
-      }
-      if (lane == 0) *n_units_s = top_k;
-    }
-    named_bar_sync(1, kConsumers);
-    return top_k;
-  }
   const int TE = nT * E;
   for (int idx = tid; idx < TE; idx += kConsumers) {
     const float v = __ldcg(logits + idx);
@@ -994,7 +1008,8 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
                   kStageFrag);
     grid_wait(p.barrier, ++nb, abort_flag, err);
     // ------------------------------------------------------------------ D
-    const int nu = plan_units<T>(p.logits, nT, p.E, p.top_k, smem, red);
+    const int nu = nT == 1 ? plan_one<T>(p.logits, p.E, p.top_k, smem, red)
+                           : plan_units<T>(p.logits, nT, p.E, p.top_k, smem, red);
     if (tid == 0) mbar_arrive(plan_ready);
     plan_weights(nT, p.E, p.top_k, p.norm, smem, red);
     // ------------------------------------------------------------------ G
