@@ -199,13 +199,17 @@ int duplex_moe_grouped(const void* x, int act_dtype, int32_t T, const void* gate
 /*
  * moe_route_grouped -- the router of duplex_moe_grouped alone (logits on the tensor
  * cores unless logits_in is given, fp32 softmax, top-k, renormalised) for T <= 512
- * tokens: w_out / sel_out [T][top_k].  Same numerics as duplex_moe_route (T <= 8).
- * workspace: at least T * E * 4 bytes (the logits), 16-byte aligned.
+ * tokens: w_out / sel_out [T][top_k] (either may be NULL when pack is given).  Same
+ * numerics as duplex_moe_route (T <= 8).  pack (optional): token t's expert-parallel
+ * exchange row at pack + t * pack_row_bytes -- the token (2 H bytes, copied from x), its
+ * top_k expert ids (int32), its top_k weights (fp32); pack_row_bytes >= 2 H + 8 top_k, a
+ * multiple of 16.  workspace: at least T * E * 4 bytes (the logits), 16-byte aligned.
  */
 int duplex_moe_route_grouped(const void* x, int act_dtype, int32_t T, const void* gate_w,
                              const void* gate_b, const float* logits_in, int32_t E, int32_t H,
                              int32_t top_k, int32_t norm_topk, float* w_out, int32_t* sel_out,
-                             void* workspace, size_t workspace_bytes, int32_t* err, void* stream);
+                             void* pack, int64_t pack_row_bytes, void* workspace,
+                             size_t workspace_bytes, int32_t* err, void* stream);
 
 /*
  * moe_experts_grouped -- the expert half of duplex_moe_grouped for a given selection,
@@ -218,7 +222,9 @@ int duplex_moe_route_grouped(const void* x, int act_dtype, int32_t T, const void
  * experts are skipped; ids outside [0, E_total) set DUPLEX_DEVERR_EXPERT and are
  * skipped.  x: T rows x_row_stride elements apart (>= H, a multiple of 8: token rows
  * packed with other per-token data, as an expert-parallel exchange delivers them).
- * sel [T][top_k] int32, w [T][top_k] fp32 (device).  T <= 512; the unit token
+ * sel / w: token t's top_k expert ids (int32) / weights (fp32) at sel / w + t *
+ * meta_stride (4-byte words; top_k when dense, the exchange row when packed).  T <= 512;
+ * the unit token
  * cap is chosen from T * top_k / E_total.  Other arguments and limits as
  * duplex_moe_grouped; workspace: duplex_moe_experts_grouped_workspace_bytes.
  */
@@ -226,8 +232,8 @@ int duplex_moe_experts_grouped_workspace_bytes(int32_t T, int32_t E_local, int32
                                                int32_t H, int32_t I, int32_t top_k,
                                                int32_t group, int has_zeros, size_t* bytes);
 int duplex_moe_experts_grouped(const void* x, int act_dtype, int32_t T, int64_t x_row_stride,
-                               const int32_t* sel, const float* w, int32_t top_k, int32_t e_begin,
-                               int32_t E_local,
+                               const int32_t* sel, const float* w, int32_t meta_stride,
+                               int32_t top_k, int32_t e_begin, int32_t E_local,
                                int32_t E_total, int32_t H, int32_t I, const void* gu_tiles,
                                const void* dn_tiles, int scale_dtype, int has_zeros,
                                int32_t group, const void* residual, void* out, int out_dtype,

@@ -253,7 +253,7 @@ def moe_experts_by_expert(x, sel, w, gu_packed, gu_scale, dn_packed, dn_scale,
         act = (g / (np.float32(1.0) + np.exp(-g))) * u
         dn = dequant(dn_packed[e], np.asarray(dn_scale[e], np.float32), Ki, dz, "float32")
         y = act[:, :Ki] @ dn.T                                       # [n, H]
-        out[t_idx] += y * w[t_idx, j_idx][:, None]
+        np.add.at(out, t_idx, y * w[t_idx, j_idx][:, None])  # a token may list e twice
     return out
 
 

@@ -121,15 +121,23 @@ __global__ void __launch_bounds__(256) g_router_kernel(const T* x, const T* gw, 
 // max-reduction over the order keys select the top k in descending order; softmax
 // in fp32 over all experts; the top-k probabilities renormalised (their sum in
 // selection order).
-template <typename T>
+// PACK: the warp also writes its token's exchange row in pack: the token (2 H bytes,
+// copied from x), its k expert ids (int32), its k weights (fp32), row_bytes apart.
+template <typename T, bool PACK>
 __global__ void __launch_bounds__(512) g_topk_kernel(const float* logits, int nT, int E, int top_k,
                                                      int norm, int* sel, float* w, int32_t* sel_out,
-                                                     float* w_out) {
+                                                     float* w_out, const T* x, int H, uint8_t* pack,
+                                                     int64_t row_bytes) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 16 + warp;
   pdl_launch_dependents();
   pdl_wait();
   if (t >= nT) return;  // whole warp
+  if constexpr (PACK) {  // the token's bytes first, while the logits loads are in flight
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t * H);
+    uint4* dst = reinterpret_cast<uint4*>(pack + (size_t)t * row_bytes);
+    for (int q = lane; q < (H >> 3); q += 32) dst[q] = __ldg(src + q);
+  }
   const float* row = logits + (size_t)t * E;
   uint32_t key[8];
   float lv[8];
@@ -140,6 +148,7 @@ __global__ void __launch_bounds__(512) g_topk_kernel(const float* logits, int nT
     key[i] = e < E ? order_key<T>(lv[i], e) : 0u;
   }
   int sj[kMaxTopK];
+  int ej = 0;  // lane j's pick
 #pragma unroll
   for (int j = 0; j < kMaxTopK; ++j) {
     sj[j] = 0;
@@ -153,6 +162,7 @@ __global__ void __launch_bounds__(512) g_topk_kernel(const float* logits, int nT
         if (key[i] == km) key[i] = 0u;
       const int e = key_expert(km);
       sj[j] = (km == 0u || e >= E) ? 0 : e;
+      ej = lane == j ? sj[j] : ej;  // taken here: read after the loop, the last pick came out 0
     }
   }
   const float m = row[sj[0]];
@@ -162,10 +172,6 @@ __global__ void __launch_bounds__(512) g_topk_kernel(const float* logits, int nT
     if (lane + 32 * i < E) den += expf(lv[i] - m);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-  int ej = 0;
-#pragma unroll
-  for (int j = 0; j < kMaxTopK; ++j)
-    if (j == lane) ej = sj[j];
   const float pj = lane < top_k ? expf(row[ej] - m) / den : 0.f;
   float psum = 0.f;
 #pragma unroll
@@ -175,10 +181,15 @@ __global__ void __launch_bounds__(512) g_topk_kernel(const float* logits, int nT
   }
   if (lane < top_k) {
     const float wj = norm ? pj / psum : pj;
-    sel[(size_t)t * top_k + lane] = ej;
-    w[(size_t)t * top_k + lane] = wj;
+    if (sel) sel[(size_t)t * top_k + lane] = ej;
+    if (w) w[(size_t)t * top_k + lane] = wj;
     if (sel_out) sel_out[(size_t)t * top_k + lane] = ej;
     if (w_out) w_out[(size_t)t * top_k + lane] = wj;
+    if constexpr (PACK) {
+      uint8_t* meta = pack + (size_t)t * row_bytes + (size_t)H * 2;
+      reinterpret_cast<int32_t*>(meta)[lane] = ej;
+      reinterpret_cast<float*>(meta + 4 * top_k)[lane] = wj;
+    }
   }
 }
 
@@ -189,9 +200,9 @@ __global__ void __launch_bounds__(512) g_topk_kernel(const float* logits, int nT
 // (expert, first assignment, count).  One CTA of 512 threads; chunks of 32
 // assignments per warp (__match_any_sync gives ranks within a chunk).  Only experts
 // [e_begin, e_begin + E) are bucketed (an expert-parallel rank's own); ids outside
-// [0, E_total) are flagged in err and skipped.
-__global__ void __launch_bounds__(512) g_bucket_kernel(const int* sel, int nT, int E, int top_k, int tcap,
-                                                       int e_begin, int E_total, int* assign, int* units,
+// [0, E_total) are flagged in err and skipped.  Token t's ids are sel[t * sel_stride ..].
+__global__ void __launch_bounds__(512) g_bucket_kernel(const int* sel, int sel_stride, int nT, int E, int top_k,
+                                                       int tcap, int e_begin, int E_total, int* assign, int* units,
                                                        int* n_units, int max_units, int* err) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int N = nT * top_k, nch = (N + 31) >> 5;
@@ -211,7 +222,8 @@ __global__ void __launch_bounds__(512) g_bucket_kernel(const int* sel, int nT, i
   // ids of other ranks' experts (outside [e_begin, e_begin + E)) are skipped
   auto expert_of = [&](int a) {
     if (a >= N) return -1;
-    const int g = sel[a];
+    const int ta = a / top_k;
+    const int g = sel[(size_t)ta * sel_stride + (a - ta * top_k)];
     if (g < 0 || g >= E_total) {
       set_error(err, DUPLEX_DEVERR_EXPERT);
       return -1;
@@ -949,8 +961,8 @@ __global__ void __launch_bounds__(kThreads, 1) g_down_kernel(const __grid_consta
 // ranks); four consecutive outputs per thread.
 template <typename T, typename O>
 __global__ void __launch_bounds__(256) g_combine_kernel(const float* ypart, const float* w, const int* sel,
-                                                        int e_begin, int E, const T* residual, int nT, int H,
-                                                        int top_k, O* out) {
+                                                        int meta_stride, int e_begin, int E, const T* residual,
+                                                        int nT, int H, int top_k, O* out) {
   const int H4 = H >> 2;
   const size_t idx = (size_t)blockIdx.x * 256 + threadIdx.x;
   pdl_launch_dependents();
@@ -959,9 +971,9 @@ __global__ void __launch_bounds__(256) g_combine_kernel(const float* ypart, cons
   const int t = (int)(idx / H4), r4 = (int)(idx - (size_t)t * H4);
   float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int j = 0; j < top_k; ++j) {
-    const unsigned e = (unsigned)(sel[(size_t)t * top_k + j] - e_begin);
+    const unsigned e = (unsigned)(sel[(size_t)t * meta_stride + j] - e_begin);
     if (e >= (unsigned)E) continue;
-    const float wj = w[(size_t)t * top_k + j];
+    const float wj = w[(size_t)t * meta_stride + j];
     const float4 v = __ldcg(reinterpret_cast<const float4*>(ypart + ((size_t)t * top_k + j) * H) + r4);
     s.x = fmaf(wj, v.x, s.x);
     s.y = fmaf(wj, v.y, s.y);
@@ -1109,7 +1121,7 @@ static int g_launch(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
 // whose experts are [e_begin, e_begin + E) (tiles indexed from e_begin); out [T][H] in
 // the activation type (out_f32 == 0) or fp32.
 static int g_expert_stage(const void* x, size_t x_row_bytes, bool f16, int T, const int* sel, const float* w,
-                          int top_k, int e_begin,
+                          int meta_stride, int top_k, int e_begin,
                           int E, int E_total, int H, int I, const void* gu_tiles, const void* dn_tiles,
                           GExpParams& p, const GScratch& L, int tcap, uint8_t* ws, const void* residual, void* out,
                           int out_f32, int* err, cudaStream_t st, bool pdl_first) {
@@ -1119,7 +1131,8 @@ static int g_expert_stage(const void* x, size_t x_row_bytes, bool f16, int T, co
     const int smem = (int)(align_up((size_t)nch * E, 16) + align_up((size_t)nch * E * 2, 16) +
                            3 * kMaxExperts * 4 + 16 * 4);
     if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(g_bucket_kernel), kGSmemMax))) return rc;
-    if ((rc = g_launch(g_bucket_kernel, dim3(1), dim3(512), smem, st, pdl_first, sel, T, E, top_k, tcap, e_begin,
+    if ((rc = g_launch(g_bucket_kernel, dim3(1), dim3(512), smem, st, pdl_first, sel, meta_stride, T, E, top_k, tcap,
+                       e_begin,
                        E_total, reinterpret_cast<int*>(ws + L.assign), reinterpret_cast<int*>(ws + L.units),
                        reinterpret_cast<int*>(ws + L.n_units), L.max_units, err)))
       return rc;
@@ -1152,24 +1165,24 @@ static int g_expert_stage(const void* x, size_t x_row_bytes, bool f16, int T, co
   if (f16) {
     const __half* res = reinterpret_cast<const __half*>(residual);
     if (out_f32)
-      return g_launch(g_combine_kernel<__half, float>, cg, cb, 0, st, true, yp, w, sel, e_begin, E, res, T, H,
+      return g_launch(g_combine_kernel<__half, float>, cg, cb, 0, st, true, yp, w, sel, meta_stride, e_begin, E, res, T, H,
                       top_k, reinterpret_cast<float*>(out));
-    return g_launch(g_combine_kernel<__half, __half>, cg, cb, 0, st, true, yp, w, sel, e_begin, E, res, T, H, top_k,
+    return g_launch(g_combine_kernel<__half, __half>, cg, cb, 0, st, true, yp, w, sel, meta_stride, e_begin, E, res, T, H, top_k,
                     reinterpret_cast<__half*>(out));
   }
   const __nv_bfloat16* res = reinterpret_cast<const __nv_bfloat16*>(residual);
   if (out_f32)
-    return g_launch(g_combine_kernel<__nv_bfloat16, float>, cg, cb, 0, st, true, yp, w, sel, e_begin, E, res, T, H,
+    return g_launch(g_combine_kernel<__nv_bfloat16, float>, cg, cb, 0, st, true, yp, w, sel, meta_stride, e_begin, E, res, T, H,
                     top_k, reinterpret_cast<float*>(out));
-  return g_launch(g_combine_kernel<__nv_bfloat16, __nv_bfloat16>, cg, cb, 0, st, true, yp, w, sel, e_begin, E, res,
+  return g_launch(g_combine_kernel<__nv_bfloat16, __nv_bfloat16>, cg, cb, 0, st, true, yp, w, sel, meta_stride, e_begin, E, res,
                   T, H, top_k, reinterpret_cast<__nv_bfloat16*>(out));
 }
 
 // Router logits (unless given) and top-k: sel / w [T][top_k] (and the optional copies
-// sel_out / w_out).
+// sel_out / w_out, and the exchange rows in pack).
 static int g_route(const void* x, bool f16, int T, const void* gate_w, const void* gate_b, const float* logits_in,
                    int E, int H, int top_k, int norm_topk, uint8_t* ws, const GScratch& L, int* sel, float* w,
-                   int32_t* sel_out, float* w_out, int* err, cudaStream_t st) {
+                   int32_t* sel_out, float* w_out, uint8_t* pack, int64_t pack_row, int* err, cudaStream_t st) {
   int rc;
   float* logits = logits_in ? const_cast<float*>(logits_in) : reinterpret_cast<float*>(ws + L.logits);
   // router
@@ -1195,13 +1208,20 @@ static int g_route(const void* x, bool f16, int T, const void* gate_w, const voi
   }
   // top-k
   const bool pdl = !logits_in;  // after the router launch
-  if (f16)
-    rc = g_launch(g_topk_kernel<__half>, dim3((T + 15) / 16), dim3(512), 0, st, pdl, (const float*)logits, T, E,
-                  top_k, norm_topk, sel, w, sel_out, w_out);
-  else
-    rc = g_launch(g_topk_kernel<__nv_bfloat16>, dim3((T + 15) / 16), dim3(512), 0, st, pdl, (const float*)logits,
-                  T, E, top_k, norm_topk, sel, w, sel_out, w_out);
-  return rc;
+  const dim3 grid((T + 15) / 16), block(512);
+  const float* lg = logits;
+  if (f16) {
+    const __half* xh = reinterpret_cast<const __half*>(x);
+    return pack ? g_launch(g_topk_kernel<__half, true>, grid, block, 0, st, pdl, lg, T, E, top_k, norm_topk, sel, w,
+                           sel_out, w_out, xh, H, pack, pack_row)
+                : g_launch(g_topk_kernel<__half, false>, grid, block, 0, st, pdl, lg, T, E, top_k, norm_topk, sel, w,
+                           sel_out, w_out, xh, H, pack, pack_row);
+  }
+  const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(x);
+  return pack ? g_launch(g_topk_kernel<__nv_bfloat16, true>, grid, block, 0, st, pdl, lg, T, E, top_k, norm_topk, sel,
+                         w, sel_out, w_out, xb, H, pack, pack_row)
+              : g_launch(g_topk_kernel<__nv_bfloat16, false>, grid, block, 0, st, pdl, lg, T, E, top_k, norm_topk, sel,
+                         w, sel_out, w_out, xb, H, pack, pack_row);
 }
 
 static bool g_misaligned(std::initializer_list<const void*> ptrs) {
@@ -1252,11 +1272,11 @@ extern "C" int duplex_moe_grouped(const void* x, int act_dtype, int32_t T, const
   const bool f16 = act_dtype == DUPLEX_DTYPE_F16;
   int rc;
   if ((rc = g_route(x, f16, T, gate_w, gate_b, logits_in, E, H, top_k, norm_topk, ws, L, sel, w, sel_out, w_out,
-                    err, st)))
+                    nullptr, 0, err, st)))
     return rc;
   // 3-5. bucketing, experts, combine
-  return g_expert_stage(x, (size_t)H * 2, f16, T, sel, w, top_k, 0, E, E, H, I, gu_tiles, dn_tiles, p, L, tcap, ws,
-                        residual, out, 0, err, st, true);
+  return g_expert_stage(x, (size_t)H * 2, f16, T, sel, w, top_k, top_k, 0, E, E, H, I, gu_tiles, dn_tiles, p, L,
+                        tcap, ws, residual, out, 0, err, st, true);
 }
 
 extern "C" int duplex_moe_experts_grouped_workspace_bytes(int32_t T, int32_t E_local, int32_t E_total,
@@ -1272,8 +1292,8 @@ extern "C" int duplex_moe_experts_grouped_workspace_bytes(int32_t T, int32_t E_l
 }
 
 extern "C" int duplex_moe_experts_grouped(const void* x, int act_dtype, int32_t T, int64_t x_row_stride,
-                                          const int32_t* sel, const float* w, int32_t top_k, int32_t e_begin,
-                                          int32_t E_local,
+                                          const int32_t* sel, const float* w, int32_t meta_stride, int32_t top_k,
+                                          int32_t e_begin, int32_t E_local,
                                           int32_t E_total, int32_t H, int32_t I, const void* gu_tiles,
                                           const void* dn_tiles, int scale_dtype, int has_zeros, int32_t group,
                                           const void* residual, void* out, int out_dtype, void* workspace,
@@ -1292,8 +1312,10 @@ extern "C" int duplex_moe_experts_grouped(const void* x, int act_dtype, int32_t 
   const GScratch L = g_scratch(T, E_local, H, I, top_k, tcap);
   if (workspace_bytes < L.total) return DUPLEX_ERR_WORKSPACE;
   if (x_row_stride < H || (x_row_stride & 7)) return DUPLEX_ERR_ALIGN;
+  if (meta_stride < top_k) return DUPLEX_ERR_ARG;
   if (g_misaligned({x, out, workspace, gu_tiles, dn_tiles, residual})) return DUPLEX_ERR_ALIGN;
-  return g_expert_stage(x, (size_t)x_row_stride * 2, act_dtype == DUPLEX_DTYPE_F16, T, sel, w, top_k, e_begin,
+  return g_expert_stage(x, (size_t)x_row_stride * 2, act_dtype == DUPLEX_DTYPE_F16, T, sel, w, meta_stride, top_k,
+                        e_begin,
                         E_local, E_total, H, I,
                         gu_tiles, dn_tiles, p, L, tcap, reinterpret_cast<uint8_t*>(workspace), residual, out,
                         out_dtype == DUPLEX_DTYPE_F32, err, (cudaStream_t)stream, false);
@@ -1302,8 +1324,12 @@ extern "C" int duplex_moe_experts_grouped(const void* x, int act_dtype, int32_t 
 extern "C" int duplex_moe_route_grouped(const void* x, int act_dtype, int32_t T, const void* gate_w,
                                         const void* gate_b, const float* logits_in, int32_t E, int32_t H,
                                         int32_t top_k, int32_t norm_topk, float* w_out, int32_t* sel_out,
-                                        void* workspace, size_t workspace_bytes, int32_t* err, void* stream) {
-  if (!x || !w_out || !sel_out || !workspace || (!gate_w && !logits_in)) return DUPLEX_ERR_ARG;
+                                        void* pack, int64_t pack_row_bytes, void* workspace,
+                                        size_t workspace_bytes, int32_t* err, void* stream) {
+  if (!x || !workspace || (!gate_w && !logits_in) || (!pack && (!w_out || !sel_out))) return DUPLEX_ERR_ARG;
+  if (pack && (pack_row_bytes < (int64_t)H * 2 + 8 * top_k || (pack_row_bytes & 15) ||
+               (reinterpret_cast<uintptr_t>(pack) & 15u)))
+    return DUPLEX_ERR_ALIGN;
   if (T < 1 || T > kGMaxT || E < 1 || E > kMaxExperts || top_k < 1 || top_k > kMaxTopK || top_k > E)
     return DUPLEX_ERR_ARG;
   if (act_dtype != DUPLEX_DTYPE_F16 && act_dtype != DUPLEX_DTYPE_BF16) return DUPLEX_ERR_DTYPE;
@@ -1314,5 +1340,6 @@ extern "C" int duplex_moe_route_grouped(const void* x, int act_dtype, int32_t T,
   if (g_misaligned({x, gate_w, logits_in, workspace})) return DUPLEX_ERR_ALIGN;
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
   return g_route(x, act_dtype == DUPLEX_DTYPE_F16, T, gate_w, gate_b, logits_in, E, H, top_k, norm_topk, ws, L,
-                 sel_out, w_out, nullptr, nullptr, err, (cudaStream_t)stream);
+                 sel_out, w_out, nullptr, nullptr, reinterpret_cast<uint8_t*>(pack), pack_row_bytes, err,
+                 (cudaStream_t)stream);
 }

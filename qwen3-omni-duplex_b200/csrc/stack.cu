@@ -598,6 +598,7 @@ DEVN int plan_one(const float* logits, int E, int top_k, uint8_t* smem, float* s
       if (e < E) ls[e] = v;
     }
     int sel[kMaxTopK];
+    int mine = 0;  // lane j's pick
 #pragma unroll
     for (int j = 0; j < kMaxTopK; ++j) {
       sel[j] = 0;
@@ -611,12 +612,10 @@ DEVN int plan_one(const float* logits, int E, int top_k, uint8_t* smem, float* s
           if (key[i] == m) key[i] = 0u;
         const int e = key_expert(m);
         sel[j] = (m == 0u || e >= E) ? 0 : e;
+        mine = lane == j ? sel[j] : mine;  // taken here: read after the loop, the last pick came out 0
       }
     }
-    int mine = 0, rank = 0;
-#pragma unroll
-    for (int j = 0; j < kMaxTopK; ++j)
-      if (j == lane) mine = sel[j];
+    int rank = 0;
 #pragma unroll
     for (int j = 0; j < kMaxTopK; ++j)
       if (j < top_k && sel[j] < mine) ++rank;

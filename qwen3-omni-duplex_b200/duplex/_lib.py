@@ -59,15 +59,15 @@ _SIGNATURES = {
                             _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr, _c_ptr],
                            _c_int),
     "duplex_moe_route_grouped": ([_c_ptr, _c_int, _c_i32, _c_ptr, _c_ptr, _c_ptr, _c_i32, _c_i32,
-                                  _c_i32, _c_i32, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr, _c_ptr],
-                                 _c_int),
+                                  _c_i32, _c_i32, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_ptr, _c_size,
+                                  _c_ptr, _c_ptr], _c_int),
     "duplex_moe_experts_grouped_workspace_bytes": ([_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
                                                     _c_i32, _c_int, ctypes.POINTER(ctypes.c_size_t)],
                                                    _c_int),
     "duplex_moe_experts_grouped": ([_c_ptr, _c_int, _c_i32, _c_i64, _c_ptr, _c_ptr, _c_i32, _c_i32,
-                                    _c_i32, _c_i32, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_int, _c_int,
-                                    _c_i32, _c_ptr, _c_ptr, _c_int, _c_ptr, _c_size, _c_ptr, _c_ptr],
-                                   _c_int),
+                                    _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_int,
+                                    _c_int, _c_i32, _c_ptr, _c_ptr, _c_int, _c_ptr, _c_size, _c_ptr,
+                                    _c_ptr], _c_int),
     "duplex_stack_workspace_bytes": ([_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
                                       ctypes.POINTER(ctypes.c_size_t)], _c_int),
     "duplex_stack_forward": ([_c_ptr, _c_i32, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_int, _c_int,

@@ -6,9 +6,10 @@ this is the multi-GPU form of the same layer, `FusedPackedMoE.forward` semantics
 token, for batched decode (many streams per rank):
 
   1. route the rank's own tokens over all E experts (router logits, fp32 softmax,
-     top-k, renormalise: `duplex_moe_route_grouped`);
-  2. exchange: one all-gather of the tokens packed with their (expert, weight)
-     selections, so that every rank sees every token that may pick one of its experts;
+     top-k, renormalise: `duplex_moe_route_grouped`), whose top-k kernel writes each
+     token's exchange row (the token, its expert ids, its weights);
+  2. exchange: one all-gather of those rows, so that every rank sees every token that
+     may pick one of its experts (the expert stage reads the gathered rows in place);
   3. the rank's experts [rank * E/N, (rank + 1) * E/N) on all gathered tokens, one fp32
      partial sum per token over the slots that hit them (`duplex_moe_experts_grouped`);
   4. exchange back: reduce-scatter (sum) of the fp32 partials, so each token's owner
@@ -32,31 +33,32 @@ from duplex.streaming.triton_dequant_gemv import Int4Tiles
 PACK = 8
 
 
+def exchange_row_bytes(H: int, elt: int, top_k: int) -> int:
+    """Bytes of one exchange row: the token, its k expert ids, its k weights (16-aligned)."""
+    return -(-(H * elt + 8 * top_k) // 16) * 16
+
+
 def ep_forward(x, route_fn, experts_fn, top_k: int, group=None, residual=None, out_dtype=None):
     """Host side of one expert-parallel layer on this rank.
 
-    x [T_local, H]; route_fn(x) -> (w [T_local, k] fp32, sel [T_local, k] int32);
-    experts_fn(x_all, sel_all, w_all) -> fp32 [N * T_local, H]: this rank's experts'
-    weighted sum per gathered token (zero where none of its experts is selected); x_all
-    may be a row-strided view.  Returns [T_local, H] in out_dtype (default x.dtype).
-
-    The tokens and their selections travel in ONE all-gather: each row packs the token
-    (2 H bytes for 16-bit activations), its k expert ids and its k weights.
+    x [T_local, H]; route_fn(x, pack) fills pack [T_local, row] uint8 with each token's
+    exchange row (the token's 2 H bytes, its k expert ids as int32, its k weights as
+    fp32); experts_fn(x_all, sel_all, w_all) -> fp32 [N * T_local, H]: this rank's
+    experts' weighted sum per gathered token (zero where none of its experts is
+    selected).  x_all, sel_all and w_all are row-strided views of the gathered rows.
+    Returns [T_local, H] in out_dtype (default x.dtype).
     """
     world = dist.get_world_size(group)
     T_l, H = x.shape
-    w, sel = route_fn(x)
-    xb = x.contiguous().view(torch.uint8)                      # [T_l, H * elt]
-    row = xb.shape[1] + 8 * top_k
+    xbytes = H * x.element_size()
+    row = exchange_row_bytes(H, x.element_size(), top_k)
     pack = torch.empty(T_l, row, dtype=torch.uint8, device=x.device)
-    pack[:, :xb.shape[1]] = xb
-    pack[:, xb.shape[1]:xb.shape[1] + 4 * top_k] = sel.to(torch.int32).contiguous().view(torch.uint8)
-    pack[:, xb.shape[1] + 4 * top_k:] = w.to(torch.float32).contiguous().view(torch.uint8)
+    route_fn(x, pack)
     pall = torch.empty(world * T_l, row, dtype=torch.uint8, device=x.device)
     dist.all_gather_into_tensor(pall, pack, group=group)
-    x_all = pall.view(x.dtype)[:, :H]                          # rows `row` bytes apart
-    sel_all = pall[:, xb.shape[1]:xb.shape[1] + 4 * top_k].contiguous().view(torch.int32)
-    w_all = pall[:, xb.shape[1] + 4 * top_k:].contiguous().view(torch.float32)
+    x_all = pall[:, :xbytes].view(x.dtype)
+    sel_all = pall[:, xbytes:xbytes + 4 * top_k].view(torch.int32)
+    w_all = pall[:, xbytes + 4 * top_k:xbytes + 8 * top_k].view(torch.float32)
     partial = experts_fn(x_all, sel_all, w_all)
     red = torch.empty(T_l, H, dtype=torch.float32, device=x.device)
     dist.reduce_scatter_tensor(red, partial.contiguous(), op=dist.ReduceOp.SUM, group=group)
@@ -119,20 +121,29 @@ class ExpertParallelMoE(nn.Module):
             self._ws[key] = ws
         return ws
 
-    def route(self, x):
-        """(w [T, k] fp32, sel [T, k] int32) over all experts, for this rank's tokens."""
-        T = x.shape[0]
-        w = torch.empty(T, self.top_k, dtype=torch.float32, device=x.device)
-        sel = torch.empty(T, self.top_k, dtype=torch.int32, device=x.device)
+    def _route_ws(self, T, device):
         ws = self._ws.get(("route", T))
         if ws is None:
-            ws = torch.empty(T * self.num_experts * 4, dtype=torch.uint8, device=x.device)
+            ws = torch.empty(T * self.num_experts * 4, dtype=torch.uint8, device=device)
             self._ws[("route", T)] = ws
+        return ws
+
+    def route(self, x, pack=None):
+        """Route this rank's tokens over all experts: with pack (an [T, row] uint8
+        exchange buffer) write the exchange rows there; without, return (w [T, k] fp32,
+        sel [T, k] int32)."""
+        T = x.shape[0]
+        w = sel = None
+        if pack is None:
+            w = torch.empty(T, self.top_k, dtype=torch.float32, device=x.device)
+            sel = torch.empty(T, self.top_k, dtype=torch.int32, device=x.device)
+        ws = self._route_ws(T, x.device)
         g = self.gate
         _lib.call("duplex_moe_route_grouped", _lib.ptr(x), _lib.dtype_code(x.dtype), T,
                   _lib.ptr(g.weight), _lib.ptr(g.bias), None, self.num_experts, self.hidden,
                   self.top_k, 1 if self.norm_topk_prob else 0, _lib.ptr(w), _lib.ptr(sel),
-                  _lib.ptr(ws), ws.numel(), _lib.ptr(self.err), _lib.stream_of(x))
+                  _lib.ptr(pack), 0 if pack is None else pack.stride(0), _lib.ptr(ws), ws.numel(),
+                  _lib.ptr(self.err), _lib.stream_of(x))
         return w, sel
 
     def local_experts(self, x_all, sel_all, w_all):
@@ -145,9 +156,11 @@ class ExpertParallelMoE(nn.Module):
             x_all.device)
         if x_all.stride(1) != 1 or x_all.data_ptr() % 16:
             raise _lib.DuplexError("token rows must be contiguous and 16-byte aligned")
+        if sel_all.stride(0) != w_all.stride(0) or sel_all.stride(1) != 1 or w_all.stride(1) != 1:
+            raise _lib.DuplexError("expert ids and weights must share one row stride")
         _lib.call("duplex_moe_experts_grouped", _lib.ptr(x_all), _lib.dtype_code(x_all.dtype), T,
-                  x_all.stride(0), _lib.ptr(sel_all), _lib.ptr(w_all), self.top_k, self.e_begin,
-                  self.E_local,
+                  x_all.stride(0), _lib.ptr(sel_all), _lib.ptr(w_all), sel_all.stride(0), self.top_k,
+                  self.e_begin, self.E_local,
                   self.num_experts, self.hidden, self.inter, _lib.ptr(self.gu_tiles.buf),
                   _lib.ptr(self.dn_tiles.buf), self.gu_tiles.scale_code,
                   1 if self.has_zeros else 0, self.group_size, None, _lib.ptr(out),
@@ -158,7 +171,8 @@ class ExpertParallelMoE(nn.Module):
     def forward(self, x, residual=None):
         _lib.require_cuda(x)
         x = _lib.aligned(x.to(self.gate.weight.dtype))
-        return ep_forward(x, self.route, self.local_experts, self.top_k, self.group, residual)
+        return ep_forward(x, lambda xt, pack: self.route(xt, pack), self.local_experts, self.top_k,
+                          self.group, residual)
 
     def device_errors(self) -> int:
         v = int(self.err.item())

@@ -56,8 +56,8 @@ def _shard_partial(cuda, L, m, x_t, sel, w, e0, n_loc, out_dtype=torch.float32, 
     out = torch.empty(Tn, H, dtype=out_dtype, device=cuda)
     err = torch.zeros(1, dtype=torch.int32, device=cuda)
     _lib.call("duplex_moe_experts_grouped", _lib.ptr(x_t), _lib.DTYPE_F16, Tn, H, _lib.ptr(sel),
-              _lib.ptr(w), k, e0, n_loc, m.num_experts, H, m.inter, _lib.ptr(gu.buf), _lib.ptr(dn.buf),
-              gu.scale_code, 1,
+              _lib.ptr(w), k, k, e0, n_loc, m.num_experts, H, m.inter, _lib.ptr(gu.buf),
+              _lib.ptr(dn.buf), gu.scale_code, 1,
               m.group, _lib.ptr(residual), _lib.ptr(out), _lib.dtype_code(out_dtype), _lib.ptr(ws),
               ws.numel(), _lib.ptr(err), _lib.stream_of(x_t))
     torch.cuda.synchronize()
@@ -115,10 +115,21 @@ def test_route_grouped_matches_the_grouped_layer_routing(cuda):
     ws = torch.empty(Tn * 128 * 4, dtype=torch.uint8, device=cuda)
     g = m.gate
     _lib.call("duplex_moe_route_grouped", _lib.ptr(x_t), _lib.DTYPE_F16, Tn, _lib.ptr(g.weight), None, None,
-              128, 2048, 8, 1, _lib.ptr(w2), _lib.ptr(sel2), _lib.ptr(ws), ws.numel(), None,
+              128, 2048, 8, 1, _lib.ptr(w2), _lib.ptr(sel2), None, 0, _lib.ptr(ws), ws.numel(), None,
               _lib.stream_of(x_t))
     torch.cuda.synchronize()
     assert torch.equal(sel, sel2) and torch.equal(w, w2)
+    # the exchange rows: token bytes, ids, weights
+    from duplex.streaming.ep_moe import exchange_row_bytes
+    row = exchange_row_bytes(2048, 2, 8)
+    pack = torch.zeros(Tn, row, dtype=torch.uint8, device=cuda)
+    _lib.call("duplex_moe_route_grouped", _lib.ptr(x_t), _lib.DTYPE_F16, Tn, _lib.ptr(g.weight), None, None,
+              128, 2048, 8, 1, None, None, _lib.ptr(pack), row, _lib.ptr(ws), ws.numel(), None,
+              _lib.stream_of(x_t))
+    torch.cuda.synchronize()
+    assert torch.equal(pack[:, :4096].view(torch.float16), x_t)
+    assert torch.equal(pack[:, 4096:4128].view(torch.int32), sel)
+    assert torch.equal(pack[:, 4128:4160].view(torch.float32), w)
 
 
 def _free_port():

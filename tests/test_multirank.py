@@ -68,9 +68,12 @@ def _ep_worker(rank, ws, port, q):
     e0, e1 = rank * (E // ws), (rank + 1) * (E // ws)
     res = torch.from_numpy(np.random.default_rng(rank).standard_normal((T_l, H)).astype(np.float32))
 
-    def route_fn(xt):
+    def route_fn(xt, pack):
         w, sel, _ = O.router(xt.numpy(), L["gate_w"], k, True, None, "float32")
-        return torch.from_numpy(w), torch.from_numpy(sel.astype(np.int32))
+        xb = xt.contiguous().view(torch.uint8)
+        pack[:, :xb.shape[1]] = xb
+        pack[:, xb.shape[1]:xb.shape[1] + 4 * k] = torch.from_numpy(sel.astype(np.int32)).view(torch.uint8)
+        pack[:, xb.shape[1] + 4 * k:xb.shape[1] + 8 * k] = torch.from_numpy(w).view(torch.uint8)
 
     def experts_fn(x_all, sel_all, w_all):
         s = sel_all.numpy()

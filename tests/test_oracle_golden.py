@@ -115,3 +115,17 @@ def test_packed_linear_two_roundings():
     acc = O.dequant_gemv(x[0], d["packed"][None], d["scale"][None], [0], d["zeros"][None])[0]
     ref = (acc.astype(np.float16).astype(np.float32) + b.astype(np.float32)).astype(np.float16)
     assert np.array_equal(y[0], ref)
+
+
+def test_by_expert_oracle_is_the_per_token_oracle():
+    """The expert-batched restatement gives the per-token forward (fp32 summation order
+    aside), also when a token lists one expert in two slots."""
+    L = synth.moe_layer_np(seed=9, E=8, H=128, I=64, top_k=3, group=32, zero_points=True, T=5)
+    rng = np.random.default_rng(9)
+    sel = np.stack([rng.choice(8, 3, replace=False) for _ in range(5)]).astype(np.int32)
+    sel[2, 1] = sel[2, 0]
+    w = rng.random((5, 3)).astype(np.float32)
+    args = (L["gu_packed"], L["gu_scale"], L["dn_packed"], L["dn_scale"], L["gu_zeros"], L["dn_zeros"])
+    a = O.moe_experts(L["x"], sel, w, *args)
+    b = O.moe_experts_by_expert(L["x"], sel, w, *args)
+    assert np.abs(a - b).max() <= 1e-5 * np.abs(a).max()
