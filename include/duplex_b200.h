@@ -241,6 +241,49 @@ int duplex_moe_experts_grouped(const void* x, int act_dtype, int32_t T, int64_t 
                                void* stream);
 
 /*
+ * Tensor-core (tcgen05) variants of the grouped path -- same computation, arguments,
+ * limits and error behaviour as duplex_moe_grouped / duplex_moe_experts_grouped, with
+ * the experts in "tensor-core records" instead of tile records, and these limits: group
+ * 128, H and I multiples of 128 and at least 256.  The weights are dequantised exactly
+ * as the reference's dequant does ((nibble - zero) * scale, one rounding into the
+ * activation type) straight into tensor memory and multiplied on the tensor cores with
+ * fp32 accumulation; units hold up to 16, 32 or 64 tokens (chosen from T * top_k /
+ * E_total).  Deterministic (fixed accumulation order), but not bit-identical to the
+ * mma.sync path, whose weights are not rounded.
+ *
+ * tc_records_bytes -- size of the records of a stacked matrix [E][R][K/8] (R a multiple of
+ * 128; pair_halves for gate|up, R = 2 I).  repack_tc_records -- build them from the
+ * reference's tensors (packed, scale [E][R][K/128], optional packed zero points), as
+ * duplex_repack_tiles does for tile records; records 16-byte aligned.
+ */
+int duplex_tc_records_bytes(int32_t E, int32_t R, int32_t K, int32_t group, int has_zeros,
+                            int32_t pair_halves, size_t* bytes);
+int duplex_repack_tc_records(const int32_t* packed, const void* scale, const int32_t* zeros,
+                             int scale_dtype, int32_t E, int32_t R, int32_t K, int32_t group,
+                             int32_t pair_halves, void* records, size_t records_bytes,
+                             void* stream);
+int duplex_moe_grouped_tc_workspace_bytes(int32_t T, int32_t E, int32_t H, int32_t I,
+                                          int32_t top_k, int32_t group, int has_zeros,
+                                          size_t* bytes);
+int duplex_moe_grouped_tc(const void* x, int act_dtype, int32_t T, const void* gate_w,
+                          const void* gate_b, const float* logits_in, int32_t E, int32_t H,
+                          int32_t I, int32_t top_k, int32_t norm_topk, const void* gu_records,
+                          const void* dn_records, int scale_dtype, int has_zeros, int32_t group,
+                          const void* residual, void* out, float* w_out, int32_t* sel_out,
+                          void* workspace, size_t workspace_bytes, int32_t* err, void* stream);
+int duplex_moe_experts_grouped_tc_workspace_bytes(int32_t T, int32_t E_local, int32_t E_total,
+                                                  int32_t H, int32_t I, int32_t top_k,
+                                                  int32_t group, int has_zeros, size_t* bytes);
+int duplex_moe_experts_grouped_tc(const void* x, int act_dtype, int32_t T, int64_t x_row_stride,
+                                  const int32_t* sel, const float* w, int32_t meta_stride,
+                                  int32_t top_k, int32_t e_begin, int32_t E_local,
+                                  int32_t E_total, int32_t H, int32_t I, const void* gu_records,
+                                  const void* dn_records, int scale_dtype, int has_zeros,
+                                  int32_t group, const void* residual, void* out, int out_dtype,
+                                  void* workspace, size_t workspace_bytes, int32_t* err,
+                                  void* stream);
+
+/*
  * Persistent clock-path stack -- the reference's clock path (src/duplex/streaming/clock.py:
  * 162-197) runs Thinker layers 0..23 per frame with TritonPackedLinear q/k/v/o and
  * FusedPackedMoE; this is every int4 linear of n_layers such layers for T <= 8 tokens in ONE

@@ -21,6 +21,7 @@
 #include "gemv_core.cuh"
 #include "moe.cuh"
 #include "topk.cuh"
+#include "umma.cuh"
 
 #include <initializer_list>
 #include <type_traits>
@@ -1232,6 +1233,8 @@ static bool g_misaligned(std::initializer_list<const void*> ptrs) {
 
 }  // namespace duplex
 
+#include "grouped_tc.cuh"
+
 using namespace duplex;
 
 extern "C" int duplex_moe_grouped_workspace_bytes(int32_t T, int32_t E, int32_t H, int32_t I,
@@ -1342,4 +1345,117 @@ extern "C" int duplex_moe_route_grouped(const void* x, int act_dtype, int32_t T,
   return g_route(x, act_dtype == DUPLEX_DTYPE_F16, T, gate_w, gate_b, logits_in, E, H, top_k, norm_topk, ws, L,
                  sel_out, w_out, nullptr, nullptr, reinterpret_cast<uint8_t*>(pack), pack_row_bytes, err,
                  (cudaStream_t)stream);
+}
+
+// ------------------------------------------------------------ tcgen05 expert path
+extern "C" int duplex_tc_records_bytes(int32_t E, int32_t R, int32_t K, int32_t group, int has_zeros,
+                                       int32_t pair_halves, size_t* bytes) {
+  if (!bytes || E < 1 || R < 1 || K < 1) return DUPLEX_ERR_ARG;
+  if (group != kTcK || K % kTcK || R % kTcM || (pair_halves && (R % 128))) return DUPLEX_ERR_UNSUPPORTED;
+  *bytes = (size_t)E * (R / kTcM) * (K / kTcK) * tc_chunk_bytes(has_zeros);
+  return DUPLEX_OK;
+}
+
+extern "C" int duplex_repack_tc_records(const int32_t* packed, const void* scale, const int32_t* zeros,
+                                        int scale_dtype, int32_t E, int32_t R, int32_t K, int32_t group,
+                                        int32_t pair_halves, void* records, size_t records_bytes, void* stream) {
+  if (!packed || !scale || !records) return DUPLEX_ERR_ARG;
+  size_t need = 0;
+  int rc = duplex_tc_records_bytes(E, R, K, group, zeros != nullptr, pair_halves, &need);
+  if (rc) return rc;
+  if (records_bytes < need) return DUPLEX_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(records) & 15u) return DUPLEX_ERR_ALIGN;
+  const long long words = (long long)(need / 4);
+  int blocks = (int)((words + 255) / 256);
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  cudaStream_t st = (cudaStream_t)stream;
+  const uint32_t cb = tc_chunk_bytes(zeros != nullptr);
+  if (scale_dtype == DUPLEX_DTYPE_F16)
+    tc_repack_kernel<__half><<<blocks, 256, 0, st>>>(packed, reinterpret_cast<const __half*>(scale), zeros, E, R, K,
+                                                     pair_halves, cb, reinterpret_cast<uint32_t*>(records));
+  else if (scale_dtype == DUPLEX_DTYPE_BF16)
+    tc_repack_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(packed, reinterpret_cast<const __nv_bfloat16*>(scale),
+                                                            zeros, E, R, K, pair_halves, cb,
+                                                            reinterpret_cast<uint32_t*>(records));
+  else
+    return DUPLEX_ERR_DTYPE;
+  return record_cuda(cudaGetLastError());
+}
+
+extern "C" int duplex_moe_grouped_tc_workspace_bytes(int32_t T, int32_t E, int32_t H, int32_t I, int32_t top_k,
+                                                     int32_t group, int has_zeros, size_t* bytes) {
+  (void)has_zeros;
+  if (!bytes || T < 1 || T > kGMaxT || E < 1 || E > kMaxExperts || top_k < 1 || top_k > kMaxTopK || top_k > E)
+    return DUPLEX_ERR_ARG;
+  if (!tc_geometry_ok(H, I, group) || g_router_smem(H) > kGSmemMax) return DUPLEX_ERR_UNSUPPORTED;
+  *bytes = tc_scratch(T, E, H, I, top_k, tc_cols(T, E, top_k)).g.total;
+  return DUPLEX_OK;
+}
+
+extern "C" int duplex_moe_grouped_tc(const void* x, int act_dtype, int32_t T, const void* gate_w,
+                                     const void* gate_b, const float* logits_in, int32_t E, int32_t H, int32_t I,
+                                     int32_t top_k, int32_t norm_topk, const void* gu_records,
+                                     const void* dn_records, int scale_dtype, int has_zeros, int32_t group,
+                                     const void* residual, void* out, float* w_out, int32_t* sel_out,
+                                     void* workspace, size_t workspace_bytes, int32_t* err, void* stream) {
+  if (!x || !out || !gu_records || !dn_records || !workspace || (!gate_w && !logits_in)) return DUPLEX_ERR_ARG;
+  if (T < 1 || T > kGMaxT || E < 1 || E > kMaxExperts || top_k < 1 || top_k > kMaxTopK || top_k > E)
+    return DUPLEX_ERR_ARG;
+  if (act_dtype != DUPLEX_DTYPE_F16 && act_dtype != DUPLEX_DTYPE_BF16) return DUPLEX_ERR_DTYPE;
+  if (scale_dtype != act_dtype) return DUPLEX_ERR_DTYPE;
+  if (!tc_geometry_ok(H, I, group) || g_router_smem(H) > kGSmemMax) return DUPLEX_ERR_UNSUPPORTED;
+  const int N = tc_cols(T, E, top_k);
+  const TcScratch L = tc_scratch(T, E, H, I, top_k, N);
+  if (workspace_bytes < L.g.total) return DUPLEX_ERR_WORKSPACE;
+  if (g_misaligned({x, out, workspace, gu_records, dn_records, gate_w, residual, logits_in})) return DUPLEX_ERR_ALIGN;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  int* sel = reinterpret_cast<int*>(ws + L.g.sel);
+  float* w = reinterpret_cast<float*>(ws + L.g.w);
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool f16 = act_dtype == DUPLEX_DTYPE_F16;
+  int rc;
+  if ((rc = g_route(x, f16, T, gate_w, gate_b, logits_in, E, H, top_k, norm_topk, ws, L.g, sel, w, sel_out, w_out,
+                    nullptr, 0, err, st)))
+    return rc;
+  return tc_expert_stage(x, (size_t)H * 2, f16, T, sel, w, top_k, top_k, 0, E, E, H, I, has_zeros, gu_records,
+                         dn_records, L, N, ws, residual, out, 0, err, st, true);
+}
+
+extern "C" int duplex_moe_experts_grouped_tc_workspace_bytes(int32_t T, int32_t E_local, int32_t E_total, int32_t H,
+                                                             int32_t I, int32_t top_k, int32_t group, int has_zeros,
+                                                             size_t* bytes) {
+  (void)has_zeros;
+  if (!bytes || T < 1 || T > kGMaxT || E_local < 1 || E_total < E_local || E_total > kMaxExperts || top_k < 1 ||
+      top_k > kMaxTopK || top_k > E_total)
+    return DUPLEX_ERR_ARG;
+  if (!tc_geometry_ok(H, I, group)) return DUPLEX_ERR_UNSUPPORTED;
+  *bytes = tc_scratch(T, E_local, H, I, top_k, tc_cols(T, E_total, top_k)).g.total;
+  return DUPLEX_OK;
+}
+
+extern "C" int duplex_moe_experts_grouped_tc(const void* x, int act_dtype, int32_t T, int64_t x_row_stride,
+                                             const int32_t* sel, const float* w, int32_t meta_stride, int32_t top_k,
+                                             int32_t e_begin, int32_t E_local, int32_t E_total, int32_t H, int32_t I,
+                                             const void* gu_records, const void* dn_records, int scale_dtype,
+                                             int has_zeros, int32_t group, const void* residual, void* out,
+                                             int out_dtype, void* workspace, size_t workspace_bytes, int32_t* err,
+                                             void* stream) {
+  if (!x || !sel || !w || !out || !gu_records || !dn_records || !workspace) return DUPLEX_ERR_ARG;
+  if (T < 1 || T > kGMaxT || E_local < 1 || e_begin < 0 || e_begin + E_local > E_total ||
+      E_total > kMaxExperts || top_k < 1 || top_k > kMaxTopK || top_k > E_total)
+    return DUPLEX_ERR_ARG;
+  if (act_dtype != DUPLEX_DTYPE_F16 && act_dtype != DUPLEX_DTYPE_BF16) return DUPLEX_ERR_DTYPE;
+  if (scale_dtype != act_dtype) return DUPLEX_ERR_DTYPE;
+  if (out_dtype != act_dtype && out_dtype != DUPLEX_DTYPE_F32) return DUPLEX_ERR_DTYPE;
+  if (!tc_geometry_ok(H, I, group)) return DUPLEX_ERR_UNSUPPORTED;
+  const int N = tc_cols(T, E_total, top_k);
+  const TcScratch L = tc_scratch(T, E_local, H, I, top_k, N);
+  if (workspace_bytes < L.g.total) return DUPLEX_ERR_WORKSPACE;
+  if (x_row_stride < H || (x_row_stride & 7)) return DUPLEX_ERR_ALIGN;
+  if (meta_stride < top_k) return DUPLEX_ERR_ARG;
+  if (g_misaligned({x, out, workspace, gu_records, dn_records, residual})) return DUPLEX_ERR_ALIGN;
+  return tc_expert_stage(x, (size_t)x_row_stride * 2, act_dtype == DUPLEX_DTYPE_F16, T, sel, w, meta_stride, top_k,
+                         e_begin, E_local, E_total, H, I, has_zeros, gu_records, dn_records, L, N,
+                         reinterpret_cast<uint8_t*>(workspace), residual, out, out_dtype == DUPLEX_DTYPE_F32, err,
+                         (cudaStream_t)stream, false);
 }

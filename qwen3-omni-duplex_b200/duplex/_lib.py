@@ -68,6 +68,23 @@ _SIGNATURES = {
                                     _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_int,
                                     _c_int, _c_i32, _c_ptr, _c_ptr, _c_int, _c_ptr, _c_size, _c_ptr,
                                     _c_ptr], _c_int),
+    "duplex_tc_records_bytes": ([_c_i32, _c_i32, _c_i32, _c_i32, _c_int, _c_i32,
+                                 ctypes.POINTER(ctypes.c_size_t)], _c_int),
+    "duplex_repack_tc_records": ([_c_ptr, _c_ptr, _c_ptr, _c_int, _c_i32, _c_i32, _c_i32, _c_i32,
+                                  _c_i32, _c_ptr, _c_size, _c_ptr], _c_int),
+    "duplex_moe_grouped_tc_workspace_bytes": ([_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
+                                               _c_int, ctypes.POINTER(ctypes.c_size_t)], _c_int),
+    "duplex_moe_grouped_tc": ([_c_ptr, _c_int, _c_i32, _c_ptr, _c_ptr, _c_ptr, _c_i32, _c_i32,
+                               _c_i32, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_int, _c_int, _c_i32,
+                               _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr, _c_ptr],
+                              _c_int),
+    "duplex_moe_experts_grouped_tc_workspace_bytes": ([_c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
+                                                       _c_i32, _c_i32, _c_int,
+                                                       ctypes.POINTER(ctypes.c_size_t)], _c_int),
+    "duplex_moe_experts_grouped_tc": ([_c_ptr, _c_int, _c_i32, _c_i64, _c_ptr, _c_ptr, _c_i32,
+                                       _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_ptr,
+                                       _c_ptr, _c_int, _c_int, _c_i32, _c_ptr, _c_ptr, _c_int,
+                                       _c_ptr, _c_size, _c_ptr, _c_ptr], _c_int),
     "duplex_stack_workspace_bytes": ([_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
                                       ctypes.POINTER(ctypes.c_size_t)], _c_int),
     "duplex_stack_forward": ([_c_ptr, _c_i32, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_int, _c_int,

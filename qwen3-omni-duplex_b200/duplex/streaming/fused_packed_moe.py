@@ -34,7 +34,8 @@ import torch
 import torch.nn as nn
 
 from duplex import _lib
-from duplex.streaming.triton_dequant_gemv import HAVE_TRITON, Int4Tiles, dequant_gemv  # noqa: F401
+from duplex.streaming.triton_dequant_gemv import (HAVE_TRITON, Int4Tiles, TcRecords,  # noqa: F401
+                                                  dequant_gemv)
 
 NUM_BITS = 4
 PACK = 32 // NUM_BITS
@@ -76,13 +77,14 @@ class FusedPackedMoE(nn.Module):
     """SparseMoeBlock replacement for int4-packed experts, on the B200 kernels."""
 
     def __init__(self, block: nn.Module = None, dtype=torch.bfloat16, device="cuda",
-                 host_resident: bool = False, cpu_compute: bool = False):
+                 host_resident: bool = False, cpu_compute: bool = False, tc: bool = True):
         super().__init__()
         if dtype not in (torch.float16, torch.bfloat16):
             raise _lib.DuplexError("FusedPackedMoE on B200 runs fp16 or bf16 modules")
         self.host_resident = host_resident      # recorded; all weights stay in HBM
         self.cpu_compute = cpu_compute and host_resident
         self.pdl = True
+        self.tc = tc                            # build tensor-core records (batched decode)
         if block is None:                       # filled by from_stacked()
             return
         experts = block.experts
@@ -104,9 +106,9 @@ class FusedPackedMoE(nn.Module):
     @classmethod
     def from_stacked(cls, gate_weight, gu_packed, gu_scale, dn_packed, dn_scale, top_k,
                      gu_zeros=None, dn_zeros=None, norm_topk_prob=True, gate_bias=None,
-                     dtype=torch.float16, device="cuda"):
+                     dtype=torch.float16, device="cuda", tc=True):
         """Build from raw stacked tensors ([E,2I,H/8], [E,2I,G], [E,H,I/8], [E,H,G'])."""
-        m = cls(None, dtype=dtype, device=device)
+        m = cls(None, dtype=dtype, device=device, tc=tc)
         E, H = gate_weight.shape
         m.num_experts, m.top_k, m.norm_topk_prob = E, top_k, norm_topk_prob
         m.gate = nn.Linear(H, E, bias=gate_bias is not None).to(device=device, dtype=dtype)
@@ -135,6 +137,15 @@ class FusedPackedMoE(nn.Module):
             raise _lib.DuplexError("gate|up and down must both have or both lack zero points")
         self.gu_tiles = Int4Tiles(gu_p, gu_s, gu_z, group=self.group, K=hidden, pair_halves=True)
         self.dn_tiles = Int4Tiles(dp, ds, dz, group=self.group, K=inter_in)
+        # tensor-core records for batched decode (a second copy of the experts, in the
+        # layout of the tcgen05 kernels), where the geometry allows them
+        E = gu_p.shape[0]
+        self.gu_tc = self.dn_tc = None
+        if (self.tc and hid_out == hidden and inter_in == inter
+                and TcRecords.supported(E, 2 * inter, hidden, self.group, pair_halves=True)
+                and TcRecords.supported(E, hidden, inter, self.group)):
+            self.gu_tc = TcRecords(gu_p, gu_s, gu_z, group=self.group, K=hidden, pair_halves=True)
+            self.dn_tc = TcRecords(dp, ds, dz, group=self.group, K=inter_in)
         self.register_buffer("err", torch.zeros(1, dtype=torch.int32, device=gu_p.device),
                              persistent=False)
         self.inter, self.hidden, self.hid_out, self.inter_in = inter, hidden, hid_out, inter_in
@@ -181,35 +192,50 @@ class FusedPackedMoE(nn.Module):
             1 if self.has_zeros else 0, _lib.ctypes.byref(n))
         return rc == 0
 
-    def grouped_workspace(self, T: int, device) -> torch.Tensor:
-        ws = self._ws.get(("grouped", T, device))
+    def grouped_engine(self, T: int) -> str:
+        """The expert engine the grouped path takes for T tokens: "tc" (tcgen05 kernels on
+        the tensor-core records) when the records exist, else "mma" (mma.sync kernels)."""
+        return "tc" if self.gu_tc is not None else "mma"
+
+    def grouped_workspace(self, T: int, device, engine: str = "mma") -> torch.Tensor:
+        key = ("grouped", engine, T, device)
+        ws = self._ws.get(key)
         if ws is None:
             n = _lib.ctypes.c_size_t()
-            _lib.call("duplex_moe_grouped_workspace_bytes", T, self.num_experts, self.hidden,
-                      self.inter, self.top_k, self.group, 1 if self.has_zeros else 0,
-                      _lib.ctypes.byref(n))
+            fn = ("duplex_moe_grouped_tc_workspace_bytes" if engine == "tc"
+                  else "duplex_moe_grouped_workspace_bytes")
+            _lib.call(fn, T, self.num_experts, self.hidden, self.inter, self.top_k, self.group,
+                      1 if self.has_zeros else 0, _lib.ctypes.byref(n))
             ws = torch.empty(n.value, dtype=torch.uint8, device=device)
-            self._ws[("grouped", T, device)] = ws
+            self._ws[key] = ws
         return ws
 
     def forward_grouped_into(self, x, out, residual=None, w_out=None, sel_out=None,
-                             logits=None):
+                             logits=None, engine=None):
         """x [T<=512, H] -> out [T, H] (+ residual) through the grouped path, no host
         synchronisation.  logits: optional [T, E] fp32 router logits (already rounded to
-        the module dtype) used in place of the gate."""
+        the module dtype) used in place of the gate.  engine: "tc", "mma" or None (the
+        module's choice, grouped_engine)."""
         T = x.shape[0]
         if T > GROUPED_MAX_TOKENS:
             raise _lib.DuplexError(f"grouped MoE takes at most {GROUPED_MAX_TOKENS} tokens")
-        ws = self.grouped_workspace(T, x.device)
+        engine = engine or self.grouped_engine(T)
+        if engine == "tc":
+            if self.gu_tc is None:
+                raise _lib.DuplexError("this layer has no tensor-core records (geometry or tc=False)")
+            fn, gu, dn, code = "duplex_moe_grouped_tc", self.gu_tc.buf, self.dn_tc.buf, self.gu_tc.scale_code
+        else:
+            fn, gu, dn, code = "duplex_moe_grouped", self.gu_tiles.buf, self.dn_tiles.buf, self.gu_tiles.scale_code
+        ws = self.grouped_workspace(T, x.device, engine)
         g = self.gate
         lg = None if logits is None else _lib.aligned(logits.float())
         _lib.call(
-            "duplex_moe_grouped", _lib.ptr(x), _lib.dtype_code(x.dtype), T, _lib.ptr(g.weight),
+            fn, _lib.ptr(x), _lib.dtype_code(x.dtype), T, _lib.ptr(g.weight),
             _lib.ptr(g.bias), _lib.ptr(lg), self.num_experts, self.hidden, self.inter,
-            self.top_k, 1 if self.norm_topk_prob else 0, _lib.ptr(self.gu_tiles.buf),
-            _lib.ptr(self.dn_tiles.buf), self.gu_tiles.scale_code, 1 if self.has_zeros else 0,
-            self.group, _lib.ptr(residual), _lib.ptr(out), _lib.ptr(w_out), _lib.ptr(sel_out),
-            _lib.ptr(ws), ws.numel(), _lib.ptr(self.err), _lib.stream_of(x))
+            self.top_k, 1 if self.norm_topk_prob else 0, _lib.ptr(gu), _lib.ptr(dn), code,
+            1 if self.has_zeros else 0, self.group, _lib.ptr(residual), _lib.ptr(out),
+            _lib.ptr(w_out), _lib.ptr(sel_out), _lib.ptr(ws), ws.numel(), _lib.ptr(self.err),
+            _lib.stream_of(x))
         return out
 
     def forward_into(self, x, out, residual=None, w_out=None, sel_out=None, rms_eps=0.0):

@@ -95,6 +95,55 @@ class Int4Tiles:
         return self.buf.numel()
 
 
+class TcRecords:
+    """Tensor-core records of a stacked int4 matrix [E, R, K/8] (+ scales, zero points).
+
+    One record per (expert, 128-row tile, 128-column chunk): the chunk's nibbles in a
+    thread-per-row order, its 128 scales and optionally 128 zero points, so one bulk
+    copy feeds a ring stage of the tcgen05 expert kernels (layout documented in
+    csrc/grouped_tc.cuh).  Scale groups of 128 only.  `pair_halves` (gate | up):
+    every tile holds 64 gate rows and the matching 64 up rows.
+    """
+
+    def __init__(self, packed, scale, zeros=None, group=None, K=None, pair_halves=False):
+        _lib.require_cuda(packed, scale, zeros)
+        if packed.dim() == 2:
+            packed, scale = packed.unsqueeze(0), scale.unsqueeze(0)
+            zeros = None if zeros is None else zeros.unsqueeze(0)
+        E, R, NW = packed.shape
+        K = int(K if K is not None else NW * 8)
+        G = scale.shape[-1]
+        group = int(group if group is not None else -(-K // G))
+        if NW * 8 != K:
+            packed = packed[..., : K // 8]
+        self.E, self.R, self.K, self.group = E, R, K, group
+        self.has_zeros = zeros is not None
+        scale = _lib.aligned(_kernel_scale(scale))
+        self.scale_dtype = scale.dtype
+        n = _lib.ctypes.c_size_t()
+        _lib.call("duplex_tc_records_bytes", E, R, K, group, 1 if self.has_zeros else 0,
+                  1 if pair_halves else 0, _lib.ctypes.byref(n))
+        self.buf = torch.empty(n.value, dtype=torch.uint8, device=packed.device)
+        p = _lib.aligned(packed.to(torch.int32))
+        z = None if zeros is None else _lib.aligned(zeros.to(torch.int32))
+        _lib.call("duplex_repack_tc_records", _lib.ptr(p), _lib.ptr(scale), _lib.ptr(z),
+                  _lib.dtype_code(scale.dtype), E, R, K, group, 1 if pair_halves else 0,
+                  _lib.ptr(self.buf), self.buf.numel(), _lib.stream_of(p))
+
+    @staticmethod
+    def supported(E, R, K, group, pair_halves=False) -> bool:
+        n = _lib.ctypes.c_size_t()
+        return _lib.load().duplex_tc_records_bytes(E, R, K, group, 0, 1 if pair_halves else 0,
+                                                   _lib.ctypes.byref(n)) == 0
+
+    @property
+    def scale_code(self) -> int:
+        return _lib.dtype_code(self.scale_dtype)
+
+    def nbytes(self) -> int:
+        return self.buf.numel()
+
+
 _TILE_CACHE: collections.OrderedDict = collections.OrderedDict()
 _TILE_CACHE_MAX = 16
 
