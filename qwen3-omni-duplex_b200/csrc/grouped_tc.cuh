@@ -17,17 +17,19 @@
 // shared memory; the MMA accumulates the tile's whole K in fp32 in tensor memory.
 //
 // Roles in a CTA (320 threads):
-//   warps 0-3, 4-7  two dequantising warp groups, alternate chunks (chunk c -> group c & 1);
+//   warps 0-3, 4-7  two dequantising warp groups, one chunk of every two-chunk stage each;
 //                   thread (warp & 3) * 32 + lane owns tile row m (its tensor-memory lane);
 //                   after the first chunk of the next item, the epilogue of the previous
 //                   one (each group reads half of the token columns).
-//   warp 8          producer: one bulk copy of the weight chunk and one of the unit's token
-//                   tile (16 column chunks of 8 values x N tokens) per ring stage.
+//   warp 8          producer: per ring stage one bulk copy of two weight chunks and one of
+//                   the unit's two token tiles (16 column chunks of 8 values x N tokens each).
 //   warp 9          allocates 512 tensor-memory columns; lane 0 issues the 8 MMAs
 //                   (K = 16 each) of every chunk and commits them to the barriers below.
-// Tensor memory: A buffers [group][2] x 64 columns at 0..255, D [2 items] x 64 at 256..383.
-// Barriers: full/empty per ring stage; A ready (4 warps) / A free (MMA commit) per A
-// buffer; D ready (commit) / D free (8 epilogue warps) per D buffer.  Every wait is
+// Tensor memory: A buffers [group][2] x 64 columns at 0..255, D [2 items] x 128 at 256..511
+// (128 / N accumulators of N columns per item).
+// Barriers: full/empty per ring stage (empty: one MMA commit per stage, which also frees
+// the A buffers the stage's MMAs read); A ready (4 warps) per A buffer; D ready (commit) /
+// D free (8 epilogue warps) per D buffer.  Every wait is
 // bounded: on timeout the error word gets DUPLEX_DEVERR_TIMEOUT, an abort flag stops all
 // roles, the MMA thread and the producer drain what they issued, and tensor memory is
 // released before the CTA exits.
@@ -41,9 +43,11 @@ constexpr int kTcThreads = 320;
 constexpr int kTcMaxN = 64;
 constexpr uint32_t kTcInt4Bytes = 8192;   // 128 rows x 128 nibbles
 constexpr uint32_t kTcFixed = 1024;       // barrier / flag area ahead of the ring
-constexpr uint32_t kTcFull = 0, kTcEmpty = 128, kTcAReady = 256, kTcAFree = 288, kTcDReady = 320,
+constexpr uint32_t kTcFull = 0, kTcEmpty = 128, kTcAReady = 256, kTcDReady = 320,
                    kTcDFree = 336, kTcDrain = 352, kTcAbort = 360, kTcTmem = 364;
 constexpr uint32_t kTcColsD = 256;        // first D column
+constexpr uint32_t kTcDCols = 128;        // D columns per item: 128 / N accumulators of N columns
+constexpr int kTcCps = 2;                 // chunks per ring stage (one per dequantising group)
 constexpr uint32_t kTcMinSmem = 120 * 1024;  // > half an SM: one CTA per SM, so the 512-column
                                              // tensor-memory allocation never waits
 
@@ -153,10 +157,16 @@ DEVI void tc_dequant(const uint8_t* stage, int m, int has_zeros, uint32_t ta) {
   }
 }
 
-// Producer (one thread): every chunk of items [i0, i1) into the ring.
+// Producer (one thread): items [i0, i1) into the ring, two chunks per stage.  A stage is
+// [weights of chunk 2 cp | of chunk 2 cp + 1 | token tile of chunk 2 cp | of 2 cp + 1]:
+// both halves are contiguous at their source, so a stage costs two bulk copies (each
+// copy has a fixed issue cost of a few hundred cycles, so fewer and larger copies stream
+// faster).
 DEVI void tc_produce(const TcParams& p, int N, uint64_t* full, uint64_t* empty, volatile int* abort_flag,
                      uint8_t* ring, int i0, int i1) {
   const uint64_t pol = policy_evict_first();
+  const int pairs = p.chunks / kTcCps;
+  const uint32_t wbytes = kTcCps * p.chunk_bytes, bbytes = kTcCps * p.b_bytes;
   int j = 0;
   for (int it = i0; it < i1; ++it) {
     const int u = it / p.tiles, t = it - u * p.tiles;
@@ -164,13 +174,13 @@ DEVI void tc_produce(const TcParams& p, int N, uint64_t* full, uint64_t* empty, 
     tc_unit(p, u, N, e, first, n);
     const uint8_t* wsrc = p.rec + (size_t)(e * p.tiles + t) * p.chunks * p.chunk_bytes;
     const uint8_t* bsrc = p.bsrc + (size_t)u * p.chunks * p.b_bytes;
-    for (int c = 0; c < p.chunks; ++c, ++j) {
+    for (int cp = 0; cp < pairs; ++cp, ++j) {
       const int s = j % p.ns, use = j / p.ns;
       if (use > 0 && !tc_wait(&empty[s], (uint32_t)(use - 1) & 1u, abort_flag, p.err)) goto drain;
       uint8_t* dst = ring + (size_t)s * p.stage_bytes;
-      mbar_arrive_expect_tx(&full[s], p.chunk_bytes + p.b_bytes);
-      bulk_g2s_stream(dst, wsrc + (size_t)c * p.chunk_bytes, p.chunk_bytes, &full[s], pol);
-      bulk_g2s(dst + p.chunk_bytes, bsrc + (size_t)c * p.b_bytes, p.b_bytes, &full[s]);
+      mbar_arrive_expect_tx(&full[s], wbytes + bbytes);
+      bulk_g2s_stream(dst, wsrc + (size_t)cp * wbytes, wbytes, &full[s], pol);
+      bulk_g2s(dst + wbytes, bsrc + (size_t)cp * bbytes, bbytes, &full[s]);
     }
   }
 drain:
@@ -185,31 +195,41 @@ drain:
   }
 }
 
-// MMA issuer (one thread).
+// MMA issuer (one thread).  The 8 K-steps of a chunk rotate over NACC = 128 / N
+// accumulators of N columns: an MMA this narrow is short next to the latency of the
+// accumulator it reads back, so back-to-back MMAs into one accumulator would serialise.
 template <int N>
-DEVI void tc_mma(const TcParams& p, uint64_t* full, uint64_t* empty, uint64_t* aready, uint64_t* afree,
-                 uint64_t* dready, uint64_t* dfree, uint64_t* drain, volatile int* abort_flag, uint8_t* ring,
+DEVI void tc_mma(const TcParams& p, uint64_t* full, uint64_t* empty, uint64_t* aready, uint64_t* dready, uint64_t* dfree, uint64_t* drain, volatile int* abort_flag, uint8_t* ring,
                  uint32_t tbase, uint32_t idesc, int i0, int i1) {
-  int j = 0, ii = 0, k0 = 0, k1 = 0;  // chunks so far of group 0 / group 1
+  constexpr int NACC = kTcDCols / N;
+  const int pairs = p.chunks / kTcCps;
+  int j = 0, ii = 0, k0 = 0, k1 = 0;  // stages so far; chunks so far of group 0 / group 1
   for (int it = i0; it < i1; ++it, ++ii) {
     const int db = ii & 1;
-    const uint32_t dcol = kTcColsD + (uint32_t)db * 64u;
-    for (int c = 0; c < p.chunks; ++c, ++j) {
-      const int s = j % p.ns, use = j / p.ns, wg = c & 1;
-      const int k = wg ? k1++ : k0++, ab = k & 1, b = wg * 2 + ab;
+    const uint32_t dcol = kTcColsD + (uint32_t)db * kTcDCols;
+    for (int cp = 0; cp < pairs; ++cp, ++j) {
+      const int s = j % p.ns, use = j / p.ns;
       if (!tc_wait(&full[s], (uint32_t)use & 1u, abort_flag, p.err)) goto out;
-      if (!tc_wait(&aready[b], (uint32_t)(k >> 1) & 1u, abort_flag, p.err)) goto out;
-      if (c == 0 && ii >= 2 && !tc_wait(&dfree[db], (uint32_t)((ii >> 1) - 1) & 1u, abort_flag, p.err)) goto out;
-      tc_fence_after();
-      const uint32_t acol = (uint32_t)b * 64u;
-      const uint32_t b0 = smem_u32(ring + (size_t)s * p.stage_bytes + p.chunk_bytes);
+      uint8_t* st = ring + (size_t)s * p.stage_bytes;
 #pragma unroll
-      for (int s8 = 0; s8 < kTcK / 16; ++s8)
-        umma_ts(tbase + dcol, tbase + acol + 8u * s8, smem_desc_kmajor(b0 + (uint32_t)s8 * 32u * N, 16u * N, 128u),
-                idesc, (c | s8) != 0);
-      umma_commit(&afree[b]);
+      for (int wg = 0; wg < kTcCps; ++wg) {
+        const int c = cp * kTcCps + wg;
+        const int k = wg ? k1++ : k0++, b = wg * 2 + (k & 1);
+        if (!tc_wait(&aready[b], (uint32_t)(k >> 1) & 1u, abort_flag, p.err)) goto out;
+        if (c == 0 && ii >= 2 && !tc_wait(&dfree[db], (uint32_t)((ii >> 1) - 1) & 1u, abort_flag, p.err))
+          goto out;
+        tc_fence_after();
+        const uint32_t acol = (uint32_t)b * 64u;
+        const uint32_t b0 = smem_u32(st + kTcCps * p.chunk_bytes + (uint32_t)wg * p.b_bytes);
+#pragma unroll
+        for (int s8 = 0; s8 < kTcK / 16; ++s8)
+          umma_ts(tbase + dcol + (uint32_t)(s8 % NACC) * N, tbase + acol + 8u * s8,
+                  smem_desc_kmajor(b0 + (uint32_t)s8 * 32u * N, 16u * N, 128u), idesc, !(c == 0 && s8 < NACC));
+      }
+      // one commit per stage (a commit costs about as much as an MMA): it frees the ring
+      // slot and, for the dequantising groups, the A buffers this stage read
       umma_commit(&empty[s]);
-      if (c == p.chunks - 1) umma_commit(&dready[db]);
+      if (cp == pairs - 1) umma_commit(&dready[db]);
     }
   }
 out:
@@ -225,30 +245,38 @@ out:
   }
 }
 
-// Epilogue of the CTA's ii-th item `it` for this warp: columns [wg N/2, (wg + 1) N/2).
+// Epilogue of the CTA's ii-th item `it` for this warp: columns [wg N/2, (wg + 1) N/2),
+// the NACC accumulators added in a fixed order.
 template <typename T, int MODE, int N>
 DEVI bool tc_epilogue(const TcParams& p, uint64_t* dready, uint64_t* dfree, volatile int* abort_flag,
                       uint32_t tbase, int it, int ii) {
-  constexpr int NH = N / 2;
+  constexpr int NH = N / 2, NACC = kTcDCols / N;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wg = warp >> 2, q = warp & 3, m = q * 32 + lane;
   const int db = ii & 1;
   if (!tc_wait(&dready[db], (uint32_t)(ii >> 1) & 1u, abort_flag, p.err)) return false;
   tc_fence_after();
-  uint32_t r[NH];
-  const uint32_t ta = tmem_addr(tbase, (uint32_t)q * 32u, kTcColsD + (uint32_t)db * 64u + (uint32_t)wg * NH);
-  if constexpr (NH == 8) {
-    tmem_ld8(ta, r);
-  } else {
+  float y[NH];
 #pragma unroll
-    for (int h = 0; h < NH / 16; ++h) {
-      uint32_t r16[16];
-      tmem_ld16(ta + h * 16, r16);
+  for (int a = 0; a < NACC; ++a) {
+    const uint32_t ta = tmem_addr(tbase, (uint32_t)q * 32u,
+                                  kTcColsD + (uint32_t)db * kTcDCols + (uint32_t)(a * N + wg * NH));
+    uint32_t r[NH];
+    if constexpr (NH == 8) {
+      tmem_ld8(ta, r);
+    } else {
 #pragma unroll
-      for (int k = 0; k < 16; ++k) r[h * 16 + k] = r16[k];
+      for (int h = 0; h < NH / 16; ++h) {
+        uint32_t r16[16];
+        tmem_ld16(ta + h * 16, r16);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) r[h * 16 + k] = r16[k];
+      }
     }
+    tc_wait_ld();
+#pragma unroll
+    for (int k = 0; k < NH; ++k) y[k] = a == 0 ? __uint_as_float(r[k]) : y[k] + __uint_as_float(r[k]);
   }
-  tc_wait_ld();
   tc_fence_before();
   __syncwarp();
   if (lane == 0) mbar_arrive(&dfree[db]);
@@ -261,10 +289,9 @@ DEVI bool tc_epilogue(const TcParams& p, uint64_t* dready, uint64_t* dfree, vola
     T* dst = reinterpret_cast<T*>(p.acm + ((size_t)u * (p.I >> 3) + (i >> 3)) * N * 16) + (i & 7);
 #pragma unroll
     for (int k = 0; k < NH; ++k) {
-      const float v = __uint_as_float(r[k]);
-      const float other = __shfl_xor_sync(0xffffffffu, v, 16);
+      const float other = __shfl_xor_sync(0xffffffffu, y[k], 16);
       const int tok = wg * NH + k;
-      if (lane < 16 && tok < n) dst[(size_t)tok * 8] = from_f32<T>(silu_f32(v) * other);
+      if (lane < 16 && tok < n) dst[(size_t)tok * 8] = from_f32<T>(silu_f32(y[k]) * other);
     }
   } else {
     const int h = t * kTcM + m;
@@ -273,26 +300,29 @@ DEVI bool tc_epilogue(const TcParams& p, uint64_t* dready, uint64_t* dfree, vola
       const int tok = wg * NH + k;
       if (tok < n) {
         const int a = p.assign[first + tok];
-        p.ypart[((size_t)(a >> 3) * p.top_k + (a & 7)) * p.H + h] = __uint_as_float(r[k]);
+        p.ypart[((size_t)(a >> 3) * p.top_k + (a & 7)) * p.H + h] = y[k];
       }
     }
   }
   return true;
 }
 
+// Dequantising warp group wg: chunk wg of every stage.
 template <typename T, int MODE, int N>
-DEVI void tc_consume(const TcParams& p, uint64_t* full, uint64_t* aready, uint64_t* afree, uint64_t* dready,
+DEVI void tc_consume(const TcParams& p, uint64_t* full, uint64_t* empty, uint64_t* aready, uint64_t* dready,
                      uint64_t* dfree, volatile int* abort_flag, const uint8_t* ring, uint32_t tbase, int i0, int i1) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wg = warp >> 2, q = warp & 3, m = q * 32 + lane;
+  const int pairs = p.chunks / kTcCps;
   int j = 0, k = 0, ii = 0, pending = -1;
   for (int it = i0; it < i1; ++it, ++ii) {
-    for (int c = 0; c < p.chunks; ++c, ++j) {
-      if ((c & 1) != wg) continue;
-      const int s = j % p.ns, use = j / p.ns, ab = k & 1, b = wg * 2 + ab;
+    for (int cp = 0; cp < pairs; ++cp, ++j) {
+      const int s = j % p.ns, use = j / p.ns, b = wg * 2 + (k & 1);
       if (!tc_wait(&full[s], (uint32_t)use & 1u, abort_flag, p.err)) return;
-      if (k >= 2 && !tc_wait(&afree[b], (uint32_t)((k >> 1) - 1) & 1u, abort_flag, p.err)) return;
-      tc_dequant<T>(ring + (size_t)s * p.stage_bytes, m, p.has_zeros,
+      // A buffer b was last read by stage j - 2, released with that stage's slot (the
+      // slot's next release needs this group's own later A, so the phase cannot alias)
+      if (j >= 2 && !tc_wait(&empty[(j - 2) % p.ns], (uint32_t)((j - 2) / p.ns) & 1u, abort_flag, p.err)) return;
+      tc_dequant<T>(ring + (size_t)s * p.stage_bytes + (size_t)wg * p.chunk_bytes, m, p.has_zeros,
                     tmem_addr(tbase, (uint32_t)q * 32u, (uint32_t)b * 64u));
       tc_wait_st();
       tc_fence_before();
@@ -316,7 +346,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTcFull);
   uint64_t* empty = reinterpret_cast<uint64_t*>(smem + kTcEmpty);
   uint64_t* aready = reinterpret_cast<uint64_t*>(smem + kTcAReady);
-  uint64_t* afree = reinterpret_cast<uint64_t*>(smem + kTcAFree);
   uint64_t* dready = reinterpret_cast<uint64_t*>(smem + kTcDReady);
   uint64_t* dfree = reinterpret_cast<uint64_t*>(smem + kTcDFree);
   uint64_t* drain = reinterpret_cast<uint64_t*>(smem + kTcDrain);
@@ -330,10 +359,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 4; ++b) {
-      mbar_init(&aready[b], 4);
-      mbar_init(&afree[b], 1);
-    }
+    for (int b = 0; b < 4; ++b) mbar_init(&aready[b], 4);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&dready[b], 1);
       mbar_init(&dfree[b], 8);
@@ -356,10 +382,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
     if (lane == 0) tc_produce(p, N, full, empty, abort_flag, ring, i0, i1);
   } else if (warp == 9) {
     if (lane == 0)
-      tc_mma<N>(p, full, empty, aready, afree, dready, dfree, drain, abort_flag, ring, tbase,
+      tc_mma<N>(p, full, empty, aready, dready, dfree, drain, abort_flag, ring, tbase,
                 idesc_f16(std::is_same<T, __nv_bfloat16>::value ? 1 : 0, kTcM, N), i0, i1);
   } else {
-    tc_consume<T, MODE, N>(p, full, aready, afree, dready, dfree, abort_flag, ring, tbase, i0, i1);
+    tc_consume<T, MODE, N>(p, full, empty, aready, dready, dfree, abort_flag, ring, tbase, i0, i1);
   }
   tc_fence_before();
   __syncthreads();
@@ -442,8 +468,8 @@ __global__ void tc_repack_kernel(const int32_t* __restrict__ packed, const S* __
 }
 
 // ---------------------------------------------------------------------- host side
-static bool tc_geometry_ok(int H, int I, int group) {
-  return group == kTcK && H % kTcM == 0 && H >= 2 * kTcK && I % kTcK == 0 && I >= 2 * kTcK;
+static bool tc_geometry_ok(int H, int I, int group) {  // whole stages of two chunks
+  return group == kTcK && H % (kTcCps * kTcK) == 0 && I % (kTcCps * kTcK) == 0;
 }
 
 // MMA columns (the unit token cap) for T tokens: units of at most N tokens.
@@ -480,7 +506,7 @@ static TcScratch tc_scratch(int T, int E, int H, int I, int top_k, int N) {
 static void tc_ring(int N, int has_zeros, TcParams& p) {
   p.chunk_bytes = tc_chunk_bytes(has_zeros);
   p.b_bytes = 16u * (uint32_t)N * 16u;
-  p.stage_bytes = (uint32_t)align_up((size_t)p.chunk_bytes + p.b_bytes, 128);
+  p.stage_bytes = (uint32_t)align_up((size_t)kTcCps * (p.chunk_bytes + p.b_bytes), 128);
   int ns = (int)((kGSmemMax - kTcFixed) / p.stage_bytes);
   p.ns = ns > kTcMaxSlots ? kTcMaxSlots : ns;
 }

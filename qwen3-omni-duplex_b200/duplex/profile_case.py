@@ -3,12 +3,14 @@
     python -m duplex.profile_case --stack clock --layers 4 --steps 4
     python -m duplex.profile_case --stack moe --layers 24 --steps 20 --time
     python -m duplex.profile_case --stack grouped --tokens 256 --layers 4 --steps 40 --time
+    python -m duplex.profile_case --stack grouped --engine mma --tokens 256 --layers 4 --steps 40 --time
 
 Builds seeded synthetic Thinker-geometry layers (hidden 2048, 128 experts, top-8,
 int4 group 128 with zero points, fp16) and runs `--steps` launches of the persistent
 kernel: the clock path (`ClockStack`: q|k|v, o, MoE per layer) or the MoE chain
 (`MoEChain`: MoE only); or `--steps` grouped MoE calls (`duplex_moe_grouped`, batched
-decode of `--tokens` streams), cycling over `--layers` distinct layers so that no
+decode of `--tokens` streams, on the tcgen05 or the mma.sync expert engine), cycling
+over `--layers` distinct layers so that no
 call finds its experts in L2.  With --time it prints the time per step (per layer)
 measured with CUDA events over the last half of the steps, and for the grouped path
 the bytes of the experts it selected; device errors are always checked.
@@ -30,6 +32,7 @@ def main(argv=None) -> int:
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--tokens", type=int, default=1)
     ap.add_argument("--time", action="store_true")
+    ap.add_argument("--engine", choices=["tc", "mma"], default="tc", help="grouped expert engine")
     a = ap.parse_args(argv)
     dev = torch.device("cuda:0")
     if a.stack == "grouped":
@@ -79,11 +82,11 @@ def grouped(a, dev) -> int:
     sel = torch.empty(a.tokens, layers[0].top_k, dtype=torch.int32, device=dev)
     half = max(1, a.steps // 2)
     for s in range(a.steps - half):
-        layers[s % a.layers].forward_grouped_into(x, out, sel_out=sel)
+        layers[s % a.layers].forward_grouped_into(x, out, sel_out=sel, engine=a.engine)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for s in range(half):
-        layers[s % a.layers].forward_grouped_into(x, out)
+        layers[s % a.layers].forward_grouped_into(x, out, engine=a.engine)
     e1.record()
     torch.cuda.synchronize(dev)
     err = 0
@@ -92,10 +95,11 @@ def grouped(a, dev) -> int:
     if a.time:
         us = e0.elapsed_time(e1) * 1e3 / half
         L0 = layers[0]
-        per_expert = (L0.gu_tiles.buf.numel() + L0.dn_tiles.buf.numel()) / L0.num_experts
+        gu, dn = (L0.gu_tc, L0.dn_tc) if a.engine == "tc" else (L0.gu_tiles, L0.dn_tiles)
+        per_expert = (gu.buf.numel() + dn.buf.numel()) / L0.num_experts
         n_sel = int(torch.unique(sel).numel())
         mb = n_sel * per_expert / 1e6
-        print(f"grouped T={a.tokens}: {us:.1f} us/layer, {n_sel} experts selected, "
+        print(f"grouped[{a.engine}] T={a.tokens}: {us:.1f} us/layer, {n_sel} experts selected, "
               f"{mb:.1f} MB of experts -> {mb / us:.2f} TB/s, device errors {err}")
     if err:
         print(f"device error word {err:#x}")
