@@ -25,8 +25,7 @@
 //                   the unit's two token tiles (16 column chunks of 8 values x N tokens each).
 //   warp 9          allocates 512 tensor-memory columns; lane 0 issues the 8 MMAs
 //                   (K = 16 each) of every chunk and commits them to the barriers below.
-// Tensor memory: A buffers [group][2] x 64 columns at 0..255, D [2 items] x 128 at 256..511
-// (128 / N accumulators of N columns per item).
+// Tensor memory: A buffers [group][3] x 64 columns at 0..383, D [2 items] x 64 at 384..511.
 // Barriers: full/empty per ring stage (empty: one MMA commit per stage, which also frees
 // the A buffers the stage's MMAs read); A ready (4 warps) per A buffer; D ready (commit) /
 // D free (8 epilogue warps) per D buffer.  Every wait is
@@ -45,8 +44,9 @@ constexpr uint32_t kTcInt4Bytes = 8192;   // 128 rows x 128 nibbles
 constexpr uint32_t kTcFixed = 1024;       // barrier / flag area ahead of the ring
 constexpr uint32_t kTcFull = 0, kTcEmpty = 128, kTcAReady = 256, kTcDReady = 320,
                    kTcDFree = 336, kTcDrain = 352, kTcAbort = 360, kTcTmem = 364;
-constexpr uint32_t kTcColsD = 256;        // first D column
-constexpr uint32_t kTcDCols = 128;        // D columns per item: 128 / N accumulators of N columns
+constexpr int kTcABuf = 3;                // A buffers per dequantising group (64 columns each)
+constexpr uint32_t kTcColsD = 384;        // first D column (after 2 x 3 A buffers)
+constexpr uint32_t kTcDCols = 64;         // D columns per item (N <= 64)
 constexpr int kTcCps = 2;                 // chunks per ring stage (one per dequantising group)
 constexpr uint32_t kTcMinSmem = 120 * 1024;  // > half an SM: one CTA per SM, so the 512-column
                                              // tensor-memory allocation never waits
@@ -195,13 +195,10 @@ drain:
   }
 }
 
-// MMA issuer (one thread).  The 8 K-steps of a chunk rotate over NACC = 128 / N
-// accumulators of N columns: an MMA this narrow is short next to the latency of the
-// accumulator it reads back, so back-to-back MMAs into one accumulator would serialise.
+// MMA issuer (one thread): the 8 K-steps of each chunk into the item's accumulator.
 template <int N>
 DEVI void tc_mma(const TcParams& p, uint64_t* full, uint64_t* empty, uint64_t* aready, uint64_t* dready, uint64_t* dfree, uint64_t* drain, volatile int* abort_flag, uint8_t* ring,
                  uint32_t tbase, uint32_t idesc, int i0, int i1) {
-  constexpr int NACC = kTcDCols / N;
   const int pairs = p.chunks / kTcCps;
   int j = 0, ii = 0, k0 = 0, k1 = 0;  // stages so far; chunks so far of group 0 / group 1
   for (int it = i0; it < i1; ++it, ++ii) {
@@ -214,8 +211,8 @@ DEVI void tc_mma(const TcParams& p, uint64_t* full, uint64_t* empty, uint64_t* a
 #pragma unroll
       for (int wg = 0; wg < kTcCps; ++wg) {
         const int c = cp * kTcCps + wg;
-        const int k = wg ? k1++ : k0++, b = wg * 2 + (k & 1);
-        if (!tc_wait(&aready[b], (uint32_t)(k >> 1) & 1u, abort_flag, p.err)) goto out;
+        const int k = wg ? k1++ : k0++, b = wg * kTcABuf + k % kTcABuf;
+        if (!tc_wait(&aready[b], (uint32_t)(k / kTcABuf) & 1u, abort_flag, p.err)) goto out;
         if (c == 0 && ii >= 2 && !tc_wait(&dfree[db], (uint32_t)((ii >> 1) - 1) & 1u, abort_flag, p.err))
           goto out;
         tc_fence_after();
@@ -223,8 +220,8 @@ DEVI void tc_mma(const TcParams& p, uint64_t* full, uint64_t* empty, uint64_t* a
         const uint32_t b0 = smem_u32(st + kTcCps * p.chunk_bytes + (uint32_t)wg * p.b_bytes);
 #pragma unroll
         for (int s8 = 0; s8 < kTcK / 16; ++s8)
-          umma_ts(tbase + dcol + (uint32_t)(s8 % NACC) * N, tbase + acol + 8u * s8,
-                  smem_desc_kmajor(b0 + (uint32_t)s8 * 32u * N, 16u * N, 128u), idesc, !(c == 0 && s8 < NACC));
+          umma_ts(tbase + dcol, tbase + acol + 8u * s8, smem_desc_kmajor(b0 + (uint32_t)s8 * 32u * N, 16u * N, 128u),
+                  idesc, (c | s8) != 0);
       }
       // one commit per stage (a commit costs about as much as an MMA): it frees the ring
       // slot and, for the dequantising groups, the A buffers this stage read
@@ -245,22 +242,19 @@ out:
   }
 }
 
-// Epilogue of the CTA's ii-th item `it` for this warp: columns [wg N/2, (wg + 1) N/2),
-// the NACC accumulators added in a fixed order.
+// Epilogue of the CTA's ii-th item `it` for this warp: columns [wg N/2, (wg + 1) N/2).
 template <typename T, int MODE, int N>
 DEVI bool tc_epilogue(const TcParams& p, uint64_t* dready, uint64_t* dfree, volatile int* abort_flag,
                       uint32_t tbase, int it, int ii) {
-  constexpr int NH = N / 2, NACC = kTcDCols / N;
+  constexpr int NH = N / 2;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wg = warp >> 2, q = warp & 3, m = q * 32 + lane;
   const int db = ii & 1;
   if (!tc_wait(&dready[db], (uint32_t)(ii >> 1) & 1u, abort_flag, p.err)) return false;
   tc_fence_after();
   float y[NH];
-#pragma unroll
-  for (int a = 0; a < NACC; ++a) {
-    const uint32_t ta = tmem_addr(tbase, (uint32_t)q * 32u,
-                                  kTcColsD + (uint32_t)db * kTcDCols + (uint32_t)(a * N + wg * NH));
+  {
+    const uint32_t ta = tmem_addr(tbase, (uint32_t)q * 32u, kTcColsD + (uint32_t)db * kTcDCols + (uint32_t)(wg * NH));
     uint32_t r[NH];
     if constexpr (NH == 8) {
       tmem_ld8(ta, r);
@@ -275,7 +269,7 @@ DEVI bool tc_epilogue(const TcParams& p, uint64_t* dready, uint64_t* dfree, vola
     }
     tc_wait_ld();
 #pragma unroll
-    for (int k = 0; k < NH; ++k) y[k] = a == 0 ? __uint_as_float(r[k]) : y[k] + __uint_as_float(r[k]);
+    for (int k = 0; k < NH; ++k) y[k] = __uint_as_float(r[k]);
   }
   tc_fence_before();
   __syncwarp();
@@ -317,11 +311,14 @@ DEVI void tc_consume(const TcParams& p, uint64_t* full, uint64_t* empty, uint64_
   int j = 0, k = 0, ii = 0, pending = -1;
   for (int it = i0; it < i1; ++it, ++ii) {
     for (int cp = 0; cp < pairs; ++cp, ++j) {
-      const int s = j % p.ns, use = j / p.ns, b = wg * 2 + (k & 1);
+      const int s = j % p.ns, use = j / p.ns, b = wg * kTcABuf + k % kTcABuf;
       if (!tc_wait(&full[s], (uint32_t)use & 1u, abort_flag, p.err)) return;
-      // A buffer b was last read by stage j - 2, released with that stage's slot (the
-      // slot's next release needs this group's own later A, so the phase cannot alias)
-      if (j >= 2 && !tc_wait(&empty[(j - 2) % p.ns], (uint32_t)((j - 2) / p.ns) & 1u, abort_flag, p.err)) return;
+      // A buffer b was last read by stage j - kTcABuf, released with that stage's slot
+      // (the slot's next release needs this group's own later A, ns > kTcABuf, so the
+      // phase cannot alias)
+      if (j >= kTcABuf &&
+          !tc_wait(&empty[(j - kTcABuf) % p.ns], (uint32_t)((j - kTcABuf) / p.ns) & 1u, abort_flag, p.err))
+        return;
       tc_dequant<T>(ring + (size_t)s * p.stage_bytes + (size_t)wg * p.chunk_bytes, m, p.has_zeros,
                     tmem_addr(tbase, (uint32_t)q * 32u, (uint32_t)b * 64u));
       tc_wait_st();
@@ -359,7 +356,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 4; ++b) mbar_init(&aready[b], 4);
+    for (int b = 0; b < 2 * kTcABuf; ++b) mbar_init(&aready[b], 4);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&dready[b], 1);
       mbar_init(&dfree[b], 8);
@@ -553,6 +550,7 @@ static int tc_expert_stage(const void* x, size_t x_row_bytes, bool f16, int T, c
   p.acm = ws + L.acm;
   p.err = err;
   tc_ring(N, has_zeros, p);
+  if (p.ns <= kTcABuf) return DUPLEX_ERR_UNSUPPORTED;  // A-buffer release needs ns > kTcABuf
   // gate|up
   p.tiles = 2 * I / kTcM; p.chunks = H / kTcK;
   p.rec = reinterpret_cast<const uint8_t*>(gu_rec);
