@@ -113,6 +113,44 @@ def test_grouped_moe_rejects_before_any_launch(lib):
     assert grouped(ws=16) == 4
 
 
+def test_tc_path_sizes_and_rejections(lib):
+    """Tensor-core records and the tcgen05 entry points: sizes, and every geometry they do
+    not take rejected before any launch."""
+    n = ctypes.c_size_t()
+
+    def rb(E=128, R=1536, K=2048, group=128, zp=1, pair=1):
+        return lib.duplex_tc_records_bytes(E, R, K, group, zp, pair, ctypes.byref(n))
+
+    assert rb() == 0 and n.value == 128 * 12 * 16 * (8192 + 256 + 128)   # Thinker gate|up
+    assert rb(R=2048, K=768, pair=0) == 0 and n.value == 128 * 16 * 6 * (8192 + 256 + 128)
+    assert rb(zp=0) == 0 and n.value == 128 * 12 * 16 * (8192 + 256)
+    assert rb(group=64) == 6 and rb(K=2000) == 6 and rb(R=1000) == 6
+    assert rb(E=0) == 1
+
+    def wsb(T=256, E=128, H=2048, I=768, k=8, group=128):
+        return lib.duplex_moe_grouped_tc_workspace_bytes(T, E, H, I, k, group, 1, ctypes.byref(n))
+
+    assert wsb() == 0 and n.value > 256 * 8 * 2048 * 4
+    assert wsb(T=513) == 1 and wsb(k=9) == 1
+    assert wsb(group=64) == 6                      # one scale group per 128-column chunk
+    assert wsb(H=2176) == 6 and wsb(I=640) == 6    # whole two-chunk stages only
+    assert wsb(I=512) == 0
+    assert lib.duplex_moe_experts_grouped_tc_workspace_bytes(256, 16, 128, 2048, 768, 8, 128, 1,
+                                                             ctypes.byref(n)) == 0
+    assert lib.duplex_moe_experts_grouped_tc_workspace_bytes(256, 16, 8, 2048, 768, 8, 128, 1,
+                                                             ctypes.byref(n)) == 1  # E_total < E_local
+    p = ctypes.c_void_p(1 << 20)
+
+    def tc(x=p, T=64, group=128, ws=1 << 30, act=0, sdt=0):
+        return lib.duplex_moe_grouped_tc(x, act, T, p, None, None, 128, 2048, 768, 8, 1, p, p, sdt, 1,
+                                         group, None, p, None, None, p, ws, p, None)
+
+    assert tc(T=0) == 1 and tc(sdt=1) == 3 and tc(group=64) == 6 and tc(ws=16) == 4
+    assert tc(x=ctypes.c_void_p((1 << 20) + 4)) == 2
+    pk = ctypes.c_void_p(1 << 20)
+    assert lib.duplex_repack_tc_records(pk, pk, None, 0, 1, 128, 256, 128, 0, pk, 16, None) == 4  # too small
+
+
 def test_python_wrappers_refuse_cpu_tensors():
     import torch
     from duplex.streaming.fused_packed_moe import unpack4
