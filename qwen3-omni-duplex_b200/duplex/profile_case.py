@@ -75,7 +75,7 @@ def grouped(a, dev) -> int:
         layers.append(FusedPackedMoE.from_stacked(
             m["gate_w"], m["gu_packed"], m["gu_scale"], m["dn_packed"], m["dn_scale"],
             synth.THINKER_ACTIVE, gu_zeros=m["gu_zeros"], dn_zeros=m["dn_zeros"],
-            dtype=torch.float16, device=dev))
+            dtype=torch.float16, device=dev, tc=a.engine == "tc"))
         del m
     x = torch.randn(a.tokens, layers[0].hidden, device=dev, dtype=torch.float16, generator=gen)
     out = torch.empty_like(x)

@@ -77,14 +77,15 @@ class FusedPackedMoE(nn.Module):
     """SparseMoeBlock replacement for int4-packed experts, on the B200 kernels."""
 
     def __init__(self, block: nn.Module = None, dtype=torch.bfloat16, device="cuda",
-                 host_resident: bool = False, cpu_compute: bool = False, tc: bool = True):
+                 host_resident: bool = False, cpu_compute: bool = False, tc: bool = False):
         super().__init__()
         if dtype not in (torch.float16, torch.bfloat16):
             raise _lib.DuplexError("FusedPackedMoE on B200 runs fp16 or bf16 modules")
         self.host_resident = host_resident      # recorded; all weights stay in HBM
         self.cpu_compute = cpu_compute and host_resident
         self.pdl = True
-        self.tc = tc                            # build tensor-core records (batched decode)
+        self.tc = tc                            # also build tensor-core records (batched decode,
+                                                # a second copy of the experts; opt-in)
         if block is None:                       # filled by from_stacked()
             return
         experts = block.experts
@@ -106,7 +107,7 @@ class FusedPackedMoE(nn.Module):
     @classmethod
     def from_stacked(cls, gate_weight, gu_packed, gu_scale, dn_packed, dn_scale, top_k,
                      gu_zeros=None, dn_zeros=None, norm_topk_prob=True, gate_bias=None,
-                     dtype=torch.float16, device="cuda", tc=True):
+                     dtype=torch.float16, device="cuda", tc=False):
         """Build from raw stacked tensors ([E,2I,H/8], [E,2I,G], [E,H,I/8], [E,H,G'])."""
         m = cls(None, dtype=dtype, device=device, tc=tc)
         E, H = gate_weight.shape
@@ -199,7 +200,7 @@ class FusedPackedMoE(nn.Module):
 
     def grouped_engine(self, T: int) -> str:
         """The expert engine the grouped path takes for T tokens: "tc" (tcgen05 kernels on
-        the tensor-core records) above TC_MIN_TOKENS when the records exist, else "mma"
+        the tensor-core records, built with tc=True) above TC_MIN_TOKENS, else "mma"
         (mma.sync kernels on the tile records)."""
         return "tc" if self.gu_tc is not None and T > self.TC_MIN_TOKENS else "mma"
 
@@ -228,7 +229,8 @@ class FusedPackedMoE(nn.Module):
         engine = engine or self.grouped_engine(T)
         if engine == "tc":
             if self.gu_tc is None:
-                raise _lib.DuplexError("this layer has no tensor-core records (geometry or tc=False)")
+                raise _lib.DuplexError("this layer has no tensor-core records (build with tc=True; "
+                                       "group 128, hidden and inter multiples of 256)")
             fn, gu, dn, code = "duplex_moe_grouped_tc", self.gu_tc.buf, self.dn_tc.buf, self.gu_tc.scale_code
         else:
             fn, gu, dn, code = "duplex_moe_grouped", self.gu_tiles.buf, self.dn_tiles.buf, self.gu_tiles.scale_code

@@ -79,7 +79,7 @@ def _layer(cuda, seed, E, H, I, k, Tn, zp=True, dtype=torch.float16):
     m = FusedPackedMoE.from_stacked(T(L["gate_w"], cuda, dtype), T(L["gu_packed"], cuda),
                                     T(L["gu_scale"], cuda, dtype), T(L["dn_packed"], cuda),
                                     T(L["dn_scale"], cuda, dtype), k, gu_zeros=z("gu_zeros"),
-                                    dn_zeros=z("dn_zeros"), dtype=dtype)
+                                    dn_zeros=z("dn_zeros"), dtype=dtype, tc=True)
     assert m.gu_tc is not None
     return L, m, x
 
