@@ -18,7 +18,9 @@ bounded sample, and SM clocks sampled around the timed region.  With --gpus N
 not shard); value is the sum, time is the max over ranks.
 
 --workload ep runs BASELINE config 4 instead (duplex/ep_bench.py: 48 MoE layers, 256
-streams, experts split over the N GPUs); it prints its own line.
+streams, experts split over the N GPUs); it prints its own line. --workload batched
+runs config 3 (duplex/batched_bench.py: --streams streams through one MoE layer, one
+GPU, router logits ~N(0,1)).
 
 --impl reference times the reference algorithm on the host cores (the numpy port
 of the reference's torch dequant + gather-bmm path, oracle/), one of the 24
@@ -302,13 +304,20 @@ def main():
     ap.add_argument("--soak", type=float, default=1.0, help="seconds of load before timing")
     ap.add_argument("--cpu-samples", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["clock", "ep"], default="clock",
+    ap.add_argument("--workload", choices=["clock", "ep", "batched"], default="clock",
                     help="clock: config 2 (default line); ep: config 4, the expert-parallel "
-                         "48-layer MoE stack at 256 streams (duplex/ep_bench.py)")
+                         "48-layer MoE stack at 256 streams (duplex/ep_bench.py); batched: "
+                         "config 3, --streams streams through one MoE layer on one GPU "
+                         "(duplex/batched_bench.py)")
+    ap.add_argument("--streams", type=int, default=256, help="batched: concurrent streams")
     args = ap.parse_args()
     if args.workload == "ep" and args.impl == "ours":
         from duplex import ep_bench
         raise SystemExit(ep_bench.main(["--steps", str(args.steps), "--warmup", str(args.warmup)]))
+    if args.workload == "batched" and args.impl == "ours":
+        from duplex import batched_bench
+        raise SystemExit(batched_bench.main(["--streams", str(args.streams), "--steps", str(args.steps),
+                                             "--warmup", str(args.warmup)]))
     if args.impl == "reference":
         run_reference(args)
     else:
