@@ -217,14 +217,19 @@ __global__ void __launch_bounds__(512) g_bucket_kernel(const int* sel, int sel_s
   int* total = reinterpret_cast<int*>(smem + c_bytes + p_bytes);        // [E]
   int* base = total + kMaxExperts;                                         // [E]
   int* ubase = base + kMaxExperts;                                         // [E]
+  int* sel_s = ubase + kMaxExperts + 16;                                   // [N]: after wsum
   for (int i = tid; i < nch * E; i += 512) cnt[i] = 0;
+  // every selection into shared memory in one round of loads (both passes below read it)
+  for (int a = tid; a < N; a += 512) {
+    const int ta = a / top_k;
+    sel_s[a] = sel[(size_t)ta * sel_stride + (a - ta * top_k)];
+  }
   __syncthreads();
   // local expert of assignment a: ids outside [0, E_total) are flagged and skipped,
   // ids of other ranks' experts (outside [e_begin, e_begin + E)) are skipped
   auto expert_of = [&](int a) {
     if (a >= N) return -1;
-    const int ta = a / top_k;
-    const int g = sel[(size_t)ta * sel_stride + (a - ta * top_k)];
+    const int g = sel_s[a];
     if (g < 0 || g >= E_total) {
       set_error(err, DUPLEX_DEVERR_EXPERT);
       return -1;
@@ -1130,7 +1135,7 @@ static int g_expert_stage(const void* x, size_t x_row_bytes, bool f16, int T, co
   {
     const int N = T * top_k, nch = (N + 31) / 32;
     const int smem = (int)(align_up((size_t)nch * E, 16) + align_up((size_t)nch * E * 2, 16) +
-                           3 * kMaxExperts * 4 + 16 * 4);
+                           3 * kMaxExperts * 4 + 16 * 4 + (size_t)N * 4);
     if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(g_bucket_kernel), kGSmemMax))) return rc;
     if ((rc = g_launch(g_bucket_kernel, dim3(1), dim3(512), smem, st, pdl_first, sel, meta_stride, T, E, top_k, tcap,
                        e_begin,

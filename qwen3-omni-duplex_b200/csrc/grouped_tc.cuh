@@ -529,7 +529,7 @@ static int tc_expert_stage(const void* x, size_t x_row_bytes, bool f16, int T, c
   {
     const int NA = T * top_k, nch = (NA + 31) / 32;
     const int smem = (int)(align_up((size_t)nch * E, 16) + align_up((size_t)nch * E * 2, 16) +
-                           3 * kMaxExperts * 4 + 16 * 4);
+                           3 * kMaxExperts * 4 + 16 * 4 + (size_t)NA * 4);
     if ((rc = ensure_smem_attr(reinterpret_cast<const void*>(g_bucket_kernel), kGSmemMax))) return rc;
     if ((rc = g_launch(g_bucket_kernel, dim3(1), dim3(512), smem, st, pdl_first, sel, meta_stride, T, E, top_k, N,
                        e_begin, E_total, reinterpret_cast<int*>(ws + G.assign), reinterpret_cast<int*>(ws + G.units),
