@@ -8,7 +8,7 @@
 // epilogue) and down (128 output rows, fp32 partial rows per assignment), and the shared
 // combine.
 //
-// Weights: "MMA records", per (expert, 128-row tile, 128-column chunk) 8192 bytes of int4
+// Weights: "tensor-core records", per (expert, 128-row tile, 128-column chunk) 8192 bytes of int4
 // in a thread-per-row order, 128 scales and optionally 128 zero points (bytes).  The
 // chunk is one scale group, so a thread dequantises its row's 128 values exactly as the
 // reference does: (nibble - zero) is an exact small integer in the 16-bit activation
@@ -39,7 +39,6 @@ constexpr int kTcK = 128;                 // K per chunk (one scale group)
 constexpr int kTcM = 128;                 // rows per tile (MMA M)
 constexpr int kTcMaxSlots = 16;
 constexpr int kTcThreads = 320;
-constexpr int kTcMaxN = 64;
 constexpr uint32_t kTcInt4Bytes = 8192;   // 128 rows x 128 nibbles
 constexpr uint32_t kTcFixed = 1024;       // barrier / flag area ahead of the ring
 constexpr uint32_t kTcFull = 0, kTcEmpty = 128, kTcAReady = 256, kTcDReady = 320,
@@ -60,7 +59,7 @@ struct TcParams {
   int tiles, chunks;          // this kernel's weight: gate|up 2I/128 x H/128, down H/128 x I/128
   int has_zeros, ns;
   uint32_t chunk_bytes, b_bytes, stage_bytes;
-  const uint8_t* rec;         // MMA records of local expert 0
+  const uint8_t* rec;         // tensor-core records of local expert 0
   const uint8_t* bsrc;        // token tiles [unit][K/8][N][8 values]
   uint8_t* acm;               // gate|up output, down's token tiles [unit][I/8][N][8 values]
   const int* assign;
@@ -414,7 +413,7 @@ __global__ void __launch_bounds__(256) tc_gather_kernel(const uint8_t* x, size_t
   }
 }
 
-// MMA records from the reference's stacked tensors: packed [E][R][K/8] int32 (value k at
+// Tensor-core records from the reference's stacked tensors: packed [E][R][K/8] int32 (value k at
 // bits 4 (k % 8) of word k / 8), scale [E][R][K/128], zeros [E][R][ceil(G/8)] int32 or
 // null (zero point 8).  pair_halves (gate|up, R = 2 I): tile t holds intermediate rows
 // 64 t .. 64 t + 63 as tile row 32 q + 16 h + j = source row h I + 64 t + 16 q + j.
