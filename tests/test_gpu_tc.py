@@ -170,3 +170,41 @@ def test_tc_expert_shards_sum_to_the_layer(cuda, shards):
                                   L["dn_packed"], L["dn_scale"], L["gu_zeros"], L["dn_zeros"])
     assert rel_err(total.cpu().numpy(), ref) <= 2e-3
     assert rel_err(total.cpu().numpy(), out_full.float().cpu().numpy()) <= 1e-3
+
+
+@pytest.mark.parametrize("Tn", [1, 3])
+def test_tc_smallest_calls(cuda, Tn):
+    """One token and a ragged three: 16-column units almost entirely padding."""
+    L, m, x = _layer(cuda, 90 + Tn, 128, 2048, 768, 8, Tn)
+    res = O.round_to(np.random.default_rng(Tn).standard_normal((Tn, 2048)), "float16")
+    out, w, sel = _run(cuda, m, x, torch.float16, residual=T(res, cuda, torch.float16))
+    assert int(m.err.item()) == 0
+    ref = O.moe_experts_by_expert(x, sel.cpu().numpy(), w.cpu().numpy(), L["gu_packed"], L["gu_scale"],
+                                  L["dn_packed"], L["dn_scale"], L["gu_zeros"], L["dn_zeros"])
+    assert rel_err(out.float().cpu().numpy() - res.astype(np.float32), ref) <= 2e-3
+
+
+def test_tc_skewed_routing_splits_experts_into_many_units(cuda):
+    """512 tokens that all pick experts 0-7 (router logits given): every selected expert
+    holds 512 assignments, split into eight 64-token units, 120 experts idle."""
+    L, m, x = _layer(cuda, 95, 128, 2048, 768, 8, 512)
+    rng = np.random.default_rng(95)
+    lg = rng.standard_normal((512, 128)).astype(np.float32) * 0.1
+    lg[:, :8] += 10.0
+    lg = O.round_to(lg, "float16").astype(np.float32)
+    x_t = T(x, cuda, torch.float16)
+    outs = {}
+    for eng in ("tc", "mma"):
+        out = torch.empty(512, 2048, dtype=torch.float16, device=cuda)
+        w = torch.empty(512, 8, dtype=torch.float32, device=cuda)
+        sel = torch.empty(512, 8, dtype=torch.int32, device=cuda)
+        m.forward_grouped_into(x_t, out, w_out=w, sel_out=sel, logits=T(lg, cuda), engine=eng)
+        torch.cuda.synchronize()
+        assert int(m.err.item()) == 0
+        outs[eng] = (out.float().cpu().numpy(), w.cpu().numpy(), sel.cpu().numpy())
+    _, w, sel = outs["tc"]
+    assert set(np.unique(sel)) == set(range(8))
+    ref = O.moe_experts_by_expert(x, sel, w, L["gu_packed"], L["gu_scale"], L["dn_packed"], L["dn_scale"],
+                                  L["gu_zeros"], L["dn_zeros"])
+    assert rel_err(outs["tc"][0], ref) <= 2e-3
+    assert rel_err(outs["mma"][0], ref) <= 2e-3
