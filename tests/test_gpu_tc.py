@@ -208,3 +208,39 @@ def test_tc_skewed_routing_splits_experts_into_many_units(cuda):
                                   L["gu_zeros"], L["dn_zeros"])
     assert rel_err(outs["tc"][0], ref) <= 2e-3
     assert rel_err(outs["mma"][0], ref) <= 2e-3
+
+
+def test_tc_experts_read_packed_exchange_rows(cuda):
+    """An expert-parallel rank's view: token rows, ids and weights read straight out of
+    the exchange rows (row stride > H, meta stride > k) give the same bits as the dense
+    inputs."""
+    from duplex.streaming.ep_moe import exchange_row_bytes
+    L, m, x = _layer(cuda, 97, 128, 2048, 768, 8, 96)
+    Tn, H, I = 96, 2048, 768
+    x_t = T(x, cuda, torch.float16)
+    row = exchange_row_bytes(H, 2, 8)
+    pack = torch.zeros(Tn, row, dtype=torch.uint8, device=cuda)
+    lws = torch.empty(Tn * 128 * 4, dtype=torch.uint8, device=cuda)
+    _lib.call("duplex_moe_route_grouped", _lib.ptr(x_t), _lib.DTYPE_F16, Tn, _lib.ptr(m.gate.weight), None, None,
+              128, H, 8, 1, None, None, _lib.ptr(pack), row, _lib.ptr(lws), lws.numel(), None, _lib.stream_of(x_t))
+    sel = pack[:, 2 * H:2 * H + 32].contiguous().view(torch.int32)
+    w = pack[:, 2 * H + 32:2 * H + 64].contiguous().view(torch.float32)
+    n = _lib.ctypes.c_size_t()
+    _lib.call("duplex_moe_experts_grouped_tc_workspace_bytes", Tn, 128, 128, H, I, 8, 128, 1, _lib.ctypes.byref(n))
+    ws = torch.empty(n.value, dtype=torch.uint8, device=cuda)
+    outs = []
+    for xp, xs, sp, wp, ms in ((x_t, H, sel, w, 8),
+                               (pack, row // 2, pack[:, 2 * H:], pack[:, 2 * H + 32:], row // 4)):
+        out = torch.empty(Tn, H, dtype=torch.float32, device=cuda)
+        err = torch.zeros(1, dtype=torch.int32, device=cuda)
+        _lib.call("duplex_moe_experts_grouped_tc", _lib.ptr(xp), _lib.DTYPE_F16, Tn, xs, _lib.ptr(sp), _lib.ptr(wp),
+                  ms, 8, 0, 128, 128, H, I, _lib.ptr(m.gu_tc.buf), _lib.ptr(m.dn_tc.buf), m.gu_tc.scale_code, 1,
+                  128, None, _lib.ptr(out), _lib.DTYPE_F32, _lib.ptr(ws), ws.numel(), _lib.ptr(err),
+                  _lib.stream_of(x_t))
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1])
+    ref = O.moe_experts_by_expert(x, sel.cpu().numpy(), w.cpu().numpy(), L["gu_packed"], L["gu_scale"],
+                                  L["dn_packed"], L["dn_scale"], L["gu_zeros"], L["dn_zeros"])
+    assert rel_err(outs[1].cpu().numpy(), ref) <= 2e-3
