@@ -408,7 +408,11 @@ extern "C" int duplex_moe_forward_noalloc(
     const void* dn_tiles, int scale_dtype, int has_zeros, int32_t group, const void* residual,
     void* out, float* w_out, int32_t* sel_out, int32_t* err, float rms_eps, int pdl,
     void* stream) {
-  if (T < 1 || E < 1 || H < 1 || I < 1 || top_k < 1) return DUPLEX_ERR_ARG;
+  // the limits of duplex_moe_forward first, so the scratch size below cannot overflow
+  if (T < 1 || T > kMaxTokens || E < 1 || E > kMaxExperts || top_k < 1 || top_k > kMaxTopK ||
+      top_k > E || H < 1 || I < 1)
+    return DUPLEX_ERR_ARG;
+  if (H > kRouteMaxChunks * 32 * 8 || I > (1 << 20)) return DUPLEX_ERR_UNSUPPORTED;
   const MoeScratch L = moe_scratch_layout(T, E, H, I, top_k);
   if (L.total > kNoAllocScratchBytes) return DUPLEX_ERR_SCRATCH_LIMIT;
   void* ws = nullptr;

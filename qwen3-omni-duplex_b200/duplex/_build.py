@@ -45,21 +45,36 @@ def needs_build(lib: Path = LIB) -> bool:
     return any(p.stat().st_mtime > t for p in deps())
 
 
-def build(force: bool = False, verbose: bool = False, lib: Path = LIB) -> Path:
-    if not force and not needs_build(lib):
-        return lib
-    tmp = lib.with_suffix(".so.tmp")
-    cmd = [nvcc_path(), ARCH, "-O3", "-lineinfo", "-std=c++17", "--shared",
+def _compile(src: Path, obj: Path, verbose: bool) -> str:
+    cmd = [nvcc_path(), ARCH, "-O3", "-lineinfo", "-std=c++17", "-c",
            "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr",
-           f"-I{INCLUDE}", f"-I{CSRC}", "-o", str(tmp)]
+           f"-I{INCLUDE}", f"-I{CSRC}", "-o", str(obj), str(src)]
     if verbose:
         cmd += ["-Xptxas", "-v"]
-    cmd += [str(s) for s in sources()]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
-        raise RuntimeError("nvcc failed:\n" + r.stdout + r.stderr)
+        raise RuntimeError(f"nvcc failed on {src.name}:\n" + r.stdout + r.stderr)
+    return r.stdout + r.stderr
+
+
+def build(force: bool = False, verbose: bool = False, lib: Path = LIB) -> Path:
+    """Compile every csrc/*.cu for sm_100a (one nvcc process per file, in parallel)
+    and link them into the shared library."""
+    if not force and not needs_build(lib):
+        return lib
+    from concurrent.futures import ThreadPoolExecutor
+    import tempfile
+    with tempfile.TemporaryDirectory(prefix="duplex_build_") as tmpd:
+        objs = [Path(tmpd) / (s.stem + ".o") for s in sources()]
+        with ThreadPoolExecutor(max(1, min(len(objs), os.cpu_count() or 1))) as ex:
+            logs = list(ex.map(lambda so: _compile(so[0], so[1], verbose), zip(sources(), objs)))
+        tmp = lib.with_suffix(".so.tmp")
+        cmd = [nvcc_path(), ARCH, "--shared", "-o", str(tmp)] + [str(o) for o in objs]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError("nvcc link failed:\n" + r.stdout + r.stderr)
     if verbose:
-        sys.stderr.write(r.stdout + r.stderr)
+        sys.stderr.write("".join(logs))
     os.replace(tmp, lib)
     return lib
 

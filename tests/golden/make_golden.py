@@ -107,9 +107,12 @@ def moe_case(torch, nn, F, fpm, synth, seed, E, H, I, top_k, group, T, dtypes):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("DUPLEX_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("DUPLEX_REFERENCE"),
+                    help="checkout of the reference project (or set DUPLEX_REFERENCE)")
     ap.add_argument("--skip-large", action="store_true")
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("give --ref (or DUPLEX_REFERENCE): the reference checkout to run")
 
     import torch
     import torch.nn as nn
