@@ -42,8 +42,9 @@ extern "C" {
 /* ---- device-side error word bits (written with atomicOr into `err`, never trap) */
 #define DUPLEX_DEVERR_EXPERT 1    /* an expert id outside [0, E) was clamped to 0 */
 #define DUPLEX_DEVERR_TIMEOUT 2   /* a bounded pipeline wait gave up */
-/* duplex_stack_forward also ORs, from this bit up, which of its waits gave up:
- * 1 ring slot free, 2 routing plan, 3 ring slot filled, 4 exchange word, 5 drain. */
+/* duplex_stack_forward also records, from this bit up, which of its waits gave up
+ * first: 1 ring slot free, 2 routing plan, 3 ring slot filled, 4 grid barrier,
+ * 5 drain, 6 cluster exchange. */
 #define DUPLEX_DEVERR_SITE_SHIFT 8
 
 /* ---- dtype codes */
@@ -290,16 +291,24 @@ int duplex_moe_experts_grouped_tc(const void* x, int act_dtype, int32_t T, int64
  * launch: per layer q|k|v of rms(h), o of q (+ h) -> h1, router / top-k / plan on rms(h1),
  * gate|up + SiLU, down + combine (+ h1 when moe_residual) -> next h.  With has_attn == 0 a
  * layer is only the MoE (x -> MoE(rms(x)) (+ x)).  `layers` is a DEVICE array of n_layers
- * descriptors (tiles from duplex_repack_tiles: qkv [qkv_R][H], o [H][q_dim], gate|up with
- * pair_halves, down).  The attention core is not part of it: o reads the first q_dim
- * outputs of q|k|v.  H, I, q_dim and group multiples of 64; scale dtype == act dtype.
- * workspace: duplex_stack_workspace_bytes, ZERO-FILLED before the first call and kept
- * unchanged between calls (phases hand data over through flagged words in it, and a
- * generation counter in it, advanced by every launch, keeps the flags of earlier
- * launches from matching).  One call at a time per workspace.  err is required: a
- * wait that times out sets DUPLEX_DEVERR_TIMEOUT in it, and while that bit stays set
- * later launches give up at once instead of waiting.  The launch is cooperative (one
- * CTA per SM, all co-resident).
+ * descriptors: q|k|v [qkv_R][H] and o [H][q_dim] tiles and the gate|up tiles (pair_halves)
+ * from duplex_repack_tiles, in gate_w the router's gate matrix as gate records from
+ * duplex_repack_gate_records (+ gate_b [E] in the act dtype), and in dn_tiles the down
+ * projection as K-slice records from duplex_repack_down_slices.  The attention
+ * core is not part of it: o reads the first q_dim outputs of q|k|v.
+ * Limits: H a multiple of 128 and <= 4096, I a multiple of 128, q_dim a multiple of 64,
+ * group 32, 64 or 128, scale dtype == act dtype.
+ * The launch is in clusters of 8 CTAs (one CTA per SM, as many clusters as can be resident
+ * at once): each MoE layer has one grid-wide barrier, the other hand-offs stay inside a
+ * cluster.  It expects the GPU's SMs to itself while it runs: a CTA that cannot start
+ * in time makes the grid barrier give up (DUPLEX_DEVERR_TIMEOUT), it never hangs.  workspace: duplex_stack_workspace_bytes; one call at a time per workspace
+ * (the grid barrier counter in it is zeroed by a memset issued before the launch).
+ * err is required: a bounded wait that gives up sets DUPLEX_DEVERR_TIMEOUT (and the
+ * site of the first one from DUPLEX_DEVERR_SITE_SHIFT) instead of hanging, and while
+ * that bit stays set later launches give up at once.  wait_limit_cycles: the bound of
+ * every wait in SM clock cycles (<= 0: about 2 s).  test_flags: 0; bit 0 makes the first
+ * grid barrier wait for one arrival more than the grid makes, so that it gives up (the
+ * timeout path's test).  Bit-identical results run to run.
  */
 typedef struct duplex_stack_layer {
   const void* qkv_tiles;
@@ -317,7 +326,33 @@ int duplex_stack_forward(const duplex_stack_layer* layers, int32_t n_layers, int
                          int scale_dtype, int has_zeros, int32_t T, int32_t H, int32_t E,
                          int32_t I, int32_t top_k, int32_t norm_topk, int32_t qkv_R,
                          int32_t q_dim, int32_t group, float rms_eps, void* workspace,
-                         size_t workspace_bytes, int32_t* err, void* stream);
+                         size_t workspace_bytes, int64_t wait_limit_cycles, int32_t test_flags,
+                         int32_t* err, void* stream);
+
+/*
+ * down_slices_bytes / repack_down_slices -- the down projection's layout for
+ * duplex_stack_forward, built once from the reference's stacked down tensors (packed
+ * [E][H][I/8] int32, scale [E][H][I/group], zeros [E][H][ceil(G/8)] or NULL; the
+ * reference stacks them at fused_packed_moe.py:117-123): one record per (expert, 128-column
+ * slice of I, 16 rows of H) in the tile-record layout with K = 128, padded to 16 bytes,
+ * ordered [E][I/128][H/16].  group 32, 64 or 128; H a multiple of 16, I of 128.
+ */
+/*
+ * gate_records_bytes / repack_gate_records -- the router's gate matrix (nn.Linear weight
+ * [E][H], fp16 or bf16, as the reference's FusedPackedMoE.gate holds it,
+ * fused_packed_moe.py:112) for duplex_stack_forward: per block of 16 experts and
+ * 16-column step, the 32 lanes' mma.sync A fragments (512 bytes), rows past E zero.
+ * H a multiple of 16.
+ */
+int duplex_gate_records_bytes(int32_t E, int32_t H, size_t* bytes);
+int duplex_repack_gate_records(const void* gate_w, int dtype, int32_t E, int32_t H, void* out,
+                               size_t out_bytes, void* stream);
+
+int duplex_down_slices_bytes(int32_t E, int32_t H, int32_t I, int32_t group, int has_zeros,
+                             size_t* bytes);
+int duplex_repack_down_slices(const int32_t* packed, const void* scale, const int32_t* zeros,
+                              int scale_dtype, int32_t E, int32_t H, int32_t I, int32_t group,
+                              void* out, size_t out_bytes, void* stream);
 
 /*
  * moe_forward_noalloc -- no counterpart in the reference.  Same computation and

@@ -1,34 +1,42 @@
-// Persistent clock-path kernel: every int4 linear of L Thinker layers for T <= 8
-// decode tokens in ONE launch (one CTA per SM, 16 consumer warps + 1 producer warp).
+// Persistent clock-path kernel on thread-block clusters: every int4 linear of L
+// Thinker layers for T <= 8 decode tokens in ONE launch.
 //
-// Per layer the consumers run the phases
-//   Q  fused q|k|v dequant-GEMV of rms(h)                      -> qkv
-//   O  o projection of q (+ h)                                 -> h1
-//   R  router logits of rms(h1), one gate row per CTA          -> logits
-//   D  top-k / softmax / renormalise / unit plan, redundantly in every CTA
-//   G  gate|up of the selected experts, SiLU(gate)*up           -> act
-//   N  down projection over all units, routing-weighted combine (+ h1) -> h'
+// The grid is C clusters of kCS = 8 CTAs (one CTA per SM, 16 consumer warps + one
+// producer warp).  A decode MoE layer runs
 //
-// Phases hand their outputs to the next phase through small buffers in global
-// memory, separated by grid-wide barriers: one red.release per CTA on a counter
-// and one acquiring poller per CTA, the fastest all-to-all hand-off measured on
-// this part (~1.3 us for 148 CTAs; polling the data words themselves from many
-// threads turns the few lines involved into L2 hot spots and is several times
-// slower).  Outputs are read back through L2 (ld.global.cg).  Per MoE layer
-// there are three barriers (h, logits, act), per clock layer five (+ qkv, h1).
+//   reduce   the layer input h = sum of the C clusters' partial outputs of the
+//            previous layer (+ residual), each CTA for its H / 8 rows, then sent to
+//            the other CTAs of its cluster through distributed shared memory (DSMEM),
+//            with each CTA's partial sum of squares (RMSNorm)
+//   router   each CTA of a cluster computes E / 8 logits from gate rows that were
+//            streamed into its shared memory during the previous layer, and sends
+//            them to the cluster (DSMEM)
+//   plan     top-k / softmax / renormalise / unit plan, identical in every CTA
+//   items    the cluster's share of the (selected expert, 128-column slice of the
+//            intermediate) items: CTA r computes gate|up rows [16 r, 16 r + 16) of
+//            the slice, SiLU(gate) * up, and sends them to the cluster (DSMEM); then
+//            every CTA multiplies the slice's 128 intermediate values by the matching
+//            128 columns of the expert's down weights for its H / 8 output rows,
+//            weighted by the routing weight, accumulating in registers
+//   end      each CTA writes its rows of the cluster's partial output (fp32) and
+//            arrives on the grid barrier
 //
-// The producer warp walks the same schedule and streams the weight records of the
-// CTA's tiles into a shared-memory ring with one bulk copy each: the static
-// weights (q|k|v, o, gate rows) are in flight ahead of their phase, the next
-// layer's static weights are prefetched into L2 while the router decides, and
-// the experts' gate|up and down records are all issued as soon as this CTA has
-// built the routing plan.
+// so a MoE layer has ONE grid-wide barrier; every other hand-off stays inside a
+// cluster (mbarriers with cluster-scope release / acquire).  A clock layer adds the
+// fused q|k|v and the o projection, each followed by a grid barrier (their outputs
+// are needed by every CTA).
+//
+// The producer warp streams each stage (one bulk copy into a shared-memory ring):
+// the static weights of a layer (q|k|v and o tiles, this CTA's gate rows) as soon
+// as ring slots free up -- i.e. while the previous layer's experts are consumed --
+// and the experts' gate|up tile pairs and down K-slice records as soon as this CTA
+// has built the routing plan.
 //
 // Numerics follow dq_gemv_kernel (gemv.cu) and route_kernel (moe.cu): offset
 // dequantisation ((M + n) in fp16/bf16 straight into mma.sync, fp32 accumulation,
 // the exact group correction D - P - z Q applied in fp32 with the group scale),
 // logits rounded to the activation dtype, fp32 softmax, ties of the top-k to the
-// lower expert id.
+// lower expert id.  Every sum runs in a fixed order, so launches are bit-identical.
 #include "gemv_core.cuh"
 #include "moe.cuh"
 #include "topk.cuh"
@@ -39,65 +47,169 @@ int record_cuda(cudaError_t e);
 int num_sms();
 int ensure_smem_attr(const void* fn, int bytes);
 
+constexpr int kCS = 8;            // CTAs per cluster
+constexpr int kMaxClusters = 32;  // partial-sum slots in the workspace
+constexpr int kSliceK = 128;      // intermediate columns per item (kCS gate|up tiles of 16 rows)
+static_assert(kSliceK == 16 * kCS, "one gate|up tile per CTA of a cluster per item");
+constexpr int kMaxRecPerWarp = 2; // down records (16 output rows) per warp: H <= 4096
+constexpr uint32_t kXdPitch = 320;  // bytes per token row of a staged slice (conflict-free)
+
 struct StackParams {
   const duplex_stack_layer* layers;
   int n_layers, T, H, E, I, top_k, norm, q_dim, qkv_R, has_attn, moe_residual;
-  TileGeom tq, to, tgu, tdn;
-  int RbQ, RbO, RbD;
+  TileGeom tq, to, tgu, tks;  // q|k|v, o, gate|up tiles; down K-slice records
+  int RbQ, RbO;
+  int S;      // down K-slices per expert (I / kSliceK)
+  int rrows;  // output rows of the down projection per CTA (H / kCS)
+  int nblk;   // 16-expert blocks of the gate records
+  int KS;     // 16-column k-steps of a gate block (H / 16)
+  int kps;    // k-steps per gate ring stage
   float rms_eps;
   const void* x_in;
   void* out;
-  void* hbuf[2];  // layer input / output h   [T][H] (layer parity)
-  void* qkv;      // q|k|v                     [T][qkv_R]
-  void* h1;       // h + o(q)                  [T][H]
-  float* logits;  // [T][E]
-  void* act;      // SiLU(gate)*up            [units][T][I]
+  float* part;  // [2][kMaxClusters][T][H] partial outputs of the clusters
+  void* qkv;    // q|k|v [T][qkv_R]
+  void* h1;     // h + o(q) [T][H]
   unsigned* barrier;  // grid barrier counter, zeroed before the launch
   int* err;
-  int nslots, ups, act_units;
-  uint32_t slot_bytes, off_ring, off_x, off_gsum, x_pitch, xd_pitch;
+  long long wait_limit;
+  int test_flags;
+  int nslots;
+  int ib;             // items per batch
+  uint32_t dn_bytes;  // a CTA's down records of one item
+  uint32_t slot_bytes, off_ring, off_x, off_gsum, off_h, off_xd, off_av, off_dg, x_pitch;
 };
 
 // fixed shared-memory map (bytes)
 constexpr uint32_t kSFull = 0;        // 16 mbarriers
 constexpr uint32_t kSEmpty = 128;     // 16 mbarriers
-constexpr uint32_t kSPlan = 256;      // mbarrier: plan of the current layer ready
-constexpr uint32_t kSAbort = 272;     // int
-constexpr uint32_t kSNUnits = 276;    // int
-constexpr uint32_t kSSel = 512;       // [8 tokens][8] ints
-constexpr uint32_t kSSelBits = 768;   // [8 tokens][8] words: selected experts
-constexpr uint32_t kSUnitE = 1024;    // kMaxUnits ints
-constexpr uint32_t kSUnitM = 1280;    // kMaxUnits uints
-constexpr uint32_t kSUnitW = 1536;    // kMaxUnits * 8 floats
-constexpr uint32_t kSLogit = 3584;    // [8][kMaxExperts] floats
+constexpr uint32_t kSPlan = 256;      // mbarrier: plan of the current layer ready (producer)
+constexpr uint32_t kSHx = 264;        // mbarrier: h slices of the cluster arrived
+constexpr uint32_t kSLg = 272;        // mbarrier: logits of the cluster arrived
+constexpr uint32_t kSAct = 280;       // 2 mbarriers: intermediate slices arrived
+constexpr uint32_t kSAbort = 296;     // int
+constexpr uint32_t kSNUnits = 300;    // int
+constexpr uint32_t kSSsq = 320;       // [kCS ranks][8 tokens] floats: sums of squares
+constexpr uint32_t kSSel = 576;       // [8 tokens][8] ints
+constexpr uint32_t kSSelBits = 832;   // [8 tokens][8] words: selected experts
+constexpr uint32_t kSUnitE = 1088;    // kMaxUnits ints
+constexpr uint32_t kSUnitM = 1344;    // kMaxUnits uints
+constexpr uint32_t kSUnitW = 1600;    // kMaxUnits * 8 floats
+constexpr uint32_t kSLogit = 3648;    // [8 tokens][kMaxExperts] floats
+constexpr uint32_t kSInv = 11840;     // [8] floats: RMS scale per token
 // cross-warp reductions (kCW warps x 2 records x kRedStride floats) and scratch
 constexpr int kRedStride = 152;  // swizzled [8 tokens][16 rows] block, see red_at
-constexpr uint32_t kSRed = kSLogit + 8 * kMaxExperts * 4;
+constexpr uint32_t kSRed = 11904;
 constexpr uint32_t kSRedBytes = kCW * 2 * kRedStride * 4;
 constexpr uint32_t kSFixedEnd = kSRed + kSRedBytes;
+static_assert(kSSel >= kSSsq + kCS * 8 * 4, "smem map");
+static_assert(kSInv >= kSLogit + 8 * kMaxExperts * 4, "smem map");
+static_assert(kSRed % 128 == 0 && kSRed >= kSInv + 32, "smem map");
+constexpr int kMaxBatch = 4;      // items of a CTA processed together (one exchange)
+constexpr int kMaxBatchRows = 32; // batch items x tokens: staged intermediate rows per buffer
 constexpr int kSlotsMax = 16;
 constexpr int kMaxChunks = 8;  // 8-value chunks of staged rows per consumer thread
 
 // Which wait of this kernel gave up first: err bits from DUPLEX_DEVERR_SITE_SHIFT.
-enum : int { kSiteEmpty = 1, kSitePlan = 2, kSiteFull = 3, kSiteGrid = 4, kSiteDrain = 5 };
+enum : int {
+  kSiteEmpty = 1, kSitePlan = 2, kSiteFull = 3, kSiteGrid = 4, kSiteDrain = 5, kSiteCluster = 6
+};
 
-// Code size matters here: every layer walks all phases, so the per-phase work
-// lives in one non-inlined copy each (staging, tile compute, router, plan, the
-// barrier, the slow path of the waits) to keep the loop inside the instruction
-// cache.
+// Code size and calls both cost here.  The phases on the per-item path (the tile
+// loops, the exchanges, the router) are inlined: a call saves live registers to
+// the stack, and with ~227 KB of shared memory the L1 left for that local memory is
+// small (measured: 21.7 -> 18.6 us per MoE layer).  The once-per-layer phases stay
+// in one non-inlined copy each, to keep the layer loop inside the instruction cache.
 #define DEVN __device__ __noinline__
 
-DEVI void give_up(volatile int* abort, int* err, int site) {
-  *abort = 1;
-  set_error(err, DUPLEX_DEVERR_TIMEOUT | (site << DUPLEX_DEVERR_SITE_SHIFT));
+// Position in the ring of stage buffers: slot and the parity of its use, advanced
+// stage by stage (no division per stage).
+struct RingPos {
+  int slot;
+  uint32_t phase;
+  DEVI void next(int ns) {
+    if (++slot == ns) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
+// ------------------------------------------------------------------ cluster PTX
+DEVI uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+DEVI uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+DEVI uint32_t nclusters_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// address of the same shared-memory location in CTA `rank` of this cluster
+DEVI uint32_t peer_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+DEVI void st_peer_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x),
+               "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+DEVI void st_peer_v2(uint32_t addr, uint2 v) {
+  asm volatile("st.shared::cluster.v2.b32 [%0], {%1, %2};" ::"r"(addr), "r"(v.x), "r"(v.y)
+               : "memory");
+}
+DEVI void st_peer_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+DEVI void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+// one arrival on the mbarrier at cluster shared address `addr`, releasing this
+// thread's (and, through the preceding CTA barrier, its CTA's) earlier writes
+DEVI void mbar_arrive_peer(uint32_t addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr)
+               : "memory");
+}
+DEVI bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
+      : "memory");
+  return ok != 0;
+}
+// all threads of all CTAs of the cluster (every thread of the CTA executes it)
+DEVI void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
 }
 
-DEVN void wait_phase_slow(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
-                          int site) {
+// ------------------------------------------------------------------ bounded waits
+// Give up: stop this CTA's waits and record DUPLEX_DEVERR_TIMEOUT; the first wait
+// of the launch that gives up also records its site.
+DEVI void give_up(volatile int* abort, int* err, int site) {
+  *abort = 1;
+  const int old = atomicOr(err, DUPLEX_DEVERR_TIMEOUT);
+  if (((old >> DUPLEX_DEVERR_SITE_SHIFT) & 0xFF) == 0)
+    atomicCAS(err, old | DUPLEX_DEVERR_TIMEOUT,
+              old | DUPLEX_DEVERR_TIMEOUT | (site << DUPLEX_DEVERR_SITE_SHIFT));
+}
+
+DEVN void wait_phase_slow(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int site,
+                          long long limit, bool cluster) {
   const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!(cluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity))) {
     if (*abort) return;
-    if (clock64() - t0 > kWaitLimitCycles) {
+    if (clock64() - t0 > limit) {
       give_up(abort, err, site);
       return;
     }
@@ -105,9 +217,29 @@ DEVN void wait_phase_slow(uint64_t* bar, uint32_t parity, volatile int* abort, i
 }
 
 // Bounded wait on an mbarrier phase; returns at once when this CTA has given up.
-DEVI void wait_phase(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int site) {
+DEVI void wait_phase(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int site,
+                     long long limit) {
   if (*abort || mbar_try_wait(bar, parity)) return;
-  wait_phase_slow(bar, parity, abort, err, site);
+  wait_phase_slow(bar, parity, abort, err, site, limit, false);
+}
+
+// Bounded wait of the consumers on a cluster exchange: thread 0 waits (acquire at
+// cluster scope), then the consumer barrier publishes the data to the CTA.
+DEVI void wait_cluster_xchg(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
+                            long long limit) {
+  if (threadIdx.x == 0 && !*abort && !mbar_try_wait_cluster(bar, parity))
+    wait_phase_slow(bar, parity, abort, err, kSiteCluster, limit, true);
+  named_bar_sync(1, kConsumers);
+}
+
+// After this CTA's consumers wrote their part of an exchange into every CTA of the
+// cluster: one arrival on `bar` of each CTA (the consumer barrier orders the writes
+// of all threads before the arriving threads' releases).
+DEVI void signal_cluster_xchg(uint64_t* bar) {
+  named_bar_sync(1, kConsumers);
+  // thread q arrives on CTA q's barrier: each release is a fence of its own, so the
+  // eight run in parallel rather than one after another
+  if (threadIdx.x < kCS) mbar_arrive_peer(peer_addr(bar, threadIdx.x));
 }
 
 DEVI unsigned ld_acquire_gpu(const unsigned* p) {
@@ -117,20 +249,21 @@ DEVI unsigned ld_acquire_gpu(const unsigned* p) {
 }
 
 // Grid-wide barrier of the consumer warps of all CTAs, split into arrival and
-// wait so that local work can run in between: the n-th barrier of a launch (n
-// from 1) completes when the counter reaches n * gridDim.x.  grid_arrive follows
-// a consumer barrier, so the CTA's writes before it are released with the
-// arrival (cumulativity), and they are visible to every CTA after grid_wait.
-// Bounded: gives up after ~kWaitLimitCycles, or as soon as any CTA has given up.
+// wait: the n-th barrier of a launch (n from 1) completes when the counter reaches
+// n * gridDim.x (+ 1 with `unreachable`, which only the timeout test asks for).
+// grid_arrive follows a consumer barrier, so the CTA's writes before it are
+// released with the arrival.  Bounded: gives up after `limit` cycles, or as soon
+// as any CTA has given up.
 DEVI void grid_arrive(unsigned* counter) {
   named_bar_sync(1, kConsumers);
   if (threadIdx.x == 0)
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
 }
 
-DEVN void grid_wait(unsigned* counter, unsigned n, volatile int* abort, int* err) {
+DEVN void grid_wait(unsigned* counter, unsigned n, bool unreachable, volatile int* abort, int* err,
+                    long long limit) {
   if (threadIdx.x == 0 && !*abort) {
-    const unsigned target = n * gridDim.x;
+    const unsigned target = n * gridDim.x + (unreachable ? 1u : 0u);
     const long long t0 = clock64();
     int k = 0;
     while ((int)(ld_acquire_gpu(counter) - target) < 0) {
@@ -138,7 +271,7 @@ DEVN void grid_wait(unsigned* counter, unsigned n, volatile int* abort, int* err
         *abort = 1;
         break;
       }
-      if (clock64() - t0 > kWaitLimitCycles) {
+      if (clock64() - t0 > limit) {
         give_up(abort, err, kSiteGrid);
         break;
       }
@@ -152,34 +285,23 @@ DEVI uint32_t fast_div_m(uint32_t d) { return 0xFFFFFFFFu / d + 1u; }
 DEVI uint32_t fast_div(uint32_t i, uint32_t m, uint32_t d) { return d == 1u ? i : __umulhi(i, m); }
 
 // Stage `nrows` rows of K 16-bit values (row r at src + r * row_stride elements,
-// read through L2; K % 64 == 0, nrows * K <= 32768) into shared memory in
-// fragment order for the offset path (fp16: odd columns / 16), optionally
-// RMS-normalised per row (rounded to T) and copied in natural order to
-// `plain_out`, and build the correction sums of every `cw` 32-column windows (a
-// pair, or a window for group 32): gsum [unit][K / (32 cw)][8 tokens] float2,
-// row r = unit * rows_per_unit + token.  `part` is 16 KB of scratch.  Runs on the
-// 512 consumer threads; starts and ends with a consumer-wide barrier.
-// mode kStageAll does everything; kStageNorm stops after the (normalised)
-// natural-order rows are in xsh (and plain_out); kStageFrag takes them from there
-// and does the rest (fragment order, correction sums).
-enum : int { kStageAll = 0, kStageNorm = 1, kStageFrag = 2 };
+// read through L2; K % 64 == 0) into shared memory in fragment order for the
+// offset path (fp16: odd columns / 16) and build the correction sums of every `cw`
+// 32-column windows: gsum [K / (32 cw)][8 tokens] float2.  `part` is scratch.  Runs
+// on the 512 consumer threads; starts and ends with a consumer-wide barrier.
+// mode kStageAll fetches from src; kStageFrag takes natural-order rows already in
+// xsh and converts them in place.
+enum : int { kStageAll = 0, kStageFrag = 2 };
 
 template <typename T>
-DEVN void stage_rows(const uint8_t* src, int row_stride, int nrows, int K, int rows_per_unit,
-                     uint8_t* xsh, uint32_t pitch, bool rms, float eps, uint8_t* plain_out,
-                     float2* gsum, int cw, float* part, int mode) {
-  const int tid = threadIdx.x, lane = tid & 31;
+DEVN void stage_rows(const uint8_t* src, int row_stride, int nrows, int K, uint8_t* xsh,
+                     uint32_t pitch, float2* gsum, int cw, int mode) {
+  const int tid = threadIdx.x;
   const int nq = K >> 3;  // 8-value chunks per row, a multiple of 8
   const int total = nrows * nq;
-  const uint32_t mq = fast_div_m((uint32_t)nq), mu = fast_div_m((uint32_t)rows_per_unit);
-  // sums of squares: one partial per 32 chunks when rows are whole warps, else
-  // per 8 chunks; each row's partials are added in a fixed order (identical run
-  // to run)
-  const int seg = (nq & 31) == 0 ? 32 : 8;
+  const uint32_t mq = fast_div_m((uint32_t)nq);
   named_bar_sync(1, kConsumers);
-  // pass 1: fetch into xsh in natural order; sums of squares
   for (int base = 0; mode != kStageFrag && base < total; base += 2 * kConsumers) {
-    // both loads of the pair are issued before either is used
     uint4 vv[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -192,32 +314,15 @@ DEVN void stage_rows(const uint8_t* src, int row_stride, int nrows, int K, int r
     }
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-    const int idx = base + h * kConsumers + tid;
-    const uint4 v = vv[h];
-    if (idx < total) {
-      const int r = (int)fast_div((uint32_t)idx, mq, (uint32_t)nq), q = idx - r * nq;
-      *reinterpret_cast<uint4*>(xsh + (uint32_t)r * pitch + (uint32_t)q * 16u) = v;
-    }
-    if (rms) {
-      float a = 0.f;
-      const T* e = reinterpret_cast<const T*>(&v);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) a = fmaf(to_f32<T>(e[k]), to_f32<T>(e[k]), a);
-      a += __shfl_xor_sync(0xffffffffu, a, 1);
-      a += __shfl_xor_sync(0xffffffffu, a, 2);
-      a += __shfl_xor_sync(0xffffffffu, a, 4);
-      if (seg == 32) {
-        a += __shfl_xor_sync(0xffffffffu, a, 8);
-        a += __shfl_xor_sync(0xffffffffu, a, 16);
+      const int idx = base + h * kConsumers + tid;
+      if (idx < total) {
+        const int r = (int)fast_div((uint32_t)idx, mq, (uint32_t)nq), q = idx - r * nq;
+        *reinterpret_cast<uint4*>(xsh + (uint32_t)r * pitch + (uint32_t)q * 16u) = vv[h];
       }
-      if ((lane & (seg - 1)) == 0 && idx < total) part[idx / seg] = a;
-    }
     }
   }
   if (mode != kStageFrag) named_bar_sync(1, kConsumers);
-  // pass 2: normalise, natural-order copy, fragment order (+ /16), correction sums
   const int cq = 4 * cw;  // chunks per correction unit
-  const int Nc = nq / cq;
   for (int base = 0; base < total; base += kConsumers) {
     const int idx = base + tid;
     float se = 0.f, so = 0.f;
@@ -226,36 +331,20 @@ DEVN void stage_rows(const uint8_t* src, int row_stride, int nrows, int K, int r
       r = (int)fast_div((uint32_t)idx, mq, (uint32_t)nq);
       q = idx - r * nq;
       uint8_t* cp = xsh + (uint32_t)r * pitch + (uint32_t)q * 16u;
-      uint4 o = *reinterpret_cast<const uint4*>(cp);
-      if (rms && mode != kStageFrag) {
-        const int per = nq / seg;
-        const float* pr = part + r * per;
-        float a = 0.f;
-        for (int c = 0; c < per; ++c) a += pr[c];
-        const float sc = 1.0f / sqrtf(a / (float)K + eps);
-        T* e = reinterpret_cast<T*>(&o);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) e[k] = from_f32<T>(to_f32<T>(e[k]) * sc);
+      uint4 o = to_frag_order(*reinterpret_cast<const uint4*>(cp));
+      if (DqOff<T>::kOddDiv16) {
+        const __half2 q16 = __float2half2_rn(0.0625f);
+        __half2 hy = __hmul2(*reinterpret_cast<__half2*>(&o.y), q16);
+        __half2 hw = __hmul2(*reinterpret_cast<__half2*>(&o.w), q16);
+        o.y = *reinterpret_cast<uint32_t*>(&hy);
+        o.w = *reinterpret_cast<uint32_t*>(&hw);
       }
-      if (plain_out && mode != kStageFrag)
-        *reinterpret_cast<uint4*>(plain_out + ((size_t)r * K + q * 8) * 2) = o;
-      if (mode != kStageNorm) {
-        o = to_frag_order(o);
-        if (DqOff<T>::kOddDiv16) {
-          const __half2 q16 = __float2half2_rn(0.0625f);
-          __half2 hy = __hmul2(*reinterpret_cast<__half2*>(&o.y), q16);
-          __half2 hw = __hmul2(*reinterpret_cast<__half2*>(&o.w), q16);
-          o.y = *reinterpret_cast<uint32_t*>(&hy);
-          o.w = *reinterpret_cast<uint32_t*>(&hw);
-        }
-        // fragment order: e0 = x0, e1 = x4, e2 = x1, e3 = x5, e4 = x2, e5 = x6, e6 = x3, e7 = x7
-        const T* e = reinterpret_cast<const T*>(&o);
-        se = (to_f32<T>(e[0]) + to_f32<T>(e[1])) + (to_f32<T>(e[4]) + to_f32<T>(e[5]));
-        so = (to_f32<T>(e[2]) + to_f32<T>(e[3])) + (to_f32<T>(e[6]) + to_f32<T>(e[7]));
-      }
+      // fragment order: e0 = x0, e1 = x4, e2 = x1, e3 = x5, e4 = x2, e5 = x6, e6 = x3, e7 = x7
+      const T* e = reinterpret_cast<const T*>(&o);
+      se = (to_f32<T>(e[0]) + to_f32<T>(e[1])) + (to_f32<T>(e[4]) + to_f32<T>(e[5]));
+      so = (to_f32<T>(e[2]) + to_f32<T>(e[3])) + (to_f32<T>(e[6]) + to_f32<T>(e[7]));
       *reinterpret_cast<uint4*>(cp) = o;
     }
-    if (mode == kStageNorm) continue;  // uniform: the same for every thread
     // a correction unit is cq consecutive chunks of one row (aligned lanes)
     se += __shfl_xor_sync(0xffffffffu, se, 1);
     so += __shfl_xor_sync(0xffffffffu, so, 1);
@@ -266,8 +355,6 @@ DEVN void stage_rows(const uint8_t* src, int row_stride, int nrows, int K, int r
       so += __shfl_xor_sync(0xffffffffu, so, 4);
     }
     if (idx < total && (q & (cq - 1)) == 0) {
-      const int u = (int)fast_div((uint32_t)r, mu, (uint32_t)rows_per_unit);
-      const int n = r - u * rows_per_unit;
       float P, Q;
       if (DqOff<T>::kOddDiv16) {
         P = 1024.f * (se + so);
@@ -276,7 +363,7 @@ DEVN void stage_rows(const uint8_t* src, int row_stride, int nrows, int K, int r
         Q = se + so;
         P = 128.f * Q;
       }
-      gsum[((size_t)u * Nc + q / cq) * 8 + n] = make_float2(P, Q);
+      gsum[(size_t)(q / cq) * 8 + r] = make_float2(P, Q);
     }
   }
   named_bar_sync(1, kConsumers);
@@ -293,7 +380,7 @@ DEVI int red_at(int n, int r) { return n * 16 + r + (n >> 1) * 8; }
 static_assert(7 * 16 + 15 + 3 * 8 < kRedStride, "reduction block");
 static_assert(kSRedBytes >= 4 * (kMaxTokens * kMaxExperts + kMaxTokens * kMaxExperts / 4 +
                                    kMaxExperts),
-              "scratch users of red: RMS partials, plan keys, candidates, unit_of");
+              "scratch users of red: plan keys, candidates, unit_of");
 
 template <int NREC>
 DEVI float2 reduce_rows(float* red, const float (&acc)[NREC][4], int nT, int tid, int warp,
@@ -324,16 +411,12 @@ DEVI float2 reduce_rows(float* red, const float (&acc)[NREC][4], int nT, int tid
   return make_float2(v, v2);
 }
 
-// Accumulators of one lane for up to two records (rows g, g + 8 x tokens 2t, 2t + 1).
-struct Acc2 {
-  float v[2][4];
-};
-
 // One ring stage of NREC records sharing the staged rows: the warp's pair range,
-// then the slot is released.  Returns this lane's accumulators.
+// then the slot is released and the warp's partial sums go to `red` as deferred
+// tile jj ([jj][record][warp][token][row], tokens < nT only).
 template <typename T, typename S, int NREC, bool G32>
-DEVN Acc2 tile_acc(const uint8_t* st, const TileGeom tg, const uint8_t* xsh, uint32_t pitch,
-                   const float2* gsum, int nT, uint64_t* empty_bar) {
+DEVI void tile_acc(const uint8_t* st, const TileGeom tg, const uint8_t* xsh, uint32_t pitch,
+                   const float2* gsum, int nT, uint64_t* empty_bar, float* red, int jj) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int np = tg.npairs;
   float acc[NREC][4];
@@ -349,237 +432,274 @@ DEVN Acc2 tile_acc(const uint8_t* st, const TileGeom tg, const uint8_t* xsh, uin
                                pitch, gsum, xon, acc);
   __syncwarp();
   if (lane == 0) mbar_arrive(empty_bar);
-  Acc2 out;
-#pragma unroll
-  for (int r = 0; r < 2; ++r)
-#pragma unroll
-    for (int k = 0; k < 4; ++k) out.v[r][k] = r < NREC ? acc[r][k] : 0.f;
-  return out;
-}
-
-// Deferred cross-warp reduction: the warps' partial sums of up to `rmax` tiles
-// wait in `red` ([tile][record][warp][token][row]); one barrier and one pass then
-// reduce them all.  Only tokens < nT are kept.
-template <int NREC>
-DEVI void put_partials(float* red, int jj, const Acc2& a, int nT, int warp, int lane) {
+  // the warp's partial sums, deferred: red [jj][record][warp][token][row]
   const int g = lane >> 2, t = lane & 3;
 #pragma unroll
   for (int r = 0; r < NREC; ++r) {
     float* b = red + ((jj * NREC + r) * kCW + warp) * (nT * 16);
     if (2 * t < nT) {
-      b[(2 * t) * 16 + g] = a.v[r][0];
-      b[(2 * t) * 16 + g + 8] = a.v[r][2];
+      b[(2 * t) * 16 + g] = acc[r][0];
+      b[(2 * t) * 16 + g + 8] = acc[r][2];
     }
     if (2 * t + 1 < nT) {
-      b[(2 * t + 1) * 16 + g] = a.v[r][1];
-      b[(2 * t + 1) * 16 + g + 8] = a.v[r][3];
+      b[(2 * t + 1) * 16 + g] = acc[r][1];
+      b[(2 * t + 1) * 16 + g + 8] = acc[r][3];
     }
   }
 }
 
-// Sums of output o = jj * nT * 16 + token * 16 + row (records 0 and 1).
-template <int NREC>
-DEVI float2 sum_partials(const float* red, int o, int nT) {
+
+// Sum of output o = jj * nT * 16 + token * 16 + row.
+DEVI float sum_partials(const float* red, int o, int nT) {
   const int per = nT * 16;
   const int jj = o / per, rem = o - jj * per;
-  float v = 0.f, v2 = 0.f;
+  float v = 0.f;
 #pragma unroll
-  for (int w = 0; w < kCW; ++w) {
-    v += red[((jj * NREC) * kCW + w) * per + rem];
-    if (NREC == 2) v2 += red[((jj * NREC + 1) * kCW + w) * per + rem];
-  }
-  return make_float2(v, v2);
+  for (int w = 0; w < kCW; ++w) v += red[(jj * kCW + w) * per + rem];
+  return v;
 }
 
 // Tiles whose partials fit in `red` at once.
-DEVI int defer_tiles(int nrec, int nT) {
-  int r = (int)(kSRedBytes / 4) / (nrec * kCW * nT * 16);
+DEVI int defer_tiles(int nT) {
+  int r = (int)(kSRedBytes / 4) / (kCW * nT * 16);
   const int by_threads = kConsumers / (nT * 16);
   return r < by_threads ? r : by_threads;
 }
 
-// One down-projection stage: `cnt` unit records, each with its own staged rows;
-// returns this lane's partial sums (rows g, g + 8 x tokens 2t, 2t + 1).
-template <typename T, typename S, bool G32>
-DEVN float4 stage_rm(const uint8_t* st, const TileGeom tg, int cnt, const uint8_t* xd,
-                     uint32_t xpitch, int nT, const float2* gsum, int ncu, const float* colw,
-                     uint64_t* empty_bar) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int items = cnt * tg.npairs;
-  float acc[4];
-  zero4(acc);
-  const bool xon = (lane >> 2) < nT;
-  if (!G32 && tg.gshift == 1 && (tg.npairs & 1) == 0)
-    rm_grouped<T, S, 2>(st, tg, cnt, warp, lane, xd, xpitch, nT, gsum, ncu, colw, xon, acc);
-  else
-    rm_offset<T, S, G32>(st, tg, (warp * items) / kCW, ((warp + 1) * items) / kCW, lane, xd, xpitch,
-                         nT, gsum, ncu, colw, xon, acc);
-  __syncwarp();
-  if (lane == 0) mbar_arrive(empty_bar);
-  return make_float4(acc[0], acc[1], acc[2], acc[3]);
-}
-
-DEVN float reduce4(float* red, const float4 a, int nT) {
-  const int tid = threadIdx.x;
-  const float acc[1][4] = {{a.x, a.y, a.z, a.w}};
-  return reduce_rows<1>(red, acc, nT, tid, tid >> 5, tid & 31).x;
-}
-
-// Router logits of expert e for nT tokens: the gate row (H values, natural order)
-// in `wrow`, the normalised tokens in natural order at xrows + n * xpitch.  Thread
-// n < nT returns logit n.
-template <typename T>
-DEVN float router_row(const uint8_t* wrow, const uint8_t* xrows, uint32_t xpitch, int H, int nT,
-                      const void* gate_b, int e, float* red, uint64_t* empty_bar) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint4* wr = reinterpret_cast<const uint4*>(wrow);
-  const int nq = H >> 3;
-  float part[kMaxTokens];
+// ------------------------------------------------------------------ h exchange
+// The layer input, this CTA's rows [row0, row0 + rrows): h = sum over the C clusters'
+// partial outputs `P` ([C][nT][H] fp32) (+ res, the rows of the previous layer's MoE
+// input in `hpl`), rounded once to T.  Eight lanes share a (token, 4 rows) group:
+// lane j loads clusters j, j + 8, j + 16, j + 24 (all loads in flight at once), and the
+// eight partial sums are combined by an xor butterfly, which gives every lane the same
+// bits (a fixed order).  With `out` null the rows go into `hpl` of every CTA of the
+// cluster (lane j writes CTA j), with this CTA's sums of squares of the rounded rows
+// (per token, fixed order) into the cluster's `ssq[rank]`; with `out` they are the
+// launch's result.
+static_assert(kMaxClusters <= 32 && kCS == 8, "reduce: 8 lanes x 4 clusters per group");
+template <typename T, int KT>  // KT: tokens at most (1 in the one-token kernel)
+DEVN void reduce_rows_h(const float* P, int C, int nT, int H, int row0, int rrows, bool residual,
+                        T* hpl, float* ssq, int rank, T* out, float* scratch) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, j = lane & 7;
+  const int q4 = rrows >> 2;  // 4-row groups per token
+  const int total = nT * q4;
+  float ss[KT];
 #pragma unroll
-  for (int n = 0; n < kMaxTokens; ++n) part[n] = 0.f;
-  for (int q = tid; q < nq; q += kConsumers) {
-    const uint4 wv = wr[q];
-    const T* we = reinterpret_cast<const T*>(&wv);
+  for (int n = 0; n < KT; ++n) ss[n] = 0.f;
+  // the trip count is the same for the whole warp (the shuffles need every lane)
+  for (int wb = warp * 4; wb < total; wb += kCW * 4) {
+    const int g = wb + (lane >> 3);
+    const bool on = g < total;
+    const int n = on ? g / q4 : 0, q = on ? g - n * q4 : 0;
+    const int row = row0 + 4 * q;
+    float4 v[4];
 #pragma unroll
-    for (int n = 0; n < kMaxTokens; ++n) {
-      if (n < nT) {
-        const uint4 xv = *reinterpret_cast<const uint4*>(xrows + (size_t)n * xpitch + (size_t)q * 16);
-        const T* xe = reinterpret_cast<const T*>(&xv);
+    for (int k = 0; k < 4; ++k) {
+      const int c = j + 8 * k;
+      v[k] = on && c < C
+                 ? __ldcg(reinterpret_cast<const float4*>(P + ((size_t)c * nT + n) * H + row))
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float4 s = v[0];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) part[n] = fmaf(to_f32<T>(we[k]), to_f32<T>(xe[k]), part[n]);
+    for (int k = 1; k < 4; ++k) {
+      s.x += v[k].x;
+      s.y += v[k].y;
+      s.z += v[k].z;
+      s.w += v[k].w;
+    }
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+      s.x += __shfl_xor_sync(0xffffffffu, s.x, o);
+      s.y += __shfl_xor_sync(0xffffffffu, s.y, o);
+      s.z += __shfl_xor_sync(0xffffffffu, s.z, o);
+      s.w += __shfl_xor_sync(0xffffffffu, s.w, o);
+    }
+    if (!on) continue;  // after the shuffles: uniform from here on per 8-lane set
+    if (residual) {
+      const uint2 rv = *reinterpret_cast<const uint2*>(hpl + (size_t)n * H + row);
+      const T* re = reinterpret_cast<const T*>(&rv);
+      s.x += to_f32<T>(re[0]);
+      s.y += to_f32<T>(re[1]);
+      s.z += to_f32<T>(re[2]);
+      s.w += to_f32<T>(re[3]);
+    }
+    union {
+      uint2 u;
+      T h[4];
+    } pk;
+    pk.h[0] = from_f32<T>(s.x);
+    pk.h[1] = from_f32<T>(s.y);
+    pk.h[2] = from_f32<T>(s.z);
+    pk.h[3] = from_f32<T>(s.w);
+    if (out) {
+      if (j == 0) *reinterpret_cast<uint2*>(out + (size_t)n * H + row) = pk.u;
+    } else {
+      if (j == 0) {
+        const float a = to_f32<T>(pk.h[0]), b = to_f32<T>(pk.h[1]);
+        const float c = to_f32<T>(pk.h[2]), d = to_f32<T>(pk.h[3]);
+        const float sq = fmaf(a, a, fmaf(b, b, fmaf(c, c, d * d)));
+#pragma unroll
+        for (int m = 0; m < KT; ++m)
+          if (m == n) ss[m] += sq;
       }
+      // every lane has the row values: lane j writes them into CTA j of the cluster
+      st_peer_v2(peer_addr(hpl + (size_t)n * H + row, (uint32_t)j), pk.u);
     }
   }
-  __syncwarp();
-  if (lane == 0) mbar_arrive(empty_bar);
+  if (out) return;
+  // per-token sums of squares: warp shuffles, then the warps in order
 #pragma unroll
-  for (int n = 0; n < kMaxTokens; ++n) {
-    if (n < nT) {
-      float a = part[n];
+  for (int n = 0; n < KT; ++n) {
+    float a = ss[n];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-      if (lane == 0) red[warp * 8 + n] = a;
-    }
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    if (lane == 0) scratch[warp * kMaxTokens + n] = a;
   }
   named_bar_sync(1, kConsumers);
-  float a = 0.f;
   if (tid < nT) {
+    float a = 0.f;
 #pragma unroll
-    for (int w = 0; w < kCW; ++w) a += red[w * 8 + tid];
-    if (gate_b) a += to_f32<T>(reinterpret_cast<const T*>(gate_b)[e]);
-    a = to_f32<T>(from_f32<T>(a));
+    for (int w = 0; w < kCW; ++w) a += scratch[w * kMaxTokens + tid];
+#pragma unroll
+    for (int p = 0; p < kCS; ++p) st_peer_f32(peer_addr(ssq + rank * kMaxTokens + tid, (uint32_t)p), a);
   }
-  named_bar_sync(1, kConsumers);
-  return a;
 }
 
-// Router logits with the RMS staging fused in: fetch the nT rows of h (H values,
-// through L2), RMS-normalise them in registers (rounded to T), leave them in
-// natural order in xsh for the fragment staging that follows, and dot them with
-// this CTA's gate row `wrow` (natural order in the ring slot; null when the CTA has
-// no router row).  Threads tid < nT return the rounded logit of row tid.  Every
-// sum runs in a fixed order.  nT * H <= kMaxChunks * 8 * 512.
+// RMS scale per token from the full rows in hpl ([nT][H], natural order), fixed
+// order: warp n sums row n.
 template <typename T>
-DEVN float router_fused(const uint8_t* src, int H, int nT, bool rms, float eps, uint8_t* xsh,
-                        uint32_t pitch, const uint8_t* wrow, const void* gate_b, int e, float* red,
-                        uint64_t* empty_bar) {
-  const int tid = threadIdx.x, lane = tid & 31;
-  const int nq = H >> 3, total = nT * nq;
-  const uint32_t mq = fast_div_m((uint32_t)nq);
-  const int seg = (nq & 31) == 0 ? 32 : 8;
-  const int per = nq / seg;  // segments per row
-  float* part = red;         // sums of squares, one per segment
-  float* dotp = red + 1024;  // dot products, one per segment
-  named_bar_sync(1, kConsumers);
-  uint4 v[kMaxChunks];
+DEVN void local_inv_rms(const T* hpl, int nT, int H, float eps, float* inv) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (warp < nT) {
+    float a = 0.f;
+    for (int q = lane; q < (H >> 3); q += 32) {
+      const uint4 v = *reinterpret_cast<const uint4*>(hpl + (size_t)warp * H + q * 8);
+      const T* e = reinterpret_cast<const T*>(&v);
 #pragma unroll
-  for (int j = 0; j < kMaxChunks; ++j) {
-    const int idx = tid + j * kConsumers;
-    v[j] = make_uint4(0, 0, 0, 0);
-    if (idx < total) {
-      const int r = (int)fast_div((uint32_t)idx, mq, (uint32_t)nq), q = idx - r * nq;
-      v[j] = __ldcg(reinterpret_cast<const uint4*>(src + ((size_t)r * H + q * 8) * 2));
+      for (int k = 0; k < 8; ++k) a = fmaf(to_f32<T>(e[k]), to_f32<T>(e[k]), a);
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    if (lane == 0) inv[warp] = 1.0f / sqrtf(a / (float)H + eps);
   }
-  if (rms) {
+  named_bar_sync(1, kConsumers);
+}
+
+// Rows of hpl ([nT][H]) into xsh in natural order, RMS-normalised with `inv` (one
+// rounding to T) when rms.
+template <typename T>
+DEVN void normalise_rows(const T* hpl, int nT, int H, const float* inv, bool rms, uint8_t* xsh,
+                         uint32_t pitch) {
+  const int nq = H >> 3;
+  for (int idx = threadIdx.x; idx < nT * nq; idx += kConsumers) {
+    const int n = idx / nq, q = idx - n * nq;
+    uint4 v = *reinterpret_cast<const uint4*>(hpl + (size_t)n * H + q * 8);
+    if (rms) {
+      const float sc = inv[n];
+      T* e = reinterpret_cast<T*>(&v);
 #pragma unroll
-    for (int j = 0; j < kMaxChunks; ++j) {
-      if (j * kConsumers >= total) break;  // uniform
-      const int idx = tid + j * kConsumers;
-      float a = 0.f;
-      const T* x = reinterpret_cast<const T*>(&v[j]);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) a = fmaf(to_f32<T>(x[k]), to_f32<T>(x[k]), a);
-      a += __shfl_xor_sync(0xffffffffu, a, 1);
-      a += __shfl_xor_sync(0xffffffffu, a, 2);
-      a += __shfl_xor_sync(0xffffffffu, a, 4);
-      if (seg == 32) {
-        a += __shfl_xor_sync(0xffffffffu, a, 8);
-        a += __shfl_xor_sync(0xffffffffu, a, 16);
+      for (int k = 0; k < 8; ++k) e[k] = from_f32<T>(to_f32<T>(e[k]) * sc);
+    }
+    *reinterpret_cast<uint4*>(xsh + (uint32_t)n * pitch + (uint32_t)q * 16u) = v;
+  }
+  named_bar_sync(1, kConsumers);
+}
+
+// Rows of a global [nT][H] buffer (written by other CTAs: read through L2) into hpl.
+template <typename T>
+DEVN void load_rows(const T* src, int nT, int H, T* hpl) {
+  const int total = nT * (H >> 3);
+  for (int idx = threadIdx.x; idx < total; idx += kConsumers)
+    *reinterpret_cast<uint4*>(hpl + (size_t)idx * 8) =
+        __ldcg(reinterpret_cast<const uint4*>(src + (size_t)idx * 8));
+  named_bar_sync(1, kConsumers);
+}
+
+// ------------------------------------------------------------------ router
+// Gate records (duplex_repack_gate_records): the gate matrix [E][H] in blocks of 16
+// experts, per 16-column k-step the mma.sync A fragments of the 32 lanes (lane (g, t):
+// rows g, g + 8 x columns 2t, 2t + 1, 2t + 8, 2t + 9), 512 bytes per (block, k-step).
+// CTA `rank` of a cluster takes blocks rank, rank + 8, ...; a block's k-steps arrive in
+// ring stages of `kps` k-steps.  Warp w takes k-steps [w KS / 16, (w + 1) KS / 16) of
+// every block (B = the normalised tokens, natural order in xsh), the partial sums
+// are added in warp order, and each logit, rounded to T (+ bias), goes to every CTA
+// of the cluster: ls[n][e].  Every warp then releases every gate stage.
+template <typename T>
+DEVI void router_mma(const uint8_t* ring, uint32_t slot_bytes, int NS, RingPos pos, int rank,
+                     int nblk, int KS, int kps, int E, int nT, const uint8_t* xsh, uint32_t pitch,
+                     const void* gate_b, float* ls, float* red, uint64_t* full, uint64_t* empty,
+                     volatile int* abort, int* err, long long limit) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const bool xon = g < nT;
+  const int ks0 = (warp * KS) / kCW, ks1 = ((warp + 1) * KS) / kCW;
+  const uint8_t* xrow = xsh + (uint32_t)g * pitch + (uint32_t)t * 4u;
+  RingPos rp = pos;
+  int nst = 0;
+  for (int b = rank; b < nblk; b += kCS) {
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k0 = 0; k0 < KS; k0 += kps, rp.next(NS), ++nst) {
+      const int lo = ks0 > k0 ? ks0 : k0;
+      const int hi = ks1 < k0 + kps ? ks1 : k0 + kps;
+      if (lo >= hi) continue;
+      wait_phase(&full[rp.slot], rp.phase, abort, err, kSiteFull, limit);
+      const uint8_t* ap = ring + (uint32_t)rp.slot * slot_bytes + (uint32_t)(lo - k0) * 512u +
+                          (uint32_t)lane * 16u;
+      const uint8_t* xp = xrow + (uint32_t)lo * 32u;
+      for (int ks = lo; ks < hi; ++ks, ap += 512, xp += 32) {
+        const uint4 a = *reinterpret_cast<const uint4*>(ap);
+        uint32_t b0 = 0u, b1 = 0u;
+        if (xon) {
+          b0 = *reinterpret_cast<const uint32_t*>(xp);
+          b1 = *reinterpret_cast<const uint32_t*>(xp + 16);
+        }
+        MmaOp<T>::run(d, a.x, a.y, a.z, a.w, b0, b1);
       }
-      if ((lane & (seg - 1)) == 0 && idx < total) part[idx / seg] = a;
+    }
+    // partials [warp][token][row]; tokens 2t, 2t + 1 of rows g, g + 8
+    float* rb = red + warp * 128;
+    if (2 * t < nT) {
+      rb[(2 * t) * 16 + g] = d[0];
+      rb[(2 * t) * 16 + g + 8] = d[2];
+    }
+    if (2 * t + 1 < nT) {
+      rb[(2 * t + 1) * 16 + g] = d[1];
+      rb[(2 * t + 1) * 16 + g + 8] = d[3];
+    }
+    named_bar_sync(1, kConsumers);
+    if (tid < nT * 16) {
+      float a = 0.f;
+#pragma unroll
+      for (int w = 0; w < kCW; ++w) a += red[w * 128 + tid];
+      const int n = tid >> 4, e = b * 16 + (tid & 15);
+      if (e < E) {
+        if (gate_b) a += to_f32<T>(reinterpret_cast<const T*>(gate_b)[e]);
+        a = to_f32<T>(from_f32<T>(a));
+#pragma unroll
+        for (int q = 0; q < kCS; ++q) st_peer_f32(peer_addr(ls + n * E + e, (uint32_t)q), a);
+      }
     }
     named_bar_sync(1, kConsumers);
   }
-#pragma unroll
-  for (int j = 0; j < kMaxChunks; ++j) {
-    if (j * kConsumers >= total) break;  // uniform
-    const int idx = tid + j * kConsumers;
-    float d = 0.f;
-    if (idx < total) {
-      const int r = (int)fast_div((uint32_t)idx, mq, (uint32_t)nq), q = idx - r * nq;
-      uint4 o = v[j];
-      if (rms) {
-        float a = 0.f;
-        for (int c = 0; c < per; ++c) a += part[r * per + c];
-        const float sc = 1.0f / sqrtf(a / (float)H + eps);
-        T* x = reinterpret_cast<T*>(&o);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) x[k] = from_f32<T>(to_f32<T>(x[k]) * sc);
-      }
-      *reinterpret_cast<uint4*>(xsh + (uint32_t)r * pitch + (uint32_t)q * 16u) = o;
-      if (wrow) {
-        const uint4 wv = *reinterpret_cast<const uint4*>(wrow + (size_t)q * 16);
-        const T* w = reinterpret_cast<const T*>(&wv);
-        const T* x = reinterpret_cast<const T*>(&o);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) d = fmaf(to_f32<T>(w[k]), to_f32<T>(x[k]), d);
-      }
-    }
-    if (wrow) {
-      d += __shfl_xor_sync(0xffffffffu, d, 1);
-      d += __shfl_xor_sync(0xffffffffu, d, 2);
-      d += __shfl_xor_sync(0xffffffffu, d, 4);
-      if (seg == 32) {
-        d += __shfl_xor_sync(0xffffffffu, d, 8);
-        d += __shfl_xor_sync(0xffffffffu, d, 16);
-      }
-      if ((lane & (seg - 1)) == 0 && idx < total) dotp[idx / seg] = d;
-    }
+  __syncwarp();
+  if (lane == 0) {
+    RingPos r = pos;
+    for (int j = 0; j < nst; ++j, r.next(NS)) mbar_arrive(&empty[r.slot]);
   }
-  if (wrow) {
-    __syncwarp();
-    if (lane == 0) mbar_arrive(empty_bar);
-  }
-  named_bar_sync(1, kConsumers);
-  float a = 0.f;
-  if (wrow && tid < nT) {
-    for (int c = 0; c < per; ++c) a += dotp[tid * per + c];
-    if (gate_b) a += to_f32<T>(reinterpret_cast<const T*>(gate_b)[e]);
-    a = to_f32<T>(from_f32<T>(a));
-  }
-  return a;
 }
 
+// ------------------------------------------------------------------ routing plan
 // plan_units for one token: warp 0 alone (lane holds experts lane + 32 i), the same
 // keys and max-reductions as the general path, so the same selection; the units are
 // the k selected experts in ascending id order (position = number of selected ids
-// below).  A function of its own: inside plan_units the general path's code made this
-// path ~2.5x slower (3,100 vs 1,250 cycles measured).
-template <typename T>
-DEVN int plan_one(const float* logits, int E, int top_k, uint8_t* smem, float* scratch) {
+// below).  With norm it also writes the renormalised routing weights.  A function of
+// its own: inside plan_units the general path's code made this path ~2.5x slower
+// (3,100 vs 1,250 cycles measured).
+template <typename T, int KPL>  // KPL: keys per lane, E <= 32 KPL
+DEVN int plan_one(int E, int top_k, int norm, uint8_t* smem, float* scratch) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float* ls = reinterpret_cast<float*>(smem + kSLogit);
+  const float* ls = reinterpret_cast<const float*>(smem + kSLogit);
   int* sel_s = reinterpret_cast<int*>(smem + kSSel);
   int* unit_e = reinterpret_cast<int*>(smem + kSUnitE);
   uint32_t* unit_m = reinterpret_cast<uint32_t*>(smem + kSUnitM);
@@ -589,13 +709,11 @@ DEVN int plan_one(const float* logits, int E, int top_k, uint8_t* smem, float* s
       reinterpret_cast<int*>(scratch) + kMaxTokens * kMaxExperts + kMaxTokens * (kMaxExperts / 4);
   (void)tid;
   if (warp == 0) {
-    uint32_t key[kMaxExperts / 32];
+    uint32_t key[KPL];
 #pragma unroll
-    for (int i = 0; i < kMaxExperts / 32; ++i) {
+    for (int i = 0; i < KPL; ++i) {
       const int e = lane + 32 * i;
-      const float v = e < E ? __ldcg(logits + e) : 0.f;
-      key[i] = e < E ? order_key<T>(v, e) : 0u;
-      if (e < E) ls[e] = v;
+      key[i] = e < E ? order_key<T>(ls[e], e) : 0u;
     }
     int sel[kMaxTopK];
     int mine = 0;  // lane j's pick
@@ -605,10 +723,10 @@ DEVN int plan_one(const float* logits, int E, int top_k, uint8_t* smem, float* s
       if (j < top_k) {
         uint32_t lm = 0u;
 #pragma unroll
-        for (int i = 0; i < kMaxExperts / 32; ++i) lm = key[i] > lm ? key[i] : lm;
+        for (int i = 0; i < KPL; ++i) lm = key[i] > lm ? key[i] : lm;
         const uint32_t m = __reduce_max_sync(0xffffffffu, lm);
 #pragma unroll
-        for (int i = 0; i < kMaxExperts / 32; ++i)
+        for (int i = 0; i < KPL; ++i)
           if (key[i] == m) key[i] = 0u;
         const int e = key_expert(m);
         sel[j] = (m == 0u || e >= E) ? 0 : e;
@@ -619,6 +737,16 @@ DEVN int plan_one(const float* logits, int E, int top_k, uint8_t* smem, float* s
 #pragma unroll
     for (int j = 0; j < kMaxTopK; ++j)
       if (j < top_k && sel[j] < mine) ++rank;
+    // renormalised top-k weights: the softmax denominator over all experts cancels,
+    // so p_j / sum_i p_i = exp(l_j - l_max) / sum over the selection (in order)
+    const float lmax = ls[sel[0]];
+    const float ej = lane < top_k ? expf(ls[mine] - lmax) : 0.f;
+    float esum = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j) {
+      const float x = __shfl_sync(0xffffffffu, ej, j);
+      if (j < top_k) esum += x;
+    }
     if (lane < top_k) {
       sel_s[lane] = mine;
       unit_of[mine] = rank;
@@ -626,6 +754,7 @@ DEVN int plan_one(const float* logits, int E, int top_k, uint8_t* smem, float* s
       unit_m[rank] = 1u;
 #pragma unroll
       for (int n = 0; n < kMaxTokens; ++n) unit_w[rank * kMaxTokens + n] = 0.f;
+      if (norm) unit_w[rank * kMaxTokens] = ej / esum;
     }
     if (lane == 0) *n_units_s = top_k;
   }
@@ -641,9 +770,9 @@ DEVN int plan_one(const float* logits, int E, int top_k, uint8_t* smem, float* s
 // clears its key), then one warp per token merges the blocks' candidates.
 // scratch: keys [T][E] | candidates [T][blocks * top_k] | unit_of [E].
 template <typename T>
-DEVN int plan_units(const float* logits, int nT, int E, int top_k, uint8_t* smem, float* scratch) {
+DEVN int plan_units(int nT, int E, int top_k, uint8_t* smem, float* scratch) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float* ls = reinterpret_cast<float*>(smem + kSLogit);
+  const float* ls = reinterpret_cast<const float*>(smem + kSLogit);
   int* sel_s = reinterpret_cast<int*>(smem + kSSel);
   int* unit_e = reinterpret_cast<int*>(smem + kSUnitE);
   uint32_t* unit_m = reinterpret_cast<uint32_t*>(smem + kSUnitM);
@@ -656,10 +785,8 @@ DEVN int plan_units(const float* logits, int nT, int E, int top_k, uint8_t* smem
   int* unit_of = reinterpret_cast<int*>(cand + kMaxTokens * (kMaxExperts / 4));
   const int TE = nT * E;
   for (int idx = tid; idx < TE; idx += kConsumers) {
-    const float v = __ldcg(logits + idx);
     const int tk = idx / E;
-    ls[idx] = v;
-    keys[idx] = order_key<T>(v, idx - tk * E);
+    keys[idx] = order_key<T>(ls[idx], idx - tk * E);
   }
   if (tid < kMaxTokens * 8) selbits[tid] = 0u;
   named_bar_sync(1, kConsumers);
@@ -756,16 +883,226 @@ DEVN void plan_weights(int nT, int E, int top_k, int norm, uint8_t* smem, const 
   named_bar_sync(1, kConsumers);
 }
 
-DEVI void prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+// ------------------------------------------------------------------ items
+// A CTA takes its items in batches of up to p.ib: the gate|up tile pairs of the
+// batch (partial sums of each warp deferred in `red`), one pass of sums, one
+// exchange of the batch's intermediate rows, then the down records, two items per
+// ring stage.
+
+
+// Gate (x) and up (y) sums of output o = jj * nT * 16 + token * 16 + row, warps in order.
+DEVI float2 sum_pair_partials(const float* red, int o, int nT) {
+  const int per = nT * 16;
+  const int jj = o / per, rem = o - jj * per;
+  float v = 0.f, v2 = 0.f;
+#pragma unroll
+  for (int w = 0; w < kCW; ++w) {
+    v += red[((jj * 2) * kCW + w) * per + rem];
+    v2 += red[((jj * 2 + 1) * kCW + w) * per + rem];
+  }
+  return make_float2(v, v2);
 }
 
+// After the batch's gate|up partials are in `red`: SiLU(gate) * up of this CTA's 16
+// rows for each (item, token) (0 for tokens outside the item's unit), rounded to T,
+// in fragment order (fp16: odd columns / 16) into rows [16 rank, 16 rank + 16) of xd
+// (row item * nT + token) of every CTA of the cluster, with the partial column sums
+// of those stored values (even, odd columns, as stage_rows sums them) into
+// dgp[item][rank][token] of every CTA; then one arrival on every CTA's `bar`.  Thread
+// o < nbt * nT * 16 holds row o & 15 of (item, token) o >> 4; an 8-lane group gathers
+// its 8 rows by shuffles and lane j of the group writes CTA j.
+template <typename T>
+DEVI void act_send(const float* red, int nbt, int nT, int b0, int S, const uint32_t* unit_m,
+                   int rank, uint8_t* xd, float2* dgp, uint64_t* bar) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int total = nbt * nT * 16;
+  if ((tid & ~31) < total) {  // whole warps: every lane takes part in the shuffles
+    const bool on = tid < total;
+    float x = 0.f;
+    int k = 0, n = 0;
+    if (on) {
+      const float2 v = sum_pair_partials(red, tid, nT);
+      k = tid / (nT * 16);
+      n = (tid >> 4) - k * nT;
+      const int u = (b0 + k) / S;
+      x = ((unit_m[u] >> n) & 1u) ? silu_f32(v.x) * v.y : 0.f;
+    }
+    x = to_f32<T>(from_f32<T>(x));
+    const int base = lane & ~7, j = lane & 7;
+    union {
+      uint4 u;
+      T h[8];
+    } pk;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) pk.h[q] = from_f32<T>(__shfl_sync(0xffffffffu, x, base + q));
+    uint4 o = to_frag_order(pk.u);
+    if (DqOff<T>::kOddDiv16) {
+      const __half2 q16 = __float2half2_rn(0.0625f);
+      __half2 hy = __hmul2(*reinterpret_cast<__half2*>(&o.y), q16);
+      __half2 hw = __hmul2(*reinterpret_cast<__half2*>(&o.w), q16);
+      o.y = *reinterpret_cast<uint32_t*>(&hy);
+      o.w = *reinterpret_cast<uint32_t*>(&hw);
+    }
+    const T* e = reinterpret_cast<const T*>(&o);
+    float se = (to_f32<T>(e[0]) + to_f32<T>(e[1])) + (to_f32<T>(e[4]) + to_f32<T>(e[5]));
+    float so = (to_f32<T>(e[2]) + to_f32<T>(e[3])) + (to_f32<T>(e[6]) + to_f32<T>(e[7]));
+    se += __shfl_xor_sync(0xffffffffu, se, 8);  // the other half of the 16 rows
+    so += __shfl_xor_sync(0xffffffffu, so, 8);
+    if (on) {
+      const int h = (tid >> 3) & 1, r = k * nT + n;
+      st_peer_v4(peer_addr(xd + (uint32_t)r * kXdPitch + (uint32_t)(rank * 16 + h * 8) * 2u,
+                           (uint32_t)j),
+                 o);
+      if (h == 0)
+        st_peer_v2(peer_addr(dgp + (k * kCS + rank) * 8 + n, (uint32_t)j),
+                   make_uint2(__float_as_uint(se), __float_as_uint(so)));
+    }
+  }
+  signal_cluster_xchg(bar);
+}
+
+// (P, Q) of the offset path from column sums (se: even columns, so: odd, as stored).
+template <typename T>
+DEVI float2 corr_pq(float se, float so) {
+  if (DqOff<T>::kOddDiv16) return make_float2(1024.f * (se + so), fmaf(16.f, so, se));
+  const float q = se + so;
+  return make_float2(128.f * q, q);
+}
+
+// Correction sums of the staged slices per window of 32 columns (`cw` = 1, group 32)
+// or pair of 64 (`cw` = 2) from the CTAs' partials, dg [item][window][8 tokens]
+// (the general path; the group-128 path adds the partials inside the down loop).
+template <typename T>
+DEVI void dg_from_partials(const float2* dgp, int nbt, int nT, int cw, float2* dg) {
+  const int tid = threadIdx.x;
+  const int nwin = kSliceK / (32 * cw), per = kCS / nwin;
+  if (tid < nbt * nT * nwin) {
+    const int wi = tid % nwin, r = tid / nwin;
+    const int k = r / nT, n = r - k * nT;
+    float se = 0.f, so = 0.f;
+    for (int q = wi * per; q < (wi + 1) * per; ++q) {
+      const float2 v = dgp[(k * kCS + q) * 8 + n];
+      se += v.x;
+      so += v.y;
+    }
+    dg[(k * nwin + wi) * 8 + n] = corr_pq<T>(se, so);
+  }
+  named_bar_sync(1, kConsumers);
+}
+
+// One K-slice record (16 output rows x 128 columns, group 128: one group of two
+// pairs) against the staged slice rows xd (token g of lane (g, t)): acc += w * dot.
+template <typename T, typename S>
+DEVI void ks_record_g128(const uint8_t* rec, const TileGeom& tg, int lane, const uint8_t* xd,
+                         const float2* dgp, float w0, float w1, bool xon, float (&acc)[4]) {
+  const int g = lane >> 2, t = lane & 3;
+  const uint8_t* xrow = xd + (uint32_t)g * kXdPitch + (uint32_t)t * 16u;
+  const uint8_t* wp = rec + (uint32_t)lane * 16u;
+  // the slice's column sums for tokens 2t, 2t + 1: the 8 CTAs' partials in rank order
+  float4 c = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int q = 0; q < kCS; ++q) {
+    const float4 v = *reinterpret_cast<const float4*>(dgp + q * 8 + 2 * t);
+    c.x += v.x;
+    c.y += v.y;
+    c.z += v.z;
+    c.w += v.w;
+  }
+  const float2 pq0 = corr_pq<T>(c.x, c.y), pq1 = corr_pq<T>(c.z, c.w);
+  const float4 gs = make_float4(pq0.x, pq0.y, pq1.x, pq1.y);
+  float d[4];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    uint4 xa = make_uint4(0, 0, 0, 0), xb = make_uint4(0, 0, 0, 0);
+    if (xon) {
+      xa = *reinterpret_cast<const uint4*>(xrow + k * 128);
+      xb = *reinterpret_cast<const uint4*>(xrow + k * 128 + 64);
+    }
+    const uint4 w = *reinterpret_cast<const uint4*>(wp + k * 512);
+    uint32_t A[4], B[4];
+    DqOff<T>::expand(w.x, w.y, A, B);
+    if (k == 0)
+      mma_first<T>(d, A[0], A[1], A[2], A[3], xa.x, xa.y);
+    else
+      MmaOp<T>::run(d, A[0], A[1], A[2], A[3], xa.x, xa.y);
+    MmaOp<T>::run(d, B[0], B[1], B[2], B[3], xa.z, xa.w);
+    DqOff<T>::expand(w.z, w.w, A, B);
+    MmaOp<T>::run(d, A[0], A[1], A[2], A[3], xb.x, xb.y);
+    MmaOp<T>::run(d, B[0], B[1], B[2], B[3], xb.z, xb.w);
+  }
+  const float zero4v[4] = {0.f, 0.f, 0.f, 0.f};
+  flush_group<S>(acc, d, zero4v, rec, tg, 0, g, gs, w0, w1);
+}
+
+// Down projection of `nit` (1 or 2) items of a DN stage (item j's records at st + j *
+// dn_bytes) for this warp's records (16 output rows each): K = the item's 128-column
+// slice in xd (rows j * nT + token), weights w[j] of its unit's tokens.
 template <typename T, typename S, bool G32>
+DEVI void slice_down(const uint8_t* st, const TileGeom tg, int nrec, uint32_t dn_bytes, int nit,
+                     const uint8_t* xd, const float2* dgp, const float2* dg, int nwin,
+                     const float* w0, const float* w1, int nT, float (&acc)[kMaxRecPerWarp][4],
+                     uint64_t* empty_bar) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool xon = (lane >> 2) < nT;
+  const int t = lane & 3;
+  for (int j = 0; j < nit; ++j) {
+    const float* w = j ? w1 : w0;
+#pragma unroll
+    for (int k = 0; k < kMaxRecPerWarp; ++k) {
+      const int rec = warp + k * kCW;
+      if (rec >= nrec) continue;
+      const uint8_t* r = st + j * dn_bytes + (uint32_t)rec * tg.rec_bytes;
+      const uint8_t* xj = xd + (uint32_t)(j * nT) * kXdPitch;
+      if (!G32 && tg.gshift == 1)
+        ks_record_g128<T, S>(r, tg, lane, xj, dgp + j * kCS * 8, w[2 * t], w[2 * t + 1], xon,
+                             acc[k]);
+      else
+        rm_offset<T, S, G32>(r, tg, 0, tg.npairs, lane, xj, kXdPitch, 0, dg + j * nwin * 8, 0, w,
+                             xon, acc[k]);
+    }
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(empty_bar);
+}
+
+// This CTA's rows of the cluster's partial output: part[c][n][row] (fp32).
+DEVI void write_partials(float* part, int nT, int H, int row0, int nrec,
+                         float (&acc)[kMaxRecPerWarp][4]) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int k = 0; k < kMaxRecPerWarp; ++k) {
+    const int rec = warp + k * kCW;
+    if (rec < nrec) {
+      const int row = row0 + rec * 16 + g;
+      if (2 * t < nT) {
+        part[(size_t)(2 * t) * H + row] = acc[k][0];
+        part[(size_t)(2 * t) * H + row + 8] = acc[k][2];
+      }
+      if (2 * t + 1 < nT) {
+        part[(size_t)(2 * t + 1) * H + row] = acc[k][1];
+        part[(size_t)(2 * t + 1) * H + row + 8] = acc[k][3];
+      }
+    }
+    zero4(acc[k]);
+  }
+}
+
+DEVI void item_range(int n_items, int C, int c, int& i0, int& i1) {
+  i0 = (int)((long long)n_items * c / C);
+  i1 = (int)((long long)n_items * (c + 1) / C);
+}
+
+// NT: 1 for the one-token kernel (the per-token loops fold away), 0 for T from p.T.
+template <typename T, typename S, bool G32, int NT>
 __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constant__ StackParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSFull);
   uint64_t* empty = reinterpret_cast<uint64_t*>(smem + kSEmpty);
   uint64_t* plan_ready = reinterpret_cast<uint64_t*>(smem + kSPlan);
+  uint64_t* hx_full = reinterpret_cast<uint64_t*>(smem + kSHx);
+  uint64_t* lg_full = reinterpret_cast<uint64_t*>(smem + kSLg);
+  uint64_t* act_full = reinterpret_cast<uint64_t*>(smem + kSAct);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSAbort);
   int* n_units_s = reinterpret_cast<int*>(smem + kSNUnits);
   int* unit_e = reinterpret_cast<int*>(smem + kSUnitE);
@@ -775,6 +1112,10 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int NS = p.nslots;
   const int cta = blockIdx.x, G = gridDim.x;
+  const int rank = (int)cluster_ctarank();
+  const int cid = (int)cluster_id_x();
+  const int C = (int)nclusters_x();
+  const long long limit = p.wait_limit;
 
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
@@ -782,329 +1123,406 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
       mbar_init(&empty[s], kCW);
     }
     mbar_init(plan_ready, 1);
-    *abort_flag = 0;
+    mbar_init(hx_full, kCS);
+    mbar_init(lg_full, kCS);
+    mbar_init(&act_full[0], kCS);
+    mbar_init(&act_full[1], kCS);
+    // an earlier launch that gave up leaves the bit set: give up at once
+    *abort_flag = (*reinterpret_cast<volatile int*>(p.err) & DUPLEX_DEVERR_TIMEOUT) ? 1 : 0;
     fence_mbar_init();
   }
-  __syncthreads();
+  // every CTA's barriers exist before any CTA of the cluster arrives on them
+  cluster_sync_all();
 
-  const int perG = p.I >> 4;  // gate|up tiles per unit
+  const int perG = p.I >> 4;             // gate|up tiles per unit
+  const int spb = (p.KS + p.kps - 1) / p.kps;                   // ring stages per gate block
+  const int ngs = (p.nblk > rank ? (p.nblk - rank + kCS - 1) / kCS : 0) * spb;  // per layer
+  const int nrec = p.rrows >> 4;             // down records of this CTA per item
+  const int row0 = rank * p.rrows;
 
   if (warp == kCW) {
     // ================================================================ producer
-    const uint64_t pol = policy_evict_first();
-    int i = 0;  // stage sequence number
-    auto acquire = [&](int j) {
-      if (j >= NS)
-        wait_phase(&empty[j % NS], (uint32_t)((j / NS) - 1) & 1u, abort_flag, p.err, kSiteEmpty);
-    };
-    auto slot_ptr = [&](int j) { return smem + p.off_ring + (uint32_t)(j % NS) * p.slot_bytes; };
-    // one-copy stage (weights); the second arrival of the full barrier follows at once
-    auto issue1 = [&](const uint8_t* src, uint32_t bytes) {
-      acquire(i);
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&full[i % NS], bytes);
-        bulk_g2s_stream(slot_ptr(i), src, bytes, &full[i % NS], pol);
-        mbar_arrive(&full[i % NS]);
-      }
-      __syncwarp();
-      ++i;
-    };
-
-    for (int l = 0; l < p.n_layers; ++l) {
-      const duplex_stack_layer L = p.layers[l];
-      if (p.has_attn) {
-        for (int t = cta; t < p.RbQ; t += G)
-          issue1(reinterpret_cast<const uint8_t*>(L.qkv_tiles) + (size_t)t * p.tq.rec_bytes,
-                 p.tq.rec_bytes);
-        for (int t = cta; t < p.RbO; t += G)
-          issue1(reinterpret_cast<const uint8_t*>(L.o_tiles) + (size_t)t * p.to.rec_bytes,
-                 p.to.rec_bytes);
-      }
-      for (int e = cta; e < p.E; e += G)
-        issue1(reinterpret_cast<const uint8_t*>(L.gate_w) + (size_t)e * p.H * 2, (uint32_t)p.H * 2u);
-      // while the router decides: the next layer's static weights into L2
-      if (l + 1 < p.n_layers && lane == 0) {
-        const duplex_stack_layer Ln = p.layers[l + 1];
-        if (p.has_attn) {
-          for (int t = cta; t < p.RbQ; t += G)
-            prefetch_l2(reinterpret_cast<const uint8_t*>(Ln.qkv_tiles) + (size_t)t * p.tq.rec_bytes,
-                        p.tq.rec_bytes);
-          for (int t = cta; t < p.RbO; t += G)
-            prefetch_l2(reinterpret_cast<const uint8_t*>(Ln.o_tiles) + (size_t)t * p.to.rec_bytes,
-                        p.to.rec_bytes);
-        }
-        for (int e = cta; e < p.E; e += G)
-          prefetch_l2(reinterpret_cast<const uint8_t*>(Ln.gate_w) + (size_t)e * p.H * 2,
-                      (uint32_t)p.H * 2u);
-      }
-      __syncwarp();
-      // routing plan of this layer (built by this CTA's consumers)
-      wait_phase(plan_ready, (uint32_t)(l & 1), abort_flag, p.err, kSitePlan);
-      int nu = *n_units_s;
-      nu = nu < 0 ? 0 : (nu > kMaxUnits ? kMaxUnits : nu);
-      // never turn an out-of-range id into a copy address
-      for (int u = lane; u < nu; u += 32)
-        if ((unsigned)unit_e[u] >= (unsigned)p.E) {
-          set_error(p.err, DUPLEX_DEVERR_EXPERT);
-          unit_e[u] = 0;
-        }
-      __syncwarp();
-      // gate|up: one copy of the (gate, up) record pair per tile
-      for (int t = cta; t < nu * perG; t += G) {
-        const int u = t / perG, rbi = t - u * perG;
-        issue1(reinterpret_cast<const uint8_t*>(L.gu_tiles) +
-                   ((size_t)unit_e[u] * (2 * perG) + 2 * rbi) * p.tgu.rec_bytes,
-               2u * p.tgu.rec_bytes);
-      }
-      // down: the records of up to `ups` units per stage, one copy per lane.  Down
-      // tiles are dealt from the last CTA backwards, so the CTAs with the fewest
-      // gate|up tiles take them first.
-      const int nstg = (nu + p.ups - 1) / p.ups;
-      for (int t = G - 1 - cta; t < p.RbD; t += G) {
-        for (int s = 0; s < nstg; ++s) {
-          const int u0 = s * p.ups;
-          const int cnt = (nu - u0) < p.ups ? (nu - u0) : p.ups;
-          acquire(i);
-          if (lane == 0) mbar_arrive_expect_tx(&full[i % NS], (uint32_t)cnt * p.tdn.rec_bytes);
-          __syncwarp();
-          if (lane < cnt)
-            bulk_g2s_stream(slot_ptr(i) + (uint32_t)lane * p.tdn.rec_bytes,
-                            reinterpret_cast<const uint8_t*>(L.dn_tiles) +
-                                ((size_t)unit_e[u0 + lane] * p.RbD + t) * p.tdn.rec_bytes,
-                            p.tdn.rec_bytes, &full[i % NS], pol);
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&full[i % NS]);
-          __syncwarp();
-          ++i;
-        }
-      }
-    }
-    // drain: never leave the CTA while a bulk copy may still target its smem
     if (lane == 0) {
+      // the producer waits on the consumers: a longer limit, so that a stuck consumer
+      // wait is the one that gives up (and names its site)
+      const long long plimit = 4 * limit;
+      const uint64_t pol = policy_evict_first();
+      int i = 0;  // stage sequence number
+      RingPos wp = {0, 0u};
+      bool ok = true;
+      // one stage of one or two copies of `bytes` each, side by side in the slot
+      auto issue2 = [&](const uint8_t* src0, const uint8_t* src1, uint32_t bytes) {
+        if (i >= NS)  // the slot's previous stage has been released by every consumer warp
+          wait_phase(&empty[wp.slot], wp.phase ^ 1u, abort_flag, p.err, kSiteEmpty, plimit);
+        if (*abort_flag) {
+          ok = false;
+          return;
+        }
+        uint8_t* dst = smem + p.off_ring + (uint32_t)wp.slot * p.slot_bytes;
+        mbar_arrive_expect_tx(&full[wp.slot], src1 ? 2u * bytes : bytes);
+        bulk_g2s_stream(dst, src0, bytes, &full[wp.slot], pol);
+        if (src1) bulk_g2s_stream(dst + bytes, src1, bytes, &full[wp.slot], pol);
+        mbar_arrive(&full[wp.slot]);
+        ++i;
+        wp.next(NS);
+      };
+      auto issue = [&](const uint8_t* src, uint32_t bytes) { issue2(src, nullptr, bytes); };
+      for (int l = 0; l < p.n_layers && ok; ++l) {
+        const duplex_stack_layer L = p.layers[l];
+        if (p.has_attn) {
+          for (int t = cta; t < p.RbQ && ok; t += G)
+            issue(reinterpret_cast<const uint8_t*>(L.qkv_tiles) + (size_t)t * p.tq.rec_bytes,
+                  p.tq.rec_bytes);
+          for (int t = cta; t < p.RbO && ok; t += G)
+            issue(reinterpret_cast<const uint8_t*>(L.o_tiles) + (size_t)t * p.to.rec_bytes,
+                  p.to.rec_bytes);
+        }
+        for (int b = rank; b < p.nblk && ok; b += kCS)
+          for (int k = 0; k < spb && ok; ++k) {
+            const int nks = (p.KS - k * p.kps) < p.kps ? (p.KS - k * p.kps) : p.kps;
+            issue(reinterpret_cast<const uint8_t*>(L.gate_w) +
+                      ((size_t)b * p.KS + (size_t)k * p.kps) * 512u,
+                  (uint32_t)nks * 512u);
+          }
+        if (!ok) break;
+        // routing plan of this layer (built by this CTA's consumers)
+        wait_phase(plan_ready, (uint32_t)(l & 1), abort_flag, p.err, kSitePlan, plimit);
+        if (*abort_flag) break;
+        int nu = *n_units_s;
+        nu = nu < 0 ? 0 : (nu > kMaxUnits ? kMaxUnits : nu);
+        int i0, i1;
+        item_range(nu * p.S, C, cid, i0, i1);
+        auto expert = [&](int it) {
+          int e = unit_e[it / p.S];
+          if ((unsigned)e >= (unsigned)p.E) {  // never turn a bad id into an address
+            set_error(p.err, DUPLEX_DEVERR_EXPERT);
+            e = 0;
+          }
+          return e;
+        };
+        auto dn_src = [&](int it) {
+          return reinterpret_cast<const uint8_t*>(L.dn_tiles) +
+                 (((size_t)expert(it) * p.S + it % p.S) * (p.H >> 4) + (size_t)rank * nrec) *
+                     p.tks.rec_bytes;
+        };
+        for (int b0 = i0; b0 < i1 && ok; b0 += p.ib) {
+          const int nbt = (i1 - b0) < p.ib ? (i1 - b0) : p.ib;
+          for (int k = 0; k < nbt && ok; ++k) {
+            const int it = b0 + k;
+            issue(reinterpret_cast<const uint8_t*>(L.gu_tiles) +
+                      ((size_t)expert(it) * (2 * perG) + 2 * ((it % p.S) * kCS + rank)) *
+                          p.tgu.rec_bytes,
+                  2u * p.tgu.rec_bytes);
+          }
+          for (int k = 0; k < nbt && ok; k += 2) {
+            if (k + 1 < nbt)
+              issue2(dn_src(b0 + k), dn_src(b0 + k + 1), p.dn_bytes);
+            else
+              issue(dn_src(b0 + k), p.dn_bytes);
+          }
+        }
+      }
+      // drain: never leave the CTA while a bulk copy may still target its smem
       const int first = i > NS ? i - NS : 0;
       for (int j = first; j < i; ++j) {
         const long long t0 = clock64();
-        bool ok = true;
+        bool done = true;
         while (!mbar_try_wait(&full[j % NS], (uint32_t)(j / NS) & 1u))
           if (clock64() - t0 > 200000000LL) {
-            ok = false;
+            done = false;
             break;
           }
-        if (!ok) {
+        if (!done) {
           give_up(abort_flag, p.err, kSiteDrain);
           break;
         }
       }
     }
+    __syncwarp();
+    cluster_sync_all();  // no CTA leaves while a peer may still write into its smem
     return;
   }
 
   // ================================================================== consumers
   float* red = reinterpret_cast<float*>(smem + kSRed);
+  float* ssq = reinterpret_cast<float*>(smem + kSSsq);
+  float* ls = reinterpret_cast<float*>(smem + kSLogit);
+  float* inv = reinterpret_cast<float*>(smem + kSInv);
+  float2* dgp0 = reinterpret_cast<float2*>(smem + p.off_av);  // [2][ib][kCS][8] partial sums
+  float2* dg = reinterpret_cast<float2*>(smem + p.off_dg);
+  const int nwin = kSliceK / (32 * (G32 ? 1 : 2));
   uint8_t* xsh = smem + p.off_x;
   float2* gsum = reinterpret_cast<float2*>(smem + p.off_gsum);
-  const int nT = p.T;
+  T* hpl = reinterpret_cast<T*>(smem + p.off_h);
+  const int nT = NT ? NT : p.T;
+  constexpr int KT = NT ? NT : kMaxTokens;
   const int cw = G32 ? 1 : 2;
+  const bool rms = p.rms_eps > 0.f;
   int* err = p.err;
-  int i = 0;       // stage sequence number
+  int i = 0;        // stage sequence number
   unsigned nb = 0;  // grid barriers passed
+  int kbatch = 0;   // item batches done (intermediate buffer parity)
+  float acc[kMaxRecPerWarp][4];
+#pragma unroll
+  for (int k = 0; k < kMaxRecPerWarp; ++k) zero4(acc[k]);
 
-  auto wait_full = [&](int j) {
-    wait_phase(&full[j % NS], (uint32_t)(j / NS) & 1u, abort_flag, err, kSiteFull);
+  RingPos rp = {0, 0u};  // the consumers' position in the ring (stage i)
+  auto wait_full = [&]() { wait_phase(&full[rp.slot], rp.phase, abort_flag, err, kSiteFull, limit); };
+  auto slot_ptr = [&]() { return smem + p.off_ring + (uint32_t)rp.slot * p.slot_bytes; };
+  auto next_stage = [&]() {
+    ++i;
+    rp.next(NS);
   };
-  auto slot_ptr = [&](int j) { return smem + p.off_ring + (uint32_t)(j % NS) * p.slot_bytes; };
   auto sync_grid = [&]() {
     grid_arrive(p.barrier);
-    grid_wait(p.barrier, ++nb, abort_flag, err);
+    ++nb;
+    grid_wait(p.barrier, nb, nb == 1 && (p.test_flags & 1), abort_flag, err, limit);
+  };
+  auto partials = [&](int l) {
+    return p.part + (size_t)(l & 1) * kMaxClusters * nT * p.H;
   };
 
   for (int l = 0; l < p.n_layers; ++l) {
     const duplex_stack_layer L = p.layers[l];
-    const bool last = l == p.n_layers - 1;
-    const T* hin = reinterpret_cast<const T*>(l == 0 ? p.x_in : p.hbuf[l & 1]);
-    T* hout = reinterpret_cast<T*>(last ? p.out : p.hbuf[(l + 1) & 1]);
-    const T* hm = hin;  // MoE input
-    if (p.has_attn) {
-      // ---------------------------------------------------------------- Q
-      stage_rows<T>(reinterpret_cast<const uint8_t*>(hin), p.H, nT, p.H, nT, xsh, p.x_pitch,
-                    p.rms_eps > 0.f, p.rms_eps, nullptr, gsum, cw, red, kStageAll);
-      {
-        const int rmax = defer_tiles(1, nT);
-        int j = 0, t0 = cta;
-        for (int tile = cta; tile < p.RbQ; tile += G, ++i) {
-          wait_full(i);
-          const Acc2 a = tile_acc<T, S, 1, G32>(slot_ptr(i), p.tq, xsh, p.x_pitch, gsum, nT,
-                                                &empty[i % NS]);
-          put_partials<1>(red, j++, a, nT, warp, lane);
-          if (j == rmax || tile + G >= p.RbQ) {
-            named_bar_sync(1, kConsumers);
-            if (tid < j * nT * 16) {
-              const float v = sum_partials<1>(red, tid, nT).x;
-              const int jj = tid / (nT * 16), n = (tid >> 4) - jj * nT;
-              const int row = (t0 + jj * G) * 16 + (tid & 15);
-              reinterpret_cast<T*>(p.qkv)[(size_t)n * p.qkv_R + row] = from_f32<T>(v);
-            }
-            named_bar_sync(1, kConsumers);
-            j = 0;
-            t0 = tile + G;
-          }
-        }
-      }
-      sync_grid();
-      // ---------------------------------------------------------------- O
-      if (cta < p.RbO)
-        stage_rows<T>(reinterpret_cast<const uint8_t*>(p.qkv), p.qkv_R, nT, p.q_dim, nT, xsh,
-                      p.x_pitch, false, 0.f, nullptr, gsum, cw, red, kStageAll);
-      {
-        const int rmax = defer_tiles(1, nT);
-        int j = 0, t0 = cta;
-        for (int tile = cta; tile < p.RbO; tile += G, ++i) {
-          wait_full(i);
-          const Acc2 a = tile_acc<T, S, 1, G32>(slot_ptr(i), p.to, xsh, p.x_pitch, gsum, nT,
-                                                &empty[i % NS]);
-          put_partials<1>(red, j++, a, nT, warp, lane);
-          if (j == rmax || tile + G >= p.RbO) {
-            named_bar_sync(1, kConsumers);
-            if (tid < j * nT * 16) {
-              const float v = sum_partials<1>(red, tid, nT).x;
-              const int jj = tid / (nT * 16), n = (tid >> 4) - jj * nT;
-              const int row = (t0 + jj * G) * 16 + (tid & 15);
-              const float res = to_f32<T>(__ldcg(hin + (size_t)n * p.H + row));
-              reinterpret_cast<T*>(p.h1)[(size_t)n * p.H + row] =
-                  from_f32<T>(to_f32<T>(from_f32<T>(v)) + res);
-            }
-            named_bar_sync(1, kConsumers);
-            j = 0;
-            t0 = tile + G;
-          }
-        }
-      }
-      sync_grid();
-      hm = reinterpret_cast<const T*>(p.h1);
-    }
-    // ------------------------------------------------------------------ R
-    // normalised rows and this CTA's logit first; their fragment-order staging for
-    // the gate|up tiles runs while the logits barrier is in flight
-    {
-      const bool row = cta < p.E;
-      if (row) wait_full(i);
-      const float a = router_fused<T>(reinterpret_cast<const uint8_t*>(hm), p.H, nT, p.rms_eps > 0.f,
-                                      p.rms_eps, xsh, p.x_pitch, row ? slot_ptr(i) : nullptr,
-                                      L.gate_b, cta, red, &empty[i % NS]);
-      if (row) {
-        if (tid < nT) p.logits[(size_t)tid * p.E + cta] = a;
-        ++i;
-      }
-      for (int e = cta + G; e < p.E; e += G, ++i) {  // more experts than CTAs
-        wait_full(i);
-        const float a2 = router_row<T>(slot_ptr(i), xsh, p.x_pitch, p.H, nT, L.gate_b, e, red,
-                                       &empty[i % NS]);
-        if (tid < nT) p.logits[(size_t)tid * p.E + e] = a2;
-      }
-    }
-    grid_arrive(p.barrier);
-    stage_rows<T>(nullptr, 0, nT, p.H, nT, xsh, p.x_pitch, false, 0.f, nullptr, gsum, cw, red,
-                  kStageFrag);
-    grid_wait(p.barrier, ++nb, abort_flag, err);
-    // ------------------------------------------------------------------ D
-    const int nu = nT == 1 ? plan_one<T>(p.logits, p.E, p.top_k, smem, red)
-                           : plan_units<T>(p.logits, nT, p.E, p.top_k, smem, red);
-    if (tid == 0) mbar_arrive(plan_ready);
-    plan_weights(nT, p.E, p.top_k, p.norm, smem, red);
-    // ------------------------------------------------------------------ G
-    {
-      const int rmax = defer_tiles(2, nT);
-      int j = 0, t0 = cta;
-      for (int tile = cta; tile < nu * perG; tile += G, ++i) {
-        wait_full(i);
-        const Acc2 a = tile_acc<T, S, 2, G32>(slot_ptr(i), p.tgu, xsh, p.x_pitch, gsum, nT,
-                                              &empty[i % NS]);
-        put_partials<2>(red, j++, a, nT, warp, lane);
-        if (j == rmax || tile + G >= nu * perG) {
-          named_bar_sync(1, kConsumers);
-          if (tid < j * nT * 16) {
-            const float2 v = sum_partials<2>(red, tid, nT);
-            const int jj = tid / (nT * 16), n = (tid >> 4) - jj * nT;
-            const int tl = t0 + jj * G;
-            const int u = tl / perG, row = (tl - u * perG) * 16 + (tid & 15);
-            const float a = ((unit_m[u] >> n) & 1u) ? silu_f32(v.x) * v.y : 0.f;
-            reinterpret_cast<T*>(p.act)[((size_t)u * nT + n) * p.I + row] = from_f32<T>(a);
-          }
-          named_bar_sync(1, kConsumers);
-          j = 0;
-          t0 = tile + G;
-        }
-      }
-    }
-    sync_grid();
-    // ------------------------------------------------------------------ N
-    const int nstg = (nu + p.ups - 1) / p.ups;
-    const int ncu = p.tdn.npairs * (G32 ? 2 : 1);  // correction units per record
-    int a0 = -1, acnt = 0;                         // staged activation units [a0, a0 + acnt)
-    for (int tile = G - 1 - cta; tile < p.RbD; tile += G) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int s = 0; s < nstg; ++s, ++i) {
-        const int u0 = s * p.ups;
-        const int cnt = (nu - u0) < p.ups ? (nu - u0) : p.ups;
-        if (a0 < 0 || u0 < a0 || u0 + cnt > a0 + acnt) {
-          a0 = u0;
-          acnt = (nu - u0) < p.act_units ? (nu - u0) : p.act_units;
-          stage_rows<T>(reinterpret_cast<const uint8_t*>(p.act) + (size_t)a0 * nT * p.I * 2, p.I,
-                        acnt * nT, p.I, nT, xsh, p.xd_pitch, false, 0.f, nullptr, gsum, cw, red,
-                        kStageAll);
-        }
-        wait_full(i);
-        const float4 d = stage_rm<T, S, G32>(slot_ptr(i), p.tdn, cnt,
-                                             xsh + (uint32_t)((u0 - a0) * nT) * p.xd_pitch,
-                                             p.xd_pitch, nT, gsum + (size_t)(u0 - a0) * ncu * 8, ncu,
-                                             unit_w + u0 * kMaxTokens, &empty[i % NS]);
-        acc.x += d.x;
-        acc.y += d.y;
-        acc.z += d.z;
-        acc.w += d.w;
-      }
-      const float v = reduce4(red, acc, nT);
-      if (tid < nT * 16) {
-        const int n = tid >> 4, row = tile * 16 + (tid & 15);
-        float y = v;
-        if (p.moe_residual) y += to_f32<T>(__ldcg(hm + (size_t)n * p.H + row));
-        hout[(size_t)n * p.H + row] = from_f32<T>(y);
+    // ------------------------------------------------------------------ h
+    if (l == 0) {
+      load_rows<T>(reinterpret_cast<const T*>(p.x_in), nT, p.H, hpl);
+      if (rms) local_inv_rms<T>(hpl, nT, p.H, p.rms_eps, inv);
+    } else {
+      ++nb;
+      grid_wait(p.barrier, nb, nb == 1 && (p.test_flags & 1), abort_flag, err, limit);
+      reduce_rows_h<T, KT>(partials(l - 1), C, nT, p.H, row0, p.rrows,
+                       p.moe_residual != 0, hpl, ssq, rank, nullptr, red);
+      signal_cluster_xchg(hx_full);
+      wait_cluster_xchg(hx_full, (uint32_t)((l - 1) & 1), abort_flag, err, limit);
+      if (tid < nT) {
+        float a = 0.f;
+#pragma unroll
+        for (int q = 0; q < kCS; ++q) a += ssq[q * kMaxTokens + tid];
+        inv[tid] = 1.0f / sqrtf(a / (float)p.H + p.rms_eps);
       }
       named_bar_sync(1, kConsumers);
     }
-    if (!last) sync_grid();
+    normalise_rows<T>(hpl, nT, p.H, inv, rms, xsh, p.x_pitch);
+    if (p.has_attn) {
+      // -------------------------------------------------------------- Q
+      stage_rows<T>(nullptr, 0, nT, p.H, xsh, p.x_pitch, gsum, cw, kStageFrag);
+      {
+        const int rmax = defer_tiles(nT);
+        int j = 0, t0 = cta;
+        for (int tile = cta; tile < p.RbQ; tile += G, next_stage()) {
+          wait_full();
+          tile_acc<T, S, 1, G32>(slot_ptr(), p.tq, xsh, p.x_pitch, gsum, nT, &empty[rp.slot], red,
+                                 j++);
+          if (j == rmax || tile + G >= p.RbQ) {
+            named_bar_sync(1, kConsumers);
+            if (tid < j * nT * 16) {
+              const float v = sum_partials(red, tid, nT);
+              const int jj = tid / (nT * 16), n = (tid >> 4) - jj * nT;
+              const int row = (t0 + jj * G) * 16 + (tid & 15);
+              if (row < p.qkv_R)
+                reinterpret_cast<T*>(p.qkv)[(size_t)n * p.qkv_R + row] = from_f32<T>(v);
+            }
+            named_bar_sync(1, kConsumers);
+            j = 0;
+            t0 = tile + G;
+          }
+        }
+      }
+      sync_grid();
+      // -------------------------------------------------------------- O
+      if (cta < p.RbO)
+        stage_rows<T>(reinterpret_cast<const uint8_t*>(p.qkv), p.qkv_R, nT, p.q_dim, xsh,
+                      p.x_pitch, gsum, cw, kStageAll);
+      {
+        const int rmax = defer_tiles(nT);
+        int j = 0, t0 = cta;
+        for (int tile = cta; tile < p.RbO; tile += G, next_stage()) {
+          wait_full();
+          tile_acc<T, S, 1, G32>(slot_ptr(), p.to, xsh, p.x_pitch, gsum, nT, &empty[rp.slot], red,
+                                 j++);
+          if (j == rmax || tile + G >= p.RbO) {
+            named_bar_sync(1, kConsumers);
+            if (tid < j * nT * 16) {
+              const float v = sum_partials(red, tid, nT);
+              const int jj = tid / (nT * 16), n = (tid >> 4) - jj * nT;
+              const int row = (t0 + jj * G) * 16 + (tid & 15);
+              if (row < p.H) {
+                const float res = to_f32<T>(hpl[(size_t)n * p.H + row]);
+                reinterpret_cast<T*>(p.h1)[(size_t)n * p.H + row] =
+                    from_f32<T>(to_f32<T>(from_f32<T>(v)) + res);
+              }
+            }
+            named_bar_sync(1, kConsumers);
+            j = 0;
+            t0 = tile + G;
+          }
+        }
+      }
+      sync_grid();
+      // the MoE input (and residual): h1 from every CTA's o rows
+      load_rows<T>(reinterpret_cast<const T*>(p.h1), nT, p.H, hpl);
+      if (rms) local_inv_rms<T>(hpl, nT, p.H, p.rms_eps, inv);
+      normalise_rows<T>(hpl, nT, p.H, inv, rms, xsh, p.x_pitch);
+    }
+    // ------------------------------------------------------------------ router
+    router_mma<T>(smem + p.off_ring, p.slot_bytes, NS, rp, rank, p.nblk, p.KS, p.kps, p.E, nT,
+                  xsh, p.x_pitch, L.gate_b, ls, red, full, empty, abort_flag, err, limit);
+    for (int k = 0; k < ngs; ++k) next_stage();
+    signal_cluster_xchg(lg_full);
+    // fragment-order staging of the normalised tokens while the logits travel
+    stage_rows<T>(nullptr, 0, nT, p.H, xsh, p.x_pitch, gsum, cw, kStageFrag);
+    wait_cluster_xchg(lg_full, (uint32_t)(l & 1), abort_flag, err, limit);
+    // ------------------------------------------------------------------ plan
+    const int nu = nT != 1   ? plan_units<T>(nT, p.E, p.top_k, smem, red)
+                   : p.E <= 128 ? plan_one<T, 4>(p.E, p.top_k, p.norm, smem, red)
+                                : plan_one<T, kMaxExperts / 32>(p.E, p.top_k, p.norm, smem, red);
+    if (tid == 0) mbar_arrive(plan_ready);
+    if (nT != 1 || !p.norm) plan_weights(nT, p.E, p.top_k, p.norm, smem, red);
+    // ------------------------------------------------------------------ items
+    int i0, i1;
+    item_range(nu * p.S, C, cid, i0, i1);
+    for (int b0 = i0; b0 < i1; b0 += p.ib) {
+      const int nbt = (i1 - b0) < p.ib ? (i1 - b0) : p.ib;
+      const int b = kbatch & 1;
+      uint8_t* xd = smem + p.off_xd + (uint32_t)b * (uint32_t)(p.ib * nT) * kXdPitch;
+      // gate|up tile pairs (slice rows [16 rank, 16 rank + 16)), partials deferred
+      for (int k = 0; k < nbt; ++k, next_stage()) {
+        wait_full();
+        tile_acc<T, S, 2, G32>(slot_ptr(), p.tgu, xsh, p.x_pitch, gsum, nT, &empty[rp.slot], red,
+                               k);
+      }
+      named_bar_sync(1, kConsumers);
+      float2* dgp = dgp0 + (uint32_t)b * (uint32_t)(p.ib * kCS * 8);
+      act_send<T>(red, nbt, nT, b0, p.S, unit_m, rank, xd, dgp, &act_full[b]);
+      wait_cluster_xchg(&act_full[b], (uint32_t)((kbatch >> 1) & 1), abort_flag, err, limit);
+      if (G32 || p.tks.gshift != 1) dg_from_partials<T>(dgp, nbt, nT, cw, dg);
+      // down: this CTA's output rows x each item's 128 columns, two items per stage
+      for (int k = 0; k < nbt; k += 2, next_stage()) {
+        const int nit = (nbt - k) < 2 ? 1 : 2;
+        const int u0 = (b0 + k) / p.S, u1 = (b0 + k + nit - 1) / p.S;
+        wait_full();
+        slice_down<T, S, G32>(slot_ptr(), p.tks, nrec, p.dn_bytes, nit,
+                              xd + (uint32_t)(k * nT) * kXdPitch, dgp + k * kCS * 8,
+                              dg + k * nwin * 8, nwin,
+                              unit_w + u0 * kMaxTokens, unit_w + u1 * kMaxTokens, nT, acc,
+                              &empty[rp.slot]);
+      }
+      ++kbatch;
+    }
+    // ------------------------------------------------------------------ end of layer
+    write_partials(partials(l) + (size_t)cid * nT * p.H, nT, p.H, row0, nrec, acc);
+    grid_arrive(p.barrier);
   }
+  // the result: cluster 0 adds the last layer's partial outputs
+  ++nb;
+  grid_wait(p.barrier, nb, nb == 1 && (p.test_flags & 1), abort_flag, err, limit);
+  if (cid == 0)
+    reduce_rows_h<T, KT>(partials(p.n_layers - 1), C, nT, p.H, row0, p.rrows, p.moe_residual != 0, hpl,
+                     ssq, rank, reinterpret_cast<T*>(p.out), red);
+  cluster_sync_all();
+}
+
+// ---------------------------------------------------------------- down K-slices
+// Record (e, s, rb): rows [16 rb, 16 rb + 16) x columns [128 s, 128 s + 128) of
+// expert e's down matrix [H][I] in the tile-record layout of tiles.cuh (K = 128, its
+// 128 / group groups), padded to 16 bytes; records ordered [E][I / 128][H / 16].
+template <typename S>
+__global__ void slice_repack_kernel(const int32_t* __restrict__ packed,
+                                    const S* __restrict__ scale, const int32_t* __restrict__ zeros,
+                                    int E, int H, int I, int G, int GZ, TileGeom tg,
+                                    uint32_t* __restrict__ out) {
+  const int Rb = H >> 4, NSl = I / kSliceK, C = I >> 3;
+  const uint32_t wpr = tg.rec_bytes / 4u;
+  const long long total = (long long)E * NSl * Rb * wpr;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const long long rec = idx / wpr;
+    const uint32_t o = (uint32_t)(idx - rec * wpr) * 4u;
+    const int rb = (int)(rec % Rb);
+    const long long es = rec / Rb;
+    const int s = (int)(es % NSl), e = (int)(es / NSl);
+    uint32_t val = 0;
+    if (o < tg.off_scale) {
+      const int pr = (int)(o >> 9);
+      const int ln = (int)((o & 511u) >> 4);
+      const int j = (int)((o & 15u) >> 2);
+      const int g = ln >> 2, t = ln & 3;
+      const int row = rb * 16 + g + ((j & 1) ? 8 : 0);
+      const int word = s * (kSliceK / 8) + 8 * pr + t + ((j & 2) ? 4 : 0);
+      val = (uint32_t)packed[((long long)e * H + row) * C + word];
+    } else if (o < tg.off_zero) {
+      const int q = (int)((o - tg.off_scale) >> 2);
+      const int grp = s * tg.Gr + (q >> 3), g = q & 7;
+      const int ra = rb * 16 + g, rbw = ra + 8;
+      const uint16_t sa = *reinterpret_cast<const uint16_t*>(&scale[((long long)e * H + ra) * G + grp]);
+      const uint16_t sb = *reinterpret_cast<const uint16_t*>(&scale[((long long)e * H + rbw) * G + grp]);
+      val = (uint32_t)sa | ((uint32_t)sb << 16);
+    } else if (tg.has_zeros && o < tg.off_zero + (uint32_t)tg.Gr * 8u) {
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int q = (int)(o - tg.off_zero) + b;
+        const int grp = s * tg.Gr + (q >> 3), g = q & 7;
+        const int ra = rb * 16 + g, rbw = ra + 8;
+        const uint32_t za =
+            ((uint32_t)zeros[((long long)e * H + ra) * GZ + (grp >> 3)] >> ((grp & 7) * 4)) & 15u;
+        const uint32_t zb =
+            ((uint32_t)zeros[((long long)e * H + rbw) * GZ + (grp >> 3)] >> ((grp & 7) * 4)) & 15u;
+        val |= (za | (zb << 4)) << (8 * b);
+      }
+    }
+    out[idx] = val;
+  }
+}
+
+// Gate records: word j of lane (g, t) for (block b, k-step ks) is the mma.sync A
+// register j of rows 16 b + g (j = 0, 2) or 16 b + g + 8 (j = 1, 3), columns
+// 16 ks + 2t, 2t + 1 (j = 0, 1) or 16 ks + 2t + 8, 2t + 9 (j = 2, 3); rows past E are 0.
+__global__ void gate_repack_kernel(const uint16_t* __restrict__ w, int E, int H,
+                                   uint32_t* __restrict__ out) {
+  const int KS = H >> 4;
+  const long long total = (long long)((E + 15) >> 4) * KS * 128;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int j = (int)(idx & 3), lane = (int)((idx >> 2) & 31);
+    const long long bk = idx >> 7;
+    const int ks = (int)(bk % KS), b = (int)(bk / KS);
+    const int g = lane >> 2, t = lane & 3;
+    const int row = b * 16 + g + ((j & 1) ? 8 : 0);
+    const int col = ks * 16 + 2 * t + ((j & 2) ? 8 : 0);
+    uint32_t v = 0;
+    if (row < E)
+      v = (uint32_t)w[(size_t)row * H + col] | ((uint32_t)w[(size_t)row * H + col + 1] << 16);
+    out[idx] = v;
+  }
+}
+
+static int slice_geom(int group, int has_zeros, TileGeom* tg) {
+  if (group != 32 && group != 64 && group != 128) return 1;
+  if (tile_geom(kSliceK, group, has_zeros, tg)) return 1;
+  const uint32_t end = tg->off_zero + (has_zeros ? (uint32_t)tg->Gr * 8u : 0u);
+  tg->rec_bytes = (end + 15u) / 16u * 16u;
+  return 0;
 }
 
 // ====================================================================== host side
 static inline uint32_t up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
 struct StackScratch {
-  size_t barrier, hbuf[2], qkv, h1, logits, act, total;
+  size_t barrier, part, qkv, h1, total;
 };
 
-static int units_cap(int T, int E, int top_k) {
-  int units = T * top_k < E ? T * top_k : E;
-  return units > kMaxUnits ? kMaxUnits : units;
-}
-
-static StackScratch stack_scratch(int T, int H, int E, int I, int top_k, int qkv_R) {
+static StackScratch stack_scratch(int T, int H, int qkv_R) {
   StackScratch s;
   size_t off = 0;
   s.barrier = off;
   off += 256;
-  for (int k = 0; k < 2; ++k) {
-    s.hbuf[k] = off;
-    off += align_up((size_t)T * H * 2, 256);
-  }
+  s.part = off;
+  off += align_up((size_t)2 * kMaxClusters * T * H * 4, 256);
   s.qkv = off;
   off += align_up((size_t)T * (qkv_R > 0 ? qkv_R : 1) * 2, 256);
   s.h1 = off;
   off += align_up((size_t)T * H * 2, 256);
-  s.logits = off;
-  off += align_up((size_t)T * E * 4, 256);
-  s.act = off;
-  off += align_up((size_t)units_cap(T, E, top_k) * T * I * 2, 256);
   s.total = off;
   return s;
 }
@@ -1113,10 +1531,72 @@ static StackScratch stack_scratch(int T, int H, int E, int I, int top_k, int qkv
 
 using namespace duplex;
 
+extern "C" int duplex_down_slices_bytes(int32_t E, int32_t H, int32_t I, int32_t group,
+                                        int has_zeros, size_t* bytes) {
+  if (!bytes || E < 1 || H < 16 || (H & 15) || I < kSliceK || (I % kSliceK)) return DUPLEX_ERR_ARG;
+  TileGeom tg;
+  if (slice_geom(group, has_zeros, &tg)) return DUPLEX_ERR_UNSUPPORTED;
+  *bytes = (size_t)E * (I / kSliceK) * (H / 16) * tg.rec_bytes;
+  return DUPLEX_OK;
+}
+
+extern "C" int duplex_repack_down_slices(const int32_t* packed, const void* scale,
+                                         const int32_t* zeros, int scale_dtype, int32_t E,
+                                         int32_t H, int32_t I, int32_t group, void* out,
+                                         size_t out_bytes, void* stream) {
+  size_t need = 0;
+  int rc = duplex_down_slices_bytes(E, H, I, group, zeros != nullptr, &need);
+  if (rc) return rc;
+  if (!packed || !scale || !out) return DUPLEX_ERR_ARG;
+  if (out_bytes < need) return DUPLEX_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(out) & 15u) return DUPLEX_ERR_ALIGN;
+  TileGeom tg;
+  slice_geom(group, zeros != nullptr, &tg);
+  const int G = I / group, GZ = (G + 7) / 8;
+  const long long words = (long long)(need / 4);
+  long long blocks = (words + 255) / 256;
+  if (blocks > 65535) blocks = 65535;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (scale_dtype == DUPLEX_DTYPE_F16)
+    slice_repack_kernel<__half><<<(int)blocks, 256, 0, st>>>(
+        packed, reinterpret_cast<const __half*>(scale), zeros, E, H, I, G, GZ, tg,
+        reinterpret_cast<uint32_t*>(out));
+  else if (scale_dtype == DUPLEX_DTYPE_BF16)
+    slice_repack_kernel<__nv_bfloat16><<<(int)blocks, 256, 0, st>>>(
+        packed, reinterpret_cast<const __nv_bfloat16*>(scale), zeros, E, H, I, G, GZ, tg,
+        reinterpret_cast<uint32_t*>(out));
+  else
+    return DUPLEX_ERR_DTYPE;
+  return record_cuda(cudaGetLastError());
+}
+
+extern "C" int duplex_gate_records_bytes(int32_t E, int32_t H, size_t* bytes) {
+  if (!bytes || E < 1 || H < 16 || (H & 15)) return DUPLEX_ERR_ARG;
+  *bytes = (size_t)((E + 15) / 16) * (H / 16) * 512;
+  return DUPLEX_OK;
+}
+
+extern "C" int duplex_repack_gate_records(const void* gate_w, int dtype, int32_t E, int32_t H,
+                                          void* out, size_t out_bytes, void* stream) {
+  size_t need = 0;
+  int rc = duplex_gate_records_bytes(E, H, &need);
+  if (rc) return rc;
+  if (!gate_w || !out) return DUPLEX_ERR_ARG;
+  if (dtype != DUPLEX_DTYPE_F16 && dtype != DUPLEX_DTYPE_BF16) return DUPLEX_ERR_DTYPE;
+  if (out_bytes < need) return DUPLEX_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(out) & 15u) return DUPLEX_ERR_ALIGN;
+  const long long words = (long long)(need / 4);
+  long long blocks = (words + 255) / 256;
+  if (blocks > 65535) blocks = 65535;
+  gate_repack_kernel<<<(int)blocks, 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const uint16_t*>(gate_w), E, H, reinterpret_cast<uint32_t*>(out));
+  return record_cuda(cudaGetLastError());
+}
+
 extern "C" int duplex_stack_workspace_bytes(int32_t T, int32_t H, int32_t E, int32_t I,
                                             int32_t top_k, int32_t qkv_R, size_t* bytes) {
   if (!bytes || T < 1 || H < 1 || E < 1 || I < 1 || top_k < 1) return DUPLEX_ERR_ARG;
-  *bytes = stack_scratch(T, H, E, I, top_k, qkv_R).total;
+  *bytes = stack_scratch(T, H, qkv_R).total;
   return DUPLEX_OK;
 }
 
@@ -1126,7 +1606,8 @@ extern "C" int duplex_stack_forward(const duplex_stack_layer* layers, int32_t n_
                                     int32_t T, int32_t H, int32_t E, int32_t I, int32_t top_k,
                                     int32_t norm_topk, int32_t qkv_R, int32_t q_dim,
                                     int32_t group, float rms_eps, void* workspace,
-                                    size_t workspace_bytes, int32_t* err, void* stream) {
+                                    size_t workspace_bytes, int64_t wait_limit_cycles,
+                                    int32_t test_flags, int32_t* err, void* stream) {
   if (!layers || n_layers < 1 || n_layers > 255 || !x_in || !out || !workspace || !err)
     return DUPLEX_ERR_ARG;
   if (T < 1 || T > kMaxTokens || E < 1 || E > kMaxExperts || top_k < 1 || top_k > kMaxTopK ||
@@ -1134,9 +1615,11 @@ extern "C" int duplex_stack_forward(const duplex_stack_layer* layers, int32_t n_
     return DUPLEX_ERR_ARG;
   if (act_dtype != DUPLEX_DTYPE_F16 && act_dtype != DUPLEX_DTYPE_BF16) return DUPLEX_ERR_DTYPE;
   if (scale_dtype != act_dtype) return DUPLEX_ERR_DTYPE;
-  if ((H & 63) || (I & 63) || group < 32 || (group & (group - 1))) return DUPLEX_ERR_UNSUPPORTED;
+  // H: whole 16-row down records per CTA, at most kMaxRecPerWarp per warp; I: whole slices
+  if (H % (16 * kCS) || H > 16 * kCS * kCW * kMaxRecPerWarp || I % kSliceK || I < kSliceK)
+    return DUPLEX_ERR_UNSUPPORTED;
   StackParams p = {};
-  if (tile_geom(H, group, has_zeros, &p.tgu) || tile_geom(I, group, has_zeros, &p.tdn))
+  if (tile_geom(H, group, has_zeros, &p.tgu) || slice_geom(group, has_zeros, &p.tks))
     return DUPLEX_ERR_UNSUPPORTED;
   p.has_attn = has_attn ? 1 : 0;
   if (p.has_attn) {
@@ -1145,13 +1628,11 @@ extern "C" int duplex_stack_forward(const duplex_stack_layer* layers, int32_t n_
     if (tile_geom(H, group, has_zeros, &p.tq) || tile_geom(q_dim, group, has_zeros, &p.to))
       return DUPLEX_ERR_UNSUPPORTED;
   }
-  const int G = num_sms();
-  const StackScratch L = stack_scratch(T, H, E, I, top_k, p.has_attn ? qkv_R : 0);
+  const StackScratch L = stack_scratch(T, H, p.has_attn ? qkv_R : 0);
   if (workspace_bytes < L.total) return DUPLEX_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) | reinterpret_cast<uintptr_t>(x_in) |
        reinterpret_cast<uintptr_t>(out)) & 15u)
     return DUPLEX_ERR_ALIGN;
-  // staged rows must fit the per-thread chunk registers
   const int maxK = p.has_attn && q_dim > H ? q_dim : H;
   if (T * maxK > kMaxChunks * 8 * kConsumers) return DUPLEX_ERR_UNSUPPORTED;
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
@@ -1159,48 +1640,49 @@ extern "C" int duplex_stack_forward(const duplex_stack_layer* layers, int32_t n_
   p.n_layers = n_layers;
   p.T = T; p.H = H; p.E = E; p.I = I; p.top_k = top_k; p.norm = norm_topk;
   p.q_dim = q_dim; p.qkv_R = qkv_R; p.moe_residual = moe_residual ? 1 : 0;
-  p.RbQ = (qkv_R + 15) / 16; p.RbO = (H + 15) / 16; p.RbD = (H + 15) / 16;
+  p.RbQ = (qkv_R + 15) / 16; p.RbO = (H + 15) / 16;
+  p.S = I / kSliceK;
+  p.rrows = H / kCS;
+  p.nblk = (E + 15) / 16;
   p.rms_eps = rms_eps;
   p.x_in = x_in; p.out = out;
-  for (int k = 0; k < 2; ++k) p.hbuf[k] = ws + L.hbuf[k];
+  p.part = reinterpret_cast<float*>(ws + L.part);
   p.qkv = ws + L.qkv;
   p.h1 = ws + L.h1;
-  p.logits = reinterpret_cast<float*>(ws + L.logits);
-  p.act = ws + L.act;
   p.barrier = reinterpret_cast<unsigned*>(ws + L.barrier);
   p.err = err;
-  // ring slot: the largest stage -- a q|k|v record, an o record, a gate row, or a
-  // gate|up record pair; down stages take as many unit records as fit
+  p.wait_limit = wait_limit_cycles > 0 ? (long long)wait_limit_cycles : kWaitLimitCycles;
+  p.test_flags = test_flags;
+  // ring slot: the largest stage -- a q|k|v record, an o record, a gate|up record pair,
+  // a CTA's down records of one slice; gate rows take as many rows as fit
   uint32_t slot = 2u * p.tgu.rec_bytes;
   if (p.has_attn) {
     slot = slot > p.tq.rec_bytes ? slot : p.tq.rec_bytes;
     slot = slot > p.to.rec_bytes ? slot : p.to.rec_bytes;
   }
-  slot = slot > (uint32_t)H * 2u ? slot : (uint32_t)H * 2u;
-  if (slot < p.tdn.rec_bytes) slot = p.tdn.rec_bytes;
+  p.dn_bytes = (uint32_t)(p.rrows / 16) * p.tks.rec_bytes;
+  slot = slot > 2u * p.dn_bytes ? slot : 2u * p.dn_bytes;
   slot = up(slot, 128);
-  int ups = (int)(slot / p.tdn.rec_bytes);
-  if (ups > 32) ups = 32;
-  // activation units staged at once for the down projection (at least one stage)
-  const int by_regs = (kMaxChunks * 8 * kConsumers) / (T * I);
-  if (by_regs < 1) return DUPLEX_ERR_UNSUPPORTED;
-  if (ups > by_regs) ups = by_regs;
-  const int ucap = units_cap(T, E, top_k);
-  int act_units = ucap < by_regs ? ucap : by_regs;
-  if (act_units < ups) act_units = ups;
-  p.ups = ups;
-  p.act_units = act_units;
+  p.KS = H / 16;
+  p.kps = (int)(slot / 512u);
+  if (p.kps > p.KS) p.kps = p.KS;
   p.slot_bytes = slot;
   p.x_pitch = up((uint32_t)((maxK + 63) / 64 * 64) * 2u, 128) + 64u;
-  p.xd_pitch = up((uint32_t)I * 2u, 128) + 64u;
-  const uint32_t x_bytes_q = (uint32_t)T * p.x_pitch;
-  const uint32_t x_bytes_d = (uint32_t)(act_units * T) * p.xd_pitch;
-  const uint32_t x_bytes = x_bytes_q > x_bytes_d ? x_bytes_q : x_bytes_d;
-  const int gs_q = (maxK / 32) * 8, gs_d = act_units * (I / 32) * 8;
-  const uint32_t gsum_bytes = (uint32_t)((gs_q > gs_d ? gs_q : gs_d) * 8);
-  p.off_gsum = up(kSFixedEnd, 128);
-  p.off_x = up(p.off_gsum + gsum_bytes, 128);
-  p.off_ring = up(p.off_x + x_bytes, 128);
+  const uint32_t gsum_bytes = (uint32_t)((maxK / 32) * 8 * 8);
+  // items per batch: their deferred gate|up partials fit `red`, their rows fit xd
+  int ib = kMaxBatch;
+  const int by_red = (int)(kSRedBytes / 4) / (2 * kCW * T * 16);
+  if (ib > by_red) ib = by_red;
+  if (ib > kMaxBatchRows / T) ib = kMaxBatchRows / T;
+  if (ib < 1) return DUPLEX_ERR_UNSUPPORTED;
+  p.ib = ib;
+  p.off_xd = up(kSFixedEnd, 128);
+  p.off_av = p.off_xd + 2u * (uint32_t)(ib * T) * kXdPitch;           // column-sum partials
+  p.off_dg = up(p.off_av + 2u * (uint32_t)ib * kCS * 8u * 8u, 16);
+  p.off_gsum = up(p.off_dg + (uint32_t)ib * 4u * 8u * 8u, 128);
+  p.off_h = up(p.off_gsum + gsum_bytes, 128);
+  p.off_x = up(p.off_h + (uint32_t)T * (uint32_t)H * 2u, 128);
+  p.off_ring = up(p.off_x + (uint32_t)T * p.x_pitch, 128);
   const size_t kMax = 227 * 1024;
   int ns = p.off_ring < kMax ? (int)((kMax - p.off_ring) / slot) : 0;
   if (ns > kSlotsMax) ns = kSlotsMax;
@@ -1211,28 +1693,45 @@ extern "C" int duplex_stack_forward(const duplex_stack_layer* layers, int32_t n_
   cudaStream_t st = (cudaStream_t)stream;
   const bool g32 = group == 32;
   void (*kern)(StackParams);
-  if (act_dtype == DUPLEX_DTYPE_F16)
-    kern = g32 ? stack_kernel<__half, __half, true> : stack_kernel<__half, __half, false>;
-  else
-    kern = g32 ? stack_kernel<__nv_bfloat16, __nv_bfloat16, true>
-               : stack_kernel<__nv_bfloat16, __nv_bfloat16, false>;
+  using H16 = __half;
+  using B16 = __nv_bfloat16;
+  if (act_dtype == DUPLEX_DTYPE_F16) {
+    if (T == 1)
+      kern = g32 ? stack_kernel<H16, H16, true, 1> : stack_kernel<H16, H16, false, 1>;
+    else
+      kern = g32 ? stack_kernel<H16, H16, true, 0> : stack_kernel<H16, H16, false, 0>;
+  } else {
+    if (T == 1)
+      kern = g32 ? stack_kernel<B16, B16, true, 1> : stack_kernel<B16, B16, false, 1>;
+    else
+      kern = g32 ? stack_kernel<B16, B16, true, 0> : stack_kernel<B16, B16, false, 0>;
+  }
   int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), (int)kMax);
   if (rc) return rc;
-  int occ = 0;
-  rc = record_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem));
-  if (rc) return rc;
-  if (occ < 1) return DUPLEX_ERR_UNSUPPORTED;
-  rc = record_cuda(cudaMemsetAsync(ws + L.barrier, 0, 256, st));
-  if (rc) return rc;
+  // clusters of kCS CTAs, as many as can be resident at once: the grid barrier needs
+  // every CTA running.  (No cooperative attribute: it adds only an up-front check,
+  // and the profiler cannot launch cluster kernels with it.  A CTA that cannot start
+  // in time -- another kernel holding SMs -- makes the barrier give up with
+  // DUPLEX_DEVERR_TIMEOUT; it never hangs.)
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kCS;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(G);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  cfg.gridDim = dim3(kCS * kMaxClusters);
+  int nclusters = 0;
+  rc = record_cuda(cudaOccupancyMaxActiveClusters(&nclusters, kern, &cfg));
+  if (rc) return rc;
+  if (nclusters < 1) return DUPLEX_ERR_UNSUPPORTED;
+  if (nclusters > kMaxClusters) nclusters = kMaxClusters;
+  cfg.gridDim = dim3(kCS * nclusters);
+  rc = record_cuda(cudaMemsetAsync(ws + L.barrier, 0, 256, st));
+  if (rc) return rc;
   return record_cuda(cudaLaunchKernelEx(&cfg, kern, p));
 }

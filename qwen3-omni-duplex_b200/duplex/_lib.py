@@ -89,7 +89,15 @@ _SIGNATURES = {
                                       ctypes.POINTER(ctypes.c_size_t)], _c_int),
     "duplex_stack_forward": ([_c_ptr, _c_i32, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_int, _c_int,
                               _c_int, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
-                              _c_i32, _c_i32, _c_f32, _c_ptr, _c_size, _c_ptr, _c_ptr], _c_int),
+                              _c_i32, _c_i32, _c_f32, _c_ptr, _c_size, _c_i64, _c_i32, _c_ptr,
+                              _c_ptr], _c_int),
+    "duplex_gate_records_bytes": ([_c_i32, _c_i32, ctypes.POINTER(ctypes.c_size_t)], _c_int),
+    "duplex_repack_gate_records": ([_c_ptr, _c_int, _c_i32, _c_i32, _c_ptr, _c_size, _c_ptr],
+                                   _c_int),
+    "duplex_down_slices_bytes": ([_c_i32, _c_i32, _c_i32, _c_i32, _c_int,
+                                  ctypes.POINTER(ctypes.c_size_t)], _c_int),
+    "duplex_repack_down_slices": ([_c_ptr, _c_ptr, _c_ptr, _c_int, _c_i32, _c_i32, _c_i32, _c_i32,
+                                   _c_ptr, _c_size, _c_ptr], _c_int),
 }
 
 

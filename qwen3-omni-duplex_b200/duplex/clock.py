@@ -83,13 +83,16 @@ class Persistent:
         self.args = (has_attn, moe_residual, T, H, E, I, top_k, norm, qkv_R, q_dim, group,
                      has_zeros, _lib.dtype_code(dtype), float(rms_eps))
 
-    def run(self, x, out):
+    def run(self, x, out, wait_limit_cycles=0, test_flags=0):
+        """Enqueue the launch for x [T, H] -> out.  wait_limit_cycles / test_flags are the
+        C entry point's (0: waits bounded at about 2 s; bit 0 of test_flags: the first
+        grid barrier cannot complete, for the timeout test)."""
         (has_attn, moe_res, T, H, E, I, top_k, norm, qkv_R, q_dim, group, hz, code,
          eps) = self.args
         _lib.call("duplex_stack_forward", _lib.ptr(self.desc), self.n, has_attn, moe_res,
                   _lib.ptr(x), _lib.ptr(out), code, code, hz, T, H, E, I, top_k, norm, qkv_R,
-                  q_dim, group, eps, _lib.ptr(self.ws), self.ws.numel(), _lib.ptr(self.err),
-                  _lib.stream_of(x))
+                  q_dim, group, eps, _lib.ptr(self.ws), self.ws.numel(), int(wait_limit_cycles),
+                  int(test_flags), _lib.ptr(self.err), _lib.stream_of(x))
         return out
 
     def device_errors(self) -> int:
@@ -98,13 +101,34 @@ class Persistent:
         return v
 
 
+def gate_records(moe: FusedPackedMoE) -> torch.Tensor:
+    """The router's gate matrix as the persistent kernel's gate records (built once,
+    kept on the module)."""
+    rec = getattr(moe, "_gate_records", None)
+    w = moe.gate.weight
+    if rec is None or rec[1] != (w.data_ptr(), w._version):
+        E, H = w.shape
+        n = _lib.ctypes.c_size_t()
+        _lib.call("duplex_gate_records_bytes", E, H, _lib.ctypes.byref(n))
+        buf = torch.empty(n.value, dtype=torch.uint8, device=w.device)
+        src = _lib.aligned(w.detach())
+        _lib.call("duplex_repack_gate_records", _lib.ptr(src), _lib.dtype_code(src.dtype), E, H,
+                  _lib.ptr(buf), buf.numel(), _lib.stream_of(src))
+        rec = (buf, (w.data_ptr(), w._version))
+        moe._gate_records = rec
+    return rec[0]
+
+
 def _moe_desc(moe: FusedPackedMoE, qkv=None, o=None):
+    if moe.dn_slices is None:
+        raise _lib.DuplexError("the persistent stack needs the down K-slices: build the MoE "
+                               "with stack=True (group 32, 64 or 128, dims multiples of 128)")
     g = moe.gate
     return _lib.StackLayer(
         qkv_tiles=None if qkv is None else qkv.tiles.buf.data_ptr(),
         o_tiles=None if o is None else o.tiles.buf.data_ptr(),
-        gate_w=g.weight.data_ptr(), gate_b=None if g.bias is None else g.bias.data_ptr(),
-        gu_tiles=moe.gu_tiles.buf.data_ptr(), dn_tiles=moe.dn_tiles.buf.data_ptr())
+        gate_w=gate_records(moe).data_ptr(), gate_b=None if g.bias is None else g.bias.data_ptr(),
+        gu_tiles=moe.gu_tiles.buf.data_ptr(), dn_tiles=moe.dn_slices.buf.data_ptr())
 
 
 class MoEChain:
@@ -168,7 +192,7 @@ class ClockStack:
             moe = FusedPackedMoE.from_stacked(m["gate_w"], m["gu_packed"], m["gu_scale"],
                                               m["dn_packed"], m["dn_scale"], top_k,
                                               gu_zeros=m["gu_zeros"], dn_zeros=m["dn_zeros"],
-                                              dtype=dtype, device=device)
+                                              dtype=dtype, device=device, stack=fused)
             layers.append(ClockLayer(qkv, o, moe))
         return cls(layers, H, q, T, device=device, dtype=dtype, fused=fused)
 
@@ -189,7 +213,7 @@ class ClockStack:
                                               t(d["dn_packed"]), t(d["dn_scale"]), top_k,
                                               gu_zeros=t(d.get("gu_zeros")),
                                               dn_zeros=t(d.get("dn_zeros")), dtype=dtype,
-                                              device=device)
+                                              device=device, stack=True)
             layers.append(ClockLayer(qkv, o, moe))
         H = arrays[0]["gate_w"].shape[1]
         return cls(layers, H, None, T, device=device, dtype=dtype, fused=fused)

@@ -34,8 +34,8 @@ import torch
 import torch.nn as nn
 
 from duplex import _lib
-from duplex.streaming.triton_dequant_gemv import (HAVE_TRITON, Int4Tiles, TcRecords,  # noqa: F401
-                                                  dequant_gemv)
+from duplex.streaming.triton_dequant_gemv import (HAVE_TRITON, DownSlices, Int4Tiles,  # noqa: F401
+                                                  TcRecords, dequant_gemv)
 
 NUM_BITS = 4
 PACK = 32 // NUM_BITS
@@ -77,13 +77,15 @@ class FusedPackedMoE(nn.Module):
     """SparseMoeBlock replacement for int4-packed experts, on the B200 kernels."""
 
     def __init__(self, block: nn.Module = None, dtype=torch.bfloat16, device="cuda",
-                 host_resident: bool = False, cpu_compute: bool = False, tc: bool = False):
+                 host_resident: bool = False, cpu_compute: bool = False, tc: bool = False,
+                 stack: bool = False):
         super().__init__()
         if dtype not in (torch.float16, torch.bfloat16):
             raise _lib.DuplexError("FusedPackedMoE on B200 runs fp16 or bf16 modules")
         self.host_resident = host_resident      # recorded; all weights stay in HBM
         self.cpu_compute = cpu_compute and host_resident
         self.pdl = True
+        self.stack = stack                      # also build the down K-slices (clock-path stack)
         self.tc = tc                            # also build tensor-core records (batched decode,
                                                 # a second copy of the experts; opt-in)
         if block is None:                       # filled by from_stacked()
@@ -107,9 +109,9 @@ class FusedPackedMoE(nn.Module):
     @classmethod
     def from_stacked(cls, gate_weight, gu_packed, gu_scale, dn_packed, dn_scale, top_k,
                      gu_zeros=None, dn_zeros=None, norm_topk_prob=True, gate_bias=None,
-                     dtype=torch.float16, device="cuda", tc=False):
+                     dtype=torch.float16, device="cuda", tc=False, stack=False):
         """Build from raw stacked tensors ([E,2I,H/8], [E,2I,G], [E,H,I/8], [E,H,G'])."""
-        m = cls(None, dtype=dtype, device=device, tc=tc)
+        m = cls(None, dtype=dtype, device=device, tc=tc, stack=stack)
         E, H = gate_weight.shape
         m.num_experts, m.top_k, m.norm_topk_prob = E, top_k, norm_topk_prob
         m.gate = nn.Linear(H, E, bias=gate_bias is not None).to(device=device, dtype=dtype)
@@ -138,6 +140,11 @@ class FusedPackedMoE(nn.Module):
             raise _lib.DuplexError("gate|up and down must both have or both lack zero points")
         self.gu_tiles = Int4Tiles(gu_p, gu_s, gu_z, group=self.group, K=hidden, pair_halves=True)
         self.dn_tiles = Int4Tiles(dp, ds, dz, group=self.group, K=inter_in)
+        # the down projection as K-slice records for the persistent clock-path kernel
+        # (a second copy of the down weights; opt-in)
+        self.dn_slices = None
+        if self.stack and DownSlices.supported(gu_p.shape[0], hid_out, inter_in, self.group):
+            self.dn_slices = DownSlices(dp, ds, dz, group=self.group)
         # tensor-core records for batched decode (a second copy of the experts, in the
         # layout of the tcgen05 kernels), where the geometry allows them
         E = gu_p.shape[0]

@@ -144,6 +144,37 @@ class TcRecords:
         return self.buf.numel()
 
 
+class DownSlices:
+    """The down projection of a stacked expert set [E, H, I/8] (+ scales [E, H, I/group],
+    zero points) as K-slice records for the persistent clock-path kernel: one record per
+    (expert, 128-column slice of I, 16 rows of H), tile-record layout with K = 128,
+    16-byte padded (duplex_repack_down_slices).  Groups of 32, 64 or 128."""
+
+    def __init__(self, packed, scale, zeros=None, group=None):
+        _lib.require_cuda(packed, scale, zeros)
+        E, H, NW = packed.shape
+        I = NW * 8
+        group = int(group if group is not None else -(-I // scale.shape[-1]))
+        self.E, self.H, self.I, self.group = E, H, I, group
+        self.has_zeros = zeros is not None
+        scale = _lib.aligned(_kernel_scale(scale))
+        self.scale_dtype = scale.dtype
+        n = _lib.ctypes.c_size_t()
+        _lib.call("duplex_down_slices_bytes", E, H, I, group, 1 if self.has_zeros else 0,
+                  _lib.ctypes.byref(n))
+        self.buf = torch.empty(n.value, dtype=torch.uint8, device=packed.device)
+        p = _lib.aligned(packed.to(torch.int32))
+        z = None if zeros is None else _lib.aligned(zeros.to(torch.int32))
+        _lib.call("duplex_repack_down_slices", _lib.ptr(p), _lib.ptr(scale), _lib.ptr(z),
+                  _lib.dtype_code(scale.dtype), E, H, I, group, _lib.ptr(self.buf),
+                  self.buf.numel(), _lib.stream_of(p))
+
+    @staticmethod
+    def supported(E, H, I, group) -> bool:
+        n = _lib.ctypes.c_size_t()
+        return _lib.load().duplex_down_slices_bytes(E, H, I, group, 0, _lib.ctypes.byref(n)) == 0
+
+
 _TILE_CACHE: collections.OrderedDict = collections.OrderedDict()
 _TILE_CACHE_MAX = 16
 
