@@ -1,30 +1,41 @@
 """Benchmark: int4 MoE + dequant-GEMV decode on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
 
-Workload (the clock path): every int4 linear of Thinker
-layers 0-23 for one decode token -- fused q|k|v (2048 -> 5120), o (4096 -> 2048)
-and the 128-expert top-8 MoE (router, gate|up 2048 -> 2x768, down 768 -> 2048),
-group 128 with 4-bit zero points, fp16 activations, seeded synthetic weights.
-A step is one token through the 24 layers (one CUDA-graph replay, 120 kernels).
-The step's working set (~720 MB) is larger than the 126 MB L2, so every step
-streams its weights from HBM.
+Headline workload ("decode tok/s at 1/2/4/8 GPUs"): a 48-layer
+Thinker MoE stack for 256 concurrent decode streams, the 128 experts of every layer
+split evenly over the N GPUs (one process per GPU, NCCL): per layer each rank routes
+its 256/N streams, one all-to-all dispatches every token to the ranks that hold its
+experts, the rank's experts run as grouped int4 kernels, one all-to-all returns the
+partial sums to the token's owner, which adds them.  A step is every stream through
+the 48 layers (each layer on the same input: the attention blocks between them are
+outside this config), one CUDA graph per rank.  Seeded synthetic weights in the
+config-0 distributions (int4 group 128 with zero points, fp16).  value = 256 * steps /
+max-over-ranks time; the per-GPU working set (314/N MB of experts per layer x 48) is
+far larger than the 126 MB L2.
 
-Reported: tokens/s (value), us/layer, the decode-MoE layer (config 0 geometry)
-timed alone over 24 distinct layers as the roofline unit, the end-to-end figure
-through `ClockStack.decode()` with pinned host buffers, the CPU oracle timed on a
-bounded sample, and SM clocks sampled around the timed region.  With --gpus N
-(torchrun) every rank runs an independent replica (the batch-1 clock path does
-not shard); value is the sum, time is the max over ranks.
+Beside it, on every rank (reported from the max over ranks):
+  roofline  the decode MoE layer of config 0 (batch 1: router, top-8 of 128, gate|up,
+            SiLU, down, combine) timed inside the persistent kernel over 24 distinct
+            layers (MoEChain): algorithmic bytes per layer / time, against the measured
+            HBM copy bandwidth; DRAM traffic per layer from the committed ncu summary;
+  clock     config 2: the int4 linears of Thinker layers 0-23 for one token (fused
+            q|k|v, o, MoE), one launch of the persistent kernel per token;
+  e2e       the headline through the module's forward with pinned host buffers: H2D of
+            the step's tokens, the 48 layers, D2H of the last layer's output;
+  cpu_baseline  (rank 0, N = 1) the oracle (numpy restatement of the reference's
+            dequant + gather-bmm) on two layer samples of the same workload.
 
---workload ep runs BASELINE config 4 instead (duplex/ep_bench.py: 48 MoE layers, 256
-streams, experts split over the N GPUs); it prints its own line. --workload batched
-runs config 3 (duplex/batched_bench.py: --streams streams through one MoE layer, one
-GPU, router logits ~N(0,1)).
+--workload clock | batched | gemv select the other configs' lines (clock: config 2 as
+the headline; batched: config 3, duplex/batched_bench.py; gemv: config 1,
+duplex/gemv_bench.py).
 
---impl reference times the reference algorithm on the host cores (the numpy port
-of the reference's torch dequant + gather-bmm path, oracle/), one of the 24
-layers per step.
+--impl reference times the reference algorithm on the host cores for the headline
+workload: rank 0 alone (other ranks exit), each step one of the 48 layers for all 256
+streams through the oracle's by-expert restatement of the reference's gather-bmm
+(fused_packed_moe.py:265-275), so ms_per_step is the real time of a step;
+tokens/s = 256 / (48 x ms_per_step).
 """
 
 from __future__ import annotations
@@ -32,6 +43,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import socket
 import sys
 import time
 from pathlib import Path
@@ -41,12 +53,11 @@ for _p in (str(ROOT), str(ROOT / "qwen3-omni-duplex_b200")):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
-METRIC = ("int4 MoE+GEMV µs/layer @batch1, % HBM peak; decode tok/s at 1/2/4/8 GPUs")
-N_LAYERS = 24
+METRIC = "int4 MoE+GEMV µs/layer @batch1, % HBM peak; decode tok/s at 1/2/4/8 GPUs"
+EP_LAYERS, EP_STREAMS = 48, 256
+CLOCK_LAYERS = 24
 HIDDEN = 2048
-# DRAM bytes (read + write) per MoE layer of the roofline unit, from one ncu capture of
-# the 24-layer MoE-chain launch (profiles/moe_chain_dram_24layers.md)
-MOE_LAYER_DRAM_BYTES = 20_302_560
+TRAFFIC = ROOT / "profiles" / "traffic.txt"
 
 
 def peaks():
@@ -57,79 +68,87 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def config_block(n_gpus, batch=1):
-    return {
-        "workload": "config 2 clock path: int4 linears of Thinker layers 0-23 (fused qkv, o, "
-                    "router + 128-expert top-8 MoE), one decode token",
-        "layers": N_LAYERS, "hidden": HIDDEN, "experts": 128, "top_k": 8, "moe_inter": 768,
-        "q_heads": 32, "kv_heads": 4, "head_dim": 128, "group": 128, "zero_points": True,
-        "batch": batch, "activations": "fp16",
-        "parallelism": "replicas" if n_gpus == 1 else f"{n_gpus} replicas (batch-1 decode)",
-        "l2": "no flush: each step streams ~720 MB of distinct weights (> 126 MB L2)",
-    }
+def traffic(key):
+    """A figure of the committed ncu summary profiles/traffic.txt (key = value lines)."""
+    if TRAFFIC.exists():
+        for line in TRAFFIC.read_text().splitlines():
+            k, _, v = line.partition("=")
+            if k.strip() == key:
+                return float(v.split()[0])
+    return None
+
+
+def ep_config(n):
+    return {"workload": "config 4: 48-layer Thinker MoE stack, 256 decode streams, the 128 "
+                        f"experts of every layer split over {n} GPU(s); all-to-all dispatch "
+                        "and combine over NCCL",
+            "layers": EP_LAYERS, "streams": EP_STREAMS, "streams_per_gpu": EP_STREAMS // n,
+            "experts": 128, "experts_per_gpu": 128 // n, "top_k": 8, "hidden": HIDDEN,
+            "moe_inter": 768, "group": 128, "zero_points": True, "activations": "fp16",
+            "parallelism": f"ep{n}", "graph": "one CUDA graph per rank per step",
+            "l2": "no flush: a step streams 48 x 314/N MB of distinct experts (> 126 MB L2)"}
 
 
 # ------------------------------------------------------------------ CPU (oracle) arms
-def cpu_layer_sample(seed=5):
-    """One full-geometry clock-path layer as numpy arrays (same distributions)."""
-    import numpy as np
+def cpu_layer_sample(seed=5, T=EP_STREAMS):
     from duplex import synth
-    rng = np.random.Generator(np.random.PCG64(seed))
-    qkv = synth.linear_np(rng, 5120, HIDDEN, 128, True)
-    o = synth.linear_np(rng, HIDDEN, 4096, 128, True)
-    m = synth.moe_layer_np(seed=seed + 1, T=1)
-    d = dict(qkv_packed=qkv["packed"], qkv_scale=qkv["scale"], qkv_zeros=qkv["zeros"],
-             o_packed=o["packed"], o_scale=o["scale"], o_zeros=o["zeros"])
-    for k in ("gate_w", "gu_packed", "gu_scale", "gu_zeros", "dn_packed", "dn_scale", "dn_zeros"):
-        d[k] = m[k]
-    return d, m["x"].astype(np.float32)
+    return synth.moe_layer_np(seed=seed, T=T)
 
 
-def time_cpu_layers(n_samples, n_warm=1):
-    from oracle.clock_oracle import clock_layer
-    threads = os.cpu_count() or 1
-    d, h = cpu_layer_sample()
-    for _ in range(n_warm):
-        clock_layer(h, d, 8, threads=threads)
-    ts = []
-    for _ in range(n_samples):
-        t0 = time.perf_counter()
-        clock_layer(h, d, 8, threads=threads)
-        ts.append(time.perf_counter() - t0)
-    return ts, threads
+def time_cpu_layer(L):
+    """One layer of the headline workload through the oracle: routing and the by-expert
+    gather-bmm restatement for all streams.  Returns seconds."""
+    import numpy as np
+    import oracle as O
+    x = L["x"].astype(np.float32)
+    t0 = time.perf_counter()
+    w, sel, _ = O.router(x, L["gate_w"], 8, True, None, "float16")
+    O.moe_experts_by_expert(x, sel, w, L["gu_packed"], L["gu_scale"], L["dn_packed"],
+                            L["dn_scale"], L["gu_zeros"], L["dn_zeros"])
+    return time.perf_counter() - t0
 
 
-def cpu_baseline_block(n_samples=3):
-    ts, threads = time_cpu_layers(n_samples)
-    t_layer = sorted(ts)[len(ts) // 2]
-    return {"value": 1.0 / (N_LAYERS * t_layer), "unit": "tokens/s", "cores": threads,
+def cpu_threads():
+    try:
+        import torch
+        return torch.get_num_threads()
+    except Exception:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
+def cpu_baseline_block(n_samples=2):
+    L = cpu_layer_sample()
+    ts = [time_cpu_layer(L) for _ in range(n_samples)]
+    t = sorted(ts)[len(ts) // 2]
+    return {"value": EP_STREAMS / (EP_LAYERS * t), "unit": "tokens/s", "cores": cpu_threads(),
             "kind": "port",
-            "sample": f"{n_samples} of the 24 layers (median {t_layer * 1e3:.0f} ms/layer), "
-                      "numpy port of the reference's dequant + gather-bmm path, experts on a "
-                      f"{threads}-thread pool; tokens/s = 1/(24 x t_layer)"}
+            "sample": f"{n_samples} samples of one layer x 256 streams (median {t:.2f} s), numpy "
+                      "restatement of the reference's dequant + gather-bmm (oracle/); "
+                      "tokens/s = 256 / (48 x t_layer)"}
 
 
 def run_reference(args):
-    ws, rank, _ = (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0)
+    ws, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    steps, warm = max(1, args.steps), max(0, args.warmup)
-    # keep the whole run to a few minutes: at most 20 timed layer samples
-    steps_eff = min(steps, 20)
-    ts, threads = time_cpu_layers(steps_eff, n_warm=min(warm, 2))
-    t_layer = sum(ts) / len(ts)
-    value = 1.0 / (N_LAYERS * t_layer)
+    K, W = max(1, args.steps), max(0, args.warmup)
+    L = cpu_layer_sample()
+    for _ in range(W):
+        time_cpu_layer(L)
+    ts = [time_cpu_layer(L) for _ in range(K)]
+    t = sum(ts) / len(ts)
+    value = EP_STREAMS / (EP_LAYERS * t)
+    sample = ("each step: one of the 48 layers for all 256 streams (routing + by-expert "
+              "gather-bmm), numpy restatement of the reference's torch path (oracle/); "
+              "tokens/s = 256 / (48 x ms_per_step)")
     line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": steps, "warmup": warm, "ms_per_step": N_LAYERS * t_layer * 1e3,
-        "us_per_layer": t_layer * 1e6,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int4 x f32 (numpy port, fp16-rounded activations)",
-        "data": "synthetic (seeded)", "config": config_block(args.gpus), "impl": "reference",
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"{steps_eff} timed layer samples (1 of 24 layers per step) "
-                                   "of the numpy port of the reference's torch dequant + "
-                                   "gather-bmm path"},
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": K,
+        "warmup": W, "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int4 x f32 (numpy port, fp16-rounded activations)",
+        "data": "synthetic (seeded)", "config": ep_config(ws), "impl": "reference",
+        "step_unit": "one layer of the 48 (all 256 streams)",
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cpu_threads(),
+                         "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -137,121 +156,171 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------ GPU arm
-def run_ours(args):
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def init_group(local):
+    """NCCL group of the torchrun ranks (a group of one without torchrun)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    if "WORLD_SIZE" not in os.environ:
+        os.environ.update(WORLD_SIZE="1", RANK="0", LOCAL_RANK="0", MASTER_ADDR="127.0.0.1",
+                          MASTER_PORT=str(_free_port()))
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=180))
+    return dist
+
+
+def time_graph(g, K, dev, pre=None):
+    """CUDA-event time of K replays (max over ranks), ms total."""
     import torch
     from duplex import benchutil as bu
-    from duplex.clock import ClockStack, moe_bytes
-
-    n_gpus = args.gpus
-    ws, rank, local = bu.dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if ws > 1:
-        bu.init_dist("nccl")
-    K, W = args.steps, max(3, args.warmup)
-
-    stack = ClockStack.synthetic(n_layers=N_LAYERS, seed=1234 + rank, device=dev)
-    pool = torch.randn(64, 1, HIDDEN, device=dev, dtype=torch.float16,
-                       generator=torch.Generator(device=dev).manual_seed(77 + rank))
-    stack.capture()
-
-    def step(i):
-        stack.x_in.copy_(pool[i % 64])
-        stack.replay()
-
-    for i in range(W):
-        step(i)
     torch.cuda.synchronize(dev)
-
-    # clocks: sampled over a soak of the same loop bracketing the timed steps
-    sampler = bu.ClockSampler(bu.visible_gpu_indices(max(1, ws))).start() if rank == 0 else None
-    t_soak = time.perf_counter()
-    i = 0
-    while time.perf_counter() - t_soak < args.soak:
-        step(i)
-        i += 1
-        if i % 64 == 0:
-            torch.cuda.synchronize(dev)
-    torch.cuda.synchronize(dev)
-
     bu.barrier()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(K):
-        step(i)
+        if pre:
+            pre(i)
+        g.replay()
     e1.record()
     torch.cuda.synchronize(dev)
     bu.barrier()
-    ms = bu.max_over_ranks(e0.elapsed_time(e1), dev)
-    ms_step = ms / K
-    value = ws * K / (ms / 1e3)
+    return bu.max_over_ranks(e0.elapsed_time(e1), dev)
 
-    # end to end through the public decode() call, host buffers
-    xh = torch.randn(64, 1, HIDDEN, dtype=torch.float16).pin_memory()
-    oh = torch.empty(64, 1, HIDDEN, dtype=torch.float16).pin_memory()
-    for i in range(W):
-        stack.decode(xh[i % 64], oh[i % 64])
+
+def capture(fn, dev):
+    import torch
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        fn()
+    torch.cuda.synchronize(dev)
+    return g
+
+
+def run_ours(args):
+    import torch
+    from duplex import benchutil as bu, synth
+    from duplex.streaming.ep_moe import ExpertParallelMoE
+
+    _, _, local = bu.dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = init_group(local)
+    ws, rank = dist.get_world_size(), dist.get_rank()
+    if EP_STREAMS % ws or 128 % ws:
+        raise SystemExit(f"{ws} GPUs do not split 256 streams / 128 experts")
+    K, W = args.steps, max(3, args.warmup)
+    T_l = EP_STREAMS // ws
+
+    # ---------------------------------------------------------------- config 4
+    layers = []
+    for li in range(EP_LAYERS):
+        gen = torch.Generator(device=dev).manual_seed(1000 + li)  # identical on every rank
+        m = synth.moe_layer_torch(gen, device=dev)
+        layers.append(ExpertParallelMoE(m["gate_w"], m["gu_packed"], m["gu_scale"], m["dn_packed"],
+                                        m["dn_scale"], synth.THINKER_ACTIVE, gu_zeros=m["gu_zeros"],
+                                        dn_zeros=m["dn_zeros"], dtype=torch.float16, device=dev))
+        del m
+    torch.cuda.empty_cache()
+    gen = torch.Generator(device=dev).manual_seed(7 + rank)
+    x = torch.randn(T_l, HIDDEN, device=dev, dtype=torch.float16, generator=gen)
+    outs = [None] * EP_LAYERS
+
+    def step():
+        for li, L in enumerate(layers):
+            outs[li] = L(x)
+
+    g = capture(step, dev)
+    for _ in range(W):
+        g.replay()
+    # clocks sampled around a soak of the same loop and the timed region
+    sampler = bu.ClockSampler(bu.visible_gpu_indices(ws)).start() if rank == 0 else None
+    t_soak = time.perf_counter()
+    while time.perf_counter() - t_soak < args.soak:
+        g.replay()
+        torch.cuda.synchronize(dev)
+    ms = time_graph(g, K, dev)
+    ms_step = ms / K
+    value = EP_STREAMS * K / (ms / 1e3)
+    derr = sum(L.device_errors() for L in layers)
+
+    # per-GPU bytes of the selected local experts per layer (HBM roofline of the stage)
+    per_expert = (layers[0].gu_tiles.buf.numel() + layers[0].dn_tiles.buf.numel()) / layers[0].E_local
+    x_all = torch.empty(ws * T_l, HIDDEN, dtype=x.dtype, device=dev)
+    dist.all_gather_into_tensor(x_all, x)
+    _, sel = layers[0].route(x_all)
+    loc = sel[(sel >= layers[0].e_begin) & (sel < layers[0].e_begin + layers[0].E_local)]
+    ep_bytes = int(torch.unique(loc).numel()) * per_expert
+
+    # end to end through the module: pinned host tokens in, last layer's output out
+    xh = torch.randn(T_l, HIDDEN, dtype=torch.float16).pin_memory()
+    oh = torch.empty(T_l, HIDDEN, dtype=torch.float16).pin_memory()
+
     torch.cuda.synchronize(dev)
     bu.barrier()
-    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(K):
-        stack.decode(xh[i % 64], oh[i % 64])
+        x.copy_(xh, non_blocking=True)
+        g.replay()
+        oh.copy_(outs[-1], non_blocking=True)
     e1.record()
     torch.cuda.synchronize(dev)
     bu.barrier()
     ms_e2e = bu.max_over_ranks(e0.elapsed_time(e1), dev)
-    e2e_value = ws * K / (ms_e2e / 1e3)
+    e2e_value = EP_STREAMS * K / (ms_e2e / 1e3)
+    clocks = sampler.stop().summary() if sampler else None
+    del g
+    layers.clear()
+    outs = None
+    torch.cuda.empty_cache()
 
-    # roofline unit: the decode MoE layer (router, top-k, gate|up, down, combine) of
-    # config 0, timed over the 24 distinct MoE layers of the stack in one persistent
-    # launch: x -> MoE(rms(x)) layer after layer
-    from duplex.clock import MoEChain
-    moes = [L.moe for L in stack.layers]
+    # ---------------------------------------------------------------- configs 2 and 0
+    from duplex.clock import ClockStack, MoEChain, moe_bytes
+    stack = ClockStack.synthetic(n_layers=CLOCK_LAYERS, seed=1234 + rank, device=dev)
+    pool = torch.randn(64, 1, HIDDEN, device=dev, dtype=torch.float16,
+                       generator=torch.Generator(device=dev).manual_seed(77 + rank))
+    gc = stack.capture()
+    for i in range(W):
+        stack.x_in.copy_(pool[i % 64])
+        gc.replay()
+    ms_c = time_graph(gc, K, dev, pre=lambda i: stack.x_in.copy_(pool[i % 64]))
+    clock = {"value": K / (ms_c / 1e3), "unit": "tokens/s per GPU",
+             "us_per_layer": ms_c * 1e3 / (K * CLOCK_LAYERS),
+             "workload": "config 2: int4 linears of Thinker layers 0-23 (fused q|k|v, o, "
+                         "router + 128-expert top-8 MoE), one decode token, one launch",
+             "bytes_per_token": stack.bytes_per_step()}
+    moes = [Lc.moe for Lc in stack.layers]
     chain = MoEChain(moes, rms_eps=1e-6, residual=False)
     hx = torch.zeros(1, HIDDEN, device=dev, dtype=torch.float16)
     hout = torch.zeros(1, HIDDEN, device=dev, dtype=torch.float16)
-
-    def moe_chain():
-        chain.forward_into(hx, hout)
-
-    moe_chain()
-    torch.cuda.synchronize(dev)
-    s = torch.cuda.Stream(dev)
-    s.wait_stream(torch.cuda.current_stream(dev))
-    gm = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(s):
-        with torch.cuda.graph(gm, stream=s):
-            moe_chain()
-    torch.cuda.current_stream(dev).wait_stream(s)
+    gm = capture(lambda: chain.forward_into(hx, hout), dev)
     for i in range(W):
         hx.copy_(pool[i % 64])
         gm.replay()
-    torch.cuda.synchronize(dev)
-    bu.barrier()
-    torch.cuda.synchronize(dev)
     Km = max(K, 50)
-    e0.record()
-    for i in range(Km):
-        hx.copy_(pool[i % 64])
-        gm.replay()
-    e1.record()
-    torch.cuda.synchronize(dev)
-    bu.barrier()
-    ms_moe = bu.max_over_ranks(e0.elapsed_time(e1), dev)
-    us_moe = ms_moe * 1e3 / (Km * N_LAYERS)
+    ms_m = time_graph(gm, Km, dev, pre=lambda i: hx.copy_(pool[i % 64]))
+    us_moe = ms_m * 1e3 / (Km * CLOCK_LAYERS)
     mb = moe_bytes(moes[0])
-
-    # drain the soak sampler after a short tail of load
-    t_tail = time.perf_counter()
-    i = 0
-    while time.perf_counter() - t_tail < 0.3:
-        step(i)
-        i += 1
-    torch.cuda.synchronize(dev)
-    clocks = sampler.stop().summary() if sampler else None
-    errors = stack.device_errors()
+    derr += stack.device_errors() + chain.p.device_errors()
+    del gm, gc
+    stack.graph = None
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -259,65 +328,69 @@ def run_ours(args):
 
     peak, peak_kind = peaks()
     achieved = mb / (us_moe * 1e-6) / 1e9
-    bytes_step = stack.bytes_per_step()
+    us_layer = ms_step * 1e3 / EP_LAYERS
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": K,
-        "warmup": W, "ms_per_step": ms_step, "us_per_layer": ms_step * 1e3 / N_LAYERS,
+        "warmup": W, "ms_per_step": ms_step, "us_per_layer": us_layer,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int4 weights x f16 activations, f32 accumulate",
         "data": "synthetic (seeded; BASELINE config distributions)",
-        "config": config_block(ws),
-        "step_hbm": {"bytes": bytes_step, "GBps": bytes_step / (ms_step * 1e-3) / 1e9,
-                     "frac": bytes_step / (ms_step * 1e-3) / 1e9 / peak},
+        "config": ep_config(ws),
+        "ep_hbm": {"bytes_per_layer_per_gpu": ep_bytes,
+                   "GBps": ep_bytes / (us_layer * 1e3), "frac": ep_bytes / (us_layer * 1e3) / peak,
+                   "note": "bytes of the selected local experts (tile records) per layer per GPU"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": MOE_LAYER_DRAM_BYTES,
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
-                                       "24-layer MoE-chain launch / 24 "
-                                       "(profiles/moe_chain_dram_24layers.md)",
-                     "kernel": "decode MoE layer (router, top-k, gate|up, down, combine) in the "
-                               "persistent stack kernel, config 0 geometry, batch 1, 24 distinct "
-                               "layers per launch",
+                     "frac": achieved / peak, "traffic": traffic("moe_layer_dram_bytes"),
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a "
+                                       "4-layer MoE-chain launch / 4 (profiles/traffic.txt)",
+                     "kernel": "decode MoE layer (config 0: router, top-8 of 128, gate|up, "
+                               "down, combine), batch 1, inside the persistent clustered stack "
+                               "kernel over 24 distinct layers",
                      "us_per_launch": us_moe, "algorithmic_bytes": mb,
                      "peak_kind": f"{peak_kind} (copy bandwidth, MEASURED_PEAKS.json)"},
+        "clock": clock,
         "cpu_baseline": cpu,
-        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": HIDDEN * 2,
-                "d2h_bytes_per_step": HIDDEN * 2},
-        "gpu_launches": stack.kernels_per_step() * K,
+        "e2e": {"value": e2e_value, "unit": "tokens/s",
+                "h2d_bytes_per_step": T_l * HIDDEN * 2, "d2h_bytes_per_step": T_l * HIDDEN * 2},
+        "gpu_launches": 8 * EP_LAYERS * K,
+        "gpu_launches_note": "per layer: router, top-k, dispatch pack, bucketing, gate|up, down, "
+                             "expert combine, rank combine (+ 2 NCCL all-to-alls)",
         "clocks": clocks,
-        "device_errors": errors,
+        "device_errors": derr,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del gm
-    stack.graph = None
-    if ws > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--soak", type=float, default=1.0, help="seconds of load before timing")
-    ap.add_argument("--cpu-samples", type=int, default=3)
+    ap.add_argument("--cpu-samples", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["clock", "ep", "batched"], default="clock",
-                    help="clock: config 2 (default line); ep: config 4, the expert-parallel "
-                         "48-layer MoE stack at 256 streams (duplex/ep_bench.py); batched: "
-                         "config 3, --streams streams through one MoE layer on one GPU "
-                         "(duplex/batched_bench.py)")
+    ap.add_argument("--workload", choices=["ep", "clock", "batched", "gemv"], default="ep",
+                    help="ep: config 4, the default line (see the module docstring); clock: "
+                         "config 2 as the line (duplex/clock_bench.py); batched: config 3 "
+                         "(duplex/batched_bench.py); gemv: config 1 (duplex/gemv_bench.py)")
     ap.add_argument("--streams", type=int, default=256, help="batched: concurrent streams")
     args = ap.parse_args()
-    if args.workload == "ep" and args.impl == "ours":
-        from duplex import ep_bench
-        raise SystemExit(ep_bench.main(["--steps", str(args.steps), "--warmup", str(args.warmup)]))
     if args.workload == "batched" and args.impl == "ours":
         from duplex import batched_bench
         raise SystemExit(batched_bench.main(["--streams", str(args.streams), "--steps", str(args.steps),
                                              "--warmup", str(args.warmup)]))
+    if args.workload == "gemv":
+        from duplex import gemv_bench
+        raise SystemExit(gemv_bench.main(["--steps", str(args.steps), "--warmup", str(args.warmup),
+                                          "--impl", args.impl]))
+    if args.workload == "clock":
+        from duplex import clock_bench
+        raise SystemExit(clock_bench.main(["--steps", str(args.steps), "--warmup", str(args.warmup),
+                                           "--impl", args.impl]))
     if args.impl == "reference":
         run_reference(args)
     else:

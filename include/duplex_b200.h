@@ -242,6 +242,28 @@ int duplex_moe_experts_grouped(const void* x, int act_dtype, int32_t T, int64_t 
                                void* stream);
 
 /*
+ * ep_dispatch_pack / ep_combine -- the two device steps around the expert-parallel
+ * all-to-alls (no counterpart in the reference, which keeps every expert on one GPU,
+ * fused_packed_moe.py:165-169; the expert stage between them is
+ * duplex_moe_experts_grouped).  n_ranks ranks, E / n_ranks experts each.
+ * dispatch_pack: rows [T][row_bytes] are this rank's exchange rows (duplex_moe_route_grouped
+ * with pack: the token, its top_k expert ids (int32) at ids_offset, its top_k weights
+ * (fp32) right after); for every rank d, the rows of the tokens that selected one of d's
+ * experts go, compacted in token order, to block d of send ([n_ranks][T][row_bytes]);
+ * rows of a block past its count get the first expert id of rank d + 1 (mod n_ranks) and
+ * weight 0, which d's expert stage skips.  slot_of[d][t] = token t's row in block d, -1
+ * when t was not sent to d.  T <= 512, row_bytes % 16 == 0.
+ * ep_combine: out[t] = sum over d = 0 .. n_ranks - 1 of partials[d][slot_of[d][t]] (fp32
+ * rows [n_ranks][T][H], as the second all-to-all returns them) (+ residual[t]), one
+ * rounding to act_dtype.  H % 4 == 0.
+ */
+int duplex_ep_dispatch_pack(const void* rows, int64_t row_bytes, int32_t T, int32_t top_k,
+                            int32_t E, int32_t n_ranks, int64_t ids_offset, void* send,
+                            int32_t* slot_of, void* stream);
+int duplex_ep_combine(const float* partials, const int32_t* slot_of, int32_t T, int32_t n_ranks,
+                      int32_t H, const void* residual, void* out, int act_dtype, void* stream);
+
+/*
  * Tensor-core (tcgen05) variants of the grouped path -- same computation, arguments,
  * limits and error behaviour as duplex_moe_grouped / duplex_moe_experts_grouped, with
  * the experts in "tensor-core records" instead of tile records, and these limits: group

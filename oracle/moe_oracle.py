@@ -22,6 +22,8 @@ means zero == 8 everywhere, which reproduces the reference bit-exactly.
 
 from __future__ import annotations
 
+from concurrent.futures import ThreadPoolExecutor
+
 import numpy as np
 
 __all__ = [
@@ -231,11 +233,13 @@ def moe_experts(x, sel, w, gu_packed, gu_scale, dn_packed, dn_scale,
 
 
 def moe_experts_by_expert(x, sel, w, gu_packed, gu_scale, dn_packed, dn_scale,
-                          gu_zeros=None, dn_zeros=None):
+                          gu_zeros=None, dn_zeros=None, threads=1):
     """`moe_experts` in fp32 with one dequantisation per selected expert, shared by every
     token that selects it (the reference's per-token loop of fused_packed_moe.py:265-275,
     reordered so that batches of hundreds of tokens finish in seconds).  Same values up
-    to fp32 summation order: each token's slots are added in ascending expert order."""
+    to fp32 summation order: each token's slots are added in ascending expert order.
+    `threads` > 1 computes the experts on a thread pool (numpy releases the GIL in its
+    kernels); their outputs are still added in ascending expert order."""
     x = np.asarray(x, dtype=np.float32)
     sel = np.asarray(sel)
     w = np.asarray(w, dtype=np.float32)
@@ -243,7 +247,8 @@ def moe_experts_by_expert(x, sel, w, gu_packed, gu_scale, dn_packed, dn_scale,
     I = gu_packed.shape[-2] // 2
     Ki = dn_packed.shape[-1] * PACK
     out = np.zeros((T, dn_packed.shape[-2]), dtype=np.float32)
-    for e in np.unique(sel):
+
+    def one(e):
         t_idx, j_idx = np.nonzero(sel == e)
         gz = None if gu_zeros is None else gu_zeros[e]
         dz = None if dn_zeros is None else dn_zeros[e]
@@ -252,8 +257,16 @@ def moe_experts_by_expert(x, sel, w, gu_packed, gu_scale, dn_packed, dn_scale,
         g, u = h[:, :I], h[:, I:]
         act = (g / (np.float32(1.0) + np.exp(-g))) * u
         dn = dequant(dn_packed[e], np.asarray(dn_scale[e], np.float32), Ki, dz, "float32")
-        y = act[:, :Ki] @ dn.T                                       # [n, H]
-        np.add.at(out, t_idx, y * w[t_idx, j_idx][:, None])  # a token may list e twice
+        return t_idx, (act[:, :Ki] @ dn.T) * w[t_idx, j_idx][:, None]   # [n, H]
+
+    experts = np.unique(sel)
+    if threads > 1:
+        with ThreadPoolExecutor(threads) as pool:
+            results = list(pool.map(one, experts))
+    else:
+        results = [one(e) for e in experts]
+    for t_idx, y in results:
+        np.add.at(out, t_idx, y)  # a token may list e twice
     return out
 
 

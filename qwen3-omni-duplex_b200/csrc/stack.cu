@@ -1150,8 +1150,11 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
       int i = 0;  // stage sequence number
       RingPos wp = {0, 0u};
       bool ok = true;
-      // one stage of one or two copies of `bytes` each, side by side in the slot
-      auto issue2 = [&](const uint8_t* src0, const uint8_t* src1, uint32_t bytes) {
+      // one stage of one or two copies of `bytes` each, side by side in the slot; weights
+      // read once carry the evict-first hint, the gate records (read by every cluster)
+      // stay in L2 for the other clusters
+      auto issue2 = [&](const uint8_t* src0, const uint8_t* src1, uint32_t bytes,
+                        bool keep = false) {
         if (i >= NS)  // the slot's previous stage has been released by every consumer warp
           wait_phase(&empty[wp.slot], wp.phase ^ 1u, abort_flag, p.err, kSiteEmpty, plimit);
         if (*abort_flag) {
@@ -1160,13 +1163,18 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
         }
         uint8_t* dst = smem + p.off_ring + (uint32_t)wp.slot * p.slot_bytes;
         mbar_arrive_expect_tx(&full[wp.slot], src1 ? 2u * bytes : bytes);
-        bulk_g2s_stream(dst, src0, bytes, &full[wp.slot], pol);
+        if (keep)
+          bulk_g2s(dst, src0, bytes, &full[wp.slot]);
+        else
+          bulk_g2s_stream(dst, src0, bytes, &full[wp.slot], pol);
         if (src1) bulk_g2s_stream(dst + bytes, src1, bytes, &full[wp.slot], pol);
         mbar_arrive(&full[wp.slot]);
         ++i;
         wp.next(NS);
       };
-      auto issue = [&](const uint8_t* src, uint32_t bytes) { issue2(src, nullptr, bytes); };
+      auto issue = [&](const uint8_t* src, uint32_t bytes, bool keep = false) {
+        issue2(src, nullptr, bytes, keep);
+      };
       for (int l = 0; l < p.n_layers && ok; ++l) {
         const duplex_stack_layer L = p.layers[l];
         if (p.has_attn) {
@@ -1182,7 +1190,7 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
             const int nks = (p.KS - k * p.kps) < p.kps ? (p.KS - k * p.kps) : p.kps;
             issue(reinterpret_cast<const uint8_t*>(L.gate_w) +
                       ((size_t)b * p.KS + (size_t)k * p.kps) * 512u,
-                  (uint32_t)nks * 512u);
+                  (uint32_t)nks * 512u, true);
           }
         if (!ok) break;
         // routing plan of this layer (built by this CTA's consumers)

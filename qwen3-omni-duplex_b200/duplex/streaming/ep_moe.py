@@ -3,22 +3,26 @@ process group (one process per GPU), tokens data-parallel.
 
 The reference runs every expert on one GPU (`src/duplex/streaming/fused_packed_moe.py`);
 this is the multi-GPU form of the same layer, `FusedPackedMoE.forward` semantics per
-token, for batched decode (many streams per rank):
+token, for batched decode (many streams per rank).  Per layer on every rank:
 
   1. route the rank's own tokens over all E experts (router logits, fp32 softmax,
      top-k, renormalise: `duplex_moe_route_grouped`), whose top-k kernel writes each
-     token's exchange row (the token, its expert ids, its weights);
-  2. exchange: one all-gather of those rows, so that every rank sees every token that
-     may pick one of its experts (the expert stage reads the gathered rows in place);
-  3. the rank's experts [rank * E/N, (rank + 1) * E/N) on all gathered tokens, one fp32
-     partial sum per token over the slots that hit them (`duplex_moe_experts_grouped`);
-  4. exchange back: reduce-scatter (sum) of the fp32 partials, so each token's owner
-     receives the sum over ranks; then + residual, one rounding to the activation type.
+     token's exchange row (the token, its k expert ids, its k weights);
+  2. dispatch: for every rank d, the rows of the tokens that picked one of d's experts,
+     compacted into block d of a send buffer (`duplex_ep_dispatch_pack`), then ONE NCCL
+     all-to-all: rank d receives, from every rank, the tokens that need its experts;
+  3. the rank's experts [rank * E/N, (rank + 1) * E/N) on the received rows, one fp32
+     partial sum per row over the slots that hit them (`duplex_moe_experts_grouped`);
+  4. combine: ONE NCCL all-to-all sends every partial row back to the token's owner,
+     which adds the partials in rank order (+ residual), one rounding to the activation
+     type (`duplex_ep_combine`).
 
-Both exchanges are NCCL collectives of fixed size (N * T_local rows), so no host
-synchronisation is needed and the layer can be captured in a CUDA graph.  The host
-logic lives in `ep_forward`, which takes the routing and expert steps as callables: the
-module passes the sm_100a kernels; the multi-rank CPU tests pass the numpy oracle.
+Each block of the send buffers holds up to T_local rows (a token can need every rank),
+so both all-to-alls have a fixed size: no host synchronisation, and a 48-layer step is
+one CUDA graph.  The rows of a block past its count carry an expert id of another rank
+and weight 0, which the receiving expert stage skips.  The host logic lives in
+`ep_forward`, which takes the device steps as callables: the module passes the sm_100a
+kernels; the multi-rank CPU tests pass torch / numpy restatements of the same steps.
 """
 
 from __future__ import annotations
@@ -38,33 +42,47 @@ def exchange_row_bytes(H: int, elt: int, top_k: int) -> int:
     return -(-(H * elt + 8 * top_k) // 16) * 16
 
 
-def ep_forward(x, route_fn, experts_fn, top_k: int, group=None, residual=None, out_dtype=None):
+def ep_forward(x, route_fn, pack_fn, experts_fn, combine_fn, top_k: int, group=None,
+               residual=None, bufs=None):
     """Host side of one expert-parallel layer on this rank.
 
-    x [T_local, H]; route_fn(x, pack) fills pack [T_local, row] uint8 with each token's
-    exchange row (the token's 2 H bytes, its k expert ids as int32, its k weights as
-    fp32); experts_fn(x_all, sel_all, w_all) -> fp32 [N * T_local, H]: this rank's
-    experts' weighted sum per gathered token (zero where none of its experts is
-    selected).  x_all, sel_all and w_all are row-strided views of the gathered rows.
-    Returns [T_local, H] in out_dtype (default x.dtype).
+    x [T_local, H].  route_fn(x, rows) fills rows [T_local, row] uint8 with each token's
+    exchange row (the token's H * elt bytes, its k expert ids as int32, its k weights as
+    fp32); pack_fn(rows, send, slot_of) fills send [N, T_local, row] and slot_of
+    [N, T_local] int32 (dispatch_pack); experts_fn(x_all, sel_all, w_all) -> fp32
+    [N * T_local, H], this rank's experts' weighted sum per received row (row-strided
+    views of the received rows); combine_fn(back [N, T_local, H] fp32, slot_of,
+    residual) -> [T_local, H], the layer output.  bufs: optional dict of preallocated
+    buffers (rows, send, slot_of, recv, back), reused across calls of the same shape.
     """
     world = dist.get_world_size(group)
     T_l, H = x.shape
     xbytes = H * x.element_size()
     row = exchange_row_bytes(H, x.element_size(), top_k)
-    pack = torch.empty(T_l, row, dtype=torch.uint8, device=x.device)
-    route_fn(x, pack)
-    pall = torch.empty(world * T_l, row, dtype=torch.uint8, device=x.device)
-    dist.all_gather_into_tensor(pall, pack, group=group)
-    x_all = pall[:, :xbytes].view(x.dtype)
-    sel_all = pall[:, xbytes:xbytes + 4 * top_k].view(torch.int32)
-    w_all = pall[:, xbytes + 4 * top_k:xbytes + 8 * top_k].view(torch.float32)
-    partial = experts_fn(x_all, sel_all, w_all)
-    red = torch.empty(T_l, H, dtype=torch.float32, device=x.device)
-    dist.reduce_scatter_tensor(red, partial.contiguous(), op=dist.ReduceOp.SUM, group=group)
-    if residual is not None:
-        red += residual.to(torch.float32)
-    return red.to(out_dtype or x.dtype)
+    dev = x.device
+    b = bufs if bufs is not None else {}
+    if "rows" not in b:
+        b["rows"] = torch.empty(T_l, row, dtype=torch.uint8, device=dev)
+        b["send"] = torch.empty(world, T_l, row, dtype=torch.uint8, device=dev)
+        b["slot_of"] = torch.empty(world, T_l, dtype=torch.int32, device=dev)
+        if world > 1:
+            b["recv"] = torch.empty(world, T_l, row, dtype=torch.uint8, device=dev)
+            b["back"] = torch.empty(world, T_l, H, dtype=torch.float32, device=dev)
+    route_fn(x, b["rows"])
+    pack_fn(b["rows"], b["send"], b["slot_of"])
+    # an all-to-all over one rank is the identity: read the send buffer in place
+    recv = b["send"] if world == 1 else b["recv"]
+    if world > 1:
+        dist.all_to_all_single(recv, b["send"], group=group)
+    rv = recv.view(world * T_l, row)
+    x_all = rv[:, :xbytes].view(x.dtype)
+    sel_all = rv[:, xbytes:xbytes + 4 * top_k].view(torch.int32)
+    w_all = rv[:, xbytes + 4 * top_k:xbytes + 8 * top_k].view(torch.float32)
+    partial = experts_fn(x_all, sel_all, w_all).view(world, T_l, H)
+    back = partial if world == 1 else b["back"]
+    if world > 1:
+        dist.all_to_all_single(back, partial, group=group)
+    return combine_fn(back, b["slot_of"], residual)
 
 
 class ExpertParallelMoE(nn.Module):
@@ -74,7 +92,7 @@ class ExpertParallelMoE(nn.Module):
     [E, H], gate|up packed [E, 2I, H/8] + scales [E, 2I, G] (+ zeros), down packed
     [E, H, I/8] + scales [E, H, G'] (+ zeros)); every rank keeps the router and its own
     E/N experts (repacked once into tile records).  forward(x [T_local, H]) returns the
-    layer output for this rank's tokens; N * T_local <= 512.
+    layer output for this rank's tokens; N * T_local <= 512 (the received rows).
     """
 
     def __init__(self, gate_weight, gu_packed, gu_scale, dn_packed, dn_scale, top_k,
@@ -168,11 +186,37 @@ class ExpertParallelMoE(nn.Module):
                   _lib.stream_of(x_all))
         return out
 
+    def pack(self, rows, send, slot_of):
+        """Dispatch: rows of this rank's tokens into the per-rank blocks of `send`."""
+        T = rows.shape[0]
+        xbytes = self.hidden * self.gate.weight.element_size()
+        _lib.call("duplex_ep_dispatch_pack", _lib.ptr(rows), rows.stride(0), T, self.top_k,
+                  self.num_experts, self.world, xbytes, _lib.ptr(send), _lib.ptr(slot_of),
+                  _lib.stream_of(rows))
+
+    def combine(self, back, slot_of, residual=None, out=None):
+        """Layer output of this rank's tokens from the partial rows returned by every rank."""
+        N, T, H = back.shape
+        dt = self.gate.weight.dtype
+        out = out if out is not None else torch.empty(T, H, dtype=dt, device=back.device)
+        res = None if residual is None else _lib.aligned(residual.to(dt))
+        _lib.call("duplex_ep_combine", _lib.ptr(back), _lib.ptr(slot_of), T, N, H, _lib.ptr(res),
+                  _lib.ptr(out), _lib.dtype_code(dt), _lib.stream_of(back))
+        return out
+
     def forward(self, x, residual=None):
+        """x [T_local, H] (this rank's tokens) -> [T_local, H]; every rank calls it with
+        the same T_local.  Buffers are kept per T_local (no allocation after the first
+        call of a shape, so a layer can be captured in a CUDA graph)."""
         _lib.require_cuda(x)
         x = _lib.aligned(x.to(self.gate.weight.dtype))
-        return ep_forward(x, lambda xt, pack: self.route(xt, pack), self.local_experts, self.top_k,
-                          self.group, residual)
+        T = x.shape[0]
+        if T > 512:
+            raise _lib.DuplexError("ExpertParallelMoE takes at most 512 tokens per rank")
+        bufs = self._ws.setdefault(("ep", T), {})
+        return ep_forward(x, lambda xt, rows: self.route(xt, rows), self.pack,
+                          self.local_experts, lambda back, slot_of, res: self.combine(back, slot_of, res),
+                          self.top_k, self.group, residual, bufs)
 
     def device_errors(self) -> int:
         v = int(self.err.item())

@@ -159,14 +159,23 @@ def _ep_rank(rank, world, port, q, T_l):
                            dtype=torch.float16, device=dev)
     x = T(x_full[rank * T_l:(rank + 1) * T_l], dev, torch.float16)
     y = ep(x)
+    y2 = ep(x)                      # second call: reused buffers, same bits
     torch.cuda.synchronize()
     full = FusedPackedMoE.from_stacked(*args, 8, gu_zeros=T(L["gu_zeros"], dev), dn_zeros=T(L["dn_zeros"], dev),
                                        dtype=torch.float16, device=dev)
     y_ref = torch.empty(world * T_l, 2048, dtype=torch.float16, device=dev)
-    full.forward_grouped_into(T(x_full, dev, torch.float16), y_ref)
+    w = torch.empty(world * T_l, 8, dtype=torch.float32, device=dev)
+    sel = torch.empty(world * T_l, 8, dtype=torch.int32, device=dev)
+    full.forward_grouped_into(T(x_full, dev, torch.float16), y_ref, w_out=w, sel_out=sel)
     torch.cuda.synchronize()
-    err = rel_err(y.float().cpu().numpy(), y_ref[rank * T_l:(rank + 1) * T_l].float().cpu().numpy())
-    q.put((rank, err, ep.device_errors()))
+    mine = slice(rank * T_l, (rank + 1) * T_l)
+    err = rel_err(y.float().cpu().numpy(), y_ref[mine].float().cpu().numpy())
+    # the oracle: the reference's gather-bmm restated, on the routing of the same tokens
+    ref = O.moe_experts_by_expert(x_full[mine], sel[mine].cpu().numpy(), w[mine].cpu().numpy(),
+                                  L["gu_packed"], L["gu_scale"], L["dn_packed"], L["dn_scale"],
+                                  L["gu_zeros"], L["dn_zeros"])
+    oerr = rel_err(y.float().cpu().numpy(), ref)
+    q.put((rank, err, ep.device_errors(), oerr, bool(torch.equal(y, y2))))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -186,15 +195,53 @@ def _run_ranks(world, T_l):
     return res
 
 
-def test_expert_parallel_module_one_rank(cuda):
-    """NCCL group of one: the module's exchange degenerates to copies; the output equals
-    the single-GPU grouped layer within the fp32 summation-order bar."""
-    for rank, err, derr in _run_ranks(1, 64):
-        assert err <= 1e-3 and derr == 0
+@pytest.mark.parametrize("T_l", [64, 256])
+def test_expert_parallel_module_one_rank(cuda, T_l):
+    """NCCL group of one: the all-to-alls degenerate to copies; the output equals the
+    single-GPU grouped layer (fp32 summation-order bar) and the oracle (2e-3)."""
+    for rank, err, derr, oerr, same in _run_ranks(1, T_l):
+        assert err <= 1e-3 and oerr <= TOL and derr == 0 and same
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_expert_parallel_module_two_ranks(cuda):
-    """Two GPUs, 64 experts each, 32 streams per rank (no multicast loads anywhere)."""
-    for rank, err, derr in _run_ranks(2, 32):
-        assert err <= 1e-3 and derr == 0
+    """Two GPUs, 64 experts each, 32 streams per rank, dispatch / combine all-to-alls over
+    NCCL (no multicast loads anywhere), against the oracle."""
+    for rank, err, derr, oerr, same in _run_ranks(2, 32):
+        assert err <= 1e-3 and oerr <= TOL and derr == 0 and same
+
+
+@pytest.mark.parametrize("N", [1, 2, 4, 8])
+def test_dispatch_pack_and_combine_kernels(cuda, N):
+    """duplex_ep_dispatch_pack / duplex_ep_combine against their torch restatements:
+    rows, slots and padding bit for bit; the combine within fp32 order (same order)."""
+    from ep_ref import combine_ref, dispatch_pack_ref
+    from duplex.streaming.ep_moe import exchange_row_bytes
+    E, H, k, T_l = 128, 2048, 8, 48
+    rng = np.random.default_rng(N)
+    row = exchange_row_bytes(H, 2, k)
+    rows = torch.from_numpy(rng.integers(0, 255, (T_l, row), dtype=np.uint8))
+    ids = np.stack([rng.choice(E, k, replace=False) for _ in range(T_l)]).astype(np.int32)
+    rows[:, 2 * H:2 * H + 4 * k] = torch.from_numpy(ids).view(torch.uint8)
+    rows[:, 2 * H + 4 * k:2 * H + 8 * k] = torch.from_numpy(
+        rng.random((T_l, k), dtype=np.float32)).view(torch.uint8)
+    send_ref = torch.zeros(N, T_l, row, dtype=torch.uint8)
+    slot_ref = torch.empty(N, T_l, dtype=torch.int32)
+    dispatch_pack_ref(rows, send_ref, slot_ref, k, E, N, 2 * H)
+    rows_d = rows.to(cuda)
+    send = torch.zeros(N, T_l, row, dtype=torch.uint8, device=cuda)
+    slot = torch.empty(N, T_l, dtype=torch.int32, device=cuda)
+    _lib.call("duplex_ep_dispatch_pack", _lib.ptr(rows_d), row, T_l, k, E, N, 2 * H, _lib.ptr(send),
+              _lib.ptr(slot), _lib.stream_of(rows_d))
+    torch.cuda.synchronize()
+    assert torch.equal(slot.cpu(), slot_ref)
+    assert torch.equal(send.cpu(), send_ref)          # padding rows included
+    back = torch.from_numpy(rng.standard_normal((N, T_l, H)).astype(np.float32))
+    res = torch.from_numpy(rng.standard_normal((T_l, H)).astype(np.float16))
+    out = torch.empty(T_l, H, dtype=torch.float16, device=cuda)
+    back_d, res_d = back.to(cuda), res.to(cuda)   # held until the kernel has run
+    _lib.call("duplex_ep_combine", _lib.ptr(back_d), _lib.ptr(slot), T_l, N, H,
+              _lib.ptr(res_d), _lib.ptr(out), _lib.DTYPE_F16, _lib.stream_of(out))
+    torch.cuda.synchronize()
+    ref = combine_ref(back, slot_ref, res.float()).to(torch.float16)
+    assert torch.equal(out.cpu(), ref)

@@ -59,6 +59,7 @@ def _ep_worker(rank, ws, port, q):
     import oracle as O
     from duplex import synth
     from duplex.streaming.ep_moe import ep_forward
+    from ep_ref import combine_ref, dispatch_pack_ref
 
     dist.init_process_group("gloo", rank=rank, world_size=ws)
     E, H, I, k, T_l = 8, 64, 64, 3, 5
@@ -82,7 +83,8 @@ def _ep_worker(rank, ws, port, q):
                                     L["dn_packed"], L["dn_scale"], L["gu_zeros"], L["dn_zeros"])
         return torch.from_numpy(y)
 
-    out = ep_forward(x, route_fn, experts_fn, k, residual=res, out_dtype=torch.float32)
+    out = ep_forward(x, route_fn, lambda r, s, so: dispatch_pack_ref(r, s, so, k, E, ws, 4 * H),
+                     experts_fn, lambda b, so, r: combine_ref(b, so, r), k, residual=res)
     w_ref, sel_ref, _ = O.router(x_full, L["gate_w"], k, True, None, "float32")
     ref = O.moe_experts_by_expert(x_full, sel_ref, w_ref, L["gu_packed"], L["gu_scale"],
                                   L["dn_packed"], L["dn_scale"], L["gu_zeros"], L["dn_zeros"])
@@ -93,8 +95,9 @@ def _ep_worker(rank, ws, port, q):
 
 
 def test_expert_parallel_host_logic_gloo():
-    """Two ranks, four experts each: gathered routing, local experts, reduce-scatter of
-    the partial sums give each rank the single-process layer output for its tokens."""
+    """Two ranks, four experts each: routing, dispatch all-to-all of the rows that need
+    each rank's experts, local experts, combine all-to-all of the partial rows, give each
+    rank the single-process layer output for its tokens."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
