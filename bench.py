@@ -43,7 +43,6 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import socket
 import sys
 import time
 from pathlib import Path
@@ -143,7 +142,7 @@ def run_reference(args):
               "tokens/s = 256 / (48 x ms_per_step)")
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": K,
-        "warmup": W, "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
+        "warmup": W, "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int4 x f32 (numpy port, fp16-rounded activations)",
         "data": "synthetic (seeded)", "config": ep_config(ws), "impl": "reference",
         "step_unit": "one layer of the 48 (all 256 streams)",
@@ -156,26 +155,13 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------ GPU arm
-def _free_port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
-
-
 def init_group(local):
-    """NCCL group of the torchrun ranks (a group of one without torchrun)."""
-    import datetime
-
+    """NCCL group of the torchrun ranks (a group of one without torchrun), with a
+    non-blocking communicator and a 180 s collective timeout (duplex.benchutil)."""
     import torch
     import torch.distributed as dist
-    if "WORLD_SIZE" not in os.environ:
-        os.environ.update(WORLD_SIZE="1", RANK="0", LOCAL_RANK="0", MASTER_ADDR="127.0.0.1",
-                          MASTER_PORT=str(_free_port()))
-    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-    dev = torch.device("cuda", local)
-    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=180))
+    from duplex import benchutil as bu
+    bu.init_nccl(torch.device("cuda", local), timeout_s=180)
     return dist
 
 
@@ -332,7 +318,7 @@ def run_ours(args):
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": K,
         "warmup": W, "ms_per_step": ms_step, "us_per_layer": us_layer,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "int4 weights x f16 activations, f32 accumulate",
         "data": "synthetic (seeded; BASELINE config distributions)",
         "config": ep_config(ws),

@@ -283,6 +283,67 @@ __global__ void __launch_bounds__(kThreads, 1) dq_gemv_kernel(const __grid_const
   const int npairs = tg.npairs;
   const int ips = p.nrec * npairs;  // items per stage
 
+  if (MODE == kLinear && CORR) {
+    // Dense linear over many tiles per CTA (q, o, lm_head): each warp's partial sums of
+    // up to `rmax` tiles wait in `red` ([tile][warp][column][row]); one consumer barrier
+    // and one pass then reduce them (warps in order) and write the rows.  The ring
+    // position advances stage by stage.
+    const int per = p.ncols * 16;
+    int rmax = (kCW * 8 * 32) / (kCW * per);
+    if (rmax > kConsumers / per) rmax = kConsumers / per;
+    const int lo = (warp * ips) / kCW, hi = ((warp + 1) * ips) / kCW;
+    int slot = 0;
+    uint32_t phase = 0u;
+    int j = 0, t0 = blockIdx.x;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+      if (!mbar_wait_bounded(&full[slot], phase, abort_flag)) {
+        if (lane == 0) set_error(p.err, DUPLEX_DEVERR_TIMEOUT);
+      }
+      const uint8_t* st = smem + p.smem_stage0 + (uint32_t)slot * p.stage_bytes;
+      float acc0[4] = {0.f, 0.f, 0.f, 0.f};
+      float acc1[4] = {0.f, 0.f, 0.f, 0.f};
+      consume_corr<T, S, G32>(st, tg, lo, hi, lane, xsh, p.x_pitch, corr, xon, acc0, acc1);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (++slot == NS) {
+        slot = 0;
+        phase ^= 1u;
+      }
+      float* b = red + (j * kCW + warp) * per;
+      if (2 * t < p.ncols) {
+        b[(2 * t) * 16 + g] = acc0[0];
+        b[(2 * t) * 16 + g + 8] = acc0[2];
+      }
+      if (2 * t + 1 < p.ncols) {
+        b[(2 * t + 1) * 16 + g] = acc0[1];
+        b[(2 * t + 1) * 16 + g + 8] = acc0[3];
+      }
+      if (++j == rmax || tile + (int)gridDim.x >= ntiles) {
+        named_bar_sync(1, kConsumers);
+        for (int o = tid; o < j * per; o += kConsumers) {
+          const int jj = o / per, rem = o - jj * per;
+          float v = 0.f;
+#pragma unroll
+          for (int w = 0; w < kCW; ++w) v += red[(jj * kCW + w) * per + rem];
+          const int n = rem >> 4, row = (t0 + jj * (int)gridDim.x) * 16 + (rem & 15);
+          if (row < p.R) {
+            T y = from_f32<T>(v);
+            if (p.bias)
+              y = from_f32<T>(to_f32<T>(y) + to_f32<T>(reinterpret_cast<const T*>(p.bias)[row]));
+            if (p.residual)
+              y = from_f32<T>(to_f32<T>(y) + to_f32<T>(reinterpret_cast<const T*>(
+                                                  p.residual)[n * p.res_col_stride + row]));
+            reinterpret_cast<T*>(p.out)[n * p.out_col_stride + row] = y;
+          }
+        }
+        named_bar_sync(1, kConsumers);
+        j = 0;
+        t0 = tile + (int)gridDim.x;
+      }
+    }
+    return;
+  }
+
   int i = 0;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     float acc0[4] = {0.f, 0.f, 0.f, 0.f};

@@ -20,6 +20,8 @@ ROOT = PKG.parent                      # qwen3-omni-duplex_b200/
 CSRC = ROOT / "csrc"
 INCLUDE = ROOT.parent / "include"
 LIB = PKG / "libduplex_b200.so"
+TORCH_OPS_SRC = CSRC / "torch_ops.cpp"
+TORCH_OPS_LIB = PKG / "libduplex_torch_ops.so"
 ARCH = "-gencode=arch=compute_100a,code=sm_100a"
 
 
@@ -79,6 +81,30 @@ def build(force: bool = False, verbose: bool = False, lib: Path = LIB) -> Path:
     return lib
 
 
+def build_torch_ops(force: bool = False, lib: Path = TORCH_OPS_LIB) -> Path:
+    """The TORCH_LIBRARY(duplex_b200) ops (csrc/torch_ops.cpp) against torch's headers,
+    linked to libduplex_b200.so (found next to it at run time)."""
+    if (not force and lib.exists() and lib.stat().st_mtime > TORCH_OPS_SRC.stat().st_mtime
+            and lib.stat().st_mtime > LIB.stat().st_mtime):
+        return lib
+    import torch
+    from torch.utils import cpp_extension as ce
+    abi = int(torch.compiled_with_cxx11_abi())
+    cuda_inc = Path(nvcc_path()).resolve().parent.parent / "include"
+    cmd = ["g++", "-O2", "-std=c++17", "-shared", "-fPIC", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           str(TORCH_OPS_SRC), f"-I{INCLUDE}", f"-I{cuda_inc}"]
+    cmd += [f"-I{p}" for p in ce.include_paths()]
+    cmd += [f"-L{p}" for p in ce.library_paths()]
+    cmd += ["-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", f"-L{PKG}", "-lduplex_b200",
+            "-Wl,-rpath,$ORIGIN", "-o", str(lib.with_suffix(".so.tmp"))]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("g++ failed on torch_ops.cpp:\n" + r.stdout + r.stderr)
+    os.replace(lib.with_suffix(".so.tmp"), lib)
+    return lib
+
+
 if __name__ == "__main__":
     build(force="--force" in sys.argv, verbose="-v" in sys.argv)
+    build_torch_ops(force="--force" in sys.argv)
     print(LIB)

@@ -135,6 +135,23 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
     return lib
 
 
+_torch_ops_loaded = False
+
+
+def load_torch_ops():
+    """Register the TORCH_LIBRARY(duplex_b200) ops (libduplex_torch_ops.so, in-tree):
+    afterwards torch.ops.duplex_b200.<op> call the same C entry points."""
+    global _torch_ops_loaded
+    if not _torch_ops_loaded:
+        load()
+        p = _PKG / "libduplex_torch_ops.so"
+        if not p.exists():
+            raise RuntimeError(f"duplex_b200: {p} not found; build it with duplex._build")
+        torch.ops.load_library(str(p))
+        _torch_ops_loaded = True
+    return torch.ops.duplex_b200
+
+
 def exported_symbols() -> list[str]:
     return list(_SIGNATURES)
 

@@ -27,6 +27,29 @@ def init_dist(backend: str, timeout_s: int = 120):
     return ws, rank
 
 
+def init_nccl(device, timeout_s: int = 180):
+    """NCCL process group of the torchrun ranks with a NON-BLOCKING communicator: NCCL
+    calls return at once and report errors asynchronously; torch's watchdog polls them
+    (ncclCommGetAsyncError) and aborts the communicator when a collective exceeds
+    `timeout_s`, so a rank that dies makes the others' next collective fail instead of
+    hanging.  A group of one when not launched by torchrun."""
+    import socket
+    if "WORLD_SIZE" not in os.environ:
+        s = socket.socket()
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+        s.close()
+        os.environ.update(WORLD_SIZE="1", RANK="0", LOCAL_RANK="0", MASTER_ADDR="127.0.0.1",
+                          MASTER_PORT=str(port))
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "1")
+    opts = dist.ProcessGroupNCCL.Options()
+    opts.config.blocking = 0
+    dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=timeout_s),
+                            pg_options=opts)
+    return dist.get_world_size(), dist.get_rank()
+
+
 def barrier():
     if dist.is_available() and dist.is_initialized():
         dist.barrier()

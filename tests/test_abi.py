@@ -160,3 +160,16 @@ def test_python_wrappers_refuse_cpu_tensors():
     with pytest.raises(_lib.DuplexError):
         dequant_gemv(torch.zeros(64, dtype=torch.float16), torch.zeros(1, 16, 8, dtype=torch.int32),
                      torch.ones(1, 16, 2, dtype=torch.float16), torch.zeros(1, dtype=torch.int32))
+
+
+def test_torch_library_ops_are_registered():
+    """TORCH_LIBRARY(duplex_b200) registers every op (schemas only; no GPU call)."""
+    from duplex import _build
+    _build.build_torch_ops()
+    ops = _lib.load_torch_ops()
+    import torch
+    for name in ("unpack4", "dequant", "dequant_gemv", "packed_linear", "moe_forward",
+                 "moe_grouped", "ep_dispatch", "ep_combine"):
+        op = getattr(ops, name)
+        assert isinstance(op.default, torch._ops.OpOverload), name
+    assert "Tensor(a!) send" in str(ops.ep_dispatch.default._schema)

@@ -142,15 +142,14 @@ def _free_port():
 
 def _ep_rank(rank, world, port, q, T_l):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
-    import datetime
-
     import torch.distributed as dist
     from duplex.streaming.ep_moe import ExpertParallelMoE
     from duplex.streaming.fused_packed_moe import FusedPackedMoE
+    from duplex import benchutil as bu
     dev = torch.device("cuda", rank)
     torch.cuda.set_device(dev)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
-                            timeout=datetime.timedelta(seconds=60))
+    os.environ.update(WORLD_SIZE=str(world), RANK=str(rank), LOCAL_RANK=str(rank))
+    bu.init_nccl(dev, timeout_s=60)        # non-blocking communicator
     L = synth.moe_layer_np(seed=60, E=128, H=2048, I=768, top_k=8, group=128, zero_points=True,
                            T=world * T_l)
     x_full = O.round_to(L["x"].astype(np.float32), "float16")

@@ -111,3 +111,79 @@ def test_expert_parallel_host_logic_gloo():
     for rank, err, shape in res:
         assert shape == (5, 64)
         assert err < 1e-5, (rank, err)
+
+
+# ------------------------------------------------------------------ failure detection
+def _ep_leave_worker(rank, ws, port, q):
+    """Two ranks run one expert-parallel layer step; rank 1 then leaves (between steps,
+    nothing in flight).  Rank 0's next step must fail with an error within the process
+    group's timeout instead of hanging."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(ws),
+                      RANK=str(rank), LOCAL_RANK=str(rank))
+    import datetime
+    import time
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import oracle as O
+    from duplex import synth
+    from duplex.streaming.ep_moe import ep_forward
+    from ep_ref import combine_ref, dispatch_pack_ref
+
+    dist.init_process_group("gloo", rank=rank, world_size=ws, timeout=datetime.timedelta(seconds=5))
+    E, H, I, k, T_l = 8, 64, 64, 3, 4
+    L = synth.moe_layer_np(seed=22, E=E, H=H, I=I, top_k=k, group=64, zero_points=True, T=ws * T_l)
+    x = torch.from_numpy(L["x"][rank * T_l:(rank + 1) * T_l].astype(np.float32))
+    e0, e1 = rank * (E // ws), (rank + 1) * (E // ws)
+
+    def route_fn(xt, pack):
+        w, sel, _ = O.router(xt.numpy(), L["gate_w"], k, True, None, "float32")
+        xb = xt.contiguous().view(torch.uint8)
+        pack[:, :xb.shape[1]] = xb
+        pack[:, xb.shape[1]:xb.shape[1] + 4 * k] = torch.from_numpy(sel.astype(np.int32)).view(torch.uint8)
+        pack[:, xb.shape[1] + 4 * k:xb.shape[1] + 8 * k] = torch.from_numpy(w).view(torch.uint8)
+
+    def experts_fn(x_all, sel_all, w_all):
+        s = sel_all.numpy()
+        w = np.where((s >= e0) & (s < e1), w_all.numpy(), 0.0).astype(np.float32)
+        return torch.from_numpy(O.moe_experts_by_expert(
+            x_all.numpy(), s, w, L["gu_packed"], L["gu_scale"], L["dn_packed"], L["dn_scale"],
+            L["gu_zeros"], L["dn_zeros"]))
+
+    def step():
+        return ep_forward(x, route_fn, lambda r, s, so: dispatch_pack_ref(r, s, so, k, E, ws, 4 * H),
+                          experts_fn, lambda b, so, r: combine_ref(b, so, r), k)
+
+    step()
+    if rank == 1:
+        q.put((rank, "left", 0.0, ""))
+        q.close()
+        q.join_thread()           # flush the message before leaving
+        os._exit(0)               # leaves between steps, no destroy_process_group
+    time.sleep(0.5)
+    t0 = time.time()
+    try:
+        step()
+        q.put((rank, "no error", time.time() - t0, ""))
+    except Exception as e:       # the peer is gone: the collective fails
+        q.put((rank, "error", time.time() - t0, type(e).__name__))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_ep_rank_leaving_between_steps_fails_fast():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_ep_leave_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in ps)
+    for p in ps:
+        p.join(timeout=60)
+    assert res[1][1] == "left"
+    assert res[0][1] == "error", res[0]
+    assert res[0][2] < 30.0        # within the 5 s group timeout plus start-up slack
