@@ -115,15 +115,40 @@ def cpu_threads():
         return os.cpu_count() or 1
 
 
+def reference_torch_cpu():
+    """The reference's own torch FusedPackedMoE CPU path (baseline/_ref), one decode token
+    per forward as its serving loop feeds it, in its own process (duplex/ref_cpu_bench.py);
+    None when the reference is not installed."""
+    import subprocess
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "duplex" / "streaming" / "fused_packed_moe.py").exists():
+        return None
+    script = ROOT / "qwen3-omni-duplex_b200" / "duplex" / "ref_cpu_bench.py"
+    r = subprocess.run([sys.executable, str(script)], capture_output=True, text=True,
+                       env=dict(os.environ, PYTHONPATH=str(ref)), timeout=600)
+    if r.returncode != 0:
+        return {"unavailable": ((r.stderr or r.stdout).strip().splitlines() or ["?"])[-1][:200]}
+    d = json.loads(r.stdout.strip().splitlines()[-1])
+    t = d["s_per_token_layer"]
+    return {"value": 1.0 / (EP_LAYERS * t), "unit": "tokens/s", "cores": d["threads"],
+            "kind": "reference",
+            "sample": f"the reference's FusedPackedMoE.forward (torch gather-bmm branch, fp32, "
+                      f"HAVE_TRITON off) on one token of one Thinker-geometry layer, median of "
+                      f"{len(d['runs'])} ({t:.3f} s); tokens/s = 1 / (48 x t): it serves one "
+                      "token per forward"}
+
+
 def cpu_baseline_block(n_samples=2):
     L = cpu_layer_sample()
     ts = [time_cpu_layer(L) for _ in range(n_samples)]
     t = sorted(ts)[len(ts) // 2]
-    return {"value": EP_STREAMS / (EP_LAYERS * t), "unit": "tokens/s", "cores": cpu_threads(),
-            "kind": "port",
-            "sample": f"{n_samples} samples of one layer x 256 streams (median {t:.2f} s), numpy "
-                      "restatement of the reference's dequant + gather-bmm (oracle/); "
-                      "tokens/s = 256 / (48 x t_layer)"}
+    out = {"value": EP_STREAMS / (EP_LAYERS * t), "unit": "tokens/s", "cores": cpu_threads(),
+           "kind": "port",
+           "sample": f"{n_samples} samples of one layer x 256 streams (median {t:.2f} s), numpy "
+                     "restatement of the reference's dequant + gather-bmm (oracle/), by expert; "
+                     "tokens/s = 256 / (48 x t_layer)"}
+    out["reference_torch"] = reference_torch_cpu()
+    return out
 
 
 def run_reference(args):
@@ -193,7 +218,9 @@ def capture(fn, dev):
     torch.cuda.current_stream(dev).wait_stream(s)
     torch.cuda.synchronize(dev)
     g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=s):
+    # thread-local capture: CUDA calls of other threads (NCCL's, torch's watchdog) may
+    # run meanwhile without invalidating the capture
+    with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
         fn()
     torch.cuda.synchronize(dev)
     return g
@@ -338,9 +365,9 @@ def run_ours(args):
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "tokens/s",
                 "h2d_bytes_per_step": T_l * HIDDEN * 2, "d2h_bytes_per_step": T_l * HIDDEN * 2},
-        "gpu_launches": 8 * EP_LAYERS * K,
-        "gpu_launches_note": "per layer: router, top-k, dispatch pack, bucketing, gate|up, down, "
-                             "expert combine, rank combine (+ 2 NCCL all-to-alls)",
+        "gpu_launches": (8 if ws > 1 else 7) * EP_LAYERS * K,
+        "gpu_launches_note": "per layer: router, top-k, dispatch pack (N > 1), bucketing, gate|up, "
+                             "down, expert combine, rank combine (+ 2 NCCL all-to-alls at N > 1)",
         "clocks": clocks,
         "device_errors": derr,
     }

@@ -18,14 +18,20 @@ namespace duplex {
 int record_cuda(cudaError_t e);
 
 constexpr int kPackThreads = 512;
+constexpr int kPackChunk = 8;  // tokens whose rows one CTA copies
 
-// Block d = blockIdx.x.  T <= kPackThreads.
+// Grid (destination d, chunk c).  Every CTA ranks all T tokens for d (one thread per
+// token, ballot + warp-count scan: cheap, and the same in every CTA of d), then copies
+// the rows of tokens [c * kPackChunk, (c + 1) * kPackChunk) that go to d and writes the
+// padding rows of block d with positions in the same range, so the 1-4 MB of rows of
+// a layer are spread over n_ranks * T / kPackChunk CTAs.  T <= kPackThreads.
 __global__ void __launch_bounds__(kPackThreads) ep_pack_kernel(
     const uint8_t* __restrict__ rows, int64_t row_bytes, int T, int top_k, int E, int nranks,
     int64_t ids_off, uint8_t* __restrict__ send, int32_t* __restrict__ slot_of) {
   __shared__ int warp_count[kPackThreads / 32];
-  __shared__ int pos_s[kPackThreads];
-  const int d = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ int pos_s[kPackChunk];
+  const int d = blockIdx.x, c0 = blockIdx.y * kPackChunk;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int E_l = E / nranks, e0 = d * E_l, e1 = e0 + E_l;
   bool hit = false;
   if (tid < T) {
@@ -41,28 +47,33 @@ __global__ void __launch_bounds__(kPackThreads) ep_pack_kernel(
     total += warp_count[w];
   }
   const int pos = hit ? before + __popc(ballot & ((1u << lane) - 1u)) : -1;
-  pos_s[tid] = pos;
-  if (tid < T) slot_of[(int64_t)d * T + tid] = pos;
+  if (tid >= c0 && tid < c0 + kPackChunk && tid < T) {
+    pos_s[tid - c0] = pos;
+    slot_of[(int64_t)d * T + tid] = pos;
+  }
   __syncthreads();
-  // rows: one warp per row, 16-byte pieces (row_bytes % 16 == 0)
+  // this chunk's rows: kPackThreads / 32 / kPackChunk warps per row, 16-byte pieces
   uint8_t* blk = send + (int64_t)d * T * row_bytes;
   const int64_t q16 = row_bytes >> 4;
-  for (int t = warp; t < T; t += kPackThreads / 32) {
-    const int p = pos_s[t];
-    if (p < 0) continue;
-    const uint4* src = reinterpret_cast<const uint4*>(rows + (int64_t)t * row_bytes);
-    uint4* dst = reinterpret_cast<uint4*>(blk + (int64_t)p * row_bytes);
-    for (int64_t q = lane; q < q16; q += 32) dst[q] = src[q];
+  constexpr int kWpr = kPackThreads / 32 / kPackChunk;
+  {
+    const int i = warp / kWpr, t = c0 + i;
+    const int p = t < T ? pos_s[i] : -1;
+    if (p >= 0) {
+      const uint4* src = reinterpret_cast<const uint4*>(rows + (int64_t)t * row_bytes);
+      uint4* dst = reinterpret_cast<uint4*>(blk + (int64_t)p * row_bytes);
+      for (int64_t q = (warp % kWpr) * 32 + lane; q < q16; q += 32 * kWpr) dst[q] = src[q];
+    }
   }
-  // padding rows: an expert of the next rank (skipped by the receiver), weight 0
+  // padding rows with positions in this chunk's range: an expert of the next rank
+  // (skipped by the receiver), weight 0
   const int sentinel = ((d + 1) % nranks) * E_l;
-  for (int r = total + tid; r < T; r += kPackThreads) {
+  const int r = c0 + tid / top_k, j = tid % top_k;
+  if (tid < kPackChunk * top_k && r >= total && r < T) {
     int32_t* ids = reinterpret_cast<int32_t*>(blk + (int64_t)r * row_bytes + ids_off);
     float* w = reinterpret_cast<float*>(ids + top_k);
-    for (int j = 0; j < top_k; ++j) {
-      ids[j] = sentinel;
-      w[j] = 0.f;
-    }
+    ids[j] = sentinel;
+    w[j] = 0.f;
   }
 }
 
@@ -114,7 +125,8 @@ extern "C" int duplex_ep_dispatch_pack(const void* rows, int64_t row_bytes, int3
   if ((reinterpret_cast<uintptr_t>(rows) | reinterpret_cast<uintptr_t>(send)) & 15u ||
       (ids_offset & 3))
     return DUPLEX_ERR_ALIGN;
-  ep_pack_kernel<<<n_ranks, kPackThreads, 0, (cudaStream_t)stream>>>(
+  const dim3 grid((unsigned)n_ranks, (unsigned)((T + kPackChunk - 1) / kPackChunk));
+  ep_pack_kernel<<<grid, kPackThreads, 0, (cudaStream_t)stream>>>(
       reinterpret_cast<const uint8_t*>(rows), row_bytes, T, top_k, E, n_ranks, ids_offset,
       reinterpret_cast<uint8_t*>(send), slot_of);
   return record_cuda(cudaGetLastError());

@@ -283,8 +283,9 @@ __global__ void __launch_bounds__(kThreads, 1) dq_gemv_kernel(const __grid_const
   const int npairs = tg.npairs;
   const int ips = p.nrec * npairs;  // items per stage
 
-  if (MODE == kLinear && CORR) {
-    // Dense linear over many tiles per CTA (q, o, lm_head): each warp's partial sums of
+  if (MODE == kLinear && CORR && ntiles > (int)gridDim.x) {
+    // Dense linear with more tiles than CTAs (q, fused q|k|v, lm_head; a tile is one
+    // stage): each warp's partial sums of
     // up to `rmax` tiles wait in `red` ([tile][warp][column][row]); one consumer barrier
     // and one pass then reduce them (warps in order) and write the rows.  The ring
     // position advances stage by stage.

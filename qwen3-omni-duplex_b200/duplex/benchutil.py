@@ -47,6 +47,11 @@ def init_nccl(device, timeout_s: int = 180):
     opts.config.blocking = 0
     dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=timeout_s),
                             pg_options=opts)
+    # a non-blocking communicator finishes its set-up on NCCL's own thread: complete it
+    # with one collective now, before any stream capture begins
+    t = torch.ones(1, device=device)
+    dist.all_reduce(t)
+    torch.cuda.synchronize(device)
     return dist.get_world_size(), dist.get_rank()
 
 

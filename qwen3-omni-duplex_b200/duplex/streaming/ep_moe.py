@@ -17,6 +17,9 @@ token, for batched decode (many streams per rank).  Per layer on every rank:
      which adds the partials in rank order (+ residual), one rounding to the activation
      type (`duplex_ep_combine`).
 
+With one rank, steps 2 and 4 are the identity and are skipped: the expert stage reads
+the routed rows in place.
+
 Each block of the send buffers holds up to T_local rows (a token can need every rank),
 so both all-to-alls have a fixed size: no host synchronisation, and a 48-layer step is
 one CUDA graph.  The rows of a block past its count carry an expert id of another rank
@@ -69,10 +72,15 @@ def ep_forward(x, route_fn, pack_fn, experts_fn, combine_fn, top_k: int, group=N
             b["recv"] = torch.empty(world, T_l, row, dtype=torch.uint8, device=dev)
             b["back"] = torch.empty(world, T_l, H, dtype=torch.float32, device=dev)
     route_fn(x, b["rows"])
-    pack_fn(b["rows"], b["send"], b["slot_of"])
-    # an all-to-all over one rank is the identity: read the send buffer in place
-    recv = b["send"] if world == 1 else b["recv"]
-    if world > 1:
+    if world == 1:
+        # one rank: every token goes to it, in order, so the block IS the routed rows and
+        # the all-to-all is the identity -- no pack, no exchange
+        if "ident" not in b:
+            b["ident"] = torch.arange(T_l, dtype=torch.int32, device=dev).view(1, T_l)
+        recv, slot_of = b["rows"], b["ident"]
+    else:
+        pack_fn(b["rows"], b["send"], b["slot_of"])
+        recv, slot_of = b["recv"], b["slot_of"]
         dist.all_to_all_single(recv, b["send"], group=group)
     rv = recv.view(world * T_l, row)
     x_all = rv[:, :xbytes].view(x.dtype)
@@ -82,7 +90,7 @@ def ep_forward(x, route_fn, pack_fn, experts_fn, combine_fn, top_k: int, group=N
     back = partial if world == 1 else b["back"]
     if world > 1:
         dist.all_to_all_single(back, partial, group=group)
-    return combine_fn(back, b["slot_of"], residual)
+    return combine_fn(back, slot_of, residual)
 
 
 class ExpertParallelMoE(nn.Module):

@@ -108,3 +108,43 @@ def test_place_unpacked_keeps_packed_tensors():
     assert stats == {"moved_params": 16, "kept_on_host": 8, "device": "meta"}
     assert root[0].weight.device.type == "meta" and root[1].weight_packed.device.type == "cpu"
     assert place_thinker is place_unpacked
+
+
+def test_overlay_onto_the_installed_reference():
+    """duplex_b200_overlay.install() on the reference installed in baseline/_ref: the
+    three hot-path modules resolve to this build, every other reference module (config,
+    loader, streaming.clock, ...) to the reference's own file, and the reference's
+    clock path finds the names it imports."""
+    import subprocess
+    import sys
+    root = HERE.parent
+    ref, pkg = root / "baseline" / "_ref", root / "qwen3-omni-duplex_b200"
+    if not (ref / "duplex" / "streaming" / "clock.py").exists():
+        pytest.skip("reference not installed in baseline/_ref")
+    code = f"""
+import sys, json
+sys.path[:0] = [{str(ref)!r}, {str(pkg)!r}]
+import duplex
+out = dict(init=duplex.__file__)
+import duplex_b200_overlay
+out["files"] = duplex_b200_overlay.install()
+import duplex.config, duplex.loader, duplex._lib
+from duplex.streaming.fused_packed_moe import fuse_packed_moe_blocks
+from duplex.quant.dequant import patch_packed_linears
+from duplex.streaming.triton_dequant_gemv import patch_attention_to_triton
+out.update(config=duplex.config.__file__, loader=duplex.loader.__file__, lib=duplex._lib.__file__,
+           fpm=sys.modules[fuse_packed_moe_blocks.__module__].__file__)
+import duplex.streaming.clock as c
+out["clock"] = c.__file__
+out["again"] = duplex_b200_overlay.install()
+print(json.dumps(out))
+"""
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300,
+                       cwd=str(root / "tests"))
+    assert r.returncode == 0, r.stderr[-2000:]
+    out = json.loads(r.stdout.strip().splitlines()[-1])
+    under = lambda f, d: Path(f).resolve().is_relative_to(d.resolve())  # noqa: E731
+    assert under(out["init"], ref)
+    assert all(under(f, pkg) for f in out["files"].values()) and out["again"] == out["files"]
+    assert under(out["fpm"], pkg) and under(out["lib"], pkg)
+    assert under(out["config"], ref) and under(out["loader"], ref) and under(out["clock"], ref)

@@ -210,6 +210,101 @@ def test_expert_parallel_module_two_ranks(cuda):
         assert err <= 1e-3 and oerr <= TOL and derr == 0 and same
 
 
+def _leave_rank(rank, world, port, q):
+    """Heartbeat-gated expert-parallel steps on `world` GPUs; the last rank leaves after
+    step 1 has completed (nothing of it in flight).  The others must raise PeerLost in
+    ready(2), on the host, before launching any kernel or collective of step 2."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      WORLD_SIZE=str(world), RANK=str(rank), LOCAL_RANK=str(rank))
+    import time
+
+    from duplex import benchutil as bu
+    from duplex.health import Heartbeat, PeerLost, abort_group, guard_step
+    from duplex.streaming.ep_moe import ExpertParallelMoE
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    bu.init_nccl(dev, timeout_s=60)
+    L = synth.moe_layer_np(seed=61, E=128, H=2048, I=768, top_k=8, group=128, zero_points=True,
+                           T=world * 32)
+    args = [T(L[n], dev) for n in ("gate_w", "gu_packed", "gu_scale", "dn_packed", "dn_scale")]
+    ep = ExpertParallelMoE(*args, 8, gu_zeros=T(L["gu_zeros"], dev), dn_zeros=T(L["dn_zeros"], dev),
+                           dtype=torch.float16, device=dev)
+    x = T(L["x"][rank * 32:(rank + 1) * 32], dev, torch.float16)
+    hb = Heartbeat(timeout_s=3.0)
+    hb.ready(1)
+    ep(x)
+    guard_step(60.0)                     # step 1 complete on this rank
+    if rank == world - 1:
+        q.put((rank, "left", 0.0))
+        q.close()
+        q.join_thread()
+        os._exit(0)
+    t0 = time.time()
+    try:
+        hb.ready(2)
+        ep(x)
+        guard_step(60.0)
+        res = "no error"
+    except PeerLost:
+        res = "peer lost"
+    q.put((rank, res, time.time() - t0))
+    q.close()
+    q.join_thread()
+    abort_group()                        # nothing in flight: the communicator just goes
+    os._exit(0)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_rank_leaving_is_seen_on_the_host_before_the_next_step(cuda):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_leave_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted(q.get(timeout=300) for _ in ps)
+    for p in ps:
+        p.join(timeout=120)
+    assert res[1][1] == "left"
+    assert res[0][1] == "peer lost" and res[0][2] < 20.0, res[0]
+
+
+def _guard_rank(q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(_free_port()), WORLD_SIZE="1",
+                      RANK="0", LOCAL_RANK="0")
+    from duplex import benchutil as bu
+    from duplex.health import StepTimeout, guard_step
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    bu.init_nccl(dev, timeout_s=60)
+    torch.cuda._sleep(2_000_000_000)     # a slow step: ~1 s of clock64 spinning, then it ends
+    try:
+        guard_step(0.2)
+        res = "no timeout"
+    except StepTimeout:
+        res = "timeout"
+    torch.cuda.synchronize()             # the sleep kernel still finishes on its own
+    ok = float(torch.ones(2, device=dev).sum()) == 2.0
+    q.put((res, ok))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_guard_step_times_out_on_the_host_and_aborts_the_group(cuda):
+    """A step that outlives the host timeout (a bounded sleep kernel, no fault) raises
+    StepTimeout and aborts the group; the device context stays usable."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_guard_rank, args=(q,))
+    p.start()
+    res, ok = q.get(timeout=300)
+    p.join(timeout=60)
+    assert res == "timeout" and ok
+
+
 @pytest.mark.parametrize("N", [1, 2, 4, 8])
 def test_dispatch_pack_and_combine_kernels(cuda, N):
     """duplex_ep_dispatch_pack / duplex_ep_combine against their torch restatements:

@@ -37,7 +37,7 @@ def test_torch_ops_match_the_oracle(cuda):
                                     dn_zeros=t(L["dn_zeros"]), dtype=torch.float16, device=cuda)
     xs = t(L["x"])
     ws = m.workspace(3, cuda)
-    out = ops.moe_forward(xs, m.gate.weight, None, m.gu_tiles.buf, m.dn_tiles.buf, 256, 4, True, 128,
+    out = ops.moe_forward(xs, m.gate.weight.detach(), None, m.gu_tiles.buf, m.dn_tiles.buf, 256, 4, True, 128,
                           True, ws, m.err, None, 0.0)
     ref_mod = torch.empty_like(xs)
     m.forward_into(xs, ref_mod)

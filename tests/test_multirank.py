@@ -187,3 +187,52 @@ def test_ep_rank_leaving_between_steps_fails_fast():
     assert res[1][1] == "left"
     assert res[0][1] == "error", res[0]
     assert res[0][2] < 30.0        # within the 5 s group timeout plus start-up slack
+
+
+def _hb_worker(rank, ws, port, q):
+    """Heartbeat-gated steps: rank 1 leaves after step 1; rank 0 must learn of it on the
+    host in ready(2), before launching anything of step 2."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(ws),
+                      RANK=str(rank), LOCAL_RANK=str(rank))
+    import datetime
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    from duplex.health import Heartbeat, PeerLost
+
+    dist.init_process_group("gloo", rank=rank, world_size=ws, timeout=datetime.timedelta(seconds=30))
+    hb = Heartbeat(timeout_s=2.0)
+    t = torch.ones(4)
+    hb.ready(1)
+    dist.all_reduce(t)                 # step 1 of both ranks
+    if rank == 1:
+        q.put((rank, "left", 0.0, float(t[0])))
+        q.close()
+        q.join_thread()
+        os._exit(0)
+    t0 = time.time()
+    try:
+        hb.ready(2)
+        q.put((rank, "no error", time.time() - t0, float(t[0])))
+    except PeerLost as e:
+        q.put((rank, "peer lost" if "[1]" in str(e) else str(e), time.time() - t0, float(t[0])))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_heartbeat_reports_a_rank_that_left_before_the_next_step():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_hb_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in ps)
+    for p in ps:
+        p.join(timeout=60)
+    assert res[1][1] == "left" and res[1][3] == 2.0
+    assert res[0][1] == "peer lost", res[0]
+    assert 1.5 < res[0][2] < 15.0      # the 2 s heartbeat timeout, not the 30 s group one
