@@ -42,6 +42,8 @@ extern "C" {
 /* ---- device-side error word bits (written with atomicOr into `err`, never trap) */
 #define DUPLEX_DEVERR_EXPERT 1    /* an expert id outside [0, E) was clamped to 0 */
 #define DUPLEX_DEVERR_TIMEOUT 2   /* a bounded pipeline wait gave up */
+#define DUPLEX_DEVERR_NONFINITE 4 /* duplex_stack_forward: a partial layer output was NaN or
+                                     beyond +-2^26 and was clamped (its fixed-point sum) */
 /* duplex_stack_forward also records, from this bit up, which of its waits gave up
  * first: 1 ring slot free, 2 routing plan, 3 ring slot filled, 4 grid barrier,
  * 5 drain, 6 cluster exchange. */

@@ -4,10 +4,9 @@
 // The grid is C clusters of kCS = 8 CTAs (one CTA per SM, 16 consumer warps + one
 // producer warp).  A decode MoE layer runs
 //
-//   reduce   the layer input h = sum of the C clusters' partial outputs of the
-//            previous layer (+ residual), each CTA for its H / 8 rows, then sent to
-//            the other CTAs of its cluster through distributed shared memory (DSMEM),
-//            with each CTA's partial sum of squares (RMSNorm)
+//   input    the layer input h = the previous layer's output, which every CTA added
+//            into a fixed-point accumulator (+ residual), read by every CTA after the
+//            grid barrier, with its RMS scale
 //   router   each CTA of a cluster computes E / 8 logits from gate rows that were
 //            streamed into its shared memory during the previous layer, and sends
 //            them to the cluster (DSMEM)
@@ -18,8 +17,9 @@
 //            every CTA multiplies the slice's 128 intermediate values by the matching
 //            128 columns of the expert's down weights for its H / 8 output rows,
 //            weighted by the routing weight, accumulating in registers
-//   end      each CTA writes its rows of the cluster's partial output (fp32) and
-//            arrives on the grid barrier
+//   end      each CTA adds its rows of the cluster's partial output into the layer's
+//            fixed-point accumulator (red.global.add of int64: order-independent, so
+//            bit-identical) and arrives on the grid barrier
 //
 // so a MoE layer has ONE grid-wide barrier; every other hand-off stays inside a
 // cluster (mbarriers with cluster-scope release / acquire).  A clock layer adds the
@@ -67,7 +67,7 @@ struct StackParams {
   float rms_eps;
   const void* x_in;
   void* out;
-  float* part;  // [2][kMaxClusters][T][H] partial outputs of the clusters
+  unsigned long long* acc;  // [3][T][H] fixed-point layer outputs (see add_partials)
   void* qkv;    // q|k|v [T][qkv_R]
   void* h1;     // h + o(q) [T][H]
   unsigned* barrier;  // grid barrier counter, zeroed before the launch
@@ -84,12 +84,12 @@ struct StackParams {
 constexpr uint32_t kSFull = 0;        // 16 mbarriers
 constexpr uint32_t kSEmpty = 128;     // 16 mbarriers
 constexpr uint32_t kSPlan = 256;      // mbarrier: plan of the current layer ready (producer)
-constexpr uint32_t kSHx = 264;        // mbarrier: h slices of the cluster arrived
+constexpr uint32_t kSHx = 264;        // (free)
 constexpr uint32_t kSLg = 272;        // mbarrier: logits of the cluster arrived
 constexpr uint32_t kSAct = 280;       // 2 mbarriers: intermediate slices arrived
 constexpr uint32_t kSAbort = 296;     // int
 constexpr uint32_t kSNUnits = 300;    // int
-constexpr uint32_t kSSsq = 320;       // [kCS ranks][8 tokens] floats: sums of squares
+constexpr uint32_t kSSsq = 320;       // (free)
 constexpr uint32_t kSSel = 576;       // [8 tokens][8] ints
 constexpr uint32_t kSSelBits = 832;   // [8 tokens][8] words: selected experts
 constexpr uint32_t kSUnitE = 1088;    // kMaxUnits ints
@@ -467,103 +467,147 @@ DEVI int defer_tiles(int nT) {
 }
 
 // ------------------------------------------------------------------ h exchange
-// The layer input, this CTA's rows [row0, row0 + rrows): h = sum over the C clusters'
-// partial outputs `P` ([C][nT][H] fp32) (+ res, the rows of the previous layer's MoE
-// input in `hpl`), rounded once to T.  Eight lanes share a (token, 4 rows) group:
-// lane j loads clusters j, j + 8, j + 16, j + 24 (all loads in flight at once), and the
-// eight partial sums are combined by an xor butterfly, which gives every lane the same
-// bits (a fixed order).  With `out` null the rows go into `hpl` of every CTA of the
-// cluster (lane j writes CTA j), with this CTA's sums of squares of the rounded rows
-// (per token, fixed order) into the cluster's `ssq[rank]`; with `out` they are the
-// launch's result.
-static_assert(kMaxClusters <= 32 && kCS == 8, "reduce: 8 lanes x 4 clusters per group");
-template <typename T, int KT>  // KT: tokens at most (1 in the one-token kernel)
-DEVN void reduce_rows_h(const float* P, int C, int nT, int H, int row0, int rrows, bool residual,
-                        T* hpl, float* ssq, int rank, T* out, float* scratch) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, j = lane & 7;
-  const int q4 = rrows >> 2;  // 4-row groups per token
-  const int total = nT * q4;
-  float ss[KT];
-#pragma unroll
-  for (int n = 0; n < KT; ++n) ss[n] = 0.f;
-  // the trip count is the same for the whole warp (the shuffles need every lane)
-  for (int wb = warp * 4; wb < total; wb += kCW * 4) {
-    const int g = wb + (lane >> 3);
-    const bool on = g < total;
-    const int n = on ? g / q4 : 0, q = on ? g - n * q4 : 0;
-    const int row = row0 + 4 * q;
-    float4 v[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int c = j + 8 * k;
-      v[k] = on && c < C
-                 ? __ldcg(reinterpret_cast<const float4*>(P + ((size_t)c * nT + n) * H + row))
-                 : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    float4 s = v[0];
-#pragma unroll
-    for (int k = 1; k < 4; ++k) {
-      s.x += v[k].x;
-      s.y += v[k].y;
-      s.z += v[k].z;
-      s.w += v[k].w;
-    }
-#pragma unroll
-    for (int o = 4; o > 0; o >>= 1) {
-      s.x += __shfl_xor_sync(0xffffffffu, s.x, o);
-      s.y += __shfl_xor_sync(0xffffffffu, s.y, o);
-      s.z += __shfl_xor_sync(0xffffffffu, s.z, o);
-      s.w += __shfl_xor_sync(0xffffffffu, s.w, o);
-    }
-    if (!on) continue;  // after the shuffles: uniform from here on per 8-lane set
-    if (residual) {
-      const uint2 rv = *reinterpret_cast<const uint2*>(hpl + (size_t)n * H + row);
-      const T* re = reinterpret_cast<const T*>(&rv);
-      s.x += to_f32<T>(re[0]);
-      s.y += to_f32<T>(re[1]);
-      s.z += to_f32<T>(re[2]);
-      s.w += to_f32<T>(re[3]);
-    }
+// The clusters' partial layer outputs meet in a fixed-point accumulator: every CTA adds
+// its rows' partial sums, scaled by 2^32 and rounded to int64, with red.global.add
+// (add_partials).  Integer addition is associative, so the sum is the same bits
+// whatever order the 15 clusters' adds land in: no partial buffers, no cross-cluster
+// reduction pass, and bit-identical launches.  Partials are clamped to +-2^26 (beyond
+// the fp16 range; a clamped or NaN partial sets DUPLEX_DEVERR_NONFINITE), so the sum of
+// up to 32 clusters stays inside int64; below 2^-9 a partial keeps 2^-33 absolute
+// resolution, finer than any fp16 / bf16 output needs.
+constexpr float kFixScale = 4294967296.0f;           // 2^32
+constexpr float kFixInv = 2.3283064365386963e-10f;   // 2^-32
+constexpr float kFixClamp = 67108864.0f;             // 2^26
+static_assert(kMaxClusters * kCS <= 256, "fixed-point sum of every CTA's partial fits int64");
+
+DEVI unsigned long long to_fix(float v, int* err) {
+  if (!(fabsf(v) <= kFixClamp)) {
+    set_error(err, DUPLEX_DEVERR_NONFINITE);
+    v = v > 0.f ? kFixClamp : (v < 0.f ? -kFixClamp : 0.f);
+  }
+  return (unsigned long long)__float2ll_rn(v * kFixScale);
+}
+
+// h = A (the fixed-point sum, [nT][H] int64) x 2^-32 (one rounding to fp32) (+ res, the
+// previous MoE input in hpl), rounded once to T.  With `out` null every CTA converts all
+// rows into its hpl (in place: each element is read and written by one thread), and a
+// consumer barrier ends it; with `out` the CTA writes its share (CTA g of G takes every
+// G-th group of 4 values) of the launch's result.
+template <typename T>
+DEVN void load_sum_rows(const unsigned long long* A, int nT, int H, bool residual, T* hpl,
+                        T* out, int g, int G) {
+  const int total = (nT * H) >> 2;  // groups of 4 values (32 bytes of A)
+  const int first = out ? g * kConsumers + (int)threadIdx.x : (int)threadIdx.x;
+  const int step = out ? G * kConsumers : kConsumers;
+  for (int idx = first; idx < total; idx += step) {
+    const longlong2* src = reinterpret_cast<const longlong2*>(A) + 2 * idx;
+    const longlong2 a0 = __ldcg(src), a1 = __ldcg(src + 1);
+    float v[4] = {__ll2float_rn(a0.x) * kFixInv, __ll2float_rn(a0.y) * kFixInv,
+                  __ll2float_rn(a1.x) * kFixInv, __ll2float_rn(a1.y) * kFixInv};
     union {
       uint2 u;
       T h[4];
     } pk;
-    pk.h[0] = from_f32<T>(s.x);
-    pk.h[1] = from_f32<T>(s.y);
-    pk.h[2] = from_f32<T>(s.z);
-    pk.h[3] = from_f32<T>(s.w);
-    if (out) {
-      if (j == 0) *reinterpret_cast<uint2*>(out + (size_t)n * H + row) = pk.u;
-    } else {
-      if (j == 0) {
-        const float a = to_f32<T>(pk.h[0]), b = to_f32<T>(pk.h[1]);
-        const float c = to_f32<T>(pk.h[2]), d = to_f32<T>(pk.h[3]);
-        const float sq = fmaf(a, a, fmaf(b, b, fmaf(c, c, d * d)));
+    if (residual) {
+      pk.u = *reinterpret_cast<const uint2*>(hpl + (size_t)idx * 4);
 #pragma unroll
-        for (int m = 0; m < KT; ++m)
-          if (m == n) ss[m] += sq;
+      for (int k = 0; k < 4; ++k) v[k] += to_f32<T>(pk.h[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) pk.h[k] = from_f32<T>(v[k]);
+    *reinterpret_cast<uint2*>((out ? out : hpl) + (size_t)idx * 4) = pk.u;
+  }
+  if (!out) named_bar_sync(1, kConsumers);
+}
+
+// The MoE layer input in one pass: h = A x 2^-32 (+ res, the previous MoE input in
+// hpl), rounded once to T, into hpl; each warp's sums of squares of the rounded values
+// per token (fixed order: the thread's groups in order, an xor butterfly, then the
+// warps in order -- every thread adds the 16 warp sums itself, so all get the same
+// bits without a second barrier) give the RMS scale; each thread then normalises its
+// own groups into xsh (natural order).  Two consumer barriers.
+template <typename T, int KT>
+DEVN void input_rows(const unsigned long long* A, int nT, int H, bool residual, bool rms,
+                     float eps, T* hpl, float* inv, uint8_t* xsh, uint32_t pitch, float* scratch) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gpt = H >> 2;  // groups of 4 values per token
+  const int total = nT * gpt;
+  float ss[KT];
+#pragma unroll
+  for (int n = 0; n < KT; ++n) ss[n] = 0.f;
+  for (int idx = tid; idx < total; idx += kConsumers) {
+    const int n = idx / gpt;
+    const longlong2* src = reinterpret_cast<const longlong2*>(A) + 2 * idx;
+    const longlong2 a0 = __ldcg(src), a1 = __ldcg(src + 1);
+    float v[4] = {__ll2float_rn(a0.x) * kFixInv, __ll2float_rn(a0.y) * kFixInv,
+                  __ll2float_rn(a1.x) * kFixInv, __ll2float_rn(a1.y) * kFixInv};
+    union {
+      uint2 u;
+      T h[4];
+    } pk;
+    if (residual) {
+      pk.u = *reinterpret_cast<const uint2*>(hpl + (size_t)idx * 4);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) v[k] += to_f32<T>(pk.h[k]);
+    }
+    float sq = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      pk.h[k] = from_f32<T>(v[k]);
+      const float r = to_f32<T>(pk.h[k]);
+      sq = fmaf(r, r, sq);
+    }
+    *reinterpret_cast<uint2*>(hpl + (size_t)idx * 4) = pk.u;
+    if (!rms)
+      *reinterpret_cast<uint2*>(xsh + (uint32_t)n * pitch + (uint32_t)(idx - n * gpt) * 8u) = pk.u;
+#pragma unroll
+    for (int m = 0; m < KT; ++m)
+      if (m == n) ss[m] += sq;
+  }
+  if (rms) {
+#pragma unroll
+    for (int n = 0; n < KT; ++n) {
+      float a = ss[n];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      if (lane == 0 && n < nT) scratch[warp * kMaxTokens + n] = a;
+    }
+    named_bar_sync(1, kConsumers);
+    float sc[KT];
+#pragma unroll
+    for (int n = 0; n < KT; ++n) {
+      float a = 0.f;
+      if (n < nT) {
+#pragma unroll
+        for (int w = 0; w < kCW; ++w) a += scratch[w * kMaxTokens + n];
       }
-      // every lane has the row values: lane j writes them into CTA j of the cluster
-      st_peer_v2(peer_addr(hpl + (size_t)n * H + row, (uint32_t)j), pk.u);
+      sc[n] = 1.0f / sqrtf(a / (float)H + eps);
+      if (tid == n && n < nT) inv[n] = sc[n];
+    }
+    for (int idx = tid; idx < total; idx += kConsumers) {
+      const int n = idx / gpt;
+      float s = sc[0];
+#pragma unroll
+      for (int m = 1; m < KT; ++m)
+        if (m == n) s = sc[m];
+      union {
+        uint2 u;
+        T h[4];
+      } pk;
+      pk.u = *reinterpret_cast<const uint2*>(hpl + (size_t)idx * 4);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) pk.h[k] = from_f32<T>(to_f32<T>(pk.h[k]) * s);
+      *reinterpret_cast<uint2*>(xsh + (uint32_t)n * pitch + (uint32_t)(idx - n * gpt) * 8u) = pk.u;
     }
   }
-  if (out) return;
-  // per-token sums of squares: warp shuffles, then the warps in order
-#pragma unroll
-  for (int n = 0; n < KT; ++n) {
-    float a = ss[n];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-    if (lane == 0) scratch[warp * kMaxTokens + n] = a;
-  }
   named_bar_sync(1, kConsumers);
-  if (tid < nT) {
-    float a = 0.f;
-#pragma unroll
-    for (int w = 0; w < kCW; ++w) a += scratch[w * kMaxTokens + tid];
-#pragma unroll
-    for (int p = 0; p < kCS; ++p) st_peer_f32(peer_addr(ssq + rank * kMaxTokens + tid, (uint32_t)p), a);
-  }
+}
+
+// Zero CTA g's share (of G) of an accumulator of n int64 values (n % 2 == 0).
+DEVI void zero_share(unsigned long long* A, int n, int g, int G) {
+  const int pairs = n >> 1;
+  for (int i = g * kConsumers + (int)threadIdx.x; i < pairs; i += G * kConsumers)
+    reinterpret_cast<longlong2*>(A)[i] = make_longlong2(0, 0);
 }
 
 // RMS scale per token from the full rows in hpl ([nT][H], natural order), fixed
@@ -697,7 +741,7 @@ DEVI void router_mma(const uint8_t* ring, uint32_t slot_bytes, int NS, RingPos p
 // its own: inside plan_units the general path's code made this path ~2.5x slower
 // (3,100 vs 1,250 cycles measured).
 template <typename T, int KPL>  // KPL: keys per lane, E <= 32 KPL
-DEVN int plan_one(int E, int top_k, int norm, uint8_t* smem, float* scratch) {
+DEVN int plan_one(int E, int top_k, int norm, uint8_t* smem, float* scratch, uint64_t* ready) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const float* ls = reinterpret_cast<const float*>(smem + kSLogit);
   int* sel_s = reinterpret_cast<int*>(smem + kSSel);
@@ -757,6 +801,9 @@ DEVN int plan_one(int E, int top_k, int norm, uint8_t* smem, float* scratch) {
       if (norm) unit_w[rank * kMaxTokens] = ej / esum;
     }
     if (lane == 0) *n_units_s = top_k;
+    // the producer needs only the unit list: release it now, not after the barrier
+    __syncwarp();
+    if (lane == 0) mbar_arrive(ready);
   }
   named_bar_sync(1, kConsumers);
   return top_k;
@@ -1066,8 +1113,10 @@ DEVI void slice_down(const uint8_t* st, const TileGeom tg, int nrec, uint32_t dn
 }
 
 // This CTA's rows of the cluster's partial output: part[c][n][row] (fp32).
-DEVI void write_partials(float* part, int nT, int H, int row0, int nrec,
-                         float (&acc)[kMaxRecPerWarp][4]) {
+// This CTA's partial output rows (the down projection's accumulators, warp w holding
+// records w, w + 16) added into the fixed-point accumulator A ([nT][H]).
+DEVI void add_partials(unsigned long long* A, int nT, int H, int row0, int nrec,
+                       float (&acc)[kMaxRecPerWarp][4], int* err) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
 #pragma unroll
@@ -1076,12 +1125,12 @@ DEVI void write_partials(float* part, int nT, int H, int row0, int nrec,
     if (rec < nrec) {
       const int row = row0 + rec * 16 + g;
       if (2 * t < nT) {
-        part[(size_t)(2 * t) * H + row] = acc[k][0];
-        part[(size_t)(2 * t) * H + row + 8] = acc[k][2];
+        atomicAdd(A + (size_t)(2 * t) * H + row, to_fix(acc[k][0], err));
+        atomicAdd(A + (size_t)(2 * t) * H + row + 8, to_fix(acc[k][2], err));
       }
       if (2 * t + 1 < nT) {
-        part[(size_t)(2 * t + 1) * H + row] = acc[k][1];
-        part[(size_t)(2 * t + 1) * H + row + 8] = acc[k][3];
+        atomicAdd(A + (size_t)(2 * t + 1) * H + row, to_fix(acc[k][1], err));
+        atomicAdd(A + (size_t)(2 * t + 1) * H + row + 8, to_fix(acc[k][3], err));
       }
     }
     zero4(acc[k]);
@@ -1100,7 +1149,6 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSFull);
   uint64_t* empty = reinterpret_cast<uint64_t*>(smem + kSEmpty);
   uint64_t* plan_ready = reinterpret_cast<uint64_t*>(smem + kSPlan);
-  uint64_t* hx_full = reinterpret_cast<uint64_t*>(smem + kSHx);
   uint64_t* lg_full = reinterpret_cast<uint64_t*>(smem + kSLg);
   uint64_t* act_full = reinterpret_cast<uint64_t*>(smem + kSAct);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSAbort);
@@ -1123,7 +1171,6 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
       mbar_init(&empty[s], kCW);
     }
     mbar_init(plan_ready, 1);
-    mbar_init(hx_full, kCS);
     mbar_init(lg_full, kCS);
     mbar_init(&act_full[0], kCS);
     mbar_init(&act_full[1], kCS);
@@ -1253,7 +1300,6 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
 
   // ================================================================== consumers
   float* red = reinterpret_cast<float*>(smem + kSRed);
-  float* ssq = reinterpret_cast<float*>(smem + kSSsq);
   float* ls = reinterpret_cast<float*>(smem + kSLogit);
   float* inv = reinterpret_cast<float*>(smem + kSInv);
   float2* dgp0 = reinterpret_cast<float2*>(smem + p.off_av);  // [2][ib][kCS][8] partial sums
@@ -1286,9 +1332,7 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
     ++nb;
     grid_wait(p.barrier, nb, nb == 1 && (p.test_flags & 1), abort_flag, err, limit);
   };
-  auto partials = [&](int l) {
-    return p.part + (size_t)(l & 1) * kMaxClusters * nT * p.H;
-  };
+  auto accbuf = [&](int l) { return p.acc + (size_t)(l % 3) * nT * p.H; };
 
   for (int l = 0; l < p.n_layers; ++l) {
     const duplex_stack_layer L = p.layers[l];
@@ -1296,22 +1340,16 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
     if (l == 0) {
       load_rows<T>(reinterpret_cast<const T*>(p.x_in), nT, p.H, hpl);
       if (rms) local_inv_rms<T>(hpl, nT, p.H, p.rms_eps, inv);
+      normalise_rows<T>(hpl, nT, p.H, inv, rms, xsh, p.x_pitch);
     } else {
       ++nb;
       grid_wait(p.barrier, nb, nb == 1 && (p.test_flags & 1), abort_flag, err, limit);
-      reduce_rows_h<T, KT>(partials(l - 1), C, nT, p.H, row0, p.rrows,
-                       p.moe_residual != 0, hpl, ssq, rank, nullptr, red);
-      signal_cluster_xchg(hx_full);
-      wait_cluster_xchg(hx_full, (uint32_t)((l - 1) & 1), abort_flag, err, limit);
-      if (tid < nT) {
-        float a = 0.f;
-#pragma unroll
-        for (int q = 0; q < kCS; ++q) a += ssq[q * kMaxTokens + tid];
-        inv[tid] = 1.0f / sqrtf(a / (float)p.H + p.rms_eps);
-      }
-      named_bar_sync(1, kConsumers);
+      input_rows<T, KT>(accbuf(l - 1), nT, p.H, p.moe_residual != 0, rms, p.rms_eps, hpl, inv,
+                        xsh, p.x_pitch, red);
     }
-    normalise_rows<T>(hpl, nT, p.H, inv, rms, xsh, p.x_pitch);
+    // the accumulator of layer l + 1 was last read at the start of layer l - 1, and is
+    // next added into after this layer's grid barrier
+    zero_share(accbuf(l + 1), nT * p.H, cta, G);
     if (p.has_attn) {
       // -------------------------------------------------------------- Q
       stage_rows<T>(nullptr, 0, nT, p.H, xsh, p.x_pitch, gsum, cw, kStageFrag);
@@ -1383,9 +1421,10 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
     wait_cluster_xchg(lg_full, (uint32_t)(l & 1), abort_flag, err, limit);
     // ------------------------------------------------------------------ plan
     const int nu = nT != 1   ? plan_units<T>(nT, p.E, p.top_k, smem, red)
-                   : p.E <= 128 ? plan_one<T, 4>(p.E, p.top_k, p.norm, smem, red)
-                                : plan_one<T, kMaxExperts / 32>(p.E, p.top_k, p.norm, smem, red);
-    if (tid == 0) mbar_arrive(plan_ready);
+                   : p.E <= 128 ? plan_one<T, 4>(p.E, p.top_k, p.norm, smem, red, plan_ready)
+                                : plan_one<T, kMaxExperts / 32>(p.E, p.top_k, p.norm, smem, red,
+                                                                plan_ready);
+    if (nT != 1 && tid == 0) mbar_arrive(plan_ready);
     if (nT != 1 || !p.norm) plan_weights(nT, p.E, p.top_k, p.norm, smem, red);
     // ------------------------------------------------------------------ items
     int i0, i1;
@@ -1419,15 +1458,14 @@ __global__ void __launch_bounds__(kThreads, 1) stack_kernel(const __grid_constan
       ++kbatch;
     }
     // ------------------------------------------------------------------ end of layer
-    write_partials(partials(l) + (size_t)cid * nT * p.H, nT, p.H, row0, nrec, acc);
+    add_partials(accbuf(l), nT, p.H, row0, nrec, acc, err);
     grid_arrive(p.barrier);
   }
-  // the result: cluster 0 adds the last layer's partial outputs
+  // the result: every CTA converts its share of the last layer's sum
   ++nb;
   grid_wait(p.barrier, nb, nb == 1 && (p.test_flags & 1), abort_flag, err, limit);
-  if (cid == 0)
-    reduce_rows_h<T, KT>(partials(p.n_layers - 1), C, nT, p.H, row0, p.rrows, p.moe_residual != 0, hpl,
-                     ssq, rank, reinterpret_cast<T*>(p.out), red);
+  load_sum_rows<T>(accbuf(p.n_layers - 1), nT, p.H, p.moe_residual != 0, hpl,
+                   reinterpret_cast<T*>(p.out), cta, G);
   cluster_sync_all();
 }
 
@@ -1517,7 +1555,7 @@ static int slice_geom(int group, int has_zeros, TileGeom* tg) {
 static inline uint32_t up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
 struct StackScratch {
-  size_t barrier, part, qkv, h1, total;
+  size_t barrier, acc, qkv, h1, total;
 };
 
 static StackScratch stack_scratch(int T, int H, int qkv_R) {
@@ -1525,8 +1563,8 @@ static StackScratch stack_scratch(int T, int H, int qkv_R) {
   size_t off = 0;
   s.barrier = off;
   off += 256;
-  s.part = off;
-  off += align_up((size_t)2 * kMaxClusters * T * H * 4, 256);
+  s.acc = off;  // right after the barrier counter: one memset zeroes both
+  off += align_up((size_t)3 * T * H * 8, 256);
   s.qkv = off;
   off += align_up((size_t)T * (qkv_R > 0 ? qkv_R : 1) * 2, 256);
   s.h1 = off;
@@ -1654,7 +1692,7 @@ extern "C" int duplex_stack_forward(const duplex_stack_layer* layers, int32_t n_
   p.nblk = (E + 15) / 16;
   p.rms_eps = rms_eps;
   p.x_in = x_in; p.out = out;
-  p.part = reinterpret_cast<float*>(ws + L.part);
+  p.acc = reinterpret_cast<unsigned long long*>(ws + L.acc);
   p.qkv = ws + L.qkv;
   p.h1 = ws + L.h1;
   p.barrier = reinterpret_cast<unsigned*>(ws + L.barrier);
@@ -1739,7 +1777,10 @@ extern "C" int duplex_stack_forward(const duplex_stack_layer* layers, int32_t n_
   if (nclusters < 1) return DUPLEX_ERR_UNSUPPORTED;
   if (nclusters > kMaxClusters) nclusters = kMaxClusters;
   cfg.gridDim = dim3(kCS * nclusters);
-  rc = record_cuda(cudaMemsetAsync(ws + L.barrier, 0, 256, st));
+  // the barrier counter and the first layer's accumulator (the two later ones are
+  // zeroed inside the launch)
+  static_assert(sizeof(unsigned long long) == 8, "int64 accumulator");
+  rc = record_cuda(cudaMemsetAsync(ws + L.barrier, 0, L.acc + (size_t)T * H * 8 - L.barrier, st));
   if (rc) return rc;
   return record_cuda(cudaLaunchKernelEx(&cfg, kern, p));
 }
