@@ -127,6 +127,19 @@ class FusedPackedMoE(nn.Module):
                    I, H, dn_packed.shape[1], dn_packed.shape[2] * PACK)
         return m
 
+    @classmethod
+    def from_checkpoint(cls, tensors, prefix, top_k, norm_topk_prob=True, dtype=torch.bfloat16,
+                        device="cuda", tc=False, stack=False):
+        """Build from the packed triplets of one MoE layer in a checkpoint mapping (name ->
+        tensor, e.g. duplex.streaming.packed_checkpoint.ShardedTensors): `<prefix>.experts.
+        <i>.<gate|up|down>_proj.weight_{packed,scale,shape}` and `<prefix>.gate.weight`."""
+        from duplex.streaming.packed_checkpoint import stack_layer
+        st = stack_layer(tensors, prefix, dtype=dtype)
+        return cls.from_stacked(st["gate_weight"], st["gu_packed"], st["gu_scale"], st["dn_packed"],
+                                st["dn_scale"], top_k, gu_zeros=st["gu_zeros"],
+                                dn_zeros=st["dn_zeros"], norm_topk_prob=norm_topk_prob,
+                                dtype=dtype, device=device, tc=tc, stack=stack)
+
     def _install(self, gu_p, gu_s, gu_z, dp, ds, dz, inter, hidden, hid_out, inter_in):
         """Repack the stacked experts once into tile records (gate and up blocks paired)."""
         if inter % 16 or hidden % 32 or inter_in % 32 or hid_out % 16:
@@ -314,8 +327,24 @@ class FusedPackedMoE(nn.Module):
 
 def fuse_packed_moe_blocks(model, dtype=torch.bfloat16, device="cuda",
                            n_pinned: int | None = None, cpu_compute: bool = False,
-                           verbose: bool = True) -> int:
-    """Replace every packed SparseMoeBlock with a FusedPackedMoE (reference :278-319)."""
+                           verbose: bool = True, checkpoint=None, prefix: str = "") -> int:
+    """Replace every packed SparseMoeBlock with a FusedPackedMoE (reference :278-319).
+
+    With `checkpoint` (a name -> tensor mapping of the packed checkpoint, e.g.
+    packed_checkpoint.ShardedTensors) the fused-expert blocks of transformers >= 5, which
+    have no per-expert modules to hold the packed triplets, are replaced too: their
+    experts are stacked straight from the checkpoint keys `prefix + <block name>.experts.
+    <i>.*` (packed_checkpoint.fused_expert_sites)."""
+    n_fused = 0
+    if checkpoint is not None:
+        from duplex.streaming.packed_checkpoint import fused_expert_sites
+        for parent, attr, key, top_k, norm in fused_expert_sites(model, checkpoint, prefix):
+            setattr(parent, attr, FusedPackedMoE.from_checkpoint(
+                checkpoint, key, top_k, norm_topk_prob=norm, dtype=dtype, device=device))
+            n_fused += 1
+            gc.collect()
+        if n_fused and torch.cuda.is_available():
+            torch.cuda.empty_cache()
     sites = []
     for parent in model.modules():
         for name, child in list(parent.named_children()):
@@ -338,6 +367,7 @@ def fuse_packed_moe_blocks(model, dtype=torch.bfloat16, device="cuda",
         if verbose and n % 6 == 0:
             used = torch.cuda.memory_allocated() / 1024**3 if torch.cuda.is_available() else 0
             print(f"    fused {n}/{len(sites)} packed blocks, {used:.2f} GB", flush=True)
+    n += n_fused
     if verbose:
         print(f"fused {n} packed MoE blocks, all GPU-resident (B200 kernels)")
     return n
