@@ -266,6 +266,31 @@ int duplex_ep_combine(const float* partials, const int32_t* slot_of, int32_t T, 
                       int32_t H, const void* residual, void* out, int act_dtype, void* stream);
 
 /*
+ * talker_moe_forward -- the Talker's MoE block, `FusedMoE.forward` of the reference
+ * (src/duplex/streaming/fused_moe.py:40-141), for T <= 8 tokens: router (as moe_route),
+ * the selected experts' gate|up with SiLU(gate) * up, down, the routing-weighted sum over
+ * the slots in selection order, plus the shared expert gated by
+ * sigmoid(x . sh_gate_w) (fused_moe.py:136-140), with the reference's rounding to the
+ * act dtype after each of those steps.  gate_up [E][2I][H] (gate rows, then up rows),
+ * down [E][H][I]: act dtype, or int8 (weight_int8 != 0) with per-row scales
+ * gu_scale [E][2I] and dn_scale [E][H] in the act dtype, a weight being round(q * s)
+ * (the reference's q8 format, fused_moe.py:84-97).  Shared expert (optional: sh_gate
+ * NULL): sh_gate / sh_up [S][H], sh_down [H][S], sh_gate_w [H] or NULL (gate 1), act
+ * dtype.  H, I, S multiples of 8 (of 16 for int8 rows); pointers 16-byte aligned.
+ * w_out / sel_out [T][top_k] or NULL.  workspace: duplex_talker_moe_workspace_bytes,
+ * zero-filled once before first use.  err: DUPLEX_DEVERR_EXPERT for an out-of-range id.
+ */
+int duplex_talker_moe_workspace_bytes(int32_t T, int32_t E, int32_t H, int32_t I, int32_t top_k,
+                                      int32_t S, size_t* bytes);
+int duplex_talker_moe_forward(const void* x, int act_dtype, int32_t T, const void* gate_w,
+                              int32_t E, int32_t H, int32_t I, int32_t top_k, int32_t norm_topk,
+                              const void* gate_up, const void* down, int weight_int8,
+                              const void* gu_scale, const void* dn_scale, const void* sh_gate,
+                              const void* sh_up, const void* sh_down, int32_t S,
+                              const void* sh_gate_w, void* out, float* w_out, int32_t* sel_out,
+                              void* workspace, size_t workspace_bytes, int32_t* err, void* stream);
+
+/*
  * Tensor-core (tcgen05) variants of the grouped path -- same computation, arguments,
  * limits and error behaviour as duplex_moe_grouped / duplex_moe_experts_grouped, with
  * the experts in "tensor-core records" instead of tile records, and these limits: group

@@ -95,6 +95,12 @@ _SIGNATURES = {
                                  _c_ptr, _c_ptr], _c_int),
     "duplex_ep_combine": ([_c_ptr, _c_ptr, _c_i32, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_int, _c_ptr],
                           _c_int),
+    "duplex_talker_moe_workspace_bytes": ([_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
+                                           ctypes.POINTER(ctypes.c_size_t)], _c_int),
+    "duplex_talker_moe_forward": ([_c_ptr, _c_int, _c_i32, _c_ptr, _c_i32, _c_i32, _c_i32, _c_i32,
+                                   _c_i32, _c_ptr, _c_ptr, _c_int, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
+                                   _c_ptr, _c_i32, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size,
+                                   _c_ptr, _c_ptr], _c_int),
     "duplex_gate_records_bytes": ([_c_i32, _c_i32, ctypes.POINTER(ctypes.c_size_t)], _c_int),
     "duplex_repack_gate_records": ([_c_ptr, _c_int, _c_i32, _c_i32, _c_ptr, _c_size, _c_ptr],
                                    _c_int),

@@ -2,9 +2,10 @@
 
 The reference (thecodacus/qwen3-omni-duplex, `src/duplex/`) reaches its int4 hot path
 through three modules: `duplex.streaming.fused_packed_moe`,
-`duplex.streaming.triton_dequant_gemv` and `duplex.quant.dequant`.  `install()` puts
-this build's `streaming/` and `quant/` directories FIRST on the reference packages'
-`__path__`, so those three names (and `duplex.streaming.ep_moe`) resolve to the sm_100a
+`duplex.streaming.triton_dequant_gemv` and `duplex.quant.dequant`, and its Talker's
+MoE through `duplex.streaming.fused_moe`.  `install()` puts this build's `streaming/`
+and `quant/` directories FIRST on the reference packages' `__path__`, so those four
+names (and `duplex.streaming.ep_moe`, `packed_checkpoint`) resolve to the sm_100a
 modules, and appends this build's `duplex/` directory LAST on `duplex.__path__`, so
 `duplex._lib`, `duplex.clock`, `duplex.health` and the rest are found while every module
 the reference has itself -- `duplex.config`, `duplex.loader`, `duplex.fast_engine`,
@@ -27,7 +28,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent / "duplex"
 REPLACED = ("duplex.streaming.fused_packed_moe", "duplex.streaming.triton_dequant_gemv",
-            "duplex.quant.dequant")
+            "duplex.quant.dequant", "duplex.streaming.fused_moe")
 
 
 def install() -> dict:

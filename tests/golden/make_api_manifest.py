@@ -4,7 +4,8 @@
 
 Parses (with `ast`, nothing is imported or run) the reference modules that this
 build replaces -- src/duplex/streaming/fused_packed_moe.py,
-src/duplex/streaming/triton_dequant_gemv.py, src/duplex/quant/dequant.py -- and
+src/duplex/streaming/triton_dequant_gemv.py, src/duplex/quant/dequant.py and the
+Talker's src/duplex/streaming/fused_moe.py -- and
 writes `reference_api.json` next to this script:
 
   modules:  {module: {name: {"kind": "function" | "class" | "value",
@@ -32,6 +33,7 @@ MODULES = {
     "duplex.streaming.fused_packed_moe": "src/duplex/streaming/fused_packed_moe.py",
     "duplex.streaming.triton_dequant_gemv": "src/duplex/streaming/triton_dequant_gemv.py",
     "duplex.quant.dequant": "src/duplex/quant/dequant.py",
+    "duplex.streaming.fused_moe": "src/duplex/streaming/fused_moe.py",
 }
 KEEP_PRIVATE = {"_dequant", "_stack_packed"}
 
