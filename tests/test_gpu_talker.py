@@ -105,19 +105,23 @@ def test_talker_geometry_vs_fp32(cuda, dt, T, q8):
     assert torch.equal(first, out)
     ref = fp32_talker(x, gate_w, gate_up, down, gu_s, dn_s, shg, shu, shd, sgw, k, False)
     assert rel(out, ref) <= BAR[dt], rel(out, ref)
-    # the selection is the fp32 restatement's (logits rounded to the act dtype first)
+    # the selection: logits rounded to the act dtype, larger first, ties to the lower id
     lg = (x.float() @ gate_w.float().T).to(dt).float()
-    assert torch.equal(sel.long().cpu(), torch.topk(lg, k, dim=-1).indices.cpu())
+    want = torch.argsort(-lg, dim=-1, stable=True)[:, :k]
+    assert torch.equal(sel.long().cpu(), want.cpu())
     assert int(err.item()) == 0
 
 
 def test_transformers_talker_block_vs_its_own_forward(cuda):
-    from types import SimpleNamespace
     from duplex.streaming.fused_moe import fuse_moe_blocks
     from transformers.models.qwen3_omni_moe import modeling_qwen3_omni_moe as tm
-    cfg = SimpleNamespace(num_experts=32, hidden_size=256, moe_intermediate_size=128,
-                          hidden_act="silu", num_experts_per_tok=4, norm_topk_prob=False,
-                          shared_expert_intermediate_size=192, intermediate_size=512)
+    from transformers.models.qwen3_omni_moe.configuration_qwen3_omni_moe import (
+        Qwen3OmniMoeTalkerTextConfig)
+    cfg = Qwen3OmniMoeTalkerTextConfig(num_experts=32, hidden_size=256, moe_intermediate_size=128,
+                                       num_experts_per_tok=4, norm_topk_prob=False,
+                                       intermediate_size=512, num_hidden_layers=1,
+                                       num_attention_heads=4, num_key_value_heads=2)
+    cfg.shared_expert_intermediate_size = 192
     torch.manual_seed(3)
     blk = tm.Qwen3OmniMoeTalkerTextSparseMoeBlock(cfg)
     with torch.no_grad():
