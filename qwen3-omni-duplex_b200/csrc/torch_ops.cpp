@@ -188,6 +188,52 @@ at::Tensor ep_combine(const at::Tensor& partials, const at::Tensor& slot_of,
   return out;
 }
 
+// the router of FusedPackedMoE.forward (fused_packed_moe.py:195-199), T <= 8 tokens:
+// (w [T, top_k] fp32, sel [T, top_k] int32); workspace from duplex_moe_workspace_bytes,
+// zero-filled once
+std::tuple<at::Tensor, at::Tensor> moe_route(const at::Tensor& x, const at::Tensor& gate_w,
+                                             const std::optional<at::Tensor>& gate_b, int64_t top_k,
+                                             bool norm_topk, const at::Tensor& workspace) {
+  require(x, "x");
+  require(gate_w, "gate_w");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t T = x.size(0), H = x.size(1), E = gate_w.size(0);
+  at::Tensor w = at::empty({T, top_k}, x.options().dtype(at::kFloat));
+  at::Tensor sel = at::empty({T, top_k}, x.options().dtype(at::kInt));
+  check(duplex_moe_route(x.data_ptr(), act_code(x.scalar_type()), (int32_t)T, gate_w.data_ptr(),
+                         opt_ptr(gate_b), (int32_t)E, (int32_t)H, (int32_t)top_k, norm_topk ? 1 : 0,
+                         w.data_ptr<float>(), sel.data_ptr<int32_t>(), workspace.data_ptr(),
+                         (size_t)workspace.numel(), 0.f, 0, stream()),
+        "moe_route");
+  return {w, sel};
+}
+
+// the Talker's MoE block (fused_moe.py:40-141), T <= 8 tokens
+at::Tensor talker_moe(const at::Tensor& x, const at::Tensor& gate_w, const at::Tensor& gate_up,
+                      const at::Tensor& down, const std::optional<at::Tensor>& gu_scale,
+                      const std::optional<at::Tensor>& dn_scale, int64_t top_k, bool norm_topk,
+                      const std::optional<at::Tensor>& sh_gate, const std::optional<at::Tensor>& sh_up,
+                      const std::optional<at::Tensor>& sh_down,
+                      const std::optional<at::Tensor>& sh_gate_w, const at::Tensor& workspace,
+                      const at::Tensor& err) {
+  require(x, "x");
+  require(gate_up, "gate_up");
+  require(down, "down");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t T = x.size(0), H = x.size(1), E = gate_up.size(0), I = gate_up.size(1) / 2;
+  const int64_t S = sh_gate.has_value() ? sh_gate->size(0) : 0;
+  at::Tensor out = at::empty_like(x);
+  check(duplex_talker_moe_forward(
+            x.data_ptr(), act_code(x.scalar_type()), (int32_t)T, gate_w.data_ptr(), (int32_t)E,
+            (int32_t)H, (int32_t)I, (int32_t)top_k, norm_topk ? 1 : 0, gate_up.data_ptr(),
+            down.data_ptr(), gate_up.scalar_type() == at::kChar ? 1 : 0, opt_ptr(gu_scale),
+            opt_ptr(dn_scale), opt_ptr(sh_gate), opt_ptr(sh_up), opt_ptr(sh_down), (int32_t)S,
+            opt_ptr(sh_gate_w), out.data_ptr(), nullptr, nullptr, workspace.data_ptr(),
+            (size_t)workspace.numel(), err.data_ptr<int32_t>(), stream()),
+        "talker_moe");
+  return out;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(duplex_b200, m) {
@@ -207,6 +253,11 @@ TORCH_LIBRARY(duplex_b200, m) {
         "Tensor(a!) send, Tensor(b!) slot_of) -> ()");
   m.def("ep_combine(Tensor partials, Tensor slot_of, Tensor? residual, ScalarType out_dtype) "
         "-> Tensor");
+  m.def("moe_route(Tensor x, Tensor gate_w, Tensor? gate_b, int top_k, bool norm_topk, "
+        "Tensor workspace) -> (Tensor, Tensor)");
+  m.def("talker_moe(Tensor x, Tensor gate_w, Tensor gate_up, Tensor down, Tensor? gu_scale, "
+        "Tensor? dn_scale, int top_k, bool norm_topk, Tensor? sh_gate, Tensor? sh_up, "
+        "Tensor? sh_down, Tensor? sh_gate_w, Tensor workspace, Tensor err) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(duplex_b200, CUDA, m) {
@@ -218,4 +269,6 @@ TORCH_LIBRARY_IMPL(duplex_b200, CUDA, m) {
   m.impl("moe_grouped", &moe_grouped);
   m.impl("ep_dispatch", &ep_dispatch);
   m.impl("ep_combine", &ep_combine);
+  m.impl("moe_route", &moe_route);
+  m.impl("talker_moe", &talker_moe);
 }

@@ -169,7 +169,7 @@ def test_torch_library_ops_are_registered():
     ops = _lib.load_torch_ops()
     import torch
     for name in ("unpack4", "dequant", "dequant_gemv", "packed_linear", "moe_forward",
-                 "moe_grouped", "ep_dispatch", "ep_combine"):
+                 "moe_grouped", "ep_dispatch", "ep_combine", "moe_route", "talker_moe"):
         op = getattr(ops, name)
         assert isinstance(op.default, torch._ops.OpOverload), name
     assert "Tensor(a!) send" in str(ops.ep_dispatch.default._schema)

@@ -48,3 +48,35 @@ def test_torch_ops_match_the_oracle(cuda):
                          L["dn_scale"], L["gu_zeros"], L["dn_zeros"])
     assert np.abs(out.float().cpu().numpy() - yref).max() <= 2e-3 * np.abs(yref).max()
     assert m.device_errors() == 0
+
+
+def test_route_and_talker_ops(cuda):
+    """torch.ops.duplex_b200.moe_route against the oracle's router (same ids and weights,
+    a token on a rounding boundary excepted), and talker_moe equal, bit for bit, to the
+    module's forward."""
+    import torch
+    from duplex import _lib
+    from duplex.streaming.fused_moe import FusedMoE
+    from test_talker_moe import golden_block
+    from test_gpu_talker import to_dev
+    ops = torch.ops.duplex_b200
+    L = synth.moe_layer_np(seed=31, T=4)
+    x = torch.from_numpy(L["x"]).to(cuda)
+    n = _lib.ctypes.c_size_t()
+    _lib.call("duplex_moe_workspace_bytes", 4, 128, 2048, 768, 8, _lib.ctypes.byref(n))
+    ws = torch.zeros(n.value, dtype=torch.uint8, device=cuda)
+    w, sel = ops.moe_route(x, torch.from_numpy(L["gate_w"]).to(cuda), None, 8, True, ws)
+    wr, selr, _ = O.router(L["x"], L["gate_w"], 8, True, None, "float16")
+    same = [np.array_equal(a, b) for a, b in zip(sel.cpu().numpy(), selr)]
+    assert sum(same) >= len(same) - 1      # a logit on a rounding boundary may flip one token
+    for t in np.flatnonzero(same):
+        assert np.abs(w.cpu().numpy()[t] - wr[t]).max() <= 1e-6
+    m = FusedMoE(to_dev(golden_block(), cuda)).to(cuda)
+    xt = torch.randn(3, m.hidden, device=cuda).to(torch.bfloat16)
+    ref = m(xt)
+    se = m.shared_expert
+    out = ops.talker_moe(xt, m.gate.weight.detach(), m.gate_up, m.down, None, None, m.top_k,
+                         m.norm_topk_prob, se.gate_proj.weight.detach(), se.up_proj.weight.detach(),
+                         se.down_proj.weight.detach(), m.shared_expert_gate.weight.detach(),
+                         m._workspace(3, cuda), m.err)
+    assert torch.equal(out, ref)
