@@ -182,7 +182,7 @@ def run_reference(args):
 # ------------------------------------------------------------------ GPU arm
 def init_group(local):
     """NCCL group of the torchrun ranks (a group of one without torchrun), with a
-    non-blocking communicator and a 180 s collective timeout (duplex.benchutil)."""
+    180 s collective timeout watched by torch's NCCL watchdog (duplex.benchutil)."""
     import torch
     import torch.distributed as dist
     from duplex import benchutil as bu

@@ -28,11 +28,15 @@ def init_dist(backend: str, timeout_s: int = 120):
 
 
 def init_nccl(device, timeout_s: int = 180):
-    """NCCL process group of the torchrun ranks with a NON-BLOCKING communicator: NCCL
-    calls return at once and report errors asynchronously; torch's watchdog polls them
-    (ncclCommGetAsyncError) and aborts the communicator when a collective exceeds
-    `timeout_s`, so a rank that dies makes the others' next collective fail instead of
-    hanging.  A group of one when not launched by torchrun."""
+    """NCCL process group of the torchrun ranks (a group of one when not launched by
+    torchrun), with a `timeout_s` collective timeout: torch's watchdog polls the
+    communicators' asynchronous errors (ncclCommGetAsyncError) and aborts a communicator
+    whose collective outlives the timeout, so a rank that dies makes the others' next
+    collective fail instead of hanging.  duplex.health adds the host-side guards: a
+    heartbeat that finds a departed rank before the next launch, and a step guard that
+    aborts the group.  The communicators are blocking: with `config.blocking = 0` this
+    torch build's all-to-all raised "NCCL Error 7: operation in progress" on 2 and 4 B200s.
+    """
     import socket
     if "WORLD_SIZE" not in os.environ:
         s = socket.socket()
@@ -43,12 +47,8 @@ def init_nccl(device, timeout_s: int = 180):
                           MASTER_PORT=str(port))
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
     os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "1")
-    opts = dist.ProcessGroupNCCL.Options()
-    opts.config.blocking = 0
-    dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=timeout_s),
-                            pg_options=opts)
-    # a non-blocking communicator finishes its set-up on NCCL's own thread: complete it
-    # with one collective now, before any stream capture begins
+    dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=timeout_s))
+    # set the communicator up with one collective now, before any stream capture begins
     t = torch.ones(1, device=device)
     dist.all_reduce(t)
     torch.cuda.synchronize(device)

@@ -13,9 +13,9 @@ the host, neither needing a GPU fault to test:
   collective of step s, so no collective ever waits on a peer that is gone.
 * `guard_step` -- waits for the step's completion event on the host under a timeout.
   On expiry it aborts the group's communicators (ncclCommAbort through torch, which
-  also stops collectives in flight) and raises `StepTimeout`.  The communicators are
-  non-blocking (duplex.benchutil.init_nccl), so torch's watchdog additionally polls
-  their asynchronous errors.
+  also stops collectives in flight) and raises `StepTimeout`.  torch's NCCL watchdog
+  additionally polls the communicators' asynchronous errors and aborts a collective that
+  outlives the group's timeout (duplex.benchutil.init_nccl).
 """
 
 from __future__ import annotations

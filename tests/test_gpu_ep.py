@@ -149,7 +149,7 @@ def _ep_rank(rank, world, port, q, T_l):
     dev = torch.device("cuda", rank)
     torch.cuda.set_device(dev)
     os.environ.update(WORLD_SIZE=str(world), RANK=str(rank), LOCAL_RANK=str(rank))
-    bu.init_nccl(dev, timeout_s=60)        # non-blocking communicator
+    bu.init_nccl(dev, timeout_s=60)
     L = synth.moe_layer_np(seed=60, E=128, H=2048, I=768, top_k=8, group=128, zero_points=True,
                            T=world * T_l)
     x_full = O.round_to(L["x"].astype(np.float32), "float16")
