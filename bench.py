@@ -77,10 +77,13 @@ def traffic(key):
     return None
 
 
-def ep_config(n):
+def ep_config(n, exchange="peer"):
+    how = ("dispatch and combine as NVLink peer stores from the pack and return kernels, "
+           "with flags" if exchange == "peer" else "all-to-all dispatch and combine over NCCL")
     return {"workload": "config 4: 48-layer Thinker MoE stack, 256 decode streams, the 128 "
-                        f"experts of every layer split over {n} GPU(s); all-to-all dispatch "
-                        "and combine over NCCL",
+                        f"experts of every layer split over {n} GPU(s); "
+                        + (how if n > 1 else "one GPU: no exchange"),
+            "exchange": exchange if n > 1 else None,
             "layers": EP_LAYERS, "streams": EP_STREAMS, "streams_per_gpu": EP_STREAMS // n,
             "experts": 128, "experts_per_gpu": 128 // n, "top_k": 8, "hidden": HIDDEN,
             "moe_inter": 768, "group": 128, "zero_points": True, "activations": "fp16",
@@ -248,7 +251,8 @@ def run_ours(args):
         m = synth.moe_layer_torch(gen, device=dev)
         layers.append(ExpertParallelMoE(m["gate_w"], m["gu_packed"], m["gu_scale"], m["dn_packed"],
                                         m["dn_scale"], synth.THINKER_ACTIVE, gu_zeros=m["gu_zeros"],
-                                        dn_zeros=m["dn_zeros"], dtype=torch.float16, device=dev))
+                                        dn_zeros=m["dn_zeros"], dtype=torch.float16, device=dev,
+                                        exchange=args.exchange))
         del m
     torch.cuda.empty_cache()
     gen = torch.Generator(device=dev).manual_seed(7 + rank)
@@ -300,6 +304,8 @@ def run_ours(args):
     e2e_value = EP_STREAMS * K / (ms_e2e / 1e3)
     clocks = sampler.stop().summary() if sampler else None
     del g
+    for L in layers:
+        L.close()
     layers.clear()
     outs = None
     torch.cuda.empty_cache()
@@ -348,7 +354,7 @@ def run_ours(args):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "int4 weights x f16 activations, f32 accumulate",
         "data": "synthetic (seeded; BASELINE config distributions)",
-        "config": ep_config(ws),
+        "config": ep_config(ws, args.exchange),
         "ep_hbm": {"bytes_per_layer_per_gpu": ep_bytes,
                    "GBps": ep_bytes / (us_layer * 1e3), "frac": ep_bytes / (us_layer * 1e3) / peak,
                    "note": "bytes of the selected local experts (tile records) per layer per GPU"},
@@ -392,6 +398,9 @@ def main():
                          "(duplex/batched_bench.py); gemv: config 1 (duplex/gemv_bench.py); "
                          "talker: the Talker MoE (duplex/talker_bench.py)")
     ap.add_argument("--streams", type=int, default=256, help="batched: concurrent streams")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="config 4 at N > 1: dispatch / combine over NVLink peer stores (one "
+                         "pack-and-send kernel, flags, bounded waits) or NCCL all-to-alls")
     args = ap.parse_args()
     if args.workload == "batched" and args.impl == "ours":
         from duplex import batched_bench

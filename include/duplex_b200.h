@@ -266,6 +266,36 @@ int duplex_ep_combine(const float* partials, const int32_t* slot_of, int32_t T, 
                       int32_t H, const void* residual, void* out, int act_dtype, void* stream);
 
 /*
+ * Peer exchange of the expert-parallel layer over NVLink (the NCCL all-to-alls' stand-in):
+ * buffers allocated with ipc_alloc (cudaMalloc, zero-filled, with a CUDA IPC handle of
+ * ipc_handle_bytes() bytes), shared through the host's process group and opened on every
+ * other rank with ipc_open (plain peer mappings: no NVLink multicast object).
+ * ep_dispatch_peer is ep_dispatch_pack writing block d straight into destination d's
+ * receive buffer (recv_peers[d], at block `rank`); ep_put_peer copies block d of `src`
+ * (n_ranks blocks of block_bytes) into dst_peers[d] at block `rank`.  Both end with the
+ * last CTA writing the exchange's epoch (counted in `epoch`, local) into slot `rank` of
+ * every destination's flag array (flag_peers[d]); ep_wait waits on this rank's own
+ * flag array until every slot holds the epoch, bounded by wait_limit_cycles (<= 0:
+ * about 2 s), after which it sets DUPLEX_DEVERR_TIMEOUT and returns instead of hanging.
+ * recv_peers / dst_peers / flag_peers are DEVICE arrays of n_ranks pointers.
+ */
+int duplex_ipc_handle_bytes(void);
+int duplex_ipc_alloc(size_t bytes, void** ptr, void* handle);
+int duplex_ipc_open(const void* handle, void** ptr);
+int duplex_ipc_close(void* ptr);
+int duplex_ipc_free(void* ptr);
+int duplex_ep_dispatch_peer(const void* rows, int64_t row_bytes, int32_t T, int32_t top_k,
+                            int32_t E, int32_t n_ranks, int32_t rank, int64_t ids_offset,
+                            void* const* recv_peers, int32_t* slot_of,
+                            unsigned* const* flag_peers, unsigned* counter, unsigned* epoch,
+                            void* stream);
+int duplex_ep_put_peer(const void* src, int64_t block_bytes, int32_t n_ranks, int32_t rank,
+                       void* const* dst_peers, unsigned* const* flag_peers, unsigned* counter,
+                       unsigned* epoch, void* stream);
+int duplex_ep_wait(const unsigned* flags, const unsigned* epoch, int32_t n_ranks,
+                   int64_t wait_limit_cycles, int32_t* err, void* stream);
+
+/*
  * talker_moe_forward -- the Talker's MoE block, `FusedMoE.forward` of the reference
  * (src/duplex/streaming/fused_moe.py:40-141), for T <= 8 tokens: router (as moe_route),
  * the selected experts' gate|up with SiLU(gate) * up, down, the routing-weighted sum over

@@ -95,6 +95,16 @@ _SIGNATURES = {
                                  _c_ptr, _c_ptr], _c_int),
     "duplex_ep_combine": ([_c_ptr, _c_ptr, _c_i32, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_int, _c_ptr],
                           _c_int),
+    "duplex_ipc_handle_bytes": ([], _c_int),
+    "duplex_ipc_alloc": ([_c_size, ctypes.POINTER(ctypes.c_void_p), _c_ptr], _c_int),
+    "duplex_ipc_open": ([_c_ptr, ctypes.POINTER(ctypes.c_void_p)], _c_int),
+    "duplex_ipc_close": ([_c_ptr], _c_int),
+    "duplex_ipc_free": ([_c_ptr], _c_int),
+    "duplex_ep_dispatch_peer": ([_c_ptr, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i64,
+                                 _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr], _c_int),
+    "duplex_ep_put_peer": ([_c_ptr, _c_i64, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr],
+                           _c_int),
+    "duplex_ep_wait": ([_c_ptr, _c_ptr, _c_i32, _c_i64, _c_ptr, _c_ptr], _c_int),
     "duplex_talker_moe_workspace_bytes": ([_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
                                            ctypes.POINTER(ctypes.c_size_t)], _c_int),
     "duplex_talker_moe_forward": ([_c_ptr, _c_int, _c_i32, _c_ptr, _c_i32, _c_i32, _c_i32, _c_i32,

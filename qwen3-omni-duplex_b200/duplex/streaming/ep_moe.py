@@ -3,7 +3,8 @@ process group (one process per GPU), tokens data-parallel.
 
 The reference runs every expert on one GPU (`src/duplex/streaming/fused_packed_moe.py`);
 this is the multi-GPU form of the same layer, `FusedPackedMoE.forward` semantics per
-token, for batched decode (many streams per rank).  Per layer on every rank:
+token, for batched decode (many streams per rank).  Per layer on every rank (with
+exchange="peer" steps 2-4 run over NVLink peer memory instead: PeerExchange):
 
   1. route the rank's own tokens over all E experts (router logits, fp32 softmax,
      top-k, renormalise: `duplex_moe_route_grouped`), whose top-k kernel writes each
@@ -45,8 +46,102 @@ def exchange_row_bytes(H: int, elt: int, top_k: int) -> int:
     return -(-(H * elt + 8 * top_k) // 16) * 16
 
 
+class _DeviceArray:
+    """A raw device allocation seen by torch (no copy, no ownership)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (ptr, False), "version": 3}
+
+
+class PeerExchange:
+    """The two exchanges of an expert-parallel layer over NVLink peer memory, in place of
+    the NCCL all-to-alls: every rank allocates its receive buffer [N, T_l, row], its
+    return buffer [N, T_l, H] fp32 and a flag block with cudaMalloc (duplex_ipc_alloc),
+    the CUDA IPC handles go round the process group, and every rank maps the others'
+    buffers (duplex_ipc_open: plain peer mappings, no multicast object).  dispatch()
+    packs each destination's rows straight into that destination's receive buffer
+    (duplex_ep_dispatch_peer: the pack and the exchange are one kernel) and waits for
+    every source's epoch in its own flags (duplex_ep_wait, bounded); give_back() puts the
+    partial rows into their owners' return buffers and waits the same way.  A sender
+    writes a destination's buffer again only after that destination's next signal to it,
+    which it sends after it has read the buffer, so one buffer per exchange suffices."""
+
+    def __init__(self, group, T_l: int, row_bytes: int, H: int, E: int, device):
+        self.group = group
+        self.E = E
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.T_l, self.row_bytes, self.H = T_l, row_bytes, H
+        N = self.world
+        lib = _lib.load()
+        hb = lib.duplex_ipc_handle_bytes()
+        sizes = (N * T_l * row_bytes, N * T_l * H * 4, (2 * N + 8) * 4)
+        self._own, handles = [], []
+        for n in sizes:
+            h = _lib.ctypes.create_string_buffer(hb)
+            ptr = _lib.ctypes.c_void_p()
+            _lib.call("duplex_ipc_alloc", n, _lib.ctypes.byref(ptr), h)
+            self._own.append(ptr.value)
+            handles.append(h.raw)
+        allh = [None] * N
+        dist.all_gather_object(allh, handles, group=group)
+        self._opened = []
+        peers = []
+        for r in range(N):
+            if r == self.rank:
+                peers.append(list(self._own))
+                continue
+            row = []
+            for h in allh[r]:
+                ptr = _lib.ctypes.c_void_p()
+                _lib.call("duplex_ipc_open", _lib.ctypes.create_string_buffer(h, hb),
+                          _lib.ctypes.byref(ptr))
+                self._opened.append(ptr.value)
+                row.append(ptr.value)
+            peers.append(row)
+        dev = torch.device(device)
+        i64 = lambda v: torch.tensor(v, dtype=torch.int64, device=dev)  # noqa: E731
+        self.recv_peers = i64([p[0] for p in peers])
+        self.back_peers = i64([p[1] for p in peers])
+        self.fdisp_peers = i64([p[2] for p in peers])
+        self.fcomb_peers = i64([p[2] + 4 * N for p in peers])
+        f = self._own[2]
+        self.fdisp, self.fcomb = f, f + 4 * N
+        self.disp_counter, self.disp_epoch = f + 8 * N, f + 8 * N + 4
+        self.comb_counter, self.comb_epoch = f + 8 * N + 8, f + 8 * N + 12
+        self.recv = torch.as_tensor(_DeviceArray(self._own[0], (N, T_l, row_bytes), "|u1"), device=dev)
+        self.back = torch.as_tensor(_DeviceArray(self._own[1], (N, T_l, H), "<f4"), device=dev)
+
+    def dispatch(self, rows, top_k: int, ids_offset: int, slot_of, err):
+        st = _lib.stream_of(rows)
+        _lib.call("duplex_ep_dispatch_peer", _lib.ptr(rows), rows.stride(0), self.T_l, top_k, self.E,
+                  self.world, self.rank, ids_offset, _lib.ptr(self.recv_peers), _lib.ptr(slot_of),
+                  _lib.ptr(self.fdisp_peers), self.disp_counter, self.disp_epoch, st)
+        _lib.call("duplex_ep_wait", self.fdisp, self.disp_epoch, self.world, 0, _lib.ptr(err), st)
+        return self.recv
+
+    def give_back(self, partial, err):
+        st = _lib.stream_of(partial)
+        _lib.call("duplex_ep_put_peer", _lib.ptr(partial), self.T_l * self.H * 4, self.world,
+                  self.rank, _lib.ptr(self.back_peers), _lib.ptr(self.fcomb_peers),
+                  self.comb_counter, self.comb_epoch, st)
+        _lib.call("duplex_ep_wait", self.fcomb, self.comb_epoch, self.world, 0, _lib.ptr(err), st)
+        return self.back
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (after a device synchronise, and
+        before the process group goes)."""
+        torch.cuda.synchronize()
+        for ptr in self._opened:
+            _lib.call("duplex_ipc_close", ptr)
+        for ptr in self._own:
+            _lib.call("duplex_ipc_free", ptr)
+        self._opened, self._own = [], []
+
+
 def ep_forward(x, route_fn, pack_fn, experts_fn, combine_fn, top_k: int, group=None,
-               residual=None, bufs=None):
+               residual=None, bufs=None, peer=None, err=None):
     """Host side of one expert-parallel layer on this rank.
 
     x [T_local, H].  route_fn(x, rows) fills rows [T_local, row] uint8 with each token's
@@ -72,6 +167,16 @@ def ep_forward(x, route_fn, pack_fn, experts_fn, combine_fn, top_k: int, group=N
             b["recv"] = torch.empty(world, T_l, row, dtype=torch.uint8, device=dev)
             b["back"] = torch.empty(world, T_l, H, dtype=torch.float32, device=dev)
     route_fn(x, b["rows"])
+    if peer is not None and world > 1:
+        # the pack writes into the destinations' receive buffers; the partials go back
+        # into the owners' return buffers (NVLink peer stores, flags, bounded waits)
+        recv = peer.dispatch(b["rows"], top_k, xbytes, b["slot_of"], err)
+        rv = recv.view(world * T_l, row)
+        x_all = rv[:, :xbytes].view(x.dtype)
+        sel_all = rv[:, xbytes:xbytes + 4 * top_k].view(torch.int32)
+        w_all = rv[:, xbytes + 4 * top_k:xbytes + 8 * top_k].view(torch.float32)
+        partial = experts_fn(x_all, sel_all, w_all).view(world, T_l, H)
+        return combine_fn(peer.give_back(partial, err), b["slot_of"], residual)
     if world == 1:
         # one rank: every token goes to it, in order, so the block IS the routed rows and
         # the all-to-all is the identity -- no pack, no exchange
@@ -105,10 +210,13 @@ class ExpertParallelMoE(nn.Module):
 
     def __init__(self, gate_weight, gu_packed, gu_scale, dn_packed, dn_scale, top_k,
                  gu_zeros=None, dn_zeros=None, norm_topk_prob=True, gate_bias=None,
-                 dtype=torch.float16, device="cuda", group=None):
+                 dtype=torch.float16, device="cuda", group=None, exchange: str = "nccl"):
         super().__init__()
         if dtype not in (torch.float16, torch.bfloat16):
             raise _lib.DuplexError("ExpertParallelMoE runs fp16 or bf16 modules")
+        if exchange not in ("nccl", "peer"):
+            raise _lib.DuplexError("exchange is 'nccl' (all-to-alls) or 'peer' (NVLink peer stores)")
+        self.exchange = exchange
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -222,9 +330,21 @@ class ExpertParallelMoE(nn.Module):
         if T > 512:
             raise _lib.DuplexError("ExpertParallelMoE takes at most 512 tokens per rank")
         bufs = self._ws.setdefault(("ep", T), {})
+        peer = None
+        if self.exchange == "peer" and self.world > 1:
+            peer = self._ws.get(("peer", T))
+            if peer is None:   # collective: every rank builds it on its first call of a shape
+                row = exchange_row_bytes(self.hidden, x.element_size(), self.top_k)
+                peer = PeerExchange(self.group, T, row, self.hidden, self.num_experts, x.device)
+                self._ws[("peer", T)] = peer
         return ep_forward(x, lambda xt, rows: self.route(xt, rows), self.pack,
                           self.local_experts, lambda back, slot_of, res: self.combine(back, slot_of, res),
-                          self.top_k, self.group, residual, bufs)
+                          self.top_k, self.group, residual, bufs, peer=peer, err=self.err)
+
+    def close(self) -> None:
+        """Release the peer exchange buffers (before the process group is destroyed)."""
+        for key in [k for k in self._ws if k[0] == "peer"]:
+            self._ws.pop(key).close()
 
     def device_errors(self) -> int:
         v = int(self.err.item())

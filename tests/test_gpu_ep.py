@@ -210,6 +210,75 @@ def test_expert_parallel_module_two_ranks(cuda):
         assert err <= 1e-3 and oerr <= TOL and derr == 0 and same
 
 
+def _peer_rank(rank, world, port, q):
+    """The NVLink peer exchange against the NCCL all-to-alls on the same weights and
+    tokens: bit-identical outputs, eagerly (three calls) and in a CUDA graph replayed."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      WORLD_SIZE=str(world), RANK=str(rank), LOCAL_RANK=str(rank))
+    import torch.distributed as dist
+    from duplex import benchutil as bu
+    from duplex.streaming.ep_moe import ExpertParallelMoE
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    bu.init_nccl(dev, timeout_s=60)
+    L = synth.moe_layer_np(seed=62, E=128, H=2048, I=768, top_k=8, group=128, zero_points=True,
+                           T=world * 32)
+    args = [T(L[n], dev) for n in ("gate_w", "gu_packed", "gu_scale", "dn_packed", "dn_scale")]
+    kw = dict(gu_zeros=T(L["gu_zeros"], dev), dn_zeros=T(L["dn_zeros"], dev), dtype=torch.float16,
+              device=dev)
+    ref = ExpertParallelMoE(*args, 8, **kw)
+    mods = [ExpertParallelMoE(*args, 8, exchange="peer", **kw) for _ in range(2)]
+    x = T(L["x"][rank * 32:(rank + 1) * 32], dev, torch.float16)
+    res = T(np.random.default_rng(rank).standard_normal((32, 2048)).astype(np.float16), dev)
+    want = ref(x, residual=res)
+    eager = [mods[0](x, residual=res) for _ in range(3)]
+    ok_eager = all(bool(torch.equal(y, want)) for y in eager)
+    outs = [None, None]
+
+    def step():   # two peer layers back to back, as in the bench
+        outs[0] = mods[0](x, residual=res)
+        outs[1] = mods[1](outs[0])
+    s_ = torch.cuda.Stream(dev)
+    s_.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s_):
+        step()
+    torch.cuda.current_stream(dev).wait_stream(s_)
+    torch.cuda.synchronize()
+    want1 = ref(want)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s_, capture_error_mode="thread_local"):
+        step()
+    ok_graph = True
+    for _ in range(3):
+        g.replay()
+        torch.cuda.synchronize()
+        ok_graph &= bool(torch.equal(outs[0], want)) and bool(torch.equal(outs[1], want1))
+    derr = sum(m.device_errors() for m in mods)
+    del g
+    for m in mods:
+        m.close()
+    q.put((rank, ok_eager, ok_graph, derr))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_exchange_matches_the_nccl_all_to_alls(cuda):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_peer_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted(q.get(timeout=300) for _ in ps)
+    for p in ps:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, ok_eager, ok_graph, derr in res:
+        assert ok_eager and ok_graph and derr == 0, (rank, ok_eager, ok_graph, derr)
+
+
 def _leave_rank(rank, world, port, q):
     """Heartbeat-gated expert-parallel steps on `world` GPUs; the last rank leaves after
     step 1 has completed (nothing of it in flight).  The others must raise PeerLost in
