@@ -91,6 +91,15 @@ def ep_config(n, exchange="peer"):
             "l2": "no flush: a step streams 48 x 314/N MB of distinct experts (> 126 MB L2)"}
 
 
+def ep_launches_per_layer(n, exchange="peer"):
+    """Our kernels launched per layer of the config-4 step: route (router, top-k), expert
+    stage (bucketing, gate|up, down, expert combine), rank combine; at N > 1 the dispatch
+    pack, and with the peer exchange the dispatch wait, the give-back put and its wait."""
+    if n == 1:
+        return 7
+    return 11 if exchange == "peer" else 8
+
+
 # ------------------------------------------------------------------ CPU (oracle) arms
 def cpu_layer_sample(seed=5, T=EP_STREAMS):
     from duplex import synth
@@ -371,9 +380,11 @@ def run_ours(args):
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "tokens/s",
                 "h2d_bytes_per_step": T_l * HIDDEN * 2, "d2h_bytes_per_step": T_l * HIDDEN * 2},
-        "gpu_launches": (8 if ws > 1 else 7) * EP_LAYERS * K,
-        "gpu_launches_note": "per layer: router, top-k, dispatch pack (N > 1), bucketing, gate|up, "
-                             "down, expert combine, rank combine (+ 2 NCCL all-to-alls at N > 1)",
+        "gpu_launches": ep_launches_per_layer(ws, args.exchange) * EP_LAYERS * K,
+        "gpu_launches_note": "per layer: router, top-k, bucketing, gate|up, down, expert combine, "
+                             "rank combine; at N > 1 also the dispatch pack, and with the peer "
+                             "exchange its wait, the give-back put and its wait (the NCCL form "
+                             "adds 2 all-to-alls instead)",
         "clocks": clocks,
         "device_errors": derr,
     }
