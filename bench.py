@@ -27,9 +27,10 @@ Beside it, on every rank (reported from the max over ranks):
   cpu_baseline  (rank 0, N = 1) the oracle (numpy restatement of the reference's
             dequant + gather-bmm) on two layer samples of the same workload.
 
---workload clock | batched | gemv | talker select the other configs' lines (clock:
-config 2 as the headline; batched: config 3, duplex/batched_bench.py; gemv: config 1,
-duplex/gemv_bench.py; talker: the Talker's bf16 / int8 MoE, duplex/talker_bench.py).
+--workload clock | batched | gemv | talker | staged select the other configs' lines
+(clock: config 2 as the headline; batched: config 3, duplex/batched_bench.py; gemv:
+config 1, duplex/gemv_bench.py; talker: the Talker's bf16 / int8 MoE,
+duplex/talker_bench.py; staged: host-resident layers, duplex/staged_bench.py).
 
 --impl reference times the reference algorithm on the host cores for the headline
 workload: rank 0 alone (other ranks exit), each step one of the 48 layers for all 256
@@ -403,11 +404,13 @@ def main():
     ap.add_argument("--soak", type=float, default=1.0, help="seconds of load before timing")
     ap.add_argument("--cpu-samples", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["ep", "clock", "batched", "gemv", "talker"], default="ep",
+    ap.add_argument("--workload", choices=["ep", "clock", "batched", "gemv", "talker", "staged"],
+                    default="ep",
                     help="ep: config 4, the default line (see the module docstring); clock: "
                          "config 2 as the line (duplex/clock_bench.py); batched: config 3 "
                          "(duplex/batched_bench.py); gemv: config 1 (duplex/gemv_bench.py); "
-                         "talker: the Talker MoE (duplex/talker_bench.py)")
+                         "talker: the Talker MoE (duplex/talker_bench.py); staged: host-resident "
+                         "layers (duplex/staged_bench.py)")
     ap.add_argument("--streams", type=int, default=256, help="batched: concurrent streams")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="config 4 at N > 1: dispatch / combine over NVLink peer stores (one "
@@ -421,6 +424,9 @@ def main():
         from duplex import gemv_bench
         raise SystemExit(gemv_bench.main(["--steps", str(args.steps), "--warmup", str(args.warmup),
                                           "--impl", args.impl]))
+    if args.workload == "staged":
+        from duplex import staged_bench
+        raise SystemExit(staged_bench.main(["--steps", str(args.steps), "--warmup", str(args.warmup)]))
     if args.workload == "talker":
         from duplex import talker_bench
         raise SystemExit(talker_bench.main(["--steps", str(args.steps), "--warmup", str(args.warmup)]))

@@ -164,6 +164,34 @@ int duplex_moe_forward(const void* x, int act_dtype, int32_t T, const void* gate
                        int32_t* err, float rms_eps, int pdl, void* stream);
 
 /*
+ * Host-resident experts -- the reference's `FusedPackedMoE(host_resident=True)` layers
+ * (fused_packed_moe.py:130-164 staging blobs, :233-253 per-token copies).
+ * host_alloc: mapped pinned host memory (cudaHostAllocMapped | cudaHostAllocPortable);
+ * *host_ptr is for host code, *dev_ptr the address kernels read it at.  host_free
+ * releases it (host pointer).
+ * moe_forward_staged: duplex_moe_forward with the expert tile records (same layout)
+ * in host memory: gu_tiles_host / dn_tiles_host are DEVICE addresses of mapped pinned
+ * memory (host_alloc's dev_ptr).  The router writes the unit plan, one kernel copies
+ * the records of the planned experts from host memory into the slots of `stage`
+ * (duplex_moe_stage_bytes), and the expert kernels run on the slots: no host
+ * synchronisation, bit-identical output to duplex_moe_forward on resident records.
+ * The expert kernels follow the router in plain stream order (pdl applies to the
+ * router only).  One call at a time per stage buffer and per workspace.
+ */
+int duplex_host_alloc(size_t bytes, void** host_ptr, void** dev_ptr);
+int duplex_host_free(void* host_ptr);
+int duplex_moe_stage_bytes(int32_t T, int32_t E, int32_t H, int32_t I, int32_t top_k,
+                           int32_t group, int has_zeros, size_t* bytes);
+int duplex_moe_forward_staged(const void* x, int act_dtype, int32_t T, const void* gate_w,
+                              const void* gate_b, int32_t E, int32_t H, int32_t I,
+                              int32_t top_k, int32_t norm_topk, const void* gu_tiles_host,
+                              const void* dn_tiles_host, int scale_dtype, int has_zeros,
+                              int32_t group, const void* residual, void* out, float* w_out,
+                              int32_t* sel_out, void* workspace, size_t workspace_bytes,
+                              void* stage, size_t stage_bytes, int32_t* err, float rms_eps,
+                              int pdl, void* stream);
+
+/*
  * moe_grouped_workspace_bytes -- scratch of duplex_moe_grouped for T tokens (logits,
  * selection, the expert-sorted assignment list, the unit list and one fp32 output row
  * per (token, slot)).  No zero fill needed.  Returns DUPLEX_ERR_UNSUPPORTED for a

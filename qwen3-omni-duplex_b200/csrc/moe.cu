@@ -308,6 +308,23 @@ static RouteParams make_route(const void* x, int T, const void* gate_w, const vo
   return rp;
 }
 
+// The router step of duplex_moe_forward with all of its argument checks: w / sel and
+// the unit plan into the workspace.  Used by the host-resident path (staging.cu),
+// which then stages the planned experts before the expert kernels run.
+int moe_route_checked(const void* x, int act_dtype, int T, const void* gate_w, const void* gate_b,
+                      int E, int H, int I, int top_k, int norm_topk, float* w_out,
+                      int32_t* sel_out, void* workspace, size_t workspace_bytes, int* err,
+                      float rms_eps, bool pdl, cudaStream_t st) {
+  int rc = check_route(x, act_dtype, T, gate_w, E, H, top_k, workspace, workspace_bytes, I);
+  if (rc) return rc;
+  if (I < 16) return DUPLEX_ERR_ARG;
+  const MoeScratch L = moe_scratch_layout(T, E, H, I, top_k);
+  RouteParams rp = make_route(x, T, gate_w, gate_b, E, H, top_k, norm_topk, rms_eps, w_out,
+                              sel_out, reinterpret_cast<uint8_t*>(workspace), L);
+  rp.err = err;
+  return launch_route(act_dtype, rp, pdl, st);
+}
+
 }  // namespace duplex
 
 using namespace duplex;

@@ -47,6 +47,15 @@ _SIGNATURES = {
                             _c_i32, _c_i32, _c_ptr, _c_ptr, _c_int, _c_int, _c_i32, _c_ptr,
                             _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr, _c_f32, _c_int,
                             _c_ptr], _c_int),
+    "duplex_host_alloc": ([_c_size, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)],
+                          _c_int),
+    "duplex_host_free": ([_c_ptr], _c_int),
+    "duplex_moe_stage_bytes": ([_c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_int,
+                                ctypes.POINTER(ctypes.c_size_t)], _c_int),
+    "duplex_moe_forward_staged": ([_c_ptr, _c_int, _c_i32, _c_ptr, _c_ptr, _c_i32, _c_i32, _c_i32,
+                                   _c_i32, _c_i32, _c_ptr, _c_ptr, _c_int, _c_int, _c_i32, _c_ptr,
+                                   _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr, _c_size, _c_ptr,
+                                   _c_f32, _c_int, _c_ptr], _c_int),
     "duplex_moe_noalloc_scratch_bytes": ([], _c_size),
     "duplex_moe_forward_noalloc": ([_c_ptr, _c_int, _c_i32, _c_ptr, _c_ptr, _c_i32, _c_i32,
                                     _c_i32, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_int, _c_int,

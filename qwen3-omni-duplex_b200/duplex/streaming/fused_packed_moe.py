@@ -12,9 +12,14 @@ Drop-in for the reference module of the same name
                                                             (:278-319)
 
 Differences, all deliberate:
-  * every layer is GPU resident (180 GB of HBM holds all 48 layers' experts), so
-    `host_resident`, `n_pinned` and `cpu_compute` are accepted and recorded, but
-    weights are never staged from host memory and nothing is computed on the CPU;
+  * `host_resident=True` (and `fuse_packed_moe_blocks(n_pinned=...)` for the layers past
+    n_pinned) keeps the layer's expert tile records in mapped pinned host memory.  Each
+    call stages only the planned experts into device slots with one kernel that reads
+    host memory directly (`duplex_moe_forward_staged`).  The reference instead reads the
+    selection back to the host and issues one copy per expert and token
+    (fused_packed_moe.py:233-253).  Outputs are bit-identical to a resident layer.
+    `cpu_compute` is recorded but nothing is computed on the CPU: a host-resident layer
+    is staged and computed on the GPU;
   * batches of up to 8 tokens run as ONE pass (tokens that select the same expert
     share its weight stream) instead of a per-token Python loop; larger batches
     (batched decode of many streams, prefill chunks) run the grouped path, up to
@@ -28,6 +33,7 @@ Differences, all deliberate:
 
 from __future__ import annotations
 
+import ctypes
 import gc
 
 import torch
@@ -73,6 +79,27 @@ def _stack_zeros(linears, device):
     return torch.stack([lin.weight_zeros.to(device, torch.int32) for lin in linears])
 
 
+class HostRecords:
+    """Tile records moved into mapped pinned host memory (duplex_host_alloc): the GPU
+    reads them over the host link at `dev_ptr`; no device copy is kept."""
+
+    def __init__(self, dev_buf: torch.Tensor):
+        n = dev_buf.numel()
+        h, d = ctypes.c_void_p(), ctypes.c_void_p()
+        _lib.call("duplex_host_alloc", n, ctypes.byref(h), ctypes.byref(d))
+        self.host_ptr, self.dev_ptr, self.nbytes = h.value, d.value, n
+        view = torch.frombuffer((ctypes.c_uint8 * n).from_address(h.value), dtype=torch.uint8)
+        view.copy_(dev_buf)       # device -> host, synchronous
+
+    def __del__(self):
+        if getattr(self, "host_ptr", None):
+            try:
+                _lib.load().duplex_host_free(self.host_ptr)
+            except Exception:     # interpreter shutdown: the process frees it anyway
+                pass
+            self.host_ptr = None
+
+
 class FusedPackedMoE(nn.Module):
     """SparseMoeBlock replacement for int4-packed experts, on the B200 kernels."""
 
@@ -82,8 +109,11 @@ class FusedPackedMoE(nn.Module):
         super().__init__()
         if dtype not in (torch.float16, torch.bfloat16):
             raise _lib.DuplexError("FusedPackedMoE on B200 runs fp16 or bf16 modules")
-        self.host_resident = host_resident      # recorded; all weights stay in HBM
-        self.cpu_compute = cpu_compute and host_resident
+        if host_resident and (tc or stack):
+            raise _lib.DuplexError("host-resident layers run the staged decode path only "
+                                   "(no tensor-core records, no clock-path stack)")
+        self.host_resident = host_resident      # experts in mapped pinned host memory
+        self.cpu_compute = cpu_compute and host_resident   # recorded; computed on the GPU
         self.pdl = True
         self.stack = stack                      # also build the down K-slices (clock-path stack)
         self.tc = tc                            # also build tensor-core records (batched decode,
@@ -109,9 +139,10 @@ class FusedPackedMoE(nn.Module):
     @classmethod
     def from_stacked(cls, gate_weight, gu_packed, gu_scale, dn_packed, dn_scale, top_k,
                      gu_zeros=None, dn_zeros=None, norm_topk_prob=True, gate_bias=None,
-                     dtype=torch.float16, device="cuda", tc=False, stack=False):
+                     dtype=torch.float16, device="cuda", tc=False, stack=False,
+                     host_resident=False):
         """Build from raw stacked tensors ([E,2I,H/8], [E,2I,G], [E,H,I/8], [E,H,G'])."""
-        m = cls(None, dtype=dtype, device=device, tc=tc, stack=stack)
+        m = cls(None, dtype=dtype, device=device, tc=tc, stack=stack, host_resident=host_resident)
         E, H = gate_weight.shape
         m.num_experts, m.top_k, m.norm_topk_prob = E, top_k, norm_topk_prob
         m.gate = nn.Linear(H, E, bias=gate_bias is not None).to(device=device, dtype=dtype)
@@ -172,6 +203,14 @@ class FusedPackedMoE(nn.Module):
         self.inter, self.hidden, self.hid_out, self.inter_in = inter, hidden, hid_out, inter_in
         self.has_zeros = gu_z is not None
         self._ws = {}
+        self.gu_host = self.dn_host = None
+        if self.host_resident:
+            # the records go to mapped pinned host memory; the device copies are dropped
+            # (built on the GPU one layer at a time, so the spike is one layer's records)
+            self.gu_host = HostRecords(self.gu_tiles.buf)
+            self.dn_host = HostRecords(self.dn_tiles.buf)
+            self.gu_tiles.buf = self.gu_tiles.buf.new_empty(0)
+            self.dn_tiles.buf = self.dn_tiles.buf.new_empty(0)
 
     @staticmethod
     def _dequant(packed, scale, cols, zeros=None):
@@ -283,6 +322,39 @@ class FusedPackedMoE(nn.Module):
             _lib.stream_of(x))
         return out
 
+    def stage_buffer(self, T: int, device) -> torch.Tensor:
+        """Device slots of a host-resident layer for T tokens (duplex_moe_stage_bytes: the
+        staged plan and min(T * top_k, E) experts' records)."""
+        key = ("stage", T, device)
+        buf = self._ws.get(key)
+        if buf is None:
+            n = ctypes.c_size_t()
+            _lib.call("duplex_moe_stage_bytes", T, self.num_experts, self.hidden, self.inter,
+                      self.top_k, self.group, 1 if self.has_zeros else 0, ctypes.byref(n))
+            buf = torch.empty(n.value, dtype=torch.uint8, device=device)
+            self._ws[key] = buf
+        return buf
+
+    def forward_staged_into(self, x, out, residual=None, w_out=None, sel_out=None, rms_eps=0.0):
+        """forward_into for a host-resident layer: route, stage the planned experts from
+        host memory into device slots, run the expert kernels on them (no host
+        synchronisation)."""
+        if self.gu_host is None:
+            raise _lib.DuplexError("this layer is GPU resident (build with host_resident=True)")
+        T = x.shape[0]
+        ws = self.workspace(T, x.device)
+        stage = self.stage_buffer(T, x.device)
+        g = self.gate
+        _lib.call(
+            "duplex_moe_forward_staged", _lib.ptr(x), _lib.dtype_code(x.dtype), T,
+            _lib.ptr(g.weight), _lib.ptr(g.bias), self.num_experts, self.hidden, self.inter,
+            self.top_k, 1 if self.norm_topk_prob else 0, self.gu_host.dev_ptr,
+            self.dn_host.dev_ptr, self.gu_tiles.scale_code, 1 if self.has_zeros else 0,
+            self.group, _lib.ptr(residual), _lib.ptr(out), _lib.ptr(w_out), _lib.ptr(sel_out),
+            _lib.ptr(ws), ws.numel(), _lib.ptr(stage), stage.numel(), _lib.ptr(self.err),
+            float(rms_eps), 1 if self.pdl else 0, _lib.stream_of(x))
+        return out
+
     def route(self, hidden_states):
         """(w [T, k] fp32, sel [T, k] int32) exactly as the forward routes them."""
         x = _lib.aligned(hidden_states.reshape(-1, self.hidden))
@@ -308,7 +380,10 @@ class FusedPackedMoE(nn.Module):
             x = x.to(self.gate.weight.dtype)
         T = x.shape[0]
         out = torch.empty(T, self.hid_out, dtype=x.dtype, device=x.device)
-        if T > 8 and self.grouped_supported():
+        if self.host_resident:
+            for t0 in range(0, T, 8):
+                self.forward_staged_into(x[t0:t0 + 8], out[t0:t0 + 8])
+        elif T > 8 and self.grouped_supported():
             for t0 in range(0, T, GROUPED_MAX_TOKENS):
                 self.forward_grouped_into(x[t0:t0 + GROUPED_MAX_TOKENS],
                                           out[t0:t0 + GROUPED_MAX_TOKENS])
@@ -369,5 +444,7 @@ def fuse_packed_moe_blocks(model, dtype=torch.bfloat16, device="cuda",
             print(f"    fused {n}/{len(sites)} packed blocks, {used:.2f} GB", flush=True)
     n += n_fused
     if verbose:
-        print(f"fused {n} packed MoE blocks, all GPU-resident (B200 kernels)")
+        n_host = 0 if n_pinned is None else max(0, len(sites) - n_pinned)
+        print(f"fused {n} packed MoE blocks ({n - n_host} GPU-resident, {n_host} host-resident; "
+              "B200 kernels)")
     return n

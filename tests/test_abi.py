@@ -173,3 +173,50 @@ def test_torch_library_ops_are_registered():
         op = getattr(ops, name)
         assert isinstance(op.default, torch._ops.OpOverload), name
     assert "Tensor(a!) send" in str(ops.ep_dispatch.default._schema)
+
+
+def test_host_resident_staging_sizes_and_rejections(lib):
+    """duplex_moe_stage_bytes: the staged plan plus min(T * top_k, E) experts' gate|up and
+    down records; duplex_moe_forward_staged rejects bad arguments before any launch."""
+    def rec(K, zp):
+        n = ctypes.c_size_t()
+        assert lib.duplex_tile_record_bytes(K, 128, zp, ctypes.byref(n)) == 0
+        return n.value
+
+    def up256(v):
+        return -(-v // 256) * 256
+
+    H, I, E, k = 2048, 768, 128, 8
+    gu, dn = (2 * I // 16) * rec(H, 1), (H // 16) * rec(I, 1)
+    plan = up256(16 + 64 * 4 + 64 * 4 + 64 * 8 * 4)      # MoePlan
+    n = ctypes.c_size_t()
+    for T, slots in ((1, 8), (8, 64)):
+        assert lib.duplex_moe_stage_bytes(T, E, H, I, k, 128, 1, ctypes.byref(n)) == 0
+        assert n.value == plan + up256(slots * gu) + up256(slots * dn)
+    # fewer experts than T * top_k: one slot per expert
+    assert lib.duplex_moe_stage_bytes(8, 16, 256, 128, 4, 32, 0, ctypes.byref(n)) == 0
+    r256, r128 = ctypes.c_size_t(), ctypes.c_size_t()
+    assert lib.duplex_tile_record_bytes(256, 32, 0, ctypes.byref(r256)) == 0
+    assert lib.duplex_tile_record_bytes(128, 32, 0, ctypes.byref(r128)) == 0
+    assert n.value == plan + up256(16 * 16 * r256.value) + up256(16 * 16 * r128.value)
+    assert lib.duplex_moe_stage_bytes(9, E, H, I, k, 128, 1, ctypes.byref(n)) == 1
+    assert lib.duplex_moe_stage_bytes(1, E, H, I, k, 96, 1, ctypes.byref(n)) == 6
+
+    p = ctypes.c_void_p(1 << 20)          # aligned, never dereferenced: every call rejects
+    odd = ctypes.c_void_p((1 << 20) + 8)
+    big = 1 << 40
+
+    def staged(T=1, out=p, stage=p, stage_bytes=big, ws=p, ws_bytes=big, gu=p):
+        return lib.duplex_moe_forward_staged(p, 0, T, p, None, E, H, I, k, 1, gu, p, 0, 1, 128,
+                                             None, out, None, None, ws, ws_bytes, stage,
+                                             stage_bytes, None, 0.0, 0, None)
+
+    assert staged(stage=None) == 1                      # DUPLEX_ERR_ARG
+    assert staged(T=9) == 1
+    assert staged(out=odd) == 2                         # DUPLEX_ERR_ALIGN
+    assert staged(gu=odd) == 2
+    assert staged(stage_bytes=1024) == 4                # DUPLEX_ERR_WORKSPACE
+    assert staged(ws_bytes=16) == 4                     # the router's workspace check
+    assert lib.duplex_host_alloc(0, ctypes.byref(ctypes.c_void_p()),
+                                 ctypes.byref(ctypes.c_void_p())) == 1
+    assert lib.duplex_host_free(None) == 1
