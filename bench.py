@@ -278,10 +278,17 @@ def run_ours(args):
         g.replay()
     # clocks sampled around a soak of the same loop and the timed region
     sampler = bu.ClockSampler(bu.visible_gpu_indices(ws)).start() if rank == 0 else None
-    t_soak = time.perf_counter()
-    while time.perf_counter() - t_soak < args.soak:
+    # every step exchanges with the other ranks, so all ranks replay the same number of
+    # times: the soak length comes from one replay timed on every rank (max over ranks)
+    torch.cuda.synchronize(dev)
+    bu.barrier()
+    t_one = time.perf_counter()
+    g.replay()
+    torch.cuda.synchronize(dev)
+    n_soak = bu.soak_replays(args.soak, time.perf_counter() - t_one, dev)
+    for _ in range(n_soak):
         g.replay()
-        torch.cuda.synchronize(dev)
+    torch.cuda.synchronize(dev)
     ms = time_graph(g, K, dev)
     ms_step = ms / K
     value = EP_STREAMS * K / (ms / 1e3)

@@ -70,6 +70,15 @@ def max_over_ranks(value: float, device=None) -> float:
     return float(t.item())
 
 
+def soak_replays(seconds: float, one_replay_s: float, device=None) -> int:
+    """How many replays of a step fill about `seconds`, given one replay's time on this
+    rank.  The count is the same on every rank (from the max over ranks of the replay
+    time), which a step that exchanges with the other ranks requires: a rank that
+    replayed once more than its peers would wait on exchanges that never come."""
+    t = max_over_ranks(one_replay_s, device)
+    return max(1, int(seconds / max(t, 1e-6))) if seconds > 0 else 0
+
+
 QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")

@@ -262,13 +262,16 @@ def _peer_rank(rank, world, port, q):
     dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_peer_exchange_matches_the_nccl_all_to_alls(cuda):
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_peer_exchange_matches_the_nccl_all_to_alls(cuda, world):
+    """world GPUs (skipped on a smaller box), 128 / world experts and 32 streams each."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_peer_rank, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_peer_rank, args=(r, world, port, q)) for r in range(world)]
     for p in ps:
         p.start()
     res = sorted(q.get(timeout=300) for _ in ps)

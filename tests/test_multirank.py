@@ -21,8 +21,10 @@ def _worker(rank, ws, port, q):
     import torch.distributed as dist
     bu.init_dist("gloo", timeout_s=60)
     got = bu.max_over_ranks(10.0 + rank)
+    # a rank whose replay looked 3x faster must still soak as many replays as the others
+    soak = bu.soak_replays(1.0, 0.01 if rank == 0 else 0.03)
     bu.barrier()
-    q.put((rank, got, bu.dist_env()))
+    q.put((rank, got, bu.dist_env(), soak))
     dist.destroy_process_group()
 
 
@@ -39,11 +41,14 @@ def test_max_over_ranks_gloo():
         assert p.exitcode == 0
     assert [r[1] for r in res] == [11.0, 11.0]
     assert res[0][2] == (2, 0, 0) and res[1][2] == (2, 1, 1)
+    assert [r[3] for r in res] == [33, 33]    # int(1.0 / 0.03) on both ranks
 
 
 def test_max_over_ranks_without_group():
     from duplex import benchutil as bu
     assert bu.max_over_ranks(3.5) == 3.5
+    assert bu.soak_replays(1.0, 0.25) == 4 and bu.soak_replays(0.0, 0.25) == 0
+    assert bu.soak_replays(1.0, 5.0) == 1
 
 
 # ------------------------------------------------------------------ expert parallelism
