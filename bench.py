@@ -280,15 +280,17 @@ def run_ours(args):
     sampler = bu.ClockSampler(bu.visible_gpu_indices(ws)).start() if rank == 0 else None
     # every step exchanges with the other ranks, so all ranks replay the same number of
     # times: the soak length comes from one replay timed on every rank (max over ranks)
-    torch.cuda.synchronize(dev)
-    bu.barrier()
-    t_one = time.perf_counter()
-    g.replay()
-    torch.cuda.synchronize(dev)
-    n_soak = bu.soak_replays(args.soak, time.perf_counter() - t_one, dev)
-    for _ in range(n_soak):
+    # (--soak 0, the same on every rank, skips it: the launch sequence stays W + K replays)
+    if args.soak > 0:
+        torch.cuda.synchronize(dev)
+        bu.barrier()
+        t_one = time.perf_counter()
         g.replay()
-    torch.cuda.synchronize(dev)
+        torch.cuda.synchronize(dev)
+        n_soak = bu.soak_replays(args.soak, time.perf_counter() - t_one, dev)
+        for _ in range(n_soak):
+            g.replay()
+        torch.cuda.synchronize(dev)
     ms = time_graph(g, K, dev)
     ms_step = ms / K
     value = EP_STREAMS * K / (ms / 1e3)
