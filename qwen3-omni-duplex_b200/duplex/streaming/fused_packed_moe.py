@@ -160,7 +160,7 @@ class FusedPackedMoE(nn.Module):
 
     @classmethod
     def from_checkpoint(cls, tensors, prefix, top_k, norm_topk_prob=True, dtype=torch.bfloat16,
-                        device="cuda", tc=False, stack=False):
+                        device="cuda", tc=False, stack=False, host_resident=False):
         """Build from the packed triplets of one MoE layer in a checkpoint mapping (name ->
         tensor, e.g. duplex.streaming.packed_checkpoint.ShardedTensors): `<prefix>.experts.
         <i>.<gate|up|down>_proj.weight_{packed,scale,shape}` and `<prefix>.gate.weight`."""
@@ -169,7 +169,8 @@ class FusedPackedMoE(nn.Module):
         return cls.from_stacked(st["gate_weight"], st["gu_packed"], st["gu_scale"], st["dn_packed"],
                                 st["dn_scale"], top_k, gu_zeros=st["gu_zeros"],
                                 dn_zeros=st["dn_zeros"], norm_topk_prob=norm_topk_prob,
-                                dtype=dtype, device=device, tc=tc, stack=stack)
+                                dtype=dtype, device=device, tc=tc, stack=stack,
+                                host_resident=host_resident)
 
     def _install(self, gu_p, gu_s, gu_z, dp, ds, dz, inter, hidden, hid_out, inter_in):
         """Repack the stacked experts once into tile records (gate and up blocks paired)."""
@@ -409,13 +410,19 @@ def fuse_packed_moe_blocks(model, dtype=torch.bfloat16, device="cuda",
     packed_checkpoint.ShardedTensors) the fused-expert blocks of transformers >= 5, which
     have no per-expert modules to hold the packed triplets, are replaced too: their
     experts are stacked straight from the checkpoint keys `prefix + <block name>.experts.
-    <i>.*` (packed_checkpoint.fused_expert_sites)."""
+    <i>.*` (packed_checkpoint.fused_expert_sites).
+
+    n_pinned: the first n_pinned replaced blocks (checkpoint-built ones first) stay GPU
+    resident and every later one is host-resident (FusedPackedMoE(host_resident=True)),
+    as in the reference; None keeps every block on the GPU."""
     n_fused = 0
     if checkpoint is not None:
         from duplex.streaming.packed_checkpoint import fused_expert_sites
         for parent, attr, key, top_k, norm in fused_expert_sites(model, checkpoint, prefix):
+            host = n_pinned is not None and n_fused >= n_pinned
             setattr(parent, attr, FusedPackedMoE.from_checkpoint(
-                checkpoint, key, top_k, norm_topk_prob=norm, dtype=dtype, device=device))
+                checkpoint, key, top_k, norm_topk_prob=norm, dtype=dtype, device=device,
+                host_resident=host))
             n_fused += 1
             gc.collect()
         if n_fused and torch.cuda.is_available():
@@ -430,7 +437,7 @@ def fuse_packed_moe_blocks(model, dtype=torch.bfloat16, device="cuda",
     n = 0
     for parent, name in sites:
         child = getattr(parent, name)
-        host = n_pinned is not None and n >= n_pinned
+        host = n_pinned is not None and n_fused + n >= n_pinned
         setattr(parent, name, FusedPackedMoE(child, dtype, device, host_resident=host,
                                              cpu_compute=cpu_compute))
         child.experts = None
@@ -444,7 +451,7 @@ def fuse_packed_moe_blocks(model, dtype=torch.bfloat16, device="cuda",
             print(f"    fused {n}/{len(sites)} packed blocks, {used:.2f} GB", flush=True)
     n += n_fused
     if verbose:
-        n_host = 0 if n_pinned is None else max(0, len(sites) - n_pinned)
+        n_host = 0 if n_pinned is None else max(0, n - n_pinned)
         print(f"fused {n} packed MoE blocks ({n - n_host} GPU-resident, {n_host} host-resident; "
               "B200 kernels)")
     return n
