@@ -220,3 +220,30 @@ def test_host_resident_staging_sizes_and_rejections(lib):
     assert lib.duplex_host_alloc(0, ctypes.byref(ctypes.c_void_p()),
                                  ctypes.byref(ctypes.c_void_p())) == 1
     assert lib.duplex_host_free(None) == 1
+
+
+def test_expert_parallel_entry_points_reject_before_any_launch(lib):
+    """The exchange entry points (dispatch pack, peer dispatch / put / wait, combine, CUDA
+    IPC) reject bad arguments with a status and touch no device."""
+    p = ctypes.c_void_p(1 << 20)          # aligned, never dereferenced: every call rejects
+    null = None
+    assert lib.duplex_ipc_handle_bytes() == 64
+    assert lib.duplex_ipc_alloc(0, ctypes.byref(ctypes.c_void_p()), p) == 1
+    assert lib.duplex_ipc_open(null, ctypes.byref(ctypes.c_void_p())) == 1
+    # dispatch pack: T over 512, experts not split evenly, rows not a multiple of 16 B
+    assert lib.duplex_ep_dispatch_pack(p, 4112, 513, 8, 128, 2, 4096, p, p, null) == 1
+    assert lib.duplex_ep_dispatch_pack(p, 4112, 32, 8, 128, 3, 4096, p, p, null) == 1
+    assert lib.duplex_ep_dispatch_pack(p, 4104, 32, 8, 128, 2, 4096, p, p, null) == 2
+    # peer dispatch: rank outside the group, missing flags
+    assert lib.duplex_ep_dispatch_peer(p, 4112, 32, 8, 128, 2, 2, 4096, p, p, p, p, p, null) == 1
+    assert lib.duplex_ep_dispatch_peer(p, 4112, 32, 8, 128, 2, 0, 4096, p, p, null, p, p,
+                                       null) == 1
+    # put: blocks under 16 B or not a multiple of 16 B
+    assert lib.duplex_ep_put_peer(p, 8, 2, 0, p, p, p, p, null) == 1
+    assert lib.duplex_ep_put_peer(p, 24, 2, 0, p, p, p, p, null) == 2
+    # wait: no error word, no ranks
+    assert lib.duplex_ep_wait(p, p, 2, 0, null, null) == 1
+    assert lib.duplex_ep_wait(p, p, 0, 0, p, null) == 1
+    # combine: H not a multiple of 4, unsupported activation dtype
+    assert lib.duplex_ep_combine(p, p, 32, 2, 2046, null, p, 0, null) == 1
+    assert lib.duplex_ep_combine(p, p, 32, 2, 2048, null, p, 7, null) == 3
