@@ -247,3 +247,22 @@ def test_expert_parallel_entry_points_reject_before_any_launch(lib):
     # combine: H not a multiple of 4, unsupported activation dtype
     assert lib.duplex_ep_combine(p, p, 32, 2, 2046, null, p, 0, null) == 1
     assert lib.duplex_ep_combine(p, p, 32, 2, 2048, null, p, 7, null) == 3
+
+
+def test_plain_c_host_links_and_calls_the_library(lib, tmp_path):
+    """include/duplex_b200.h compiles as C99 and a C program links the library and gets
+    its answers (tests/c/abi_smoke.c): the boundary needs no C++ or Python on the host."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    src = Path(__file__).resolve().parent / "c" / "abi_smoke.c"
+    so = Path(_lib.__file__).resolve().parent / "libduplex_b200.so"
+    exe = tmp_path / "abi_smoke"
+    r = subprocess.run([cc, "-std=c99", "-Wall", "-Werror", f"-I{HEADER.parent}", str(src),
+                        "-o", str(exe), f"-L{so.parent}", "-lduplex_b200",
+                        f"-Wl,-rpath,{so.parent}"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
