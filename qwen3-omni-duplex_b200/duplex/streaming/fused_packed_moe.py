@@ -284,6 +284,9 @@ class FusedPackedMoE(nn.Module):
         the module dtype) used in place of the gate.  engine: "tc", "mma" or None (the
         module's choice, grouped_engine)."""
         T = x.shape[0]
+        if self.host_resident:
+            raise _lib.DuplexError("a host-resident layer runs the staged path (forward, "
+                                   "forward_into or forward_staged_into), 8 tokens per call")
         if T > GROUPED_MAX_TOKENS:
             raise _lib.DuplexError(f"grouped MoE takes at most {GROUPED_MAX_TOKENS} tokens")
         engine = engine or self.grouped_engine(T)
@@ -308,7 +311,10 @@ class FusedPackedMoE(nn.Module):
 
     def forward_into(self, x, out, residual=None, w_out=None, sel_out=None, rms_eps=0.0):
         """x [T<=8, H] -> out [T, H] (+ residual), no host synchronisation.  rms_eps > 0 routes
-        and computes on the RMS-normalised x (clock-path stack)."""
+        and computes on the RMS-normalised x (clock-path stack).  A host-resident layer takes
+        the staged path (forward_staged_into)."""
+        if self.host_resident:
+            return self.forward_staged_into(x, out, residual, w_out, sel_out, rms_eps)
         T = x.shape[0]
         ws = self.workspace(T, x.device)
         g = self.gate
