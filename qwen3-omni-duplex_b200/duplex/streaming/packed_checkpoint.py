@@ -20,9 +20,16 @@ triplets straight from the checkpoint and stacks them per layer:
                                           gu_zeros=st["gu_zeros"], dn_zeros=st["dn_zeros"])
 
 or `fuse_packed_moe_blocks(model, ..., checkpoint=ckpt, prefix="thinker.model.")`, which
-also replaces the fused-expert blocks.  Optional zero points: `weight_zeros` (this build's
-name) or `weight_zero_point` (compressed-tensors'), [R, ceil(G/8)] int32 with nibble j of
-word m the zero point of group 8m + j.  Everything here is host-side tensor plumbing.
+also replaces the fused-expert blocks.  Optional zero points come in one of two forms:
+  * `weight_zeros` (this build's): [R, ceil(G/8)] int32, nibble j of word m the zero
+    point z of group 8m + j, value = (nibble - z) * scale;
+  * `weight_zero_point` (compressed-tensors' asymmetric pack-quantized format): the
+    signed zero point zp in [-8, 7] per (row, group), either packed as compressed-tensors
+    writes it (`pack_to_int32(zp, 4, packed_dim=0)`: zp + 8 in nibble j of word m of
+    row block m, [ceil(R/8), G] int32) or unpacked ([R, G]).  Its weights hold
+    q = nibble - 8 and dequantise to (q - zp) * scale, which is (nibble - (zp + 8)) *
+    scale, so z = zp + 8, converted here to the layout above.
+Everything here is host-side tensor plumbing.
 """
 
 from __future__ import annotations
@@ -97,10 +104,40 @@ def moe_prefixes(tensors: Mapping) -> list[str]:
     return sorted(found, key=key)
 
 
-def _zeros(tensors: Mapping, base: str):
-    for z in ZERO_KEYS:
-        if f"{base}.{z}" in tensors:
-            return tensors[f"{base}.{z}"].to(torch.int32)
+def pack_group_zeros(z: torch.Tensor) -> torch.Tensor:
+    """[R, G] zero points in 0..15 -> [R, ceil(G/8)] int32, nibble j of word m = group 8m + j."""
+    R, G = z.shape
+    Gw = -(-G // 8)
+    zz = torch.zeros(R, Gw * 8, dtype=torch.int64)
+    zz[:, :G] = z.to(torch.int64) & 0xF
+    words = (zz.view(R, Gw, 8) << (4 * torch.arange(8, dtype=torch.int64))).sum(-1)
+    return torch.where(words >= 1 << 31, words - (1 << 32), words).to(torch.int32)
+
+
+def zeros_from_compressed_tensors(zp: torch.Tensor, R: int, G: int) -> torch.Tensor:
+    """compressed-tensors' `weight_zero_point` of an R-row linear with G groups -> this
+    build's [R, ceil(G/8)] int32 layout.  Packed form: [ceil(R/8), G] int32 (zp + 8 in
+    nibble j of word m = row 8m + j); unpacked form: [R, G] signed zero points."""
+    zp = zp.to(torch.int64)
+    if tuple(zp.shape) == (-(-R // 8), G) and R != -(-R // 8):
+        shifts = 4 * torch.arange(8, dtype=torch.int64)
+        nib = ((zp & 0xFFFFFFFF).unsqueeze(1) >> shifts.view(1, 8, 1)) & 0xF   # [R/8, 8, G]
+        z = nib.reshape(-1, G)[:R]
+    elif tuple(zp.shape) == (R, G):
+        z = zp + 8
+    else:
+        raise ValueError(f"weight_zero_point of shape {tuple(zp.shape)} fits neither "
+                         f"[{-(-R // 8)}, {G}] (packed) nor [{R}, {G}]")
+    if int(z.min()) < 0 or int(z.max()) > 15:
+        raise ValueError("weight_zero_point outside the 4-bit range")
+    return pack_group_zeros(z)
+
+
+def _zeros(tensors: Mapping, base: str, R: int, G: int):
+    if f"{base}.weight_zeros" in tensors:
+        return tensors[f"{base}.weight_zeros"].to(torch.int32)
+    if f"{base}.weight_zero_point" in tensors:
+        return zeros_from_compressed_tensors(tensors[f"{base}.weight_zero_point"], R, G)
     return None
 
 
@@ -121,7 +158,7 @@ def _stack(tensors: Mapping, prefix: str, proj: str, E: int, dtype):
                              f"{shp} disagree with expert 0's {shape}")
         packed.append(p.to(torch.int32))
         scale.append(s.to(dtype) if dtype is not None else s)
-        zeros.append(_zeros(tensors, base))
+        zeros.append(_zeros(tensors, base, shape[0], s.shape[1]))
     if any(z is None for z in zeros) and not all(z is None for z in zeros):
         raise ValueError(f"{prefix}.{proj}: zero points on some experts only")
     z = None if zeros[0] is None else torch.stack(zeros)

@@ -62,6 +62,18 @@ def test_zero_point_eight_is_reference(golden_dir):
         assert np.array_equal(np.asarray(a, np.float32), np.asarray(b, np.float32))
 
 
+@pytest.mark.parametrize("g", [64, 128])
+@pytest.mark.parametrize("dt", ["float16", "bfloat16", "float32"])
+def test_zero_point_dequant_matches_compressed_tensors(golden_dir, g, dt):
+    """value = (nibble - z) * scale, bit for bit against compressed-tensors' asymmetric
+    group dequantisation (q - zp) * scale with q = nibble - 8, zp = z - 8
+    (golden_zero_point_dequant.npz, made by make_zero_point_golden.py)."""
+    d = load(golden_dir, "golden_zero_point_dequant.npz")
+    s = O.round_to(d[f"g{g}_{dt}_scale"], dt)
+    w = O.dequant(d[f"g{g}_packed"], s, 256, d[f"g{g}_zeros"], dt)
+    assert np.array_equal(np.asarray(w, np.float32), d[f"g{g}_{dt}_w"])
+
+
 def test_gemv_matches_reference_gemv(golden_dir):
     g = load(golden_dir, "golden_gemv.npz")
     y = O.dequant_gemv(g["x"], g["packed"], g["scale"], g["sel"])

@@ -10,11 +10,14 @@ import numpy as np
 import pytest
 import torch
 
+import oracle as O
 from duplex import synth
 from duplex.streaming.packed_checkpoint import (ShardedTensors, fused_expert_sites, moe_prefixes,
                                                 stack_layer)
 
 PROJS = ("gate_proj", "up_proj", "down_proj")
+pack_to_int32 = pytest.importorskip(
+    "compressed_tensors.compressors.pack_quantized.helpers").pack_to_int32
 
 
 def checkpoint_tensors(L, prefix, zero_key="weight_zeros"):
@@ -30,7 +33,15 @@ def checkpoint_tensors(L, prefix, zero_key="weight_zeros"):
             t[f"{base}.weight_scale"] = torch.from_numpy(L[f"{src}_scale"][i, rows].copy())
             t[f"{base}.weight_shape"] = torch.tensor(shape, dtype=torch.int64)
             if L[f"{src}_zeros"] is not None:
-                t[f"{base}.{zero_key}"] = torch.from_numpy(L[f"{src}_zeros"][i, rows].copy())
+                zw = L[f"{src}_zeros"][i, rows].copy()        # this build's [R, ceil(G/8)]
+                if zero_key == "weight_zeros":
+                    t[f"{base}.weight_zeros"] = torch.from_numpy(zw)
+                else:                                         # compressed-tensors' forms
+                    G = L[f"{src}_scale"].shape[-1]
+                    zp = torch.from_numpy(O.unpack_zeros(zw, G).astype(np.int8) - 8)
+                    if zero_key == "weight_zero_point":
+                        zp = pack_to_int32(zp, 4, packed_dim=0)
+                    t[f"{base}.weight_zero_point"] = zp
     return t
 
 
@@ -46,7 +57,8 @@ def write_checkpoint(path, tensors, n_shards=2):
     (path / "model.safetensors.index.json").write_text(json.dumps({"weight_map": wm}))
 
 
-@pytest.mark.parametrize("zero_key", [None, "weight_zeros", "weight_zero_point"])
+@pytest.mark.parametrize("zero_key", [None, "weight_zeros", "weight_zero_point",
+                                      "weight_zero_point_unpacked"])
 def test_sharded_checkpoint_stacks_to_the_module_layout(tmp_path, zero_key):
     layers = [synth.moe_layer_np(seed=40 + l, E=4, H=64, I=32, top_k=2, group=32,
                                  zero_points=zero_key is not None) for l in range(2)]
@@ -114,3 +126,24 @@ def test_fused_expert_blocks_of_transformers_are_found():
     assert parent is model.layers[0] and attr == "mlp"
     assert key == "thinker.model.layers.0.mlp" and top_k == 2 and norm is True
     assert fused_expert_sites(model, t, prefix="") == []   # keys under another prefix
+
+
+@pytest.mark.parametrize("R,G", [(768, 16), (2048, 6), (13, 9), (1, 3)])
+def test_compressed_tensors_zero_points_convert_to_the_group_layout(R, G):
+    """compressed-tensors' asymmetric zero points (signed zp, packed over rows by its own
+    pack_to_int32 or unpacked) -> this build's z = zp + 8, nibbles along the groups."""
+    from duplex.streaming.fused_packed_moe import _stack_zeros
+    from duplex.streaming.packed_checkpoint import zeros_from_compressed_tensors
+    z = np.random.default_rng(R * 31 + G).integers(0, 16, (R, G))
+    want = O.pack_zeros(z)
+    zp = torch.from_numpy((z - 8).astype(np.int8))
+    assert np.array_equal(zeros_from_compressed_tensors(zp, R, G).numpy(), want)
+    if R > 1:
+        packed = pack_to_int32(zp, 4, packed_dim=0)
+        assert tuple(packed.shape) == (-(-R // 8), G)
+        assert np.array_equal(zeros_from_compressed_tensors(packed, R, G).numpy(), want)
+    lin = NS(weight_shape=torch.tensor([R, 8 * G]), weight_scale=torch.ones(R, G),
+             weight_zero_point=zp)
+    assert np.array_equal(_stack_zeros([lin, lin], "cpu").numpy(), np.stack([want, want]))
+    with pytest.raises(ValueError):
+        zeros_from_compressed_tensors(torch.zeros(R + 1, G + 1, dtype=torch.int32), R, G)
