@@ -12,7 +12,8 @@ src/duplex/quant/dequant.py (every public name of it is here, same signatures).
 (`weight_packed` [out, in/8] int32, `weight_scale` [out, G], `weight_shape`),
 bit-identical to the reference: the scale is first cast to `dtype`, then every
 element is one rounding of the exact (nibble - 8) * scale product into `dtype`.  An
-optional `weight_zeros` buffer ([out, ceil(G/8)] int32) replaces the constant 8.
+optional `weight_zeros` buffer ([out, ceil(G/8)] int32) replaces the constant 8, and so
+does compressed-tensors' asymmetric `weight_zero_point` (converted on use).
 
 `patch_packed_linears` installs a forward on every packed Linear.  The reference's
 forward dequantises the whole weight on every call and runs F.linear; here the
@@ -42,7 +43,8 @@ def _shape(mod):
 def dequantize_weight(mod, dtype: torch.dtype | None = None, device=None) -> torch.Tensor:
     out_f, in_f = _shape(mod)
     packed, scale = mod.weight_packed, mod.weight_scale
-    zeros = getattr(mod, "weight_zeros", None)
+    from duplex.streaming.packed_checkpoint import linear_zeros
+    zeros = linear_zeros(mod)
     if device is not None:
         packed, scale = packed.to(device), scale.to(device)
         zeros = None if zeros is None else zeros.to(device)

@@ -77,15 +77,13 @@ def _stack_zeros(linears, device):
     """Zero points of the stacked linears in this build's [R, ceil(G/8)] int32 layout:
     `weight_zeros` as is, or compressed-tensors' asymmetric `weight_zero_point` converted
     (packed_checkpoint.zeros_from_compressed_tensors); None for symmetric linears."""
-    if getattr(linears[0], "weight_zeros", None) is not None:
-        return torch.stack([lin.weight_zeros.to(device, torch.int32) for lin in linears])
-    if getattr(linears[0], "weight_zero_point", None) is not None:
-        from duplex.streaming.packed_checkpoint import zeros_from_compressed_tensors
-        R = int(linears[0].weight_shape[0])
-        return torch.stack([zeros_from_compressed_tensors(lin.weight_zero_point.cpu(), R,
-                                                          lin.weight_scale.shape[1]).to(device)
-                            for lin in linears])
-    return None
+    from duplex.streaming.packed_checkpoint import linear_zeros
+    zs = [linear_zeros(lin) for lin in linears]
+    if all(z is None for z in zs):
+        return None
+    if any(z is None for z in zs):
+        raise _lib.DuplexError("zero points on some experts only")
+    return torch.stack([z.to(device, torch.int32) for z in zs])
 
 
 class HostRecords:

@@ -133,6 +133,23 @@ def zeros_from_compressed_tensors(zp: torch.Tensor, R: int, G: int) -> torch.Ten
     return pack_group_zeros(z)
 
 
+def linear_zeros(mod):
+    """A packed Linear's zero points in this build's [R, ceil(G/8)] int32 layout, on the
+    module's device: `weight_zeros` as is, compressed-tensors' `weight_zero_point`
+    converted (zeros_from_compressed_tensors), or None for a symmetric module."""
+    z = getattr(mod, "weight_zeros", None)
+    if z is not None:
+        return z
+    zp = getattr(mod, "weight_zero_point", None)
+    if zp is None:
+        return None
+    s = mod.weight_scale
+    R = int(mod.weight_shape[0]) if getattr(mod, "weight_shape", None) is not None \
+        else int(mod.weight_packed.shape[0])
+    G = s.shape[1] if s.dim() == 2 else 1
+    return zeros_from_compressed_tensors(zp.cpu(), R, G).to(zp.device)
+
+
 def _zeros(tensors: Mapping, base: str, R: int, G: int):
     if f"{base}.weight_zeros" in tensors:
         return tensors[f"{base}.weight_zeros"].to(torch.int32)

@@ -253,7 +253,8 @@ class TritonPackedLinear(torch.nn.Module):
         super().__init__()
         shape = tuple(int(v) for v in mod.weight_shape.tolist())
         self.out_features, self.in_features = shape
-        zeros = getattr(mod, "weight_zeros", None)
+        from duplex.streaming.packed_checkpoint import linear_zeros
+        zeros = linear_zeros(mod)
         scale = mod.weight_scale.to(device)
         self.group = -(-self.in_features // scale.shape[-1])
         self.tiles = Int4Tiles(mod.weight_packed.to(device), scale,

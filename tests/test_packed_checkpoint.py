@@ -147,3 +147,21 @@ def test_compressed_tensors_zero_points_convert_to_the_group_layout(R, G):
     assert np.array_equal(_stack_zeros([lin, lin], "cpu").numpy(), np.stack([want, want]))
     with pytest.raises(ValueError):
         zeros_from_compressed_tensors(torch.zeros(R + 1, G + 1, dtype=torch.int32), R, G)
+
+
+def test_linear_zeros_reads_either_key_and_refuses_mixed_experts():
+    from duplex import _lib
+    from duplex.streaming.fused_packed_moe import _stack_zeros
+    from duplex.streaming.packed_checkpoint import linear_zeros
+    R, G = 24, 4
+    z = np.random.default_rng(3).integers(0, 16, (R, G))
+    ours = torch.from_numpy(O.pack_zeros(z))
+    ct = pack_to_int32(torch.from_numpy((z - 8).astype(np.int8)), 4, packed_dim=0)
+    base = dict(weight_shape=torch.tensor([R, 8 * G]), weight_scale=torch.ones(R, G))
+    a, b, sym = NS(weight_zeros=ours, **base), NS(weight_zero_point=ct, **base), NS(**base)
+    assert linear_zeros(a) is ours
+    assert torch.equal(linear_zeros(b), ours)
+    assert linear_zeros(sym) is None and _stack_zeros([sym, sym], "cpu") is None
+    assert torch.equal(_stack_zeros([a, b], "cpu"), torch.stack([ours, ours]))
+    with pytest.raises(_lib.DuplexError):
+        _stack_zeros([a, sym], "cpu")
